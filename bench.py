@@ -1,0 +1,308 @@
+#!/usr/bin/env python3
+"""Batch-1 greedy decode of the Granite-3B-A800M-shaped MoE model on B200.
+
+Workload: 32 layers, hidden 1536, 24 q / 8 kv heads (d 64), 40 experts top-8 (I 512), vocab 49155, random-init
+bf16 weights (synthetic generator, seed 2, std 0.02), KV cache pre-filled to 2048 positions by decoding 2048
+uniform random ids (seed 2) through the model itself, then greedy decode.  One bench step = one decoded token.
+
+  value  device-resident throughput: K graph-replayed decode steps, the token fed back on the device, timed with
+         CUDA events on the library's stream (max over ranks; every rank decodes its own replica: batch-1 decode
+         does not shard, so N GPUs run N independent replicas = weak scaling)
+  e2e    the same decode through the public C-ABI step call a user makes (lastro_model_step): the token goes
+         host->device and the next token device->host every step, inside the timed region
+  roofline  the dominant kernel (by device time) of the step: algorithmic bytes per launch / its mean duration,
+         measured live with events between direct launches (lastro_model_profile)
+  cpu_baseline  the CPU oracle (a C restatement of the reference's CPU path, rust/moe-rt/src/{cpu,model}.rs)
+         decoding the same model at the same context on this host's cores
+
+--impl reference times that CPU path as the reference arm (the reference itself is Rust + cuTile and cannot be
+built here: no cargo, no network).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "lastro-rust_b200"))
+
+from lastro_b200 import configs as CFG  # noqa: E402
+
+KERNELS = ("qkv_rope", "attention", "oproj", "router", "gate_up", "down", "head")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", choices=("lastro", "reference"), default="lastro")
+    ap.add_argument("--context", type=int, default=CFG.C3_3B["context"])
+    ap.add_argument("--kv", choices=("bf16", "f32"), default="bf16")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample")
+    ap.add_argument("--profile-only", action="store_true", help="small run for ncu: prefill + a few steps")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def kernel_bytes(cfg, context):
+    """Algorithmic HBM bytes of one launch of each kernel (bf16 weights, bf16 KV), at the given mean context."""
+    H, I, E, k, V = cfg["hidden"], cfg["inter"], cfg["experts"], cfg["k"], cfg["vocab"]
+    qd, kvd = cfg["heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
+    return dict(qkv_rope=(qd + 2 * kvd) * H * 2 + 2 * kvd * 2, attention=2 * kvd * 2 * context, oproj=H * qd * 2,
+                router=E * H * 2, gate_up=k * 2 * I * H * 2, down=k * H * I * 2, head=V * H * 2)
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.flush()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], 0.0, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for n, v in zip(names, r[5:9]):
+                    if "Active" in v and "Not" not in v:
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_decode_rate(cfg, context, seed, seconds, steps=None, warmup=1):
+    """The oracle (reference CPU path restated) decoding at `context`: returns (tok/s, threads, tokens, sample)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    threads = os.cpu_count() or 1
+    t0 = time.time()
+    om = O.Model(cfg, synthetic_seed=seed, std=CFG.WEIGHT_STD, norm_std=0.0, threads=threads)
+    pool = O.Pool(threads)
+    n_max = (steps or 64) + warmup + 2
+    s = O.Session(om, pool, context + n_max)
+    s.fill_kv(context, seed, 0.5)
+    setup = time.time() - t0
+    tok = CFG.synthetic_tokens(1, seed, cfg["vocab"])[0]
+    for _ in range(warmup):
+        lg, _, _ = s.step(tok)
+        tok = O.argmax_last(lg)
+    n, t1 = 0, time.time()
+    while True:
+        lg, _, _ = s.step(tok)
+        tok = O.argmax_last(lg)
+        n += 1
+        el = time.time() - t1
+        if (steps is not None and n >= steps) or (steps is None and el >= seconds):
+            break
+    s.close()
+    om.close()
+    pool.close()
+    sample = (f"{n} greedy decode steps of the full {cfg['layers']}-layer model at context {context}-{context + n}"
+              f" (K/V rows synthetic), weights from the same generator; setup {setup:.1f} s untimed")
+    return n / el, threads, n, sample
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cfg = CFG.C3_3B["model"]
+    rate, threads, n, sample = cpu_decode_rate(cfg, a.context, CFG.C3_3B["weight_seed"], 0, steps=a.steps,
+                                               warmup=min(a.warmup, 2))
+    line = {
+        "impl": "reference", "metric": "decode tok/s (bs1) Granite-3B-A800M shape, ctx 2048", "value": rate,
+        "unit": "tok/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1000.0 / rate,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": CFG.C3_3B["name"], "context": a.context, "batch": 1},
+        "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference (Rust + cuTile, rust/moe-rt) cannot be built here; its CPU path is timed through the "
+                "C restatement in oracle/ with all host threads",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        return run_reference(a)
+
+    import torch
+    import torch.distributed as dist
+
+    import lastro_b200 as LB
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    c = CFG.C3_3B
+    cfg = c["model"]
+    K, W = a.steps, a.warmup
+    if a.profile_only:
+        K, W = 2, 1
+    stream = torch.cuda.Stream()
+    ctx = LB.Context(local, stream.cuda_stream)
+    max_len = a.context + 2 * (K + W) + 64
+    model = LB.GpuModel(ctx, cfg, max_len, kv_dtype=a.kv)
+    model.fill_synthetic(c["weight_seed"], CFG.WEIGHT_STD, 0.0)
+    prompt = CFG.synthetic_tokens(a.context, c["prompt_seed"], cfg["vocab"])
+    t0 = time.time()
+    model.generate(prompt, 1)  # pre-fill the KV cache through the model (untimed)
+    prefill_s = time.time() - t0
+    if a.profile_only:
+        model.decode(K)
+        ctx.synchronize()
+        print(json.dumps({"profile_only": True, "prefill_s": prefill_s}))
+        return 0
+
+    # ---- device-resident decode ------------------------------------------------------------------------------
+    model.decode(W)
+    ctx.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx0 = model.pos
+    ev0.record(stream)
+    model.decode(K)
+    ev1.record(stream)
+    stream.synchronize()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    mean_ctx = ctx0 + (K + 1) / 2.0
+    value = world * K / (ms / 1000.0)
+
+    # ---- end to end through the C-ABI step call (host token in, host token out) -----------------------------
+    tok = int(CFG.synthetic_tokens(1, 99, cfg["vocab"])[0])
+    for _ in range(W):
+        _, tok, _, _ = model.step(tok, want_logits=False, want_routes=False)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(K):
+        _, tok, _, _ = model.step(tok, want_logits=False, want_routes=False)
+    e1.record(stream)
+    stream.synchronize()
+    wall_ms = (time.perf_counter() - w0) * 1000.0
+    e2e_ms = max(e0.elapsed_time(e1), wall_ms)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": world * K / (e2e_ms / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4}
+
+    # ---- per-kernel device time (direct launches, events between kernels) --------------------------------------
+    prof = model.profile(4)
+    L = cfg["layers"]
+    prof_ctx = model.pos - 2
+    kb = kernel_bytes(cfg, prof_ctx)
+    launches = {k: (1 if k == "head" else L) for k in KERNELS}
+    dominant = max(KERNELS, key=lambda k: prof[k])
+    per_launch_ms = prof[dominant] / launches[dominant]
+    hbm, peak_kind = peaks()
+    achieved = kb[dominant] / (per_launch_ms / 1000.0) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get(dominant)
+    moe_bytes = kb["router"] + kb["gate_up"] + kb["down"]
+    moe_ms = (prof["router"] + prof["gate_up"] + prof["down"]) / L
+    B = CFG.bytes_per_token(cfg, mean_ctx)
+    step_s = ms / 1000.0 / K
+    line = {
+        "metric": "decode tok/s (bs1) Granite-3B-A800M shape, ctx 2048", "value": value, "unit": "tok/s",
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": c["name"], "batch": 1, "context_start": ctx0, "mean_context": mean_ctx,
+                   "kv_cache": f"paged {a.kv}", "weights": "bf16, activations/accumulators f32",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2: every step streams ~1.9 GB of weights and KV (L2 126 MB)",
+                   "prefill_s": round(prefill_s, 2)},
+        "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": traffic,
+                     "bytes_per_launch": kb[dominant], "ms_per_launch": per_launch_ms},
+        "step_roofline": {"literal_bytes": B["literal"], "full_bytes": B["full"],
+                          "literal_frac": B["literal"] / step_s / 1e9 / hbm,
+                          "full_frac": B["full"] / step_s / 1e9 / hbm,
+                          "literal_frac_vs_8tbs": B["literal"] / step_s / 1e9 / 8000.0},
+        "moe_block": {"gbs": moe_bytes / (moe_ms / 1000.0) / 1e9, "frac": moe_bytes / (moe_ms / 1000.0) / 1e9 / hbm,
+                      "us_per_layer": moe_ms * 1000.0},
+        "kernels_ms_per_step": {k: round(v, 4) for k, v in prof.items()},
+        "e2e": e2e,
+        "gpu_launches": K * (6 * L + 1),
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        rate, threads, n, sample = cpu_decode_rate(cfg, a.context, c["weight_seed"], a.cpu_seconds)
+        line["cpu_baseline"] = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
+    model.close()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

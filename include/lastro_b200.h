@@ -1,0 +1,108 @@
+/*
+ * lastro_b200.h -- C ABI of the B200-native Granite-MoE decode library (liblastro_b200.so).
+ *
+ * Drop-in boundary for the GPU operator API of brenoperucchi/lastro-rust
+ * (rust/moe-rt).  Every entry point below names the reference item it replaces
+ * (file:line inside that project).  Plain pointers and sizes only; host buffers
+ * are caller-owned and only read/written during the call.
+ *
+ * Status codes follow the reference's error policy (gpu_model.rs:249-267,
+ * gpu.rs:345-355):
+ *   - argument errors are refused before any launch and leave the object usable;
+ *   - a CUDA runtime error synchronizes the stream, then poisons the object:
+ *     every later call on it returns LASTRO_E_POISONED.
+ * One caller thread per object (the reference's &mut self).
+ */
+#ifndef LASTRO_B200_H
+#define LASTRO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LASTRO_OK 0
+#define LASTRO_E_ARG 1         /* bad argument or shape: refused before any launch */
+#define LASTRO_E_CUDA 2        /* CUDA runtime error: stream synchronized, object poisoned */
+#define LASTRO_E_POISONED 3    /* object unusable after an earlier runtime error */
+#define LASTRO_E_FULL 4        /* KV cache full (gpu_model.rs:252-254) */
+#define LASTRO_E_NOMEM 5       /* device allocation failed */
+#define LASTRO_E_UNSUPPORTED 6 /* shape/dtype outside what the kernels implement */
+#define LASTRO_E_STATE 7       /* e.g. a weight tensor not loaded yet */
+
+#define LASTRO_DTYPE_BF16 1
+#define LASTRO_DTYPE_F32 2
+
+typedef struct lastro_ctx lastro_ctx;
+typedef struct lastro_layer lastro_layer;
+typedef struct lastro_model lastro_model;
+
+/* model.rs:14-31 Config (+ the dtypes the device keeps) */
+typedef struct {
+    int32_t hidden, inter, layers, heads, kv_heads, head_dim, vocab, experts, k;
+    float rope_theta, eps, embedding_multiplier, residual_multiplier, attention_multiplier, logits_scaling;
+    int32_t weight_dtype; /* LASTRO_DTYPE_BF16 */
+    int32_t kv_dtype;     /* LASTRO_DTYPE_BF16 (paged bf16 KV) or LASTRO_DTYPE_F32 */
+} lastro_model_desc;
+
+/* ---- context: one device, one stream (the reference's Arc<Stream>, gpu.rs:333) ---------------------------------- */
+/* stream_or_null: a cudaStream_t to enqueue on, or NULL for a stream owned by the context */
+int lastro_ctx_create(int32_t device, void *stream_or_null, lastro_ctx **out);
+void lastro_ctx_destroy(lastro_ctx *ctx);
+int lastro_ctx_synchronize(lastro_ctx *ctx);
+/* text of the last error on this context ("" if none); valid until the next call on ctx */
+const char *lastro_last_error(const lastro_ctx *ctx);
+const char *lastro_version(void);
+
+/* ---- MoE block: GpuLayer (gpu.rs:325-541) ---------------------------------------------------------------------- */
+/* GpuLayer::upload (gpu.rs:430-449): copies router [E,H], gate_up [E,2I,H], down [E,H,I] (bf16 bits) to the device */
+int lastro_layer_create(lastro_ctx *ctx, int32_t experts, int32_t hidden, int32_t inter, int32_t k,
+                        const uint16_t *router, const uint16_t *gate_up, const uint16_t *down, lastro_layer **out);
+/* GpuLayer::forward (gpu.rs:461-478): x [H] host in -> y [H] host out, the routing (ids/weights [k], in
+ * descending-logit order) and optionally the router logits [E]; any output pointer may be NULL */
+int lastro_layer_forward(lastro_layer *layer, const float *x, float *y, int32_t *ids, float *weights,
+                         float *logits);
+/* GpuLayer::add_into (gpu.rs:480-505): h <- h + resid * moe(xn), xn/h device pointers [H], enqueued on the context's
+ * stream without synchronizing; ids/weights (device, [k]) receive the routing when non-NULL */
+int lastro_layer_add_into(lastro_layer *layer, const float *xn_dev, float *h_dev, float resid, int32_t *ids_dev,
+                          float *weights_dev);
+void lastro_layer_destroy(lastro_layer *layer);
+
+/* ---- whole model: GpuModel (gpu_model.rs:154-455) --------------------------------------------------------------- */
+/* GpuModel::upload (gpu_model.rs:191-242): allocates weights, the paged KV cache for max_len positions and the
+ * step's scratch; tensors are then loaded with lastro_model_load_tensor or lastro_model_fill_synthetic */
+int lastro_model_create(lastro_ctx *ctx, const lastro_model_desc *desc, int32_t max_len, lastro_model **out);
+/* copies one checkpoint tensor (model.rs:99-132 names, e.g. "model.layers.3.self_attn.q_proj.weight",
+ * "model.layers.3.block_sparse_moe.input_linear.weight"); dtype BF16 (uint16 bits) or F32 (norms only) */
+int lastro_model_load_tensor(lastro_model *model, const char *name, int32_t dtype, const int64_t *shape,
+                             int32_t ndim, const void *host);
+/* random-init every tensor on the device from the synthetic generator (weights ~ std, norms 1 + norm_std) */
+int lastro_model_fill_synthetic(lastro_model *model, uint64_t seed, float stddev, float norm_stddev);
+/* GpuModel::step (gpu_model.rs:251-267): one token; logits [V] (already / logits_scaling), the greedy next token
+ * (argmax, last maximum on ties), routes ids/weights [layers*k]; every output may be NULL */
+int lastro_model_step(lastro_model *model, int32_t token, float *logits, int32_t *next_token, int32_t *route_ids,
+                      float *route_weights);
+/* greedy loop of bin/m1b-gulosa.rs:84-110 kept on the device: feeds prompt[0..n_prompt) then generates n_new
+ * tokens, each step's argmax fed back without a host round trip; out_ids [n_new] may be NULL */
+int lastro_model_generate(lastro_model *model, const int32_t *prompt, int32_t n_prompt, int32_t n_new,
+                          int32_t *out_ids);
+/* device-resident greedy decode of n tokens continuing from the last token (no host copies; for timing) */
+int lastro_model_decode(lastro_model *model, int32_t n);
+/* GpuModel::reset (gpu_model.rs:244-247): position 0, page table reset */
+int lastro_model_reset(lastro_model *model);
+int lastro_model_position(const lastro_model *model, int32_t *pos);
+/* per-kernel device time of `steps` decode steps (direct launches with an event between kernels, no graph, no
+ * PDL), averaged per step and summed over layers: kernel_ms[0..6] = qkv_rope, attention, oproj, router, gate_up,
+ * down, head.  Advances the position like lastro_model_decode.  No reference counterpart: measurement only
+ * (the reference's step_probe, gpu_model.rs:275-300, times whole steps). */
+int lastro_model_profile(lastro_model *model, int32_t steps, float *kernel_ms, int32_t n_kinds);
+/* tuning: use CUDA graphs (default 1) and programmatic dependent launch (default 1) */
+int lastro_model_set_options(lastro_model *model, int32_t use_graphs, int32_t use_pdl);
+void lastro_model_destroy(lastro_model *model);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,933 @@
+// C ABI of liblastro_b200.so: context, MoE block (GpuLayer) and whole model (GpuModel).
+//
+// Host-side mirror of the reference's operator API (brenoperucchi/lastro-rust, rust/moe-rt/src/gpu.rs and
+// gpu_model.rs): same objects, same argument meaning, same error policy -- argument errors are refused before any
+// launch, runtime errors synchronize the stream and poison the object (gpu_model.rs:249-267).
+//
+// B200 layout: all weights resident in HBM (the reference's expert cache collapses: the 3B model is 6.4 GB of a
+// 180 GB part), q/k/v projections concatenated into one [qd + 2 kvd, H] matrix, K/V in pages of 64 positions
+// ([page][kv_head][slot][d], bf16 or f32) behind a page table, and the whole decode step captured once as a CUDA
+// graph whose kernels read the token and position from device memory, so one graph serves every position.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/lastro_b200.h"
+#include "kernels.h"
+
+using namespace lastro;
+
+#define LASTRO_VERSION "lastro-b200 0.1.0 (sm_100a)"
+
+struct lastro_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    std::string err;
+};
+
+namespace {
+
+int set_err(lastro_ctx* c, int code, const char* fmt, ...) {
+    if (c) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof buf, fmt, ap);
+        va_end(ap);
+        c->err = buf;
+    }
+    return code;
+}
+
+// synthetic tensor seed: the same formula as the CPU oracle's lo_tensor_seed
+uint64_t mix64_host(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+uint64_t tensor_seed(uint64_t base, int layer, int kind) {
+    return mix64_host(base * 0x9E3779B97F4A7C15ull + ((uint64_t)(uint32_t)(layer + 1) << 8) + (uint64_t)kind + 1u);
+}
+
+float synth_scale(float sd) { return sd / 37837.2265f; }
+
+enum { K_EMBED = 0, K_NORM, K_LN_ATTN, K_LN_MOE, K_Q, K_K, K_V, K_O, K_ROUTER, K_GATE_UP, K_DOWN, K_COUNT };
+
+// Device allocations of one object, freed together.
+struct Arena {
+    std::vector<void*> ptrs;
+    size_t bytes = 0;
+    cudaError_t alloc(void** p, size_t n) {
+        *p = nullptr;
+        if (n == 0) n = 16;
+        cudaError_t e = cudaMalloc(p, n);
+        if (e == cudaSuccess) {
+            ptrs.push_back(*p);
+            bytes += n;
+        }
+        return e;
+    }
+    template <typename T>
+    cudaError_t alloc(T** p, size_t count) {
+        return alloc(reinterpret_cast<void**>(p), count * sizeof(T));
+    }
+    void release() {
+        for (void* p : ptrs) cudaFree(p);
+        ptrs.clear();
+        bytes = 0;
+    }
+};
+
+}  // namespace
+
+// =====================================================================================================================
+// context
+// =====================================================================================================================
+extern "C" const char* lastro_version(void) { return LASTRO_VERSION; }
+
+extern "C" int lastro_ctx_create(int32_t device, void* stream, lastro_ctx** out) {
+    if (!out) return LASTRO_E_ARG;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return LASTRO_E_CUDA;
+    }
+    if (device < 0 || device >= n) return LASTRO_E_ARG;
+    if (cudaSetDevice(device) != cudaSuccess) return LASTRO_E_CUDA;
+    lastro_ctx* c = new lastro_ctx();
+    c->device = device;
+    if (stream) {
+        c->stream = static_cast<cudaStream_t>(stream);
+    } else {
+        if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+            delete c;
+            return LASTRO_E_CUDA;
+        }
+        c->own_stream = true;
+    }
+    *out = c;
+    return LASTRO_OK;
+}
+
+extern "C" void lastro_ctx_destroy(lastro_ctx* c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->own_stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+extern "C" int lastro_ctx_synchronize(lastro_ctx* c) {
+    if (!c) return LASTRO_E_ARG;
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return set_err(c, LASTRO_E_CUDA, "synchronize: %s", cudaGetErrorString(e));
+    return LASTRO_OK;
+}
+
+extern "C" const char* lastro_last_error(const lastro_ctx* c) { return c ? c->err.c_str() : "null context"; }
+
+// =====================================================================================================================
+// MoE block (GpuLayer)
+// =====================================================================================================================
+struct lastro_layer {
+    lastro_ctx* ctx = nullptr;
+    int E = 0, H = 0, I = 0, k = 0;
+    bool poisoned = false;
+    Arena arena;
+    uint16_t *router = nullptr, *gate_up = nullptr, *down = nullptr;
+    float *x = nullptr, *y = nullptr, *logits = nullptr, *weights = nullptr, *a = nullptr;
+    int* ids = nullptr;
+    unsigned int* counter = nullptr;
+};
+
+namespace {
+
+int check_block_shape(lastro_ctx* c, int E, int H, int I, int k) {
+    if (E < 1 || H < 8 || I < 8 || k < 1) return set_err(c, LASTRO_E_ARG, "block shape E=%d H=%d I=%d k=%d", E, H, I, k);
+    if (k > E) return set_err(c, LASTRO_E_ARG, "k=%d > experts=%d", k, E);
+    if (H % 8 || I % 8) return set_err(c, LASTRO_E_UNSUPPORTED, "H=%d and I=%d must be multiples of 8", H, I);
+    if (H > kMaxHidden || I > kMaxInter || E > kMaxExperts || k > kMaxTopK)
+        return set_err(c, LASTRO_E_UNSUPPORTED, "block shape beyond the kernels' limits (H<=%d I<=%d E<=%d k<=%d)",
+                       kMaxHidden, kMaxInter, kMaxExperts, kMaxTopK);
+    if ((size_t)k * I * sizeof(float) > 48 * 1024)
+        return set_err(c, LASTRO_E_UNSUPPORTED, "k*I=%d activations exceed the down kernel's shared memory", k * I);
+    return LASTRO_OK;
+}
+
+// gpu.rs:345-355: synchronize the stream before reporting, then poison
+int cuda_fail(lastro_ctx* c, bool* poisoned, cudaError_t e, const char* what) {
+    cudaStreamSynchronize(c->stream);
+    cudaGetLastError();
+    *poisoned = true;
+    return set_err(c, LASTRO_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define LASTRO_TRY(expr, what)                                                   \
+    do {                                                                         \
+        cudaError_t e_ = (expr);                                                 \
+        if (e_ != cudaSuccess) return cuda_fail(ctx, &obj->poisoned, e_, what);  \
+    } while (0)
+
+// router -> gate_up -> down of one block; `xn` is the block input, `out` receives y (accumulate=0) or h += resid*y
+int enqueue_block(lastro_layer* obj, const float* xn, float* out, float resid, int accumulate) {
+    lastro_ctx* ctx = obj->ctx;
+    cudaStream_t s = ctx->stream;
+    RouterArgs ra{};
+    ra.x = xn;
+    ra.norm_mode = 0;
+    ra.w = obj->router;
+    ra.logits = obj->logits;
+    ra.ids = obj->ids;
+    ra.weights = obj->weights;
+    ra.counter = obj->counter;
+    ra.E = obj->E;
+    ra.H = obj->H;
+    ra.k = obj->k;
+    LASTRO_TRY(launch_router(ra, s, false), "router launch");
+    GateUpArgs ga{};
+    ga.x = xn;
+    ga.norm_mode = 0;
+    ga.ids = obj->ids;
+    ga.w = obj->gate_up;
+    ga.a = obj->a;
+    ga.H = obj->H;
+    ga.I = obj->I;
+    ga.k = obj->k;
+    ga.E = obj->E;
+    LASTRO_TRY(launch_gate_up(ga, s, true), "gate_up launch");
+    DownArgs da{};
+    da.a = obj->a;
+    da.ids = obj->ids;
+    da.weights = obj->weights;
+    da.w = obj->down;
+    da.out = out;
+    da.resid = resid;
+    da.accumulate = accumulate;
+    da.H = obj->H;
+    da.I = obj->I;
+    da.k = obj->k;
+    da.E = obj->E;
+    LASTRO_TRY(launch_down(da, s, true), "down launch");
+    return LASTRO_OK;
+}
+
+}  // namespace
+
+extern "C" int lastro_layer_create(lastro_ctx* ctx, int32_t E, int32_t H, int32_t I, int32_t k, const uint16_t* router,
+                                   const uint16_t* gate_up, const uint16_t* down, lastro_layer** out) {
+    if (!ctx || !out) return LASTRO_E_ARG;
+    *out = nullptr;
+    if (!router || !gate_up || !down) return set_err(ctx, LASTRO_E_ARG, "null weight pointer");
+    int rc = check_block_shape(ctx, E, H, I, k);
+    if (rc) return rc;
+    cudaSetDevice(ctx->device);
+    lastro_layer* obj = new lastro_layer();
+    obj->ctx = ctx;
+    obj->E = E;
+    obj->H = H;
+    obj->I = I;
+    obj->k = k;
+    Arena& A = obj->arena;
+    const size_t nr = (size_t)E * H, ngu = (size_t)E * 2 * I * H, nd = (size_t)E * H * I;
+    if (A.alloc(&obj->router, nr) || A.alloc(&obj->gate_up, ngu) || A.alloc(&obj->down, nd) || A.alloc(&obj->x, H) ||
+        A.alloc(&obj->y, H) || A.alloc(&obj->logits, E) || A.alloc(&obj->weights, k) || A.alloc(&obj->a, (size_t)k * I) ||
+        A.alloc(&obj->ids, k) || A.alloc(&obj->counter, 1)) {
+        cudaGetLastError();
+        A.release();
+        delete obj;
+        return set_err(ctx, LASTRO_E_NOMEM, "layer allocation failed");
+    }
+    cudaError_t e = cudaMemcpyAsync(obj->router, router, nr * 2, cudaMemcpyHostToDevice, ctx->stream);
+    if (!e) e = cudaMemcpyAsync(obj->gate_up, gate_up, ngu * 2, cudaMemcpyHostToDevice, ctx->stream);
+    if (!e) e = cudaMemcpyAsync(obj->down, down, nd * 2, cudaMemcpyHostToDevice, ctx->stream);
+    if (!e) e = cudaMemsetAsync(obj->counter, 0, sizeof(unsigned int), ctx->stream);
+    if (!e) e = cudaMemsetAsync(obj->ids, 0, sizeof(int) * k, ctx->stream);
+    if (!e) e = cudaMemsetAsync(obj->weights, 0, sizeof(float) * k, ctx->stream);
+    if (!e) e = cudaStreamSynchronize(ctx->stream);
+    if (e) {
+        cudaGetLastError();
+        A.release();
+        delete obj;
+        return set_err(ctx, LASTRO_E_CUDA, "layer upload: %s", cudaGetErrorString(e));
+    }
+    *out = obj;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_layer_forward(lastro_layer* obj, const float* x, float* y, int32_t* ids, float* weights,
+                                    float* logits) {
+    if (!obj) return LASTRO_E_ARG;
+    lastro_ctx* ctx = obj->ctx;
+    if (obj->poisoned) return set_err(ctx, LASTRO_E_POISONED, "layer unusable after an earlier error");
+    if (!x) return set_err(ctx, LASTRO_E_ARG, "null x");
+    cudaSetDevice(ctx->device);
+    cudaStream_t s = ctx->stream;
+    LASTRO_TRY(cudaMemcpyAsync(obj->x, x, sizeof(float) * obj->H, cudaMemcpyHostToDevice, s), "x upload");
+    int rc = enqueue_block(obj, obj->x, obj->y, 0.0f, 0);
+    if (rc) return rc;
+    if (y) LASTRO_TRY(cudaMemcpyAsync(y, obj->y, sizeof(float) * obj->H, cudaMemcpyDeviceToHost, s), "y download");
+    if (ids) LASTRO_TRY(cudaMemcpyAsync(ids, obj->ids, sizeof(int) * obj->k, cudaMemcpyDeviceToHost, s), "ids download");
+    if (weights)
+        LASTRO_TRY(cudaMemcpyAsync(weights, obj->weights, sizeof(float) * obj->k, cudaMemcpyDeviceToHost, s), "w download");
+    if (logits)
+        LASTRO_TRY(cudaMemcpyAsync(logits, obj->logits, sizeof(float) * obj->E, cudaMemcpyDeviceToHost, s), "logits");
+    LASTRO_TRY(cudaStreamSynchronize(s), "layer forward");
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_layer_add_into(lastro_layer* obj, const float* xn, float* h, float resid, int32_t* ids,
+                                     float* weights) {
+    if (!obj) return LASTRO_E_ARG;
+    lastro_ctx* ctx = obj->ctx;
+    if (obj->poisoned) return set_err(ctx, LASTRO_E_POISONED, "layer unusable after an earlier error");
+    if (!xn || !h) return set_err(ctx, LASTRO_E_ARG, "null device pointer");
+    cudaSetDevice(ctx->device);
+    cudaStream_t s = ctx->stream;
+    int rc = enqueue_block(obj, xn, h, resid, 1);
+    if (rc) return rc;
+    if (ids) LASTRO_TRY(cudaMemcpyAsync(ids, obj->ids, sizeof(int) * obj->k, cudaMemcpyDeviceToDevice, s), "ids copy");
+    if (weights)
+        LASTRO_TRY(cudaMemcpyAsync(weights, obj->weights, sizeof(float) * obj->k, cudaMemcpyDeviceToDevice, s), "w copy");
+    return LASTRO_OK;
+}
+
+extern "C" void lastro_layer_destroy(lastro_layer* obj) {
+    if (!obj) return;
+    cudaSetDevice(obj->ctx->device);
+    cudaStreamSynchronize(obj->ctx->stream);  // gpu.rs:544-550: kernels may still read the weights
+    obj->arena.release();
+    delete obj;
+}
+
+// =====================================================================================================================
+// whole model (GpuModel)
+// =====================================================================================================================
+namespace {
+
+struct LayerDev {
+    float *ln_attn = nullptr, *ln_moe = nullptr;
+    uint16_t *wqkv = nullptr, *wo = nullptr, *router = nullptr, *gate_up = nullptr, *down = nullptr;
+    void *k_pool = nullptr, *v_pool = nullptr;
+};
+
+constexpr int kPageSize = 64;
+
+}  // namespace
+
+struct lastro_model {
+    lastro_ctx* ctx = nullptr;
+    lastro_model_desc d{};
+    int max_len = 0, qd = 0, kvd = 0, G = 1, max_pages = 0, ns = 1, head_grid = 1;
+    bool poisoned = false;
+    bool use_graphs = true, use_pdl = true;
+    Arena arena;
+    uint16_t* embed = nullptr;
+    float* norm = nullptr;
+    std::vector<LayerDev> L;
+    float* rope_cs = nullptr;
+    int* page_table = nullptr;
+    // per-step state
+    float *h = nullptr, *q = nullptr, *att = nullptr, *part_acc = nullptr, *part_ml = nullptr;
+    float *rlogits = nullptr, *route_w = nullptr, *rnorm = nullptr, *a = nullptr, *logits = nullptr;
+    int *route_ids = nullptr, *d_token = nullptr, *d_pos = nullptr, *d_step = nullptr, *d_out_ids = nullptr;
+    int* d_prompt = nullptr;
+    unsigned int *attn_counters = nullptr, *router_counter = nullptr, *head_counter = nullptr;
+    unsigned long long* head_partial = nullptr;
+    int* h_token = nullptr;  // pinned
+    int pos_host = 0;
+    std::vector<char> loaded;  // per (layer, kind)
+    cudaGraphExec_t graph = nullptr;
+};
+
+namespace {
+
+int model_fail(lastro_model* m, cudaError_t e, const char* what) { return cuda_fail(m->ctx, &m->poisoned, e, what); }
+
+#define MTRY(expr, what)                                        \
+    do {                                                        \
+        cudaError_t e_ = (expr);                                \
+        if (e_ != cudaSuccess) return model_fail(m, e_, what);  \
+    } while (0)
+
+size_t kv_elem_bytes(const lastro_model* m) { return m->d.kv_dtype == LASTRO_DTYPE_F32 ? 4 : 2; }
+
+char& loaded_flag(lastro_model* m, int layer, int kind) { return m->loaded[(size_t)(layer + 1) * K_COUNT + kind]; }
+
+const char* kind_name(int kind) {
+    static const char* names[K_COUNT] = {"model.embed_tokens.weight",
+                                         "model.norm.weight",
+                                         "input_layernorm.weight",
+                                         "post_attention_layernorm.weight",
+                                         "self_attn.q_proj.weight",
+                                         "self_attn.k_proj.weight",
+                                         "self_attn.v_proj.weight",
+                                         "self_attn.o_proj.weight",
+                                         "block_sparse_moe.router.layer.weight",
+                                         "block_sparse_moe.input_linear.weight",
+                                         "block_sparse_moe.output_linear.weight"};
+    return names[kind];
+}
+
+int missing_tensor(lastro_model* m) {
+    if (!loaded_flag(m, -1, K_EMBED)) return set_err(m->ctx, LASTRO_E_STATE, "tensor %s not loaded", kind_name(K_EMBED));
+    if (!loaded_flag(m, -1, K_NORM)) return set_err(m->ctx, LASTRO_E_STATE, "tensor %s not loaded", kind_name(K_NORM));
+    for (int l = 0; l < m->d.layers; ++l)
+        for (int k = K_LN_ATTN; k < K_COUNT; ++k)
+            if (!loaded_flag(m, l, k))
+                return set_err(m->ctx, LASTRO_E_STATE, "tensor model.layers.%d.%s not loaded", l, kind_name(k));
+    return LASTRO_OK;
+}
+
+// Kernel kinds of one step, in launch order within a layer (the head closes the step).
+enum { KK_QKV = 0, KK_ATTN, KK_OPROJ, KK_ROUTER, KK_GATE_UP, KK_DOWN, KK_HEAD, KK_COUNT };
+
+// Optional per-launch events: ev[0] before the first launch, ev[i + 1] after launch i.
+struct StepEvents {
+    cudaEvent_t* ev = nullptr;
+    int next = 0;
+};
+
+cudaError_t mark(StepEvents* pe, cudaStream_t s) {
+    if (!pe) return cudaSuccess;
+    return cudaEventRecord(pe->ev[pe->next++], s);
+}
+
+// Enqueue the kernels of one decode step; the token is read from d_token, the position from d_pos.
+cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullptr) {
+    const lastro_model_desc& d = m->d;
+    const bool pdl = m->use_pdl && !pe;
+    cudaError_t e;
+    if ((e = mark(pe, s)) != cudaSuccess) return e;
+    for (int l = 0; l < d.layers; ++l) {
+        const LayerDev& L = m->L[l];
+        QkvArgs qa{};
+        qa.h = m->h;
+        qa.h_write = m->h;
+        qa.embed = m->embed;
+        qa.token = m->d_token;
+        qa.emb_mult = d.embedding_multiplier;
+        qa.embed_mode = (l == 0);
+        qa.ln = L.ln_attn;
+        qa.w = L.wqkv;
+        qa.rope_cs = m->rope_cs;
+        qa.pos = m->d_pos;
+        qa.q_out = m->q;
+        qa.k_pool = L.k_pool;
+        qa.v_pool = L.v_pool;
+        qa.page_table = m->page_table;
+        qa.page_size = kPageSize;
+        qa.kv_f32 = d.kv_dtype == LASTRO_DTYPE_F32;
+        qa.H = d.hidden;
+        qa.qd = m->qd;
+        qa.kvd = m->kvd;
+        qa.d = d.head_dim;
+        qa.kv_heads = d.kv_heads;
+        qa.eps = d.eps;
+        if ((e = launch_qkv_rope(qa, s, pdl && l > 0)) != cudaSuccess) return e;
+        if ((e = mark(pe, s)) != cudaSuccess) return e;
+
+        AttnArgs aa{};
+        aa.q = m->q;
+        aa.k_pool = L.k_pool;
+        aa.v_pool = L.v_pool;
+        aa.page_table = m->page_table;
+        aa.page_size = kPageSize;
+        aa.kv_f32 = qa.kv_f32;
+        aa.pos = m->d_pos;
+        aa.part_acc = m->part_acc;
+        aa.part_ml = m->part_ml;
+        aa.counters = m->attn_counters;
+        aa.att_out = m->att;
+        aa.kv_heads = d.kv_heads;
+        aa.G = m->G;
+        aa.d = d.head_dim;
+        aa.ns = m->ns;
+        aa.scale = d.attention_multiplier;
+        if ((e = launch_attention(aa, s, pdl)) != cudaSuccess) return e;
+        if ((e = mark(pe, s)) != cudaSuccess) return e;
+
+        OprojArgs oa{};
+        oa.att = m->att;
+        oa.w = L.wo;
+        oa.h = m->h;
+        oa.resid = d.residual_multiplier;
+        oa.H = d.hidden;
+        oa.qd = m->qd;
+        if ((e = launch_oproj(oa, s, pdl)) != cudaSuccess) return e;
+        if ((e = mark(pe, s)) != cudaSuccess) return e;
+
+        RouterArgs ra{};
+        ra.x = m->h;
+        ra.ln = L.ln_moe;
+        ra.eps = d.eps;
+        ra.norm_mode = 1;
+        ra.w = L.router;
+        ra.logits = m->rlogits;
+        ra.ids = m->route_ids + (size_t)l * d.k;
+        ra.weights = m->route_w + (size_t)l * d.k;
+        ra.rnorm_out = m->rnorm;
+        ra.counter = m->router_counter;
+        ra.E = d.experts;
+        ra.H = d.hidden;
+        ra.k = d.k;
+        if ((e = launch_router(ra, s, pdl)) != cudaSuccess) return e;
+        if ((e = mark(pe, s)) != cudaSuccess) return e;
+
+        GateUpArgs ga{};
+        ga.x = m->h;
+        ga.ln = L.ln_moe;
+        ga.rnorm = m->rnorm;
+        ga.norm_mode = 1;
+        ga.ids = ra.ids;
+        ga.w = L.gate_up;
+        ga.a = m->a;
+        ga.H = d.hidden;
+        ga.I = d.inter;
+        ga.k = d.k;
+        ga.E = d.experts;
+        if ((e = launch_gate_up(ga, s, pdl)) != cudaSuccess) return e;
+        if ((e = mark(pe, s)) != cudaSuccess) return e;
+
+        DownArgs da{};
+        da.a = m->a;
+        da.ids = ra.ids;
+        da.weights = ra.weights;
+        da.w = L.down;
+        da.out = m->h;
+        da.resid = d.residual_multiplier;
+        da.accumulate = 1;
+        da.H = d.hidden;
+        da.I = d.inter;
+        da.k = d.k;
+        da.E = d.experts;
+        if ((e = launch_down(da, s, pdl)) != cudaSuccess) return e;
+        if ((e = mark(pe, s)) != cudaSuccess) return e;
+    }
+    HeadArgs ha{};
+    ha.h = m->h;
+    ha.ln = m->norm;
+    ha.eps = d.eps;
+    ha.w = m->embed;
+    ha.logits_scaling = d.logits_scaling;
+    ha.logits_out = m->logits;
+    ha.partial = m->head_partial;
+    ha.counter = m->head_counter;
+    ha.token_out = m->d_token;
+    ha.out_ids = m->d_out_ids;
+    ha.out_cap = m->max_len + 1;
+    ha.step = m->d_step;
+    ha.pos = m->d_pos;
+    ha.V = d.vocab;
+    ha.H = d.hidden;
+    if ((e = launch_head(ha, s, pdl, nullptr)) != cudaSuccess) return e;
+    return mark(pe, s);
+}
+
+// one step on the stream: graph replay (captured at first use) or direct launches
+int run_step(lastro_model* m) {
+    cudaStream_t s = m->ctx->stream;
+    if (!m->use_graphs) {
+        MTRY(enqueue_step(m, s), "step launch");
+        return LASTRO_OK;
+    }
+    if (!m->graph) {
+        cudaGraph_t g = nullptr;
+        MTRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
+        cudaError_t e = enqueue_step(m, s);
+        cudaError_t e2 = cudaStreamEndCapture(s, &g);
+        if (e == cudaSuccess) e = e2;
+        if (e != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            return model_fail(m, e, "step capture");
+        }
+        e = cudaGraphInstantiate(&m->graph, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) {
+            m->graph = nullptr;
+            return model_fail(m, e, "graph instantiate");
+        }
+    }
+    MTRY(cudaGraphLaunch(m->graph, s), "graph launch");
+    return LASTRO_OK;
+}
+
+int check_ready(lastro_model* m) {
+    if (m->poisoned) return set_err(m->ctx, LASTRO_E_POISONED, "model unusable after an earlier error");
+    return missing_tensor(m);
+}
+
+// host copy of the paged layout's identity page table
+int init_page_table(lastro_model* m) {
+    std::vector<int> pt(m->max_pages);
+    for (int i = 0; i < m->max_pages; ++i) pt[i] = i;
+    MTRY(cudaMemcpyAsync(m->page_table, pt.data(), sizeof(int) * pt.size(), cudaMemcpyHostToDevice, m->ctx->stream),
+         "page table");
+    MTRY(cudaStreamSynchronize(m->ctx->stream), "page table");
+    return LASTRO_OK;
+}
+
+}  // namespace
+
+extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* desc, int32_t max_len, lastro_model** out) {
+    if (!ctx || !desc || !out) return LASTRO_E_ARG;
+    *out = nullptr;
+    const lastro_model_desc& d = *desc;
+    if (d.layers < 1 || d.heads < 1 || d.kv_heads < 1 || d.vocab < 2 || max_len < 1)
+        return set_err(ctx, LASTRO_E_ARG, "bad model description");
+    if (d.heads % d.kv_heads) return set_err(ctx, LASTRO_E_ARG, "heads %d not a multiple of kv_heads %d", d.heads, d.kv_heads);
+    if (d.head_dim != kHeadDim) return set_err(ctx, LASTRO_E_UNSUPPORTED, "head_dim %d (kernels implement %d)", d.head_dim, kHeadDim);
+    const int G = d.heads / d.kv_heads;
+    if (!(G == 1 || G == 2 || G == 3 || G == 4 || G == 6 || G == 8))
+        return set_err(ctx, LASTRO_E_UNSUPPORTED, "GQA group %d", G);
+    int rc = check_block_shape(ctx, d.experts, d.hidden, d.inter, d.k);
+    if (rc) return rc;
+    if (d.heads * d.head_dim > kMaxHidden) return set_err(ctx, LASTRO_E_UNSUPPORTED, "heads*head_dim > %d", kMaxHidden);
+    if (d.weight_dtype != LASTRO_DTYPE_BF16) return set_err(ctx, LASTRO_E_UNSUPPORTED, "weight dtype %d", d.weight_dtype);
+    if (d.kv_dtype != LASTRO_DTYPE_BF16 && d.kv_dtype != LASTRO_DTYPE_F32)
+        return set_err(ctx, LASTRO_E_UNSUPPORTED, "kv dtype %d", d.kv_dtype);
+    if (!(d.eps >= 0.0f) || !(d.logits_scaling != 0.0f) || !(d.rope_theta > 0.0f))
+        return set_err(ctx, LASTRO_E_ARG, "bad eps / logits_scaling / rope_theta");
+
+    cudaSetDevice(ctx->device);
+    lastro_model* m = new lastro_model();
+    m->ctx = ctx;
+    m->d = d;
+    m->max_len = max_len;
+    m->qd = d.heads * d.head_dim;
+    m->kvd = d.kv_heads * d.head_dim;
+    m->G = G;
+    m->max_pages = (max_len + kPageSize - 1) / kPageSize;
+    m->ns = std::min(64, std::max(1, (2 * 148 + d.kv_heads - 1) / d.kv_heads));
+    m->head_grid = head_grid(d.vocab);
+    m->loaded.assign((size_t)(d.layers + 1) * K_COUNT, 0);
+    m->L.resize(d.layers);
+    const size_t H = d.hidden, I = d.inter, E = d.experts, V = d.vocab;
+    const size_t kvpool = (size_t)m->max_pages * d.kv_heads * kPageSize * d.head_dim * kv_elem_bytes(m);
+    Arena& A = m->arena;
+    bool bad = A.alloc(&m->embed, V * H) || A.alloc(&m->norm, H);
+    for (int l = 0; l < d.layers && !bad; ++l) {
+        LayerDev& L = m->L[l];
+        bad = A.alloc(&L.ln_attn, H) || A.alloc(&L.ln_moe, H) || A.alloc(&L.wqkv, (size_t)(m->qd + 2 * m->kvd) * H) ||
+              A.alloc(&L.wo, H * m->qd) || A.alloc(&L.router, E * H) || A.alloc(&L.gate_up, E * 2 * I * H) ||
+              A.alloc(&L.down, E * H * I) || A.alloc(&L.k_pool, kvpool) || A.alloc(&L.v_pool, kvpool);
+    }
+    bad = bad || A.alloc(&m->rope_cs, (size_t)max_len * d.head_dim) || A.alloc(&m->page_table, m->max_pages) ||
+          A.alloc(&m->h, H) || A.alloc(&m->q, m->qd) || A.alloc(&m->att, m->qd) ||
+          A.alloc(&m->part_acc, (size_t)d.kv_heads * m->ns * G * d.head_dim) ||
+          A.alloc(&m->part_ml, (size_t)d.kv_heads * m->ns * G * 2) || A.alloc(&m->rlogits, E) ||
+          A.alloc(&m->route_w, (size_t)d.layers * d.k) || A.alloc(&m->route_ids, (size_t)d.layers * d.k) ||
+          A.alloc(&m->rnorm, 1) || A.alloc(&m->a, (size_t)d.k * I) || A.alloc(&m->logits, V) ||
+          A.alloc(&m->d_token, 1) || A.alloc(&m->d_pos, 1) || A.alloc(&m->d_step, 1) ||
+          A.alloc(&m->d_out_ids, (size_t)max_len + 1) || A.alloc(&m->d_prompt, (size_t)max_len + 1) ||
+          A.alloc(&m->attn_counters, d.kv_heads) || A.alloc(&m->router_counter, 1) || A.alloc(&m->head_counter, 1) ||
+          A.alloc(&m->head_partial, m->head_grid);
+    if (bad || cudaMallocHost(&m->h_token, sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        A.release();
+        delete m;
+        return set_err(ctx, LASTRO_E_NOMEM, "model allocation failed");
+    }
+    cudaStream_t s = ctx->stream;
+    cudaError_t e = cudaSuccess;
+    for (int l = 0; l < d.layers && !e; ++l) {
+        e = cudaMemsetAsync(m->L[l].k_pool, 0, kvpool, s);
+        if (!e) e = cudaMemsetAsync(m->L[l].v_pool, 0, kvpool, s);
+    }
+    for (void* p : {(void*)m->attn_counters, (void*)m->router_counter, (void*)m->head_counter, (void*)m->d_pos,
+                    (void*)m->d_step, (void*)m->d_token})
+        if (!e) e = cudaMemsetAsync(p, 0, p == (void*)m->attn_counters ? sizeof(unsigned) * d.kv_heads : sizeof(int), s);
+    if (!e) e = cudaMemsetAsync(m->route_ids, 0, sizeof(int) * d.layers * d.k, s);
+    if (!e) e = cudaMemsetAsync(m->route_w, 0, sizeof(float) * d.layers * d.k, s);
+    // model.rs:63-73: inv_freq = 1/theta^(2j/d) and cos/sin of pos*inv_freq, in f32 on the host
+    std::vector<float> cs((size_t)max_len * d.head_dim);
+    const int half = d.head_dim / 2;
+    for (int p = 0; p < max_len; ++p)
+        for (int j = 0; j < half; ++j) {
+            const float inv = 1.0f / powf(d.rope_theta, (float)(2 * j) / (float)d.head_dim);
+            const float f = (float)p * inv;
+            cs[(size_t)p * d.head_dim + j] = cosf(f);
+            cs[(size_t)p * d.head_dim + half + j] = sinf(f);
+        }
+    if (!e) e = cudaMemcpyAsync(m->rope_cs, cs.data(), sizeof(float) * cs.size(), cudaMemcpyHostToDevice, s);
+    if (!e) e = cudaStreamSynchronize(s);
+    if (e) {
+        cudaGetLastError();
+        A.release();
+        cudaFreeHost(m->h_token);
+        delete m;
+        return set_err(ctx, LASTRO_E_CUDA, "model init: %s", cudaGetErrorString(e));
+    }
+    if (init_page_table(m)) {
+        A.release();
+        cudaFreeHost(m->h_token);
+        delete m;
+        return LASTRO_E_CUDA;
+    }
+    *out = m;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_model_load_tensor(lastro_model* m, const char* name, int32_t dtype, const int64_t* shape,
+                                        int32_t ndim, const void* host) {
+    if (!m) return LASTRO_E_ARG;
+    lastro_ctx* ctx = m->ctx;
+    if (m->poisoned) return set_err(ctx, LASTRO_E_POISONED, "model unusable after an earlier error");
+    if (!name || !host || (!shape && ndim > 0)) return set_err(ctx, LASTRO_E_ARG, "null argument");
+    const lastro_model_desc& d = m->d;
+    const int64_t H = d.hidden, I = d.inter, E = d.experts, V = d.vocab, qd = m->qd, kvd = m->kvd;
+    int layer = -1, kind = -1;
+    const char* rest = nullptr;
+    if (!strcmp(name, kind_name(K_EMBED)))
+        kind = K_EMBED;
+    else if (!strcmp(name, kind_name(K_NORM)))
+        kind = K_NORM;
+    else if (!strncmp(name, "model.layers.", 13)) {
+        char* endp = nullptr;
+        long l = strtol(name + 13, &endp, 10);
+        if (endp == name + 13 || *endp != '.' || l < 0 || l >= d.layers)
+            return set_err(ctx, LASTRO_E_ARG, "tensor %s: bad layer index", name);
+        layer = (int)l;
+        rest = endp + 1;
+        for (int k = K_LN_ATTN; k < K_COUNT; ++k)
+            if (!strcmp(rest, kind_name(k))) kind = k;
+    }
+    if (kind < 0) return set_err(ctx, LASTRO_E_ARG, "unknown tensor %s", name);
+    std::vector<int64_t> want;
+    void* dst = nullptr;
+    bool is_norm = false;
+    const LayerDev* L = layer >= 0 ? &m->L[layer] : nullptr;
+    switch (kind) {
+    case K_EMBED: want = {V, H}; dst = m->embed; break;
+    case K_NORM: want = {H}; dst = m->norm; is_norm = true; break;
+    case K_LN_ATTN: want = {H}; dst = L->ln_attn; is_norm = true; break;
+    case K_LN_MOE: want = {H}; dst = L->ln_moe; is_norm = true; break;
+    case K_Q: want = {qd, H}; dst = L->wqkv; break;
+    case K_K: want = {kvd, H}; dst = L->wqkv + (size_t)qd * H; break;
+    case K_V: want = {kvd, H}; dst = L->wqkv + (size_t)(qd + kvd) * H; break;
+    case K_O: want = {H, qd}; dst = L->wo; break;
+    case K_ROUTER: want = {E, H}; dst = L->router; break;
+    case K_GATE_UP: want = {E, 2 * I, H}; dst = L->gate_up; break;
+    case K_DOWN: want = {E, H, I}; dst = L->down; break;
+    }
+    bool shape_ok = ndim == (int32_t)want.size();
+    for (int i = 0; shape_ok && i < ndim; ++i) shape_ok = shape[i] == want[i];
+    if (!shape_ok) return set_err(ctx, LASTRO_E_ARG, "tensor %s: unexpected shape", name);
+    size_t n = 1;
+    for (int64_t v : want) n *= (size_t)v;
+    cudaSetDevice(ctx->device);
+    cudaStream_t s = ctx->stream;
+    if (is_norm) {
+        std::vector<float> f(n);
+        if (dtype == LASTRO_DTYPE_BF16) {
+            const uint16_t* b = static_cast<const uint16_t*>(host);
+            for (size_t i = 0; i < n; ++i) {
+                uint32_t u = (uint32_t)b[i] << 16;
+                memcpy(&f[i], &u, 4);
+            }
+        } else if (dtype == LASTRO_DTYPE_F32) {
+            memcpy(f.data(), host, n * 4);
+        } else {
+            return set_err(ctx, LASTRO_E_ARG, "tensor %s: dtype %d", name, dtype);
+        }
+        MTRY(cudaMemcpyAsync(dst, f.data(), n * 4, cudaMemcpyHostToDevice, s), "tensor upload");
+        MTRY(cudaStreamSynchronize(s), "tensor upload");
+    } else {
+        if (dtype != LASTRO_DTYPE_BF16) return set_err(ctx, LASTRO_E_ARG, "tensor %s: dtype %d (bf16 expected)", name, dtype);
+        MTRY(cudaMemcpyAsync(dst, host, n * 2, cudaMemcpyHostToDevice, s), "tensor upload");
+        MTRY(cudaStreamSynchronize(s), "tensor upload");
+    }
+    loaded_flag(m, layer, kind) = 1;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_model_fill_synthetic(lastro_model* m, uint64_t seed, float sd, float norm_sd) {
+    if (!m) return LASTRO_E_ARG;
+    lastro_ctx* ctx = m->ctx;
+    if (m->poisoned) return set_err(ctx, LASTRO_E_POISONED, "model unusable after an earlier error");
+    cudaSetDevice(ctx->device);
+    cudaStream_t s = ctx->stream;
+    const lastro_model_desc& d = m->d;
+    const size_t H = d.hidden, I = d.inter, E = d.experts, V = d.vocab, qd = m->qd, kvd = m->kvd;
+    const float sc = synth_scale(sd), nsc = synth_scale(norm_sd);
+    MTRY(launch_synth_bf16(m->embed, V * H, tensor_seed(seed, -1, K_EMBED), sc, 0.0f, s), "synth");
+    MTRY(launch_synth_norm_f32(m->norm, H, tensor_seed(seed, -1, K_NORM), nsc, s), "synth");
+    for (int l = 0; l < d.layers; ++l) {
+        LayerDev& L = m->L[l];
+        MTRY(launch_synth_norm_f32(L.ln_attn, H, tensor_seed(seed, l, K_LN_ATTN), nsc, s), "synth");
+        MTRY(launch_synth_norm_f32(L.ln_moe, H, tensor_seed(seed, l, K_LN_MOE), nsc, s), "synth");
+        MTRY(launch_synth_bf16(L.wqkv, qd * H, tensor_seed(seed, l, K_Q), sc, 0.0f, s), "synth");
+        MTRY(launch_synth_bf16(L.wqkv + qd * H, kvd * H, tensor_seed(seed, l, K_K), sc, 0.0f, s), "synth");
+        MTRY(launch_synth_bf16(L.wqkv + (qd + kvd) * H, kvd * H, tensor_seed(seed, l, K_V), sc, 0.0f, s), "synth");
+        MTRY(launch_synth_bf16(L.wo, H * qd, tensor_seed(seed, l, K_O), sc, 0.0f, s), "synth");
+        MTRY(launch_synth_bf16(L.router, E * H, tensor_seed(seed, l, K_ROUTER), sc, 0.0f, s), "synth");
+        MTRY(launch_synth_bf16(L.gate_up, E * 2 * I * H, tensor_seed(seed, l, K_GATE_UP), sc, 0.0f, s), "synth");
+        MTRY(launch_synth_bf16(L.down, E * H * I, tensor_seed(seed, l, K_DOWN), sc, 0.0f, s), "synth");
+    }
+    MTRY(cudaStreamSynchronize(s), "synth");
+    std::fill(m->loaded.begin(), m->loaded.end(), 1);
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_model_step(lastro_model* m, int32_t token, float* logits, int32_t* next_token, int32_t* route_ids,
+                                 float* route_weights) {
+    if (!m) return LASTRO_E_ARG;
+    lastro_ctx* ctx = m->ctx;
+    int rc = check_ready(m);
+    if (rc) return rc;
+    // gpu_model.rs:252-257: refused before any launch, the model stays usable
+    if (m->pos_host >= m->max_len) return set_err(ctx, LASTRO_E_FULL, "KV cache full (%d positions)", m->max_len);
+    if (token < 0 || token >= m->d.vocab) return set_err(ctx, LASTRO_E_ARG, "token %d outside the vocabulary (%d)", token, m->d.vocab);
+    cudaSetDevice(ctx->device);
+    cudaStream_t s = ctx->stream;
+    *m->h_token = token;
+    MTRY(cudaMemcpyAsync(m->d_token, m->h_token, sizeof(int), cudaMemcpyHostToDevice, s), "token upload");
+    rc = run_step(m);
+    if (rc) return rc;
+    const lastro_model_desc& d = m->d;
+    if (logits) MTRY(cudaMemcpyAsync(logits, m->logits, sizeof(float) * d.vocab, cudaMemcpyDeviceToHost, s), "logits");
+    if (next_token) MTRY(cudaMemcpyAsync(next_token, m->d_token, sizeof(int), cudaMemcpyDeviceToHost, s), "token");
+    if (route_ids)
+        MTRY(cudaMemcpyAsync(route_ids, m->route_ids, sizeof(int) * d.layers * d.k, cudaMemcpyDeviceToHost, s), "routes");
+    if (route_weights)
+        MTRY(cudaMemcpyAsync(route_weights, m->route_w, sizeof(float) * d.layers * d.k, cudaMemcpyDeviceToHost, s), "routes");
+    MTRY(cudaStreamSynchronize(s), "step");
+    m->pos_host += 1;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_model_generate(lastro_model* m, const int32_t* prompt, int32_t n_prompt, int32_t n_new,
+                                     int32_t* out_ids) {
+    if (!m) return LASTRO_E_ARG;
+    lastro_ctx* ctx = m->ctx;
+    int rc = check_ready(m);
+    if (rc) return rc;
+    if (n_prompt < 1 || n_new < 0 || !prompt) return set_err(ctx, LASTRO_E_ARG, "generate needs a prompt");
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= m->d.vocab) return set_err(ctx, LASTRO_E_ARG, "prompt token %d out of range", prompt[i]);
+    const int steps = n_prompt + (n_new > 0 ? n_new - 1 : 0);
+    if (m->pos_host + steps > m->max_len) return set_err(ctx, LASTRO_E_FULL, "generate would overflow the KV cache");
+    cudaSetDevice(ctx->device);
+    cudaStream_t s = ctx->stream;
+    MTRY(cudaMemcpyAsync(m->d_prompt, prompt, sizeof(int) * n_prompt, cudaMemcpyHostToDevice, s), "prompt upload");
+    MTRY(cudaMemsetAsync(m->d_step, 0, sizeof(int), s), "step reset");
+    for (int i = 0; i < n_prompt; ++i) {
+        MTRY(cudaMemcpyAsync(m->d_token, m->d_prompt + i, sizeof(int), cudaMemcpyDeviceToDevice, s), "token");
+        rc = run_step(m);
+        if (rc) return rc;
+    }
+    for (int i = 1; i < n_new; ++i) {
+        rc = run_step(m);
+        if (rc) return rc;
+    }
+    if (out_ids && n_new > 0)
+        MTRY(cudaMemcpyAsync(out_ids, m->d_out_ids + (n_prompt - 1), sizeof(int) * n_new, cudaMemcpyDeviceToHost, s),
+             "ids download");
+    MTRY(cudaStreamSynchronize(s), "generate");
+    m->pos_host += steps;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_model_decode(lastro_model* m, int32_t n) {
+    if (!m) return LASTRO_E_ARG;
+    lastro_ctx* ctx = m->ctx;
+    int rc = check_ready(m);
+    if (rc) return rc;
+    if (n < 0) return set_err(ctx, LASTRO_E_ARG, "negative step count");
+    if (m->pos_host + n > m->max_len) return set_err(ctx, LASTRO_E_FULL, "decode would overflow the KV cache");
+    cudaSetDevice(ctx->device);
+    MTRY(cudaMemsetAsync(m->d_step, 0, sizeof(int), ctx->stream), "step reset");
+    for (int i = 0; i < n; ++i) {
+        rc = run_step(m);
+        if (rc) return rc;
+    }
+    m->pos_host += n;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_model_reset(lastro_model* m) {
+    if (!m) return LASTRO_E_ARG;
+    if (m->poisoned) return set_err(m->ctx, LASTRO_E_POISONED, "model unusable after an earlier error");
+    cudaSetDevice(m->ctx->device);
+    cudaStream_t s = m->ctx->stream;
+    MTRY(cudaMemsetAsync(m->d_pos, 0, sizeof(int), s), "reset");
+    MTRY(cudaMemsetAsync(m->d_step, 0, sizeof(int), s), "reset");
+    MTRY(cudaStreamSynchronize(s), "reset");
+    m->pos_host = 0;
+    return init_page_table(m);
+}
+
+extern "C" int lastro_model_position(const lastro_model* m, int32_t* pos) {
+    if (!m || !pos) return LASTRO_E_ARG;
+    *pos = m->pos_host;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_model_profile(lastro_model* m, int32_t steps, float* kernel_ms, int32_t n_kinds) {
+    if (!m) return LASTRO_E_ARG;
+    lastro_ctx* ctx = m->ctx;
+    int rc = check_ready(m);
+    if (rc) return rc;
+    if (steps < 1 || !kernel_ms || n_kinds < KK_COUNT) return set_err(ctx, LASTRO_E_ARG, "profile arguments");
+    if (m->pos_host + steps > m->max_len) return set_err(ctx, LASTRO_E_FULL, "profile would overflow the KV cache");
+    cudaSetDevice(ctx->device);
+    cudaStream_t s = ctx->stream;
+    const int launches = KK_HEAD + (KK_DOWN + 1) * (m->d.layers - 1) + 1;  // 6 per layer + head
+    const int n_ev = 6 * m->d.layers + 2;
+    (void)launches;
+    std::vector<cudaEvent_t> ev(n_ev, nullptr);
+    for (auto& e : ev) MTRY(cudaEventCreate(&e), "event create");
+    std::vector<double> acc(KK_COUNT, 0.0);
+    int result = LASTRO_OK;
+    for (int st = 0; st < steps && result == LASTRO_OK; ++st) {
+        StepEvents pe;
+        pe.ev = ev.data();
+        cudaError_t e = enqueue_step(m, s, &pe);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) {
+            result = model_fail(m, e, "profile step");
+            break;
+        }
+        for (int i = 0; i + 1 < pe.next; ++i) {
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
+            const int kind = (i == pe.next - 2) ? KK_HEAD : (i % 6);
+            acc[kind] += ms;
+        }
+        m->pos_host += 1;
+    }
+    for (auto& e : ev) cudaEventDestroy(e);
+    for (int k = 0; k < KK_COUNT; ++k) kernel_ms[k] = (float)(acc[k] / steps);
+    return result;
+}
+
+extern "C" int lastro_model_set_options(lastro_model* m, int32_t use_graphs, int32_t use_pdl) {
+    if (!m) return LASTRO_E_ARG;
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    if (m->graph) {
+        cudaGraphExecDestroy(m->graph);
+        m->graph = nullptr;
+    }
+    m->use_graphs = use_graphs != 0;
+    m->use_pdl = use_pdl != 0;
+    return LASTRO_OK;
+}
+
+extern "C" void lastro_model_destroy(lastro_model* m) {
+    if (!m) return;
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);  // gpu_model.rs:448-455
+    if (m->graph) cudaGraphExecDestroy(m->graph);
+    m->arena.release();
+    if (m->h_token) cudaFreeHost(m->h_token);
+    delete m;
+}

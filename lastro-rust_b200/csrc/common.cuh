@@ -1,0 +1,107 @@
+// Shared device helpers of the lastro-b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define LDEV __device__ __forceinline__
+
+namespace lastro {
+
+constexpr int kWarp = 32;
+
+// ---- programmatic dependent launch (PDL) -----------------------------------------------------------------------
+// Every kernel of the decode chain reads only immutable weights before pdl_wait(); activations written by the
+// previous kernel are read, and any buffer is written, only after it.  griddepcontrol.wait returns once the
+// preceding grid has completed and its memory is visible; launch_dependents lets the next kernel of the stream be
+// scheduled early so that its weight loads overlap this kernel.
+LDEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+LDEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---- loads ------------------------------------------------------------------------------------------------------
+// 16-byte weight load, read once per step: non-coherent path, no L1 allocation.
+LDEV uint4 ld_weight(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// Load of data written by another CTA of the same grid (after a fence/ticket): bypass L1.
+LDEV float ld_cg(const float* p) { return __ldcg(p); }
+LDEV int ld_cg(const int* p) { return __ldcg(p); }
+
+// ---- bf16 -------------------------------------------------------------------------------------------------------
+LDEV float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
+LDEV float bf_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+
+// sum_{i<8} w[i] * x[i] for 8 bf16 weights packed in a uint4 and 8 f32 activations
+LDEV float dot8(uint4 w, float4 xa, float4 xb, float acc) {
+    acc = fmaf(bf_lo(w.x), xa.x, acc);
+    acc = fmaf(bf_hi(w.x), xa.y, acc);
+    acc = fmaf(bf_lo(w.y), xa.z, acc);
+    acc = fmaf(bf_hi(w.y), xa.w, acc);
+    acc = fmaf(bf_lo(w.z), xb.x, acc);
+    acc = fmaf(bf_hi(w.z), xb.y, acc);
+    acc = fmaf(bf_lo(w.w), xb.z, acc);
+    acc = fmaf(bf_hi(w.w), xb.w, acc);
+    return acc;
+}
+
+LDEV uint16_t f32_to_bf16_rne(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x7fffffu)) return (uint16_t)((u >> 16) | 0x40);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+// ---- reductions ---------------------------------------------------------------------------------------------------
+LDEV float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+LDEV float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Key that orders floats like Rust's f32::total_cmp when compared as signed integers.
+LDEV int32_t total_key(float f) {
+    int32_t x = __float_as_int(f);
+    return x ^ (int32_t)(((uint32_t)(x >> 31)) >> 1);
+}
+
+// Block-wide sum; `red` holds >= blockDim.x/32 floats.  All threads get the result.
+LDEV float block_sum(float v, float* red) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[wid] = v;
+    __syncthreads();
+    float t = 0.0f;
+    for (int i = 0; i < nw; ++i) t += red[i];
+    return t;
+}
+
+// Last-CTA election: every CTA calls this once after writing its results; returns true in exactly one CTA (the
+// last to arrive), which may then read every other CTA's results.  The counter is reset for the next launch.
+LDEV bool last_block_arrives(unsigned int* counter, unsigned int total, bool* flag_smem) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned int t = atomicAdd(counter, 1u);
+        bool last = (t == total - 1);
+        if (last) atomicExch(counter, 0u);
+        *flag_smem = last;
+    }
+    __syncthreads();
+    bool last = *flag_smem;
+    if (last) __threadfence();
+    return last;
+}
+
+}  // namespace lastro

@@ -1,0 +1,711 @@
+// Batch-1 Granite-MoE decode kernels for sm_100a.
+//
+// Design (B200): every kernel is one streaming pass over bf16 weights with 16-byte non-coherent loads, a warp per
+// output row (or row pair), f32 activations staged in shared memory and warp-shuffle reductions.  Weight loads that
+// do not depend on the previous kernel are issued before griddepcontrol.wait, so with programmatic dependent launch
+// a kernel's HBM traffic overlaps the tail of its predecessor.  Cross-CTA reductions (router top-k, attention split
+// merge, lm_head argmax) use a last-CTA ticket instead of a second launch.
+//
+// Reference behaviour restated (brenoperucchi/lastro-rust, rust/moe-rt/src):
+//   RMSNorm  model.rs:141-145   RoPE rotate_half model.rs:147-158   attention model.rs:203-222
+//   routing  block.rs:79-89     SwiGLU cpu.rs:154-158               experts cpu.rs:205-240
+//   step     model.rs:181-243   argmax (last maximum) bin/m1b-gulosa.rs:22-24
+#include "common.cuh"
+#include "kernels.h"
+
+namespace lastro {
+
+namespace {
+
+template <typename Kern, typename... Args>
+cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// y = ln * (x * r), r = 1/sqrt(mean(x^2) + eps), into shared memory (model.rs:141-145; the sum of squares is a
+// parallel reduction here).  Returns r.  `x` is read through L2 (written by an earlier kernel).
+LDEV float norm_to_smem(const float* x, const float* ln, int H, float eps, float* xs, float* red) {
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        float v = __ldcg(x + i);
+        xs[i] = v;
+        ss = fmaf(v, v, ss);
+    }
+    float tot = block_sum(ss, red);
+    float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)H), eps)));
+    for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = __fmul_rn(__ldg(ln + i), __fmul_rn(xs[i], r));
+    __syncthreads();
+    return r;
+}
+
+LDEV void copy_to_smem(const float* x, int n, float* xs) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = __ldcg(x + i);
+    __syncthreads();
+}
+
+// dot of a bf16 row held as NCH 16-byte chunks per lane (chunk c covers columns (c*32+lane)*8 .. +8) with xs.
+template <int NCH>
+LDEV float row_dot(const uint4 (&w)[NCH], const float* xs, int H, int lane) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        int col = (c * 32 + lane) * 8;
+        if (col < H) {
+            float4 xa = *reinterpret_cast<const float4*>(xs + col);
+            float4 xb = *reinterpret_cast<const float4*>(xs + col + 4);
+            acc = dot8(w[c], xa, xb, acc);
+        }
+    }
+    return acc;
+}
+
+template <int NCH>
+LDEV void load_row(uint4 (&w)[NCH], const uint16_t* row, int H, int lane, bool active) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        int col = (c * 32 + lane) * 8;
+        if (active && col < H)
+            w[c] = ld_weight(row + col);
+        else
+            w[c] = make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// qkv_rope: one warp per row pair (j, j + d/2) of a head, so RoPE's rotate_half partner is in the same warp.
+// ------------------------------------------------------------------------------------------------------------------
+template <int NCH, bool KV_F32>
+__global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
+    extern __shared__ float smem[];
+    float* xs = smem;
+    float* red = smem + a.H;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int half = a.d >> 1;
+    const int npairs = (a.qd + 2 * a.kvd) >> 1;
+    const int pair = blockIdx.x * (blockDim.x >> 5) + warp;
+    const bool active = pair < npairs;
+    const int head = pair / half, j = pair - (pair / half) * half;
+    const int r0 = head * a.d + j, r1 = r0 + half;
+
+    uint4 w0[NCH], w1[NCH];
+    load_row<NCH>(w0, a.w + (size_t)r0 * a.H, a.H, lane, active);
+    load_row<NCH>(w1, a.w + (size_t)r1 * a.H, a.H, lane, active);
+
+    pdl_wait();
+    pdl_launch();
+
+    const int pos = __ldcg(a.pos);
+    if (a.embed_mode) {
+        // model.rs:134-138: embedding row x embedding_multiplier is the residual stream of layer 0
+        const int tok = __ldcg(a.token);
+        const uint16_t* er = a.embed + (size_t)tok * a.H;
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
+            float v = __fmul_rn(__uint_as_float((uint32_t)er[i] << 16), a.emb_mult);
+            xs[i] = v;
+            if (blockIdx.x == 0) a.h_write[i] = v;
+            ss = fmaf(v, v, ss);
+        }
+        float tot = block_sum(ss, red);
+        float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.H), a.eps)));
+        for (int i = threadIdx.x; i < a.H; i += blockDim.x) xs[i] = __fmul_rn(__ldg(a.ln + i), __fmul_rn(xs[i], r));
+        __syncthreads();
+    } else {
+        norm_to_smem(a.h, a.ln, a.H, a.eps, xs, red);
+    }
+    if (!active) return;
+
+    float x1 = warp_sum(row_dot<NCH>(w0, xs, a.H, lane));
+    float x2 = warp_sum(row_dot<NCH>(w1, xs, a.H, lane));
+    if (lane != 0) return;
+    const float* cs = a.rope_cs + (size_t)pos * a.d;
+    const float c = __ldg(cs + j), s = __ldg(cs + half + j);
+    // model.rs:153-155: x1*c - x2*s, x2*c + x1*s (no contraction)
+    const float ro0 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+    const float ro1 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+    if (r0 < a.qd) {
+        a.q_out[r0] = ro0;
+        a.q_out[r1] = ro1;
+        return;
+    }
+    int rr = r0 - a.qd;
+    const bool is_k = rr < a.kvd;
+    if (!is_k) rr -= a.kvd;
+    const int kvh = rr / a.d;
+    const float v0 = is_k ? ro0 : x1, v1 = is_k ? ro1 : x2;
+    const int page = __ldcg(a.page_table + pos / a.page_size), slot = pos % a.page_size;
+    const size_t base = (((size_t)page * a.kv_heads + kvh) * a.page_size + slot) * a.d;
+    void* pool = is_k ? a.k_pool : a.v_pool;
+    if (KV_F32) {
+        float* p = static_cast<float*>(pool) + base;
+        p[j] = v0;
+        p[j + half] = v1;
+    } else {
+        uint16_t* p = static_cast<uint16_t*>(pool) + base;
+        p[j] = f32_to_bf16_rne(v0);
+        p[j + half] = f32_to_bf16_rne(v1);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// attention: CTA (split s, kv head). Each lane scores one position against the G query heads of the group
+// (GQA: the K/V rows are read once for all G heads), online softmax per warp, warps merged in shared memory,
+// then the last CTA of the KV head merges the splits (flash-decoding).  Positions past `len` are never read.
+// ------------------------------------------------------------------------------------------------------------------
+template <bool KV_F32>
+LDEV const void* kv_row(const void* pool, const int* page_table, int page_size, int kv_heads, int kvh, int p) {
+    const int page = __ldcg(page_table + p / page_size), slot = p - (p / page_size) * page_size;
+    const size_t off = (((size_t)page * kv_heads + kvh) * page_size + slot) * kHeadDim;
+    if (KV_F32) return static_cast<const float*>(pool) + off;
+    return static_cast<const uint16_t*>(pool) + off;
+}
+
+template <bool KV_F32, int G>
+__global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
+    constexpr int D = kHeadDim;
+    constexpr int NW = 4;
+    __shared__ __align__(16) float sq[G][D];
+    __shared__ float sm_m[NW][G], sm_l[NW][G];
+    __shared__ float sacc[NW][G][D];
+    __shared__ bool is_last;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int s = blockIdx.x, kvh = blockIdx.y;
+
+    pdl_wait();
+    pdl_launch();
+
+    const int len = __ldcg(a.pos) + 1;
+    const int p0 = (int)(((long long)len * s) / a.ns), p1 = (int)(((long long)len * (s + 1)) / a.ns);
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x) sq[i / D][i % D] = __ldcg(a.q + (size_t)kvh * G * D + i);
+    __syncthreads();
+
+    float m[G], l[G], acc0[G], acc1[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+        acc0[g] = 0.0f;
+        acc1[g] = 0.0f;
+    }
+
+    for (int base = p0 + warp * 32; base < p1; base += NW * 32) {
+        const int p = base + lane;
+        const bool valid = p < p1;
+        float sc[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) sc[g] = 0.0f;
+        if (valid) {
+            const void* kr = kv_row<KV_F32>(a.k_pool, a.page_table, a.page_size, a.kv_heads, kvh, p);
+            if (KV_F32) {
+                const float4* k4 = static_cast<const float4*>(kr);
+#pragma unroll
+                for (int c = 0; c < D / 4; ++c) {
+                    float4 kv = __ldcg(k4 + c);
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        float4 qv = *reinterpret_cast<const float4*>(&sq[g][c * 4]);
+                        sc[g] = fmaf(qv.x, kv.x, sc[g]);
+                        sc[g] = fmaf(qv.y, kv.y, sc[g]);
+                        sc[g] = fmaf(qv.z, kv.z, sc[g]);
+                        sc[g] = fmaf(qv.w, kv.w, sc[g]);
+                    }
+                }
+            } else {
+                const uint4* k8 = static_cast<const uint4*>(kr);
+#pragma unroll
+                for (int c = 0; c < D / 8; ++c) {
+                    uint4 kv = __ldcg(k8 + c);
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        float4 qa = *reinterpret_cast<const float4*>(&sq[g][c * 8]);
+                        float4 qb = *reinterpret_cast<const float4*>(&sq[g][c * 8 + 4]);
+                        sc[g] = dot8(kv, qa, qb, sc[g]);
+                    }
+                }
+            }
+        }
+        float pr[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float scv = valid ? __fmul_rn(sc[g], a.scale) : -INFINITY;
+            const float mt = warp_max(scv);
+            const float mn = fmaxf(m[g], mt);
+            pr[g] = valid ? expf(scv - mn) : 0.0f;
+            const float alpha = (m[g] == -INFINITY) ? 0.0f : expf(m[g] - mn);
+            l[g] = l[g] * alpha + warp_sum(pr[g]);
+            acc0[g] *= alpha;
+            acc1[g] *= alpha;
+            m[g] = mn;
+        }
+        const int nj = min(32, p1 - base);
+        for (int jj = 0; jj < nj; ++jj) {
+            const void* vr = kv_row<KV_F32>(a.v_pool, a.page_table, a.page_size, a.kv_heads, kvh, base + jj);
+            float v0, v1;
+            if (KV_F32) {
+                float2 t = __ldcg(static_cast<const float2*>(vr) + lane);
+                v0 = t.x;
+                v1 = t.y;
+            } else {
+                uint32_t t = __ldcg(static_cast<const unsigned int*>(vr) + lane);
+                v0 = bf_lo(t);
+                v1 = bf_hi(t);
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float pj = __shfl_sync(0xffffffffu, pr[g], jj);
+                acc0[g] = fmaf(pj, v0, acc0[g]);
+                acc1[g] = fmaf(pj, v1, acc1[g]);
+            }
+        }
+    }
+
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        if (lane == 0) {
+            sm_m[warp][g] = m[g];
+            sm_l[warp][g] = l[g];
+        }
+        sacc[warp][g][2 * lane] = acc0[g];
+        sacc[warp][g][2 * lane + 1] = acc1[g];
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
+        const int g = t / D, dim = t - (t / D) * D;
+        float M = -INFINITY;
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_m[w][g]);
+        float L = 0.0f, A = 0.0f;
+        if (M != -INFINITY) {
+            for (int w = 0; w < NW; ++w) {
+                if (sm_m[w][g] == -INFINITY) continue;
+                const float e = expf(sm_m[w][g] - M);
+                L = fmaf(sm_l[w][g], e, L);
+                A = fmaf(sacc[w][g][dim], e, A);
+            }
+        }
+        const size_t slot = ((size_t)kvh * a.ns + s) * G + g;
+        a.part_acc[slot * D + dim] = A;
+        if (dim == 0) {
+            a.part_ml[slot * 2] = M;
+            a.part_ml[slot * 2 + 1] = L;
+        }
+    }
+
+    if (!last_block_arrives(a.counters + kvh, (unsigned int)a.ns, &is_last)) return;
+    for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
+        const int g = t / D, dim = t - (t / D) * D;
+        float M = -INFINITY;
+        for (int sp = 0; sp < a.ns; ++sp) M = fmaxf(M, __ldcg(a.part_ml + (((size_t)kvh * a.ns + sp) * G + g) * 2));
+        float num = 0.0f, den = 0.0f;
+        for (int sp = 0; sp < a.ns; ++sp) {
+            const size_t slot = ((size_t)kvh * a.ns + sp) * G + g;
+            const float ms = __ldcg(a.part_ml + slot * 2);
+            if (ms == -INFINITY) continue;
+            const float e = expf(ms - M);
+            den = fmaf(__ldcg(a.part_ml + slot * 2 + 1), e, den);
+            num = fmaf(__ldcg(a.part_acc + slot * D + dim), e, num);
+        }
+        a.att_out[((size_t)kvh * G + g) * D + dim] = num / den;
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// oproj: h[r] += resid * (W_o[r] . att), one warp per row (model.rs:223-227)
+// ------------------------------------------------------------------------------------------------------------------
+template <int NCH>
+__global__ void __launch_bounds__(128) oproj_kernel(OprojArgs a) {
+    extern __shared__ float smem[];
+    float* xs = smem;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int row = blockIdx.x * (blockDim.x >> 5) + warp;
+    const bool active = row < a.H;
+    uint4 w[NCH];
+    load_row<NCH>(w, a.w + (size_t)row * a.qd, a.qd, lane, active);
+    pdl_wait();
+    pdl_launch();
+    copy_to_smem(a.att, a.qd, xs);
+    if (!active) return;
+    const float o = warp_sum(row_dot<NCH>(w, xs, a.qd, lane));
+    if (lane == 0) a.h[row] = __fadd_rn(__ldcg(a.h + row), __fmul_rn(a.resid, o));
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// router: logits = W_r . xn (one warp per expert), then the last CTA takes the top-k with block.rs:81-89's order
+// (total_cmp descending, lower index first on ties) and the softmax over the k.
+// ------------------------------------------------------------------------------------------------------------------
+LDEV unsigned long long route_key(float v, int idx) {
+    // larger is better: value by total order, then lower index
+    return ((unsigned long long)((uint32_t)total_key(v) ^ 0x80000000u) << 32) | (uint32_t)(~(uint32_t)idx);
+}
+
+LDEV unsigned long long shfl_xor_u64(unsigned long long v, int o) {
+    uint32_t lo = (uint32_t)v, hi = (uint32_t)(v >> 32);
+    lo = __shfl_xor_sync(0xffffffffu, lo, o);
+    hi = __shfl_xor_sync(0xffffffffu, hi, o);
+    return ((unsigned long long)hi << 32) | lo;
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
+    extern __shared__ float smem[];
+    float* xs = smem;
+    float* red = smem + a.H;
+    __shared__ bool is_last;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int e = blockIdx.x * (blockDim.x >> 5) + warp;
+    const bool active = e < a.E;
+    uint4 w[NCH];
+    load_row<NCH>(w, a.w + (size_t)e * a.H, a.H, lane, active);
+    pdl_wait();
+    pdl_launch();
+    if (a.norm_mode) {
+        const float r = norm_to_smem(a.x, a.ln, a.H, a.eps, xs, red);
+        if (blockIdx.x == 0 && threadIdx.x == 0) *a.rnorm_out = r;
+    } else {
+        copy_to_smem(a.x, a.H, xs);
+    }
+    if (active) {
+        const float lg = warp_sum(row_dot<NCH>(w, xs, a.H, lane));
+        if (lane == 0) a.logits[e] = lg;
+    }
+    if (!last_block_arrives(a.counter, gridDim.x, &is_last)) return;
+    if (warp != 0) return;
+    // E <= 64: lane holds experts lane and lane + 32
+    float v0 = lane < a.E ? __ldcg(a.logits + lane) : 0.0f;
+    float v1 = lane + 32 < a.E ? __ldcg(a.logits + lane + 32) : 0.0f;
+    unsigned long long k0 = lane < a.E ? route_key(v0, lane) : 0ull;
+    unsigned long long k1 = lane + 32 < a.E ? route_key(v1, lane + 32) : 0ull;
+    int ids[kMaxTopK];
+    float vals[kMaxTopK];
+    for (int j = 0; j < a.k; ++j) {
+        unsigned long long b = k0 > k1 ? k0 : k1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            unsigned long long t = shfl_xor_u64(b, o);
+            b = t > b ? t : b;
+        }
+        const int idx = (int)(~(uint32_t)b);
+        ids[j] = idx;
+        const int src = idx & 31;
+        const float val = __shfl_sync(0xffffffffu, idx < 32 ? v0 : v1, src);
+        vals[j] = val;
+        if (lane == src) {
+            if (idx < 32)
+                k0 = 0ull;
+            else
+                k1 = 0ull;
+        }
+    }
+    if (lane == 0) {
+        // block.rs:85-88: exp(v - v0) over the k in order, then divide by their sum
+        float ex[kMaxTopK];
+        float sum = 0.0f;
+        for (int j = 0; j < a.k; ++j) ex[j] = expf(__fsub_rn(vals[j], vals[0]));
+        for (int j = 0; j < a.k; ++j) sum = __fadd_rn(sum, ex[j]);
+        for (int j = 0; j < a.k; ++j) {
+            a.ids[j] = ids[j];
+            a.weights[j] = __fdiv_rn(ex[j], sum);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// gate_up: warp per (expert slot, intermediate row j): g = W[e][j] . xn, u = W[e][I+j] . xn, a = silu(g) * u
+// (cpu.rs:154-158, gpu.rs:45-74); all k experts in one grid.
+// ------------------------------------------------------------------------------------------------------------------
+template <int NCH>
+__global__ void __launch_bounds__(128) gate_up_kernel(GateUpArgs a) {
+    extern __shared__ float smem[];
+    float* xs = smem;
+    float* red = smem + a.H;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int item = blockIdx.x * (blockDim.x >> 5) + warp;
+    const bool active = item < a.k * a.I;
+    const int slot = item / a.I, j = item - (item / a.I) * a.I;
+
+    pdl_wait();
+    pdl_launch();
+
+    uint4 wg[NCH], wu[NCH];
+    if (active) {
+        // expert ids come from the router; clamped so that a stale id can never address outside the weights
+        const int e = min(max(__ldcg(a.ids + slot), 0), a.E - 1);
+        const uint16_t* base = a.w + (size_t)e * 2 * a.I * a.H;
+        load_row<NCH>(wg, base + (size_t)j * a.H, a.H, lane, true);
+        load_row<NCH>(wu, base + (size_t)(a.I + j) * a.H, a.H, lane, true);
+    } else {
+        load_row<NCH>(wg, a.w, a.H, lane, false);
+        load_row<NCH>(wu, a.w, a.H, lane, false);
+    }
+    if (a.norm_mode) {
+        // xn = ln * (h * r) with the router's r
+        const float r = __ldcg(a.rnorm);
+        for (int i = threadIdx.x; i < a.H; i += blockDim.x) xs[i] = __fmul_rn(__ldg(a.ln + i), __fmul_rn(__ldcg(a.x + i), r));
+        __syncthreads();
+    } else {
+        copy_to_smem(a.x, a.H, xs);
+    }
+    (void)red;
+    if (!active) return;
+    const float g = warp_sum(row_dot<NCH>(wg, xs, a.H, lane));
+    const float u = warp_sum(row_dot<NCH>(wu, xs, a.H, lane));
+    if (lane == 0) a.a[(size_t)slot * a.I + j] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// down: warp per output row r: y = sum_j w_j * (W_d[e_j][r] . a_j) in routing order (cpu.rs:231-238), then
+// h[r] += resid * y (model.rs:230-232) or out[r] = y (block forward).  Expert ids and weights come from the router
+// (two kernels back), so the down weights are loaded before griddepcontrol.wait.
+// ------------------------------------------------------------------------------------------------------------------
+template <int NCI>
+__global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
+    extern __shared__ float smem[];
+    float* as = smem;  // [k, I]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int row = blockIdx.x * (blockDim.x >> 5) + warp;
+    const bool active = row < a.H;
+    uint4 w[kMaxTopK][NCI];
+    float gw[kMaxTopK];
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) {
+        const bool on = active && j < a.k;
+        const int e = on ? min(max(__ldcg(a.ids + j), 0), a.E - 1) : 0;
+        gw[j] = on ? __ldcg(a.weights + j) : 0.0f;
+        load_row<NCI>(w[j], a.w + ((size_t)e * a.H + row) * a.I, a.I, lane, on);
+    }
+    pdl_wait();
+    pdl_launch();
+    copy_to_smem(a.a, a.k * a.I, as);
+    if (!active) return;
+    float acc = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) {
+        if (j < a.k) {
+            const float d = warp_sum(row_dot<NCI>(w[j], as + (size_t)j * a.I, a.I, lane));
+            acc = __fadd_rn(acc, __fmul_rn(gw[j], d));
+        }
+    }
+    if (lane == 0) {
+        if (a.accumulate)
+            a.out[row] = __fadd_rn(__ldcg(a.out + row), __fmul_rn(a.resid, acc));
+        else
+            a.out[row] = acc;
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// head: final RMSNorm, logits = (E . xn) / logits_scaling over the tied embedding, argmax keeping the last maximum
+// (Iterator::max_by with total_cmp).  The last CTA publishes the token, appends it to the history and advances pos.
+// ------------------------------------------------------------------------------------------------------------------
+constexpr int kHeadRowsPerWarp = 2;
+constexpr int kHeadWarps = 8;
+
+LDEV unsigned long long arg_key(float v, int idx) {
+    // larger is better: value by total order, then the larger index (last maximum)
+    return ((unsigned long long)((uint32_t)total_key(v) ^ 0x80000000u) << 32) | (uint32_t)idx;
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(256) head_kernel(HeadArgs a) {
+    extern __shared__ float smem[];
+    float* xs = smem;
+    float* red = smem + a.H;
+    __shared__ unsigned long long wbest[kHeadWarps];
+    __shared__ bool is_last;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int row0 = (blockIdx.x * kHeadWarps + warp) * kHeadRowsPerWarp;
+    uint4 w[kHeadRowsPerWarp][NCH];
+#pragma unroll
+    for (int r = 0; r < kHeadRowsPerWarp; ++r)
+        load_row<NCH>(w[r], a.w + (size_t)(row0 + r) * a.H, a.H, lane, row0 + r < a.V);
+    pdl_wait();
+    pdl_launch();
+    norm_to_smem(a.h, a.ln, a.H, a.eps, xs, red);
+    unsigned long long best = 0ull;
+#pragma unroll
+    for (int r = 0; r < kHeadRowsPerWarp; ++r) {
+        const int row = row0 + r;
+        const float d = warp_sum(row_dot<NCH>(w[r], xs, a.H, lane));
+        if (row < a.V) {
+            const float lg = __fdiv_rn(d, a.logits_scaling);
+            if (lane == 0 && a.logits_out) a.logits_out[row] = lg;
+            const unsigned long long k = arg_key(lg, row);
+            best = k > best ? k : best;
+        }
+    }
+    if (lane == 0) wbest[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long b = 0ull;
+        for (int i = 0; i < kHeadWarps; ++i) b = wbest[i] > b ? wbest[i] : b;
+        a.partial[blockIdx.x] = b;
+    }
+    if (!last_block_arrives(a.counter, gridDim.x, &is_last)) return;
+    unsigned long long b = 0ull;
+    for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) {
+        const unsigned long long t = __ldcg(a.partial + i);
+        b = t > b ? t : b;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long t = shfl_xor_u64(b, o);
+        b = t > b ? t : b;
+    }
+    if (lane == 0) wbest[warp] = b;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long m = 0ull;
+        for (int i = 0; i < kHeadWarps; ++i) m = wbest[i] > m ? wbest[i] : m;
+        const int tok = (int)(uint32_t)m;
+        *a.token_out = tok;
+        if (a.out_ids) {
+            const int st = __ldcg(a.step);
+            if (st >= 0 && st < a.out_cap) a.out_ids[st] = tok;
+            *a.step = st + 1;
+        }
+        *a.pos = __ldcg(a.pos) + 1;
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// synthetic fill
+// ------------------------------------------------------------------------------------------------------------------
+LDEV uint64_t mix64(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+LDEV float synth_value(uint64_t seed, uint64_t idx, float scale) {
+    const uint64_t h = mix64(seed + (idx + 1ull) * 0x9E3779B97F4A7C15ull);
+    const int s = (int)(h & 0xffffu) + (int)((h >> 16) & 0xffffu) + (int)((h >> 32) & 0xffffu) + (int)(h >> 48);
+    return __fmul_rn((float)(s - 131070), scale);
+}
+
+__global__ void synth_bf16_kernel(uint16_t* out, size_t n, uint64_t seed, float scale, float mean) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float v = synth_value(seed, i, scale);
+        if (mean != 0.0f) v = __fadd_rn(v, mean);
+        out[i] = f32_to_bf16_rne(v);
+    }
+}
+
+__global__ void synth_norm_kernel(float* out, size_t n, uint64_t seed, float scale) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const float v = __fadd_rn(synth_value(seed, i, scale), 1.0f);
+        out[i] = __uint_as_float((uint32_t)f32_to_bf16_rne(v) << 16);
+    }
+}
+
+int chunks_for(int n) { return (n + 255) / 256; }
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------------------------------
+// launchers
+// ---------------------------------------------------------------------------------------------------------------------
+#define LASTRO_NCH_SWITCH(nch, KERNEL_EXPR)                     \
+    switch (nch) {                                              \
+    case 1: { constexpr int N = 1; return KERNEL_EXPR; }        \
+    case 2: { constexpr int N = 2; return KERNEL_EXPR; }        \
+    case 3: { constexpr int N = 3; return KERNEL_EXPR; }        \
+    case 4: { constexpr int N = 4; return KERNEL_EXPR; }        \
+    case 5: { constexpr int N = 5; return KERNEL_EXPR; }        \
+    case 6: { constexpr int N = 6; return KERNEL_EXPR; }        \
+    case 7: { constexpr int N = 7; return KERNEL_EXPR; }        \
+    case 8: { constexpr int N = 8; return KERNEL_EXPR; }        \
+    default: return cudaErrorInvalidValue;                      \
+    }
+
+cudaError_t launch_qkv_rope(const QkvArgs& a, cudaStream_t s, bool pdl) {
+    const int npairs = (a.qd + 2 * a.kvd) / 2;
+    const dim3 grid((npairs + 3) / 4), block(128);
+    const size_t smem = sizeof(float) * (a.H + 32);
+    if (a.kv_f32) {
+        LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(qkv_rope_kernel<N, true>, grid, block, smem, s, pdl, a));
+    }
+    LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(qkv_rope_kernel<N, false>, grid, block, smem, s, pdl, a));
+}
+
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
+    const dim3 grid(a.ns, a.kv_heads), block(128);
+#define LASTRO_ATTN_G(GV)                                                                      \
+    case GV:                                                                                   \
+        return a.kv_f32 ? launch_ex(attention_kernel<true, GV>, grid, block, 0, s, pdl, a)     \
+                        : launch_ex(attention_kernel<false, GV>, grid, block, 0, s, pdl, a);
+    switch (a.G) {
+        LASTRO_ATTN_G(1)
+        LASTRO_ATTN_G(2)
+        LASTRO_ATTN_G(3)
+        LASTRO_ATTN_G(4)
+        LASTRO_ATTN_G(6)
+        LASTRO_ATTN_G(8)
+    default: return cudaErrorInvalidValue;
+    }
+#undef LASTRO_ATTN_G
+}
+
+cudaError_t launch_oproj(const OprojArgs& a, cudaStream_t s, bool pdl) {
+    const dim3 grid((a.H + 3) / 4), block(128);
+    const size_t smem = sizeof(float) * a.qd;
+    LASTRO_NCH_SWITCH(chunks_for(a.qd), launch_ex(oproj_kernel<N>, grid, block, smem, s, pdl, a));
+}
+
+cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, bool pdl) {
+    const dim3 grid((a.E + 3) / 4), block(128);
+    const size_t smem = sizeof(float) * (a.H + 32);
+    LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(router_kernel<N>, grid, block, smem, s, pdl, a));
+}
+
+cudaError_t launch_gate_up(const GateUpArgs& a, cudaStream_t s, bool pdl) {
+    const int items = a.k * a.I;
+    const dim3 grid((items + 3) / 4), block(128);
+    const size_t smem = sizeof(float) * (a.H + 32);
+    LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(gate_up_kernel<N>, grid, block, smem, s, pdl, a));
+}
+
+cudaError_t launch_down(const DownArgs& a, cudaStream_t s, bool pdl) {
+    const dim3 grid((a.H + 7) / 8), block(256);
+    const size_t smem = sizeof(float) * (size_t)a.k * a.I;
+    if (smem > 48 * 1024) return cudaErrorInvalidValue;
+    LASTRO_NCH_SWITCH(chunks_for(a.I), launch_ex(down_kernel<N>, grid, block, smem, s, pdl, a));
+}
+
+int head_grid(int V) {
+    const int rows = kHeadWarps * kHeadRowsPerWarp;
+    return (V + rows - 1) / rows;
+}
+
+cudaError_t launch_head(const HeadArgs& a, cudaStream_t s, bool pdl, int* grid_out) {
+    const dim3 grid(head_grid(a.V)), block(32 * kHeadWarps);
+    if (grid_out) *grid_out = (int)grid.x;
+    const size_t smem = sizeof(float) * (a.H + 32);
+    LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(head_kernel<N>, grid, block, smem, s, pdl, a));
+}
+
+cudaError_t launch_synth_bf16(uint16_t* out, size_t n, uint64_t seed, float scale, float mean, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    size_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 64) blocks = 148 * 64;
+    synth_bf16_kernel<<<(unsigned)blocks, 256, 0, s>>>(out, n, seed, scale, mean);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_synth_norm_f32(float* out, size_t n, uint64_t seed, float scale, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    size_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 64) blocks = 148 * 64;
+    synth_norm_kernel<<<(unsigned)blocks, 256, 0, s>>>(out, n, seed, scale);
+    return cudaGetLastError();
+}
+
+}  // namespace lastro

@@ -1,0 +1,140 @@
+// Kernel arguments and host-side launchers of the batch-1 Granite-MoE decode step.
+//
+// One decode step of layer l is six kernels, each a single pass over its weights:
+//   qkv_rope     RMSNorm(h) -> [q;k;v] GEMV -> RoPE(q,k) -> K/V appended to the paged cache
+//   attention    split-KV GQA decode attention; the last CTA of each KV head merges the splits
+//   oproj        h += resid * (W_o . att)
+//   router       RMSNorm(h) -> router GEMV -> top-k (lowest index on ties) -> softmax over k
+//   gate_up      a[j] = silu(W_g x) * (W_u x) for the k chosen experts, grouped in one launch
+//   down         h += resid * sum_j w_j (W_d[e_j] . a_j), experts summed in routing order
+// and the step ends with
+//   head         RMSNorm(h) -> tied-embedding GEMV / logits_scaling -> argmax (last max on ties)
+// All activations are f32, weights bf16, accumulators f32.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lastro {
+
+struct QkvArgs {
+    const float* h;        // residual stream [H] (ignored when embed_mode)
+    float* h_write;        // embed_mode: CTA 0 writes the embedding row x multiplier here
+    const uint16_t* embed; // [V, H] bf16 (embed_mode)
+    const int* token;      // device token id (embed_mode)
+    float emb_mult;
+    int embed_mode;
+    const float* ln;       // [H]
+    const uint16_t* w;     // [qd + 2 kvd, H] bf16: q rows, k rows, v rows
+    const float* rope_cs;  // [max_len, d]: cos(d/2) then sin(d/2) per position
+    const int* pos;        // device position of the token
+    float* q_out;          // [qd] roped q
+    void* k_pool;          // [pages, kv_heads, page, d]
+    void* v_pool;
+    const int* page_table; // [max_pages]
+    int page_size, kv_f32;
+    int H, qd, kvd, d, kv_heads;
+    float eps;
+};
+
+struct AttnArgs {
+    const float* q;          // [heads*d]
+    const void* k_pool;
+    const void* v_pool;
+    const int* page_table;
+    int page_size, kv_f32;
+    const int* pos;          // attends positions 0..pos
+    float* part_acc;         // [kv_heads, ns, G, d]
+    float* part_ml;          // [kv_heads, ns, G, 2]
+    unsigned int* counters;  // [kv_heads], zero between launches
+    float* att_out;          // [heads*d]
+    int kv_heads, G, d, ns;
+    float scale;
+};
+
+struct OprojArgs {
+    const float* att;   // [qd]
+    const uint16_t* w;  // [H, qd]
+    float* h;           // [H], updated in place
+    float resid;
+    int H, qd;
+};
+
+struct RouterArgs {
+    const float* x;         // norm_mode: residual h; otherwise the block input
+    const float* ln;        // norm weight (norm_mode)
+    float eps;
+    int norm_mode;
+    const uint16_t* w;      // [E, H]
+    float* logits;          // [E]
+    int* ids;               // [k]
+    float* weights;         // [k]
+    float* rnorm_out;       // norm_mode: 1/sqrt(mean(h^2)+eps) for the experts
+    unsigned int* counter;  // zero between launches
+    int E, H, k;
+};
+
+struct GateUpArgs {
+    const float* x;       // norm_mode: residual h; otherwise the block input
+    const float* ln;      // norm_mode: norm weight
+    const float* rnorm;   // norm_mode: from the router kernel
+    int norm_mode;
+    const int* ids;       // [k]
+    const uint16_t* w;    // [E, 2I, H]
+    float* a;             // [k, I]
+    int H, I, k, E;
+};
+
+struct DownArgs {
+    const float* a;        // [k, I]
+    const int* ids;        // [k]
+    const float* weights;  // [k]
+    const uint16_t* w;     // [E, H, I]
+    float* out;            // accumulate: h += resid*y ; else out = y
+    float resid;
+    int accumulate;
+    int H, I, k, E;
+};
+
+struct HeadArgs {
+    const float* h;                 // [H]
+    const float* ln;                // final norm [H]
+    float eps;
+    const uint16_t* w;              // [V, H] (tied embedding)
+    float logits_scaling;
+    float* logits_out;              // [V] or null
+    unsigned long long* partial;    // [grid]
+    unsigned int* counter;          // zero between launches
+    int* token_out;                 // next token (device)
+    int* out_ids;                   // history of generated ids (device) or null
+    int out_cap;                    // entries of out_ids
+    int* step;                      // index into out_ids
+    int* pos;                       // incremented once per step
+    int V, H;
+};
+
+// Launchers: `pdl` marks the launch as programmatic-dependent on the previous kernel of the stream.
+cudaError_t launch_qkv_rope(const QkvArgs& a, cudaStream_t s, bool pdl);
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
+cudaError_t launch_oproj(const OprojArgs& a, cudaStream_t s, bool pdl);
+cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, bool pdl);
+cudaError_t launch_gate_up(const GateUpArgs& a, cudaStream_t s, bool pdl);
+cudaError_t launch_down(const DownArgs& a, cudaStream_t s, bool pdl);
+cudaError_t launch_head(const HeadArgs& a, cudaStream_t s, bool pdl, int* grid_out);
+int head_grid(int V);
+
+// Synthetic fill (same integer formula as the CPU oracle): value(i) = (sum of four 16-bit chunks of
+// mix64(seed + (i+1)*golden) - 131070) * scale (+ mean), rounded to bf16.
+cudaError_t launch_synth_bf16(uint16_t* out, size_t n, uint64_t seed, float scale, float mean, cudaStream_t s);
+// norms: bf16(1 + value) widened to f32
+cudaError_t launch_synth_norm_f32(float* out, size_t n, uint64_t seed, float scale, cudaStream_t s);
+
+// limits enforced by the host before any launch
+constexpr int kMaxHidden = 2048;   // H (and qd) <= 2048, multiple of 8
+constexpr int kMaxInter = 2048;
+constexpr int kMaxExperts = 64;
+constexpr int kMaxTopK = 8;
+constexpr int kHeadDim = 64;
+constexpr int kMaxGroup = 8;
+
+}  // namespace lastro

@@ -1,0 +1,243 @@
+"""Python binding of liblastro_b200.so (ctypes over the C ABI in include/lastro_b200.h).
+
+Mirrors the reference's operator API (rust/moe-rt/src/gpu.rs ``GpuLayer`` and gpu_model.rs ``GpuModel``) so
+that tests and benchmarks read like the reference's own.  There is no fallback: if the CUDA library is missing or
+no GPU is present, constructing a context raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+from . import configs  # noqa: F401
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_DIR, "liblastro_b200.so")
+HEADER = os.path.join(PKG_DIR, "..", "include", "lastro_b200.h")
+
+OK, E_ARG, E_CUDA, E_POISONED, E_FULL, E_NOMEM, E_UNSUPPORTED, E_STATE = range(8)
+DTYPE_BF16, DTYPE_F32 = 1, 2
+
+_lib = None
+
+
+class LastroError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+def build(quiet: bool = True) -> str:
+    """Compile liblastro_b200.so in place (nvcc, sm_100a)."""
+    subprocess.run(["make", "-s" if quiet else "-j2", "-C", PKG_DIR], check=True,
+                   stdout=subprocess.DEVNULL if quiet else None)
+    return LIB_PATH
+
+
+class ModelDesc(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("hidden", "inter", "layers", "heads", "kv_heads", "head_dim", "vocab",
+                                         "experts", "k")] + \
+               [(n, C.c_float) for n in ("rope_theta", "eps", "embedding_multiplier", "residual_multiplier",
+                                         "attention_multiplier", "logits_scaling")] + \
+               [("weight_dtype", C.c_int32), ("kv_dtype", C.c_int32)]
+
+
+EXPORTS = {
+    "lastro_version": (C.c_char_p, []),
+    "lastro_ctx_create": (C.c_int, [C.c_int32, C.c_void_p, C.POINTER(C.c_void_p)]),
+    "lastro_ctx_destroy": (None, [C.c_void_p]),
+    "lastro_ctx_synchronize": (C.c_int, [C.c_void_p]),
+    "lastro_last_error": (C.c_char_p, [C.c_void_p]),
+    "lastro_layer_create": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
+                                      C.c_void_p, C.POINTER(C.c_void_p)]),
+    "lastro_layer_forward": (C.c_int, [C.c_void_p] + [C.c_void_p] * 5),
+    "lastro_layer_add_into": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p]),
+    "lastro_layer_destroy": (None, [C.c_void_p]),
+    "lastro_model_create": (C.c_int, [C.c_void_p, C.POINTER(ModelDesc), C.c_int32, C.POINTER(C.c_void_p)]),
+    "lastro_model_load_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int32, C.POINTER(C.c_int64), C.c_int32,
+                                           C.c_void_p]),
+    "lastro_model_fill_synthetic": (C.c_int, [C.c_void_p, C.c_uint64, C.c_float, C.c_float]),
+    "lastro_model_step": (C.c_int, [C.c_void_p, C.c_int32] + [C.c_void_p] * 4),
+    "lastro_model_generate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
+    "lastro_model_decode": (C.c_int, [C.c_void_p, C.c_int32]),
+    "lastro_model_reset": (C.c_int, [C.c_void_p]),
+    "lastro_model_position": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
+    "lastro_model_profile": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32]),
+    "lastro_model_set_options": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32]),
+    "lastro_model_destroy": (None, [C.c_void_p]),
+}
+
+
+def lib():
+    """Load the in-tree CUDA library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: run `make -C lastro-rust_b200` (or __graft_entry__.build())")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in EXPORTS.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class Context:
+    """One device and one stream (the reference's Arc<Stream>)."""
+
+    def __init__(self, device: int = 0, stream: int | None = None):
+        h = C.c_void_p()
+        rc = lib().lastro_ctx_create(device, stream, C.byref(h))
+        if rc != OK:
+            raise LastroError(rc, f"lastro_ctx_create(device={device}) failed: no usable CUDA device")
+        self.h = h
+
+    def check(self, rc: int):
+        if rc != OK:
+            raise LastroError(rc, lib().lastro_last_error(self.h).decode())
+
+    def synchronize(self):
+        self.check(lib().lastro_ctx_synchronize(self.h))
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().lastro_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
+class GpuLayer:
+    """MoE block with every expert resident (gpu.rs GpuLayer)."""
+
+    def __init__(self, ctx: Context, router: np.ndarray, gate_up: np.ndarray, down: np.ndarray, k: int):
+        E, H = router.shape
+        I = gate_up.shape[1] // 2
+        assert gate_up.shape == (E, 2 * I, H) and down.shape == (E, H, I)
+        self.ctx, self.E, self.H, self.I, self.k = ctx, E, H, I, k
+        h = C.c_void_p()
+        r, g, d = (np.ascontiguousarray(a, dtype=np.uint16) for a in (router, gate_up, down))
+        ctx.check(lib().lastro_layer_create(ctx.h, E, H, I, k, _p(r), _p(g), _p(d), C.byref(h)))
+        self.h = h
+
+    def forward(self, x: np.ndarray):
+        """(y, ids, weights, logits) for one token, host in/out (GpuLayer::forward)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.empty(self.H, np.float32)
+        ids = np.empty(self.k, np.int32)
+        w = np.empty(self.k, np.float32)
+        lg = np.empty(self.E, np.float32)
+        self.ctx.check(lib().lastro_layer_forward(self.h, _p(x), _p(y), _p(ids), _p(w), _p(lg)))
+        return y, ids, w, lg
+
+    def add_into(self, xn_ptr: int, h_ptr: int, resid: float, ids_ptr: int | None = None, w_ptr: int | None = None):
+        self.ctx.check(lib().lastro_layer_add_into(self.h, xn_ptr, h_ptr, resid, ids_ptr, w_ptr))
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().lastro_layer_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
+TENSOR_NAMES = ("input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_proj.weight",
+                "self_attn.k_proj.weight", "self_attn.v_proj.weight", "self_attn.o_proj.weight",
+                "block_sparse_moe.router.layer.weight", "block_sparse_moe.input_linear.weight",
+                "block_sparse_moe.output_linear.weight")
+LAYER_KEYS = ("ln_attn", "ln_moe", "q", "k", "v", "o", "router", "gate_up", "down")
+
+
+class GpuModel:
+    """Whole model resident on one GPU (gpu_model.rs GpuModel), batch-1 decode."""
+
+    def __init__(self, ctx: Context, cfg: dict, max_len: int, kv_dtype: str = "bf16"):
+        self.ctx, self.cfg, self.max_len = ctx, dict(cfg), max_len
+        d = ModelDesc(**{f: cfg[f] for f, _ in ModelDesc._fields_[:15]}, weight_dtype=DTYPE_BF16,
+                      kv_dtype=DTYPE_F32 if kv_dtype == "f32" else DTYPE_BF16)
+        h = C.c_void_p()
+        ctx.check(lib().lastro_model_create(ctx.h, C.byref(d), max_len, C.byref(h)))
+        self.h = h
+        self._logits = np.empty(cfg["vocab"], np.float32)
+        self._ids = np.empty(cfg["layers"] * cfg["k"], np.int32)
+        self._w = np.empty(cfg["layers"] * cfg["k"], np.float32)
+        self._next = np.empty(1, np.int32)
+
+    def load_tensor(self, name: str, arr: np.ndarray):
+        arr = np.ascontiguousarray(arr)
+        dtype = DTYPE_F32 if arr.dtype == np.float32 else DTYPE_BF16
+        if dtype == DTYPE_BF16:
+            assert arr.dtype == np.uint16, f"{name}: bf16 tensors are passed as uint16 bit arrays"
+        shape = (C.c_int64 * arr.ndim)(*arr.shape)
+        self.ctx.check(lib().lastro_model_load_tensor(self.h, name.encode(), dtype, shape, arr.ndim, _p(arr)))
+
+    def load_weights(self, w: dict):
+        """w: embed [V,H] u16, norm [H] f32, layers[l] dict with LAYER_KEYS (u16 bf16 bits / f32 norms)."""
+        self.load_tensor("model.embed_tokens.weight", w["embed"])
+        self.load_tensor("model.norm.weight", w["norm"])
+        for l, lw in enumerate(w["layers"]):
+            for key, name in zip(LAYER_KEYS, TENSOR_NAMES):
+                self.load_tensor(f"model.layers.{l}.{name}", lw[key])
+
+    def fill_synthetic(self, seed: int, std: float = 0.02, norm_std: float = 0.0):
+        self.ctx.check(lib().lastro_model_fill_synthetic(self.h, seed, std, norm_std))
+
+    def step(self, token: int, want_logits: bool = True, want_routes: bool = True):
+        """(logits, next_token, route_ids [L,k], route_w [L,k]) (GpuModel::step)."""
+        self.ctx.check(lib().lastro_model_step(self.h, int(token), _p(self._logits) if want_logits else None,
+                                               _p(self._next), _p(self._ids) if want_routes else None,
+                                               _p(self._w) if want_routes else None))
+        c = self.cfg
+        return (self._logits.copy() if want_logits else None, int(self._next[0]),
+                self._ids.reshape(c["layers"], c["k"]).copy() if want_routes else None,
+                self._w.reshape(c["layers"], c["k"]).copy() if want_routes else None)
+
+    def generate(self, prompt, n_new: int) -> np.ndarray:
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.empty(max(n_new, 1), np.int32)
+        self.ctx.check(lib().lastro_model_generate(self.h, _p(p), p.size, n_new, _p(out)))
+        return out[:n_new]
+
+    def decode(self, n: int):
+        self.ctx.check(lib().lastro_model_decode(self.h, n))
+
+    def reset(self):
+        self.ctx.check(lib().lastro_model_reset(self.h))
+
+    @property
+    def pos(self) -> int:
+        v = C.c_int32()
+        self.ctx.check(lib().lastro_model_position(self.h, C.byref(v)))
+        return v.value
+
+    KERNELS = ("qkv_rope", "attention", "oproj", "router", "gate_up", "down", "head")
+
+    def profile(self, steps: int) -> dict:
+        """Per-kernel device ms per step (summed over layers), measured with events between direct launches."""
+        out = np.zeros(len(self.KERNELS), np.float32)
+        self.ctx.check(lib().lastro_model_profile(self.h, steps, _p(out), out.size))
+        return dict(zip(self.KERNELS, out.tolist()))
+
+    def set_options(self, graphs: bool = True, pdl: bool = True):
+        self.ctx.check(lib().lastro_model_set_options(self.h, int(graphs), int(pdl)))
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().lastro_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
