@@ -121,7 +121,7 @@ def cpu_decode_rate(cfg, context, seed, seconds, steps=None, warmup=1):
     t0 = time.time()
     om = O.Model(cfg, synthetic_seed=seed, std=CFG.WEIGHT_STD, norm_std=0.0, threads=threads)
     pool = O.Pool(threads)
-    n_max = (steps or 64) + warmup + 2
+    n_max = (steps or 256) + warmup + 2
     s = O.Session(om, pool, context + n_max)
     s.fill_kv(context, seed, 0.5)
     setup = time.time() - t0
@@ -135,7 +135,7 @@ def cpu_decode_rate(cfg, context, seed, seconds, steps=None, warmup=1):
         tok = O.argmax_last(lg)
         n += 1
         el = time.time() - t1
-        if (steps is not None and n >= steps) or (steps is None and el >= seconds):
+        if (steps is not None and n >= steps) or (steps is None and (el >= seconds or n >= 256)):
             break
     s.close()
     om.close()

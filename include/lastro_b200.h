@@ -50,6 +50,7 @@ typedef struct {
 /* ---- context: one device, one stream (the reference's Arc<Stream>, gpu.rs:333) ---------------------------------- */
 /* stream_or_null: a cudaStream_t to enqueue on, or NULL for a stream owned by the context */
 int lastro_ctx_create(int32_t device, void *stream_or_null, lastro_ctx **out);
+/* destroy every layer and model created on ctx first */
 void lastro_ctx_destroy(lastro_ctx *ctx);
 int lastro_ctx_synchronize(lastro_ctx *ctx);
 /* text of the last error on this context ("" if none); valid until the next call on ctx */

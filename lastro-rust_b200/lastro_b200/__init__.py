@@ -9,6 +9,7 @@ from __future__ import annotations
 import ctypes as C
 import os
 import subprocess
+import weakref
 
 import numpy as np
 
@@ -102,6 +103,8 @@ class Context:
         if rc != OK:
             raise LastroError(rc, f"lastro_ctx_create(device={device}) failed: no usable CUDA device")
         self.h = h
+        # objects created on this context; they are destroyed before it (the C ABI requires that order)
+        self._children = weakref.WeakSet()
 
     def check(self, rc: int):
         if rc != OK:
@@ -112,6 +115,8 @@ class Context:
 
     def close(self):
         if getattr(self, "h", None):
+            for child in list(self._children):
+                child.close()
             lib().lastro_ctx_destroy(self.h)
             self.h = None
 
@@ -131,6 +136,7 @@ class GpuLayer:
         r, g, d = (np.ascontiguousarray(a, dtype=np.uint16) for a in (router, gate_up, down))
         ctx.check(lib().lastro_layer_create(ctx.h, E, H, I, k, _p(r), _p(g), _p(d), C.byref(h)))
         self.h = h
+        ctx._children.add(self)
 
     def forward(self, x: np.ndarray):
         """(y, ids, weights, logits) for one token, host in/out (GpuLayer::forward)."""
@@ -171,6 +177,7 @@ class GpuModel:
         h = C.c_void_p()
         ctx.check(lib().lastro_model_create(ctx.h, C.byref(d), max_len, C.byref(h)))
         self.h = h
+        ctx._children.add(self)
         self._logits = np.empty(cfg["vocab"], np.float32)
         self._ids = np.empty(cfg["layers"] * cfg["k"], np.int32)
         self._w = np.empty(cfg["layers"] * cfg["k"], np.float32)

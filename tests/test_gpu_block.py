@@ -29,8 +29,13 @@ def test_block_on_gpu_matches_oracle_and_f64(gpu_ctx, pool, E, H, I, k):
         yo, io, wo, lo = O.block_forward(pool, router, gu, dn, E, H, I, k, x)
         want, wids = naive_block(router, gu, dn, x, k)
         assert ids.tolist() == wids.tolist() == io.tolist(), f"token {t}"
-        np.testing.assert_allclose(w, wo, rtol=1e-6, atol=1e-7)
+        # the kernel's softmax over its own top-k logits (block.rs:85-88) ...
+        ex = np.exp((lg[ids] - lg[ids[0]]).astype(np.float32))
+        np.testing.assert_allclose(w, ex / ex.sum(), rtol=2e-6, atol=1e-7)
+        # ... and against the oracle: logits differ by summation order (~1e-6 relative), which the softmax scales
+        # by the logit magnitude
         np.testing.assert_allclose(lg, lo, rtol=1e-5, atol=1e-5)
+        np.testing.assert_allclose(w, wo, rtol=1e-3, atol=1e-6)
         assert rel_l2(y, want) < REL, f"token {t}: {rel_l2(y, want):.2e}"
         assert rel_l2(y, yo) < REL
     layer.close()

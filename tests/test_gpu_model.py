@@ -32,8 +32,10 @@ def toks_like_reference(n, vocab, seed=77):
     return [int((float(v) + 1.0) * 16.0) % vocab for v in values(n, seed)]
 
 
-@pytest.mark.parametrize("kv,gate", [("f32", 1e-5), ("bf16", 2e-3)])
-def test_model_matches_oracle_over_more_than_one_page(gpu_ctx, pool, kv, gate):
+# f32 KV: the reference's gate (tests/model.rs:268); bf16 KV rounds every cached K/V element (2^-9 relative), which
+# moves logits by ~1e-3 and the routing weights by ~1e-3 while the routing itself stays identical.
+@pytest.mark.parametrize("kv,gate,wtol", [("f32", 1e-5, 1e-5), ("bf16", 2e-3, 5e-3)])
+def test_model_matches_oracle_over_more_than_one_page(gpu_ctx, pool, kv, gate, wtol):
     """tests/model.rs:252-281 on the reference's tiny model (70 positions: two KV pages, two attention tiles)."""
     cfg = CFG.TINY
     w = reference_tiny_weights(cfg)
@@ -48,7 +50,7 @@ def test_model_matches_oracle_over_more_than_one_page(gpu_ctx, pool, kv, gate):
         assert lg.shape == (cfg["vocab"],)
         assert rel_l2(lg, lo) < gate, f"position {t}: {rel_l2(lg, lo):.2e}"
         assert np.array_equal(ids, io), f"position {t}: routing"
-        np.testing.assert_allclose(rw, wo, rtol=1e-4, atol=1e-6)
+        np.testing.assert_allclose(rw, wo, atol=wtol)
         assert nxt == O.argmax_last(lg)
     # after reset the same sequence gives the same logits (the stale cache is masked by the length)
     m.reset()
