@@ -45,7 +45,9 @@ def parse():
     ap.add_argument("--kv", choices=("bf16", "f32"), default="bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample")
-    ap.add_argument("--profile-only", action="store_true", help="small run for ncu: prefill + a few steps")
+    ap.add_argument("--profile-only", action="store_true", help="small run for ncu: synthetic KV + 3 decode steps")
+    ap.add_argument("--synthetic-kv", action="store_true", help="fill the context with synthetic K/V instead of "
+                    "decoding the prompt through the model")
     return ap.parse_args()
 
 
@@ -194,9 +196,12 @@ def main():
     max_len = a.context + 2 * (K + W) + 64
     model = LB.GpuModel(ctx, cfg, max_len, kv_dtype=a.kv)
     model.fill_synthetic(c["weight_seed"], CFG.WEIGHT_STD, 0.0)
-    prompt = CFG.synthetic_tokens(a.context, c["prompt_seed"], cfg["vocab"])
     t0 = time.time()
-    model.generate(prompt, 1)  # pre-fill the KV cache through the model (untimed)
+    if a.synthetic_kv or a.profile_only:
+        model.fill_kv_synthetic(a.context, c["prompt_seed"], 0.5)
+    else:
+        prompt = CFG.synthetic_tokens(a.context, c["prompt_seed"], cfg["vocab"])
+        model.generate(prompt, 1)  # pre-fill the KV cache through the model (untimed)
     prefill_s = time.time() - t0
     if a.profile_only:
         model.decode(K)

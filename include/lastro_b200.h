@@ -81,6 +81,9 @@ int lastro_model_load_tensor(lastro_model *model, const char *name, int32_t dtyp
                              int32_t ndim, const void *host);
 /* random-init every tensor on the device from the synthetic generator (weights ~ std, norms 1 + norm_std) */
 int lastro_model_fill_synthetic(lastro_model *model, uint64_t seed, float stddev, float norm_stddev);
+/* benchmark/test helper, no reference counterpart: fill every K/V page with synthetic values and set the position
+ * to n, a context of n positions without running n steps */
+int lastro_model_fill_kv_synthetic(lastro_model *model, int32_t n, uint64_t seed, float stddev);
 /* GpuModel::step (gpu_model.rs:251-267): one token; logits [V] (already / logits_scaling), the greedy next token
  * (argmax, last maximum on ties), routes ids/weights [layers*k]; every output may be NULL */
 int lastro_model_step(lastro_model *model, int32_t token, float *logits, int32_t *next_token, int32_t *route_ids,

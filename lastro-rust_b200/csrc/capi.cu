@@ -777,6 +777,33 @@ extern "C" int lastro_model_fill_synthetic(lastro_model* m, uint64_t seed, float
     return LASTRO_OK;
 }
 
+extern "C" int lastro_model_fill_kv_synthetic(lastro_model* m, int32_t n, uint64_t seed, float sd) {
+    if (!m) return LASTRO_E_ARG;
+    lastro_ctx* ctx = m->ctx;
+    if (m->poisoned) return set_err(ctx, LASTRO_E_POISONED, "model unusable after an earlier error");
+    if (n < 0 || n > m->max_len) return set_err(ctx, LASTRO_E_ARG, "fill_kv_synthetic: %d positions (max_len %d)", n, m->max_len);
+    cudaSetDevice(ctx->device);
+    cudaStream_t s = ctx->stream;
+    const lastro_model_desc& d = m->d;
+    const size_t elems = (size_t)m->max_pages * d.kv_heads * kPageSize * d.head_dim;
+    const float sc = synth_scale(sd);
+    for (int l = 0; l < d.layers; ++l) {
+        const uint64_t sk = tensor_seed(seed, l, 100), sv = tensor_seed(seed, l, 101);
+        if (d.kv_dtype == LASTRO_DTYPE_F32) {
+            MTRY(launch_synth_f32(static_cast<float*>(m->L[l].k_pool), elems, sk, sc, s), "kv fill");
+            MTRY(launch_synth_f32(static_cast<float*>(m->L[l].v_pool), elems, sv, sc, s), "kv fill");
+        } else {
+            MTRY(launch_synth_bf16(static_cast<uint16_t*>(m->L[l].k_pool), elems, sk, sc, 0.0f, s), "kv fill");
+            MTRY(launch_synth_bf16(static_cast<uint16_t*>(m->L[l].v_pool), elems, sv, sc, 0.0f, s), "kv fill");
+        }
+    }
+    MTRY(cudaMemcpyAsync(m->d_pos, &n, sizeof(int), cudaMemcpyHostToDevice, s), "kv fill");
+    MTRY(cudaMemsetAsync(m->d_step, 0, sizeof(int), s), "kv fill");
+    MTRY(cudaStreamSynchronize(s), "kv fill");
+    m->pos_host = n;
+    return LASTRO_OK;
+}
+
 extern "C" int lastro_model_step(lastro_model* m, int32_t token, float* logits, int32_t* next_token, int32_t* route_ids,
                                  float* route_weights) {
     if (!m) return LASTRO_E_ARG;

@@ -599,6 +599,11 @@ __global__ void synth_bf16_kernel(uint16_t* out, size_t n, uint64_t seed, float 
     }
 }
 
+__global__ void synth_f32_kernel(float* out, size_t n, uint64_t seed, float scale) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = synth_value(seed, i, scale);
+}
+
 __global__ void synth_norm_kernel(float* out, size_t n, uint64_t seed, float scale) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const float v = __fadd_rn(synth_value(seed, i, scale), 1.0f);
@@ -697,6 +702,14 @@ cudaError_t launch_synth_bf16(uint16_t* out, size_t n, uint64_t seed, float scal
     size_t blocks = (n + 255) / 256;
     if (blocks > 148 * 64) blocks = 148 * 64;
     synth_bf16_kernel<<<(unsigned)blocks, 256, 0, s>>>(out, n, seed, scale, mean);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_synth_f32(float* out, size_t n, uint64_t seed, float scale, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    size_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 64) blocks = 148 * 64;
+    synth_f32_kernel<<<(unsigned)blocks, 256, 0, s>>>(out, n, seed, scale);
     return cudaGetLastError();
 }
 

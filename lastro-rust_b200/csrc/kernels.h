@@ -126,6 +126,7 @@ int head_grid(int V);
 // Synthetic fill (same integer formula as the CPU oracle): value(i) = (sum of four 16-bit chunks of
 // mix64(seed + (i+1)*golden) - 131070) * scale (+ mean), rounded to bf16.
 cudaError_t launch_synth_bf16(uint16_t* out, size_t n, uint64_t seed, float scale, float mean, cudaStream_t s);
+cudaError_t launch_synth_f32(float* out, size_t n, uint64_t seed, float scale, cudaStream_t s);
 // norms: bf16(1 + value) widened to f32
 cudaError_t launch_synth_norm_f32(float* out, size_t n, uint64_t seed, float scale, cudaStream_t s);
 

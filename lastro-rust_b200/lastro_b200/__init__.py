@@ -61,6 +61,7 @@ EXPORTS = {
     "lastro_model_load_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int32, C.POINTER(C.c_int64), C.c_int32,
                                            C.c_void_p]),
     "lastro_model_fill_synthetic": (C.c_int, [C.c_void_p, C.c_uint64, C.c_float, C.c_float]),
+    "lastro_model_fill_kv_synthetic": (C.c_int, [C.c_void_p, C.c_int32, C.c_uint64, C.c_float]),
     "lastro_model_step": (C.c_int, [C.c_void_p, C.c_int32] + [C.c_void_p] * 4),
     "lastro_model_generate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
     "lastro_model_decode": (C.c_int, [C.c_void_p, C.c_int32]),
@@ -201,6 +202,10 @@ class GpuModel:
 
     def fill_synthetic(self, seed: int, std: float = 0.02, norm_std: float = 0.0):
         self.ctx.check(lib().lastro_model_fill_synthetic(self.h, seed, std, norm_std))
+
+    def fill_kv_synthetic(self, n: int, seed: int = 7, std: float = 0.5):
+        """A context of n positions with synthetic K/V (no model steps): for benchmarks and profiling."""
+        self.ctx.check(lib().lastro_model_fill_kv_synthetic(self.h, n, seed, std))
 
     def step(self, token: int, want_logits: bool = True, want_routes: bool = True):
         """(logits, next_token, route_ids [L,k], route_w [L,k]) (GpuModel::step)."""
