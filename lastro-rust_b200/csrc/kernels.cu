@@ -1,10 +1,13 @@
 // Batch-1 Granite-MoE decode kernels for sm_100a.
 //
 // Design (B200): every kernel is one streaming pass over bf16 weights with 16-byte non-coherent loads, a warp per
-// output row (or row pair), f32 activations staged in shared memory and warp-shuffle reductions.  Weight loads that
-// do not depend on the previous kernel are issued before griddepcontrol.wait, so with programmatic dependent launch
-// a kernel's HBM traffic overlaps the tail of its predecessor.  Cross-CTA reductions (router top-k, attention split
-// merge, lm_head argmax) use a last-CTA ticket instead of a second launch.
+// output row (or row pair), f32 activations staged in shared memory and warp-shuffle reductions.  At batch 1 each
+// kernel is short (a few microseconds), so the design goal is memory-level parallelism on the critical path: every
+// thread issues all of its loads before it consumes any of them (no load -> use -> load chains), and loads that do
+// not depend on the previous kernel (weights, norm weights, expert ids two kernels back) are issued before
+// griddepcontrol.wait, so with programmatic dependent launch a kernel's HBM traffic overlaps the tail of its
+// predecessor.  Cross-CTA reductions (router top-k, attention split merge, lm_head argmax) use a last-CTA ticket
+// instead of a second launch.
 //
 // Reference behaviour restated (brenoperucchi/lastro-rust, rust/moe-rt/src):
 //   RMSNorm  model.rs:141-145   RoPE rotate_half model.rs:147-158   attention model.rs:203-222
@@ -32,24 +35,74 @@ cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStrea
     return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
-// y = ln * (x * r), r = 1/sqrt(mean(x^2) + eps), into shared memory (model.rs:141-145; the sum of squares is a
-// parallel reduction here).  Returns r.  `x` is read through L2 (written by an earlier kernel).
-LDEV float norm_to_smem(const float* x, const float* ln, int H, float eps, float* xs, float* red) {
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) {
-        float v = __ldcg(x + i);
-        xs[i] = v;
-        ss = fmaf(v, v, ss);
+// ---- vectors of H floats, NV float4 per thread (H <= 4 * NV * BLOCK, H a multiple of 4) ---------------------------
+
+template <int BLOCK, int NV>
+LDEV void vec_load_cg(const float* p, int n, float4 (&r)[NV]) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int i = threadIdx.x + k * BLOCK;
+        r[k] = (4 * i < n) ? __ldcg(reinterpret_cast<const float4*>(p) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    float tot = block_sum(ss, red);
-    float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)H), eps)));
-    for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = __fmul_rn(__ldg(ln + i), __fmul_rn(xs[i], r));
+}
+
+template <int BLOCK, int NV>
+LDEV void vec_load_ldg(const float* p, int n, float4 (&r)[NV]) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int i = threadIdx.x + k * BLOCK;
+        r[k] = (4 * i < n) ? __ldg(reinterpret_cast<const float4*>(p) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+LDEV float4 ln_times(float4 ln, float4 v, float r) {
+    // model.rs:144: g * (v * r)
+    return make_float4(__fmul_rn(ln.x, __fmul_rn(v.x, r)), __fmul_rn(ln.y, __fmul_rn(v.y, r)),
+                       __fmul_rn(ln.z, __fmul_rn(v.z, r)), __fmul_rn(ln.w, __fmul_rn(v.w, r)));
+}
+
+// xs = ln * (v * r), r = 1/sqrt(mean(v^2) + eps) (model.rs:141-145; the sum of squares is a parallel reduction
+// here).  v and ln are already in registers.  Returns r.
+template <int BLOCK, int NV>
+LDEV float norm_regs(const float4 (&v)[NV], const float4 (&ln)[NV], int H, float eps, float* xs, float* red) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        ss = fmaf(v[k].x, v[k].x, ss);
+        ss = fmaf(v[k].y, v[k].y, ss);
+        ss = fmaf(v[k].z, v[k].z, ss);
+        ss = fmaf(v[k].w, v[k].w, ss);
+    }
+    const float tot = block_sum(ss, red);
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)H), eps)));
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int i = threadIdx.x + k * BLOCK;
+        if (4 * i < H) reinterpret_cast<float4*>(xs)[i] = ln_times(ln[k], v[k], r);
+    }
     __syncthreads();
     return r;
 }
 
-LDEV void copy_to_smem(const float* x, int n, float* xs) {
-    for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = __ldcg(x + i);
+// n floats (n a multiple of 4) to shared memory, eight independent 16-byte loads in flight per thread
+template <int BLOCK>
+LDEV void copy_to_smem(const float* src, int n, float* dst) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    const int n4 = n >> 2;
+    for (int base = 0; base < n4; base += 8 * BLOCK) {
+        float4 t[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int i = base + threadIdx.x + k * BLOCK;
+            if (i < n4) t[k] = __ldcg(s4 + i);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int i = base + threadIdx.x + k * BLOCK;
+            if (i < n4) d4[i] = t[k];
+        }
+    }
     __syncthreads();
 }
 
@@ -59,10 +112,10 @@ LDEV float row_dot(const uint4 (&w)[NCH], const float* xs, int H, int lane) {
     float acc = 0.0f;
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
-        int col = (c * 32 + lane) * 8;
+        const int col = (c * 32 + lane) * 8;
         if (col < H) {
-            float4 xa = *reinterpret_cast<const float4*>(xs + col);
-            float4 xb = *reinterpret_cast<const float4*>(xs + col + 4);
+            const float4 xa = *reinterpret_cast<const float4*>(xs + col);
+            const float4 xb = *reinterpret_cast<const float4*>(xs + col + 4);
             acc = dot8(w[c], xa, xb, acc);
         }
     }
@@ -73,7 +126,7 @@ template <int NCH>
 LDEV void load_row(uint4 (&w)[NCH], const uint16_t* row, int H, int lane, bool active) {
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
-        int col = (c * 32 + lane) * 8;
+        const int col = (c * 32 + lane) * 8;
         if (active && col < H)
             w[c] = ld_weight(row + col);
         else
@@ -81,18 +134,26 @@ LDEV void load_row(uint4 (&w)[NCH], const uint16_t* row, int H, int lane, bool a
     }
 }
 
+// float4 per thread for a vector of NCH*256 floats over BLOCK threads
+template <int NCH, int BLOCK>
+struct Vec {
+    static constexpr int NV = (NCH * 64 + BLOCK - 1) / BLOCK;
+};
+
 // ------------------------------------------------------------------------------------------------------------------
 // qkv_rope: one warp per row pair (j, j + d/2) of a head, so RoPE's rotate_half partner is in the same warp.
 // ------------------------------------------------------------------------------------------------------------------
 template <int NCH, bool KV_F32>
 __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
-    extern __shared__ float smem[];
+    constexpr int BLOCK = 128;
+    constexpr int NV = Vec<NCH, BLOCK>::NV;
+    extern __shared__ __align__(16) float smem[];
     float* xs = smem;
     float* red = smem + a.H;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int half = a.d >> 1;
     const int npairs = (a.qd + 2 * a.kvd) >> 1;
-    const int pair = blockIdx.x * (blockDim.x >> 5) + warp;
+    const int pair = blockIdx.x * (BLOCK >> 5) + warp;
     const bool active = pair < npairs;
     const int head = pair / half, j = pair - (pair / half) * half;
     const int r0 = head * a.d + j, r1 = r0 + half;
@@ -100,33 +161,38 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
     uint4 w0[NCH], w1[NCH];
     load_row<NCH>(w0, a.w + (size_t)r0 * a.H, a.H, lane, active);
     load_row<NCH>(w1, a.w + (size_t)r1 * a.H, a.H, lane, active);
+    float4 ln[NV];
+    vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
 
     pdl_wait();
     pdl_launch();
 
     const int pos = __ldcg(a.pos);
+    float4 v[NV];
     if (a.embed_mode) {
         // model.rs:134-138: embedding row x embedding_multiplier is the residual stream of layer 0
         const int tok = __ldcg(a.token);
-        const uint16_t* er = a.embed + (size_t)tok * a.H;
-        float ss = 0.0f;
-        for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
-            float v = __fmul_rn(__uint_as_float((uint32_t)er[i] << 16), a.emb_mult);
-            xs[i] = v;
-            if (blockIdx.x == 0) a.h_write[i] = v;
-            ss = fmaf(v, v, ss);
+        const uint2* er = reinterpret_cast<const uint2*>(a.embed + (size_t)tok * a.H);  // 4 bf16 per uint2
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            const int i = threadIdx.x + k * BLOCK;
+            if (4 * i < a.H) {
+                const uint2 u = __ldg(er + i);
+                v[k] = make_float4(__fmul_rn(bf_lo(u.x), a.emb_mult), __fmul_rn(bf_hi(u.x), a.emb_mult),
+                                   __fmul_rn(bf_lo(u.y), a.emb_mult), __fmul_rn(bf_hi(u.y), a.emb_mult));
+                if (blockIdx.x == 0) reinterpret_cast<float4*>(a.h_write)[i] = v[k];
+            } else {
+                v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
         }
-        float tot = block_sum(ss, red);
-        float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.H), a.eps)));
-        for (int i = threadIdx.x; i < a.H; i += blockDim.x) xs[i] = __fmul_rn(__ldg(a.ln + i), __fmul_rn(xs[i], r));
-        __syncthreads();
     } else {
-        norm_to_smem(a.h, a.ln, a.H, a.eps, xs, red);
+        vec_load_cg<BLOCK, NV>(a.h, a.H, v);
     }
+    norm_regs<BLOCK, NV>(v, ln, a.H, a.eps, xs, red);
     if (!active) return;
 
-    float x1 = warp_sum(row_dot<NCH>(w0, xs, a.H, lane));
-    float x2 = warp_sum(row_dot<NCH>(w1, xs, a.H, lane));
+    const float x1 = warp_sum(row_dot<NCH>(w0, xs, a.H, lane));
+    const float x2 = warp_sum(row_dot<NCH>(w1, xs, a.H, lane));
     if (lane != 0) return;
     const float* cs = a.rope_cs + (size_t)pos * a.d;
     const float c = __ldg(cs + j), s = __ldg(cs + half + j);
@@ -158,25 +224,25 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------------------------------
-// attention: CTA (split s, kv head). Each lane scores one position against the G query heads of the group
-// (GQA: the K/V rows are read once for all G heads), online softmax per warp, warps merged in shared memory,
-// then the last CTA of the KV head merges the splits (flash-decoding).  Positions past `len` are never read.
+// attention: CTA (split s, kv head).  A warp takes 32 positions at a time, one per lane: the lane loads its K row and
+// its V row together (16 independent 16-byte loads for bf16), scores the row against the G query heads of the group
+// (GQA: the K/V rows are read once for all G heads), the warp updates its online softmax, stages the V rows in shared
+// memory and accumulates P.V with lane l owning dims 2l, 2l+1.  Warps merge in shared memory, then the last CTA of
+// the KV head merges the splits (flash-decoding).  Positions past `len` are never read.
 // ------------------------------------------------------------------------------------------------------------------
-template <bool KV_F32>
-LDEV const void* kv_row(const void* pool, const int* page_table, int page_size, int kv_heads, int kvh, int p) {
-    const int page = __ldcg(page_table + p / page_size), slot = p - (p / page_size) * page_size;
-    const size_t off = (((size_t)page * kv_heads + kvh) * page_size + slot) * kHeadDim;
-    if (KV_F32) return static_cast<const float*>(pool) + off;
-    return static_cast<const uint16_t*>(pool) + off;
-}
-
 template <bool KV_F32, int G>
 __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
     constexpr int D = kHeadDim;
     constexpr int NW = 4;
+    constexpr int ESZ = KV_F32 ? 4 : 2;
+    constexpr int CH = D * ESZ / 16;  // 16-byte chunks per row: 8 (bf16) or 16 (f32)
+    constexpr int MAXS = 64;          // splits handled by the merge
     __shared__ __align__(16) float sq[G][D];
+    __shared__ __align__(16) uint4 vt[NW][32][CH];
     __shared__ float sm_m[NW][G], sm_l[NW][G];
     __shared__ float sacc[NW][G][D];
+    __shared__ float cw[MAXS][G];
+    __shared__ float cden[G];
     __shared__ bool is_last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int s = blockIdx.x, kvh = blockIdx.y;
@@ -186,7 +252,8 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
 
     const int len = __ldcg(a.pos) + 1;
     const int p0 = (int)(((long long)len * s) / a.ns), p1 = (int)(((long long)len * (s + 1)) / a.ns);
-    for (int i = threadIdx.x; i < G * D; i += blockDim.x) sq[i / D][i % D] = __ldcg(a.q + (size_t)kvh * G * D + i);
+    for (int i = threadIdx.x; i < G * D / 4; i += blockDim.x)
+        reinterpret_cast<float4*>(&sq[0][0])[i] = __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)kvh * G * D) + i);
     __syncthreads();
 
     float m[G], l[G], acc0[G], acc1[G];
@@ -201,35 +268,41 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
     for (int base = p0 + warp * 32; base < p1; base += NW * 32) {
         const int p = base + lane;
         const bool valid = p < p1;
+        const uint4* kr = nullptr;
+        const uint4* vr = nullptr;
+        if (valid) {
+            const int page = __ldcg(a.page_table + p / a.page_size), slot = p - (p / a.page_size) * a.page_size;
+            const size_t off = ((((size_t)page * a.kv_heads + kvh) * a.page_size + slot) * D) * ESZ / 16;
+            kr = static_cast<const uint4*>(a.k_pool) + off;
+            vr = static_cast<const uint4*>(a.v_pool) + off;
+        }
         float sc[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) sc[g] = 0.0f;
-        if (valid) {
-            const void* kr = kv_row<KV_F32>(a.k_pool, a.page_table, a.page_size, a.kv_heads, kvh, p);
-            if (KV_F32) {
-                const float4* k4 = static_cast<const float4*>(kr);
+        // K and V rows: all loads of a group issued before any is used
 #pragma unroll
-                for (int c = 0; c < D / 4; ++c) {
-                    float4 kv = __ldcg(k4 + c);
+        for (int c0 = 0; c0 < CH; c0 += 8) {
+            uint4 kc[8], vc[8];
 #pragma unroll
-                    for (int g = 0; g < G; ++g) {
-                        float4 qv = *reinterpret_cast<const float4*>(&sq[g][c * 4]);
-                        sc[g] = fmaf(qv.x, kv.x, sc[g]);
-                        sc[g] = fmaf(qv.y, kv.y, sc[g]);
-                        sc[g] = fmaf(qv.z, kv.z, sc[g]);
-                        sc[g] = fmaf(qv.w, kv.w, sc[g]);
-                    }
-                }
-            } else {
-                const uint4* k8 = static_cast<const uint4*>(kr);
+            for (int c = 0; c < 8; ++c) {
+                kc[c] = valid ? __ldcg(kr + c0 + c) : make_uint4(0u, 0u, 0u, 0u);
+                vc[c] = valid ? __ldcg(vr + c0 + c) : make_uint4(0u, 0u, 0u, 0u);
+            }
 #pragma unroll
-                for (int c = 0; c < D / 8; ++c) {
-                    uint4 kv = __ldcg(k8 + c);
+            for (int c = 0; c < 8; ++c) {
+                vt[warp][lane][(c0 + c) ^ (lane & 7)] = vc[c];  // XOR swizzle: conflict-free stores
 #pragma unroll
-                    for (int g = 0; g < G; ++g) {
-                        float4 qa = *reinterpret_cast<const float4*>(&sq[g][c * 8]);
-                        float4 qb = *reinterpret_cast<const float4*>(&sq[g][c * 8 + 4]);
-                        sc[g] = dot8(kv, qa, qb, sc[g]);
+                for (int g = 0; g < G; ++g) {
+                    if (KV_F32) {
+                        const float4 qv = *reinterpret_cast<const float4*>(&sq[g][(c0 + c) * 4]);
+                        sc[g] = fmaf(qv.x, __uint_as_float(kc[c].x), sc[g]);
+                        sc[g] = fmaf(qv.y, __uint_as_float(kc[c].y), sc[g]);
+                        sc[g] = fmaf(qv.z, __uint_as_float(kc[c].z), sc[g]);
+                        sc[g] = fmaf(qv.w, __uint_as_float(kc[c].w), sc[g]);
+                    } else {
+                        const float4 qa = *reinterpret_cast<const float4*>(&sq[g][(c0 + c) * 8]);
+                        const float4 qb = *reinterpret_cast<const float4*>(&sq[g][(c0 + c) * 8 + 4]);
+                        sc[g] = dot8(kc[c], qa, qb, sc[g]);
                     }
                 }
             }
@@ -247,16 +320,18 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
             acc1[g] *= alpha;
             m[g] = mn;
         }
+        __syncwarp();
         const int nj = min(32, p1 - base);
         for (int jj = 0; jj < nj; ++jj) {
-            const void* vr = kv_row<KV_F32>(a.v_pool, a.page_table, a.page_size, a.kv_heads, kvh, base + jj);
             float v0, v1;
             if (KV_F32) {
-                float2 t = __ldcg(static_cast<const float2*>(vr) + lane);
+                const float2 t =
+                    reinterpret_cast<const float2*>(&vt[warp][jj][0])[(((lane >> 1) ^ (jj & 7)) << 1) | (lane & 1)];
                 v0 = t.x;
                 v1 = t.y;
             } else {
-                uint32_t t = __ldcg(static_cast<const unsigned int*>(vr) + lane);
+                const uint32_t t =
+                    reinterpret_cast<const uint32_t*>(&vt[warp][jj][0])[(((lane >> 2) ^ (jj & 7)) << 2) | (lane & 3)];
                 v0 = bf_lo(t);
                 v1 = bf_hi(t);
             }
@@ -267,6 +342,7 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
                 acc1[g] = fmaf(pj, v1, acc1[g]);
             }
         }
+        __syncwarp();
     }
 
 #pragma unroll
@@ -282,9 +358,11 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
     for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
         const int g = t / D, dim = t - (t / D) * D;
         float M = -INFINITY;
+#pragma unroll
         for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_m[w][g]);
         float L = 0.0f, A = 0.0f;
         if (M != -INFINITY) {
+#pragma unroll
             for (int w = 0; w < NW; ++w) {
                 if (sm_m[w][g] == -INFINITY) continue;
                 const float e = expf(sm_m[w][g] - M);
@@ -301,20 +379,31 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
     }
 
     if (!last_block_arrives(a.counters + kvh, (unsigned int)a.ns, &is_last)) return;
+    // merge: per-split weights exp(m_s - M) in shared memory, then every (g, dim) sums the splits
+    const float* ml = a.part_ml + (size_t)kvh * a.ns * G * 2;
+    for (int i = threadIdx.x; i < a.ns * G; i += blockDim.x) cw[i / G][i % G] = __ldcg(ml + 2 * i);
+    __syncthreads();
+    if (threadIdx.x < G) {
+        const int g = threadIdx.x;
+        float M = -INFINITY;
+        for (int sp = 0; sp < a.ns; ++sp) M = fmaxf(M, cw[sp][g]);
+        float den = 0.0f;
+        for (int sp = 0; sp < a.ns; ++sp) {
+            const float ms = cw[sp][g];
+            const float e = (ms == -INFINITY) ? 0.0f : expf(ms - M);
+            den = fmaf(__ldcg(ml + 2 * (sp * G + g) + 1), e, den);
+            cw[sp][g] = e;
+        }
+        cden[g] = den;
+    }
+    __syncthreads();
+    const float* pa = a.part_acc + (size_t)kvh * a.ns * G * D;
     for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
         const int g = t / D, dim = t - (t / D) * D;
-        float M = -INFINITY;
-        for (int sp = 0; sp < a.ns; ++sp) M = fmaxf(M, __ldcg(a.part_ml + (((size_t)kvh * a.ns + sp) * G + g) * 2));
-        float num = 0.0f, den = 0.0f;
-        for (int sp = 0; sp < a.ns; ++sp) {
-            const size_t slot = ((size_t)kvh * a.ns + sp) * G + g;
-            const float ms = __ldcg(a.part_ml + slot * 2);
-            if (ms == -INFINITY) continue;
-            const float e = expf(ms - M);
-            den = fmaf(__ldcg(a.part_ml + slot * 2 + 1), e, den);
-            num = fmaf(__ldcg(a.part_acc + slot * D + dim), e, num);
-        }
-        a.att_out[((size_t)kvh * G + g) * D + dim] = num / den;
+        float num = 0.0f;
+#pragma unroll 8
+        for (int sp = 0; sp < a.ns; ++sp) num = fmaf(__ldcg(pa + ((size_t)sp * G + g) * D + dim), cw[sp][g], num);
+        a.att_out[((size_t)kvh * G + g) * D + dim] = num / cden[g];
     }
 }
 
@@ -323,19 +412,21 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
 // ------------------------------------------------------------------------------------------------------------------
 template <int NCH>
 __global__ void __launch_bounds__(128) oproj_kernel(OprojArgs a) {
-    extern __shared__ float smem[];
+    constexpr int BLOCK = 128;
+    extern __shared__ __align__(16) float smem[];
     float* xs = smem;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int row = blockIdx.x * (blockDim.x >> 5) + warp;
+    const int row = blockIdx.x * (BLOCK >> 5) + warp;
     const bool active = row < a.H;
     uint4 w[NCH];
     load_row<NCH>(w, a.w + (size_t)row * a.qd, a.qd, lane, active);
     pdl_wait();
     pdl_launch();
-    copy_to_smem(a.att, a.qd, xs);
+    const float hr = (active && lane == 0) ? __ldcg(a.h + row) : 0.0f;
+    copy_to_smem<BLOCK>(a.att, a.qd, xs);
     if (!active) return;
     const float o = warp_sum(row_dot<NCH>(w, xs, a.qd, lane));
-    if (lane == 0) a.h[row] = __fadd_rn(__ldcg(a.h + row), __fmul_rn(a.resid, o));
+    if (lane == 0) a.h[row] = __fadd_rn(hr, __fmul_rn(a.resid, o));
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -356,22 +447,28 @@ LDEV unsigned long long shfl_xor_u64(unsigned long long v, int o) {
 
 template <int NCH>
 __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
-    extern __shared__ float smem[];
+    constexpr int BLOCK = 128;
+    constexpr int NV = Vec<NCH, BLOCK>::NV;
+    extern __shared__ __align__(16) float smem[];
     float* xs = smem;
     float* red = smem + a.H;
     __shared__ bool is_last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int e = blockIdx.x * (blockDim.x >> 5) + warp;
+    const int e = blockIdx.x * (BLOCK >> 5) + warp;
     const bool active = e < a.E;
     uint4 w[NCH];
     load_row<NCH>(w, a.w + (size_t)e * a.H, a.H, lane, active);
+    float4 ln[NV];
+    if (a.norm_mode) vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
     pdl_wait();
     pdl_launch();
     if (a.norm_mode) {
-        const float r = norm_to_smem(a.x, a.ln, a.H, a.eps, xs, red);
+        float4 v[NV];
+        vec_load_cg<BLOCK, NV>(a.x, a.H, v);
+        const float r = norm_regs<BLOCK, NV>(v, ln, a.H, a.eps, xs, red);
         if (blockIdx.x == 0 && threadIdx.x == 0) *a.rnorm_out = r;
     } else {
-        copy_to_smem(a.x, a.H, xs);
+        copy_to_smem<BLOCK>(a.x, a.H, xs);
     }
     if (active) {
         const float lg = warp_sum(row_dot<NCH>(w, xs, a.H, lane));
@@ -380,24 +477,25 @@ __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
     if (!last_block_arrives(a.counter, gridDim.x, &is_last)) return;
     if (warp != 0) return;
     // E <= 64: lane holds experts lane and lane + 32
-    float v0 = lane < a.E ? __ldcg(a.logits + lane) : 0.0f;
-    float v1 = lane + 32 < a.E ? __ldcg(a.logits + lane + 32) : 0.0f;
+    const float v0 = lane < a.E ? __ldcg(a.logits + lane) : 0.0f;
+    const float v1 = lane + 32 < a.E ? __ldcg(a.logits + lane + 32) : 0.0f;
     unsigned long long k0 = lane < a.E ? route_key(v0, lane) : 0ull;
     unsigned long long k1 = lane + 32 < a.E ? route_key(v1, lane + 32) : 0ull;
     int ids[kMaxTopK];
     float vals[kMaxTopK];
-    for (int j = 0; j < a.k; ++j) {
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) {
+        if (j >= a.k) break;
         unsigned long long b = k0 > k1 ? k0 : k1;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
-            unsigned long long t = shfl_xor_u64(b, o);
+            const unsigned long long t = shfl_xor_u64(b, o);
             b = t > b ? t : b;
         }
         const int idx = (int)(~(uint32_t)b);
         ids[j] = idx;
         const int src = idx & 31;
-        const float val = __shfl_sync(0xffffffffu, idx < 32 ? v0 : v1, src);
-        vals[j] = val;
+        vals[j] = __shfl_sync(0xffffffffu, idx < 32 ? v0 : v1, src);
         if (lane == src) {
             if (idx < 32)
                 k0 = 0ull;
@@ -409,12 +507,18 @@ __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
         // block.rs:85-88: exp(v - v0) over the k in order, then divide by their sum
         float ex[kMaxTopK];
         float sum = 0.0f;
-        for (int j = 0; j < a.k; ++j) ex[j] = expf(__fsub_rn(vals[j], vals[0]));
-        for (int j = 0; j < a.k; ++j) sum = __fadd_rn(sum, ex[j]);
-        for (int j = 0; j < a.k; ++j) {
-            a.ids[j] = ids[j];
-            a.weights[j] = __fdiv_rn(ex[j], sum);
-        }
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j)
+            if (j < a.k) ex[j] = expf(__fsub_rn(vals[j], vals[0]));
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j)
+            if (j < a.k) sum = __fadd_rn(sum, ex[j]);
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j)
+            if (j < a.k) {
+                a.ids[j] = ids[j];
+                a.weights[j] = __fdiv_rn(ex[j], sum);
+            }
     }
 }
 
@@ -424,37 +528,40 @@ __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
 // ------------------------------------------------------------------------------------------------------------------
 template <int NCH>
 __global__ void __launch_bounds__(128) gate_up_kernel(GateUpArgs a) {
-    extern __shared__ float smem[];
+    constexpr int BLOCK = 128;
+    constexpr int NV = Vec<NCH, BLOCK>::NV;
+    extern __shared__ __align__(16) float smem[];
     float* xs = smem;
-    float* red = smem + a.H;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int item = blockIdx.x * (blockDim.x >> 5) + warp;
+    const int item = blockIdx.x * (BLOCK >> 5) + warp;
     const bool active = item < a.k * a.I;
     const int slot = item / a.I, j = item - (item / a.I) * a.I;
+    float4 ln[NV];
+    if (a.norm_mode) vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
 
     pdl_wait();
     pdl_launch();
 
     uint4 wg[NCH], wu[NCH];
-    if (active) {
-        // expert ids come from the router; clamped so that a stale id can never address outside the weights
-        const int e = min(max(__ldcg(a.ids + slot), 0), a.E - 1);
-        const uint16_t* base = a.w + (size_t)e * 2 * a.I * a.H;
-        load_row<NCH>(wg, base + (size_t)j * a.H, a.H, lane, true);
-        load_row<NCH>(wu, base + (size_t)(a.I + j) * a.H, a.H, lane, true);
-    } else {
-        load_row<NCH>(wg, a.w, a.H, lane, false);
-        load_row<NCH>(wu, a.w, a.H, lane, false);
-    }
+    // expert ids come from the router; clamped so that a stale id can never address outside the weights
+    const int e = active ? min(max(__ldcg(a.ids + slot), 0), a.E - 1) : 0;
+    const uint16_t* base = a.w + (size_t)e * 2 * a.I * a.H;
+    load_row<NCH>(wg, base + (size_t)j * a.H, a.H, lane, active);
+    load_row<NCH>(wu, base + (size_t)(a.I + j) * a.H, a.H, lane, active);
     if (a.norm_mode) {
         // xn = ln * (h * r) with the router's r
+        float4 v[NV];
+        vec_load_cg<BLOCK, NV>(a.x, a.H, v);
         const float r = __ldcg(a.rnorm);
-        for (int i = threadIdx.x; i < a.H; i += blockDim.x) xs[i] = __fmul_rn(__ldg(a.ln + i), __fmul_rn(__ldcg(a.x + i), r));
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            const int i = threadIdx.x + k * BLOCK;
+            if (4 * i < a.H) reinterpret_cast<float4*>(xs)[i] = ln_times(ln[k], v[k], r);
+        }
         __syncthreads();
     } else {
-        copy_to_smem(a.x, a.H, xs);
+        copy_to_smem<BLOCK>(a.x, a.H, xs);
     }
-    (void)red;
     if (!active) return;
     const float g = warp_sum(row_dot<NCH>(wg, xs, a.H, lane));
     const float u = warp_sum(row_dot<NCH>(wu, xs, a.H, lane));
@@ -468,23 +575,28 @@ __global__ void __launch_bounds__(128) gate_up_kernel(GateUpArgs a) {
 // ------------------------------------------------------------------------------------------------------------------
 template <int NCI>
 __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
-    extern __shared__ float smem[];
+    constexpr int BLOCK = 256;
+    extern __shared__ __align__(16) float smem[];
     float* as = smem;  // [k, I]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int row = blockIdx.x * (blockDim.x >> 5) + warp;
+    const int row = blockIdx.x * (BLOCK >> 5) + warp;
     const bool active = row < a.H;
     uint4 w[kMaxTopK][NCI];
     float gw[kMaxTopK];
+    int ex[kMaxTopK];
 #pragma unroll
     for (int j = 0; j < kMaxTopK; ++j) {
         const bool on = active && j < a.k;
-        const int e = on ? min(max(__ldcg(a.ids + j), 0), a.E - 1) : 0;
+        ex[j] = on ? min(max(__ldcg(a.ids + j), 0), a.E - 1) : 0;
         gw[j] = on ? __ldcg(a.weights + j) : 0.0f;
-        load_row<NCI>(w[j], a.w + ((size_t)e * a.H + row) * a.I, a.I, lane, on);
     }
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j)
+        load_row<NCI>(w[j], a.w + ((size_t)ex[j] * a.H + row) * a.I, a.I, lane, active && j < a.k);
     pdl_wait();
     pdl_launch();
-    copy_to_smem(a.a, a.k * a.I, as);
+    const float hr = (active && lane == 0 && a.accumulate) ? __ldcg(a.out + row) : 0.0f;
+    copy_to_smem<BLOCK>(a.a, a.k * a.I, as);
     if (!active) return;
     float acc = 0.0f;
 #pragma unroll
@@ -494,20 +606,17 @@ __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
             acc = __fadd_rn(acc, __fmul_rn(gw[j], d));
         }
     }
-    if (lane == 0) {
-        if (a.accumulate)
-            a.out[row] = __fadd_rn(__ldcg(a.out + row), __fmul_rn(a.resid, acc));
-        else
-            a.out[row] = acc;
-    }
+    if (lane == 0) a.out[row] = a.accumulate ? __fadd_rn(hr, __fmul_rn(a.resid, acc)) : acc;
 }
 
 // ------------------------------------------------------------------------------------------------------------------
 // head: final RMSNorm, logits = (E . xn) / logits_scaling over the tied embedding, argmax keeping the last maximum
-// (Iterator::max_by with total_cmp).  The last CTA publishes the token, appends it to the history and advances pos.
+// (Iterator::max_by with total_cmp).  A fixed grid of CTAs walks the vocabulary two rows per warp at a time with the
+// next pair's weights already in flight; the last CTA publishes the token, appends it to the history and advances
+// the position.
 // ------------------------------------------------------------------------------------------------------------------
-constexpr int kHeadRowsPerWarp = 2;
 constexpr int kHeadWarps = 8;
+constexpr int kHeadCtas = 148 * 2;  // 128 registers x 256 threads: two CTAs per SM
 
 LDEV unsigned long long arg_key(float v, int idx) {
     // larger is better: value by total order, then the larger index (last maximum)
@@ -515,32 +624,57 @@ LDEV unsigned long long arg_key(float v, int idx) {
 }
 
 template <int NCH>
+LDEV void head_rows(const uint4 (&w)[2][NCH], int row, const HeadArgs& a, const float* xs, int lane,
+                    unsigned long long& best) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const float d = warp_sum(row_dot<NCH>(w[r], xs, a.H, lane));
+        if (row + r < a.V) {
+            const float lg = __fdiv_rn(d, a.logits_scaling);
+            if (lane == 0 && a.logits_out) a.logits_out[row + r] = lg;
+            const unsigned long long k = arg_key(lg, row + r);
+            best = k > best ? k : best;
+        }
+    }
+}
+
+template <int NCH>
+LDEV void head_load(uint4 (&w)[2][NCH], int row, const HeadArgs& a, int lane) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) load_row<NCH>(w[r], a.w + (size_t)(row + r) * a.H, a.H, lane, row + r < a.V);
+}
+
+template <int NCH>
 __global__ void __launch_bounds__(256) head_kernel(HeadArgs a) {
-    extern __shared__ float smem[];
+    constexpr int BLOCK = 32 * kHeadWarps;
+    constexpr int NV = Vec<NCH, BLOCK>::NV;
+    extern __shared__ __align__(16) float smem[];
     float* xs = smem;
     float* red = smem + a.H;
     __shared__ unsigned long long wbest[kHeadWarps];
     __shared__ bool is_last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int row0 = (blockIdx.x * kHeadWarps + warp) * kHeadRowsPerWarp;
-    uint4 w[kHeadRowsPerWarp][NCH];
-#pragma unroll
-    for (int r = 0; r < kHeadRowsPerWarp; ++r)
-        load_row<NCH>(w[r], a.w + (size_t)(row0 + r) * a.H, a.H, lane, row0 + r < a.V);
+    const int stride = gridDim.x * kHeadWarps * 2;
+    int row = (blockIdx.x * kHeadWarps + warp) * 2;
+    uint4 wa[2][NCH], wb[2][NCH];
+    head_load<NCH>(wa, row, a, lane);
+    float4 ln[NV];
+    vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
     pdl_wait();
     pdl_launch();
-    norm_to_smem(a.h, a.ln, a.H, a.eps, xs, red);
+    {
+        float4 v[NV];
+        vec_load_cg<BLOCK, NV>(a.h, a.H, v);
+        norm_regs<BLOCK, NV>(v, ln, a.H, a.eps, xs, red);
+    }
     unsigned long long best = 0ull;
-#pragma unroll
-    for (int r = 0; r < kHeadRowsPerWarp; ++r) {
-        const int row = row0 + r;
-        const float d = warp_sum(row_dot<NCH>(w[r], xs, a.H, lane));
-        if (row < a.V) {
-            const float lg = __fdiv_rn(d, a.logits_scaling);
-            if (lane == 0 && a.logits_out) a.logits_out[row] = lg;
-            const unsigned long long k = arg_key(lg, row);
-            best = k > best ? k : best;
-        }
+    // two row pairs per iteration: the loads of one pair are in flight while the other is reduced
+    for (; row < a.V; row += 2 * stride) {
+        head_load<NCH>(wb, row + stride, a, lane);
+        head_rows<NCH>(wa, row, a, xs, lane, best);
+        if (row + stride >= a.V) break;
+        head_load<NCH>(wa, row + 2 * stride, a, lane);
+        head_rows<NCH>(wb, row + stride, a, xs, lane, best);
     }
     if (lane == 0) wbest[warp] = best;
     __syncthreads();
@@ -563,9 +697,9 @@ __global__ void __launch_bounds__(256) head_kernel(HeadArgs a) {
     if (lane == 0) wbest[warp] = b;
     __syncthreads();
     if (threadIdx.x == 0) {
-        unsigned long long m = 0ull;
-        for (int i = 0; i < kHeadWarps; ++i) m = wbest[i] > m ? wbest[i] : m;
-        const int tok = (int)(uint32_t)m;
+        unsigned long long mx = 0ull;
+        for (int i = 0; i < kHeadWarps; ++i) mx = wbest[i] > mx ? wbest[i] : mx;
+        const int tok = (int)(uint32_t)mx;
         *a.token_out = tok;
         if (a.out_ids) {
             const int st = __ldcg(a.step);
@@ -642,6 +776,7 @@ cudaError_t launch_qkv_rope(const QkvArgs& a, cudaStream_t s, bool pdl) {
 }
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
+    if (a.ns < 1 || a.ns > 64 || a.d != kHeadDim) return cudaErrorInvalidValue;
     const dim3 grid(a.ns, a.kv_heads), block(128);
 #define LASTRO_ATTN_G(GV)                                                                      \
     case GV:                                                                                   \
@@ -686,8 +821,9 @@ cudaError_t launch_down(const DownArgs& a, cudaStream_t s, bool pdl) {
 }
 
 int head_grid(int V) {
-    const int rows = kHeadWarps * kHeadRowsPerWarp;
-    return (V + rows - 1) / rows;
+    const int pairs = (V + 1) / 2;
+    const int ctas = (pairs + kHeadWarps - 1) / kHeadWarps;
+    return ctas < kHeadCtas ? ctas : kHeadCtas;
 }
 
 cudaError_t launch_head(const HeadArgs& a, cudaStream_t s, bool pdl, int* grid_out) {
