@@ -147,6 +147,7 @@ struct lastro_layer {
     float *x = nullptr, *y = nullptr, *logits = nullptr, *weights = nullptr, *a = nullptr;
     int* ids = nullptr;
     unsigned int* counter = nullptr;
+    int* err = nullptr;  // device error word of the bounded waits
 };
 
 namespace {
@@ -158,8 +159,8 @@ int check_block_shape(lastro_ctx* c, int E, int H, int I, int k) {
     if (H > kMaxHidden || I > kMaxInter || E > kMaxExperts || k > kMaxTopK)
         return set_err(c, LASTRO_E_UNSUPPORTED, "block shape beyond the kernels' limits (H<=%d I<=%d E<=%d k<=%d)",
                        kMaxHidden, kMaxInter, kMaxExperts, kMaxTopK);
-    if ((size_t)k * I * sizeof(float) > 48 * 1024)
-        return set_err(c, LASTRO_E_UNSUPPORTED, "k*I=%d activations exceed the down kernel's shared memory", k * I);
+    if (down_smem(H, I, k) > kMaxSmemBytes || gate_up_smem(H) > kMaxSmemBytes)
+        return set_err(c, LASTRO_E_UNSUPPORTED, "k=%d, I=%d, H=%d: expert tiles exceed shared memory", k, I, H);
     return LASTRO_OK;
 }
 
@@ -199,6 +200,7 @@ int enqueue_block(lastro_layer* obj, const float* xn, float* out, float resid, i
     ga.ids = obj->ids;
     ga.w = obj->gate_up;
     ga.a = obj->a;
+    ga.err = obj->err;
     ga.H = obj->H;
     ga.I = obj->I;
     ga.k = obj->k;
@@ -212,6 +214,7 @@ int enqueue_block(lastro_layer* obj, const float* xn, float* out, float resid, i
     da.out = out;
     da.resid = resid;
     da.accumulate = accumulate;
+    da.err = obj->err;
     da.H = obj->H;
     da.I = obj->I;
     da.k = obj->k;
@@ -240,7 +243,7 @@ extern "C" int lastro_layer_create(lastro_ctx* ctx, int32_t E, int32_t H, int32_
     const size_t nr = (size_t)E * H, ngu = (size_t)E * 2 * I * H, nd = (size_t)E * H * I;
     if (A.alloc(&obj->router, nr) || A.alloc(&obj->gate_up, ngu) || A.alloc(&obj->down, nd) || A.alloc(&obj->x, H) ||
         A.alloc(&obj->y, H) || A.alloc(&obj->logits, E) || A.alloc(&obj->weights, k) || A.alloc(&obj->a, (size_t)k * I) ||
-        A.alloc(&obj->ids, k) || A.alloc(&obj->counter, 1)) {
+        A.alloc(&obj->ids, k) || A.alloc(&obj->counter, 1) || A.alloc(&obj->err, 1)) {
         cudaGetLastError();
         A.release();
         delete obj;
@@ -251,6 +254,7 @@ extern "C" int lastro_layer_create(lastro_ctx* ctx, int32_t E, int32_t H, int32_
     if (!e) e = cudaMemcpyAsync(obj->down, down, nd * 2, cudaMemcpyHostToDevice, ctx->stream);
     if (!e) e = cudaMemsetAsync(obj->counter, 0, sizeof(unsigned int), ctx->stream);
     if (!e) e = cudaMemsetAsync(obj->ids, 0, sizeof(int) * k, ctx->stream);
+    if (!e) e = cudaMemsetAsync(obj->err, 0, sizeof(int), ctx->stream);
     if (!e) e = cudaMemsetAsync(obj->weights, 0, sizeof(float) * k, ctx->stream);
     if (!e) e = cudaStreamSynchronize(ctx->stream);
     if (e) {
@@ -280,7 +284,13 @@ extern "C" int lastro_layer_forward(lastro_layer* obj, const float* x, float* y,
         LASTRO_TRY(cudaMemcpyAsync(weights, obj->weights, sizeof(float) * obj->k, cudaMemcpyDeviceToHost, s), "w download");
     if (logits)
         LASTRO_TRY(cudaMemcpyAsync(logits, obj->logits, sizeof(float) * obj->E, cudaMemcpyDeviceToHost, s), "logits");
+    int err = 0;
+    LASTRO_TRY(cudaMemcpyAsync(&err, obj->err, sizeof(int), cudaMemcpyDeviceToHost, s), "error word");
     LASTRO_TRY(cudaStreamSynchronize(s), "layer forward");
+    if (err) {
+        obj->poisoned = true;
+        return set_err(ctx, LASTRO_E_CUDA, "a kernel wait gave up (code %d); layer poisoned", err);
+    }
     return LASTRO_OK;
 }
 
@@ -342,7 +352,9 @@ struct lastro_model {
     int* d_prompt = nullptr;
     unsigned int *attn_counters = nullptr, *router_counter = nullptr, *head_counter = nullptr;
     unsigned long long* head_partial = nullptr;
+    int* d_err = nullptr;    // error word of the bounded waits
     int* h_token = nullptr;  // pinned
+    int* h_err = nullptr;    // pinned copy of d_err
     int pos_host = 0;
     std::vector<char> loaded;  // per (layer, kind)
     cudaGraphExec_t graph = nullptr;
@@ -490,6 +502,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         ga.ids = ra.ids;
         ga.w = L.gate_up;
         ga.a = m->a;
+        ga.err = m->d_err;
         ga.H = d.hidden;
         ga.I = d.inter;
         ga.k = d.k;
@@ -505,6 +518,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         da.out = m->h;
         da.resid = d.residual_multiplier;
         da.accumulate = 1;
+        da.err = m->d_err;
         da.H = d.hidden;
         da.I = d.inter;
         da.k = d.k;
@@ -557,6 +571,18 @@ int run_step(lastro_model* m) {
         }
     }
     MTRY(cudaGraphLaunch(m->graph, s), "graph launch");
+    return LASTRO_OK;
+}
+
+// synchronize the stream and report a bounded wait that gave up inside a kernel (poisons the model)
+int finish(lastro_model* m, const char* what) {
+    cudaStream_t s = m->ctx->stream;
+    MTRY(cudaMemcpyAsync(m->h_err, m->d_err, sizeof(int), cudaMemcpyDeviceToHost, s), what);
+    MTRY(cudaStreamSynchronize(s), what);
+    if (*m->h_err) {
+        m->poisoned = true;
+        return set_err(m->ctx, LASTRO_E_CUDA, "%s: a kernel wait gave up (code %d); model poisoned", what, *m->h_err);
+    }
     return LASTRO_OK;
 }
 
@@ -629,8 +655,8 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
           A.alloc(&m->d_token, 1) || A.alloc(&m->d_pos, 1) || A.alloc(&m->d_step, 1) ||
           A.alloc(&m->d_out_ids, (size_t)max_len + 1) || A.alloc(&m->d_prompt, (size_t)max_len + 1) ||
           A.alloc(&m->attn_counters, d.kv_heads) || A.alloc(&m->router_counter, 1) || A.alloc(&m->head_counter, 1) ||
-          A.alloc(&m->head_partial, m->head_grid);
-    if (bad || cudaMallocHost(&m->h_token, sizeof(int)) != cudaSuccess) {
+          A.alloc(&m->head_partial, m->head_grid) || A.alloc(&m->d_err, 1);
+    if (bad || cudaMallocHost(&m->h_token, 2 * sizeof(int)) != cudaSuccess) {
         cudaGetLastError();
         A.release();
         delete m;
@@ -642,8 +668,9 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
         e = cudaMemsetAsync(m->L[l].k_pool, 0, kvpool, s);
         if (!e) e = cudaMemsetAsync(m->L[l].v_pool, 0, kvpool, s);
     }
+    m->h_err = m->h_token + 1;
     for (void* p : {(void*)m->attn_counters, (void*)m->router_counter, (void*)m->head_counter, (void*)m->d_pos,
-                    (void*)m->d_step, (void*)m->d_token})
+                    (void*)m->d_step, (void*)m->d_token, (void*)m->d_err})
         if (!e) e = cudaMemsetAsync(p, 0, p == (void*)m->attn_counters ? sizeof(unsigned) * d.kv_heads : sizeof(int), s);
     if (!e) e = cudaMemsetAsync(m->route_ids, 0, sizeof(int) * d.layers * d.k, s);
     if (!e) e = cudaMemsetAsync(m->route_w, 0, sizeof(float) * d.layers * d.k, s);
@@ -826,7 +853,8 @@ extern "C" int lastro_model_step(lastro_model* m, int32_t token, float* logits, 
         MTRY(cudaMemcpyAsync(route_ids, m->route_ids, sizeof(int) * d.layers * d.k, cudaMemcpyDeviceToHost, s), "routes");
     if (route_weights)
         MTRY(cudaMemcpyAsync(route_weights, m->route_w, sizeof(float) * d.layers * d.k, cudaMemcpyDeviceToHost, s), "routes");
-    MTRY(cudaStreamSynchronize(s), "step");
+    rc = finish(m, "step");
+    if (rc) return rc;
     m->pos_host += 1;
     return LASTRO_OK;
 }
@@ -858,7 +886,8 @@ extern "C" int lastro_model_generate(lastro_model* m, const int32_t* prompt, int
     if (out_ids && n_new > 0)
         MTRY(cudaMemcpyAsync(out_ids, m->d_out_ids + (n_prompt - 1), sizeof(int) * n_new, cudaMemcpyDeviceToHost, s),
              "ids download");
-    MTRY(cudaStreamSynchronize(s), "generate");
+    rc = finish(m, "generate");
+    if (rc) return rc;
     m->pos_host += steps;
     return LASTRO_OK;
 }
@@ -876,6 +905,8 @@ extern "C" int lastro_model_decode(lastro_model* m, int32_t n) {
         rc = run_step(m);
         if (rc) return rc;
     }
+    rc = finish(m, "decode");
+    if (rc) return rc;
     m->pos_host += n;
     return LASTRO_OK;
 }

@@ -104,4 +104,46 @@ LDEV bool last_block_arrives(unsigned int* counter, unsigned int total, bool* fl
     return last;
 }
 
+// ---- bulk (TMA) copies global -> shared, completed on an mbarrier ----------------------------------------------
+LDEV uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// thread 0 only, before any copy targets the barrier; the CTA synchronizes before other threads wait on it
+LDEV void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+LDEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+// `bytes` and both addresses must be multiples of 16
+LDEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
+LDEV bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: each try_wait suspends for a hardware-chosen interval; after the iteration limit the wait gives up,
+// records `code` in the error word (the host reports it and poisons the object) and returns false.
+constexpr uint32_t kWaitLimit = 1u << 22;
+LDEV bool mbar_wait(uint64_t* bar, uint32_t phase, int* err, int code) {
+    for (uint32_t i = 0; i < kWaitLimit; ++i)
+        if (mbar_try_wait(bar, phase)) return true;
+    if (err) atomicExch(err, code);
+    return false;
+}
+
 }  // namespace lastro

@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
     __shared__ __align__(16) uint4 vt[NW][32][CH];
     __shared__ float sm_m[NW][G], sm_l[NW][G];
     __shared__ float sacc[NW][G][D];
-    __shared__ float cw[MAXS][G];
+    __shared__ float cw[MAXS][G], cl[MAXS][G];
     __shared__ float cden[G];
     __shared__ bool is_last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -379,9 +379,14 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
     }
 
     if (!last_block_arrives(a.counters + kvh, (unsigned int)a.ns, &is_last)) return;
-    // merge: per-split weights exp(m_s - M) in shared memory, then every (g, dim) sums the splits
+    // merge: (m, l) of every split to shared memory in one coalesced pass, per-split weights exp(m_s - M), then every
+    // (g, dim) sums the splits
     const float* ml = a.part_ml + (size_t)kvh * a.ns * G * 2;
-    for (int i = threadIdx.x; i < a.ns * G; i += blockDim.x) cw[i / G][i % G] = __ldcg(ml + 2 * i);
+    for (int i = threadIdx.x; i < a.ns * G; i += blockDim.x) {
+        const float2 t = __ldcg(reinterpret_cast<const float2*>(ml) + i);
+        cw[i / G][i % G] = t.x;
+        cl[i / G][i % G] = t.y;
+    }
     __syncthreads();
     if (threadIdx.x < G) {
         const int g = threadIdx.x;
@@ -391,7 +396,7 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
         for (int sp = 0; sp < a.ns; ++sp) {
             const float ms = cw[sp][g];
             const float e = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-            den = fmaf(__ldcg(ml + 2 * (sp * G + g) + 1), e, den);
+            den = fmaf(cl[sp][g], e, den);
             cw[sp][g] = e;
         }
         cden[g] = den;
@@ -523,31 +528,57 @@ __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------------------------------
-// gate_up: warp per (expert slot, intermediate row j): g = W[e][j] . xn, u = W[e][I+j] . xn, a = silu(g) * u
-// (cpu.rs:154-158, gpu.rs:45-74); all k experts in one grid.
+// gate_up: CTA per (expert slot, block of kGuRows intermediate rows).  Thread 0 streams the block's gate rows and up
+// rows (two contiguous [kGuRows, H] slabs) into shared memory with bulk async copies while the CTA builds
+// xn = ln * (h * r); then warp w computes g = W[e][j0+w] . xn, u = W[e][I+j0+w] . xn, a = silu(g) * u
+// (cpu.rs:154-158, gpu.rs:45-74).  All k experts in one grid; every byte is requested at the start.
 // ------------------------------------------------------------------------------------------------------------------
+constexpr int kGuRows = 8;
+
 template <int NCH>
-__global__ void __launch_bounds__(128) gate_up_kernel(GateUpArgs a) {
-    constexpr int BLOCK = 128;
+LDEV float smem_row_dot(const uint16_t* row, const float* xs, int H, int lane) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < H) {
+            const uint4 w = *reinterpret_cast<const uint4*>(row + col);
+            const float4 xa = *reinterpret_cast<const float4*>(xs + col);
+            const float4 xb = *reinterpret_cast<const float4*>(xs + col + 4);
+            acc = dot8(w, xa, xb, acc);
+        }
+    }
+    return acc;
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
+    constexpr int BLOCK = 256, R = kGuRows;
     constexpr int NV = Vec<NCH, BLOCK>::NV;
-    extern __shared__ __align__(16) float smem[];
-    float* xs = smem;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    uint16_t* wg = reinterpret_cast<uint16_t*>(smem_raw);  // [R, H]
+    uint16_t* wu = wg + (size_t)R * a.H;                    // [R, H]
+    float* xs = reinterpret_cast<float*>(wu + (size_t)R * a.H);
+    __shared__ __align__(8) uint64_t bar;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int item = blockIdx.x * (BLOCK >> 5) + warp;
-    const bool active = item < a.k * a.I;
-    const int slot = item / a.I, j = item - (item / a.I) * a.I;
+    const int per_slot = a.I / R;
+    const int slot = blockIdx.x / per_slot, j0 = (blockIdx.x - slot * per_slot) * R;
+    if (threadIdx.x == 0) mbar_init(&bar, 1);
     float4 ln[NV];
     if (a.norm_mode) vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
 
     pdl_wait();
     pdl_launch();
 
-    uint4 wg[NCH], wu[NCH];
-    // expert ids come from the router; clamped so that a stale id can never address outside the weights
-    const int e = active ? min(max(__ldcg(a.ids + slot), 0), a.E - 1) : 0;
-    const uint16_t* base = a.w + (size_t)e * 2 * a.I * a.H;
-    load_row<NCH>(wg, base + (size_t)j * a.H, a.H, lane, active);
-    load_row<NCH>(wu, base + (size_t)(a.I + j) * a.H, a.H, lane, active);
+    if (threadIdx.x == 0) {
+        // expert ids come from the router; clamped so that a stale id can never address outside the weights
+        const int e = min(max(__ldcg(a.ids + slot), 0), a.E - 1);
+        const uint16_t* base = a.w + (size_t)e * 2 * a.I * a.H;
+        const uint32_t bytes = (uint32_t)(R * a.H * 2);
+        mbar_expect_tx(&bar, 2 * bytes);
+        bulk_g2s(wg, base + (size_t)j0 * a.H, bytes, &bar);
+        bulk_g2s(wu, base + (size_t)(a.I + j0) * a.H, bytes, &bar);
+    }
     if (a.norm_mode) {
         // xn = ln * (h * r) with the router's r
         float4 v[NV];
@@ -562,47 +593,52 @@ __global__ void __launch_bounds__(128) gate_up_kernel(GateUpArgs a) {
     } else {
         copy_to_smem<BLOCK>(a.x, a.H, xs);
     }
-    if (!active) return;
-    const float g = warp_sum(row_dot<NCH>(wg, xs, a.H, lane));
-    const float u = warp_sum(row_dot<NCH>(wu, xs, a.H, lane));
-    if (lane == 0) a.a[(size_t)slot * a.I + j] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+    if (!mbar_wait(&bar, 0, a.err, 1)) return;
+    const float g = warp_sum(smem_row_dot<NCH>(wg + (size_t)warp * a.H, xs, a.H, lane));
+    const float u = warp_sum(smem_row_dot<NCH>(wu + (size_t)warp * a.H, xs, a.H, lane));
+    if (lane == 0) a.a[(size_t)slot * a.I + j0 + warp] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
 }
 
 // ------------------------------------------------------------------------------------------------------------------
-// down: warp per output row r: y = sum_j w_j * (W_d[e_j][r] . a_j) in routing order (cpu.rs:231-238), then
-// h[r] += resid * y (model.rs:230-232) or out[r] = y (block forward).  Expert ids and weights come from the router
-// (two kernels back), so the down weights are loaded before griddepcontrol.wait.
+// down: CTA per block of kDnRows output rows.  Expert ids and weights come from the router, two kernels back, so
+// before griddepcontrol.wait thread 0 already streams the k contiguous [kDnRows, I] slabs W_d[e_j][r0 .. r0+R] into
+// shared memory; after it the CTA stages a [k, I]; warp w computes y = sum_j w_j * (W_d[e_j][r0+w] . a_j) in routing
+// order (cpu.rs:231-238), then h[r] += resid * y (model.rs:230-232) or out[r] = y (block forward).
 // ------------------------------------------------------------------------------------------------------------------
+constexpr int kDnRows = 8;
+
 template <int NCI>
 __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
-    constexpr int BLOCK = 256;
-    extern __shared__ __align__(16) float smem[];
-    float* as = smem;  // [k, I]
+    constexpr int BLOCK = 256, R = kDnRows;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    uint16_t* wd = reinterpret_cast<uint16_t*>(smem_raw);                    // [k, R, I]
+    float* as = reinterpret_cast<float*>(wd + (size_t)a.k * R * a.I);        // [k, I]
+    __shared__ __align__(8) uint64_t bar;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int row = blockIdx.x * (BLOCK >> 5) + warp;
-    const bool active = row < a.H;
-    uint4 w[kMaxTopK][NCI];
-    float gw[kMaxTopK];
-    int ex[kMaxTopK];
-#pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j) {
-        const bool on = active && j < a.k;
-        ex[j] = on ? min(max(__ldcg(a.ids + j), 0), a.E - 1) : 0;
-        gw[j] = on ? __ldcg(a.weights + j) : 0.0f;
+    const int r0 = blockIdx.x * R, row = r0 + warp;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        const uint32_t bytes = (uint32_t)(R * a.I * 2);
+        mbar_expect_tx(&bar, bytes * a.k);
+        for (int j = 0; j < a.k; ++j) {
+            const int e = min(max(__ldcg(a.ids + j), 0), a.E - 1);
+            bulk_g2s(wd + (size_t)j * R * a.I, a.w + ((size_t)e * a.H + r0) * a.I, bytes, &bar);
+        }
     }
+    float gw[kMaxTopK];
 #pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j)
-        load_row<NCI>(w[j], a.w + ((size_t)ex[j] * a.H + row) * a.I, a.I, lane, active && j < a.k);
+    for (int j = 0; j < kMaxTopK; ++j) gw[j] = j < a.k ? __ldcg(a.weights + j) : 0.0f;
     pdl_wait();
     pdl_launch();
-    const float hr = (active && lane == 0 && a.accumulate) ? __ldcg(a.out + row) : 0.0f;
+    const float hr = (lane == 0 && a.accumulate) ? __ldcg(a.out + row) : 0.0f;
     copy_to_smem<BLOCK>(a.a, a.k * a.I, as);
-    if (!active) return;
+    if (!mbar_wait(&bar, 0, a.err, 2)) return;
     float acc = 0.0f;
 #pragma unroll
     for (int j = 0; j < kMaxTopK; ++j) {
         if (j < a.k) {
-            const float d = warp_sum(row_dot<NCI>(w[j], as + (size_t)j * a.I, a.I, lane));
+            const float d =
+                warp_sum(smem_row_dot<NCI>(wd + ((size_t)j * R + warp) * a.I, as + (size_t)j * a.I, a.I, lane));
             acc = __fadd_rn(acc, __fmul_rn(gw[j], d));
         }
     }
@@ -806,18 +842,61 @@ cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, bool pdl) {
     LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(router_kernel<N>, grid, block, smem, s, pdl, a));
 }
 
+template <typename Kern>
+cudaError_t allow_smem(Kern k, size_t bytes) {
+    if (bytes <= 48 * 1024) return cudaSuccess;
+    return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+size_t gate_up_smem(int H) { return (size_t)2 * kGuRows * H * 2 + (size_t)H * 4; }
+size_t down_smem(int H, int I, int k) { (void)H; return (size_t)k * kDnRows * I * 2 + (size_t)k * I * 4; }
+
 cudaError_t launch_gate_up(const GateUpArgs& a, cudaStream_t s, bool pdl) {
-    const int items = a.k * a.I;
-    const dim3 grid((items + 3) / 4), block(128);
-    const size_t smem = sizeof(float) * (a.H + 32);
-    LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(gate_up_kernel<N>, grid, block, smem, s, pdl, a));
+    if (a.I % kGuRows) return cudaErrorInvalidValue;
+    const dim3 grid(a.k * (a.I / kGuRows)), block(256);
+    const size_t smem = gate_up_smem(a.H);
+    if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
+#define LASTRO_GU(N)                                                                  \
+    {                                                                                 \
+        cudaError_t e = allow_smem(gate_up_kernel<N>, smem);                          \
+        return e != cudaSuccess ? e : launch_ex(gate_up_kernel<N>, grid, block, smem, s, pdl, a); \
+    }
+    switch (chunks_for(a.H)) {
+    case 1: LASTRO_GU(1)
+    case 2: LASTRO_GU(2)
+    case 3: LASTRO_GU(3)
+    case 4: LASTRO_GU(4)
+    case 5: LASTRO_GU(5)
+    case 6: LASTRO_GU(6)
+    case 7: LASTRO_GU(7)
+    case 8: LASTRO_GU(8)
+    default: return cudaErrorInvalidValue;
+    }
+#undef LASTRO_GU
 }
 
 cudaError_t launch_down(const DownArgs& a, cudaStream_t s, bool pdl) {
-    const dim3 grid((a.H + 7) / 8), block(256);
-    const size_t smem = sizeof(float) * (size_t)a.k * a.I;
-    if (smem > 48 * 1024) return cudaErrorInvalidValue;
-    LASTRO_NCH_SWITCH(chunks_for(a.I), launch_ex(down_kernel<N>, grid, block, smem, s, pdl, a));
+    if (a.H % kDnRows) return cudaErrorInvalidValue;
+    const dim3 grid(a.H / kDnRows), block(256);
+    const size_t smem = down_smem(a.H, a.I, a.k);
+    if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
+#define LASTRO_DN(N)                                                                  \
+    {                                                                                 \
+        cudaError_t e = allow_smem(down_kernel<N>, smem);                             \
+        return e != cudaSuccess ? e : launch_ex(down_kernel<N>, grid, block, smem, s, pdl, a); \
+    }
+    switch (chunks_for(a.I)) {
+    case 1: LASTRO_DN(1)
+    case 2: LASTRO_DN(2)
+    case 3: LASTRO_DN(3)
+    case 4: LASTRO_DN(4)
+    case 5: LASTRO_DN(5)
+    case 6: LASTRO_DN(6)
+    case 7: LASTRO_DN(7)
+    case 8: LASTRO_DN(8)
+    default: return cudaErrorInvalidValue;
+    }
+#undef LASTRO_DN
 }
 
 int head_grid(int V) {

@@ -82,6 +82,7 @@ struct GateUpArgs {
     const int* ids;       // [k]
     const uint16_t* w;    // [E, 2I, H]
     float* a;             // [k, I]
+    int* err;             // error word: a bounded wait that gave up writes its code here
     int H, I, k, E;
 };
 
@@ -93,6 +94,7 @@ struct DownArgs {
     float* out;            // accumulate: h += resid*y ; else out = y
     float resid;
     int accumulate;
+    int* err;
     int H, I, k, E;
 };
 
@@ -137,5 +139,10 @@ constexpr int kMaxExperts = 64;
 constexpr int kMaxTopK = 8;
 constexpr int kHeadDim = 64;
 constexpr int kMaxGroup = 8;
+constexpr size_t kMaxSmemBytes = 220 * 1024;  // dynamic shared memory one CTA may use (B200: 227 KB)
+
+// shared memory the grouped expert kernels need (host-side checks)
+size_t gate_up_smem(int H);
+size_t down_smem(int H, int I, int k);
 
 }  // namespace lastro
