@@ -336,7 +336,7 @@ constexpr int kPageSize = 64;
 struct lastro_model {
     lastro_ctx* ctx = nullptr;
     lastro_model_desc d{};
-    int max_len = 0, qd = 0, kvd = 0, G = 1, max_pages = 0, ns = 1, head_grid = 1;
+    int max_len = 0, qd = 0, kvd = 0, G = 1, max_pages = 0, head_grid = 1;
     bool poisoned = false;
     bool use_graphs = true, use_pdl = true;
     Arena arena;
@@ -346,11 +346,11 @@ struct lastro_model {
     float* rope_cs = nullptr;
     int* page_table = nullptr;
     // per-step state
-    float *h = nullptr, *q = nullptr, *att = nullptr, *part_acc = nullptr, *part_ml = nullptr;
+    float *h = nullptr, *q = nullptr, *att = nullptr;
     float *rlogits = nullptr, *route_w = nullptr, *rnorm = nullptr, *a = nullptr, *logits = nullptr;
     int *route_ids = nullptr, *d_token = nullptr, *d_pos = nullptr, *d_step = nullptr, *d_out_ids = nullptr;
     int* d_prompt = nullptr;
-    unsigned int *attn_counters = nullptr, *router_counter = nullptr, *head_counter = nullptr;
+    unsigned int *router_counter = nullptr, *head_counter = nullptr;
     unsigned long long* head_partial = nullptr;
     int* d_err = nullptr;    // error word of the bounded waits
     int* h_token = nullptr;  // pinned
@@ -455,14 +455,13 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         aa.page_size = kPageSize;
         aa.kv_f32 = qa.kv_f32;
         aa.pos = m->d_pos;
-        aa.part_acc = m->part_acc;
-        aa.part_ml = m->part_ml;
-        aa.counters = m->attn_counters;
         aa.att_out = m->att;
+        aa.err = m->d_err;
         aa.kv_heads = d.kv_heads;
         aa.G = m->G;
         aa.d = d.head_dim;
-        aa.ns = m->ns;
+        aa.max_len = m->max_len;
+        aa.split_cap = attn_split_cap(m->max_len);
         aa.scale = d.attention_multiplier;
         if ((e = launch_attention(aa, s, pdl)) != cudaSuccess) return e;
         if ((e = mark(pe, s)) != cudaSuccess) return e;
@@ -622,6 +621,8 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
         return set_err(ctx, LASTRO_E_UNSUPPORTED, "kv dtype %d", d.kv_dtype);
     if (!(d.eps >= 0.0f) || !(d.logits_scaling != 0.0f) || !(d.rope_theta > 0.0f))
         return set_err(ctx, LASTRO_E_ARG, "bad eps / logits_scaling / rope_theta");
+    if (attn_smem(max_len, d.kv_dtype == LASTRO_DTYPE_F32) > kMaxSmemBytes)
+        return set_err(ctx, LASTRO_E_UNSUPPORTED, "max_len %d: the attention CTAs cannot stage their K/V share", max_len);
 
     cudaSetDevice(ctx->device);
     lastro_model* m = new lastro_model();
@@ -632,7 +633,6 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
     m->kvd = d.kv_heads * d.head_dim;
     m->G = G;
     m->max_pages = (max_len + kPageSize - 1) / kPageSize;
-    m->ns = std::min(64, std::max(1, (2 * 148 + d.kv_heads - 1) / d.kv_heads));
     m->head_grid = head_grid(d.vocab);
     m->loaded.assign((size_t)(d.layers + 1) * K_COUNT, 0);
     m->L.resize(d.layers);
@@ -647,14 +647,12 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
               A.alloc(&L.down, E * H * I) || A.alloc(&L.k_pool, kvpool) || A.alloc(&L.v_pool, kvpool);
     }
     bad = bad || A.alloc(&m->rope_cs, (size_t)max_len * d.head_dim) || A.alloc(&m->page_table, m->max_pages) ||
-          A.alloc(&m->h, H) || A.alloc(&m->q, m->qd) || A.alloc(&m->att, m->qd) ||
-          A.alloc(&m->part_acc, (size_t)d.kv_heads * m->ns * G * d.head_dim) ||
-          A.alloc(&m->part_ml, (size_t)d.kv_heads * m->ns * G * 2) || A.alloc(&m->rlogits, E) ||
+          A.alloc(&m->h, H) || A.alloc(&m->q, m->qd) || A.alloc(&m->att, m->qd) || A.alloc(&m->rlogits, E) ||
           A.alloc(&m->route_w, (size_t)d.layers * d.k) || A.alloc(&m->route_ids, (size_t)d.layers * d.k) ||
           A.alloc(&m->rnorm, 1) || A.alloc(&m->a, (size_t)d.k * I) || A.alloc(&m->logits, V) ||
           A.alloc(&m->d_token, 1) || A.alloc(&m->d_pos, 1) || A.alloc(&m->d_step, 1) ||
           A.alloc(&m->d_out_ids, (size_t)max_len + 1) || A.alloc(&m->d_prompt, (size_t)max_len + 1) ||
-          A.alloc(&m->attn_counters, d.kv_heads) || A.alloc(&m->router_counter, 1) || A.alloc(&m->head_counter, 1) ||
+          A.alloc(&m->router_counter, 1) || A.alloc(&m->head_counter, 1) ||
           A.alloc(&m->head_partial, m->head_grid) || A.alloc(&m->d_err, 1);
     if (bad || cudaMallocHost(&m->h_token, 2 * sizeof(int)) != cudaSuccess) {
         cudaGetLastError();
@@ -669,9 +667,9 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
         if (!e) e = cudaMemsetAsync(m->L[l].v_pool, 0, kvpool, s);
     }
     m->h_err = m->h_token + 1;
-    for (void* p : {(void*)m->attn_counters, (void*)m->router_counter, (void*)m->head_counter, (void*)m->d_pos,
-                    (void*)m->d_step, (void*)m->d_token, (void*)m->d_err})
-        if (!e) e = cudaMemsetAsync(p, 0, p == (void*)m->attn_counters ? sizeof(unsigned) * d.kv_heads : sizeof(int), s);
+    for (void* p : {(void*)m->router_counter, (void*)m->head_counter, (void*)m->d_pos, (void*)m->d_step,
+                    (void*)m->d_token, (void*)m->d_err})
+        if (!e) e = cudaMemsetAsync(p, 0, sizeof(int), s);
     if (!e) e = cudaMemsetAsync(m->route_ids, 0, sizeof(int) * d.layers * d.k, s);
     if (!e) e = cudaMemsetAsync(m->route_w, 0, sizeof(float) * d.layers * d.k, s);
     // model.rs:63-73: inv_freq = 1/theta^(2j/d) and cos/sin of pos*inv_freq, in f32 on the host

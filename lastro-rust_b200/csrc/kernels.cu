@@ -13,6 +13,8 @@
 //   RMSNorm  model.rs:141-145   RoPE rotate_half model.rs:147-158   attention model.rs:203-222
 //   routing  block.rs:79-89     SwiGLU cpu.rs:154-158               experts cpu.rs:205-240
 //   step     model.rs:181-243   argmax (last maximum) bin/m1b-gulosa.rs:22-24
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -224,37 +226,74 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------------------------------
-// attention: CTA (split s, kv head).  A warp takes 32 positions at a time, one per lane: the lane loads its K row and
-// its V row together (16 independent 16-byte loads for bf16), scores the row against the G query heads of the group
-// (GQA: the K/V rows are read once for all G heads), the warp updates its online softmax, stages the V rows in shared
-// memory and accumulates P.V with lane l owning dims 2l, 2l+1.  Warps merge in shared memory, then the last CTA of
-// the KV head merges the splits (flash-decoding).  Positions past `len` are never read.
+// attention: one thread-block cluster of kAttnCluster CTAs per KV head, CTA s of the cluster owns the positions
+// [len*s/CS, len*(s+1)/CS).  K/V rows before `pos` do not change during a decode step (only the new row `pos` is
+// written, by this layer's qkv kernel), so before griddepcontrol.wait thread 0 streams the CTA's K and V rows out of
+// the paged cache into shared memory with bulk async copies (one copy per page run); after it the CTA reads q and the
+// new row.  Each lane scores one position against the G query heads of the group (GQA: K/V read once for all G
+// heads); warps keep online-softmax partials, merge them in shared memory, and the cluster merges its CTAs' partials
+// through distributed shared memory (flash-decoding without a global round trip).  Positions past `len` are never
+// read.
 // ------------------------------------------------------------------------------------------------------------------
+constexpr int kAttnWarps = 8;
+
 template <bool KV_F32, int G>
-__global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(256) attention_kernel(AttnArgs a) {
+    namespace cg = cooperative_groups;
     constexpr int D = kHeadDim;
-    constexpr int NW = 4;
+    constexpr int NW = kAttnWarps;
     constexpr int ESZ = KV_F32 ? 4 : 2;
-    constexpr int CH = D * ESZ / 16;  // 16-byte chunks per row: 8 (bf16) or 16 (f32)
-    constexpr int MAXS = 64;          // splits handled by the merge
+    constexpr int RB = D * ESZ;  // bytes per K/V row of one head
+    constexpr int CH = RB / 16;  // 16-byte chunks per row
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    unsigned char* kt = smem_raw;                          // [cap, RB]
+    unsigned char* vt = smem_raw + (size_t)a.split_cap * RB;  // [cap, RB]
     __shared__ __align__(16) float sq[G][D];
-    __shared__ __align__(16) uint4 vt[NW][32][CH];
-    __shared__ float sm_m[NW][G], sm_l[NW][G];
-    __shared__ float sacc[NW][G][D];
-    __shared__ float cw[MAXS][G], cl[MAXS][G];
-    __shared__ float cden[G];
-    __shared__ bool is_last;
+    __shared__ float wm[NW][G], wl[NW][G];
+    __shared__ __align__(16) float wacc[NW][G][D];
+    __shared__ float cm[G], cl[G];
+    __shared__ __align__(16) float cacc[G][D];
+    __shared__ __align__(8) uint64_t bar;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int CS = (int)cluster.num_blocks(), s = (int)cluster.block_rank();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int s = blockIdx.x, kvh = blockIdx.y;
+    const int kvh = blockIdx.y;
+
+    // the position is written only by the previous step's head kernel: constant for the whole step
+    const int pos = __ldcg(a.pos);
+    const int len = pos + 1;
+    const int p0 = (int)(((long long)len * s) / CS), p1 = (int)(((long long)len * (s + 1)) / CS);
+    const int pb = min(p1, pos);  // rows [p0, pb) are final already
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_expect_tx(&bar, pb > p0 ? (uint32_t)(pb - p0) * RB * 2 : 0u);
+        for (int p = p0; p < pb;) {
+            const int pg = p / a.page_size, slot = p - pg * a.page_size;
+            const int n = min(pb - p, a.page_size - slot);
+            const int page = __ldcg(a.page_table + pg);
+            const size_t off = (((size_t)page * a.kv_heads + kvh) * a.page_size + slot) * RB;
+            bulk_g2s(kt + (size_t)(p - p0) * RB, static_cast<const unsigned char*>(a.k_pool) + off, (uint32_t)n * RB, &bar);
+            bulk_g2s(vt + (size_t)(p - p0) * RB, static_cast<const unsigned char*>(a.v_pool) + off, (uint32_t)n * RB, &bar);
+            p += n;
+        }
+    }
 
     pdl_wait();
     pdl_launch();
 
-    const int len = __ldcg(a.pos) + 1;
-    const int p0 = (int)(((long long)len * s) / a.ns), p1 = (int)(((long long)len * (s + 1)) / a.ns);
     for (int i = threadIdx.x; i < G * D / 4; i += blockDim.x)
         reinterpret_cast<float4*>(&sq[0][0])[i] = __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)kvh * G * D) + i);
+    if (pos >= p0 && pos < p1 && threadIdx.x < 2 * CH) {
+        // the row this layer's qkv kernel just appended
+        const int pg = pos / a.page_size, slot = pos - pg * a.page_size;
+        const size_t off = (((size_t)__ldcg(a.page_table + pg) * a.kv_heads + kvh) * a.page_size + slot) * RB;
+        const int c = threadIdx.x % CH;
+        const bool is_v = threadIdx.x >= CH;
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const unsigned char*>(is_v ? a.v_pool : a.k_pool) + off);
+        reinterpret_cast<uint4*>((is_v ? vt : kt) + (size_t)(pos - p0) * RB)[c] = __ldcg(src + c);
+    }
     __syncthreads();
+    const bool ok = mbar_wait(&bar, 0, a.err, 3);
 
     float m[G], l[G], acc0[G], acc1[G];
 #pragma unroll
@@ -264,45 +303,30 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
         acc0[g] = 0.0f;
         acc1[g] = 0.0f;
     }
-
-    for (int base = p0 + warp * 32; base < p1; base += NW * 32) {
-        const int p = base + lane;
-        const bool valid = p < p1;
-        const uint4* kr = nullptr;
-        const uint4* vr = nullptr;
-        if (valid) {
-            const int page = __ldcg(a.page_table + p / a.page_size), slot = p - (p / a.page_size) * a.page_size;
-            const size_t off = ((((size_t)page * a.kv_heads + kvh) * a.page_size + slot) * D) * ESZ / 16;
-            kr = static_cast<const uint4*>(a.k_pool) + off;
-            vr = static_cast<const uint4*>(a.v_pool) + off;
-        }
+    const int nrow = ok ? p1 - p0 : 0;
+    for (int base = warp * 32; base < nrow; base += NW * 32) {
+        const int r = base + lane;
+        const bool valid = r < nrow;
         float sc[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) sc[g] = 0.0f;
-        // K and V rows: all loads of a group issued before any is used
+        if (valid) {
+            const uint4* kr = reinterpret_cast<const uint4*>(kt + (size_t)r * RB);
 #pragma unroll
-        for (int c0 = 0; c0 < CH; c0 += 8) {
-            uint4 kc[8], vc[8];
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                kc[c] = valid ? __ldcg(kr + c0 + c) : make_uint4(0u, 0u, 0u, 0u);
-                vc[c] = valid ? __ldcg(vr + c0 + c) : make_uint4(0u, 0u, 0u, 0u);
-            }
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                vt[warp][lane][(c0 + c) ^ (lane & 7)] = vc[c];  // XOR swizzle: conflict-free stores
+            for (int c = 0; c < CH; ++c) {
+                const uint4 kc = kr[c];
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
                     if (KV_F32) {
-                        const float4 qv = *reinterpret_cast<const float4*>(&sq[g][(c0 + c) * 4]);
-                        sc[g] = fmaf(qv.x, __uint_as_float(kc[c].x), sc[g]);
-                        sc[g] = fmaf(qv.y, __uint_as_float(kc[c].y), sc[g]);
-                        sc[g] = fmaf(qv.z, __uint_as_float(kc[c].z), sc[g]);
-                        sc[g] = fmaf(qv.w, __uint_as_float(kc[c].w), sc[g]);
+                        const float4 qv = *reinterpret_cast<const float4*>(&sq[g][c * 4]);
+                        sc[g] = fmaf(qv.x, __uint_as_float(kc.x), sc[g]);
+                        sc[g] = fmaf(qv.y, __uint_as_float(kc.y), sc[g]);
+                        sc[g] = fmaf(qv.z, __uint_as_float(kc.z), sc[g]);
+                        sc[g] = fmaf(qv.w, __uint_as_float(kc.w), sc[g]);
                     } else {
-                        const float4 qa = *reinterpret_cast<const float4*>(&sq[g][(c0 + c) * 8]);
-                        const float4 qb = *reinterpret_cast<const float4*>(&sq[g][(c0 + c) * 8 + 4]);
-                        sc[g] = dot8(kc[c], qa, qb, sc[g]);
+                        const float4 qa = *reinterpret_cast<const float4*>(&sq[g][c * 8]);
+                        const float4 qb = *reinterpret_cast<const float4*>(&sq[g][c * 8 + 4]);
+                        sc[g] = dot8(kc, qa, qb, sc[g]);
                     }
                 }
             }
@@ -311,8 +335,7 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
 #pragma unroll
         for (int g = 0; g < G; ++g) {
             const float scv = valid ? __fmul_rn(sc[g], a.scale) : -INFINITY;
-            const float mt = warp_max(scv);
-            const float mn = fmaxf(m[g], mt);
+            const float mn = fmaxf(m[g], warp_max(scv));
             pr[g] = valid ? expf(scv - mn) : 0.0f;
             const float alpha = (m[g] == -INFINITY) ? 0.0f : expf(m[g] - mn);
             l[g] = l[g] * alpha + warp_sum(pr[g]);
@@ -320,18 +343,15 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
             acc1[g] *= alpha;
             m[g] = mn;
         }
-        __syncwarp();
-        const int nj = min(32, p1 - base);
+        const int nj = min(32, nrow - base);
         for (int jj = 0; jj < nj; ++jj) {
             float v0, v1;
             if (KV_F32) {
-                const float2 t =
-                    reinterpret_cast<const float2*>(&vt[warp][jj][0])[(((lane >> 1) ^ (jj & 7)) << 1) | (lane & 1)];
+                const float2 t = reinterpret_cast<const float2*>(vt + (size_t)(base + jj) * RB)[lane];
                 v0 = t.x;
                 v1 = t.y;
             } else {
-                const uint32_t t =
-                    reinterpret_cast<const uint32_t*>(&vt[warp][jj][0])[(((lane >> 2) ^ (jj & 7)) << 2) | (lane & 3)];
+                const uint32_t t = reinterpret_cast<const uint32_t*>(vt + (size_t)(base + jj) * RB)[lane];
                 v0 = bf_lo(t);
                 v1 = bf_hi(t);
             }
@@ -342,74 +362,56 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
                 acc1[g] = fmaf(pj, v1, acc1[g]);
             }
         }
-        __syncwarp();
     }
-
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         if (lane == 0) {
-            sm_m[warp][g] = m[g];
-            sm_l[warp][g] = l[g];
+            wm[warp][g] = m[g];
+            wl[warp][g] = l[g];
         }
-        sacc[warp][g][2 * lane] = acc0[g];
-        sacc[warp][g][2 * lane + 1] = acc1[g];
+        wacc[warp][g][2 * lane] = acc0[g];
+        wacc[warp][g][2 * lane + 1] = acc1[g];
     }
     __syncthreads();
+    // this CTA's partial: warps merged
     for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
         const int g = t / D, dim = t - (t / D) * D;
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_m[w][g]);
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
         float L = 0.0f, A = 0.0f;
         if (M != -INFINITY) {
 #pragma unroll
             for (int w = 0; w < NW; ++w) {
-                if (sm_m[w][g] == -INFINITY) continue;
-                const float e = expf(sm_m[w][g] - M);
-                L = fmaf(sm_l[w][g], e, L);
-                A = fmaf(sacc[w][g][dim], e, A);
+                if (wm[w][g] == -INFINITY) continue;
+                const float e = expf(wm[w][g] - M);
+                L = fmaf(wl[w][g], e, L);
+                A = fmaf(wacc[w][g][dim], e, A);
             }
         }
-        const size_t slot = ((size_t)kvh * a.ns + s) * G + g;
-        a.part_acc[slot * D + dim] = A;
+        cacc[g][dim] = A;
         if (dim == 0) {
-            a.part_ml[slot * 2] = M;
-            a.part_ml[slot * 2 + 1] = L;
+            cm[g] = M;
+            cl[g] = L;
         }
     }
-
-    if (!last_block_arrives(a.counters + kvh, (unsigned int)a.ns, &is_last)) return;
-    // merge: (m, l) of every split to shared memory in one coalesced pass, per-split weights exp(m_s - M), then every
-    // (g, dim) sums the splits
-    const float* ml = a.part_ml + (size_t)kvh * a.ns * G * 2;
-    for (int i = threadIdx.x; i < a.ns * G; i += blockDim.x) {
-        const float2 t = __ldcg(reinterpret_cast<const float2*>(ml) + i);
-        cw[i / G][i % G] = t.x;
-        cl[i / G][i % G] = t.y;
-    }
-    __syncthreads();
-    if (threadIdx.x < G) {
-        const int g = threadIdx.x;
+    cluster.sync();
+    // the cluster's merge, spread over its CTAs: output o handled by CTA o % CS, read from every peer's shared memory
+    for (int o = threadIdx.x * CS + s; o < G * D; o += blockDim.x * CS) {
+        const int g = o / D, dim = o - (o / D) * D;
         float M = -INFINITY;
-        for (int sp = 0; sp < a.ns; ++sp) M = fmaxf(M, cw[sp][g]);
-        float den = 0.0f;
-        for (int sp = 0; sp < a.ns; ++sp) {
-            const float ms = cw[sp][g];
-            const float e = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-            den = fmaf(cl[sp][g], e, den);
-            cw[sp][g] = e;
+        for (int r = 0; r < CS; ++r) M = fmaxf(M, *cluster.map_shared_rank(&cm[g], r));
+        float num = 0.0f, den = 0.0f;
+        for (int r = 0; r < CS; ++r) {
+            const float mr = *cluster.map_shared_rank(&cm[g], r);
+            if (mr == -INFINITY) continue;
+            const float e = expf(mr - M);
+            den = fmaf(*cluster.map_shared_rank(&cl[g], r), e, den);
+            num = fmaf(*cluster.map_shared_rank(&cacc[g][dim], r), e, num);
         }
-        cden[g] = den;
+        a.att_out[((size_t)kvh * G + g) * D + dim] = num / den;
     }
-    __syncthreads();
-    const float* pa = a.part_acc + (size_t)kvh * a.ns * G * D;
-    for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
-        const int g = t / D, dim = t - (t / D) * D;
-        float num = 0.0f;
-#pragma unroll 8
-        for (int sp = 0; sp < a.ns; ++sp) num = fmaf(__ldcg(pa + ((size_t)sp * G + g) * D + dim), cw[sp][g], num);
-        a.att_out[((size_t)kvh * G + g) * D + dim] = num / cden[g];
-    }
+    cluster.sync();  // peers' shared memory stays alive until every CTA has read it
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -788,6 +790,12 @@ int chunks_for(int n) { return (n + 255) / 256; }
 // ---------------------------------------------------------------------------------------------------------------------
 // launchers
 // ---------------------------------------------------------------------------------------------------------------------
+template <typename Kern>
+cudaError_t allow_smem(Kern k, size_t bytes) {
+    if (bytes <= 48 * 1024) return cudaSuccess;
+    return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
 #define LASTRO_NCH_SWITCH(nch, KERNEL_EXPR)                     \
     switch (nch) {                                              \
     case 1: { constexpr int N = 1; return KERNEL_EXPR; }        \
@@ -811,13 +819,39 @@ cudaError_t launch_qkv_rope(const QkvArgs& a, cudaStream_t s, bool pdl) {
     LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(qkv_rope_kernel<N, false>, grid, block, smem, s, pdl, a));
 }
 
+int attn_split_cap(int max_len) { return (max_len + kAttnCluster - 1) / kAttnCluster + 1; }
+
+size_t attn_smem(int max_len, int kv_f32) { return (size_t)2 * attn_split_cap(max_len) * kHeadDim * (kv_f32 ? 4 : 2); }
+
+template <typename Kern>
+cudaError_t launch_attn_cluster(Kern kernel, const AttnArgs& a, cudaStream_t s, bool pdl) {
+    const size_t smem = attn_smem(a.max_len, a.kv_f32);
+    cudaError_t e = allow_smem(kernel, smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kAttnCluster, a.kv_heads);
+    cfg.blockDim = dim3(32 * kAttnWarps);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kAttnCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kernel, a);
+}
+
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
-    if (a.ns < 1 || a.ns > 64 || a.d != kHeadDim) return cudaErrorInvalidValue;
-    const dim3 grid(a.ns, a.kv_heads), block(128);
-#define LASTRO_ATTN_G(GV)                                                                      \
-    case GV:                                                                                   \
-        return a.kv_f32 ? launch_ex(attention_kernel<true, GV>, grid, block, 0, s, pdl, a)     \
-                        : launch_ex(attention_kernel<false, GV>, grid, block, 0, s, pdl, a);
+    if (a.d != kHeadDim || a.split_cap != attn_split_cap(a.max_len)) return cudaErrorInvalidValue;
+    if (attn_smem(a.max_len, a.kv_f32) > kMaxSmemBytes) return cudaErrorInvalidValue;
+#define LASTRO_ATTN_G(GV)                                                                       \
+    case GV:                                                                                    \
+        return a.kv_f32 ? launch_attn_cluster(attention_kernel<true, GV>, a, s, pdl)            \
+                        : launch_attn_cluster(attention_kernel<false, GV>, a, s, pdl);
     switch (a.G) {
         LASTRO_ATTN_G(1)
         LASTRO_ATTN_G(2)
@@ -840,12 +874,6 @@ cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, bool pdl) {
     const dim3 grid((a.E + 3) / 4), block(128);
     const size_t smem = sizeof(float) * (a.H + 32);
     LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(router_kernel<N>, grid, block, smem, s, pdl, a));
-}
-
-template <typename Kern>
-cudaError_t allow_smem(Kern k, size_t bytes) {
-    if (bytes <= 48 * 1024) return cudaSuccess;
-    return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
 size_t gate_up_smem(int H) { return (size_t)2 * kGuRows * H * 2 + (size_t)H * 4; }

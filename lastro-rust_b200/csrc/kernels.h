@@ -44,11 +44,10 @@ struct AttnArgs {
     const int* page_table;
     int page_size, kv_f32;
     const int* pos;          // attends positions 0..pos
-    float* part_acc;         // [kv_heads, ns, G, d]
-    float* part_ml;          // [kv_heads, ns, G, 2]
-    unsigned int* counters;  // [kv_heads], zero between launches
     float* att_out;          // [heads*d]
-    int kv_heads, G, d, ns;
+    int* err;
+    int kv_heads, G, d;
+    int max_len, split_cap;  // split_cap = attn_split_cap(max_len): K/V rows one CTA stages
     float scale;
 };
 
@@ -140,6 +139,11 @@ constexpr int kMaxTopK = 8;
 constexpr int kHeadDim = 64;
 constexpr int kMaxGroup = 8;
 constexpr size_t kMaxSmemBytes = 220 * 1024;  // dynamic shared memory one CTA may use (B200: 227 KB)
+
+// attention: CTAs per KV head (one cluster) and the shared memory they stage K/V rows in
+constexpr int kAttnCluster = 8;
+int attn_split_cap(int max_len);
+size_t attn_smem(int max_len, int kv_f32);
 
 // shared memory the grouped expert kernels need (host-side checks)
 size_t gate_up_smem(int H);
