@@ -159,6 +159,9 @@ int check_block_shape(lastro_ctx* c, int E, int H, int I, int k) {
     if (H > kMaxHidden || I > kMaxInter || E > kMaxExperts || k > kMaxTopK)
         return set_err(c, LASTRO_E_UNSUPPORTED, "block shape beyond the kernels' limits (H<=%d I<=%d E<=%d k<=%d)",
                        kMaxHidden, kMaxInter, kMaxExperts, kMaxTopK);
+    if (I % gate_up_rows_per_cta() || H % down_rows_per_cta())
+        return set_err(c, LASTRO_E_UNSUPPORTED, "I=%d must be a multiple of %d and H=%d of %d", I, gate_up_rows_per_cta(),
+                       H, down_rows_per_cta());
     if (down_smem(H, I, k) > kMaxSmemBytes || gate_up_smem(H) > kMaxSmemBytes)
         return set_err(c, LASTRO_E_UNSUPPORTED, "k=%d, I=%d, H=%d: expert tiles exceed shared memory", k, I, H);
     return LASTRO_OK;

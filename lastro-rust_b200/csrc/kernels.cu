@@ -530,42 +530,78 @@ __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------------------------------
-// gate_up: CTA per (expert slot, block of kGuRows intermediate rows).  Thread 0 streams the block's gate rows and up
-// rows (two contiguous [kGuRows, H] slabs) into shared memory with bulk async copies while the CTA builds
-// xn = ln * (h * r); then warp w computes g = W[e][j0+w] . xn, u = W[e][I+j0+w] . xn, a = silu(g) * u
-// (cpu.rs:154-158, gpu.rs:45-74).  All k experts in one grid; every byte is requested at the start.
+// x held in registers: lane l owns columns (c*32 + l)*8 .. +8 of every row it multiplies, so a warp that computes
+// several rows reads x once (shared memory bandwidth is the limit otherwise: a bf16 weight read from shared memory
+// next to its f32 activation is 3x the weight bytes).
 // ------------------------------------------------------------------------------------------------------------------
-constexpr int kGuRows = 8;
-
 template <int NCH>
-LDEV float smem_row_dot(const uint16_t* row, const float* xs, int H, int lane) {
-    float acc = 0.0f;
+LDEV void x_to_regs(const float* xs, int H, int lane, float4 (&xa)[NCH], float4 (&xb)[NCH]) {
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
         const int col = (c * 32 + lane) * 8;
         if (col < H) {
-            const uint4 w = *reinterpret_cast<const uint4*>(row + col);
-            const float4 xa = *reinterpret_cast<const float4*>(xs + col);
-            const float4 xb = *reinterpret_cast<const float4*>(xs + col + 4);
-            acc = dot8(w, xa, xb, acc);
+            xa[c] = *reinterpret_cast<const float4*>(xs + col);
+            xb[c] = *reinterpret_cast<const float4*>(xs + col + 4);
+        } else {
+            xa[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+            xb[c] = xa[c];
         }
+    }
+}
+
+template <int NCH>
+LDEV void x_to_regs_global(const float* x, int H, int lane, float4 (&xa)[NCH], float4 (&xb)[NCH]) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < H) {
+            xa[c] = __ldcg(reinterpret_cast<const float4*>(x + col));
+            xb[c] = __ldcg(reinterpret_cast<const float4*>(x + col + 4));
+        } else {
+            xa[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+            xb[c] = xa[c];
+        }
+    }
+}
+
+// dot of a bf16 row in shared memory with x in registers
+template <int NCH>
+LDEV float smem_row_dot(const uint16_t* row, const float4 (&xa)[NCH], const float4 (&xb)[NCH], int H, int lane) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < H) acc = dot8(*reinterpret_cast<const uint4*>(row + col), xa[c], xb[c], acc);
     }
     return acc;
 }
 
+// ------------------------------------------------------------------------------------------------------------------
+// gate_up: CTA per (expert slot, block of kGuPairs intermediate rows).  Thread 0 streams the block's gate rows and up
+// rows into shared memory with bulk async copies, in two stages (the first half of the rows completes on its own
+// barrier, so warps start on it while the second half is in flight); meanwhile the CTA builds xn = ln * (h * r).
+// Warp w then computes rows j0+w and j0+w+8: g = W[e][j] . xn, u = W[e][I+j] . xn, a = silu(g) * u
+// (cpu.rs:154-158, gpu.rs:45-74).  All k experts in one grid; every byte is requested at the start.
+// ------------------------------------------------------------------------------------------------------------------
+constexpr int kGuPairs = 16;
+
 template <int NCH>
 __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
-    constexpr int BLOCK = 256, R = kGuRows;
+    constexpr int BLOCK = 256, R = kGuPairs, HALF = R / 2;
     constexpr int NV = Vec<NCH, BLOCK>::NV;
+    static_assert(HALF == BLOCK / 32, "one row pair per warp per stage");
     extern __shared__ __align__(128) unsigned char smem_raw[];
     uint16_t* wg = reinterpret_cast<uint16_t*>(smem_raw);  // [R, H]
     uint16_t* wu = wg + (size_t)R * a.H;                    // [R, H]
     float* xs = reinterpret_cast<float*>(wu + (size_t)R * a.H);
-    __shared__ __align__(8) uint64_t bar;
+    __shared__ __align__(8) uint64_t bar[2];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int per_slot = a.I / R;
     const int slot = blockIdx.x / per_slot, j0 = (blockIdx.x - slot * per_slot) * R;
-    if (threadIdx.x == 0) mbar_init(&bar, 1);
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+    }
     float4 ln[NV];
     if (a.norm_mode) vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
 
@@ -576,10 +612,13 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
         // expert ids come from the router; clamped so that a stale id can never address outside the weights
         const int e = min(max(__ldcg(a.ids + slot), 0), a.E - 1);
         const uint16_t* base = a.w + (size_t)e * 2 * a.I * a.H;
-        const uint32_t bytes = (uint32_t)(R * a.H * 2);
-        mbar_expect_tx(&bar, 2 * bytes);
-        bulk_g2s(wg, base + (size_t)j0 * a.H, bytes, &bar);
-        bulk_g2s(wu, base + (size_t)(a.I + j0) * a.H, bytes, &bar);
+        const uint32_t bytes = (uint32_t)(HALF * a.H * 2);
+#pragma unroll
+        for (int st = 0; st < 2; ++st) {
+            mbar_expect_tx(&bar[st], 2 * bytes);
+            bulk_g2s(wg + (size_t)st * HALF * a.H, base + (size_t)(j0 + st * HALF) * a.H, bytes, &bar[st]);
+            bulk_g2s(wu + (size_t)st * HALF * a.H, base + (size_t)(a.I + j0 + st * HALF) * a.H, bytes, &bar[st]);
+        }
     }
     if (a.norm_mode) {
         // xn = ln * (h * r) with the router's r
@@ -595,29 +634,36 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
     } else {
         copy_to_smem<BLOCK>(a.x, a.H, xs);
     }
-    if (!mbar_wait(&bar, 0, a.err, 1)) return;
-    const float g = warp_sum(smem_row_dot<NCH>(wg + (size_t)warp * a.H, xs, a.H, lane));
-    const float u = warp_sum(smem_row_dot<NCH>(wu + (size_t)warp * a.H, xs, a.H, lane));
-    if (lane == 0) a.a[(size_t)slot * a.I + j0 + warp] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+    float4 xa[NCH], xb[NCH];
+    x_to_regs<NCH>(xs, a.H, lane, xa, xb);
+#pragma unroll
+    for (int st = 0; st < 2; ++st) {
+        if (!mbar_wait(&bar[st], 0, a.err, 1)) return;
+        const int pr = st * HALF + warp;
+        const float g = warp_sum(smem_row_dot<NCH>(wg + (size_t)pr * a.H, xa, xb, a.H, lane));
+        const float u = warp_sum(smem_row_dot<NCH>(wu + (size_t)pr * a.H, xa, xb, a.H, lane));
+        if (lane == 0) a.a[(size_t)slot * a.I + j0 + pr] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+    }
 }
 
 // ------------------------------------------------------------------------------------------------------------------
-// down: CTA per block of kDnRows output rows.  Expert ids and weights come from the router, two kernels back, so
-// before griddepcontrol.wait thread 0 already streams the k contiguous [kDnRows, I] slabs W_d[e_j][r0 .. r0+R] into
-// shared memory; after it the CTA stages a [k, I]; warp w computes y = sum_j w_j * (W_d[e_j][r0+w] . a_j) in routing
-// order (cpu.rs:231-238), then h[r] += resid * y (model.rs:230-232) or out[r] = y (block forward).
+// down: CTA per block of kDnRows output rows; warp j takes expert slot j for all rows of the block, so a_j is read
+// once into registers.  Expert ids and weights come from the router, two kernels back, so before
+// griddepcontrol.wait thread 0 already streams the k contiguous [kDnRows, I] slabs W_d[e_j][r0 .. r0+R] into
+// shared memory.  Per row the k expert dots are then summed in routing order, y = sum_j w_j * d_j (cpu.rs:231-238),
+// and h[r] += resid * y (model.rs:230-232) or out[r] = y (block forward).
 // ------------------------------------------------------------------------------------------------------------------
 constexpr int kDnRows = 8;
 
 template <int NCI>
 __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
-    constexpr int BLOCK = 256, R = kDnRows;
+    constexpr int R = kDnRows;
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    uint16_t* wd = reinterpret_cast<uint16_t*>(smem_raw);                    // [k, R, I]
-    float* as = reinterpret_cast<float*>(wd + (size_t)a.k * R * a.I);        // [k, I]
+    uint16_t* wd = reinterpret_cast<uint16_t*>(smem_raw);                // [k, R, I]
+    float* part = reinterpret_cast<float*>(wd + (size_t)a.k * R * a.I);  // [k, R]
     __shared__ __align__(8) uint64_t bar;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int r0 = blockIdx.x * R, row = r0 + warp;
+    const int r0 = blockIdx.x * R;
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         const uint32_t bytes = (uint32_t)(R * a.I * 2);
@@ -632,19 +678,24 @@ __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
     for (int j = 0; j < kMaxTopK; ++j) gw[j] = j < a.k ? __ldcg(a.weights + j) : 0.0f;
     pdl_wait();
     pdl_launch();
-    const float hr = (lane == 0 && a.accumulate) ? __ldcg(a.out + row) : 0.0f;
-    copy_to_smem<BLOCK>(a.a, a.k * a.I, as);
-    if (!mbar_wait(&bar, 0, a.err, 2)) return;
-    float acc = 0.0f;
+    const float hr = (threadIdx.x < R && a.accumulate) ? __ldcg(a.out + r0 + threadIdx.x) : 0.0f;
+    float4 xa[NCI], xb[NCI];
+    if (warp < a.k) x_to_regs_global<NCI>(a.a + (size_t)warp * a.I, a.I, lane, xa, xb);
+    const bool ok = mbar_wait(&bar, 0, a.err, 2);
+    if (ok && warp < a.k) {
 #pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j) {
-        if (j < a.k) {
-            const float d =
-                warp_sum(smem_row_dot<NCI>(wd + ((size_t)j * R + warp) * a.I, as + (size_t)j * a.I, a.I, lane));
-            acc = __fadd_rn(acc, __fmul_rn(gw[j], d));
+        for (int r = 0; r < R; ++r) {
+            const float d = warp_sum(smem_row_dot<NCI>(wd + ((size_t)warp * R + r) * a.I, xa, xb, a.I, lane));
+            if (lane == 0) part[warp * R + r] = d;
         }
     }
-    if (lane == 0) a.out[row] = a.accumulate ? __fadd_rn(hr, __fmul_rn(a.resid, acc)) : acc;
+    __syncthreads();
+    if (!ok || threadIdx.x >= R) return;
+    float acc = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j)
+        if (j < a.k) acc = __fadd_rn(acc, __fmul_rn(gw[j], part[j * R + threadIdx.x]));
+    a.out[r0 + threadIdx.x] = a.accumulate ? __fadd_rn(hr, __fmul_rn(a.resid, acc)) : acc;
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -876,12 +927,14 @@ cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, bool pdl) {
     LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(router_kernel<N>, grid, block, smem, s, pdl, a));
 }
 
-size_t gate_up_smem(int H) { return (size_t)2 * kGuRows * H * 2 + (size_t)H * 4; }
-size_t down_smem(int H, int I, int k) { (void)H; return (size_t)k * kDnRows * I * 2 + (size_t)k * I * 4; }
+size_t gate_up_smem(int H) { return (size_t)2 * kGuPairs * H * 2 + (size_t)H * 4; }
+size_t down_smem(int H, int I, int k) { (void)H; return (size_t)k * kDnRows * I * 2 + (size_t)k * kDnRows * 4; }
+int gate_up_rows_per_cta() { return kGuPairs; }
+int down_rows_per_cta() { return kDnRows; }
 
 cudaError_t launch_gate_up(const GateUpArgs& a, cudaStream_t s, bool pdl) {
-    if (a.I % kGuRows) return cudaErrorInvalidValue;
-    const dim3 grid(a.k * (a.I / kGuRows)), block(256);
+    if (a.I % kGuPairs) return cudaErrorInvalidValue;
+    const dim3 grid(a.k * (a.I / kGuPairs)), block(256);
     const size_t smem = gate_up_smem(a.H);
     if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
 #define LASTRO_GU(N)                                                                  \

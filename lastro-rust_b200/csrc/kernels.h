@@ -148,5 +148,7 @@ size_t attn_smem(int max_len, int kv_f32);
 // shared memory the grouped expert kernels need (host-side checks)
 size_t gate_up_smem(int H);
 size_t down_smem(int H, int I, int k);
+int gate_up_rows_per_cta();  // I must be a multiple
+int down_rows_per_cta();     // H must be a multiple
 
 }  // namespace lastro
