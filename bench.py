@@ -63,8 +63,8 @@ def kernel_bytes(cfg, context):
     """Algorithmic HBM bytes of one launch of each kernel (bf16 weights, bf16 KV), at the given mean context."""
     H, I, E, k, V = cfg["hidden"], cfg["inter"], cfg["experts"], cfg["k"], cfg["vocab"]
     qd, kvd = cfg["heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
-    return dict(qkv_rope=(qd + 2 * kvd) * H * 2 + 2 * kvd * 2, attention=2 * kvd * 2 * context, oproj=H * qd * 2,
-                router=E * H * 2, gate_up=k * 2 * I * H * 2, down=k * H * I * 2, head=V * H * 2)
+    return dict(qkv_rope=(qd + 2 * kvd) * H * 2 + 2 * kvd * 2, attention=2 * kvd * 2 * context,
+                oproj=H * qd * 2 + H * E * 4, router=0, gate_up=k * 2 * I * H * 2, down=k * H * I * 2, head=V * H * 2)
 
 
 class ClockSampler:
@@ -270,8 +270,9 @@ def main():
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tp):
         traffic = json.load(open(tp)).get(dominant)
-    moe_bytes = kb["router"] + kb["gate_up"] + kb["down"]
-    moe_ms = (prof["router"] + prof["gate_up"] + prof["down"]) / L
+    # the router GEMV runs inside the oproj kernel; the MoE block's streamed bytes are the experts'
+    moe_bytes = kb["gate_up"] + kb["down"]
+    moe_ms = (prof["gate_up"] + prof["down"]) / L
     B = CFG.bytes_per_token(cfg, mean_ctx)
     step_s = ms / 1000.0 / K
     line = {
@@ -294,7 +295,7 @@ def main():
                       "us_per_layer": moe_ms * 1000.0},
         "kernels_ms_per_step": {k: round(v, 4) for k, v in prof.items()},
         "e2e": e2e,
-        "gpu_launches": K * (6 * L + 1),
+        "gpu_launches": K * (5 * L + 1),
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not a.no_cpu_baseline:

@@ -328,6 +328,8 @@ namespace {
 
 struct LayerDev {
     float *ln_attn = nullptr, *ln_moe = nullptr;
+    float* wr_t = nullptr;  // [H, E] router weight x ln_moe, transposed (fused router operand)
+    bool fold_dirty = true;
     uint16_t *wqkv = nullptr, *wo = nullptr, *router = nullptr, *gate_up = nullptr, *down = nullptr;
     void *k_pool = nullptr, *v_pool = nullptr;
 };
@@ -355,6 +357,7 @@ struct lastro_model {
     int* d_prompt = nullptr;
     unsigned int *router_counter = nullptr, *head_counter = nullptr;
     unsigned long long* head_partial = nullptr;
+    float* op_partial = nullptr;  // [oproj_grid(H), E + 1]
     int* d_err = nullptr;    // error word of the bounded waits
     int* h_token = nullptr;  // pinned
     int* h_err = nullptr;    // pinned copy of d_err
@@ -408,11 +411,13 @@ enum { KK_QKV = 0, KK_ATTN, KK_OPROJ, KK_ROUTER, KK_GATE_UP, KK_DOWN, KK_HEAD, K
 // Optional per-launch events: ev[0] before the first launch, ev[i + 1] after launch i.
 struct StepEvents {
     cudaEvent_t* ev = nullptr;
+    int* kind = nullptr;  // kind of launch i (between ev[i] and ev[i + 1])
     int next = 0;
 };
 
-cudaError_t mark(StepEvents* pe, cudaStream_t s) {
+cudaError_t mark(StepEvents* pe, cudaStream_t s, int kind = -1) {
     if (!pe) return cudaSuccess;
+    if (pe->next > 0) pe->kind[pe->next - 1] = kind;
     return cudaEventRecord(pe->ev[pe->next++], s);
 }
 
@@ -448,7 +453,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         qa.kv_heads = d.kv_heads;
         qa.eps = d.eps;
         if ((e = launch_qkv_rope(qa, s, pdl && l > 0)) != cudaSuccess) return e;
-        if ((e = mark(pe, s)) != cudaSuccess) return e;
+        if ((e = mark(pe, s, KK_QKV)) != cudaSuccess) return e;
 
         AttnArgs aa{};
         aa.q = m->q;
@@ -467,7 +472,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         aa.split_cap = attn_split_cap(m->max_len);
         aa.scale = d.attention_multiplier;
         if ((e = launch_attention(aa, s, pdl)) != cudaSuccess) return e;
-        if ((e = mark(pe, s)) != cudaSuccess) return e;
+        if ((e = mark(pe, s, KK_ATTN)) != cudaSuccess) return e;
 
         OprojArgs oa{};
         oa.att = m->att;
@@ -476,32 +481,26 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         oa.resid = d.residual_multiplier;
         oa.H = d.hidden;
         oa.qd = m->qd;
+        oa.route = 1;
+        oa.wr_t = L.wr_t;
+        oa.eps = d.eps;
+        oa.partial = m->op_partial;
+        oa.counter = m->router_counter;
+        oa.logits = m->rlogits;
+        oa.ids = m->route_ids + (size_t)l * d.k;
+        oa.weights = m->route_w + (size_t)l * d.k;
+        oa.rnorm_out = m->rnorm;
+        oa.E = d.experts;
+        oa.k = d.k;
         if ((e = launch_oproj(oa, s, pdl)) != cudaSuccess) return e;
-        if ((e = mark(pe, s)) != cudaSuccess) return e;
-
-        RouterArgs ra{};
-        ra.x = m->h;
-        ra.ln = L.ln_moe;
-        ra.eps = d.eps;
-        ra.norm_mode = 1;
-        ra.w = L.router;
-        ra.logits = m->rlogits;
-        ra.ids = m->route_ids + (size_t)l * d.k;
-        ra.weights = m->route_w + (size_t)l * d.k;
-        ra.rnorm_out = m->rnorm;
-        ra.counter = m->router_counter;
-        ra.E = d.experts;
-        ra.H = d.hidden;
-        ra.k = d.k;
-        if ((e = launch_router(ra, s, pdl)) != cudaSuccess) return e;
-        if ((e = mark(pe, s)) != cudaSuccess) return e;
+        if ((e = mark(pe, s, KK_OPROJ)) != cudaSuccess) return e;
 
         GateUpArgs ga{};
         ga.x = m->h;
         ga.ln = L.ln_moe;
         ga.rnorm = m->rnorm;
         ga.norm_mode = 1;
-        ga.ids = ra.ids;
+        ga.ids = oa.ids;
         ga.w = L.gate_up;
         ga.a = m->a;
         ga.err = m->d_err;
@@ -510,12 +509,12 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         ga.k = d.k;
         ga.E = d.experts;
         if ((e = launch_gate_up(ga, s, pdl)) != cudaSuccess) return e;
-        if ((e = mark(pe, s)) != cudaSuccess) return e;
+        if ((e = mark(pe, s, KK_GATE_UP)) != cudaSuccess) return e;
 
         DownArgs da{};
         da.a = m->a;
-        da.ids = ra.ids;
-        da.weights = ra.weights;
+        da.ids = oa.ids;
+        da.weights = oa.weights;
         da.w = L.down;
         da.out = m->h;
         da.resid = d.residual_multiplier;
@@ -526,7 +525,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         da.k = d.k;
         da.E = d.experts;
         if ((e = launch_down(da, s, pdl)) != cudaSuccess) return e;
-        if ((e = mark(pe, s)) != cudaSuccess) return e;
+        if ((e = mark(pe, s, KK_DOWN)) != cudaSuccess) return e;
     }
     HeadArgs ha{};
     ha.h = m->h;
@@ -545,7 +544,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
     ha.V = d.vocab;
     ha.H = d.hidden;
     if ((e = launch_head(ha, s, pdl, nullptr)) != cudaSuccess) return e;
-    return mark(pe, s);
+    return mark(pe, s, KK_HEAD);
 }
 
 // one step on the stream: graph replay (captured at first use) or direct launches
@@ -590,7 +589,17 @@ int finish(lastro_model* m, const char* what) {
 
 int check_ready(lastro_model* m) {
     if (m->poisoned) return set_err(m->ctx, LASTRO_E_POISONED, "model unusable after an earlier error");
-    return missing_tensor(m);
+    int rc = missing_tensor(m);
+    if (rc) return rc;
+    bool any = false;
+    for (LayerDev& L : m->L)
+        if (L.fold_dirty) {
+            MTRY(launch_router_fold(L.router, L.ln_moe, L.wr_t, m->d.experts, m->d.hidden, m->ctx->stream), "router fold");
+            L.fold_dirty = false;
+            any = true;
+        }
+    if (any) MTRY(cudaStreamSynchronize(m->ctx->stream), "router fold");
+    return LASTRO_OK;
 }
 
 // host copy of the paged layout's identity page table
@@ -647,7 +656,8 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
         LayerDev& L = m->L[l];
         bad = A.alloc(&L.ln_attn, H) || A.alloc(&L.ln_moe, H) || A.alloc(&L.wqkv, (size_t)(m->qd + 2 * m->kvd) * H) ||
               A.alloc(&L.wo, H * m->qd) || A.alloc(&L.router, E * H) || A.alloc(&L.gate_up, E * 2 * I * H) ||
-              A.alloc(&L.down, E * H * I) || A.alloc(&L.k_pool, kvpool) || A.alloc(&L.v_pool, kvpool);
+              A.alloc(&L.down, E * H * I) || A.alloc(&L.k_pool, kvpool) || A.alloc(&L.v_pool, kvpool) ||
+              A.alloc(&L.wr_t, E * H);
     }
     bad = bad || A.alloc(&m->rope_cs, (size_t)max_len * d.head_dim) || A.alloc(&m->page_table, m->max_pages) ||
           A.alloc(&m->h, H) || A.alloc(&m->q, m->qd) || A.alloc(&m->att, m->qd) || A.alloc(&m->rlogits, E) ||
@@ -656,7 +666,8 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
           A.alloc(&m->d_token, 1) || A.alloc(&m->d_pos, 1) || A.alloc(&m->d_step, 1) ||
           A.alloc(&m->d_out_ids, (size_t)max_len + 1) || A.alloc(&m->d_prompt, (size_t)max_len + 1) ||
           A.alloc(&m->router_counter, 1) || A.alloc(&m->head_counter, 1) ||
-          A.alloc(&m->head_partial, m->head_grid) || A.alloc(&m->d_err, 1);
+          A.alloc(&m->head_partial, m->head_grid) || A.alloc(&m->d_err, 1) ||
+          A.alloc(&m->op_partial, (size_t)oproj_grid(d.hidden) * (E + 1));
     if (bad || cudaMallocHost(&m->h_token, 2 * sizeof(int)) != cudaSuccess) {
         cudaGetLastError();
         A.release();
@@ -774,6 +785,7 @@ extern "C" int lastro_model_load_tensor(lastro_model* m, const char* name, int32
         MTRY(cudaStreamSynchronize(s), "tensor upload");
     }
     loaded_flag(m, layer, kind) = 1;
+    if (layer >= 0 && (kind == K_ROUTER || kind == K_LN_MOE)) m->L[layer].fold_dirty = true;
     return LASTRO_OK;
 }
 
@@ -802,6 +814,7 @@ extern "C" int lastro_model_fill_synthetic(lastro_model* m, uint64_t seed, float
     }
     MTRY(cudaStreamSynchronize(s), "synth");
     std::fill(m->loaded.begin(), m->loaded.end(), 1);
+    for (LayerDev& L : m->L) L.fold_dirty = true;
     return LASTRO_OK;
 }
 
@@ -939,16 +952,16 @@ extern "C" int lastro_model_profile(lastro_model* m, int32_t steps, float* kerne
     if (m->pos_host + steps > m->max_len) return set_err(ctx, LASTRO_E_FULL, "profile would overflow the KV cache");
     cudaSetDevice(ctx->device);
     cudaStream_t s = ctx->stream;
-    const int launches = KK_HEAD + (KK_DOWN + 1) * (m->d.layers - 1) + 1;  // 6 per layer + head
-    const int n_ev = 6 * m->d.layers + 2;
-    (void)launches;
+    const int n_ev = 8 * m->d.layers + 2;
     std::vector<cudaEvent_t> ev(n_ev, nullptr);
+    std::vector<int> kinds(n_ev, -1);
     for (auto& e : ev) MTRY(cudaEventCreate(&e), "event create");
     std::vector<double> acc(KK_COUNT, 0.0);
     int result = LASTRO_OK;
     for (int st = 0; st < steps && result == LASTRO_OK; ++st) {
         StepEvents pe;
         pe.ev = ev.data();
+        pe.kind = kinds.data();
         cudaError_t e = enqueue_step(m, s, &pe);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
         if (e != cudaSuccess) {
@@ -958,8 +971,7 @@ extern "C" int lastro_model_profile(lastro_model* m, int32_t steps, float* kerne
         for (int i = 0; i + 1 < pe.next; ++i) {
             float ms = 0.0f;
             cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
-            const int kind = (i == pe.next - 2) ? KK_HEAD : (i % 6);
-            acc[kind] += ms;
+            if (kinds[i] >= 0) acc[kinds[i]] += ms;
         }
         m->pos_host += 1;
     }

@@ -136,11 +136,70 @@ LDEV void load_row(uint4 (&w)[NCH], const uint16_t* row, int H, int lane, bool a
     }
 }
 
+// dot of a bf16 row held in registers (NCH 16-byte chunks per lane) with x held in registers
+template <int NCH>
+LDEV float row_dot_regs(const uint4 (&w)[NCH], const float4 (&xa)[NCH], const float4 (&xb)[NCH], int H, int lane) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < H) acc = dot8(w[c], xa[c], xb[c], acc);
+    }
+    return acc;
+}
+
 // float4 per thread for a vector of NCH*256 floats over BLOCK threads
 template <int NCH, int BLOCK>
 struct Vec {
     static constexpr int NV = (NCH * 64 + BLOCK - 1) / BLOCK;
 };
+
+// ------------------------------------------------------------------------------------------------------------------
+// x held in registers: lane l owns columns (c*32 + l)*8 .. +8 of every row it multiplies, so a warp that computes
+// several rows reads x once (shared memory bandwidth is the limit otherwise: a bf16 weight read from shared memory
+// next to its f32 activation is 3x the weight bytes).
+// ------------------------------------------------------------------------------------------------------------------
+template <int NCH>
+LDEV void x_to_regs(const float* xs, int H, int lane, float4 (&xa)[NCH], float4 (&xb)[NCH]) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < H) {
+            xa[c] = *reinterpret_cast<const float4*>(xs + col);
+            xb[c] = *reinterpret_cast<const float4*>(xs + col + 4);
+        } else {
+            xa[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+            xb[c] = xa[c];
+        }
+    }
+}
+
+template <int NCH>
+LDEV void x_to_regs_global(const float* x, int H, int lane, float4 (&xa)[NCH], float4 (&xb)[NCH]) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < H) {
+            xa[c] = __ldcg(reinterpret_cast<const float4*>(x + col));
+            xb[c] = __ldcg(reinterpret_cast<const float4*>(x + col + 4));
+        } else {
+            xa[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+            xb[c] = xa[c];
+        }
+    }
+}
+
+// dot of a bf16 row in shared memory with x in registers
+template <int NCH>
+LDEV float smem_row_dot(const uint16_t* row, const float4 (&xa)[NCH], const float4 (&xb)[NCH], int H, int lane) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < H) acc = dot8(*reinterpret_cast<const uint4*>(row + col), xa[c], xb[c], acc);
+    }
+    return acc;
+}
 
 // ------------------------------------------------------------------------------------------------------------------
 // qkv_rope: one warp per row pair (j, j + d/2) of a head, so RoPE's rotate_half partner is in the same warp.
@@ -235,10 +294,10 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
 // through distributed shared memory (flash-decoding without a global round trip).  Positions past `len` are never
 // read.
 // ------------------------------------------------------------------------------------------------------------------
-constexpr int kAttnWarps = 8;
+constexpr int kAttnWarps = 16;
 
 template <bool KV_F32, int G>
-__global__ void __launch_bounds__(256) attention_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(512) attention_kernel(AttnArgs a) {
     namespace cg = cooperative_groups;
     constexpr int D = kHeadDim;
     constexpr int NW = kAttnWarps;
@@ -267,14 +326,18 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a) {
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         mbar_expect_tx(&bar, pb > p0 ? (uint32_t)(pb - p0) * RB * 2 : 0u);
-        for (int p = p0; p < pb;) {
-            const int pg = p / a.page_size, slot = p - pg * a.page_size;
-            const int n = min(pb - p, a.page_size - slot);
+    }
+    __syncthreads();
+    if (pb > p0) {
+        // one thread per page run: page-table reads and copies all in flight together
+        const int pg0 = p0 / a.page_size, pg1 = (pb - 1) / a.page_size;
+        for (int t = threadIdx.x; t <= pg1 - pg0; t += blockDim.x) {
+            const int pg = pg0 + t;
+            const int lo = max(p0, pg * a.page_size), hi = min(pb, (pg + 1) * a.page_size);
             const int page = __ldcg(a.page_table + pg);
-            const size_t off = (((size_t)page * a.kv_heads + kvh) * a.page_size + slot) * RB;
-            bulk_g2s(kt + (size_t)(p - p0) * RB, static_cast<const unsigned char*>(a.k_pool) + off, (uint32_t)n * RB, &bar);
-            bulk_g2s(vt + (size_t)(p - p0) * RB, static_cast<const unsigned char*>(a.v_pool) + off, (uint32_t)n * RB, &bar);
-            p += n;
+            const size_t off = (((size_t)page * a.kv_heads + kvh) * a.page_size + (lo - pg * a.page_size)) * RB;
+            bulk_g2s(kt + (size_t)(lo - p0) * RB, static_cast<const unsigned char*>(a.k_pool) + off, (uint32_t)(hi - lo) * RB, &bar);
+            bulk_g2s(vt + (size_t)(lo - p0) * RB, static_cast<const unsigned char*>(a.v_pool) + off, (uint32_t)(hi - lo) * RB, &bar);
         }
     }
 
@@ -415,28 +478,6 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------------------------------
-// oproj: h[r] += resid * (W_o[r] . att), one warp per row (model.rs:223-227)
-// ------------------------------------------------------------------------------------------------------------------
-template <int NCH>
-__global__ void __launch_bounds__(128) oproj_kernel(OprojArgs a) {
-    constexpr int BLOCK = 128;
-    extern __shared__ __align__(16) float smem[];
-    float* xs = smem;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int row = blockIdx.x * (BLOCK >> 5) + warp;
-    const bool active = row < a.H;
-    uint4 w[NCH];
-    load_row<NCH>(w, a.w + (size_t)row * a.qd, a.qd, lane, active);
-    pdl_wait();
-    pdl_launch();
-    const float hr = (active && lane == 0) ? __ldcg(a.h + row) : 0.0f;
-    copy_to_smem<BLOCK>(a.att, a.qd, xs);
-    if (!active) return;
-    const float o = warp_sum(row_dot<NCH>(w, xs, a.qd, lane));
-    if (lane == 0) a.h[row] = __fadd_rn(hr, __fmul_rn(a.resid, o));
-}
-
-// ------------------------------------------------------------------------------------------------------------------
 // router: logits = W_r . xn (one warp per expert), then the last CTA takes the top-k with block.rs:81-89's order
 // (total_cmp descending, lower index first on ties) and the softmax over the k.
 // ------------------------------------------------------------------------------------------------------------------
@@ -450,6 +491,53 @@ LDEV unsigned long long shfl_xor_u64(unsigned long long v, int o) {
     lo = __shfl_xor_sync(0xffffffffu, lo, o);
     hi = __shfl_xor_sync(0xffffffffu, hi, o);
     return ((unsigned long long)hi << 32) | lo;
+}
+
+// Warp-wide top-k of E <= 64 logits (lane holds experts lane and lane + 32) in block.rs:81-89's order -- total_cmp
+// descending, lower index first on ties -- then the softmax over the k (exp(v - v0), divided by their sum in order).
+// Lane 0 writes ids[0..k) and weights[0..k).
+LDEV void route_topk_warp(float v0, float v1, int E, int k, int* ids_out, float* w_out) {
+    const int lane = threadIdx.x & 31;
+    unsigned long long k0 = lane < E ? route_key(v0, lane) : 0ull;
+    unsigned long long k1 = lane + 32 < E ? route_key(v1, lane + 32) : 0ull;
+    int ids[kMaxTopK];
+    float vals[kMaxTopK];
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) {
+        if (j >= k) break;
+        unsigned long long b = k0 > k1 ? k0 : k1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long t = shfl_xor_u64(b, o);
+            b = t > b ? t : b;
+        }
+        const int idx = (int)(~(uint32_t)b);
+        ids[j] = idx;
+        const int src = idx & 31;
+        vals[j] = __shfl_sync(0xffffffffu, idx < 32 ? v0 : v1, src);
+        if (lane == src) {
+            if (idx < 32)
+                k0 = 0ull;
+            else
+                k1 = 0ull;
+        }
+    }
+    if (lane == 0) {
+        float ex[kMaxTopK];
+        float sum = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j)
+            if (j < k) ex[j] = expf(__fsub_rn(vals[j], vals[0]));
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j)
+            if (j < k) sum = __fadd_rn(sum, ex[j]);
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j)
+            if (j < k) {
+                ids_out[j] = ids[j];
+                w_out[j] = __fdiv_rn(ex[j], sum);
+            }
+    }
 }
 
 template <int NCH>
@@ -483,97 +571,107 @@ __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
     }
     if (!last_block_arrives(a.counter, gridDim.x, &is_last)) return;
     if (warp != 0) return;
-    // E <= 64: lane holds experts lane and lane + 32
     const float v0 = lane < a.E ? __ldcg(a.logits + lane) : 0.0f;
     const float v1 = lane + 32 < a.E ? __ldcg(a.logits + lane + 32) : 0.0f;
-    unsigned long long k0 = lane < a.E ? route_key(v0, lane) : 0ull;
-    unsigned long long k1 = lane + 32 < a.E ? route_key(v1, lane + 32) : 0ull;
-    int ids[kMaxTopK];
-    float vals[kMaxTopK];
-#pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j) {
-        if (j >= a.k) break;
-        unsigned long long b = k0 > k1 ? k0 : k1;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const unsigned long long t = shfl_xor_u64(b, o);
-            b = t > b ? t : b;
-        }
-        const int idx = (int)(~(uint32_t)b);
-        ids[j] = idx;
-        const int src = idx & 31;
-        vals[j] = __shfl_sync(0xffffffffu, idx < 32 ? v0 : v1, src);
-        if (lane == src) {
-            if (idx < 32)
-                k0 = 0ull;
-            else
-                k1 = 0ull;
-        }
+    route_topk_warp(v0, v1, a.E, a.k, a.ids, a.weights);
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// oproj (+ router): warp w of CTA b computes rows r = 32b + 2w, 2w+1: h[r] += resid * (W_o[r] . att)
+// (model.rs:223-227).  With `route` set the MoE router is folded in: RMSNorm(h) . W_r^T equals
+// r_norm * sum_c (W_r[e,c] * ln[c]) * h[c], so each CTA adds its 32 rows' share of every logit (from W_r^T scaled by
+// ln, [H, E], prepared once per layer) and of sum h^2; the last CTA sums the shares in a fixed order, applies r_norm,
+// and takes the top-k with block.rs:81-89's order and softmax.  The experts kernel reads r_norm.
+// ------------------------------------------------------------------------------------------------------------------
+constexpr int kOpWarps = 16;
+constexpr int kOpRows = 2 * kOpWarps;
+
+template <int NCH>
+__global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
+    constexpr int BLOCK = 32 * kOpWarps;
+    extern __shared__ __align__(16) float smem[];
+    float* xs = smem;                  // [qd]
+    float* wrs = smem + a.qd;          // [kOpRows, E]
+    __shared__ float hs[kOpRows];
+    __shared__ float tot[BLOCK];
+    __shared__ bool is_last;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int r0 = blockIdx.x * kOpRows;
+    const int ra = r0 + 2 * warp, rb = ra + 1;
+    uint4 wa[NCH], wb[NCH];
+    load_row<NCH>(wa, a.w + (size_t)ra * a.qd, a.qd, lane, ra < a.H);
+    load_row<NCH>(wb, a.w + (size_t)rb * a.qd, a.qd, lane, rb < a.H);
+    if (a.route) {
+        const int n = kOpRows * a.E;
+        for (int t = threadIdx.x; t < n; t += BLOCK) wrs[t] = (r0 + t / a.E < a.H) ? __ldg(a.wr_t + (size_t)r0 * a.E + t) : 0.0f;
     }
+    pdl_wait();
+    pdl_launch();
+    const float ha = (lane == 0 && ra < a.H) ? __ldcg(a.h + ra) : 0.0f;
+    const float hb = (lane == 0 && rb < a.H) ? __ldcg(a.h + rb) : 0.0f;
+    copy_to_smem<BLOCK>(a.att, a.qd, xs);
+    float4 xa[NCH], xb[NCH];
+    x_to_regs<NCH>(xs, a.qd, lane, xa, xb);
+    const float oa = warp_sum(row_dot_regs<NCH>(wa, xa, xb, a.qd, lane));
+    const float ob = warp_sum(row_dot_regs<NCH>(wb, xa, xb, a.qd, lane));
     if (lane == 0) {
-        // block.rs:85-88: exp(v - v0) over the k in order, then divide by their sum
-        float ex[kMaxTopK];
-        float sum = 0.0f;
-#pragma unroll
-        for (int j = 0; j < kMaxTopK; ++j)
-            if (j < a.k) ex[j] = expf(__fsub_rn(vals[j], vals[0]));
-#pragma unroll
-        for (int j = 0; j < kMaxTopK; ++j)
-            if (j < a.k) sum = __fadd_rn(sum, ex[j]);
-#pragma unroll
-        for (int j = 0; j < kMaxTopK; ++j)
-            if (j < a.k) {
-                a.ids[j] = ids[j];
-                a.weights[j] = __fdiv_rn(ex[j], sum);
-            }
+        const float na = __fadd_rn(ha, __fmul_rn(a.resid, oa)), nb = __fadd_rn(hb, __fmul_rn(a.resid, ob));
+        if (ra < a.H) a.h[ra] = na;
+        if (rb < a.H) a.h[rb] = nb;
+        hs[2 * warp] = ra < a.H ? na : 0.0f;
+        hs[2 * warp + 1] = rb < a.H ? nb : 0.0f;
     }
-}
-
-// ------------------------------------------------------------------------------------------------------------------
-// x held in registers: lane l owns columns (c*32 + l)*8 .. +8 of every row it multiplies, so a warp that computes
-// several rows reads x once (shared memory bandwidth is the limit otherwise: a bf16 weight read from shared memory
-// next to its f32 activation is 3x the weight bytes).
-// ------------------------------------------------------------------------------------------------------------------
-template <int NCH>
-LDEV void x_to_regs(const float* xs, int H, int lane, float4 (&xa)[NCH], float4 (&xb)[NCH]) {
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-        const int col = (c * 32 + lane) * 8;
-        if (col < H) {
-            xa[c] = *reinterpret_cast<const float4*>(xs + col);
-            xb[c] = *reinterpret_cast<const float4*>(xs + col + 4);
-        } else {
-            xa[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-            xb[c] = xa[c];
-        }
+    if (!a.route) return;
+    __syncthreads();
+    const int E1 = a.E + 1;
+    if (threadIdx.x < a.E) {
+        float p = 0.0f;
+#pragma unroll 8
+        for (int i = 0; i < kOpRows; ++i) p = fmaf(wrs[i * a.E + threadIdx.x], hs[i], p);
+        a.partial[(size_t)blockIdx.x * E1 + threadIdx.x] = p;
+    } else if (threadIdx.x == a.E) {
+        float ss = 0.0f;
+#pragma unroll 8
+        for (int i = 0; i < kOpRows; ++i) ss = fmaf(hs[i], hs[i], ss);
+        a.partial[(size_t)blockIdx.x * E1 + a.E] = ss;
     }
-}
-
-template <int NCH>
-LDEV void x_to_regs_global(const float* x, int H, int lane, float4 (&xa)[NCH], float4 (&xb)[NCH]) {
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-        const int col = (c * 32 + lane) * 8;
-        if (col < H) {
-            xa[c] = __ldcg(reinterpret_cast<const float4*>(x + col));
-            xb[c] = __ldcg(reinterpret_cast<const float4*>(x + col + 4));
-        } else {
-            xa[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-            xb[c] = xa[c];
-        }
-    }
-}
-
-// dot of a bf16 row in shared memory with x in registers
-template <int NCH>
-LDEV float smem_row_dot(const uint16_t* row, const float4 (&xa)[NCH], const float4 (&xb)[NCH], int H, int lane) {
+    if (!last_block_arrives(a.counter, gridDim.x, &is_last)) return;
+    // shares of CTA c go to thread (c % groups) * E1 + e; groups are then summed in order
+    const int groups = BLOCK / E1, nb = gridDim.x;
     float acc = 0.0f;
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-        const int col = (c * 32 + lane) * 8;
-        if (col < H) acc = dot8(*reinterpret_cast<const uint4*>(row + col), xa[c], xb[c], acc);
+    if (threadIdx.x < groups * E1) {
+        const int e = threadIdx.x % E1, gi = threadIdx.x / E1;
+        for (int c = gi; c < nb; c += groups) acc = __fadd_rn(acc, __ldcg(a.partial + (size_t)c * E1 + e));
     }
-    return acc;
+    tot[threadIdx.x] = acc;
+    __syncthreads();
+    if (warp != 0) return;
+    float v[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const int e = lane + 32 * q;
+        float t = 0.0f;
+        if (e < E1)
+            for (int gi = 0; gi < groups; ++gi) t = __fadd_rn(t, tot[gi * E1 + e]);
+        v[q] = t;
+    }
+    // the sum of squares is entry E: lane E % 32 of half E / 32
+    const float ss = __shfl_sync(0xffffffffu, v[a.E >> 5], a.E & 31);
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.H), a.eps)));
+    const float l0 = lane < a.E ? __fmul_rn(v[0], r) : 0.0f;
+    const float l1 = lane + 32 < a.E ? __fmul_rn(v[1], r) : 0.0f;
+    if (lane < a.E) a.logits[lane] = l0;
+    if (lane + 32 < a.E) a.logits[lane + 32] = l1;
+    if (lane == 0) *a.rnorm_out = r;
+    route_topk_warp(l0, l1, a.E, a.k, a.ids, a.weights);
+}
+
+// W_r^T scaled by the MoE norm weight, [H, E] f32: the fused router's operand, prepared once per layer
+__global__ void router_fold_kernel(const uint16_t* wr, const float* ln, float* wr_t, int E, int H) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= E * H) return;
+    const int c = i / E, e = i - (i / E) * E;
+    wr_t[i] = __fmul_rn(__uint_as_float((uint32_t)wr[(size_t)e * H + c] << 16), ln[c]);
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -915,10 +1013,35 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
 #undef LASTRO_ATTN_G
 }
 
+int oproj_grid(int H) { return (H + kOpRows - 1) / kOpRows; }
+
 cudaError_t launch_oproj(const OprojArgs& a, cudaStream_t s, bool pdl) {
-    const dim3 grid((a.H + 3) / 4), block(128);
-    const size_t smem = sizeof(float) * a.qd;
-    LASTRO_NCH_SWITCH(chunks_for(a.qd), launch_ex(oproj_kernel<N>, grid, block, smem, s, pdl, a));
+    const dim3 grid(oproj_grid(a.H)), block(32 * kOpWarps);
+    if (a.route && (a.E > kMaxExperts || 32 * kOpWarps / (a.E + 1) < 1)) return cudaErrorInvalidValue;
+    const size_t smem = sizeof(float) * (a.qd + (a.route ? (size_t)kOpRows * a.E : 0));
+#define LASTRO_OP(N)                                                                  \
+    {                                                                                 \
+        cudaError_t e = allow_smem(oproj_kernel<N>, smem);                            \
+        return e != cudaSuccess ? e : launch_ex(oproj_kernel<N>, grid, block, smem, s, pdl, a); \
+    }
+    switch (chunks_for(a.qd)) {
+    case 1: LASTRO_OP(1)
+    case 2: LASTRO_OP(2)
+    case 3: LASTRO_OP(3)
+    case 4: LASTRO_OP(4)
+    case 5: LASTRO_OP(5)
+    case 6: LASTRO_OP(6)
+    case 7: LASTRO_OP(7)
+    case 8: LASTRO_OP(8)
+    default: return cudaErrorInvalidValue;
+    }
+#undef LASTRO_OP
+}
+
+cudaError_t launch_router_fold(const uint16_t* wr, const float* ln, float* wr_t, int E, int H, cudaStream_t s) {
+    const int n = E * H;
+    router_fold_kernel<<<(n + 255) / 256, 256, 0, s>>>(wr, ln, wr_t, E, H);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, bool pdl) {

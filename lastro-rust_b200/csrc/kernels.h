@@ -57,6 +57,17 @@ struct OprojArgs {
     float* h;           // [H], updated in place
     float resid;
     int H, qd;
+    // fused MoE router (route != 0)
+    int route;
+    const float* wr_t;      // [H, E]: router weight x MoE norm weight, transposed (launch_router_fold)
+    float eps;
+    float* partial;         // [oproj_grid(H), E + 1] per-CTA shares of the logits and of sum h^2
+    unsigned int* counter;  // zero between launches
+    float* logits;          // [E]
+    int* ids;               // [k]
+    float* weights;         // [k]
+    float* rnorm_out;       // 1/sqrt(mean(h^2) + eps)
+    int E, k;
 };
 
 struct RouterArgs {
@@ -119,6 +130,8 @@ cudaError_t launch_qkv_rope(const QkvArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_oproj(const OprojArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, bool pdl);
+int oproj_grid(int H);
+cudaError_t launch_router_fold(const uint16_t* wr, const float* ln, float* wr_t, int E, int H, cudaStream_t s);
 cudaError_t launch_gate_up(const GateUpArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_down(const DownArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_head(const HeadArgs& a, cudaStream_t s, bool pdl, int* grid_out);
