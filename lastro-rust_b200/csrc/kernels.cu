@@ -771,6 +771,7 @@ __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
             bulk_g2s(wd + (size_t)j * R * a.I, a.w + ((size_t)e * a.H + r0) * a.I, bytes, &bar);
         }
     }
+    __syncthreads();  // the barrier is initialized before any thread waits on it
     float gw[kMaxTopK];
 #pragma unroll
     for (int j = 0; j < kMaxTopK; ++j) gw[j] = j < a.k ? __ldcg(a.weights + j) : 0.0f;

@@ -186,3 +186,19 @@ def test_c3_3b_logits_match_oracle_at_full_size(gpu_ctx, pool):
     s.close()
     om.close()
     m.close()
+
+
+def test_profile_direct_launches_report_every_kernel(gpu_ctx):
+    """lastro_model_profile: direct launches with an event between kernels, after a synthetic context."""
+    cfg = CFG.TINY_768
+    w = reference_tiny_weights(cfg)
+    m = gpu_model(gpu_ctx, cfg, 400, "bf16")
+    m.fill_kv_synthetic(300)
+    prof = m.profile(3)
+    assert m.pos == 303
+    for k in ("qkv_rope", "attention", "oproj", "gate_up", "down", "head"):
+        assert prof[k] > 0.0, k
+    assert prof["router"] == 0.0  # folded into oproj
+    lg, _, _, _ = m.step(5)
+    assert np.isfinite(lg).all()
+    m.close()
