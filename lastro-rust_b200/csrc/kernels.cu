@@ -459,18 +459,27 @@ __global__ void __launch_bounds__(512) attention_kernel(AttnArgs a) {
         }
     }
     cluster.sync();
-    // the cluster's merge, spread over its CTAs: output o handled by CTA o % CS, read from every peer's shared memory
-    for (int o = threadIdx.x * CS + s; o < G * D; o += blockDim.x * CS) {
+    // the cluster's merge, spread over its CTAs: output o handled by CTA o % CS; every peer's (m, l, acc) is read
+    // from its shared memory in one batch of independent remote loads
+    for (int o = threadIdx.x * kAttnCluster + s; o < G * D; o += blockDim.x * kAttnCluster) {
         const int g = o / D, dim = o - (o / D) * D;
+        float pm[kAttnCluster], pl[kAttnCluster], pa[kAttnCluster];
+#pragma unroll
+        for (int r = 0; r < kAttnCluster; ++r) {
+            pm[r] = *cluster.map_shared_rank(&cm[g], r);
+            pl[r] = *cluster.map_shared_rank(&cl[g], r);
+            pa[r] = *cluster.map_shared_rank(&cacc[g][dim], r);
+        }
         float M = -INFINITY;
-        for (int r = 0; r < CS; ++r) M = fmaxf(M, *cluster.map_shared_rank(&cm[g], r));
+#pragma unroll
+        for (int r = 0; r < kAttnCluster; ++r) M = fmaxf(M, pm[r]);
         float num = 0.0f, den = 0.0f;
-        for (int r = 0; r < CS; ++r) {
-            const float mr = *cluster.map_shared_rank(&cm[g], r);
-            if (mr == -INFINITY) continue;
-            const float e = expf(mr - M);
-            den = fmaf(*cluster.map_shared_rank(&cl[g], r), e, den);
-            num = fmaf(*cluster.map_shared_rank(&cacc[g][dim], r), e, num);
+#pragma unroll
+        for (int r = 0; r < kAttnCluster; ++r) {
+            if (pm[r] == -INFINITY) continue;
+            const float e = expf(pm[r] - M);
+            den = fmaf(pl[r], e, den);
+            num = fmaf(pa[r], e, num);
         }
         a.att_out[((size_t)kvh * G + g) * D + dim] = num / den;
     }
@@ -636,12 +645,24 @@ __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
         a.partial[(size_t)blockIdx.x * E1 + a.E] = ss;
     }
     if (!last_block_arrives(a.counter, gridDim.x, &is_last)) return;
-    // shares of CTA c go to thread (c % groups) * E1 + e; groups are then summed in order
+    // shares of CTA c go to thread (c % groups) * E1 + e; each thread loads all of its shares in one batch, then
+    // the groups are summed in order
+    constexpr int kMaxShares = 8;
     const int groups = BLOCK / E1, nb = gridDim.x;
     float acc = 0.0f;
     if (threadIdx.x < groups * E1) {
         const int e = threadIdx.x % E1, gi = threadIdx.x / E1;
-        for (int c = gi; c < nb; c += groups) acc = __fadd_rn(acc, __ldcg(a.partial + (size_t)c * E1 + e));
+        for (int c0 = gi; c0 < nb; c0 += groups * kMaxShares) {
+            float sh[kMaxShares];
+#pragma unroll
+            for (int q = 0; q < kMaxShares; ++q) {
+                const int c = c0 + q * groups;
+                sh[q] = c < nb ? __ldcg(a.partial + (size_t)c * E1 + e) : 0.0f;
+            }
+#pragma unroll
+            for (int q = 0; q < kMaxShares; ++q)
+                if (c0 + q * groups < nb) acc = __fadd_rn(acc, sh[q]);
+        }
     }
     tot[threadIdx.x] = acc;
     __syncthreads();

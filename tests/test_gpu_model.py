@@ -192,7 +192,7 @@ def test_profile_direct_launches_report_every_kernel(gpu_ctx):
     """lastro_model_profile: direct launches with an event between kernels, after a synthetic context."""
     cfg = CFG.TINY_768
     w = reference_tiny_weights(cfg)
-    m = gpu_model(gpu_ctx, cfg, 400, "bf16")
+    m = gpu_model(gpu_ctx, cfg, w, 400, "bf16")
     m.fill_kv_synthetic(300)
     prof = m.profile(3)
     assert m.pos == 303
