@@ -352,6 +352,7 @@ struct lastro_model {
     int* page_table = nullptr;
     // per-step state
     float *h = nullptr, *q = nullptr, *att = nullptr;
+    float *part_acc = nullptr, *part_ml = nullptr;  // attention splits [heads, kAttnSplits, d] / [.., 2]
     float *rlogits = nullptr, *route_w = nullptr, *rnorm = nullptr, *a = nullptr, *logits = nullptr;
     int *route_ids = nullptr, *d_token = nullptr, *d_pos = nullptr, *d_step = nullptr, *d_out_ids = nullptr;
     int* d_prompt = nullptr;
@@ -463,7 +464,8 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         aa.page_size = kPageSize;
         aa.kv_f32 = qa.kv_f32;
         aa.pos = m->d_pos;
-        aa.att_out = m->att;
+        aa.part_acc = m->part_acc;
+        aa.part_ml = m->part_ml;
         aa.err = m->d_err;
         aa.kv_heads = d.kv_heads;
         aa.G = m->G;
@@ -476,6 +478,9 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
 
         OprojArgs oa{};
         oa.att = m->att;
+        oa.part_acc = m->part_acc;
+        oa.part_ml = m->part_ml;
+        oa.heads = d.heads;
         oa.w = L.wo;
         oa.h = m->h;
         oa.resid = d.residual_multiplier;
@@ -661,6 +666,8 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
     }
     bad = bad || A.alloc(&m->rope_cs, (size_t)max_len * d.head_dim) || A.alloc(&m->page_table, m->max_pages) ||
           A.alloc(&m->h, H) || A.alloc(&m->q, m->qd) || A.alloc(&m->att, m->qd) || A.alloc(&m->rlogits, E) ||
+          A.alloc(&m->part_acc, (size_t)d.heads * kAttnSplits * d.head_dim) ||
+          A.alloc(&m->part_ml, (size_t)d.heads * kAttnSplits * 2) ||
           A.alloc(&m->route_w, (size_t)d.layers * d.k) || A.alloc(&m->route_ids, (size_t)d.layers * d.k) ||
           A.alloc(&m->rnorm, 1) || A.alloc(&m->a, (size_t)d.k * I) || A.alloc(&m->logits, V) ||
           A.alloc(&m->d_token, 1) || A.alloc(&m->d_pos, 1) || A.alloc(&m->d_step, 1) ||

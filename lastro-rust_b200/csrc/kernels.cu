@@ -13,8 +13,6 @@
 //   RMSNorm  model.rs:141-145   RoPE rotate_half model.rs:147-158   attention model.rs:203-222
 //   routing  block.rs:79-89     SwiGLU cpu.rs:154-158               experts cpu.rs:205-240
 //   step     model.rs:181-243   argmax (last maximum) bin/m1b-gulosa.rs:22-24
-#include <cooperative_groups.h>
-
 #include "common.cuh"
 #include "kernels.h"
 
@@ -285,43 +283,37 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------------------------------
-// attention: one thread-block cluster of kAttnCluster CTAs per KV head, CTA s of the cluster owns the positions
-// [len*s/CS, len*(s+1)/CS).  K/V rows before `pos` do not change during a decode step (only the new row `pos` is
-// written, by this layer's qkv kernel), so before griddepcontrol.wait thread 0 streams the CTA's K and V rows out of
-// the paged cache into shared memory with bulk async copies (one copy per page run); after it the CTA reads q and the
-// new row.  Each lane scores one position against the G query heads of the group (GQA: K/V read once for all G
-// heads); warps keep online-softmax partials, merge them in shared memory, and the cluster merges its CTAs' partials
-// through distributed shared memory (flash-decoding without a global round trip).  Positions past `len` are never
-// read.
+// attention: CTA (split s, KV head).  Split s owns the positions [len*s/NS, len*(s+1)/NS).  K/V rows before `pos` do
+// not change during a decode step (only the new row `pos` is written, by this layer's qkv kernel), so before
+// griddepcontrol.wait the CTA streams its K and V rows out of the paged cache into shared memory with bulk async
+// copies (one thread per page run); after it the CTA reads q and the new row.  Each lane scores one position against
+// the G query heads of the group (GQA: K/V read once for all G heads), warps keep online-softmax partials and merge
+// them in shared memory, and the CTA writes its partial (m, l, acc) per query head; the output-projection kernel
+// merges the splits as it loads the attention output (flash-decoding).  Positions past `len` are never read.
 // ------------------------------------------------------------------------------------------------------------------
-constexpr int kAttnWarps = 16;
+constexpr int kAttnWarps = 8;
 
 template <bool KV_F32, int G>
-__global__ void __launch_bounds__(512) attention_kernel(AttnArgs a) {
-    namespace cg = cooperative_groups;
+__global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) {
     constexpr int D = kHeadDim;
     constexpr int NW = kAttnWarps;
     constexpr int ESZ = KV_F32 ? 4 : 2;
     constexpr int RB = D * ESZ;  // bytes per K/V row of one head
     constexpr int CH = RB / 16;  // 16-byte chunks per row
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    unsigned char* kt = smem_raw;                          // [cap, RB]
+    unsigned char* kt = smem_raw;                             // [cap, RB]
     unsigned char* vt = smem_raw + (size_t)a.split_cap * RB;  // [cap, RB]
     __shared__ __align__(16) float sq[G][D];
     __shared__ float wm[NW][G], wl[NW][G];
     __shared__ __align__(16) float wacc[NW][G][D];
-    __shared__ float cm[G], cl[G];
-    __shared__ __align__(16) float cacc[G][D];
     __shared__ __align__(8) uint64_t bar;
-    cg::cluster_group cluster = cg::this_cluster();
-    const int CS = (int)cluster.num_blocks(), s = (int)cluster.block_rank();
+    const int NS = gridDim.x, s = blockIdx.x, kvh = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int kvh = blockIdx.y;
 
     // the position is written only by the previous step's head kernel: constant for the whole step
     const int pos = __ldcg(a.pos);
     const int len = pos + 1;
-    const int p0 = (int)(((long long)len * s) / CS), p1 = (int)(((long long)len * (s + 1)) / CS);
+    const int p0 = (int)(((long long)len * s) / NS), p1 = (int)(((long long)len * (s + 1)) / NS);
     const int pb = min(p1, pos);  // rows [p0, pb) are final already
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
@@ -378,19 +370,29 @@ __global__ void __launch_bounds__(512) attention_kernel(AttnArgs a) {
 #pragma unroll
             for (int c = 0; c < CH; ++c) {
                 const uint4 kc = kr[c];
+                // the row's elements are unpacked once and used for all G heads
+                float kf[8];
+                if (KV_F32) {
+                    kf[0] = __uint_as_float(kc.x);
+                    kf[1] = __uint_as_float(kc.y);
+                    kf[2] = __uint_as_float(kc.z);
+                    kf[3] = __uint_as_float(kc.w);
+                } else {
+                    kf[0] = bf_lo(kc.x);
+                    kf[1] = bf_hi(kc.x);
+                    kf[2] = bf_lo(kc.y);
+                    kf[3] = bf_hi(kc.y);
+                    kf[4] = bf_lo(kc.z);
+                    kf[5] = bf_hi(kc.z);
+                    kf[6] = bf_lo(kc.w);
+                    kf[7] = bf_hi(kc.w);
+                }
+                constexpr int EPC = KV_F32 ? 4 : 8;
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    if (KV_F32) {
-                        const float4 qv = *reinterpret_cast<const float4*>(&sq[g][c * 4]);
-                        sc[g] = fmaf(qv.x, __uint_as_float(kc.x), sc[g]);
-                        sc[g] = fmaf(qv.y, __uint_as_float(kc.y), sc[g]);
-                        sc[g] = fmaf(qv.z, __uint_as_float(kc.z), sc[g]);
-                        sc[g] = fmaf(qv.w, __uint_as_float(kc.w), sc[g]);
-                    } else {
-                        const float4 qa = *reinterpret_cast<const float4*>(&sq[g][c * 8]);
-                        const float4 qb = *reinterpret_cast<const float4*>(&sq[g][c * 8 + 4]);
-                        sc[g] = dot8(kc, qa, qb, sc[g]);
-                    }
+                    const float* qg = &sq[g][c * EPC];
+#pragma unroll
+                    for (int e = 0; e < EPC; ++e) sc[g] = fmaf(qg[e], kf[e], sc[g]);
                 }
             }
         }
@@ -436,7 +438,7 @@ __global__ void __launch_bounds__(512) attention_kernel(AttnArgs a) {
         wacc[warp][g][2 * lane + 1] = acc1[g];
     }
     __syncthreads();
-    // this CTA's partial: warps merged
+    // this CTA's partial: warps merged; layout [head][split][...] so the consumer reads each head's splits together
     for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
         const int g = t / D, dim = t - (t / D) * D;
         float M = -INFINITY;
@@ -452,38 +454,13 @@ __global__ void __launch_bounds__(512) attention_kernel(AttnArgs a) {
                 A = fmaf(wacc[w][g][dim], e, A);
             }
         }
-        cacc[g][dim] = A;
+        const size_t hs = (size_t)(kvh * G + g) * NS + s;
+        a.part_acc[hs * D + dim] = A;
         if (dim == 0) {
-            cm[g] = M;
-            cl[g] = L;
+            a.part_ml[hs * 2] = M;
+            a.part_ml[hs * 2 + 1] = L;
         }
     }
-    cluster.sync();
-    // the cluster's merge, spread over its CTAs: output o handled by CTA o % CS; every peer's (m, l, acc) is read
-    // from its shared memory in one batch of independent remote loads
-    for (int o = threadIdx.x * kAttnCluster + s; o < G * D; o += blockDim.x * kAttnCluster) {
-        const int g = o / D, dim = o - (o / D) * D;
-        float pm[kAttnCluster], pl[kAttnCluster], pa[kAttnCluster];
-#pragma unroll
-        for (int r = 0; r < kAttnCluster; ++r) {
-            pm[r] = *cluster.map_shared_rank(&cm[g], r);
-            pl[r] = *cluster.map_shared_rank(&cl[g], r);
-            pa[r] = *cluster.map_shared_rank(&cacc[g][dim], r);
-        }
-        float M = -INFINITY;
-#pragma unroll
-        for (int r = 0; r < kAttnCluster; ++r) M = fmaxf(M, pm[r]);
-        float num = 0.0f, den = 0.0f;
-#pragma unroll
-        for (int r = 0; r < kAttnCluster; ++r) {
-            if (pm[r] == -INFINITY) continue;
-            const float e = expf(pm[r] - M);
-            den = fmaf(pl[r], e, den);
-            num = fmaf(pa[r], e, num);
-        }
-        a.att_out[((size_t)kvh * G + g) * D + dim] = num / den;
-    }
-    cluster.sync();  // peers' shared memory stays alive until every CTA has read it
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -495,6 +472,13 @@ LDEV unsigned long long route_key(float v, int idx) {
     return ((unsigned long long)((uint32_t)total_key(v) ^ 0x80000000u) << 32) | (uint32_t)(~(uint32_t)idx);
 }
 
+LDEV unsigned long long shfl_u64(unsigned long long v, int src) {
+    uint32_t lo = (uint32_t)v, hi = (uint32_t)(v >> 32);
+    lo = __shfl_sync(0xffffffffu, lo, src);
+    hi = __shfl_sync(0xffffffffu, hi, src);
+    return ((unsigned long long)hi << 32) | lo;
+}
+
 LDEV unsigned long long shfl_xor_u64(unsigned long long v, int o) {
     uint32_t lo = (uint32_t)v, hi = (uint32_t)(v >> 32);
     lo = __shfl_xor_sync(0xffffffffu, lo, o);
@@ -503,49 +487,35 @@ LDEV unsigned long long shfl_xor_u64(unsigned long long v, int o) {
 }
 
 // Warp-wide top-k of E <= 64 logits (lane holds experts lane and lane + 32) in block.rs:81-89's order -- total_cmp
-// descending, lower index first on ties -- then the softmax over the k (exp(v - v0), divided by their sum in order).
-// Lane 0 writes ids[0..k) and weights[0..k).
-LDEV void route_topk_warp(float v0, float v1, int E, int k, int* ids_out, float* w_out) {
+// descending, lower index first on ties -- then the softmax over the k (exp(v - v0), summed in order, divided).
+// Every expert's rank is counted against all E keys at once (independent shuffles, no select-max chain); the k
+// winners are placed by rank through shared scratch (sid/sval, kMaxTopK entries).  Writes ids[0..k), weights[0..k).
+LDEV void route_topk_warp(float v0, float v1, int E, int k, int* ids_out, float* w_out, int* sid, float* sval) {
     const int lane = threadIdx.x & 31;
-    unsigned long long k0 = lane < E ? route_key(v0, lane) : 0ull;
-    unsigned long long k1 = lane + 32 < E ? route_key(v1, lane + 32) : 0ull;
-    int ids[kMaxTopK];
-    float vals[kMaxTopK];
-#pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j) {
-        if (j >= k) break;
-        unsigned long long b = k0 > k1 ? k0 : k1;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const unsigned long long t = shfl_xor_u64(b, o);
-            b = t > b ? t : b;
-        }
-        const int idx = (int)(~(uint32_t)b);
-        ids[j] = idx;
-        const int src = idx & 31;
-        vals[j] = __shfl_sync(0xffffffffu, idx < 32 ? v0 : v1, src);
-        if (lane == src) {
-            if (idx < 32)
-                k0 = 0ull;
-            else
-                k1 = 0ull;
-        }
+    const unsigned long long k0 = lane < E ? route_key(v0, lane) : 0ull;
+    const unsigned long long k1 = lane + 32 < E ? route_key(v1, lane + 32) : 0ull;
+    int r0 = 0, r1 = 0;  // keys are distinct (the index is part of the key), so ranks are a permutation
+#pragma unroll 8
+    for (int src = 0; src < 32; ++src) {
+        const unsigned long long a = shfl_u64(k0, src), b = shfl_u64(k1, src);
+        r0 += (int)(a > k0) + (int)(b > k0);
+        r1 += (int)(a > k1) + (int)(b > k1);
     }
-    if (lane == 0) {
-        float ex[kMaxTopK];
-        float sum = 0.0f;
-#pragma unroll
-        for (int j = 0; j < kMaxTopK; ++j)
-            if (j < k) ex[j] = expf(__fsub_rn(vals[j], vals[0]));
-#pragma unroll
-        for (int j = 0; j < kMaxTopK; ++j)
-            if (j < k) sum = __fadd_rn(sum, ex[j]);
-#pragma unroll
-        for (int j = 0; j < kMaxTopK; ++j)
-            if (j < k) {
-                ids_out[j] = ids[j];
-                w_out[j] = __fdiv_rn(ex[j], sum);
-            }
+    if (lane < E && r0 < k) {
+        sid[r0] = lane;
+        sval[r0] = v0;
+    }
+    if (lane + 32 < E && r1 < k) {
+        sid[r1] = lane + 32;
+        sval[r1] = v1;
+    }
+    __syncwarp();
+    const float ex = lane < k ? expf(__fsub_rn(sval[lane], sval[0])) : 0.0f;
+    float sum = 0.0f;
+    for (int j = 0; j < k; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, ex, j));
+    if (lane < k) {
+        ids_out[lane] = sid[lane];
+        w_out[lane] = __fdiv_rn(ex, sum);
     }
 }
 
@@ -557,6 +527,8 @@ __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
     float* xs = smem;
     float* red = smem + a.H;
     __shared__ bool is_last;
+    __shared__ int sid[kMaxTopK];
+    __shared__ float sval[kMaxTopK];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int e = blockIdx.x * (BLOCK >> 5) + warp;
     const bool active = e < a.E;
@@ -582,7 +554,7 @@ __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
     if (warp != 0) return;
     const float v0 = lane < a.E ? __ldcg(a.logits + lane) : 0.0f;
     const float v1 = lane + 32 < a.E ? __ldcg(a.logits + lane + 32) : 0.0f;
-    route_topk_warp(v0, v1, a.E, a.k, a.ids, a.weights);
+    route_topk_warp(v0, v1, a.E, a.k, a.ids, a.weights, sid, sval);
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -599,11 +571,16 @@ template <int NCH>
 __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
     constexpr int BLOCK = 32 * kOpWarps;
     extern __shared__ __align__(16) float smem[];
-    float* xs = smem;                  // [qd]
-    float* wrs = smem + a.qd;          // [kOpRows, E]
+    float* xs = smem;                                  // [qd]
+    float* wrs = smem + a.qd;                          // [kOpRows, E]
+    float* swt = wrs + (a.route ? kOpRows * a.E : 0);  // [heads * kAttnSplits] split weights (merge mode)
+    float* sln = swt + a.heads * kAttnSplits;          // [heads * kAttnSplits] split sums of exponentials
     __shared__ float hs[kOpRows];
     __shared__ float tot[BLOCK];
+    __shared__ float sden[kMaxHeads];
     __shared__ bool is_last;
+    __shared__ int sid[kMaxTopK];
+    __shared__ float sval[kMaxTopK];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r0 = blockIdx.x * kOpRows;
     const int ra = r0 + 2 * warp, rb = ra + 1;
@@ -618,7 +595,60 @@ __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
     pdl_launch();
     const float ha = (lane == 0 && ra < a.H) ? __ldcg(a.h + ra) : 0.0f;
     const float hb = (lane == 0 && rb < a.H) ? __ldcg(a.h + rb) : 0.0f;
-    copy_to_smem<BLOCK>(a.att, a.qd, xs);
+    if (a.part_acc) {
+        // merge the attention splits (flash-decoding) while staging the output: per head h and split s the weight
+        // exp(m_s - M_h), then att[h, d] = sum_s acc_s[h, d] w_s / sum_s l_s w_s
+        constexpr int NSP = kAttnSplits;
+        const int hsn = a.heads * NSP;
+        for (int i = threadIdx.x; i < hsn; i += BLOCK) {
+            const float2 t = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + i);
+            swt[i] = t.x;
+            sln[i] = t.y;
+        }
+        __syncthreads();
+        if (threadIdx.x < a.heads) {
+            float* w = swt + threadIdx.x * NSP;
+            const float* ln = sln + threadIdx.x * NSP;
+            float M = -INFINITY;
+#pragma unroll
+            for (int sp = 0; sp < NSP; ++sp) M = fmaxf(M, w[sp]);
+            float den = 0.0f;
+#pragma unroll
+            for (int sp = 0; sp < NSP; ++sp) {
+                const float e = w[sp] == -INFINITY ? 0.0f : expf(w[sp] - M);
+                den = fmaf(ln[sp], e, den);
+                w[sp] = e;
+            }
+            sden[threadIdx.x] = den;
+        }
+        __syncthreads();
+        // two outputs per thread per batch, all 2 x kAttnSplits loads of a batch in flight together
+        for (int c0 = threadIdx.x; c0 < a.qd; c0 += 2 * BLOCK) {
+            float pa[2][NSP];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int c = c0 + q * BLOCK;
+                const int h = c / kHeadDim, d = c - (c / kHeadDim) * kHeadDim;
+#pragma unroll
+                for (int sp = 0; sp < NSP; ++sp)
+                    pa[q][sp] = c < a.qd ? __ldcg(a.part_acc + ((size_t)h * NSP + sp) * kHeadDim + d) : 0.0f;
+            }
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int c = c0 + q * BLOCK;
+                if (c < a.qd) {
+                    const int h = c / kHeadDim;
+                    float num = 0.0f;
+#pragma unroll
+                    for (int sp = 0; sp < NSP; ++sp) num = fmaf(pa[q][sp], swt[h * NSP + sp], num);
+                    xs[c] = num / sden[h];
+                }
+            }
+        }
+        __syncthreads();
+    } else {
+        copy_to_smem<BLOCK>(a.att, a.qd, xs);
+    }
     float4 xa[NCH], xb[NCH];
     x_to_regs<NCH>(xs, a.qd, lane, xa, xb);
     const float oa = warp_sum(row_dot_regs<NCH>(wa, xa, xb, a.qd, lane));
@@ -684,7 +714,7 @@ __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
     if (lane < a.E) a.logits[lane] = l0;
     if (lane + 32 < a.E) a.logits[lane + 32] = l1;
     if (lane == 0) *a.rnorm_out = r;
-    route_topk_warp(l0, l1, a.E, a.k, a.ids, a.weights);
+    route_topk_warp(l0, l1, a.E, a.k, a.ids, a.weights, sid, sval);
 }
 
 // W_r^T scaled by the MoE norm weight, [H, E] f32: the fused router's operand, prepared once per layer
@@ -990,39 +1020,21 @@ cudaError_t launch_qkv_rope(const QkvArgs& a, cudaStream_t s, bool pdl) {
     LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(qkv_rope_kernel<N, false>, grid, block, smem, s, pdl, a));
 }
 
-int attn_split_cap(int max_len) { return (max_len + kAttnCluster - 1) / kAttnCluster + 1; }
+int attn_split_cap(int max_len) { return (max_len + kAttnSplits - 1) / kAttnSplits + 1; }
 
 size_t attn_smem(int max_len, int kv_f32) { return (size_t)2 * attn_split_cap(max_len) * kHeadDim * (kv_f32 ? 4 : 2); }
 
-template <typename Kern>
-cudaError_t launch_attn_cluster(Kern kernel, const AttnArgs& a, cudaStream_t s, bool pdl) {
-    const size_t smem = attn_smem(a.max_len, a.kv_f32);
-    cudaError_t e = allow_smem(kernel, smem);
-    if (e != cudaSuccess) return e;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kAttnCluster, a.kv_heads);
-    cfg.blockDim = dim3(32 * kAttnWarps);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kAttnCluster;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, kernel, a);
-}
-
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     if (a.d != kHeadDim || a.split_cap != attn_split_cap(a.max_len)) return cudaErrorInvalidValue;
-    if (attn_smem(a.max_len, a.kv_f32) > kMaxSmemBytes) return cudaErrorInvalidValue;
-#define LASTRO_ATTN_G(GV)                                                                       \
-    case GV:                                                                                    \
-        return a.kv_f32 ? launch_attn_cluster(attention_kernel<true, GV>, a, s, pdl)            \
-                        : launch_attn_cluster(attention_kernel<false, GV>, a, s, pdl);
+    const size_t smem = attn_smem(a.max_len, a.kv_f32);
+    if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
+    const dim3 grid(kAttnSplits, a.kv_heads), block(32 * kAttnWarps);
+#define LASTRO_ATTN_G(GV)                                                                                  \
+    case GV: {                                                                                             \
+        auto k = a.kv_f32 ? attention_kernel<true, GV> : attention_kernel<false, GV>;                      \
+        cudaError_t e = allow_smem(k, smem);                                                               \
+        return e != cudaSuccess ? e : launch_ex(k, grid, block, smem, s, pdl, a);                          \
+    }
     switch (a.G) {
         LASTRO_ATTN_G(1)
         LASTRO_ATTN_G(2)
@@ -1040,7 +1052,9 @@ int oproj_grid(int H) { return (H + kOpRows - 1) / kOpRows; }
 cudaError_t launch_oproj(const OprojArgs& a, cudaStream_t s, bool pdl) {
     const dim3 grid(oproj_grid(a.H)), block(32 * kOpWarps);
     if (a.route && (a.E > kMaxExperts || 32 * kOpWarps / (a.E + 1) < 1)) return cudaErrorInvalidValue;
-    const size_t smem = sizeof(float) * (a.qd + (a.route ? (size_t)kOpRows * a.E : 0));
+    if (a.part_acc && a.heads * kHeadDim != a.qd) return cudaErrorInvalidValue;
+    const size_t smem = sizeof(float) * (a.qd + (a.route ? (size_t)kOpRows * a.E : 0) +
+                                         (a.part_acc ? (size_t)2 * a.heads * kAttnSplits : 0));
 #define LASTRO_OP(N)                                                                  \
     {                                                                                 \
         cudaError_t e = allow_smem(oproj_kernel<N>, smem);                            \

@@ -44,7 +44,8 @@ struct AttnArgs {
     const int* page_table;
     int page_size, kv_f32;
     const int* pos;          // attends positions 0..pos
-    float* att_out;          // [heads*d]
+    float* part_acc;         // [heads, kAttnSplits, d]: per-split unnormalised outputs
+    float* part_ml;          // [heads, kAttnSplits, 2]: per-split running max and sum of exponentials
     int* err;
     int kv_heads, G, d;
     int max_len, split_cap;  // split_cap = attn_split_cap(max_len): K/V rows one CTA stages
@@ -52,7 +53,10 @@ struct AttnArgs {
 };
 
 struct OprojArgs {
-    const float* att;   // [qd]
+    const float* att;   // [qd] (used when part_acc is null)
+    const float* part_acc;  // attention splits to merge: [heads, kAttnSplits, d] (or null)
+    const float* part_ml;   // [heads, kAttnSplits, 2]
+    int heads;
     const uint16_t* w;  // [H, qd]
     float* h;           // [H], updated in place
     float resid;
@@ -151,10 +155,11 @@ constexpr int kMaxExperts = 64;
 constexpr int kMaxTopK = 8;
 constexpr int kHeadDim = 64;
 constexpr int kMaxGroup = 8;
+constexpr int kMaxHeads = kMaxHidden / kHeadDim;
 constexpr size_t kMaxSmemBytes = 220 * 1024;  // dynamic shared memory one CTA may use (B200: 227 KB)
 
-// attention: CTAs per KV head (one cluster) and the shared memory they stage K/V rows in
-constexpr int kAttnCluster = 8;
+// attention: splits (CTAs) per KV head and the shared memory they stage K/V rows in
+constexpr int kAttnSplits = 16;
 int attn_split_cap(int max_len);
 size_t attn_smem(int max_len, int kv_f32);
 
