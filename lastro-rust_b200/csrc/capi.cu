@@ -199,7 +199,6 @@ int enqueue_block(lastro_layer* obj, const float* xn, float* out, float resid, i
     LASTRO_TRY(launch_router(ra, s, false), "router launch");
     GateUpArgs ga{};
     ga.x = xn;
-    ga.norm_mode = 0;
     ga.ids = obj->ids;
     ga.w = obj->gate_up;
     ga.a = obj->a;
@@ -356,7 +355,7 @@ struct lastro_model {
     float *rlogits = nullptr, *route_w = nullptr, *rnorm = nullptr, *a = nullptr, *logits = nullptr;
     int *route_ids = nullptr, *d_token = nullptr, *d_pos = nullptr, *d_step = nullptr, *d_out_ids = nullptr;
     int* d_prompt = nullptr;
-    unsigned int *router_counter = nullptr, *head_counter = nullptr;
+    unsigned int *router_counter = nullptr, *head_counter = nullptr, *attn_counters = nullptr;
     unsigned long long* head_partial = nullptr;
     float* op_partial = nullptr;  // [oproj_grid(H), E + 1]
     int* d_err = nullptr;    // error word of the bounded waits
@@ -466,6 +465,8 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         aa.pos = m->d_pos;
         aa.part_acc = m->part_acc;
         aa.part_ml = m->part_ml;
+        aa.counters = m->attn_counters;
+        aa.att_out = m->att;
         aa.err = m->d_err;
         aa.kv_heads = d.kv_heads;
         aa.G = m->G;
@@ -478,9 +479,6 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
 
         OprojArgs oa{};
         oa.att = m->att;
-        oa.part_acc = m->part_acc;
-        oa.part_ml = m->part_ml;
-        oa.heads = d.heads;
         oa.w = L.wo;
         oa.h = m->h;
         oa.resid = d.residual_multiplier;
@@ -488,24 +486,23 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         oa.qd = m->qd;
         oa.route = 1;
         oa.wr_t = L.wr_t;
-        oa.eps = d.eps;
-        oa.partial = m->op_partial;
-        oa.counter = m->router_counter;
-        oa.logits = m->rlogits;
-        oa.ids = m->route_ids + (size_t)l * d.k;
-        oa.weights = m->route_w + (size_t)l * d.k;
-        oa.rnorm_out = m->rnorm;
+        oa.shares = m->op_partial;
         oa.E = d.experts;
-        oa.k = d.k;
         if ((e = launch_oproj(oa, s, pdl)) != cudaSuccess) return e;
         if ((e = mark(pe, s, KK_OPROJ)) != cudaSuccess) return e;
+
+        RouteShares rs{};
+        rs.shares = m->op_partial;
+        rs.nb = oproj_grid(d.hidden);
+        rs.eps = d.eps;
+        rs.ids_out = m->route_ids + (size_t)l * d.k;
+        rs.weights_out = m->route_w + (size_t)l * d.k;
+        rs.logits_out = m->rlogits;
 
         GateUpArgs ga{};
         ga.x = m->h;
         ga.ln = L.ln_moe;
-        ga.rnorm = m->rnorm;
-        ga.norm_mode = 1;
-        ga.ids = oa.ids;
+        ga.rs = rs;
         ga.w = L.gate_up;
         ga.a = m->a;
         ga.err = m->d_err;
@@ -518,8 +515,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
 
         DownArgs da{};
         da.a = m->a;
-        da.ids = oa.ids;
-        da.weights = oa.weights;
+        da.rs = rs;
         da.w = L.down;
         da.out = m->h;
         da.resid = d.residual_multiplier;
@@ -672,7 +668,7 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
           A.alloc(&m->rnorm, 1) || A.alloc(&m->a, (size_t)d.k * I) || A.alloc(&m->logits, V) ||
           A.alloc(&m->d_token, 1) || A.alloc(&m->d_pos, 1) || A.alloc(&m->d_step, 1) ||
           A.alloc(&m->d_out_ids, (size_t)max_len + 1) || A.alloc(&m->d_prompt, (size_t)max_len + 1) ||
-          A.alloc(&m->router_counter, 1) || A.alloc(&m->head_counter, 1) ||
+          A.alloc(&m->router_counter, 1) || A.alloc(&m->head_counter, 1) || A.alloc(&m->attn_counters, d.kv_heads) ||
           A.alloc(&m->head_partial, m->head_grid) || A.alloc(&m->d_err, 1) ||
           A.alloc(&m->op_partial, (size_t)oproj_grid(d.hidden) * (E + 1));
     if (bad || cudaMallocHost(&m->h_token, 2 * sizeof(int)) != cudaSuccess) {
@@ -691,6 +687,7 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
     for (void* p : {(void*)m->router_counter, (void*)m->head_counter, (void*)m->d_pos, (void*)m->d_step,
                     (void*)m->d_token, (void*)m->d_err})
         if (!e) e = cudaMemsetAsync(p, 0, sizeof(int), s);
+    if (!e) e = cudaMemsetAsync(m->attn_counters, 0, sizeof(unsigned) * d.kv_heads, s);
     if (!e) e = cudaMemsetAsync(m->route_ids, 0, sizeof(int) * d.layers * d.k, s);
     if (!e) e = cudaMemsetAsync(m->route_w, 0, sizeof(float) * d.layers * d.k, s);
     // model.rs:63-73: inv_freq = 1/theta^(2j/d) and cos/sin of pos*inv_freq, in f32 on the host

@@ -307,6 +307,8 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
     __shared__ float wm[NW][G], wl[NW][G];
     __shared__ __align__(16) float wacc[NW][G][D];
     __shared__ __align__(8) uint64_t bar;
+    __shared__ float cw[kAttnSplits][G], cl[kAttnSplits][G], cden[G];
+    __shared__ bool is_last;
     const int NS = gridDim.x, s = blockIdx.x, kvh = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
@@ -461,6 +463,40 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
             a.part_ml[hs * 2 + 1] = L;
         }
     }
+    // the last CTA of this KV head merges the NS splits of its G heads; all loads of a thread in one batch
+    if (!last_block_arrives(a.counters + kvh, (unsigned int)NS, &is_last)) return;
+    const float2* ml = reinterpret_cast<const float2*>(a.part_ml) + (size_t)kvh * G * NS;
+    for (int i = threadIdx.x; i < G * NS; i += blockDim.x) {
+        const float2 t = __ldcg(ml + i);
+        cw[i % NS][i / NS] = t.x;
+        cl[i % NS][i / NS] = t.y;
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+        const int g = threadIdx.x;
+        float M = -INFINITY;
+        for (int sp = 0; sp < NS; ++sp) M = fmaxf(M, cw[sp][g]);
+        float den = 0.0f;
+        for (int sp = 0; sp < NS; ++sp) {
+            const float e = cw[sp][g] == -INFINITY ? 0.0f : expf(cw[sp][g] - M);
+            den = fmaf(cl[sp][g], e, den);
+            cw[sp][g] = e;
+        }
+        cden[g] = den;
+    }
+    __syncthreads();
+    const float* pa = a.part_acc + (size_t)kvh * G * NS * D;
+    for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
+        const int g = t / D, dim = t - (t / D) * D;
+        float v[kAttnSplits];
+#pragma unroll
+        for (int sp = 0; sp < kAttnSplits; ++sp) v[sp] = sp < NS ? __ldcg(pa + ((size_t)g * NS + sp) * D + dim) : 0.0f;
+        float num = 0.0f;
+#pragma unroll
+        for (int sp = 0; sp < kAttnSplits; ++sp)
+            if (sp < NS) num = fmaf(v[sp], cw[sp][g], num);
+        a.att_out[((size_t)kvh * G + g) * D + dim] = num / cden[g];
+    }
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -489,8 +525,8 @@ LDEV unsigned long long shfl_xor_u64(unsigned long long v, int o) {
 // Warp-wide top-k of E <= 64 logits (lane holds experts lane and lane + 32) in block.rs:81-89's order -- total_cmp
 // descending, lower index first on ties -- then the softmax over the k (exp(v - v0), summed in order, divided).
 // Every expert's rank is counted against all E keys at once (independent shuffles, no select-max chain); the k
-// winners are placed by rank through shared scratch (sid/sval, kMaxTopK entries).  Writes ids[0..k), weights[0..k).
-LDEV void route_topk_warp(float v0, float v1, int E, int k, int* ids_out, float* w_out, int* sid, float* sval) {
+// winners land at their rank in sid/sval, the softmax weights in sw (shared, kMaxTopK entries each).
+LDEV void route_topk_warp(float v0, float v1, int E, int k, int* sid, float* sval, float* sw) {
     const int lane = threadIdx.x & 31;
     const unsigned long long k0 = lane < E ? route_key(v0, lane) : 0ull;
     const unsigned long long k1 = lane + 32 < E ? route_key(v1, lane + 32) : 0ull;
@@ -513,10 +549,64 @@ LDEV void route_topk_warp(float v0, float v1, int E, int k, int* ids_out, float*
     const float ex = lane < k ? expf(__fsub_rn(sval[lane], sval[0])) : 0.0f;
     float sum = 0.0f;
     for (int j = 0; j < k; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, ex, j));
-    if (lane < k) {
-        ids_out[lane] = sid[lane];
-        w_out[lane] = __fdiv_rn(ex, sum);
+    if (lane < k) sw[lane] = __fdiv_rn(ex, sum);
+    __syncwarp();
+}
+
+// Routing from the output projection's shares (RouteShares): the shares of CTA c go to thread (c % groups) * E1 + e,
+// each thread loads its shares in batches of independent loads and sums them in order, the groups are summed in
+// order, then r = 1/sqrt(sum h^2 / H + eps) (model.rs:141-145), logits = r * share-sums, and the top-k.  Every CTA that
+// calls this computes bitwise the same routing.  Uses __syncthreads; results in sid/sw (shared), returns r.
+template <int BLOCK>
+LDEV float route_from_shares(const RouteShares& rs, int E, int k, int H, float* red, int* sid, float* sval, float* sw,
+                             float* s_r, bool publish) {
+    constexpr int kBatch = 8;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int E1 = E + 1, groups = BLOCK / E1;
+    float acc = 0.0f;
+    if (threadIdx.x < groups * E1) {
+        const int e = threadIdx.x % E1, gi = threadIdx.x / E1;
+        for (int c0 = gi; c0 < rs.nb; c0 += groups * kBatch) {
+            float sh[kBatch];
+#pragma unroll
+            for (int q = 0; q < kBatch; ++q) {
+                const int c = c0 + q * groups;
+                sh[q] = c < rs.nb ? __ldcg(rs.shares + (size_t)c * E1 + e) : 0.0f;
+            }
+#pragma unroll
+            for (int q = 0; q < kBatch; ++q)
+                if (c0 + q * groups < rs.nb) acc = __fadd_rn(acc, sh[q]);
+        }
     }
+    red[threadIdx.x] = acc;
+    __syncthreads();
+    if (warp == 0) {
+        float v[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int e = lane + 32 * q;
+            float t = 0.0f;
+            if (e < E1)
+                for (int gi = 0; gi < groups; ++gi) t = __fadd_rn(t, red[gi * E1 + e]);
+            v[q] = t;
+        }
+        const float ss = __shfl_sync(0xffffffffu, v[E >> 5], E & 31);  // entry E is the sum of squares
+        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), rs.eps)));
+        const float l0 = lane < E ? __fmul_rn(v[0], r) : 0.0f;
+        const float l1 = lane + 32 < E ? __fmul_rn(v[1], r) : 0.0f;
+        route_topk_warp(l0, l1, E, k, sid, sval, sw);
+        if (lane == 0) *s_r = r;
+        if (publish) {
+            if (lane < E) rs.logits_out[lane] = l0;
+            if (lane + 32 < E) rs.logits_out[lane + 32] = l1;
+            if (lane < k) {
+                rs.ids_out[lane] = sid[lane];
+                rs.weights_out[lane] = sw[lane];
+            }
+        }
+    }
+    __syncthreads();
+    return *s_r;
 }
 
 template <int NCH>
@@ -528,7 +618,7 @@ __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
     float* red = smem + a.H;
     __shared__ bool is_last;
     __shared__ int sid[kMaxTopK];
-    __shared__ float sval[kMaxTopK];
+    __shared__ float sval[kMaxTopK], sw[kMaxTopK];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int e = blockIdx.x * (BLOCK >> 5) + warp;
     const bool active = e < a.E;
@@ -554,7 +644,11 @@ __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
     if (warp != 0) return;
     const float v0 = lane < a.E ? __ldcg(a.logits + lane) : 0.0f;
     const float v1 = lane + 32 < a.E ? __ldcg(a.logits + lane + 32) : 0.0f;
-    route_topk_warp(v0, v1, a.E, a.k, a.ids, a.weights, sid, sval);
+    route_topk_warp(v0, v1, a.E, a.k, sid, sval, sw);
+    if (lane < a.k) {
+        a.ids[lane] = sid[lane];
+        a.weights[lane] = sw[lane];
+    }
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -571,16 +665,9 @@ template <int NCH>
 __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
     constexpr int BLOCK = 32 * kOpWarps;
     extern __shared__ __align__(16) float smem[];
-    float* xs = smem;                                  // [qd]
-    float* wrs = smem + a.qd;                          // [kOpRows, E]
-    float* swt = wrs + (a.route ? kOpRows * a.E : 0);  // [heads * kAttnSplits] split weights (merge mode)
-    float* sln = swt + a.heads * kAttnSplits;          // [heads * kAttnSplits] split sums of exponentials
+    float* xs = smem;          // [qd]
+    float* wrs = smem + a.qd;  // [kOpRows, E]
     __shared__ float hs[kOpRows];
-    __shared__ float tot[BLOCK];
-    __shared__ float sden[kMaxHeads];
-    __shared__ bool is_last;
-    __shared__ int sid[kMaxTopK];
-    __shared__ float sval[kMaxTopK];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r0 = blockIdx.x * kOpRows;
     const int ra = r0 + 2 * warp, rb = ra + 1;
@@ -595,60 +682,7 @@ __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
     pdl_launch();
     const float ha = (lane == 0 && ra < a.H) ? __ldcg(a.h + ra) : 0.0f;
     const float hb = (lane == 0 && rb < a.H) ? __ldcg(a.h + rb) : 0.0f;
-    if (a.part_acc) {
-        // merge the attention splits (flash-decoding) while staging the output: per head h and split s the weight
-        // exp(m_s - M_h), then att[h, d] = sum_s acc_s[h, d] w_s / sum_s l_s w_s
-        constexpr int NSP = kAttnSplits;
-        const int hsn = a.heads * NSP;
-        for (int i = threadIdx.x; i < hsn; i += BLOCK) {
-            const float2 t = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + i);
-            swt[i] = t.x;
-            sln[i] = t.y;
-        }
-        __syncthreads();
-        if (threadIdx.x < a.heads) {
-            float* w = swt + threadIdx.x * NSP;
-            const float* ln = sln + threadIdx.x * NSP;
-            float M = -INFINITY;
-#pragma unroll
-            for (int sp = 0; sp < NSP; ++sp) M = fmaxf(M, w[sp]);
-            float den = 0.0f;
-#pragma unroll
-            for (int sp = 0; sp < NSP; ++sp) {
-                const float e = w[sp] == -INFINITY ? 0.0f : expf(w[sp] - M);
-                den = fmaf(ln[sp], e, den);
-                w[sp] = e;
-            }
-            sden[threadIdx.x] = den;
-        }
-        __syncthreads();
-        // two outputs per thread per batch, all 2 x kAttnSplits loads of a batch in flight together
-        for (int c0 = threadIdx.x; c0 < a.qd; c0 += 2 * BLOCK) {
-            float pa[2][NSP];
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const int c = c0 + q * BLOCK;
-                const int h = c / kHeadDim, d = c - (c / kHeadDim) * kHeadDim;
-#pragma unroll
-                for (int sp = 0; sp < NSP; ++sp)
-                    pa[q][sp] = c < a.qd ? __ldcg(a.part_acc + ((size_t)h * NSP + sp) * kHeadDim + d) : 0.0f;
-            }
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const int c = c0 + q * BLOCK;
-                if (c < a.qd) {
-                    const int h = c / kHeadDim;
-                    float num = 0.0f;
-#pragma unroll
-                    for (int sp = 0; sp < NSP; ++sp) num = fmaf(pa[q][sp], swt[h * NSP + sp], num);
-                    xs[c] = num / sden[h];
-                }
-            }
-        }
-        __syncthreads();
-    } else {
-        copy_to_smem<BLOCK>(a.att, a.qd, xs);
-    }
+    copy_to_smem<BLOCK>(a.att, a.qd, xs);
     float4 xa[NCH], xb[NCH];
     x_to_regs<NCH>(xs, a.qd, lane, xa, xb);
     const float oa = warp_sum(row_dot_regs<NCH>(wa, xa, xb, a.qd, lane));
@@ -667,54 +701,13 @@ __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
         float p = 0.0f;
 #pragma unroll 8
         for (int i = 0; i < kOpRows; ++i) p = fmaf(wrs[i * a.E + threadIdx.x], hs[i], p);
-        a.partial[(size_t)blockIdx.x * E1 + threadIdx.x] = p;
+        a.shares[(size_t)blockIdx.x * E1 + threadIdx.x] = p;
     } else if (threadIdx.x == a.E) {
         float ss = 0.0f;
 #pragma unroll 8
         for (int i = 0; i < kOpRows; ++i) ss = fmaf(hs[i], hs[i], ss);
-        a.partial[(size_t)blockIdx.x * E1 + a.E] = ss;
+        a.shares[(size_t)blockIdx.x * E1 + a.E] = ss;
     }
-    if (!last_block_arrives(a.counter, gridDim.x, &is_last)) return;
-    // shares of CTA c go to thread (c % groups) * E1 + e; each thread loads all of its shares in one batch, then
-    // the groups are summed in order
-    constexpr int kMaxShares = 8;
-    const int groups = BLOCK / E1, nb = gridDim.x;
-    float acc = 0.0f;
-    if (threadIdx.x < groups * E1) {
-        const int e = threadIdx.x % E1, gi = threadIdx.x / E1;
-        for (int c0 = gi; c0 < nb; c0 += groups * kMaxShares) {
-            float sh[kMaxShares];
-#pragma unroll
-            for (int q = 0; q < kMaxShares; ++q) {
-                const int c = c0 + q * groups;
-                sh[q] = c < nb ? __ldcg(a.partial + (size_t)c * E1 + e) : 0.0f;
-            }
-#pragma unroll
-            for (int q = 0; q < kMaxShares; ++q)
-                if (c0 + q * groups < nb) acc = __fadd_rn(acc, sh[q]);
-        }
-    }
-    tot[threadIdx.x] = acc;
-    __syncthreads();
-    if (warp != 0) return;
-    float v[2];
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-        const int e = lane + 32 * q;
-        float t = 0.0f;
-        if (e < E1)
-            for (int gi = 0; gi < groups; ++gi) t = __fadd_rn(t, tot[gi * E1 + e]);
-        v[q] = t;
-    }
-    // the sum of squares is entry E: lane E % 32 of half E / 32
-    const float ss = __shfl_sync(0xffffffffu, v[a.E >> 5], a.E & 31);
-    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.H), a.eps)));
-    const float l0 = lane < a.E ? __fmul_rn(v[0], r) : 0.0f;
-    const float l1 = lane + 32 < a.E ? __fmul_rn(v[1], r) : 0.0f;
-    if (lane < a.E) a.logits[lane] = l0;
-    if (lane + 32 < a.E) a.logits[lane + 32] = l1;
-    if (lane == 0) *a.rnorm_out = r;
-    route_topk_warp(l0, l1, a.E, a.k, a.ids, a.weights, sid, sval);
 }
 
 // W_r^T scaled by the MoE norm weight, [H, E] f32: the fused router's operand, prepared once per layer
@@ -744,22 +737,34 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
     uint16_t* wu = wg + (size_t)R * a.H;                    // [R, H]
     float* xs = reinterpret_cast<float*>(wu + (size_t)R * a.H);
     __shared__ __align__(8) uint64_t bar[2];
+    __shared__ float red[BLOCK];
+    __shared__ int sid[kMaxTopK];
+    __shared__ float sval[kMaxTopK], sw[kMaxTopK], s_r;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int per_slot = a.I / R;
     const int slot = blockIdx.x / per_slot, j0 = (blockIdx.x - slot * per_slot) * R;
+    const bool fused = a.rs.shares != nullptr;
     if (threadIdx.x == 0) {
         mbar_init(&bar[0], 1);
         mbar_init(&bar[1], 1);
     }
     float4 ln[NV];
-    if (a.norm_mode) vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
+    if (fused) vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
 
     pdl_wait();
     pdl_launch();
 
+    float4 v[NV];
+    float r = 0.0f;
+    if (fused) {
+        vec_load_cg<BLOCK, NV>(a.x, a.H, v);  // in flight while the routing is reduced
+        r = route_from_shares<BLOCK>(a.rs, a.E, a.k, a.H, red, sid, sval, sw, &s_r, blockIdx.x == 0);
+    } else {
+        __syncthreads();  // barrier init visible to every waiting thread
+    }
     if (threadIdx.x == 0) {
-        // expert ids come from the router; clamped so that a stale id can never address outside the weights
-        const int e = min(max(__ldcg(a.ids + slot), 0), a.E - 1);
+        // expert id, clamped so that a stale id can never address outside the weights
+        const int e = min(max(fused ? sid[slot] : __ldcg(a.ids + slot), 0), a.E - 1);
         const uint16_t* base = a.w + (size_t)e * 2 * a.I * a.H;
         const uint32_t bytes = (uint32_t)(HALF * a.H * 2);
 #pragma unroll
@@ -769,11 +774,8 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
             bulk_g2s(wu + (size_t)st * HALF * a.H, base + (size_t)(a.I + j0 + st * HALF) * a.H, bytes, &bar[st]);
         }
     }
-    if (a.norm_mode) {
-        // xn = ln * (h * r) with the router's r
-        float4 v[NV];
-        vec_load_cg<BLOCK, NV>(a.x, a.H, v);
-        const float r = __ldcg(a.rnorm);
+    if (fused) {
+        // xn = ln * (h * r) (model.rs:141-145)
 #pragma unroll
         for (int k = 0; k < NV; ++k) {
             const int i = threadIdx.x + k * BLOCK;
@@ -806,26 +808,32 @@ constexpr int kDnRows = 8;
 
 template <int NCI>
 __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
-    constexpr int R = kDnRows;
+    constexpr int BLOCK = 256, R = kDnRows;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     uint16_t* wd = reinterpret_cast<uint16_t*>(smem_raw);                // [k, R, I]
     float* part = reinterpret_cast<float*>(wd + (size_t)a.k * R * a.I);  // [k, R]
     __shared__ __align__(8) uint64_t bar;
+    __shared__ float red[BLOCK];
+    __shared__ int sid[kMaxTopK];
+    __shared__ float sval[kMaxTopK], sw[kMaxTopK], s_r;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r0 = blockIdx.x * R;
+    const bool fused = a.rs.shares != nullptr;
+    // the routing was produced two kernels back (router kernel, or the output projection's shares): final already
+    if (fused) route_from_shares<BLOCK>(a.rs, a.E, a.k, a.H, red, sid, sval, sw, &s_r, false);
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         const uint32_t bytes = (uint32_t)(R * a.I * 2);
         mbar_expect_tx(&bar, bytes * a.k);
         for (int j = 0; j < a.k; ++j) {
-            const int e = min(max(__ldcg(a.ids + j), 0), a.E - 1);
+            const int e = min(max(fused ? sid[j] : __ldcg(a.ids + j), 0), a.E - 1);
             bulk_g2s(wd + (size_t)j * R * a.I, a.w + ((size_t)e * a.H + r0) * a.I, bytes, &bar);
         }
     }
     __syncthreads();  // the barrier is initialized before any thread waits on it
     float gw[kMaxTopK];
 #pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j) gw[j] = j < a.k ? __ldcg(a.weights + j) : 0.0f;
+    for (int j = 0; j < kMaxTopK; ++j) gw[j] = j < a.k ? (fused ? sw[j] : __ldcg(a.weights + j)) : 0.0f;
     pdl_wait();
     pdl_launch();
     const float hr = (threadIdx.x < R && a.accumulate) ? __ldcg(a.out + r0 + threadIdx.x) : 0.0f;
@@ -991,9 +999,11 @@ int chunks_for(int n) { return (n + 255) / 256; }
 // ---------------------------------------------------------------------------------------------------------------------
 // launchers
 // ---------------------------------------------------------------------------------------------------------------------
+// Dynamic shared memory beyond the default must be opted into; the default leaves 48 KB minus the kernel's static
+// shared memory, so any sizeable request sets the attribute.
 template <typename Kern>
 cudaError_t allow_smem(Kern k, size_t bytes) {
-    if (bytes <= 48 * 1024) return cudaSuccess;
+    if (bytes <= 16 * 1024) return cudaSuccess;
     return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
@@ -1051,10 +1061,8 @@ int oproj_grid(int H) { return (H + kOpRows - 1) / kOpRows; }
 
 cudaError_t launch_oproj(const OprojArgs& a, cudaStream_t s, bool pdl) {
     const dim3 grid(oproj_grid(a.H)), block(32 * kOpWarps);
-    if (a.route && (a.E > kMaxExperts || 32 * kOpWarps / (a.E + 1) < 1)) return cudaErrorInvalidValue;
-    if (a.part_acc && a.heads * kHeadDim != a.qd) return cudaErrorInvalidValue;
-    const size_t smem = sizeof(float) * (a.qd + (a.route ? (size_t)kOpRows * a.E : 0) +
-                                         (a.part_acc ? (size_t)2 * a.heads * kAttnSplits : 0));
+    if (a.route && a.E > kMaxExperts) return cudaErrorInvalidValue;
+    const size_t smem = sizeof(float) * (a.qd + (a.route ? (size_t)kOpRows * a.E : 0));
 #define LASTRO_OP(N)                                                                  \
     {                                                                                 \
         cudaError_t e = allow_smem(oproj_kernel<N>, smem);                            \

@@ -46,6 +46,8 @@ struct AttnArgs {
     const int* pos;          // attends positions 0..pos
     float* part_acc;         // [heads, kAttnSplits, d]: per-split unnormalised outputs
     float* part_ml;          // [heads, kAttnSplits, 2]: per-split running max and sum of exponentials
+    unsigned int* counters;  // [kv_heads], zero between launches
+    float* att_out;          // [heads * d], merged by the last CTA of each KV head
     int* err;
     int kv_heads, G, d;
     int max_len, split_cap;  // split_cap = attn_split_cap(max_len): K/V rows one CTA stages
@@ -53,25 +55,28 @@ struct AttnArgs {
 };
 
 struct OprojArgs {
-    const float* att;   // [qd] (used when part_acc is null)
-    const float* part_acc;  // attention splits to merge: [heads, kAttnSplits, d] (or null)
-    const float* part_ml;   // [heads, kAttnSplits, 2]
-    int heads;
+    const float* att;   // [qd]
     const uint16_t* w;  // [H, qd]
     float* h;           // [H], updated in place
     float resid;
     int H, qd;
-    // fused MoE router (route != 0)
+    // fused MoE router (route != 0): every CTA writes its rows' shares of the router logits and of sum h^2
     int route;
     const float* wr_t;      // [H, E]: router weight x MoE norm weight, transposed (launch_router_fold)
+    float* shares;          // [oproj_grid(H), E + 1]
+    int E;
+};
+
+// Routing of the fused path: the output projection's per-CTA shares, reduced by every CTA of the expert kernels in
+// the same fixed order, so each CTA holds bitwise the same routing without another launch or cross-CTA exchange.
+struct RouteShares {
+    const float* shares;  // [nb, E + 1], or null when the routing comes from the router kernel (ids/weights)
+    int nb;
     float eps;
-    float* partial;         // [oproj_grid(H), E + 1] per-CTA shares of the logits and of sum h^2
-    unsigned int* counter;  // zero between launches
-    float* logits;          // [E]
-    int* ids;               // [k]
-    float* weights;         // [k]
-    float* rnorm_out;       // 1/sqrt(mean(h^2) + eps)
-    int E, k;
+    // published by CTA 0 of the gate_up kernel (the step's routing output)
+    int* ids_out;
+    float* weights_out;
+    float* logits_out;
 };
 
 struct RouterArgs {
@@ -89,11 +94,10 @@ struct RouterArgs {
 };
 
 struct GateUpArgs {
-    const float* x;       // norm_mode: residual h; otherwise the block input
-    const float* ln;      // norm_mode: norm weight
-    const float* rnorm;   // norm_mode: from the router kernel
-    int norm_mode;
-    const int* ids;       // [k]
+    const float* x;       // rs.shares set: residual h (xn = ln * (h * r)); otherwise the block input
+    const float* ln;      // MoE norm weight (with shares)
+    const int* ids;       // [k] from the router kernel (without shares)
+    RouteShares rs;
     const uint16_t* w;    // [E, 2I, H]
     float* a;             // [k, I]
     int* err;             // error word: a bounded wait that gave up writes its code here
@@ -102,8 +106,9 @@ struct GateUpArgs {
 
 struct DownArgs {
     const float* a;        // [k, I]
-    const int* ids;        // [k]
+    const int* ids;        // [k] from the router kernel (without shares)
     const float* weights;  // [k]
+    RouteShares rs;
     const uint16_t* w;     // [E, H, I]
     float* out;            // accumulate: h += resid*y ; else out = y
     float resid;
