@@ -70,6 +70,22 @@ int lastro_layer_forward(lastro_layer *layer, const float *x, float *y, int32_t 
 int lastro_layer_add_into(lastro_layer *layer, const float *xn_dev, float *h_dev, float resid, int32_t *ids_dev,
                           float *weights_dev);
 void lastro_layer_destroy(lastro_layer *layer);
+/* Allocation-free variant of lastro_layer_forward, with no counterpart in the reference.  For callers that cannot
+ * call cudaMalloc -- device memory owned by another runtime's allocator, code running inside a stream capture, or a
+ * path where cudaMalloc's implicit synchronisation is not acceptable: they pass every buffer, all device pointers
+ * (x [H] f32, router [E,H], gate_up [E,2I,H], down [E,H,I] bf16 bits, outputs y [H] f32, ids [k] i32, weights [k]
+ * f32), and the call enqueues the block on `stream` (a cudaStream_t, NULL = legacy stream) of the calling thread's
+ * current device without allocating or synchronising.  Its scratch (router logits, a ticket, an error word and the
+ * k*I SwiGLU activations) is one file-scope __device__ array of about 66 KB that every GPU loading the library holds
+ * until the process exits; limits: experts <= 64, k * inter <= 16384.  The first call on a device looks the array's
+ * address up (cudaGetSymbolAddress), so make that first call before any stream capture.  Every call shares the
+ * array: calls that overlap on the GPU (other streams, other threads) race; serialise them.  The call clears the
+ * array's ticket and error word itself; nothing else in it needs to start at zero.  Returns LASTRO_E_ARG or
+ * LASTRO_E_UNSUPPORTED for shapes beyond the limits, before any launch; it does not report the kernels' bounded
+ * copy-wait status (the error word stays in the scratch). */
+int lastro_moe_block_forward_noalloc(const float *x, const uint16_t *router, const uint16_t *gate_up,
+                                     const uint16_t *down, int32_t experts, int32_t hidden, int32_t inter, int32_t k,
+                                     float *y, int32_t *ids, float *weights, void *stream);
 
 /* ---- whole model: GpuModel (gpu_model.rs:154-455) --------------------------------------------------------------- */
 /* GpuModel::upload (gpu_model.rs:191-242): allocates weights, the paged KV cache for max_len positions and the

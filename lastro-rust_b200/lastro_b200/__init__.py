@@ -57,6 +57,7 @@ EXPORTS = {
     "lastro_layer_forward": (C.c_int, [C.c_void_p] + [C.c_void_p] * 5),
     "lastro_layer_add_into": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p]),
     "lastro_layer_destroy": (None, [C.c_void_p]),
+    "lastro_moe_block_forward_noalloc": (C.c_int, [C.c_void_p] * 4 + [C.c_int32] * 4 + [C.c_void_p] * 4),
     "lastro_model_create": (C.c_int, [C.c_void_p, C.POINTER(ModelDesc), C.c_int32, C.POINTER(C.c_void_p)]),
     "lastro_model_load_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int32, C.POINTER(C.c_int64), C.c_int32,
                                            C.c_void_p]),
@@ -159,6 +160,13 @@ class GpuLayer:
 
     def __del__(self):
         self.close()
+
+
+def moe_block_forward_noalloc(x: int, router: int, gate_up: int, down: int, experts: int, hidden: int, inter: int,
+                              k: int, y: int, ids: int, weights: int, stream: int | None = None) -> int:
+    """Allocation-free MoE block on device pointers (lastro_moe_block_forward_noalloc); returns the status code."""
+    return lib().lastro_moe_block_forward_noalloc(x, router, gate_up, down, experts, hidden, inter, k, y, ids, weights,
+                                                  stream)
 
 
 TENSOR_NAMES = ("input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_proj.weight",
