@@ -11,7 +11,8 @@ uniform random ids (seed 2) through the model itself, then greedy decode.  One b
   e2e    the same decode through the public C-ABI step call a user makes (lastro_model_step): the token goes
          host->device and the next token device->host every step, inside the timed region
   roofline  the dominant kernel (by device time) of the step: algorithmic bytes per launch / its mean duration,
-         measured live with events between direct launches (lastro_model_profile)
+         measured live with events around direct launches (lastro_model_profile).  --fused runs the step as one
+         persistent kernel instead of the per-layer chain; its roofline is then the whole step's bytes / its duration
   cpu_baseline  the CPU oracle (a C restatement of the reference's CPU path, rust/moe-rt/src/{cpu,model}.rs)
          decoding the same model at the same context on this host's cores
 
@@ -32,7 +33,7 @@ sys.path.insert(0, os.path.join(ROOT, "lastro-rust_b200"))
 
 from lastro_b200 import configs as CFG  # noqa: E402
 
-KERNELS = ("qkv_rope", "attention", "oproj", "router", "gate_up", "down", "head")
+KERNELS = ("qkv_rope", "attention", "oproj", "router", "gate_up", "down", "head", "fused_step")
 
 
 def parse():
@@ -48,6 +49,8 @@ def parse():
     ap.add_argument("--profile-only", action="store_true", help="small run for ncu: synthetic KV + 3 decode steps")
     ap.add_argument("--synthetic-kv", action="store_true", help="fill the context with synthetic K/V instead of "
                     "decoding the prompt through the model")
+    ap.add_argument("--fused", action="store_true", help="the fused step kernel (one persistent launch per step) instead "
+                    "of the per-layer kernel chain")
     return ap.parse_args()
 
 
@@ -63,8 +66,11 @@ def kernel_bytes(cfg, context):
     """Algorithmic HBM bytes of one launch of each kernel (bf16 weights, bf16 KV), at the given mean context."""
     H, I, E, k, V = cfg["hidden"], cfg["inter"], cfg["experts"], cfg["k"], cfg["vocab"]
     qd, kvd = cfg["heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
-    return dict(qkv_rope=(qd + 2 * kvd) * H * 2 + 2 * kvd * 2, attention=2 * kvd * 2 * context,
-                oproj=H * qd * 2 + H * E * 4, router=0, gate_up=k * 2 * I * H * 2, down=k * H * I * 2, head=V * H * 2)
+    kb = dict(qkv_rope=(qd + 2 * kvd) * H * 2 + 2 * kvd * 2, attention=2 * kvd * 2 * context,
+              oproj=H * qd * 2 + H * E * 4, router=0, gate_up=k * 2 * I * H * 2, down=k * H * I * 2, head=V * H * 2)
+    # the fused step kernel moves every layer's bytes and the head's in one launch
+    kb["fused_step"] = cfg["layers"] * sum(kb[n] for n in ("qkv_rope", "attention", "oproj", "gate_up", "down")) + kb["head"]
+    return kb
 
 
 class ClockSampler:
@@ -195,6 +201,7 @@ def main():
     ctx = LB.Context(local, stream.cuda_stream)
     max_len = a.context + 2 * (K + W) + 64
     model = LB.GpuModel(ctx, cfg, max_len, kv_dtype=a.kv)
+    model.set_options(fused=a.fused)
     model.fill_synthetic(c["weight_seed"], CFG.WEIGHT_STD, 0.0)
     t0 = time.time()
     if a.synthetic_kv or a.profile_only:
@@ -261,8 +268,9 @@ def main():
     L = cfg["layers"]
     prof_ctx = model.pos - 2
     kb = kernel_bytes(cfg, prof_ctx)
-    launches = {k: (1 if k == "head" else L) for k in KERNELS}
+    launches = {k: (1 if k in ("head", "fused_step") else L) for k in KERNELS}
     dominant = max(KERNELS, key=lambda k: prof[k])
+    fused = model.fused
     per_launch_ms = prof[dominant] / launches[dominant]
     hbm, peak_kind = peaks()
     achieved = kb[dominant] / (per_launch_ms / 1000.0) / 1e9
@@ -282,6 +290,8 @@ def main():
         "config": {"workload": c["name"], "batch": 1, "context_start": ctx0, "mean_context": mean_ctx,
                    "kv_cache": f"paged {a.kv}", "weights": "bf16, activations/accumulators f32",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "step_kernel": "fused: one persistent cooperative launch per step" if fused else
+                   "chain: 5 kernels per layer + head, PDL, CUDA graph",
                    "l2": "inputs larger than L2: every step streams ~1.9 GB of weights and KV (L2 126 MB)",
                    "prefill_s": round(prefill_s, 2)},
         "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": hbm, "unit": "GB/s",
@@ -291,11 +301,11 @@ def main():
                           "literal_frac": B["literal"] / step_s / 1e9 / hbm,
                           "full_frac": B["full"] / step_s / 1e9 / hbm,
                           "literal_frac_vs_8tbs": B["literal"] / step_s / 1e9 / 8000.0},
-        "moe_block": {"gbs": moe_bytes / (moe_ms / 1000.0) / 1e9, "frac": moe_bytes / (moe_ms / 1000.0) / 1e9 / hbm,
-                      "us_per_layer": moe_ms * 1000.0},
+        "moe_block": None if fused else {"gbs": moe_bytes / (moe_ms / 1000.0) / 1e9,
+                                         "frac": moe_bytes / (moe_ms / 1000.0) / 1e9 / hbm, "us_per_layer": moe_ms * 1000.0},
         "kernels_ms_per_step": {k: round(v, 4) for k, v in prof.items()},
         "e2e": e2e,
-        "gpu_launches": K * (5 * L + 1),
+        "gpu_launches": K * (1 if fused else 5 * L + 1),
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not a.no_cpu_baseline:

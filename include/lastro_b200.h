@@ -50,7 +50,7 @@ typedef struct {
 /* ---- context: one device, one stream (the reference's Arc<Stream>, gpu.rs:333) ---------------------------------- */
 /* stream_or_null: a cudaStream_t to enqueue on, or NULL for a stream owned by the context */
 int lastro_ctx_create(int32_t device, void *stream_or_null, lastro_ctx **out);
-/* destroy every layer and model created on ctx first */
+/* the context lives on until its last layer and model are destroyed: objects may be destroyed in any order */
 void lastro_ctx_destroy(lastro_ctx *ctx);
 int lastro_ctx_synchronize(lastro_ctx *ctx);
 /* text of the last error on this context ("" if none); valid until the next call on ctx */
@@ -114,12 +114,18 @@ int lastro_model_decode(lastro_model *model, int32_t n);
 int lastro_model_reset(lastro_model *model);
 int lastro_model_position(const lastro_model *model, int32_t *pos);
 /* per-kernel device time of `steps` decode steps (direct launches with an event between kernels, no graph, no
- * PDL), averaged per step and summed over layers: kernel_ms[0..6] = qkv_rope, attention, oproj, router, gate_up,
- * down, head.  Advances the position like lastro_model_decode.  No reference counterpart: measurement only
- * (the reference's step_probe, gpu_model.rs:275-300, times whole steps). */
+ * PDL), averaged per step and summed over layers: kernel_ms[0..7] = qkv_rope, attention, oproj, router, gate_up,
+ * down, head, fused_step (the whole step when the fused kernel runs it; then the others are 0).  Advances the
+ * position like lastro_model_decode.  No reference counterpart: measurement only (the reference's step_probe,
+ * gpu_model.rs:275-300, times whole steps). */
 int lastro_model_profile(lastro_model *model, int32_t steps, float *kernel_ms, int32_t n_kinds);
-/* tuning: use CUDA graphs (default 1) and programmatic dependent launch (default 1) */
-int lastro_model_set_options(lastro_model *model, int32_t use_graphs, int32_t use_pdl);
+/* tuning: use CUDA graphs (default 1), programmatic dependent launch between the per-layer kernels (default 1),
+ * and the fused step -- the whole step as one persistent cooperative launch, one CTA per SM -- where the model's
+ * shapes fit it (default 0: on B200 it measures slower than the per-layer kernels; lastro_model_fused reports
+ * whether the fused step runs) */
+int lastro_model_set_options(lastro_model *model, int32_t use_graphs, int32_t use_pdl, int32_t use_fused);
+/* 1 when decode steps run as the fused step kernel (shapes fit and the option is on), else 0 */
+int lastro_model_fused(const lastro_model *model);
 void lastro_model_destroy(lastro_model *model);
 
 #ifdef __cplusplus

@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -25,11 +26,15 @@ using namespace lastro;
 
 #define LASTRO_VERSION "lastro-b200 0.1.0 (sm_100a)"
 
+// Reference-counted by its layers and models, so that the context and its objects may be destroyed in any order
+// (a garbage-collected host language finalises objects in no fixed order).
 struct lastro_ctx {
     int device = 0;
     cudaStream_t stream = nullptr;
     bool own_stream = false;
     std::string err;
+    std::atomic<int> refs{1};
+    std::atomic<bool> closed{false};
 };
 
 namespace {
@@ -118,12 +123,23 @@ extern "C" int lastro_ctx_create(int32_t device, void* stream, lastro_ctx** out)
     return LASTRO_OK;
 }
 
-extern "C" void lastro_ctx_destroy(lastro_ctx* c) {
-    if (!c) return;
+namespace {
+
+void ctx_retain(lastro_ctx* c) { c->refs.fetch_add(1); }
+
+void ctx_release(lastro_ctx* c) {
+    if (c->refs.fetch_sub(1) != 1) return;
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->own_stream) cudaStreamDestroy(c->stream);
     delete c;
+}
+
+}  // namespace
+
+extern "C" void lastro_ctx_destroy(lastro_ctx* c) {
+    if (!c || c->closed.exchange(true)) return;
+    ctx_release(c);
 }
 
 extern "C" int lastro_ctx_synchronize(lastro_ctx* c) {
@@ -265,6 +281,7 @@ extern "C" int lastro_layer_create(lastro_ctx* ctx, int32_t E, int32_t H, int32_
         delete obj;
         return set_err(ctx, LASTRO_E_CUDA, "layer upload: %s", cudaGetErrorString(e));
     }
+    ctx_retain(ctx);
     *out = obj;
     return LASTRO_OK;
 }
@@ -317,7 +334,9 @@ extern "C" void lastro_layer_destroy(lastro_layer* obj) {
     cudaSetDevice(obj->ctx->device);
     cudaStreamSynchronize(obj->ctx->stream);  // gpu.rs:544-550: kernels may still read the weights
     obj->arena.release();
+    lastro_ctx* ctx = obj->ctx;
     delete obj;
+    ctx_release(ctx);
 }
 
 // =====================================================================================================================
@@ -364,6 +383,13 @@ struct lastro_model {
     int pos_host = 0;
     std::vector<char> loaded;  // per (layer, kind)
     cudaGraphExec_t graph = nullptr;
+    // fused step (one persistent launch per step) when the shapes fit it
+    bool fused_ok = false, use_fused = false;
+    FusedLayout flay{};
+    FusedLayer* f_layers = nullptr;  // [layers] (device)
+    unsigned int *f_ticket = nullptr, *f_epoch = nullptr, *f_count = nullptr;
+    FusedExchange fx{};
+    unsigned long long* f_best = nullptr;
 };
 
 namespace {
@@ -406,7 +432,50 @@ int missing_tensor(lastro_model* m) {
 }
 
 // Kernel kinds of one step, in launch order within a layer (the head closes the step).
-enum { KK_QKV = 0, KK_ATTN, KK_OPROJ, KK_ROUTER, KK_GATE_UP, KK_DOWN, KK_HEAD, KK_COUNT };
+enum { KK_QKV = 0, KK_ATTN, KK_OPROJ, KK_ROUTER, KK_GATE_UP, KK_DOWN, KK_HEAD, KK_FUSED, KK_COUNT };
+
+FusedArgs fused_args(const lastro_model* m) {
+    const lastro_model_desc& d = m->d;
+    FusedArgs a{};
+    a.layers = m->f_layers;
+    a.L = d.layers;
+    a.embed = m->embed;
+    a.norm = m->norm;
+    a.rope_cs = m->rope_cs;
+    a.page_table = m->page_table;
+    a.page_size = kPageSize;
+    a.pos = m->d_pos;
+    a.token = m->d_token;
+    a.step = m->d_step;
+    a.out_ids = m->d_out_ids;
+    a.out_cap = m->max_len + 1;
+    a.x = m->fx;
+    a.logits = m->logits;
+    a.route_ids = m->route_ids;
+    a.route_w = m->route_w;
+    a.rlogits = m->rlogits;
+    a.best = m->f_best;
+    a.ticket = m->f_ticket;
+    a.count = m->f_count;
+    a.epoch = m->f_epoch;
+    a.err = m->d_err;
+    a.H = d.hidden;
+    a.I = d.inter;
+    a.E = d.experts;
+    a.k = d.k;
+    a.qd = m->qd;
+    a.kvd = m->kvd;
+    a.kv_heads = d.kv_heads;
+    a.G = m->G;
+    a.V = d.vocab;
+    a.eps = d.eps;
+    a.emb_mult = d.embedding_multiplier;
+    a.resid = d.residual_multiplier;
+    a.attn_scale = d.attention_multiplier;
+    a.logits_scaling = d.logits_scaling;
+    a.lay = m->flay;
+    return a;
+}
 
 // Optional per-launch events: ev[0] before the first launch, ev[i + 1] after launch i.
 struct StepEvents {
@@ -427,6 +496,10 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
     const bool pdl = m->use_pdl && !pe;
     cudaError_t e;
     if ((e = mark(pe, s)) != cudaSuccess) return e;
+    if (m->fused_ok && m->use_fused) {
+        if ((e = launch_fused_step(fused_args(m), d.kv_dtype == LASTRO_DTYPE_F32, s)) != cudaSuccess) return e;
+        return mark(pe, s, KK_FUSED);
+    }
     for (int l = 0; l < d.layers; ++l) {
         const LayerDev& L = m->L[l];
         QkvArgs qa{};
@@ -671,6 +744,30 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
           A.alloc(&m->router_counter, 1) || A.alloc(&m->head_counter, 1) || A.alloc(&m->attn_counters, d.kv_heads) ||
           A.alloc(&m->head_partial, m->head_grid) || A.alloc(&m->d_err, 1) ||
           A.alloc(&m->op_partial, (size_t)oproj_grid(d.hidden) * (E + 1));
+    // the fused step: one CTA per SM, when the per-CTA shares of every phase fit in shared memory
+    int n_sm = 0, coop = 0;
+    if (cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, ctx->device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, ctx->device) != cudaSuccess) {
+        cudaGetLastError();
+        n_sm = 0;
+    }
+    if (!bad && n_sm > 0 && coop &&
+        fused_plan(d.hidden, d.inter, d.experts, d.k, m->qd, m->kvd, d.kv_heads, G, d.vocab,
+                   d.kv_dtype == LASTRO_DTYPE_F32, n_sm, &m->flay)) {
+        int per_sm = 0;
+        if (fused_blocks_per_sm(d.hidden, m->qd, d.inter, d.kv_dtype == LASTRO_DTYPE_F32, m->flay.smem, &per_sm) !=
+            cudaSuccess)
+            cudaGetLastError();
+        m->fused_ok = per_sm >= 1;
+    }
+    const size_t n_qkv = (size_t)m->qd + 2 * m->kvd, n_part = (size_t)d.heads * m->flay.max_splits * kPartStride,
+                 n_share = (size_t)m->flay.nb * (E + 1);
+    if (m->fused_ok)
+        bad = bad || A.alloc(&m->f_layers, (size_t)d.layers) || A.alloc(&m->f_ticket, 1) || A.alloc(&m->f_epoch, 1) ||
+              A.alloc(&m->f_count, (size_t)kExchangeKinds * kCountStride) ||
+              A.alloc(&m->fx.h, H) || A.alloc(&m->fx.qkv, n_qkv) || A.alloc(&m->fx.part, n_part) ||
+              A.alloc(&m->fx.att, (size_t)m->qd) || A.alloc(&m->fx.share, n_share) || A.alloc(&m->fx.act, (size_t)d.k * I) ||
+              A.alloc(&m->f_best, (size_t)m->flay.nb);
     if (bad || cudaMallocHost(&m->h_token, 2 * sizeof(int)) != cudaSuccess) {
         cudaGetLastError();
         A.release();
@@ -688,6 +785,23 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
                     (void*)m->d_token, (void*)m->d_err})
         if (!e) e = cudaMemsetAsync(p, 0, sizeof(int), s);
     if (!e) e = cudaMemsetAsync(m->attn_counters, 0, sizeof(unsigned) * d.kv_heads, s);
+    std::vector<FusedLayer> fl;
+    if (m->fused_ok) {
+        // tag 0 is never written: zeroed exchange words never match a wait
+        if (!e) e = cudaMemsetAsync(m->f_ticket, 0, sizeof(unsigned), s);
+        if (!e) e = cudaMemsetAsync(m->f_count, 0, sizeof(unsigned) * kExchangeKinds * kCountStride, s);
+        if (!e) e = cudaMemsetAsync(m->f_epoch, 0, sizeof(unsigned), s);
+        const std::pair<unsigned long long*, size_t> words[] = {{m->fx.h, H}, {m->fx.qkv, n_qkv}, {m->fx.part, n_part},
+                                                                {m->fx.att, (size_t)m->qd}, {m->fx.share, n_share},
+                                                                {m->fx.act, (size_t)d.k * I}};
+        for (const auto& w : words)
+            if (!e) e = cudaMemsetAsync(w.first, 0, w.second * sizeof(unsigned long long), s);
+        for (int l = 0; l < d.layers; ++l) {
+            const LayerDev& L = m->L[l];
+            fl.push_back(FusedLayer{L.ln_attn, L.ln_moe, L.wr_t, L.wqkv, L.wo, L.gate_up, L.down, L.k_pool, L.v_pool});
+        }
+        if (!e) e = cudaMemcpyAsync(m->f_layers, fl.data(), sizeof(FusedLayer) * fl.size(), cudaMemcpyHostToDevice, s);
+    }
     if (!e) e = cudaMemsetAsync(m->route_ids, 0, sizeof(int) * d.layers * d.k, s);
     if (!e) e = cudaMemsetAsync(m->route_w, 0, sizeof(float) * d.layers * d.k, s);
     // model.rs:63-73: inv_freq = 1/theta^(2j/d) and cos/sin of pos*inv_freq, in f32 on the host
@@ -715,6 +829,7 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
         delete m;
         return LASTRO_E_CUDA;
     }
+    ctx_retain(ctx);
     *out = m;
     return LASTRO_OK;
 }
@@ -984,7 +1099,7 @@ extern "C" int lastro_model_profile(lastro_model* m, int32_t steps, float* kerne
     return result;
 }
 
-extern "C" int lastro_model_set_options(lastro_model* m, int32_t use_graphs, int32_t use_pdl) {
+extern "C" int lastro_model_set_options(lastro_model* m, int32_t use_graphs, int32_t use_pdl, int32_t use_fused) {
     if (!m) return LASTRO_E_ARG;
     cudaSetDevice(m->ctx->device);
     cudaStreamSynchronize(m->ctx->stream);
@@ -994,8 +1109,11 @@ extern "C" int lastro_model_set_options(lastro_model* m, int32_t use_graphs, int
     }
     m->use_graphs = use_graphs != 0;
     m->use_pdl = use_pdl != 0;
+    m->use_fused = use_fused != 0;
     return LASTRO_OK;
 }
+
+extern "C" int lastro_model_fused(const lastro_model* m) { return m && m->fused_ok && m->use_fused ? 1 : 0; }
 
 extern "C" void lastro_model_destroy(lastro_model* m) {
     if (!m) return;
@@ -1004,5 +1122,7 @@ extern "C" void lastro_model_destroy(lastro_model* m) {
     if (m->graph) cudaGraphExecDestroy(m->graph);
     m->arena.release();
     if (m->h_token) cudaFreeHost(m->h_token);
+    lastro_ctx* ctx = m->ctx;
     delete m;
+    ctx_release(ctx);
 }

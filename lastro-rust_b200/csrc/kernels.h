@@ -153,6 +153,84 @@ cudaError_t launch_synth_f32(float* out, size_t n, uint64_t seed, float scale, c
 // norms: bf16(1 + value) widened to f32
 cudaError_t launch_synth_norm_f32(float* out, size_t n, uint64_t seed, float scale, cudaStream_t s);
 
+// ---- fused decode step: the whole step (every layer and the head) in one persistent cooperative launch -----------
+// One CTA per SM.  Every value one CTA hands to another inside the step travels as a 64-bit word {f32 value, u32 tag}
+// written with one relaxed store; the reader spins on the words themselves until every tag is the one it expects
+// (the tag encodes step, layer and producing phase), so a dependency costs one round trip and no counter or flag.
+// Every CTA streams the weights of its next phase into shared memory before it waits for the phase's inputs.
+constexpr int kFusedThreads = 384;
+constexpr int kPartStride = 66;  // attention partial per (head, split): acc[64], m, l
+constexpr int kGuStages = 4;     // gate_up rows arrive in this many chunks, each on its own barrier
+constexpr int kMaxHeadStages = 6;
+constexpr int kExchangeKinds = 6;  // qkv, attention, merge, oproj, gate_up, down
+constexpr int kCountStride = 32;   // u32 words per arrival counter (one 128-byte line each)
+
+struct FusedLayer {
+    const float* ln_attn;
+    const float* ln_moe;
+    const float* wr_t;  // [H, E] router weight x MoE norm weight, transposed
+    const uint16_t* wqkv;
+    const uint16_t* wo;
+    const uint16_t* gate_up;
+    const uint16_t* down;
+    void* k_pool;
+    void* v_pool;
+};
+
+// Work split maxima and shared-memory layout (bytes), computed on the host by fused_plan.
+struct FusedLayout {
+    int nb;                          // CTAs
+    int qkv_pairs, rows, gu_pairs;   // per-CTA maxima: RoPE row pairs, output rows (oproj/down), gate_up pairs
+    int max_splits, kv_cap;          // attention: splits per KV head (<= nb / kv_heads), K/V rows per staged chunk
+    int head_rows, head_stages;      // lm_head rows per staged chunk, chunks in flight
+    int off_qkv, off_kv, off_wo, off_gu, off_dn, off_head, off_f, off_own, smem;
+};
+
+// The exchange words ({value, tag}, see above) of one step, each written by one CTA and read by others.
+struct FusedExchange {
+    unsigned long long* h;      // [H] residual stream after the output projection and after the experts
+    unsigned long long* qkv;    // [qd + 2 kvd] roped q, the new K row (as cached), the new V row
+    unsigned long long* part;   // [heads, max_splits, kPartStride] attention partials
+    unsigned long long* att;    // [qd] merged attention output
+    unsigned long long* share;  // [nb, E + 1] router-logit shares and sum h^2 of each CTA's rows
+    unsigned long long* act;    // [k, I] SwiGLU activations
+};
+
+struct FusedArgs {
+    const FusedLayer* layers;  // [L] (device)
+    int L;
+    const uint16_t* embed;     // [V, H]
+    const float* norm;         // final norm [H]
+    const float* rope_cs;      // [max_len, d]
+    const int* page_table;
+    int page_size;
+    int* pos;
+    int* token;
+    int* step;
+    int* out_ids;
+    int out_cap;
+    FusedExchange x;
+    float* logits;             // [V]
+    int* route_ids;            // [L, k]
+    float* route_w;            // [L, k]
+    float* rlogits;            // [E] (last layer)
+    unsigned long long* best;  // [nb]
+    unsigned int* ticket;      // lm_head arrivals, monotonic
+    unsigned int* count;       // [kExchangeKinds * kCountStride] arrivals per exchange kind, monotonic
+    unsigned int* epoch;       // steps completed by this model's fused kernel
+    int* err;
+    int H, I, E, k, qd, kvd, kv_heads, G, V;
+    float eps, emb_mult, resid, attn_scale, logits_scaling;
+    FusedLayout lay;
+};
+
+// false when the shapes do not fit the fused kernel (the multi-kernel step is used instead); nb is the SM count
+bool fused_plan(int H, int I, int E, int k, int qd, int kvd, int kv_heads, int G, int V, int kv_f32, int nb,
+                FusedLayout* out);
+cudaError_t launch_fused_step(const FusedArgs& a, int kv_f32, cudaStream_t s);
+// CTAs of the fused kernel one SM holds with `smem` dynamic shared memory (the launch needs >= 1)
+cudaError_t fused_blocks_per_sm(int H, int qd, int I, int kv_f32, int smem, int* blocks);
+
 // limits enforced by the host before any launch
 constexpr int kMaxHidden = 2048;   // H (and qd) <= 2048, multiple of 8
 constexpr int kMaxInter = 2048;

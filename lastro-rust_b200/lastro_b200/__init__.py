@@ -69,7 +69,8 @@ EXPORTS = {
     "lastro_model_reset": (C.c_int, [C.c_void_p]),
     "lastro_model_position": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
     "lastro_model_profile": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32]),
-    "lastro_model_set_options": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32]),
+    "lastro_model_set_options": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32]),
+    "lastro_model_fused": (C.c_int, [C.c_void_p]),
     "lastro_model_destroy": (None, [C.c_void_p]),
 }
 
@@ -243,7 +244,7 @@ class GpuModel:
         self.ctx.check(lib().lastro_model_position(self.h, C.byref(v)))
         return v.value
 
-    KERNELS = ("qkv_rope", "attention", "oproj", "router", "gate_up", "down", "head")
+    KERNELS = ("qkv_rope", "attention", "oproj", "router", "gate_up", "down", "head", "fused_step")
 
     def profile(self, steps: int) -> dict:
         """Per-kernel device ms per step (summed over layers), measured with events between direct launches."""
@@ -251,8 +252,13 @@ class GpuModel:
         self.ctx.check(lib().lastro_model_profile(self.h, steps, _p(out), out.size))
         return dict(zip(self.KERNELS, out.tolist()))
 
-    def set_options(self, graphs: bool = True, pdl: bool = True):
-        self.ctx.check(lib().lastro_model_set_options(self.h, int(graphs), int(pdl)))
+    def set_options(self, graphs: bool = True, pdl: bool = True, fused: bool = False):
+        self.ctx.check(lib().lastro_model_set_options(self.h, int(graphs), int(pdl), int(fused)))
+
+    @property
+    def fused(self) -> bool:
+        """True when decode steps run as the single fused step kernel."""
+        return bool(lib().lastro_model_fused(self.h))
 
     def close(self):
         if getattr(self, "h", None):

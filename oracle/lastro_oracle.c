@@ -610,6 +610,7 @@ struct lo_session {
     const lo_model *m;
     lo_pool *pool;
     int32_t max_len, pos;
+    int32_t layers; /* own copy: the session may be destroyed after its model */
     float **k_cache, **v_cache; /* per layer [max_len, kvd] */
 };
 
@@ -618,6 +619,7 @@ lo_session *lo_session_create(const lo_model *m, lo_pool *p, int32_t max_len) {
     s->m = m;
     s->pool = p;
     s->max_len = max_len;
+    s->layers = m->cfg.layers;
     size_t kvd = (size_t)m->cfg.kv_heads * m->cfg.head_dim;
     s->k_cache = (float **)calloc((size_t)m->cfg.layers, sizeof(float *));
     s->v_cache = (float **)calloc((size_t)m->cfg.layers, sizeof(float *));
@@ -630,7 +632,7 @@ lo_session *lo_session_create(const lo_model *m, lo_pool *p, int32_t max_len) {
 
 void lo_session_destroy(lo_session *s) {
     if (!s) return;
-    for (int32_t l = 0; l < s->m->cfg.layers; ++l) {
+    for (int32_t l = 0; l < s->layers; ++l) {
         free(s->k_cache[l]);
         free(s->v_cache[l]);
     }

@@ -21,9 +21,11 @@ GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 TIE_GAP = 1e-3  # bin/m1b-gulosa.rs:20
 
 
-def gpu_model(ctx, cfg, weights, max_len, kv="f32"):
+def gpu_model(ctx, cfg, weights, max_len, kv="f32", fused=False):
     m = LB.GpuModel(ctx, cfg, max_len, kv_dtype=kv)
     m.load_weights(weights)
+    m.set_options(fused=fused)
+    assert m.fused == fused
     return m
 
 
@@ -32,15 +34,19 @@ def toks_like_reference(n, vocab, seed=77):
     return [int((float(v) + 1.0) * 16.0) % vocab for v in values(n, seed)]
 
 
-# f32 KV: the reference's gate (tests/model.rs:268); bf16 KV rounds every cached K/V element (2^-9 relative), which
-# moves logits by ~1e-3 and the routing weights by ~1e-3 while the routing itself stays identical.
-@pytest.mark.parametrize("kv,gate,wtol", [("f32", 1e-5, 1e-5), ("bf16", 2e-3, 5e-3)])
-def test_model_matches_oracle_over_more_than_one_page(gpu_ctx, pool, kv, gate, wtol):
-    """tests/model.rs:252-281 on the reference's tiny model (70 positions: two KV pages, two attention tiles)."""
+# f32 KV: the reference's gate (tests/model.rs:268) on the logits; the routing weights are a softmax of router
+# logits whose f32 sums run in another order on each side (the fused step reduces one share per CTA), which moves
+# them by up to a few 1e-5.  bf16 KV rounds every cached K/V element (2^-9 relative), which moves logits by ~1e-3
+# and the routing weights by ~1e-3 while the routing itself stays identical.
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "chain"])
+@pytest.mark.parametrize("kv,gate,wtol", [("f32", 1e-5, 5e-5), ("bf16", 2e-3, 5e-3)])
+def test_model_matches_oracle_over_more_than_one_page(gpu_ctx, pool, kv, gate, wtol, fused):
+    """tests/model.rs:252-281 on the reference's tiny model (70 positions: two KV pages, two attention tiles), for the
+    fused step kernel and for the per-layer kernel chain."""
     cfg = CFG.TINY
     w = reference_tiny_weights(cfg)
     steps = 70
-    m = gpu_model(gpu_ctx, cfg, w, 128, kv)
+    m = gpu_model(gpu_ctx, cfg, w, 128, kv, fused)
     om = O.Model(cfg, weights=w)
     s = O.Session(om, pool, 128)
     toks = toks_like_reference(steps, cfg["vocab"])
@@ -62,11 +68,12 @@ def test_model_matches_oracle_over_more_than_one_page(gpu_ctx, pool, kv, gate, w
     m.close()
 
 
-def test_model_768_hidden_matches_oracle(gpu_ctx, pool):
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "chain"])
+def test_model_768_hidden_matches_oracle(gpu_ctx, pool, fused):
     """tests/model.rs:127-157: H = 768 = 3 x 256 (the 3B shape in miniature), 12 heads / 4 KV heads."""
     cfg = CFG.TINY_768
     w = reference_tiny_weights(cfg)
-    m = gpu_model(gpu_ctx, cfg, w, 64)
+    m = gpu_model(gpu_ctx, cfg, w, 64, "f32", fused)
     om = O.Model(cfg, weights=w)
     s = O.Session(om, pool, 64)
     for t in range(12):
@@ -99,17 +106,62 @@ def test_tiny_golden_greedy_and_teacher_forced(gpu_ctx):
 
 
 def test_graph_pdl_and_direct_launches_agree_bitwise(gpu_ctx):
+    """The kernel chain is bitwise the same with and without graphs / PDL; the fused step is bitwise the same with
+    and without a graph, and within the f32 gate of the chain (different summation orders)."""
     cfg = CFG.TINY_768
     w = reference_tiny_weights(cfg)
     m = gpu_model(gpu_ctx, cfg, w, 64, "bf16")
     toks = toks_like_reference(20, cfg["vocab"], seed=5)
     runs = []
     for graphs, pdl in ((True, True), (False, True), (False, False), (True, False)):
-        m.set_options(graphs, pdl)
+        m.set_options(graphs, pdl, fused=False)
         m.reset()
         runs.append(np.stack([m.step(t)[0] for t in toks]))
     for r in runs[1:]:
         assert np.array_equal(r, runs[0])
+    fused = []
+    for graphs in (True, False):
+        m.set_options(graphs, True, fused=True)
+        assert m.fused
+        m.reset()
+        fused.append(np.stack([m.step(t)[0] for t in toks]))
+    assert np.array_equal(fused[0], fused[1])
+    for t in range(len(toks)):
+        assert rel_l2(fused[0][t], runs[0][t]) < 1e-5, f"position {t}"
+    m.close()
+
+
+@pytest.mark.parametrize("kv,n", [("f32", 5000), ("bf16", 9600)])
+def test_fused_long_context_stages_kv_in_chunks(gpu_ctx, pool, kv, n):
+    """A context longer than one staged K/V chunk per attention unit (74 splits x kv_cap rows on the tiny model):
+    the fused kernel loads the remaining chunks inside the attention phase.  Prefill by greedy steps on both sides,
+    then logits compared with the oracle (f32 KV) or the kernel chain (bf16 KV, the oracle keeps f32 K/V)."""
+    cfg = CFG.TINY
+    w = reference_tiny_weights(cfg)
+    m = gpu_model(gpu_ctx, cfg, w, n + 8, kv, True)
+    toks = toks_like_reference(n, cfg["vocab"], seed=11)
+    m.generate(toks, 1)
+    if kv == "f32":
+        om = O.Model(cfg, weights=w)
+        s = O.Session(om, pool, n + 8)
+        for t in toks:
+            s.step(t)
+        for tok in (3, 17, 29):
+            lg, _, ids, _ = m.step(tok)
+            lo, io, _ = s.step(tok)
+            assert rel_l2(lg, lo) < 1e-4, f"{rel_l2(lg, lo):.2e}"
+            assert np.array_equal(ids, io)
+        s.close()
+        om.close()
+    else:
+        ref = gpu_model(gpu_ctx, cfg, w, n + 8, kv, False)
+        ref.generate(toks, 1)
+        for tok in (3, 17, 29):
+            lg, _, ids, _ = m.step(tok)
+            lr, _, ir, _ = ref.step(tok)
+            assert rel_l2(lg, lr) < 1e-4, f"{rel_l2(lg, lr):.2e}"
+            assert np.array_equal(ids, ir)
+        ref.close()
     m.close()
 
 
@@ -155,26 +207,32 @@ def test_errors_refused_before_launch_and_model_stays_usable(gpu_ctx):
     m.close()
 
 
-def test_c2_1b_greedy_matches_transformers_golden(gpu_ctx):
+@pytest.mark.parametrize("fused", [False, True], ids=["chain", "fused"])
+def test_c2_1b_greedy_matches_transformers_golden(gpu_ctx, fused):
     """BASELINE config 1 at full size: 128-token prompt, 128 greedy ids vs transformers."""
     g = np.load(os.path.join(GOLDEN, "c2_greedy.npz"))
     c = CFG.C2_1B
     cfg = c["model"]
     m = LB.GpuModel(gpu_ctx, cfg, 320, kv_dtype="bf16")
     m.fill_synthetic(c["weight_seed"], CFG.WEIGHT_STD, 0.0)
+    m.set_options(fused=fused)
+    assert m.fused == fused
     out = m.generate(g["prompt"], len(g["generated"]))
     for i, (a, b) in enumerate(zip(out, g["generated"])):
         assert a == b or g["gaps"][i] < TIE_GAP, f"step {i}: {a} vs {b}"
     m.close()
 
 
-def test_c3_3b_logits_match_oracle_at_full_size(gpu_ctx, pool):
+@pytest.mark.parametrize("fused", [False, True], ids=["chain", "fused"])
+def test_c3_3b_logits_match_oracle_at_full_size(gpu_ctx, pool, fused):
     """BASELINE config 2 shape (Granite-3B, 32 layers, E 40): device-filled weights are bit-identical to the
     oracle's, so logits and routing can be compared at full size for a short sequence."""
     c = CFG.C3_3B
     cfg = c["model"]
     m = LB.GpuModel(gpu_ctx, cfg, 64, kv_dtype="f32")
     m.fill_synthetic(c["weight_seed"], CFG.WEIGHT_STD, 0.1)
+    m.set_options(fused=fused)
+    assert m.fused == fused  # the 3B shape fits the fused step kernel
     om = O.Model(cfg, synthetic_seed=c["weight_seed"], std=CFG.WEIGHT_STD, norm_std=0.1, threads=os.cpu_count() or 8)
     s = O.Session(om, pool, 64)
     toks = S.tokens(6, c["prompt_seed"], cfg["vocab"])
@@ -192,13 +250,20 @@ def test_profile_direct_launches_report_every_kernel(gpu_ctx):
     """lastro_model_profile: direct launches with an event between kernels, after a synthetic context."""
     cfg = CFG.TINY_768
     w = reference_tiny_weights(cfg)
-    m = gpu_model(gpu_ctx, cfg, w, 400, "bf16")
+    m = gpu_model(gpu_ctx, cfg, w, 400, "bf16", False)
     m.fill_kv_synthetic(300)
     prof = m.profile(3)
     assert m.pos == 303
     for k in ("qkv_rope", "attention", "oproj", "gate_up", "down", "head"):
         assert prof[k] > 0.0, k
     assert prof["router"] == 0.0  # folded into oproj
+    assert prof["fused_step"] == 0.0
+    m.set_options(fused=True)
+    assert m.fused
+    prof = m.profile(2)
+    assert m.pos == 305
+    assert prof["fused_step"] > 0.0
+    assert all(v == 0.0 for k, v in prof.items() if k != "fused_step")
     lg, _, _, _ = m.step(5)
     assert np.isfinite(lg).all()
     m.close()
