@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
     __shared__ float wm[NW][G], wl[NW][G];
     __shared__ __align__(16) float wacc[NW][G][D];
     __shared__ __align__(8) uint64_t bar;
-    __shared__ float cw[kAttnSplits][G], cl[kAttnSplits][G], cden[G];
+    __shared__ float cw[kAttnSplits][G], cden[G];
     __shared__ bool is_last;
     const int NS = gridDim.x, s = blockIdx.x, kvh = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -300,38 +300,46 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
             a.part_ml[hs * 2 + 1] = L;
         }
     }
-    // the last CTA of this KV head merges the NS splits of its G heads; all loads of a thread in one batch
+    // the last CTA of this KV head merges the NS splits of its G heads: every load (each thread's NS partial outputs,
+    // and one (m, l) pair per (head, split)) in one round, the per-head max and denominator by 16-lane shuffles
+    static_assert(kAttnSplits == 16, "the merge reduces one head's splits within 16 lanes");
     if (!last_block_arrives(a.counters + kvh, (unsigned int)NS, &is_last)) return;
-    const float2* ml = reinterpret_cast<const float2*>(a.part_ml) + (size_t)kvh * G * NS;
-    for (int i = threadIdx.x; i < G * NS; i += blockDim.x) {
-        const float2 t = __ldcg(ml + i);
-        cw[i % NS][i / NS] = t.x;
-        cl[i % NS][i / NS] = t.y;
-    }
-    __syncthreads();
-    if (threadIdx.x < G) {
-        const int g = threadIdx.x;
-        float M = -INFINITY;
-        for (int sp = 0; sp < NS; ++sp) M = fmaxf(M, cw[sp][g]);
-        float den = 0.0f;
-        for (int sp = 0; sp < NS; ++sp) {
-            const float e = cw[sp][g] == -INFINITY ? 0.0f : expf(cw[sp][g] - M);
-            den = fmaf(cl[sp][g], e, den);
-            cw[sp][g] = e;
-        }
-        cden[g] = den;
-    }
-    __syncthreads();
-    const float* pa = a.part_acc + (size_t)kvh * G * NS * D;
-    for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
-        const int g = t / D, dim = t - (t / D) * D;
-        float v[kAttnSplits];
+    constexpr int NT = 32 * kAttnWarps, KO = (G * D + NT - 1) / NT;
+    const float* pa = a.part_acc + (size_t)kvh * G * kAttnSplits * D;
+    float v[KO][kAttnSplits];
 #pragma unroll
-        for (int sp = 0; sp < kAttnSplits; ++sp) v[sp] = sp < NS ? __ldcg(pa + ((size_t)g * NS + sp) * D + dim) : 0.0f;
-        float num = 0.0f;
+    for (int k = 0; k < KO; ++k) {
+        const int t = threadIdx.x + k * NT;
+        const int g = t / D, dim = t - (t / D) * D;
 #pragma unroll
         for (int sp = 0; sp < kAttnSplits; ++sp)
-            if (sp < NS) num = fmaf(v[sp], cw[sp][g], num);
+            v[k][sp] = t < G * D ? __ldcg(pa + ((size_t)g * kAttnSplits + sp) * D + dim) : 0.0f;
+    }
+    const int i = threadIdx.x;
+    const float2 mlv = i < G * kAttnSplits ? __ldcg(reinterpret_cast<const float2*>(a.part_ml) + (size_t)kvh * G * kAttnSplits + i)
+                                           : make_float2(-INFINITY, 0.0f);
+    if (i < ((G * kAttnSplits + 31) & ~31)) {  // whole warps
+        float M = mlv.x;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o, 16));
+        const float e = mlv.x == -INFINITY ? 0.0f : expf(mlv.x - M);
+        float dn = mlv.y * e;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) dn += __shfl_xor_sync(0xffffffffu, dn, o, 16);
+        if (i < G * kAttnSplits) {
+            cw[i % kAttnSplits][i / kAttnSplits] = e;
+            if (i % kAttnSplits == 0) cden[i / kAttnSplits] = dn;
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < KO; ++k) {
+        const int t = threadIdx.x + k * NT;
+        if (t >= G * D) break;
+        const int g = t / D, dim = t - (t / D) * D;
+        float num = 0.0f;
+#pragma unroll
+        for (int sp = 0; sp < kAttnSplits; ++sp) num = fmaf(v[k][sp], cw[sp][g], num);
         a.att_out[((size_t)kvh * G + g) * D + dim] = num / cden[g];
     }
 }
