@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--profile-only", action="store_true", help="small run for ncu: synthetic KV + 3 decode steps")
     ap.add_argument("--synthetic-kv", action="store_true", help="fill the context with synthetic K/V instead of "
                     "decoding the prompt through the model")
+    ap.add_argument("--layers", type=int, default=0, help="with --profile-only: a 3B-shaped model with this many "
+                    "layers (small ncu captures; the kernels are those of the full model)")
     ap.add_argument("--fused", action="store_true", help="the fused step kernel (one persistent launch per step) instead "
                     "of the per-layer kernel chain")
     return ap.parse_args()
@@ -194,6 +196,9 @@ def main():
 
     c = CFG.C3_3B
     cfg = c["model"]
+    if a.layers:
+        assert a.profile_only, "--layers is for profiling captures only"
+        cfg = dict(cfg, layers=a.layers)
     K, W = a.steps, a.warmup
     if a.profile_only:
         K, W = 2, 1
