@@ -1,9 +1,11 @@
 #!/usr/bin/env python3
-"""Batch-1 greedy decode of the Granite-3B-A800M-shaped MoE model on B200 (BASELINE config 2).
+"""Batch-1 greedy decode of the Granite-3B-A800M-shaped MoE model on B200.
 
-Workload: 32 layers, hidden 1536, 24 q / 8 kv heads (d 64), 40 experts top-8 (I 512), vocab 49155, random-init
-bf16 weights (synthetic generator, seed 2, std 0.02), KV cache pre-filled to 2048 positions by decoding 2048
-uniform random ids (seed 2) through the model itself, then greedy decode.  One bench step = one decoded token.
+Workload (default, --workload c3): 32 layers, hidden 1536, 24 q / 8 kv heads (d 64), 40 experts top-8 (I 512),
+vocab 49155, random-init bf16 weights (synthetic generator, seed 2, std 0.02), KV cache pre-filled to 2048 positions
+by decoding 2048 uniform random ids (seed 2) through the model itself, then greedy decode.  One bench step = one
+decoded token.  --workload c4: the same architecture with every linear weight Q8_0 (int8 ~U[-127,127] and one fp16
+scale ~U(1e-4, 4e-3) per 32 values; embedding bf16), seeds 4, context 512.
 
   value  device-resident throughput: K graph-replayed decode steps, the token fed back on the device, timed with
          CUDA events on the library's stream (max over ranks; every rank decodes its own replica: batch-1 decode
@@ -34,6 +36,12 @@ sys.path.insert(0, os.path.join(ROOT, "lastro-rust_b200"))
 from lastro_b200 import configs as CFG  # noqa: E402
 
 KERNELS = ("qkv_rope", "attention", "oproj", "router", "gate_up", "down", "head", "fused_step")
+WORKLOADS = {"c3": CFG.C3_3B, "c4": CFG.C4_3B_Q8}
+
+
+def metric_name(c, context):
+    q8 = c["model"].get("weight_dtype") == "q8_0"
+    return f"decode tok/s (bs1) Granite-3B-A800M shape{' Q8_0' if q8 else ''}, ctx {context}"
 
 
 def parse():
@@ -42,7 +50,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", choices=("lastro", "reference"), default="lastro")
-    ap.add_argument("--context", type=int, default=CFG.C3_3B["context"])
+    ap.add_argument("--workload", choices=tuple(WORKLOADS), default="c3",
+                    help="c3: bf16 weights, ctx 2048 (the headline); c4: Q8_0 weights, ctx 512")
+    ap.add_argument("--context", type=int, default=None, help="context length (default: the workload's)")
     ap.add_argument("--kv", choices=("bf16", "f32"), default="bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample")
@@ -53,7 +63,10 @@ def parse():
                     "layers (small ncu captures; the kernels are those of the full model)")
     ap.add_argument("--fused", action="store_true", help="the fused step kernel (one persistent launch per step) instead "
                     "of the per-layer kernel chain")
-    return ap.parse_args()
+    a = ap.parse_args()
+    if a.context is None:
+        a.context = WORKLOADS[a.workload]["context"]
+    return a
 
 
 def peaks():
@@ -65,11 +78,14 @@ def peaks():
 
 
 def kernel_bytes(cfg, context):
-    """Algorithmic HBM bytes of one launch of each kernel (bf16 weights, bf16 KV), at the given mean context."""
+    """Algorithmic HBM bytes of one launch of each kernel (bf16 or Q8_0 linear weights, bf16 KV and embedding), at
+    the given mean context."""
     H, I, E, k, V = cfg["hidden"], cfg["inter"], cfg["experts"], cfg["k"], cfg["vocab"]
     qd, kvd = cfg["heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
-    kb = dict(qkv_rope=(qd + 2 * kvd) * H * 2 + 2 * kvd * 2, attention=2 * kvd * 2 * context,
-              oproj=H * qd * 2 + H * E * 4, router=0, gate_up=k * 2 * I * H * 2, down=k * H * I * 2, head=V * H * 2)
+    wb = CFG.weight_bytes(cfg)
+    kb = dict(qkv_rope=(qd + 2 * kvd) * H * wb + 2 * kvd * 2, attention=2 * kvd * 2 * context,
+              oproj=H * qd * wb + H * E * 4, router=0, gate_up=k * 2 * I * H * wb, down=k * H * I * wb,
+              head=V * H * 2)
     # the fused step kernel moves every layer's bytes and the head's in one launch
     kb["fused_step"] = cfg["layers"] * sum(kb[n] for n in ("qkv_rope", "attention", "oproj", "gate_up", "down")) + kb["head"]
     return kb
@@ -159,14 +175,16 @@ def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    cfg = CFG.C3_3B["model"]
-    rate, threads, n, sample = cpu_decode_rate(cfg, a.context, CFG.C3_3B["weight_seed"], 0, steps=a.steps,
+    c = WORKLOADS[a.workload]
+    cfg = c["model"]
+    rate, threads, n, sample = cpu_decode_rate(cfg, a.context, c["weight_seed"], 0, steps=a.steps,
                                                warmup=min(a.warmup, 2))
     line = {
-        "impl": "reference", "metric": "decode tok/s (bs1) Granite-3B-A800M shape, ctx 2048", "value": rate,
+        "impl": "reference", "metric": metric_name(c, a.context), "value": rate,
         "unit": "tok/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1000.0 / rate,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": CFG.C3_3B["name"], "context": a.context, "batch": 1},
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": cfg.get("weight_dtype", "bf16"), "data": "synthetic",
+        "config": {"workload": c["name"], "context": a.context, "batch": 1},
         "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference (Rust + cuTile, rust/moe-rt) cannot be built here; its CPU path is timed through the "
@@ -194,8 +212,9 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
 
-    c = CFG.C3_3B
+    c = WORKLOADS[a.workload]
     cfg = c["model"]
+    q8 = cfg.get("weight_dtype") == "q8_0"
     if a.layers:
         assert a.profile_only, "--layers is for profiling captures only"
         cfg = dict(cfg, layers=a.layers)
@@ -289,15 +308,18 @@ def main():
     B = CFG.bytes_per_token(cfg, mean_ctx)
     step_s = ms / 1000.0 / K
     line = {
-        "metric": "decode tok/s (bs1) Granite-3B-A800M shape, ctx 2048", "value": value, "unit": "tok/s",
+        "metric": metric_name(c, a.context), "value": value, "unit": "tok/s",
         "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": "q8_0" if q8 else "bf16", "data": "synthetic",
         "config": {"workload": c["name"], "batch": 1, "context_start": ctx0, "mean_context": mean_ctx,
-                   "kv_cache": f"paged {a.kv}", "weights": "bf16, activations/accumulators f32",
+                   "kv_cache": f"paged {a.kv}",
+                   "weights": ("Q8_0 linears (int8 + fp16 scale per 32, dequantised in registers), bf16 embedding"
+                               if q8 else "bf16") + ", activations/accumulators f32",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "step_kernel": "fused: one persistent cooperative launch per step" if fused else
                    "chain: 5 kernels per layer + head, PDL, CUDA graph",
-                   "l2": "inputs larger than L2: every step streams ~1.9 GB of weights and KV (L2 126 MB)",
+                   "l2": f"inputs larger than L2: every step streams ~{B['full'] / 1e9:.1f} GB of weights and KV "
+                         "(L2 126 MB)",
                    "prefill_s": round(prefill_s, 2)},
         "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": traffic,

@@ -34,6 +34,10 @@ extern "C" {
 
 #define LASTRO_DTYPE_BF16 1
 #define LASTRO_DTYPE_F32 2
+/* Q8_0 (no reference implementation): along each row, blocks of 32 weights stored as 34 bytes --
+ * the block's fp16 scale, then 32 int8 values; weight = scale * value.  A model created with weight_dtype Q8_0 takes
+ * every linear weight (q/k/v/o projections, router, experts) in this layout; embeddings stay bf16, norms bf16/f32. */
+#define LASTRO_DTYPE_Q8_0 3
 
 typedef struct lastro_ctx lastro_ctx;
 typedef struct lastro_layer lastro_layer;
@@ -43,7 +47,7 @@ typedef struct lastro_model lastro_model;
 typedef struct {
     int32_t hidden, inter, layers, heads, kv_heads, head_dim, vocab, experts, k;
     float rope_theta, eps, embedding_multiplier, residual_multiplier, attention_multiplier, logits_scaling;
-    int32_t weight_dtype; /* LASTRO_DTYPE_BF16 */
+    int32_t weight_dtype; /* LASTRO_DTYPE_BF16 or LASTRO_DTYPE_Q8_0 (linear weights) */
     int32_t kv_dtype;     /* LASTRO_DTYPE_BF16 (paged bf16 KV) or LASTRO_DTYPE_F32 */
 } lastro_model_desc;
 
@@ -61,6 +65,12 @@ const char *lastro_version(void);
 /* GpuLayer::upload (gpu.rs:430-449): copies router [E,H], gate_up [E,2I,H], down [E,H,I] (bf16 bits) to the device */
 int lastro_layer_create(lastro_ctx *ctx, int32_t experts, int32_t hidden, int32_t inter, int32_t k,
                         const uint16_t *router, const uint16_t *gate_up, const uint16_t *down, lastro_layer **out);
+/* GpuLayer::upload for Q8_0 weights (the reference's GpuLayer is bf16 only; its north star adds Q8_0): router [E,H],
+ * gate_up [E,2I,H], down [E,H,I] given as rows of 34-byte blocks (fp16 scale, then 32 int8 values; weight = scale *
+ * value), repacked on upload into the device row layout; H and I multiples of 32.  forward/add_into/destroy as for
+ * bf16 layers. */
+int lastro_layer_create_q8_0(lastro_ctx *ctx, int32_t experts, int32_t hidden, int32_t inter, int32_t k,
+                             const uint8_t *router, const uint8_t *gate_up, const uint8_t *down, lastro_layer **out);
 /* GpuLayer::forward (gpu.rs:461-478): x [H] host in -> y [H] host out, the routing (ids/weights [k], in
  * descending-logit order) and optionally the router logits [E]; any output pointer may be NULL */
 int lastro_layer_forward(lastro_layer *layer, const float *x, float *y, int32_t *ids, float *weights,

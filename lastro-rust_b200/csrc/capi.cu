@@ -157,9 +157,10 @@ extern "C" const char* lastro_last_error(const lastro_ctx* c) { return c ? c->er
 struct lastro_layer {
     lastro_ctx* ctx = nullptr;
     int E = 0, H = 0, I = 0, k = 0;
+    int q8 = 0;  // weights are Q8_0 rows in the device layout (wrow_bytes)
     bool poisoned = false;
     Arena arena;
-    uint16_t *router = nullptr, *gate_up = nullptr, *down = nullptr;
+    unsigned char *router = nullptr, *gate_up = nullptr, *down = nullptr;
     float *x = nullptr, *y = nullptr, *logits = nullptr, *weights = nullptr, *a = nullptr;
     int* ids = nullptr;
     unsigned int* counter = nullptr;
@@ -168,7 +169,7 @@ struct lastro_layer {
 
 namespace {
 
-int check_block_shape(lastro_ctx* c, int E, int H, int I, int k) {
+int check_block_shape(lastro_ctx* c, int E, int H, int I, int k, int q8 = 0) {
     if (E < 1 || H < 8 || I < 8 || k < 1) return set_err(c, LASTRO_E_ARG, "block shape E=%d H=%d I=%d k=%d", E, H, I, k);
     if (k > E) return set_err(c, LASTRO_E_ARG, "k=%d > experts=%d", k, E);
     if (H % 8 || I % 8) return set_err(c, LASTRO_E_UNSUPPORTED, "H=%d and I=%d must be multiples of 8", H, I);
@@ -178,7 +179,8 @@ int check_block_shape(lastro_ctx* c, int E, int H, int I, int k) {
     if (I % gate_up_rows_per_cta() || H % down_rows_per_cta())
         return set_err(c, LASTRO_E_UNSUPPORTED, "I=%d must be a multiple of %d and H=%d of %d", I, gate_up_rows_per_cta(),
                        H, down_rows_per_cta());
-    if (down_smem(H, I, k) > kMaxSmemBytes || gate_up_smem(H) > kMaxSmemBytes)
+    if (q8 && (H % 32 || I % 32)) return set_err(c, LASTRO_E_UNSUPPORTED, "Q8_0: H=%d and I=%d must be multiples of 32", H, I);
+    if (down_smem(H, I, k, q8) > kMaxSmemBytes || gate_up_smem(H, q8) > kMaxSmemBytes)
         return set_err(c, LASTRO_E_UNSUPPORTED, "k=%d, I=%d, H=%d: expert tiles exceed shared memory", k, I, H);
     return LASTRO_OK;
 }
@@ -205,6 +207,7 @@ int enqueue_block(lastro_layer* obj, const float* xn, float* out, float resid, i
     ra.x = xn;
     ra.norm_mode = 0;
     ra.w = obj->router;
+    ra.q8 = obj->q8;
     ra.logits = obj->logits;
     ra.ids = obj->ids;
     ra.weights = obj->weights;
@@ -217,6 +220,7 @@ int enqueue_block(lastro_layer* obj, const float* xn, float* out, float resid, i
     ga.x = xn;
     ga.ids = obj->ids;
     ga.w = obj->gate_up;
+    ga.q8 = obj->q8;
     ga.a = obj->a;
     ga.err = obj->err;
     ga.H = obj->H;
@@ -229,6 +233,7 @@ int enqueue_block(lastro_layer* obj, const float* xn, float* out, float resid, i
     da.ids = obj->ids;
     da.weights = obj->weights;
     da.w = obj->down;
+    da.q8 = obj->q8;
     da.out = out;
     da.resid = resid;
     da.accumulate = accumulate;
@@ -243,12 +248,28 @@ int enqueue_block(lastro_layer* obj, const float* xn, float* out, float resid, i
 
 }  // namespace
 
-extern "C" int lastro_layer_create(lastro_ctx* ctx, int32_t E, int32_t H, int32_t I, int32_t k, const uint16_t* router,
-                                   const uint16_t* gate_up, const uint16_t* down, lastro_layer** out) {
+namespace {
+
+// Q8_0 host rows (blocks of 34 bytes: fp16 scale, then 32 int8 values) -> the device row layout (wrow_bytes: the
+// row's int8 values, then its fp16 scales, padded to 16 bytes)
+std::vector<unsigned char> repack_q8_rows(const unsigned char* src, size_t rows, int cols) {
+    const size_t nb = (size_t)cols / 32, rb = wrow_bytes(cols, 1);
+    std::vector<unsigned char> buf(rows * rb, 0);
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t b = 0; b < nb; ++b) {
+            const unsigned char* blk = src + (r * nb + b) * 34;
+            memcpy(&buf[r * rb + (size_t)cols + 2 * b], blk, 2);
+            memcpy(&buf[r * rb + 32 * b], blk + 2, 32);
+        }
+    return buf;
+}
+
+int layer_create(lastro_ctx* ctx, int E, int H, int I, int k, int q8, const void* router, const void* gate_up,
+                 const void* down, lastro_layer** out) {
     if (!ctx || !out) return LASTRO_E_ARG;
     *out = nullptr;
     if (!router || !gate_up || !down) return set_err(ctx, LASTRO_E_ARG, "null weight pointer");
-    int rc = check_block_shape(ctx, E, H, I, k);
+    int rc = check_block_shape(ctx, E, H, I, k, q8);
     if (rc) return rc;
     cudaSetDevice(ctx->device);
     lastro_layer* obj = new lastro_layer();
@@ -257,8 +278,10 @@ extern "C" int lastro_layer_create(lastro_ctx* ctx, int32_t E, int32_t H, int32_
     obj->H = H;
     obj->I = I;
     obj->k = k;
+    obj->q8 = q8;
     Arena& A = obj->arena;
-    const size_t nr = (size_t)E * H, ngu = (size_t)E * 2 * I * H, nd = (size_t)E * H * I;
+    const size_t rbh = wrow_bytes(H, q8), rbi = wrow_bytes(I, q8);
+    const size_t nr = (size_t)E * rbh, ngu = (size_t)E * 2 * I * rbh, nd = (size_t)E * H * rbi;  // bytes
     if (A.alloc(&obj->router, nr) || A.alloc(&obj->gate_up, ngu) || A.alloc(&obj->down, nd) || A.alloc(&obj->x, H) ||
         A.alloc(&obj->y, H) || A.alloc(&obj->logits, E) || A.alloc(&obj->weights, k) || A.alloc(&obj->a, (size_t)k * I) ||
         A.alloc(&obj->ids, k) || A.alloc(&obj->counter, 1) || A.alloc(&obj->err, 1)) {
@@ -267,9 +290,22 @@ extern "C" int lastro_layer_create(lastro_ctx* ctx, int32_t E, int32_t H, int32_
         delete obj;
         return set_err(ctx, LASTRO_E_NOMEM, "layer allocation failed");
     }
-    cudaError_t e = cudaMemcpyAsync(obj->router, router, nr * 2, cudaMemcpyHostToDevice, ctx->stream);
-    if (!e) e = cudaMemcpyAsync(obj->gate_up, gate_up, ngu * 2, cudaMemcpyHostToDevice, ctx->stream);
-    if (!e) e = cudaMemcpyAsync(obj->down, down, nd * 2, cudaMemcpyHostToDevice, ctx->stream);
+    cudaError_t e = cudaSuccess;
+    if (q8) {
+        const auto* r8 = static_cast<const unsigned char*>(router);
+        const auto* g8 = static_cast<const unsigned char*>(gate_up);
+        const auto* d8 = static_cast<const unsigned char*>(down);
+        const std::vector<unsigned char> br = repack_q8_rows(r8, E, H), bg = repack_q8_rows(g8, (size_t)E * 2 * I, H),
+                                         bd = repack_q8_rows(d8, (size_t)E * H, I);
+        e = cudaMemcpyAsync(obj->router, br.data(), nr, cudaMemcpyHostToDevice, ctx->stream);
+        if (!e) e = cudaMemcpyAsync(obj->gate_up, bg.data(), ngu, cudaMemcpyHostToDevice, ctx->stream);
+        if (!e) e = cudaMemcpyAsync(obj->down, bd.data(), nd, cudaMemcpyHostToDevice, ctx->stream);
+        if (!e) e = cudaStreamSynchronize(ctx->stream);  // the staging vectors die with this scope
+    } else {
+        e = cudaMemcpyAsync(obj->router, router, nr, cudaMemcpyHostToDevice, ctx->stream);
+        if (!e) e = cudaMemcpyAsync(obj->gate_up, gate_up, ngu, cudaMemcpyHostToDevice, ctx->stream);
+        if (!e) e = cudaMemcpyAsync(obj->down, down, nd, cudaMemcpyHostToDevice, ctx->stream);
+    }
     if (!e) e = cudaMemsetAsync(obj->counter, 0, sizeof(unsigned int), ctx->stream);
     if (!e) e = cudaMemsetAsync(obj->ids, 0, sizeof(int) * k, ctx->stream);
     if (!e) e = cudaMemsetAsync(obj->err, 0, sizeof(int), ctx->stream);
@@ -284,6 +320,19 @@ extern "C" int lastro_layer_create(lastro_ctx* ctx, int32_t E, int32_t H, int32_
     ctx_retain(ctx);
     *out = obj;
     return LASTRO_OK;
+}
+
+}  // namespace
+
+extern "C" int lastro_layer_create(lastro_ctx* ctx, int32_t E, int32_t H, int32_t I, int32_t k, const uint16_t* router,
+                                   const uint16_t* gate_up, const uint16_t* down, lastro_layer** out) {
+    return layer_create(ctx, E, H, I, k, 0, router, gate_up, down, out);
+}
+
+extern "C" int lastro_layer_create_q8_0(lastro_ctx* ctx, int32_t E, int32_t H, int32_t I, int32_t k,
+                                        const uint8_t* router, const uint8_t* gate_up, const uint8_t* down,
+                                        lastro_layer** out) {
+    return layer_create(ctx, E, H, I, k, 1, router, gate_up, down, out);
 }
 
 extern "C" int lastro_layer_forward(lastro_layer* obj, const float* x, float* y, int32_t* ids, float* weights,
@@ -348,7 +397,8 @@ struct LayerDev {
     float *ln_attn = nullptr, *ln_moe = nullptr;
     float* wr_t = nullptr;  // [H, E] router weight x ln_moe, transposed (fused router operand)
     bool fold_dirty = true;
-    uint16_t *wqkv = nullptr, *wo = nullptr, *router = nullptr, *gate_up = nullptr, *down = nullptr;
+    // linear weights: bf16 rows, or Q8_0 rows in the device layout (wrow_bytes): byte buffers either way
+    unsigned char *wqkv = nullptr, *wo = nullptr, *router = nullptr, *gate_up = nullptr, *down = nullptr;
     void *k_pool = nullptr, *v_pool = nullptr;
 };
 
@@ -360,6 +410,7 @@ struct lastro_model {
     lastro_ctx* ctx = nullptr;
     lastro_model_desc d{};
     int max_len = 0, qd = 0, kvd = 0, G = 1, max_pages = 0, head_grid = 1;
+    int q8 = 0;  // linear weights are Q8_0
     bool poisoned = false;
     bool use_graphs = true, use_pdl = true;
     Arena arena;
@@ -511,6 +562,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         qa.embed_mode = (l == 0);
         qa.ln = L.ln_attn;
         qa.w = L.wqkv;
+        qa.q8 = m->q8;
         qa.rope_cs = m->rope_cs;
         qa.pos = m->d_pos;
         qa.q_out = m->q;
@@ -553,6 +605,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         OprojArgs oa{};
         oa.att = m->att;
         oa.w = L.wo;
+        oa.q8 = m->q8;
         oa.h = m->h;
         oa.resid = d.residual_multiplier;
         oa.H = d.hidden;
@@ -577,6 +630,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         ga.ln = L.ln_moe;
         ga.rs = rs;
         ga.w = L.gate_up;
+        ga.q8 = m->q8;
         ga.a = m->a;
         ga.err = m->d_err;
         ga.H = d.hidden;
@@ -590,6 +644,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         da.a = m->a;
         da.rs = rs;
         da.w = L.down;
+        da.q8 = m->q8;
         da.out = m->h;
         da.resid = d.residual_multiplier;
         da.accumulate = 1;
@@ -668,7 +723,8 @@ int check_ready(lastro_model* m) {
     bool any = false;
     for (LayerDev& L : m->L)
         if (L.fold_dirty) {
-            MTRY(launch_router_fold(L.router, L.ln_moe, L.wr_t, m->d.experts, m->d.hidden, m->ctx->stream), "router fold");
+            MTRY(launch_router_fold(L.router, m->q8, L.ln_moe, L.wr_t, m->d.experts, m->d.hidden, m->ctx->stream),
+                 "router fold");
             L.fold_dirty = false;
             any = true;
         }
@@ -702,7 +758,13 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
     int rc = check_block_shape(ctx, d.experts, d.hidden, d.inter, d.k);
     if (rc) return rc;
     if (d.heads * d.head_dim > kMaxHidden) return set_err(ctx, LASTRO_E_UNSUPPORTED, "heads*head_dim > %d", kMaxHidden);
-    if (d.weight_dtype != LASTRO_DTYPE_BF16) return set_err(ctx, LASTRO_E_UNSUPPORTED, "weight dtype %d", d.weight_dtype);
+    if (d.weight_dtype != LASTRO_DTYPE_BF16 && d.weight_dtype != LASTRO_DTYPE_Q8_0)
+        return set_err(ctx, LASTRO_E_UNSUPPORTED, "weight dtype %d", d.weight_dtype);
+    if (d.weight_dtype == LASTRO_DTYPE_Q8_0 && (d.hidden % 32 || d.inter % 32 || (d.heads * d.head_dim) % 32))
+        return set_err(ctx, LASTRO_E_UNSUPPORTED, "Q8_0 needs hidden, inter and heads*head_dim multiples of 32");
+    if (d.weight_dtype == LASTRO_DTYPE_Q8_0 &&
+        (gate_up_smem(d.hidden, 1) > kMaxSmemBytes || down_smem(d.hidden, d.inter, d.k, 1) > kMaxSmemBytes))
+        return set_err(ctx, LASTRO_E_UNSUPPORTED, "Q8_0 expert tiles exceed shared memory");
     if (d.kv_dtype != LASTRO_DTYPE_BF16 && d.kv_dtype != LASTRO_DTYPE_F32)
         return set_err(ctx, LASTRO_E_UNSUPPORTED, "kv dtype %d", d.kv_dtype);
     if (!(d.eps >= 0.0f) || !(d.logits_scaling != 0.0f) || !(d.rope_theta > 0.0f))
@@ -718,6 +780,7 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
     m->qd = d.heads * d.head_dim;
     m->kvd = d.kv_heads * d.head_dim;
     m->G = G;
+    m->q8 = d.weight_dtype == LASTRO_DTYPE_Q8_0;
     m->max_pages = (max_len + kPageSize - 1) / kPageSize;
     m->head_grid = head_grid(d.vocab);
     m->loaded.assign((size_t)(d.layers + 1) * K_COUNT, 0);
@@ -728,9 +791,10 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
     bool bad = A.alloc(&m->embed, V * H) || A.alloc(&m->norm, H);
     for (int l = 0; l < d.layers && !bad; ++l) {
         LayerDev& L = m->L[l];
-        bad = A.alloc(&L.ln_attn, H) || A.alloc(&L.ln_moe, H) || A.alloc(&L.wqkv, (size_t)(m->qd + 2 * m->kvd) * H) ||
-              A.alloc(&L.wo, H * m->qd) || A.alloc(&L.router, E * H) || A.alloc(&L.gate_up, E * 2 * I * H) ||
-              A.alloc(&L.down, E * H * I) || A.alloc(&L.k_pool, kvpool) || A.alloc(&L.v_pool, kvpool) ||
+        const size_t rbh = wrow_bytes((int)H, m->q8), rbq = wrow_bytes(m->qd, m->q8), rbi = wrow_bytes((int)I, m->q8);
+        bad = A.alloc(&L.ln_attn, H) || A.alloc(&L.ln_moe, H) || A.alloc(&L.wqkv, (size_t)(m->qd + 2 * m->kvd) * rbh) ||
+              A.alloc(&L.wo, H * rbq) || A.alloc(&L.router, E * rbh) || A.alloc(&L.gate_up, E * 2 * I * rbh) ||
+              A.alloc(&L.down, E * H * rbi) || A.alloc(&L.k_pool, kvpool) || A.alloc(&L.v_pool, kvpool) ||
               A.alloc(&L.wr_t, E * H);
     }
     bad = bad || A.alloc(&m->rope_cs, (size_t)max_len * d.head_dim) || A.alloc(&m->page_table, m->max_pages) ||
@@ -751,7 +815,7 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
         cudaGetLastError();
         n_sm = 0;
     }
-    if (!bad && n_sm > 0 && coop &&
+    if (!bad && n_sm > 0 && coop && !m->q8 &&
         fused_plan(d.hidden, d.inter, d.experts, d.k, m->qd, m->kvd, d.kv_heads, G, d.vocab,
                    d.kv_dtype == LASTRO_DTYPE_F32, n_sm, &m->flay)) {
         int per_sm = 0;
@@ -798,7 +862,9 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
             if (!e) e = cudaMemsetAsync(w.first, 0, w.second * sizeof(unsigned long long), s);
         for (int l = 0; l < d.layers; ++l) {
             const LayerDev& L = m->L[l];
-            fl.push_back(FusedLayer{L.ln_attn, L.ln_moe, L.wr_t, L.wqkv, L.wo, L.gate_up, L.down, L.k_pool, L.v_pool});
+            fl.push_back(FusedLayer{L.ln_attn, L.ln_moe, L.wr_t, reinterpret_cast<const uint16_t*>(L.wqkv),
+                                    reinterpret_cast<const uint16_t*>(L.wo), reinterpret_cast<const uint16_t*>(L.gate_up),
+                                    reinterpret_cast<const uint16_t*>(L.down), L.k_pool, L.v_pool});
         }
         if (!e) e = cudaMemcpyAsync(m->f_layers, fl.data(), sizeof(FusedLayer) * fl.size(), cudaMemcpyHostToDevice, s);
     }
@@ -869,8 +935,8 @@ extern "C" int lastro_model_load_tensor(lastro_model* m, const char* name, int32
     case K_LN_ATTN: want = {H}; dst = L->ln_attn; is_norm = true; break;
     case K_LN_MOE: want = {H}; dst = L->ln_moe; is_norm = true; break;
     case K_Q: want = {qd, H}; dst = L->wqkv; break;
-    case K_K: want = {kvd, H}; dst = L->wqkv + (size_t)qd * H; break;
-    case K_V: want = {kvd, H}; dst = L->wqkv + (size_t)(qd + kvd) * H; break;
+    case K_K: want = {kvd, H}; dst = L->wqkv + (size_t)qd * wrow_bytes((int)H, m->q8); break;
+    case K_V: want = {kvd, H}; dst = L->wqkv + (size_t)(qd + kvd) * wrow_bytes((int)H, m->q8); break;
     case K_O: want = {H, qd}; dst = L->wo; break;
     case K_ROUTER: want = {E, H}; dst = L->router; break;
     case K_GATE_UP: want = {E, 2 * I, H}; dst = L->gate_up; break;
@@ -898,6 +964,14 @@ extern "C" int lastro_model_load_tensor(lastro_model* m, const char* name, int32
         }
         MTRY(cudaMemcpyAsync(dst, f.data(), n * 4, cudaMemcpyHostToDevice, s), "tensor upload");
         MTRY(cudaStreamSynchronize(s), "tensor upload");
+    } else if (m->q8 && kind != K_EMBED) {
+        // Q8_0 linear: host blocks of 34 bytes (fp16 scale, 32 int8 values) along each row, repacked into the device
+        // row layout (the row's values, then its scales)
+        if (dtype != LASTRO_DTYPE_Q8_0) return set_err(ctx, LASTRO_E_ARG, "tensor %s: dtype %d (Q8_0 expected)", name, dtype);
+        const int cols = (int)want.back();
+        const std::vector<unsigned char> buf = repack_q8_rows(static_cast<const unsigned char*>(host), n / (size_t)cols, cols);
+        MTRY(cudaMemcpyAsync(dst, buf.data(), buf.size(), cudaMemcpyHostToDevice, s), "tensor upload");
+        MTRY(cudaStreamSynchronize(s), "tensor upload");
     } else {
         if (dtype != LASTRO_DTYPE_BF16) return set_err(ctx, LASTRO_E_ARG, "tensor %s: dtype %d (bf16 expected)", name, dtype);
         MTRY(cudaMemcpyAsync(dst, host, n * 2, cudaMemcpyHostToDevice, s), "tensor upload");
@@ -923,13 +997,30 @@ extern "C" int lastro_model_fill_synthetic(lastro_model* m, uint64_t seed, float
         LayerDev& L = m->L[l];
         MTRY(launch_synth_norm_f32(L.ln_attn, H, tensor_seed(seed, l, K_LN_ATTN), nsc, s), "synth");
         MTRY(launch_synth_norm_f32(L.ln_moe, H, tensor_seed(seed, l, K_LN_MOE), nsc, s), "synth");
-        MTRY(launch_synth_bf16(L.wqkv, qd * H, tensor_seed(seed, l, K_Q), sc, 0.0f, s), "synth");
-        MTRY(launch_synth_bf16(L.wqkv + qd * H, kvd * H, tensor_seed(seed, l, K_K), sc, 0.0f, s), "synth");
-        MTRY(launch_synth_bf16(L.wqkv + (qd + kvd) * H, kvd * H, tensor_seed(seed, l, K_V), sc, 0.0f, s), "synth");
-        MTRY(launch_synth_bf16(L.wo, H * qd, tensor_seed(seed, l, K_O), sc, 0.0f, s), "synth");
-        MTRY(launch_synth_bf16(L.router, E * H, tensor_seed(seed, l, K_ROUTER), sc, 0.0f, s), "synth");
-        MTRY(launch_synth_bf16(L.gate_up, E * 2 * I * H, tensor_seed(seed, l, K_GATE_UP), sc, 0.0f, s), "synth");
-        MTRY(launch_synth_bf16(L.down, E * H * I, tensor_seed(seed, l, K_DOWN), sc, 0.0f, s), "synth");
+        if (m->q8) {
+            // int8 ~U[-127, 127], fp16 scales ~U(1e-4, 4e-3), the oracle's generator
+            const size_t rbh = wrow_bytes((int)H, 1);
+            MTRY(launch_synth_q8_0(L.wqkv, qd, (int)H, tensor_seed(seed, l, K_Q), s), "synth");
+            MTRY(launch_synth_q8_0(L.wqkv + qd * rbh, kvd, (int)H, tensor_seed(seed, l, K_K), s), "synth");
+            MTRY(launch_synth_q8_0(L.wqkv + (qd + kvd) * rbh, kvd, (int)H, tensor_seed(seed, l, K_V), s), "synth");
+            MTRY(launch_synth_q8_0(L.wo, H, (int)qd, tensor_seed(seed, l, K_O), s), "synth");
+            MTRY(launch_synth_q8_0(L.router, E, (int)H, tensor_seed(seed, l, K_ROUTER), s), "synth");
+            MTRY(launch_synth_q8_0(L.gate_up, E * 2 * I, (int)H, tensor_seed(seed, l, K_GATE_UP), s), "synth");
+            MTRY(launch_synth_q8_0(L.down, E * H, (int)I, tensor_seed(seed, l, K_DOWN), s), "synth");
+            continue;
+        }
+        uint16_t *wqkv = reinterpret_cast<uint16_t*>(L.wqkv), *wo = reinterpret_cast<uint16_t*>(L.wo);
+        MTRY(launch_synth_bf16(wqkv, qd * H, tensor_seed(seed, l, K_Q), sc, 0.0f, s), "synth");
+        MTRY(launch_synth_bf16(wqkv + qd * H, kvd * H, tensor_seed(seed, l, K_K), sc, 0.0f, s), "synth");
+        MTRY(launch_synth_bf16(wqkv + (qd + kvd) * H, kvd * H, tensor_seed(seed, l, K_V), sc, 0.0f, s), "synth");
+        MTRY(launch_synth_bf16(wo, H * qd, tensor_seed(seed, l, K_O), sc, 0.0f, s), "synth");
+        MTRY(launch_synth_bf16(reinterpret_cast<uint16_t*>(L.router), E * H, tensor_seed(seed, l, K_ROUTER), sc, 0.0f, s),
+             "synth");
+        MTRY(launch_synth_bf16(reinterpret_cast<uint16_t*>(L.gate_up), E * 2 * I * H, tensor_seed(seed, l, K_GATE_UP), sc,
+                               0.0f, s),
+             "synth");
+        MTRY(launch_synth_bf16(reinterpret_cast<uint16_t*>(L.down), E * H * I, tensor_seed(seed, l, K_DOWN), sc, 0.0f, s),
+             "synth");
     }
     MTRY(cudaStreamSynchronize(s), "synth");
     std::fill(m->loaded.begin(), m->loaded.end(), 1);

@@ -39,7 +39,7 @@ cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStrea
 // ------------------------------------------------------------------------------------------------------------------
 // qkv_rope: one warp per row pair (j, j + d/2) of a head, so RoPE's rotate_half partner is in the same warp.
 // ------------------------------------------------------------------------------------------------------------------
-template <int NCH, bool KV_F32>
+template <int NCH, bool KV_F32, bool Q8>
 __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
     constexpr int BLOCK = 128;
     constexpr int NV = Vec<NCH, BLOCK>::NV;
@@ -54,9 +54,11 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
     const int head = pair / half, j = pair - (pair / half) * half;
     const int r0 = head * a.d + j, r1 = r0 + half;
 
-    uint4 w0[NCH], w1[NCH];
-    load_row<NCH>(w0, a.w + (size_t)r0 * a.H, a.H, lane, active);
-    load_row<NCH>(w1, a.w + (size_t)r1 * a.H, a.H, lane, active);
+    const unsigned char* wb = static_cast<const unsigned char*>(a.w);
+    const size_t rbh = wrow_bytes(a.H, Q8);
+    WRow<NCH, Q8> w0, w1;
+    w0.load(wb + (size_t)r0 * rbh, a.H, lane, active);
+    w1.load(wb + (size_t)r1 * rbh, a.H, lane, active);
     float4 ln[NV];
     vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
 
@@ -87,8 +89,8 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
     norm_regs<BLOCK, NV>(v, ln, a.H, a.eps, xs, red);
     if (!active) return;
 
-    const float x1 = warp_sum(row_dot<NCH>(w0, xs, a.H, lane));
-    const float x2 = warp_sum(row_dot<NCH>(w1, xs, a.H, lane));
+    const float x1 = warp_sum(w0.dot(xs, a.H, lane));
+    const float x2 = warp_sum(w1.dot(xs, a.H, lane));
     if (lane != 0) return;
     const float* cs = a.rope_cs + (size_t)pos * a.d;
     const float c = __ldg(cs + j), s = __ldg(cs + half + j);
@@ -344,7 +346,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
     }
 }
 
-template <int NCH>
+template <int NCH, bool Q8>
 __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
     constexpr int BLOCK = 128;
     constexpr int NV = Vec<NCH, BLOCK>::NV;
@@ -357,8 +359,8 @@ __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int e = blockIdx.x * (BLOCK >> 5) + warp;
     const bool active = e < a.E;
-    uint4 w[NCH];
-    load_row<NCH>(w, a.w + (size_t)e * a.H, a.H, lane, active);
+    WRow<NCH, Q8> w;
+    w.load(static_cast<const unsigned char*>(a.w) + (size_t)e * wrow_bytes(a.H, Q8), a.H, lane, active);
     float4 ln[NV];
     if (a.norm_mode) vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
     pdl_wait();
@@ -372,7 +374,7 @@ __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
         copy_to_smem<BLOCK>(a.x, a.H, xs);
     }
     if (active) {
-        const float lg = warp_sum(row_dot<NCH>(w, xs, a.H, lane));
+        const float lg = warp_sum(w.dot(xs, a.H, lane));
         if (lane == 0) a.logits[e] = lg;
     }
     if (!last_block_arrives(a.counter, gridDim.x, &is_last)) return;
@@ -396,7 +398,7 @@ __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
 constexpr int kOpWarps = 16;
 constexpr int kOpRows = 2 * kOpWarps;
 
-template <int NCH>
+template <int NCH, bool Q8>
 __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
     constexpr int BLOCK = 32 * kOpWarps;
     extern __shared__ __align__(16) float smem[];
@@ -406,9 +408,11 @@ __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r0 = blockIdx.x * kOpRows;
     const int ra = r0 + 2 * warp, rb = ra + 1;
-    uint4 wa[NCH], wb[NCH];
-    load_row<NCH>(wa, a.w + (size_t)ra * a.qd, a.qd, lane, ra < a.H);
-    load_row<NCH>(wb, a.w + (size_t)rb * a.qd, a.qd, lane, rb < a.H);
+    const unsigned char* wbase = static_cast<const unsigned char*>(a.w);
+    const size_t rbq = wrow_bytes(a.qd, Q8);
+    WRow<NCH, Q8> wa, wb;
+    wa.load(wbase + (size_t)ra * rbq, a.qd, lane, ra < a.H);
+    wb.load(wbase + (size_t)rb * rbq, a.qd, lane, rb < a.H);
     if (a.route) {
         const int n = kOpRows * a.E;
         for (int t = threadIdx.x; t < n; t += BLOCK) wrs[t] = (r0 + t / a.E < a.H) ? __ldg(a.wr_t + (size_t)r0 * a.E + t) : 0.0f;
@@ -420,8 +424,8 @@ __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
     copy_to_smem<BLOCK>(a.att, a.qd, xs);
     float4 xa[NCH], xb[NCH];
     x_to_regs<NCH>(xs, a.qd, lane, xa, xb);
-    const float oa = warp_sum(row_dot_regs<NCH>(wa, xa, xb, a.qd, lane));
-    const float ob = warp_sum(row_dot_regs<NCH>(wb, xa, xb, a.qd, lane));
+    const float oa = warp_sum(wa.dot_regs(xa, xb, a.qd, lane));
+    const float ob = warp_sum(wb.dot_regs(xa, xb, a.qd, lane));
     if (lane == 0) {
         const float na = __fadd_rn(ha, __fmul_rn(a.resid, oa)), nb = __fadd_rn(hb, __fmul_rn(a.resid, ob));
         if (ra < a.H) a.h[ra] = na;
@@ -445,12 +449,22 @@ __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
     }
 }
 
-// W_r^T scaled by the MoE norm weight, [H, E] f32: the fused router's operand, prepared once per layer
-__global__ void router_fold_kernel(const uint16_t* wr, const float* ln, float* wr_t, int E, int H) {
+// W_r^T scaled by the MoE norm weight, [H, E] f32: the fused router's operand, prepared once per layer (a Q8_0 router
+// weight is scale * value, exact in f32)
+template <bool Q8>
+__global__ void router_fold_kernel(const void* wr, const float* ln, float* wr_t, int E, int H) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= E * H) return;
     const int c = i / E, e = i - (i / E) * E;
-    wr_t[i] = __fmul_rn(__uint_as_float((uint32_t)wr[(size_t)e * H + c] << 16), ln[c]);
+    float w;
+    if (Q8) {
+        const unsigned char* row = static_cast<const unsigned char*>(wr) + (size_t)e * wrow_bytes(H, 1);
+        const float sc = f16_to_f32(reinterpret_cast<const unsigned short*>(row + H)[c >> 5]);
+        w = __fmul_rn(sc, (float)reinterpret_cast<const signed char*>(row)[c]);
+    } else {
+        w = __uint_as_float((uint32_t)static_cast<const uint16_t*>(wr)[(size_t)e * H + c] << 16);
+    }
+    wr_t[i] = __fmul_rn(w, ln[c]);
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -462,15 +476,16 @@ __global__ void router_fold_kernel(const uint16_t* wr, const float* ln, float* w
 // ------------------------------------------------------------------------------------------------------------------
 constexpr int kGuPairs = 16;
 
-template <int NCH>
+template <int NCH, bool Q8>
 __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
     constexpr int BLOCK = 256, R = kGuPairs, HALF = R / 2;
     constexpr int NV = Vec<NCH, BLOCK>::NV;
     static_assert(HALF == BLOCK / 32, "one row pair per warp per stage");
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    uint16_t* wg = reinterpret_cast<uint16_t*>(smem_raw);  // [R, H]
-    uint16_t* wu = wg + (size_t)R * a.H;                    // [R, H]
-    float* xs = reinterpret_cast<float*>(wu + (size_t)R * a.H);
+    const size_t rbh = wrow_bytes(a.H, Q8);  // bytes per weight row
+    unsigned char* wg = smem_raw;             // [R] gate rows
+    unsigned char* wu = wg + (size_t)R * rbh;  // [R] up rows
+    float* xs = reinterpret_cast<float*>(wu + (size_t)R * rbh);
     __shared__ __align__(8) uint64_t bar[2];
     __shared__ float red[BLOCK];
     __shared__ int sid[kMaxTopK];
@@ -500,13 +515,13 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
     if (threadIdx.x == 0) {
         // expert id, clamped so that a stale id can never address outside the weights
         const int e = min(max(fused ? sid[slot] : __ldcg(a.ids + slot), 0), a.E - 1);
-        const uint16_t* base = a.w + (size_t)e * 2 * a.I * a.H;
-        const uint32_t bytes = (uint32_t)(HALF * a.H * 2);
+        const unsigned char* base = static_cast<const unsigned char*>(a.w) + (size_t)e * 2 * a.I * rbh;
+        const uint32_t bytes = (uint32_t)(HALF * rbh);
 #pragma unroll
         for (int st = 0; st < 2; ++st) {
             mbar_expect_tx(&bar[st], 2 * bytes);
-            bulk_g2s(wg + (size_t)st * HALF * a.H, base + (size_t)(j0 + st * HALF) * a.H, bytes, &bar[st]);
-            bulk_g2s(wu + (size_t)st * HALF * a.H, base + (size_t)(a.I + j0 + st * HALF) * a.H, bytes, &bar[st]);
+            bulk_g2s(wg + (size_t)st * HALF * rbh, base + (size_t)(j0 + st * HALF) * rbh, bytes, &bar[st]);
+            bulk_g2s(wu + (size_t)st * HALF * rbh, base + (size_t)(a.I + j0 + st * HALF) * rbh, bytes, &bar[st]);
         }
     }
     if (fused) {
@@ -526,8 +541,8 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
     for (int st = 0; st < 2; ++st) {
         if (!mbar_wait(&bar[st], 0, a.err, 1)) return;
         const int pr = st * HALF + warp;
-        const float g = warp_sum(smem_row_dot<NCH>(wg + (size_t)pr * a.H, xa, xb, a.H, lane));
-        const float u = warp_sum(smem_row_dot<NCH>(wu + (size_t)pr * a.H, xa, xb, a.H, lane));
+        const float g = warp_sum(smem_row_dot_w<NCH, Q8>(wg + (size_t)pr * rbh, xa, xb, a.H, lane));
+        const float u = warp_sum(smem_row_dot_w<NCH, Q8>(wu + (size_t)pr * rbh, xa, xb, a.H, lane));
         if (lane == 0) a.a[(size_t)slot * a.I + j0 + pr] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
     }
 }
@@ -541,12 +556,13 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
 // ------------------------------------------------------------------------------------------------------------------
 constexpr int kDnRows = 8;
 
-template <int NCI>
+template <int NCI, bool Q8>
 __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
     constexpr int BLOCK = 256, R = kDnRows;
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    uint16_t* wd = reinterpret_cast<uint16_t*>(smem_raw);                // [k, R, I]
-    float* part = reinterpret_cast<float*>(wd + (size_t)a.k * R * a.I);  // [k, R]
+    const size_t rbi = wrow_bytes(a.I, Q8);                              // bytes per weight row
+    unsigned char* wd = smem_raw;                                        // [k, R] rows of I weights
+    float* part = reinterpret_cast<float*>(wd + (size_t)a.k * R * rbi);  // [k, R]
     __shared__ __align__(8) uint64_t bar;
     __shared__ float red[BLOCK];
     __shared__ int sid[kMaxTopK];
@@ -558,11 +574,12 @@ __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
     if (fused) route_from_shares<BLOCK>(a.rs, a.E, a.k, a.H, red, sid, sval, sw, &s_r, false);
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
-        const uint32_t bytes = (uint32_t)(R * a.I * 2);
+        const uint32_t bytes = (uint32_t)(R * rbi);
         mbar_expect_tx(&bar, bytes * a.k);
         for (int j = 0; j < a.k; ++j) {
             const int e = min(max(fused ? sid[j] : __ldcg(a.ids + j), 0), a.E - 1);
-            bulk_g2s(wd + (size_t)j * R * a.I, a.w + ((size_t)e * a.H + r0) * a.I, bytes, &bar);
+            bulk_g2s(wd + (size_t)j * R * rbi, static_cast<const unsigned char*>(a.w) + ((size_t)e * a.H + r0) * rbi, bytes,
+                     &bar);
         }
     }
     __syncthreads();  // the barrier is initialized before any thread waits on it
@@ -578,7 +595,7 @@ __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
     if (ok && warp < a.k) {
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-            const float d = warp_sum(smem_row_dot<NCI>(wd + ((size_t)warp * R + r) * a.I, xa, xb, a.I, lane));
+            const float d = warp_sum(smem_row_dot_w<NCI, Q8>(wd + ((size_t)warp * R + r) * rbi, xa, xb, a.I, lane));
             if (lane == 0) part[warp * R + r] = d;
         }
     }
@@ -723,6 +740,48 @@ __global__ void synth_norm_kernel(float* out, size_t n, uint64_t seed, float sca
     }
 }
 
+// Q8_0 synthetic fill (the CPU oracle's lo_synth_q8_0, same integer hash): value of element idx of the row-major
+// matrix uniform in [-127, 127]; block b's fp16 scale = 1e-4 + u * 3.9e-3 with u from 24 hash bits, rounded to nearest
+// even by the same integer routine as the oracle's lo_f32_to_f16
+LDEV uint16_t f32_to_f16_rne(float f) {
+    const uint32_t u = __float_as_uint(f);
+    const uint32_t sign = (u >> 16) & 0x8000u, a = u & 0x7fffffffu;
+    if (a >= 0x47800000u) return (uint16_t)(sign | 0x7c00u);
+    if (a < 0x38800000u) {
+        if (a < 0x33000000u) return (uint16_t)sign;
+        const uint32_t m = (a & 0x7fffffu) | 0x800000u;
+        const int sh = 126 - (int)(a >> 23);
+        uint32_t q = m >> sh;
+        const uint32_t rem = m & ((1u << sh) - 1u), half = 1u << (sh - 1);
+        if (rem > half || (rem == half && (q & 1u))) ++q;
+        return (uint16_t)(sign | q);
+    }
+    const uint32_t r = a - 0x38000000u;
+    uint32_t q = r >> 13;
+    const uint32_t rem = r & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (q & 1u))) ++q;
+    return (uint16_t)(sign | q);
+}
+
+__global__ void synth_q8_values_kernel(unsigned char* out, size_t rows, int cols, uint64_t seed) {
+    const size_t n = rows * (size_t)cols, rb = wrow_bytes(cols, 1);
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i / cols, c = i - r * cols;
+        const int v = (int)(mix64(seed + (i + 1ull) * 0x9E3779B97F4A7C15ull) % 255ull) - 127;
+        out[r * rb + c] = (unsigned char)(signed char)v;
+    }
+}
+
+__global__ void synth_q8_scales_kernel(unsigned char* out, size_t rows, int cols, uint64_t seed) {
+    const size_t nb = (size_t)cols / 32, n = rows * nb, rb = wrow_bytes(cols, 1);
+    for (size_t b = blockIdx.x * (size_t)blockDim.x + threadIdx.x; b < n; b += (size_t)gridDim.x * blockDim.x) {
+        const uint64_t h = mix64((seed ^ 0xA5A5A5A5A5A5A5A5ull) + (b + 1ull) * 0x9E3779B97F4A7C15ull);
+        const float u = __fmul_rn((float)(h >> 40), 1.0f / 16777216.0f);
+        const size_t r = b / nb, j = b - r * nb;
+        reinterpret_cast<uint16_t*>(out + r * rb + cols)[j] = f32_to_f16_rne(__fadd_rn(1e-4f, __fmul_rn(u, 3.9e-3f)));
+    }
+}
+
 int chunks_for(int n) { return (n + 255) / 256; }
 
 }  // namespace
@@ -755,10 +814,16 @@ cudaError_t launch_qkv_rope(const QkvArgs& a, cudaStream_t s, bool pdl) {
     const int npairs = (a.qd + 2 * a.kvd) / 2;
     const dim3 grid((npairs + 3) / 4), block(128);
     const size_t smem = sizeof(float) * (a.H + 32);
-    if (a.kv_f32) {
-        LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(qkv_rope_kernel<N, true>, grid, block, smem, s, pdl, a));
+    if (a.q8) {
+        if (a.kv_f32) {
+            LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(qkv_rope_kernel<N, true, true>, grid, block, smem, s, pdl, a));
+        }
+        LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(qkv_rope_kernel<N, false, true>, grid, block, smem, s, pdl, a));
     }
-    LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(qkv_rope_kernel<N, false>, grid, block, smem, s, pdl, a));
+    if (a.kv_f32) {
+        LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(qkv_rope_kernel<N, true, false>, grid, block, smem, s, pdl, a));
+    }
+    LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(qkv_rope_kernel<N, false, false>, grid, block, smem, s, pdl, a));
 }
 
 int attn_split_cap(int max_len) { return (max_len + kAttnSplits - 1) / kAttnSplits + 1; }
@@ -796,8 +861,9 @@ cudaError_t launch_oproj(const OprojArgs& a, cudaStream_t s, bool pdl) {
     const size_t smem = sizeof(float) * (a.qd + (a.route ? (size_t)kOpRows * a.E : 0));
 #define LASTRO_OP(N)                                                                  \
     {                                                                                 \
-        cudaError_t e = allow_smem(oproj_kernel<N>, smem);                            \
-        return e != cudaSuccess ? e : launch_ex(oproj_kernel<N>, grid, block, smem, s, pdl, a); \
+        auto k = a.q8 ? oproj_kernel<N, true> : oproj_kernel<N, false>;               \
+        cudaError_t e = allow_smem(k, smem);                                          \
+        return e != cudaSuccess ? e : launch_ex(k, grid, block, smem, s, pdl, a);     \
     }
     switch (chunks_for(a.qd)) {
     case 1: LASTRO_OP(1)
@@ -813,32 +879,40 @@ cudaError_t launch_oproj(const OprojArgs& a, cudaStream_t s, bool pdl) {
 #undef LASTRO_OP
 }
 
-cudaError_t launch_router_fold(const uint16_t* wr, const float* ln, float* wr_t, int E, int H, cudaStream_t s) {
+cudaError_t launch_router_fold(const void* wr, int q8, const float* ln, float* wr_t, int E, int H, cudaStream_t s) {
     const int n = E * H;
-    router_fold_kernel<<<(n + 255) / 256, 256, 0, s>>>(wr, ln, wr_t, E, H);
+    if (q8)
+        router_fold_kernel<true><<<(n + 255) / 256, 256, 0, s>>>(wr, ln, wr_t, E, H);
+    else
+        router_fold_kernel<false><<<(n + 255) / 256, 256, 0, s>>>(wr, ln, wr_t, E, H);
     return cudaGetLastError();
 }
 
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, bool pdl) {
     const dim3 grid((a.E + 3) / 4), block(128);
     const size_t smem = sizeof(float) * (a.H + 32);
-    LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(router_kernel<N>, grid, block, smem, s, pdl, a));
+    LASTRO_NCH_SWITCH(chunks_for(a.H),
+                      launch_ex(a.q8 ? router_kernel<N, true> : router_kernel<N, false>, grid, block, smem, s, pdl, a));
 }
 
-size_t gate_up_smem(int H) { return (size_t)2 * kGuPairs * H * 2 + (size_t)H * 4; }
-size_t down_smem(int H, int I, int k) { (void)H; return (size_t)k * kDnRows * I * 2 + (size_t)k * kDnRows * 4; }
+size_t gate_up_smem(int H, int q8) { return (size_t)2 * kGuPairs * wrow_bytes(H, q8) + (size_t)H * 4; }
+size_t down_smem(int H, int I, int k, int q8) {
+    (void)H;
+    return (size_t)k * kDnRows * wrow_bytes(I, q8) + (size_t)k * kDnRows * 4;
+}
 int gate_up_rows_per_cta() { return kGuPairs; }
 int down_rows_per_cta() { return kDnRows; }
 
 cudaError_t launch_gate_up(const GateUpArgs& a, cudaStream_t s, bool pdl) {
     if (a.I % kGuPairs) return cudaErrorInvalidValue;
     const dim3 grid(a.k * (a.I / kGuPairs)), block(256);
-    const size_t smem = gate_up_smem(a.H);
+    const size_t smem = gate_up_smem(a.H, a.q8);
     if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
 #define LASTRO_GU(N)                                                                  \
     {                                                                                 \
-        cudaError_t e = allow_smem(gate_up_kernel<N>, smem);                          \
-        return e != cudaSuccess ? e : launch_ex(gate_up_kernel<N>, grid, block, smem, s, pdl, a); \
+        auto k = a.q8 ? gate_up_kernel<N, true> : gate_up_kernel<N, false>;           \
+        cudaError_t e = allow_smem(k, smem);                                          \
+        return e != cudaSuccess ? e : launch_ex(k, grid, block, smem, s, pdl, a);     \
     }
     switch (chunks_for(a.H)) {
     case 1: LASTRO_GU(1)
@@ -857,12 +931,13 @@ cudaError_t launch_gate_up(const GateUpArgs& a, cudaStream_t s, bool pdl) {
 cudaError_t launch_down(const DownArgs& a, cudaStream_t s, bool pdl) {
     if (a.H % kDnRows) return cudaErrorInvalidValue;
     const dim3 grid(a.H / kDnRows), block(256);
-    const size_t smem = down_smem(a.H, a.I, a.k);
+    const size_t smem = down_smem(a.H, a.I, a.k, a.q8);
     if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
 #define LASTRO_DN(N)                                                                  \
     {                                                                                 \
-        cudaError_t e = allow_smem(down_kernel<N>, smem);                             \
-        return e != cudaSuccess ? e : launch_ex(down_kernel<N>, grid, block, smem, s, pdl, a); \
+        auto k = a.q8 ? down_kernel<N, true> : down_kernel<N, false>;                 \
+        cudaError_t e = allow_smem(k, smem);                                          \
+        return e != cudaSuccess ? e : launch_ex(k, grid, block, smem, s, pdl, a);     \
     }
     switch (chunks_for(a.I)) {
     case 1: LASTRO_DN(1)
@@ -889,6 +964,13 @@ cudaError_t launch_head(const HeadArgs& a, cudaStream_t s, bool pdl, int* grid_o
     if (grid_out) *grid_out = (int)grid.x;
     const size_t smem = sizeof(float) * (a.H + 32);
     LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(head_kernel<N>, grid, block, smem, s, pdl, a));
+}
+
+cudaError_t launch_synth_q8_0(unsigned char* out, size_t rows, int cols, uint64_t seed, cudaStream_t s) {
+    if (rows == 0 || cols % 32) return cols % 32 ? cudaErrorInvalidValue : cudaSuccess;
+    synth_q8_values_kernel<<<148 * 16, 256, 0, s>>>(out, rows, cols, seed);
+    synth_q8_scales_kernel<<<148 * 4, 256, 0, s>>>(out, rows, cols, seed);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_synth_bf16(uint16_t* out, size_t n, uint64_t seed, float scale, float mean, cudaStream_t s) {

@@ -17,6 +17,13 @@
 
 namespace lastro {
 
+// Linear weights are bf16 ([rows, cols] row-major) or Q8_0.  A Q8_0 row on the device is its cols int8 values, then its
+// cols/32 fp16 block scales, padded to a multiple of 16 bytes (so rows stay 16-byte aligned for bulk copies); weight =
+// scale * value.  `q8` in the argument structs below selects the Q8_0 kernels.
+__host__ __device__ inline size_t wrow_bytes(int cols, int q8) {
+    return q8 ? (((size_t)cols + (size_t)cols / 16 + 15) & ~(size_t)15) : (size_t)cols * 2;
+}
+
 struct QkvArgs {
     const float* h;        // residual stream [H] (ignored when embed_mode)
     float* h_write;        // embed_mode: CTA 0 writes the embedding row x multiplier here
@@ -25,7 +32,8 @@ struct QkvArgs {
     float emb_mult;
     int embed_mode;
     const float* ln;       // [H]
-    const uint16_t* w;     // [qd + 2 kvd, H] bf16: q rows, k rows, v rows
+    const void* w;         // [qd + 2 kvd, H] (bf16 or Q8_0 rows): q rows, k rows, v rows
+    int q8;
     const float* rope_cs;  // [max_len, d]: cos(d/2) then sin(d/2) per position
     const int* pos;        // device position of the token
     float* q_out;          // [qd] roped q
@@ -56,7 +64,8 @@ struct AttnArgs {
 
 struct OprojArgs {
     const float* att;   // [qd]
-    const uint16_t* w;  // [H, qd]
+    const void* w;      // [H, qd] (bf16 or Q8_0 rows)
+    int q8;
     float* h;           // [H], updated in place
     float resid;
     int H, qd;
@@ -84,7 +93,8 @@ struct RouterArgs {
     const float* ln;        // norm weight (norm_mode)
     float eps;
     int norm_mode;
-    const uint16_t* w;      // [E, H]
+    const void* w;          // [E, H] (bf16 or Q8_0 rows)
+    int q8;
     float* logits;          // [E]
     int* ids;               // [k]
     float* weights;         // [k]
@@ -98,7 +108,8 @@ struct GateUpArgs {
     const float* ln;      // MoE norm weight (with shares)
     const int* ids;       // [k] from the router kernel (without shares)
     RouteShares rs;
-    const uint16_t* w;    // [E, 2I, H]
+    const void* w;        // [E, 2I, H] (bf16 or Q8_0 rows)
+    int q8;
     float* a;             // [k, I]
     int* err;             // error word: a bounded wait that gave up writes its code here
     int H, I, k, E;
@@ -109,7 +120,8 @@ struct DownArgs {
     const int* ids;        // [k] from the router kernel (without shares)
     const float* weights;  // [k]
     RouteShares rs;
-    const uint16_t* w;     // [E, H, I]
+    const void* w;         // [E, H, I] (bf16 or Q8_0 rows)
+    int q8;
     float* out;            // accumulate: h += resid*y ; else out = y
     float resid;
     int accumulate;
@@ -140,7 +152,7 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_oproj(const OprojArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, bool pdl);
 int oproj_grid(int H);
-cudaError_t launch_router_fold(const uint16_t* wr, const float* ln, float* wr_t, int E, int H, cudaStream_t s);
+cudaError_t launch_router_fold(const void* wr, int q8, const float* ln, float* wr_t, int E, int H, cudaStream_t s);
 cudaError_t launch_gate_up(const GateUpArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_down(const DownArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_head(const HeadArgs& a, cudaStream_t s, bool pdl, int* grid_out);
@@ -150,6 +162,9 @@ int head_grid(int V);
 // mix64(seed + (i+1)*golden) - 131070) * scale (+ mean), rounded to bf16.
 cudaError_t launch_synth_bf16(uint16_t* out, size_t n, uint64_t seed, float scale, float mean, cudaStream_t s);
 cudaError_t launch_synth_f32(float* out, size_t n, uint64_t seed, float scale, cudaStream_t s);
+// Q8_0 matrix [rows, cols] in the device row layout: int8 values uniform in [-127, 127] and fp16 block scales uniform in
+// [1e-4, 4e-3) from the same integer hash as the CPU oracle's lo_synth_q8_0
+cudaError_t launch_synth_q8_0(unsigned char* out, size_t rows, int cols, uint64_t seed, cudaStream_t s);
 // norms: bf16(1 + value) widened to f32
 cudaError_t launch_synth_norm_f32(float* out, size_t n, uint64_t seed, float scale, cudaStream_t s);
 
@@ -247,8 +262,8 @@ int attn_split_cap(int max_len);
 size_t attn_smem(int max_len, int kv_f32);
 
 // shared memory the grouped expert kernels need (host-side checks)
-size_t gate_up_smem(int H);
-size_t down_smem(int H, int I, int k);
+size_t gate_up_smem(int H, int q8 = 0);
+size_t down_smem(int H, int I, int k, int q8 = 0);
 int gate_up_rows_per_cta();  // I must be a multiple
 int down_rows_per_cta();     // H must be a multiple
 

@@ -3,6 +3,8 @@
 // reduced from the output projection's shares.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -119,6 +121,123 @@ LDEV float row_dot_regs(const uint4 (&w)[NCH], const float4 (&xa)[NCH], const fl
     }
     return acc;
 }
+
+// ---- Q8_0 rows (device layout: cols int8 values, then cols/32 fp16 scales) -------------------------------------------
+// A lane's chunk c covers the same 8 columns as a bf16 chunk, (c*32 + lane)*8 .. +8: 8 int8 values (8 bytes) and the
+// scale of their block of 32.  dot: the 8 products summed, then scaled (one multiply per 8 weights).
+struct Q8Chunk {
+    uint2 q;
+    float s;
+};
+
+LDEV float f16_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+LDEV uint2 ld_weight8(const void* p) {
+    uint2 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+
+LDEV float dot8_q8(uint2 q, float s, float4 xa, float4 xb, float acc) {
+    float p = 0.0f;
+    p = fmaf((float)((int)(q.x << 24) >> 24), xa.x, p);
+    p = fmaf((float)((int)(q.x << 16) >> 24), xa.y, p);
+    p = fmaf((float)((int)(q.x << 8) >> 24), xa.z, p);
+    p = fmaf((float)((int)q.x >> 24), xa.w, p);
+    p = fmaf((float)((int)(q.y << 24) >> 24), xb.x, p);
+    p = fmaf((float)((int)(q.y << 16) >> 24), xb.y, p);
+    p = fmaf((float)((int)(q.y << 8) >> 24), xb.z, p);
+    p = fmaf((float)((int)q.y >> 24), xb.w, p);
+    return fmaf(s, p, acc);
+}
+
+template <int NCH>
+LDEV void load_row_q8(Q8Chunk (&w)[NCH], const unsigned char* row, int H, int lane, bool active) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (active && col < H) {
+            w[c].q = ld_weight8(row + col);
+            w[c].s = f16_to_f32(__ldg(reinterpret_cast<const unsigned short*>(row + H) + (col >> 5)));
+        } else {
+            w[c].q = make_uint2(0u, 0u);
+            w[c].s = 0.0f;
+        }
+    }
+}
+
+template <int NCH>
+LDEV float row_dot_regs_q8(const Q8Chunk (&w)[NCH], const float4 (&xa)[NCH], const float4 (&xb)[NCH], int H, int lane) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < H) acc = dot8_q8(w[c].q, w[c].s, xa[c], xb[c], acc);
+    }
+    return acc;
+}
+
+template <int NCH>
+LDEV float row_dot_q8(const Q8Chunk (&w)[NCH], const float* xs, int H, int lane) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < H) {
+            const float4 xa = *reinterpret_cast<const float4*>(xs + col);
+            const float4 xb = *reinterpret_cast<const float4*>(xs + col + 4);
+            acc = dot8_q8(w[c].q, w[c].s, xa, xb, acc);
+        }
+    }
+    return acc;
+}
+
+// bf16 or Q8_0 row staged in shared memory, x in registers
+template <int NCH, bool Q8>
+LDEV float smem_row_dot_w(const unsigned char* row, const float4 (&xa)[NCH], const float4 (&xb)[NCH], int H, int lane) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < H) {
+            if (Q8) {
+                const uint2 q = *reinterpret_cast<const uint2*>(row + col);
+                const float sc = f16_to_f32(reinterpret_cast<const unsigned short*>(row + H)[col >> 5]);
+                acc = dot8_q8(q, sc, xa[c], xb[c], acc);
+            } else {
+                acc = dot8(*reinterpret_cast<const uint4*>(row + 2 * col), xa[c], xb[c], acc);
+            }
+        }
+    }
+    return acc;
+}
+
+// A weight row held in registers (lane chunks as above), bf16 or Q8_0: load from its first byte, dot with x in shared
+// memory or in registers.
+template <int NCH, bool Q8>
+struct WRow;
+
+template <int NCH>
+struct WRow<NCH, false> {
+    uint4 w[NCH];
+    LDEV void load(const unsigned char* row, int H, int lane, bool active) {
+        load_row<NCH>(w, reinterpret_cast<const uint16_t*>(row), H, lane, active);
+    }
+    LDEV float dot(const float* xs, int H, int lane) const { return row_dot<NCH>(w, xs, H, lane); }
+    LDEV float dot_regs(const float4 (&xa)[NCH], const float4 (&xb)[NCH], int H, int lane) const {
+        return row_dot_regs<NCH>(w, xa, xb, H, lane);
+    }
+};
+
+template <int NCH>
+struct WRow<NCH, true> {
+    Q8Chunk w[NCH];
+    LDEV void load(const unsigned char* row, int H, int lane, bool active) { load_row_q8<NCH>(w, row, H, lane, active); }
+    LDEV float dot(const float* xs, int H, int lane) const { return row_dot_q8<NCH>(w, xs, H, lane); }
+    LDEV float dot_regs(const float4 (&xa)[NCH], const float4 (&xb)[NCH], int H, int lane) const {
+        return row_dot_regs_q8<NCH>(w, xa, xb, H, lane);
+    }
+};
 
 // float4 per thread for a vector of NCH*256 floats over BLOCK threads
 template <int NCH, int BLOCK>

@@ -20,7 +20,7 @@ LIB_PATH = os.path.join(PKG_DIR, "liblastro_b200.so")
 HEADER = os.path.join(PKG_DIR, "..", "include", "lastro_b200.h")
 
 OK, E_ARG, E_CUDA, E_POISONED, E_FULL, E_NOMEM, E_UNSUPPORTED, E_STATE = range(8)
-DTYPE_BF16, DTYPE_F32 = 1, 2
+DTYPE_BF16, DTYPE_F32, DTYPE_Q8_0 = 1, 2, 3
 
 _lib = None
 
@@ -54,6 +54,8 @@ EXPORTS = {
     "lastro_last_error": (C.c_char_p, [C.c_void_p]),
     "lastro_layer_create": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.POINTER(C.c_void_p)]),
+    "lastro_layer_create_q8_0": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
+                                           C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
     "lastro_layer_forward": (C.c_int, [C.c_void_p] + [C.c_void_p] * 5),
     "lastro_layer_add_into": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p]),
     "lastro_layer_destroy": (None, [C.c_void_p]),
@@ -128,16 +130,25 @@ class Context:
 
 
 class GpuLayer:
-    """MoE block with every expert resident (gpu.rs GpuLayer)."""
+    """MoE block with every expert resident (gpu.rs GpuLayer).
+
+    bf16 weights as uint16 bit arrays router [E,H], gate_up [E,2I,H], down [E,H,I]; or Q8_0 weights as uint8 arrays
+    whose last axis holds each row's 34-byte blocks (router [E, H/32*34], gate_up [E, 2I, H/32*34], down
+    [E, H, I/32*34])."""
 
     def __init__(self, ctx: Context, router: np.ndarray, gate_up: np.ndarray, down: np.ndarray, k: int):
-        E, H = router.shape
+        q8 = router.dtype == np.uint8
+        E = router.shape[0]
+        H = router.shape[1] // 34 * 32 if q8 else router.shape[1]
         I = gate_up.shape[1] // 2
-        assert gate_up.shape == (E, 2 * I, H) and down.shape == (E, H, I)
-        self.ctx, self.E, self.H, self.I, self.k = ctx, E, H, I, k
+        want_gu = (E, 2 * I, H // 32 * 34 if q8 else H)
+        want_dn = (E, H, I // 32 * 34 if q8 else I)
+        assert gate_up.shape == want_gu and down.shape == want_dn, (gate_up.shape, down.shape)
+        self.ctx, self.E, self.H, self.I, self.k, self.q8 = ctx, E, H, I, k, q8
         h = C.c_void_p()
-        r, g, d = (np.ascontiguousarray(a, dtype=np.uint16) for a in (router, gate_up, down))
-        ctx.check(lib().lastro_layer_create(ctx.h, E, H, I, k, _p(r), _p(g), _p(d), C.byref(h)))
+        r, g, d = (np.ascontiguousarray(a, dtype=np.uint8 if q8 else np.uint16) for a in (router, gate_up, down))
+        create = lib().lastro_layer_create_q8_0 if q8 else lib().lastro_layer_create
+        ctx.check(create(ctx.h, E, H, I, k, _p(r), _p(g), _p(d), C.byref(h)))
         self.h = h
         ctx._children.add(self)
 
@@ -182,7 +193,8 @@ class GpuModel:
 
     def __init__(self, ctx: Context, cfg: dict, max_len: int, kv_dtype: str = "bf16"):
         self.ctx, self.cfg, self.max_len = ctx, dict(cfg), max_len
-        d = ModelDesc(**{f: cfg[f] for f, _ in ModelDesc._fields_[:15]}, weight_dtype=DTYPE_BF16,
+        wd = DTYPE_Q8_0 if cfg.get("weight_dtype", "bf16") == "q8_0" else DTYPE_BF16
+        d = ModelDesc(**{f: cfg[f] for f, _ in ModelDesc._fields_[:15]}, weight_dtype=wd,
                       kv_dtype=DTYPE_F32 if kv_dtype == "f32" else DTYPE_BF16)
         h = C.c_void_p()
         ctx.check(lib().lastro_model_create(ctx.h, C.byref(d), max_len, C.byref(h)))
@@ -194,12 +206,21 @@ class GpuModel:
         self._next = np.empty(1, np.int32)
 
     def load_tensor(self, name: str, arr: np.ndarray):
+        """bf16 tensors as uint16 bit arrays, norms as float32 (or bf16 bits), Q8_0 tensors as uint8 arrays whose last
+        axis holds each row's 34-byte blocks (fp16 scale, then 32 int8 values): n blocks stand for n * 32 columns."""
         arr = np.ascontiguousarray(arr)
-        dtype = DTYPE_F32 if arr.dtype == np.float32 else DTYPE_BF16
-        if dtype == DTYPE_BF16:
+        dims = list(arr.shape)
+        if arr.dtype == np.float32:
+            dtype = DTYPE_F32
+        elif arr.dtype == np.uint8:
+            dtype = DTYPE_Q8_0
+            assert dims[-1] % 34 == 0, f"{name}: Q8_0 rows are whole 34-byte blocks"
+            dims[-1] = dims[-1] // 34 * 32
+        else:
             assert arr.dtype == np.uint16, f"{name}: bf16 tensors are passed as uint16 bit arrays"
-        shape = (C.c_int64 * arr.ndim)(*arr.shape)
-        self.ctx.check(lib().lastro_model_load_tensor(self.h, name.encode(), dtype, shape, arr.ndim, _p(arr)))
+            dtype = DTYPE_BF16
+        shape = (C.c_int64 * len(dims))(*dims)
+        self.ctx.check(lib().lastro_model_load_tensor(self.h, name.encode(), dtype, shape, len(dims), _p(arr)))
 
     def load_weights(self, w: dict):
         """w: embed [V,H] u16, norm [H] f32, layers[l] dict with LAYER_KEYS (u16 bf16 bits / f32 norms)."""

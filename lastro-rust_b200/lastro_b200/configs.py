@@ -31,7 +31,8 @@ WEIGHT_STD = 0.02
 C1_BLOCK = dict(name="c1-block-1b", experts=32, hidden=1024, inter=512, k=8, weight_seed=0, x_seed=0xC1, tokens=8)
 C2_1B = dict(name="c2-1b-greedy", model=GRANITE_1B, weight_seed=1, prompt_seed=1, prompt_len=128, new_tokens=128)
 C3_3B = dict(name="c3-3b-ctx2048", model=GRANITE_3B, weight_seed=2, prompt_seed=2, context=2048, new_tokens=256)
-C4_3B_Q8 = dict(name="c4-3b-q8_0-ctx512", model=GRANITE_3B, weight_seed=4, prompt_seed=4, context=512,
+GRANITE_3B_Q8 = dict(GRANITE_3B, weight_dtype="q8_0")
+C4_3B_Q8 = dict(name="c4-3b-q8_0-ctx512", model=GRANITE_3B_Q8, weight_seed=4, prompt_seed=4, context=512,
                 new_tokens=256)
 C5_BATCH = dict(name="c5-3b-bs64-ctx1024", model=GRANITE_3B, weight_seed=3, prompt_seed=3, batch=64, context=1024,
                 new_tokens=128, zipf_s=0.8)
@@ -44,18 +45,24 @@ def dims(cfg: dict) -> dict:
     return d
 
 
+def weight_bytes(cfg: dict) -> float:
+    """HBM bytes per linear weight: 2 (bf16) or 34/32 (Q8_0: 32 int8 values and one fp16 scale per block)."""
+    return 34 / 32 if cfg.get("weight_dtype", "bf16") == "q8_0" else 2
+
+
 def bytes_per_token(cfg: dict, context: float, kv_bytes: int = 2) -> dict:
-    """Algorithmic HBM bytes one batch-1 decode step reads (bf16 weights).
+    """Algorithmic HBM bytes one batch-1 decode step reads (bf16 or Q8_0 linear weights, bf16 embedding).
 
     literal = active-expert weights + KV read; full = literal + router + attention
     projections + lm_head (the tied embedding) + norms.
     """
     H, I, L, E, k, V = cfg["hidden"], cfg["inter"], cfg["layers"], cfg["experts"], cfg["k"], cfg["vocab"]
     qd, kvd = cfg["heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
-    experts = L * k * 3 * I * H * 2
+    wb = weight_bytes(cfg)
+    experts = L * k * 3 * I * H * wb
     kv = L * 2 * kvd * kv_bytes * context
-    router = L * E * H * 2
-    attn = L * (qd * H + 2 * kvd * H + H * qd) * 2
+    router = L * E * H * wb
+    attn = L * (qd * H + 2 * kvd * H + H * qd) * wb
     head = V * H * 2
     norms = (2 * L + 1) * H * 4
     literal = experts + kv

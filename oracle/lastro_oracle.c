@@ -242,6 +242,107 @@ static void pool_run(lo_pool *p, size_t tasks, lo_task_fn fn, void *ctx) {
 }
 
 /* ------------------------------------------------------------------------- */
+/* Q8_0 (no reference implementation): blocks of 32 int8    */
+/* values with one fp16 scale, stored as 34 bytes (the scale, then the values);  */
+/* a weight is scale * value, exact in f32.                                      */
+/* ------------------------------------------------------------------------- */
+
+/* f32 -> IEEE fp16, round to nearest even (finite inputs; overflow gives inf) */
+uint16_t lo_f32_to_f16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    uint32_t sign = (u >> 16) & 0x8000u, a = u & 0x7fffffffu;
+    if (a >= 0x47800000u) return (uint16_t)(sign | 0x7c00u); /* |f| >= 65536: inf */
+    if (a < 0x38800000u) {                                 /* below the smallest normal fp16: subnormal */
+        if (a < 0x33000000u) return (uint16_t)sign;          /* rounds to zero */
+        uint32_t m = (a & 0x7fffffu) | 0x800000u;
+        int e = (int)(a >> 23);                               /* 103 .. 112 */
+        int sh = 126 - e;                                     /* m >> sh is the subnormal mantissa, 14..23 */
+        uint32_t q = m >> sh, rem = m & ((1u << sh) - 1u), half = 1u << (sh - 1);
+        if (rem > half || (rem == half && (q & 1u))) ++q;
+        return (uint16_t)(sign | q);
+    }
+    uint32_t r = a - 0x38000000u; /* rebias the exponent by 127 - 15 */
+    uint32_t q = r >> 13, rem = r & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (q & 1u))) ++q;
+    return (uint16_t)(sign | q);
+}
+
+float lo_f16_to_f32(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 0x1fu, m = h & 0x3ffu, u;
+    if (e == 0) {
+        if (m == 0) {
+            u = sign;
+        } else { /* subnormal: normalise */
+            int sh = 0;
+            while (!(m & 0x400u)) {
+                m <<= 1;
+                ++sh;
+            }
+            u = sign | ((uint32_t)(113 - sh) << 23) | ((m & 0x3ffu) << 13);
+        }
+    } else if (e == 31) {
+        u = sign | 0x7f800000u | (m << 13);
+    } else {
+        u = sign | ((e + 112u) << 23) | (m << 13);
+    }
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+/* synthetic Q8_0: element idx of the row-major matrix -> int8 uniform in [-127, 127];
+ * block b (row-major over rows x cols/32) -> fp16 scale 1e-4 + u * 3.9e-3, u uniform in [0, 1) from 24 hash bits */
+int8_t lo_synth_q8_value(uint64_t seed, uint64_t idx) {
+    return (int8_t)((int32_t)(lo_mix64(seed + (idx + 1u) * LO_GOLDEN) % 255u) - 127);
+}
+
+uint16_t lo_synth_q8_scale(uint64_t seed, uint64_t block) {
+    uint64_t h = lo_mix64((seed ^ 0xA5A5A5A5A5A5A5A5ull) + (block + 1u) * LO_GOLDEN);
+    float u = (float)(h >> 40) * (1.0f / 16777216.0f);
+    return lo_f32_to_f16(1e-4f + u * 3.9e-3f);
+}
+
+size_t lo_row_bytes(int32_t dtype, size_t cols) { return dtype == LO_W_Q8_0 ? cols / 32 * 34 : cols * 2; }
+
+typedef struct {
+    uint8_t *out;
+    size_t rows, cols;
+    uint64_t seed;
+    int part, parts;
+} q8_job;
+
+static void *q8_thread(void *arg) {
+    q8_job *j = (q8_job *)arg;
+    size_t per = (j->rows + (size_t)j->parts - 1) / (size_t)j->parts;
+    size_t r0 = per * (size_t)j->part, r1 = r0 + per < j->rows ? r0 + per : j->rows;
+    size_t nb = j->cols / 32;
+    for (size_t r = r0; r < r1; ++r)
+        for (size_t b = 0; b < nb; ++b) {
+            uint8_t *blk = j->out + (r * nb + b) * 34;
+            uint16_t d = lo_synth_q8_scale(j->seed, r * nb + b);
+            memcpy(blk, &d, 2);
+            for (size_t i = 0; i < 32; ++i) blk[2 + i] = (uint8_t)lo_synth_q8_value(j->seed, r * j->cols + b * 32 + i);
+        }
+    return NULL;
+}
+
+void lo_synth_q8_0(uint8_t *out, size_t rows, size_t cols, uint64_t seed, int threads) {
+    if (threads < 1) threads = 1;
+    if (rows * cols < (size_t)1 << 16) threads = 1;
+    if (threads > 64) threads = 64;
+    q8_job jobs[64];
+    pthread_t th[64];
+    for (int t = 0; t < threads; ++t) {
+        q8_job j = {out, rows, cols, seed, t, threads};
+        jobs[t] = j;
+    }
+    for (int t = 1; t < threads; ++t) pthread_create(&th[t], NULL, q8_thread, &jobs[t]);
+    q8_thread(&jobs[0]);
+    for (int t = 1; t < threads; ++t) pthread_join(th[t], NULL);
+}
+
+/* ------------------------------------------------------------------------- */
 /* dot product -- cpu.rs:107-152                                               */
 /* ------------------------------------------------------------------------- */
 
@@ -308,13 +409,70 @@ float lo_dot(const uint16_t *w, const float *x, size_t n) {
     return lo_dot_portable(w, x, n);
 }
 
+/* The dequantised path (a Q8_0 row, n a multiple of 32): each weight is dequantised exactly (fp16 scale x int8) and
+ * enters the same 4 x 8-lane FMA accumulators and horizontal reduction as lo_dot -- a block of 32 is one step. */
+float lo_dot_q8_portable(const uint8_t *row, const float *x, size_t n) {
+    float acc[4][8];
+    memset(acc, 0, sizeof(acc));
+    for (size_t b = 0; b * 32 < n; ++b) {
+        const uint8_t *blk = row + b * 34;
+        uint16_t dh;
+        memcpy(&dh, blk, 2);
+        float d = lo_f16_to_f32(dh);
+        for (int j = 0; j < 4; ++j)
+            for (int l = 0; l < 8; ++l) {
+                float w = d * (float)(int8_t)blk[2 + 8 * j + l];
+                acc[j][l] = fmaf(w, x[b * 32 + 8 * j + l], acc[j][l]);
+            }
+    }
+    float s[8], s4[4];
+    for (int l = 0; l < 8; ++l) s[l] = (acc[0][l] + acc[1][l]) + (acc[2][l] + acc[3][l]);
+    for (int l = 0; l < 4; ++l) s4[l] = s[l] + s[l + 4];
+    return (s4[0] + s4[2]) + (s4[1] + s4[3]);
+}
+
+#if defined(__x86_64__)
+__attribute__((target("avx2,fma"))) static float dot_q8_avx2(const uint8_t *row, const float *x, size_t n) {
+    __m256 acc[4] = {_mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps()};
+    for (size_t b = 0; b * 32 < n; ++b) {
+        const uint8_t *blk = row + b * 34;
+        uint16_t dh;
+        memcpy(&dh, blk, 2);
+        __m256 d = _mm256_set1_ps(lo_f16_to_f32(dh));
+        for (int j = 0; j < 4; ++j) {
+            __m128i raw = _mm_loadl_epi64((const __m128i *)(blk + 2 + 8 * j));
+            __m256 w = _mm256_mul_ps(d, _mm256_cvtepi32_ps(_mm256_cvtepi8_epi32(raw)));
+            acc[j] = _mm256_fmadd_ps(w, _mm256_loadu_ps(x + b * 32 + 8 * j), acc[j]);
+        }
+    }
+    __m256 s = _mm256_add_ps(_mm256_add_ps(acc[0], acc[1]), _mm256_add_ps(acc[2], acc[3]));
+    __m128 h = _mm_add_ps(_mm256_castps256_ps128(s), _mm256_extractf128_ps(s, 1));
+    h = _mm_add_ps(h, _mm_movehl_ps(h, h));
+    h = _mm_add_ss(h, _mm_shuffle_ps(h, h, 1));
+    return _mm_cvtss_f32(h);
+}
+#endif
+
+float lo_dot_q8(const uint8_t *row, const float *x, size_t n) {
+#if defined(__x86_64__)
+    if (have_avx2()) return dot_q8_avx2(row, x, n);
+#endif
+    return lo_dot_q8_portable(row, x, n);
+}
+
+/* a row of either weight type */
+static inline float dot_w(int32_t dtype, const void *row, const float *x, size_t n) {
+    return dtype == LO_W_Q8_0 ? lo_dot_q8((const uint8_t *)row, x, n) : lo_dot((const uint16_t *)row, x, n);
+}
+
 /* ------------------------------------------------------------------------- */
 /* GEMV, SwiGLU, experts -- cpu.rs:154-240                                     */
 /* ------------------------------------------------------------------------- */
 #define ROWS_PER_TASK 16 /* cpu.rs:100 */
 
 typedef struct {
-    const uint16_t *w;
+    const void *w;
+    int32_t dtype;
     int32_t rows, cols;
     const float *x;
     float *y;
@@ -324,13 +482,18 @@ static void gemv_task(void *c, size_t t) {
     gemv_ctx *g = (gemv_ctx *)c;
     size_t r0 = t * ROWS_PER_TASK, r1 = r0 + ROWS_PER_TASK;
     if (r1 > (size_t)g->rows) r1 = (size_t)g->rows;
-    for (size_t r = r0; r < r1; ++r) g->y[r] = lo_dot(g->w + r * (size_t)g->cols, g->x, (size_t)g->cols);
+    size_t rb = lo_row_bytes(g->dtype, (size_t)g->cols);
+    for (size_t r = r0; r < r1; ++r) g->y[r] = dot_w(g->dtype, (const uint8_t *)g->w + r * rb, g->x, (size_t)g->cols);
 }
 
-/* cpu.rs:197-203 Cpu::gemv (rows in tasks of 16 over the pool, cpu.rs:185-195) */
-void lo_gemv(lo_pool *p, const uint16_t *w, int32_t rows, int32_t cols, const float *x, float *y) {
-    gemv_ctx g = {w, rows, cols, x, y};
+/* cpu.rs:197-203 Cpu::gemv (rows in tasks of 16 over the pool, cpu.rs:185-195), either weight type */
+void lo_gemv_w(lo_pool *p, int32_t dtype, const void *w, int32_t rows, int32_t cols, const float *x, float *y) {
+    gemv_ctx g = {w, dtype, rows, cols, x, y};
     pool_run(p, ((size_t)rows + ROWS_PER_TASK - 1) / ROWS_PER_TASK, gemv_task, &g);
+}
+
+void lo_gemv(lo_pool *p, const uint16_t *w, int32_t rows, int32_t cols, const float *x, float *y) {
+    lo_gemv_w(p, LO_W_BF16, w, rows, cols, x, y);
 }
 
 /* cpu.rs:154-158: a[j] = h[j] / (1 + exp(-h[j])) * h[I + j] */
@@ -340,9 +503,9 @@ void lo_swiglu(const float *h, int32_t inter, float *a) {
 
 typedef struct {
     const float *x;
-    int32_t k, hidden, inter;
-    const uint16_t *const *gate_up;
-    const uint16_t *const *down;
+    int32_t k, hidden, inter, dtype;
+    const void *const *gate_up;
+    const void *const *down;
     const float *weights;
     float *h; /* [k, 2I] */
     float *a; /* [k, I] */
@@ -356,20 +519,21 @@ static void experts_gu_task(void *c, size_t t) {
     size_t rows = 2 * (size_t)e->inter;
     size_t r0 = ch * ROWS_PER_TASK, r1 = r0 + ROWS_PER_TASK;
     if (r1 > rows) r1 = rows;
-    const uint16_t *w = e->gate_up[ex];
-    for (size_t r = r0; r < r1; ++r)
-        e->h[ex * rows + r] = lo_dot(w + r * (size_t)e->hidden, e->x, (size_t)e->hidden);
+    const uint8_t *w = (const uint8_t *)e->gate_up[ex];
+    size_t rb = lo_row_bytes(e->dtype, (size_t)e->hidden);
+    for (size_t r = r0; r < r1; ++r) e->h[ex * rows + r] = dot_w(e->dtype, w + r * rb, e->x, (size_t)e->hidden);
 }
 
 static void experts_down_task(void *c, size_t t) {
     experts_ctx *e = (experts_ctx *)c;
     size_t r0 = t * ROWS_PER_TASK, r1 = r0 + ROWS_PER_TASK;
     if (r1 > (size_t)e->hidden) r1 = (size_t)e->hidden;
+    size_t rb = lo_row_bytes(e->dtype, (size_t)e->inter);
     for (size_t r = r0; r < r1; ++r) {
         float acc = 0.0f;
         for (int32_t j = 0; j < e->k; ++j)
-            acc += e->weights[j] *
-                   lo_dot(e->down[j] + r * (size_t)e->inter, e->a + (size_t)j * e->inter, (size_t)e->inter);
+            acc += e->weights[j] * dot_w(e->dtype, (const uint8_t *)e->down[j] + r * rb, e->a + (size_t)j * e->inter,
+                                         (size_t)e->inter);
         e->y[r] = acc;
     }
 }
@@ -377,20 +541,25 @@ static void experts_down_task(void *c, size_t t) {
 /* cpu.rs:205-240 Cpu::experts: dispatch 1 = the 2I gate_up rows of every chosen
  * expert, SwiGLU per expert, dispatch 2 = each row of y summed over the experts
  * in routing order. */
-void lo_experts(lo_pool *p, const float *x, int32_t k, const uint16_t *const *gate_up,
-                const uint16_t *const *down, const float *weights, int32_t hidden, int32_t inter,
-                float *y) {
+void lo_experts_w(lo_pool *p, int32_t dtype, const float *x, int32_t k, const void *const *gate_up,
+                  const void *const *down, const float *weights, int32_t hidden, int32_t inter, float *y) {
     memset(y, 0, sizeof(float) * (size_t)hidden);
     if (k == 0) return;
     float *h = (float *)malloc(sizeof(float) * (size_t)k * 2 * (size_t)inter);
     float *a = (float *)malloc(sizeof(float) * (size_t)k * (size_t)inter);
-    experts_ctx e = {x, k, hidden, inter, gate_up, down, weights, h, a, y,
+    experts_ctx e = {x, k, hidden, inter, dtype, gate_up, down, weights, h, a, y,
                      ((size_t)2 * inter + ROWS_PER_TASK - 1) / ROWS_PER_TASK};
     pool_run(p, (size_t)k * e.per, experts_gu_task, &e);
     for (int32_t j = 0; j < k; ++j) lo_swiglu(h + (size_t)j * 2 * inter, inter, a + (size_t)j * inter);
     pool_run(p, ((size_t)hidden + ROWS_PER_TASK - 1) / ROWS_PER_TASK, experts_down_task, &e);
     free(h);
     free(a);
+}
+
+void lo_experts(lo_pool *p, const float *x, int32_t k, const uint16_t *const *gate_up,
+                const uint16_t *const *down, const float *weights, int32_t hidden, int32_t inter,
+                float *y) {
+    lo_experts_w(p, LO_W_BF16, x, k, (const void *const *)gate_up, (const void *const *)down, weights, hidden, inter, y);
 }
 
 /* ------------------------------------------------------------------------- */
@@ -440,24 +609,33 @@ void lo_routing(const float *logits, int32_t e, int32_t k, int32_t *ids, float *
     free(order);
 }
 
-/* block.rs:56-62 HostLayer::forward_cpu */
-void lo_block_forward(lo_pool *p, const uint16_t *router, const uint16_t *gate_up, const uint16_t *down,
-                      int32_t experts, int32_t hidden, int32_t inter, int32_t k, const float *x, float *y,
-                      int32_t *ids, float *weights, float *logits_or_null) {
+/* block.rs:56-62 HostLayer::forward_cpu, either weight type */
+void lo_block_forward_w(lo_pool *p, int32_t dtype, const void *router, const void *gate_up, const void *down,
+                        int32_t experts, int32_t hidden, int32_t inter, int32_t k, const float *x, float *y,
+                        int32_t *ids, float *weights, float *logits_or_null) {
     float *logits = (float *)malloc(sizeof(float) * (size_t)experts);
-    lo_gemv(p, router, experts, hidden, x, logits);
+    lo_gemv_w(p, dtype, router, experts, hidden, x, logits);
     lo_routing(logits, experts, k, ids, weights);
-    const uint16_t **gu = (const uint16_t **)malloc(sizeof(void *) * (size_t)k);
-    const uint16_t **dn = (const uint16_t **)malloc(sizeof(void *) * (size_t)k);
+    const void **gu = (const void **)malloc(sizeof(void *) * (size_t)k);
+    const void **dn = (const void **)malloc(sizeof(void *) * (size_t)k);
+    size_t gu_bytes = 2 * (size_t)inter * lo_row_bytes(dtype, (size_t)hidden);
+    size_t dn_bytes = (size_t)hidden * lo_row_bytes(dtype, (size_t)inter);
     for (int32_t j = 0; j < k; ++j) {
-        gu[j] = gate_up + (size_t)ids[j] * 2 * inter * hidden;
-        dn[j] = down + (size_t)ids[j] * hidden * inter;
+        gu[j] = (const uint8_t *)gate_up + (size_t)ids[j] * gu_bytes;
+        dn[j] = (const uint8_t *)down + (size_t)ids[j] * dn_bytes;
     }
-    lo_experts(p, x, k, gu, dn, weights, hidden, inter, y);
+    lo_experts_w(p, dtype, x, k, gu, dn, weights, hidden, inter, y);
     if (logits_or_null) memcpy(logits_or_null, logits, sizeof(float) * (size_t)experts);
     free(gu);
     free(dn);
     free(logits);
+}
+
+void lo_block_forward(lo_pool *p, const uint16_t *router, const uint16_t *gate_up, const uint16_t *down,
+                      int32_t experts, int32_t hidden, int32_t inter, int32_t k, const float *x, float *y,
+                      int32_t *ids, float *weights, float *logits_or_null) {
+    lo_block_forward_w(p, LO_W_BF16, router, gate_up, down, experts, hidden, inter, k, x, y, ids, weights,
+                       logits_or_null);
 }
 
 /* ------------------------------------------------------------------------- */
@@ -544,6 +722,18 @@ static uint16_t *synth_bf16_owned(lo_model *m, size_t n, uint64_t seed, float sd
     return p;
 }
 
+static uint8_t *synth_q8_owned(lo_model *m, size_t rows, size_t cols, uint64_t seed, int threads) {
+    uint8_t *p = (uint8_t *)own(m, rows * lo_row_bytes(LO_W_Q8_0, cols));
+    lo_synth_q8_0(p, rows, cols, seed, threads);
+    return p;
+}
+
+/* a linear weight [rows, cols] of the model's weight type */
+static const void *synth_linear_owned(lo_model *m, size_t rows, size_t cols, uint64_t seed, float sd, int threads) {
+    if (m->cfg.weight_dtype == LO_W_Q8_0) return synth_q8_owned(m, rows, cols, seed, threads);
+    return synth_bf16_owned(m, rows * cols, seed, sd, 0.0f, threads);
+}
+
 static float *synth_norm_owned(lo_model *m, size_t n, uint64_t seed, float sd, int threads) {
     /* norms live as bf16 in checkpoints and are widened to f32 (model.rs:95-97, 117-118) */
     uint16_t *b = (uint16_t *)malloc(n * 2);
@@ -566,13 +756,13 @@ lo_model *lo_model_create_synthetic(const lo_config *cfg, uint64_t seed, float s
         lo_layer_weights *w = &m->layers[l];
         w->ln_attn = synth_norm_owned(m, H, lo_tensor_seed(seed, l, LO_T_LN_ATTN), norm_sd, threads);
         w->ln_moe = synth_norm_owned(m, H, lo_tensor_seed(seed, l, LO_T_LN_MOE), norm_sd, threads);
-        w->q = synth_bf16_owned(m, qd * H, lo_tensor_seed(seed, l, LO_T_Q), sd, 0.0f, threads);
-        w->k = synth_bf16_owned(m, kvd * H, lo_tensor_seed(seed, l, LO_T_K), sd, 0.0f, threads);
-        w->v = synth_bf16_owned(m, kvd * H, lo_tensor_seed(seed, l, LO_T_V), sd, 0.0f, threads);
-        w->o = synth_bf16_owned(m, H * qd, lo_tensor_seed(seed, l, LO_T_O), sd, 0.0f, threads);
-        w->router = synth_bf16_owned(m, E * H, lo_tensor_seed(seed, l, LO_T_ROUTER), sd, 0.0f, threads);
-        w->gate_up = synth_bf16_owned(m, E * 2 * I * H, lo_tensor_seed(seed, l, LO_T_GATE_UP), sd, 0.0f, threads);
-        w->down = synth_bf16_owned(m, E * H * I, lo_tensor_seed(seed, l, LO_T_DOWN), sd, 0.0f, threads);
+        w->q = synth_linear_owned(m, qd, H, lo_tensor_seed(seed, l, LO_T_Q), sd, threads);
+        w->k = synth_linear_owned(m, kvd, H, lo_tensor_seed(seed, l, LO_T_K), sd, threads);
+        w->v = synth_linear_owned(m, kvd, H, lo_tensor_seed(seed, l, LO_T_V), sd, threads);
+        w->o = synth_linear_owned(m, H, qd, lo_tensor_seed(seed, l, LO_T_O), sd, threads);
+        w->router = synth_linear_owned(m, E, H, lo_tensor_seed(seed, l, LO_T_ROUTER), sd, threads);
+        w->gate_up = synth_linear_owned(m, E * 2 * I, H, lo_tensor_seed(seed, l, LO_T_GATE_UP), sd, threads);
+        w->down = synth_linear_owned(m, E * H, I, lo_tensor_seed(seed, l, LO_T_DOWN), sd, threads);
     }
     return m;
 }
@@ -611,6 +801,7 @@ struct lo_session {
     lo_pool *pool;
     int32_t max_len, pos;
     int32_t layers; /* own copy: the session may be destroyed after its model */
+    int32_t kv_bf16; /* store K/V rows rounded to bf16 (RNE), as a paged bf16 KV cache holds them */
     float **k_cache, **v_cache; /* per layer [max_len, kvd] */
 };
 
@@ -642,6 +833,11 @@ void lo_session_destroy(lo_session *s) {
 }
 
 void lo_session_reset(lo_session *s) { s->pos = 0; }
+void lo_session_set_kv_bf16(lo_session *s, int32_t on) { s->kv_bf16 = on != 0; }
+
+static void round_bf16(float *v, size_t n) {
+    for (size_t i = 0; i < n; ++i) v[i] = bf2f(lo_f32_to_bf16(v[i]));
+}
 int32_t lo_session_pos(const lo_session *s) { return s->pos; }
 const float *lo_session_k(const lo_session *s, int32_t layer) { return s->k_cache[layer]; }
 const float *lo_session_v(const lo_session *s, int32_t layer) { return s->v_cache[layer]; }
@@ -652,6 +848,10 @@ int lo_session_fill_kv(lo_session *s, int32_t n, uint64_t seed, float sd) {
     for (int32_t l = 0; l < s->m->cfg.layers; ++l) {
         lo_synth_f32(s->k_cache[l] + (size_t)s->pos * kvd, (size_t)n * kvd, lo_mix64(seed + 2 * (uint64_t)l), sd, 0.0f, 1);
         lo_synth_f32(s->v_cache[l] + (size_t)s->pos * kvd, (size_t)n * kvd, lo_mix64(seed + 2 * (uint64_t)l + 1), sd, 0.0f, 1);
+        if (s->kv_bf16) {
+            round_bf16(s->k_cache[l] + (size_t)s->pos * kvd, (size_t)n * kvd);
+            round_bf16(s->v_cache[l] + (size_t)s->pos * kvd, (size_t)n * kvd);
+        }
     }
     s->pos += n;
     return 0;
@@ -718,18 +918,23 @@ int lo_session_step(lo_session *s, int32_t token, float *logits, int32_t *ids, f
         lo_rmsnorm(x, w->ln_attn, h, c->eps, xn);
         float *kr = s->k_cache[l] + (size_t)s->pos * kvd;
         float *vr = s->v_cache[l] + (size_t)s->pos * kvd;
-        lo_gemv(s->pool, w->q, qd, h, xn, q);
-        lo_gemv(s->pool, w->k, kvd, h, xn, kr);
-        lo_gemv(s->pool, w->v, kvd, h, xn, vr);
+        lo_gemv_w(s->pool, c->weight_dtype, w->q, qd, h, xn, q);
+        lo_gemv_w(s->pool, c->weight_dtype, w->k, kvd, h, xn, kr);
+        lo_gemv_w(s->pool, c->weight_dtype, w->v, kvd, h, xn, vr);
         lo_rope(q, qd, d, cs);
         lo_rope(kr, kvd, d, cs);
+        if (s->kv_bf16) {
+            round_bf16(kr, (size_t)kvd);
+            round_bf16(vr, (size_t)kvd);
+        }
         memset(att, 0, sizeof(float) * (size_t)qd);
         attn_ctx ac = {c, q, s->k_cache[l], s->v_cache[l], s->pos + 1, att};
         pool_run(s->pool, (size_t)c->heads, attn_task, &ac);
-        lo_gemv(s->pool, w->o, h, qd, att, o);
+        lo_gemv_w(s->pool, c->weight_dtype, w->o, h, qd, att, o);
         for (int32_t i = 0; i < h; ++i) x[i] += c->residual_multiplier * o[i];
         lo_rmsnorm(x, w->ln_moe, h, c->eps, xn);
-        lo_block_forward(s->pool, w->router, w->gate_up, w->down, c->experts, h, c->inter, c->k, xn, y, ri, rw, NULL);
+        lo_block_forward_w(s->pool, c->weight_dtype, w->router, w->gate_up, w->down, c->experts, h, c->inter, c->k, xn,
+                           y, ri, rw, NULL);
         for (int32_t i = 0; i < h; ++i) x[i] += c->residual_multiplier * y[i];
         if (ids) memcpy(ids + (size_t)l * c->k, ri, sizeof(int32_t) * (size_t)c->k);
         if (weights) memcpy(weights + (size_t)l * c->k, rw, sizeof(float) * (size_t)c->k);

@@ -41,6 +41,19 @@ void lo_ref_values(float *out, size_t n, uint64_t seed);
 uint16_t lo_f32_to_bf16(float f);
 float lo_bf16_to_f32(uint16_t b);
 
+/* ---- Q8_0 (no reference implementation) --------------- */
+/* a row of cols weights (cols a multiple of 32) is cols/32 blocks of 34 bytes: the fp16 scale, then 32 int8 values;
+ * weight = scale * value (exact in f32).  The oracle's path is the dequantised one. */
+enum { LO_W_BF16 = 0, LO_W_Q8_0 = 1 };
+uint16_t lo_f32_to_f16(float f);
+float lo_f16_to_f32(uint16_t h);
+int8_t lo_synth_q8_value(uint64_t seed, uint64_t idx);
+uint16_t lo_synth_q8_scale(uint64_t seed, uint64_t block);
+void lo_synth_q8_0(uint8_t *out, size_t rows, size_t cols, uint64_t seed, int threads);
+size_t lo_row_bytes(int32_t dtype, size_t cols);
+float lo_dot_q8(const uint8_t *row, const float *x, size_t n);
+float lo_dot_q8_portable(const uint8_t *row, const float *x, size_t n);
+
 /* ---- thread pool (pool.rs: fixed workers, tasks claimed by an atomic counter) */
 typedef struct lo_pool lo_pool;
 lo_pool *lo_pool_create(int threads);
@@ -51,16 +64,22 @@ int lo_pool_threads(const lo_pool *p);
 float lo_dot(const uint16_t *w, const float *x, size_t n);          /* cpu.rs:145-152 */
 float lo_dot_portable(const uint16_t *w, const float *x, size_t n); /* same order, no SIMD */
 void lo_gemv(lo_pool *p, const uint16_t *w, int32_t rows, int32_t cols, const float *x, float *y);
+void lo_gemv_w(lo_pool *p, int32_t dtype, const void *w, int32_t rows, int32_t cols, const float *x, float *y);
 void lo_swiglu(const float *h, int32_t inter, float *a);
 void lo_routing(const float *logits, int32_t e, int32_t k, int32_t *ids, float *weights);
 void lo_experts(lo_pool *p, const float *x, int32_t k, const uint16_t *const *gate_up,
                 const uint16_t *const *down, const float *weights, int32_t hidden, int32_t inter,
                 float *y);
+void lo_experts_w(lo_pool *p, int32_t dtype, const float *x, int32_t k, const void *const *gate_up,
+                  const void *const *down, const float *weights, int32_t hidden, int32_t inter, float *y);
 /* HostLayer::forward_cpu: router [E,H], gate_up [E,2I,H], down [E,H,I] */
 void lo_block_forward(lo_pool *p, const uint16_t *router, const uint16_t *gate_up,
                       const uint16_t *down, int32_t experts, int32_t hidden, int32_t inter,
                       int32_t k, const float *x, float *y, int32_t *ids, float *weights,
                       float *logits_or_null);
+void lo_block_forward_w(lo_pool *p, int32_t dtype, const void *router, const void *gate_up, const void *down,
+                        int32_t experts, int32_t hidden, int32_t inter, int32_t k, const float *x, float *y,
+                        int32_t *ids, float *weights, float *logits_or_null);
 void lo_rmsnorm(const float *x, const float *w, int32_t n, float eps, float *out);
 void lo_rope_cos_sin(float theta, int32_t head_dim, int32_t pos, float *cs);
 void lo_rope(float *x, int32_t n, int32_t d, const float *cs);
@@ -72,14 +91,15 @@ typedef struct {
     int32_t hidden, inter, layers, heads, kv_heads, head_dim, vocab, experts, k;
     float rope_theta, eps, embedding_multiplier, residual_multiplier, attention_multiplier,
         logits_scaling;
+    int32_t weight_dtype; /* LO_W_BF16 or LO_W_Q8_0: the linear weights (embeddings and norms are bf16 / f32) */
 } lo_config;
 
 typedef struct {
     const float *ln_attn, *ln_moe; /* [H] */
-    const uint16_t *q, *k, *v, *o; /* [qd,H] [kvd,H] [kvd,H] [H,qd] */
-    const uint16_t *router;        /* [E,H] */
-    const uint16_t *gate_up;       /* [E,2I,H] */
-    const uint16_t *down;          /* [E,H,I] */
+    const void *q, *k, *v, *o;     /* [qd,H] [kvd,H] [kvd,H] [H,qd], of the config's weight type */
+    const void *router;            /* [E,H] */
+    const void *gate_up;           /* [E,2I,H] */
+    const void *down;              /* [E,H,I] */
 } lo_layer_weights;
 
 typedef struct lo_model lo_model;
@@ -96,6 +116,8 @@ const void *lo_model_tensor(const lo_model *m, int32_t layer, int32_t kind);
 typedef struct lo_session lo_session;
 lo_session *lo_session_create(const lo_model *m, lo_pool *p, int32_t max_len);
 void lo_session_destroy(lo_session *s);
+/* K/V rows rounded to bf16 (RNE) when stored: the arithmetic of a paged bf16 KV cache (off by default) */
+void lo_session_set_kv_bf16(lo_session *s, int32_t on);
 void lo_session_reset(lo_session *s);
 int32_t lo_session_pos(const lo_session *s);
 /* CpuSession::step: logits [V]; ids/weights [L*k] may be NULL. Returns 0, or -1 when full. */

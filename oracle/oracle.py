@@ -39,7 +39,11 @@ class Config(C.Structure):
     _fields_ = [(n, C.c_int32) for n in ("hidden", "inter", "layers", "heads", "kv_heads", "head_dim", "vocab",
                                          "experts", "k")] + \
                [(n, C.c_float) for n in ("rope_theta", "eps", "embedding_multiplier", "residual_multiplier",
-                                         "attention_multiplier", "logits_scaling")]
+                                         "attention_multiplier", "logits_scaling")] + \
+               [("weight_dtype", C.c_int32)]
+
+
+W_BF16, W_Q8_0 = 0, 1
 
 
 class LayerWeights(C.Structure):
@@ -74,6 +78,13 @@ def _declare(L):
         "lo_pool_threads": (C.c_int, [_P]),
         "lo_dot": (_F, [_P, _P, _SZ]),
         "lo_dot_portable": (_F, [_P, _P, _SZ]),
+        "lo_dot_q8": (_F, [_P, _P, _SZ]),
+        "lo_dot_q8_portable": (_F, [_P, _P, _SZ]),
+        "lo_f32_to_f16": (C.c_uint16, [_F]),
+        "lo_f16_to_f32": (_F, [C.c_uint16]),
+        "lo_synth_q8_0": (None, [_P, _SZ, _SZ, _U64, _I]),
+        "lo_gemv_w": (None, [_P, _I, _P, _I, _I, _P, _P]),
+        "lo_block_forward_w": (None, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
         "lo_gemv": (None, [_P, _P, _I, _I, _P, _P]),
         "lo_swiglu": (None, [_P, _I, _P]),
         "lo_routing": (None, [_P, _I, _I, _P, _P]),
@@ -91,6 +102,7 @@ def _declare(L):
         "lo_session_create": (_P, [_P, _P, _I]),
         "lo_session_destroy": (None, [_P]),
         "lo_session_reset": (None, [_P]),
+        "lo_session_set_kv_bf16": (None, [_P, C.c_int32]),
         "lo_session_pos": (_I, [_P]),
         "lo_session_step": (C.c_int, [_P, _I, _P, _P, _P]),
         "lo_session_fill_kv": (C.c_int, [_P, _I, _U64, _F]),
@@ -167,6 +179,35 @@ class Pool:
         self.close()
 
 
+def synth_q8_0(rows: int, cols: int, seed: int, threads: int = 8) -> np.ndarray:
+    """Synthetic Q8_0 matrix [rows, cols] as uint8 [rows, cols/32 * 34] (blocks: fp16 scale, 32 int8 values)."""
+    out = np.empty((rows, cols // 32 * 34), dtype=np.uint8)
+    lib().lo_synth_q8_0(_ptr(out), rows, cols, seed, threads)
+    return out
+
+
+def q8_dequant(q: np.ndarray) -> np.ndarray:
+    """Q8_0 blocks [..., nb*34] -> f32 [..., nb*32], scale * value."""
+    shp = q.shape[:-1]
+    b = q.reshape(-1, 34)
+    d = b[:, :2].copy().view(np.float16).astype(np.float32)
+    v = b[:, 2:].view(np.int8).astype(np.float32)
+    return (d * v).reshape(*shp, -1)
+
+
+def dot_q8(row: np.ndarray, x: np.ndarray, portable: bool = False) -> float:
+    f = lib().lo_dot_q8_portable if portable else lib().lo_dot_q8
+    return float(f(_ptr(row), _ptr(x), x.size))
+
+
+def f32_to_f16(v: float) -> int:
+    return int(lib().lo_f32_to_f16(v))
+
+
+def f16_to_f32(h: int) -> float:
+    return float(lib().lo_f16_to_f32(h))
+
+
 def dot(w: np.ndarray, x: np.ndarray, portable: bool = False) -> float:
     f = lib().lo_dot_portable if portable else lib().lo_dot
     return float(f(_ptr(w), _ptr(x), min(w.size, x.size)))
@@ -205,6 +246,20 @@ def block_forward(pool: Pool, router, gate_up, down, experts: int, hidden: int, 
     return y, ids, w, logits
 
 
+def block_forward_w(pool: Pool, dtype: int, router, gate_up, down, experts: int, hidden: int, inter: int, k: int,
+                    x: np.ndarray):
+    """block_forward for either weight type (W_BF16: uint16 bits; W_Q8_0: uint8 34-byte blocks along each row)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(hidden, dtype=np.float32)
+    ids = np.empty(k, dtype=np.int32)
+    w = np.empty(k, dtype=np.float32)
+    logits = np.empty(experts, dtype=np.float32)
+    router, gate_up, down = (np.ascontiguousarray(a) for a in (router, gate_up, down))
+    lib().lo_block_forward_w(pool.h, dtype, _ptr(router), _ptr(gate_up), _ptr(down), experts, hidden, inter, k,
+                             _ptr(x), _ptr(y), _ptr(ids), _ptr(w), _ptr(logits))
+    return y, ids, w, logits
+
+
 def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
     x = np.ascontiguousarray(x, dtype=np.float32)
     w = np.ascontiguousarray(w, dtype=np.float32)
@@ -231,7 +286,8 @@ def argmax_last(v: np.ndarray) -> int:
 
 
 def make_config(d: dict) -> Config:
-    return Config(**{f: d[f] for f, _ in Config._fields_})
+    vals = {f: d[f] for f, _ in Config._fields_ if f != "weight_dtype"}
+    return Config(**vals, weight_dtype=W_Q8_0 if d.get("weight_dtype", "bf16") == "q8_0" else W_BF16)
 
 
 class Model:
@@ -276,10 +332,12 @@ class Model:
 
 
 class Session:
-    def __init__(self, model: Model, pool: Pool, max_len: int):
+    def __init__(self, model: Model, pool: Pool, max_len: int, kv_bf16: bool = False):
+        """kv_bf16: K/V rows are rounded to bf16 when stored (a paged bf16 KV cache); f32 otherwise."""
         self.model = model
         self.pool = pool
         self.h = lib().lo_session_create(model.h, pool.h, max_len)
+        lib().lo_session_set_kv_bf16(self.h, int(kv_bf16))
         c = model.cfg
         self.logits = np.empty(c["vocab"], dtype=np.float32)
         self.ids = np.empty(c["layers"] * c["k"], dtype=np.int32)

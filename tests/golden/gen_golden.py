@@ -14,8 +14,11 @@ Fixtures:
                  and routing at every position
   c2_greedy.npz  the Granite-1B-shaped model of BASELINE config 1: 128-token
                  prompt, 128 greedy ids, top1-top2 gaps, top-16 logits per step
+  tiny_q8.npz    the tiny test Granite with every linear weight Q8_0 (BASELINE
+                 config C4's format), run dequantised in fp32: prompt, greedy
+                 ids, teacher-forced logits and routing at every position
 
-Run from the repository root:  python tests/golden/gen_golden.py [--skip-c2]
+Run from the repository root:  python tests/golden/gen_golden.py [--skip-c2] [--only NAME]
 """
 import argparse
 import json
@@ -149,6 +152,28 @@ def gen_tiny(out):
     print("tiny:", prompt, gen)
 
 
+def gen_tiny_q8(out):
+    cfg, seed = dict(CFG.TINY, weight_dtype="q8_0"), 12
+    wq = S.model_weights_q8(cfg, seed)
+    m = hf_model(cfg, S.dequant_model(wq))
+    prompt = S.tokens(20, 78, cfg["vocab"]).tolist()
+    gen, scores = greedy(m, prompt, 32)
+    seq = prompt + gen[:-1]
+    got, hs = router_capture(m, range(cfg["layers"]))
+    with torch.inference_mode():
+        logits = m(torch.tensor([seq]), use_cache=False).logits[0].float()
+    for h in hs:
+        h.remove()
+    idx = np.stack([topk_softmax(got[L][0], cfg["k"])[0] for L in range(cfg["layers"])])
+    top2 = scores.topk(2, dim=-1).values
+    np.savez_compressed(os.path.join(out, "tiny_q8.npz"), prompt=np.array(prompt, np.int32),
+                        generated=np.array(gen, np.int32), logits=logits.numpy(), route_idx=idx,
+                        gaps=(top2[:, 0] - top2[:, 1]).numpy(),
+                        meta=json.dumps(dict(cfg=cfg, seed=seed, torch=torch.__version__,
+                                             transformers=transformers.__version__)))
+    print("tiny_q8:", prompt, gen)
+
+
 def gen_c2(out, new_tokens):
     c = CFG.C2_1B
     cfg = c["model"]
@@ -171,12 +196,15 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--skip-c2", action="store_true")
     ap.add_argument("--c2-tokens", type=int, default=128)
+    ap.add_argument("--only", choices=("block_c1", "tiny", "tiny_q8", "c2"), help="regenerate one fixture")
     a = ap.parse_args()
     torch.set_num_threads(os.cpu_count() or 8)
-    gen_block_c1(HERE)
-    gen_tiny(HERE)
-    if not a.skip_c2:
-        gen_c2(HERE, a.c2_tokens)
+    jobs = dict(block_c1=lambda: gen_block_c1(HERE), tiny=lambda: gen_tiny(HERE), tiny_q8=lambda: gen_tiny_q8(HERE),
+                c2=lambda: gen_c2(HERE, a.c2_tokens))
+    for name, job in jobs.items():
+        if (a.only and name != a.only) or (name == "c2" and a.skip_c2 and not a.only):
+            continue
+        job()
 
 
 if __name__ == "__main__":

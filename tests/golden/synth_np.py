@@ -105,6 +105,62 @@ def model_weights(cfg, seed, std, *, stds=None):
     return w
 
 
+# ---- Q8_0: blocks of 32 int8 values with one fp16 scale, 34 bytes (scale, then values) ---------
+def q8_0(rows: int, cols: int, seed: int) -> np.ndarray:
+    """Synthetic Q8_0 matrix [rows, cols] as uint8 [rows, cols/32 * 34]: value of element i uniform in [-127, 127]
+    from mix64(seed + (i + 1) * GOLDEN) % 255 - 127; scale of block b = fp16(1e-4 + u * 3.9e-3), u = 24 hash bits of
+    mix64((seed ^ 0xA5..A5) + (b + 1) * GOLDEN) / 2^24 (f32 arithmetic, round to nearest even)."""
+    nb = cols // 32
+    idx = np.arange(rows * cols, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        h = mix64(np.uint64(seed) + (idx + np.uint64(1)) * GOLDEN)
+        vals = ((h % np.uint64(255)).astype(np.int64) - 127).astype(np.int8).reshape(rows, nb, 32)
+        bidx = np.arange(rows * nb, dtype=np.uint64)
+        hb = mix64((np.uint64(seed) ^ np.uint64(0xA5A5A5A5A5A5A5A5)) + (bidx + np.uint64(1)) * GOLDEN)
+    u = (hb >> np.uint64(40)).astype(np.float32) * np.float32(1.0 / 16777216.0)
+    d = (np.float32(1e-4) + u * np.float32(3.9e-3)).astype(np.float16).reshape(rows, nb, 1)
+    out = np.empty((rows, nb, 34), dtype=np.uint8)
+    out[:, :, :2] = d.view(np.uint8)
+    out[:, :, 2:] = vals.view(np.uint8)
+    return out.reshape(rows, nb * 34)
+
+
+def q8_dequant(q: np.ndarray) -> np.ndarray:
+    """Q8_0 [..., nb*34] -> f32 [..., nb*32]: scale * value (exact in f32)."""
+    shp = q.shape[:-1]
+    b = np.ascontiguousarray(q).reshape(-1, 34)
+    d = b[:, :2].copy().view(np.float16).astype(np.float32)
+    v = b[:, 2:].view(np.int8).astype(np.float32)
+    return (d * v).reshape(*shp, -1)
+
+
+def model_weights_q8(cfg, seed, *, embed_std=0.3, norm_std=0.1):
+    """Q8_0 linear weights (uint8 blocks, the form the oracle and the library take), bf16 embedding (uint16 bits),
+    f32 norms holding bf16 values; the same tensor seeds as model_weights."""
+    H, I, E, V = cfg["hidden"], cfg["inter"], cfg["experts"], cfg["vocab"]
+    qd, kvd = cfg["heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
+    ts = tensor_seed
+    w = dict(embed=values_bf16(V * H, ts(seed, -1, T_EMBED), embed_std).reshape(V, H),
+             norm=bf16_f32(H, ts(seed, -1, T_NORM), norm_std, 1.0), layers=[])
+    for l in range(cfg["layers"]):
+        w["layers"].append(dict(
+            ln_attn=bf16_f32(H, ts(seed, l, T_LN_ATTN), norm_std, 1.0),
+            ln_moe=bf16_f32(H, ts(seed, l, T_LN_MOE), norm_std, 1.0),
+            q=q8_0(qd, H, ts(seed, l, T_Q)), k=q8_0(kvd, H, ts(seed, l, T_K)), v=q8_0(kvd, H, ts(seed, l, T_V)),
+            o=q8_0(H, qd, ts(seed, l, T_O)), router=q8_0(E, H, ts(seed, l, T_ROUTER)),
+            gate_up=q8_0(E * 2 * I, H, ts(seed, l, T_GATE_UP)).reshape(E, 2 * I, -1),
+            down=q8_0(E * H, I, ts(seed, l, T_DOWN)).reshape(E, H, -1)))
+    return w
+
+
+def dequant_model(wq):
+    """The Q8_0 model of model_weights_q8 as f32 arrays (the dequantised path, for transformers)."""
+    def conv(key, a):
+        return a.astype(np.float32) if key.startswith("ln") else q8_dequant(a)
+    return dict(embed=bf16_to_f32(wq["embed"]), norm=wq["norm"].astype(np.float32),
+                layers=[{k: conv(k, v) for k, v in lw.items()} for lw in wq["layers"]])
+
+
 def as_bits(w):
     """The same weights as bf16 bit arrays (uint16) with f32 norms, the form the oracle and the library take."""
     def conv(key, a):

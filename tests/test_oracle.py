@@ -10,7 +10,8 @@ import oracle as O
 import synth_np as S
 
 
-from helpers import values, values_py  # noqa: E402
+from helpers import reference_tiny_weights, values, values_py  # noqa: E402
+from lastro_b200 import configs as CFG  # noqa: E402
 
 
 def bf(v):
@@ -211,3 +212,22 @@ def test_synthetic_generator_matches_numpy_restatement():
 def test_reference_test_data_generator_c_matches_python():
     for seed in (1, 2, 3, 11, 77, 300):
         assert np.array_equal(values(1000, seed), values_py(1000, seed))
+
+
+def test_session_kv_bf16_stores_rounded_rows_of_the_f32_session(pool):
+    """kv_bf16 sessions keep the K/V rows an f32 session computes, rounded to bf16 (RNE), as the paged bf16 cache
+    stores them; the first position's rows are computed before any rounding can feed back, so they match exactly."""
+    cfg = CFG.TINY
+    w = reference_tiny_weights(cfg)
+    m = O.Model(cfg, weights=w)
+    a, b = O.Session(m, pool, 8), O.Session(m, pool, 8, kv_bf16=True)
+    for tok in (3, 9, 1):
+        a.step(tok)
+        b.step(tok)
+    for layer in range(cfg["layers"]):
+        for fa, fb in zip(a.kv(layer), b.kv(layer)):
+            assert not (fb.view(np.uint32) & 0xFFFF).any()  # bf16-representable
+            want = S.bf16_to_f32(O.f32_to_bf16(fa[0]))
+            assert np.array_equal(fb[0], want)
+    for o in (a, b, m):
+        o.close()
