@@ -30,13 +30,15 @@ import sys
 import tempfile
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "lastro-rust_b200"))
 
 from lastro_b200 import configs as CFG  # noqa: E402
 
 KERNELS = ("qkv_rope", "attention", "oproj", "router", "gate_up", "down", "head", "fused_step")
-WORKLOADS = {"c3": CFG.C3_3B, "c4": CFG.C4_3B_Q8}
+WORKLOADS = {"c3": CFG.C3_3B, "c4": CFG.C4_3B_Q8, "c5": CFG.C5_BATCH}
 
 
 def metric_name(c, context):
@@ -51,7 +53,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", choices=("lastro", "reference"), default="lastro")
     ap.add_argument("--workload", choices=tuple(WORKLOADS), default="c3",
-                    help="c3: bf16 weights, ctx 2048 (the headline); c4: Q8_0 weights, ctx 512")
+                    help="c3: bf16 weights, ctx 2048 (the headline); c4: Q8_0 weights, ctx 512; c5: 64 sequences x "
+                         "ctx 1024, Zipf expert load, experts partitioned over the torchrun ranks")
     ap.add_argument("--context", type=int, default=None, help="context length (default: the workload's)")
     ap.add_argument("--kv", choices=("bf16", "f32"), default="bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -177,14 +180,17 @@ def run_reference(a):
         return 0
     c = WORKLOADS[a.workload]
     cfg = c["model"]
-    rate, threads, n, sample = cpu_decode_rate(cfg, a.context, c["weight_seed"], 0, steps=a.steps,
-                                               warmup=min(a.warmup, 2))
+    if a.workload == "c5":
+        rate, threads, n, sample = cpu_batched_rate(cfg, a.context, c, steps=min(a.steps, 2))
+    else:
+        rate, threads, n, sample = cpu_decode_rate(cfg, a.context, c["weight_seed"], 0, steps=a.steps,
+                                                   warmup=min(a.warmup, 2))
     line = {
-        "impl": "reference", "metric": metric_name(c, a.context), "value": rate,
+        "impl": "reference", "metric": metric_name(c, a.context) if a.workload != "c5" else BATCH_METRIC, "value": rate,
         "unit": "tok/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1000.0 / rate,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": cfg.get("weight_dtype", "bf16"), "data": "synthetic",
-        "config": {"workload": c["name"], "context": a.context, "batch": 1},
+        "config": {"workload": c["name"], "context": a.context, "batch": c.get("batch", 1)},
         "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference (Rust + cuTile, rust/moe-rt) cannot be built here; its CPU path is timed through the "
@@ -194,10 +200,185 @@ def run_reference(a):
     return 0
 
 
+BATCH_METRIC = "decode tok/s (bs64) Granite-3B-A800M shape, ctx 1024, Zipf(0.8) expert load"
+
+
+def cpu_batched_rate(cfg, context, c, steps=2, seqs=4):
+    """The oracle decoding `seqs` of the batch's sequences (each its own session: a CPU path has no batching, its
+    tokens/s is the per-token rate) at `context` with the Zipf router bias: (tok/s, threads, tokens, sample)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    threads = os.cpu_count() or 1
+    om = O.Model(cfg, synthetic_seed=c["weight_seed"], std=CFG.WEIGHT_STD, norm_std=0.0, threads=threads)
+    om.set_router_bias(CFG.zipf_router_bias(cfg))
+    pool = O.Pool(threads)
+    ss = [O.Session(om, pool, context + steps + 2) for _ in range(seqs)]
+    for q, s in enumerate(ss):
+        s.fill_kv(context, c["prompt_seed"] + q, 0.5)
+    toks = CFG.synthetic_tokens(seqs, c["prompt_seed"], cfg["vocab"])
+    n, t0 = 0, time.time()
+    for _ in range(steps):
+        for q, s in enumerate(ss):
+            lg, _, _ = s.step(toks[q])
+            toks[q] = O.argmax_last(lg)
+            n += 1
+    el = time.time() - t0
+    for s in ss:
+        s.close()
+    om.close()
+    pool.close()
+    sample = (f"{n} tokens: {seqs} sequences x {steps} greedy steps of the full model at context {context} (K/V rows "
+              "synthetic), one CPU session per sequence")
+    return n / el, threads, n, sample
+
+
+def run_batched(a):
+    """C5: 64 sequences (64/N per rank) with 1024-token contexts decode together; every layer's MoE pairs go to the
+    rank that owns their expert (experts 40/N per rank, contiguous) through the peer-memory exchange."""
+    import torch
+    import torch.distributed as dist
+
+    import lastro_b200 as LB
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    c = CFG.C5_BATCH
+    cfg = c["model"]
+    K, W = a.steps, a.warmup
+    total = c["batch"]
+    mine = list(CFG.shard(total, rank, world))
+    n = len(mine)
+    stream = torch.cuda.Stream()
+    ctx = LB.Context(local, stream.cuda_stream)
+    model = LB.GpuModel(ctx, cfg, 8, kv_dtype=a.kv)
+    model.fill_synthetic(c["weight_seed"], CFG.WEIGHT_STD, 0.0)
+    max_len = a.context + W + 2 * K + 8
+    batch = LB.GpuBatch(model, n, max_len, rank, world)
+    if world > 1:
+        handles = [None] * world
+        dist.all_gather_object(handles, batch.exchange_handle())
+        batch.connect(handles)
+    else:
+        batch.connect()
+    batch.set_router_bias(CFG.zipf_router_bias(cfg))
+    seqs = list(range(n))
+    t0 = time.time()
+    if a.synthetic_kv:
+        for q in seqs:
+            batch.fill_kv_synthetic(q, a.context, c["prompt_seed"] + mine[q], 0.5)
+        toks = [int(t) for t in CFG.synthetic_tokens(n, c["prompt_seed"] + 7 * rank, cfg["vocab"])]
+    else:
+        prompts = [CFG.synthetic_tokens(a.context, c["prompt_seed"] + g, cfg["vocab"]) for g in mine]
+        for t in range(a.context):  # teacher-forced prefill of the contexts, one batched step per position
+            nxt, _, _ = batch.step(seqs, [p[t] for p in prompts])
+        toks = [int(x) for x in nxt]
+    prefill_s = time.time() - t0
+    # expert load of one step: share of the token-expert pairs each rank's experts receive (all ranks' tokens)
+    nxt, _, routes = batch.step(seqs, toks, want_routes=True)
+    toks = [int(x) for x in nxt]
+    counts = np.bincount(routes.ravel(), minlength=cfg["experts"]).astype(np.int64)
+    if world > 1:
+        tc = torch.tensor(counts, device="cuda")
+        dist.all_reduce(tc)
+        counts = tc.cpu().numpy()
+    batch.decode(seqs, toks, W, want_ids=False)
+    toks = [int(x) for x in batch.decode(seqs, toks, 1)[-1]]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx0 = batch.position(0)
+    ev0.record(stream)
+    ids = batch.decode(seqs, toks, K)
+    ev1.record(stream)
+    stream.synchronize()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    toks = [int(x) for x in ids[-1]]
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    value = total * K / (ms / 1000.0)
+    # end to end through the public step call: token ids host -> device, next ids device -> host, every step
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(K):
+        nxt, _, _ = batch.step(seqs, toks)
+        toks = [int(x) for x in nxt]
+    e1.record(stream)
+    stream.synchronize()
+    e2e_ms = max(e0.elapsed_time(e1), (time.perf_counter() - w0) * 1000.0)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    mean_ctx = ctx0 + (K + 1) / 2.0
+    H, I, L, E, kk = cfg["hidden"], cfg["inter"], cfg["layers"], cfg["experts"], cfg["k"]
+    qd, kvd = cfg["heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
+    touched = int((counts > 0).sum())
+    expert_b = L * touched * 3 * I * H * 2
+    kv_b = L * total * 2 * kvd * 2 * mean_ctx
+    dense_b = L * ((qd + 2 * kvd) * H + H * qd + E * H) * 2 + cfg["vocab"] * H * 2
+    step_bytes = expert_b + kv_b + world * dense_b  # every rank streams the replicated dense weights
+    step_s = ms / 1000.0 / K
+    hbm, peak_kind = peaks()
+    achieved = step_bytes / world / step_s / 1e9  # per GPU
+    share = [float(counts[list(CFG.shard(E, r, world))].sum() / counts.sum()) for r in range(world)]
+    line = {
+        "metric": BATCH_METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": c["name"], "batch": total, "seqs_per_rank": n, "context_start": ctx0,
+                   "mean_context": mean_ctx, "kv_cache": f"paged {a.kv}",
+                   "parallelism": f"ep{world}: experts {E // world}/rank, attention data-parallel over sequences"
+                   if world > 1 else "single GPU",
+                   "weights": "bf16; batched GEMMs on tensor cores (mma.sync bf16, activations split hi + lo)",
+                   "expert_load_share_by_rank": [round(x, 4) for x in share], "experts_touched": touched,
+                   "router_bias": "Zipf(0.8), beta 0.8", "prefill": "synthetic KV" if a.synthetic_kv else
+                   "teacher-forced batched steps", "prefill_s": round(prefill_s, 2),
+                   "l2": f"inputs larger than L2: every step streams ~{step_bytes / 1e9:.1f} GB (L2 126 MB)"},
+        "roofline": {"bound": "hbm", "kernel": "batched step (all kernels)", "achieved": achieved, "peak": hbm,
+                     "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": None,
+                     "bytes_per_step": step_bytes, "bytes_note": "touched experts + KV of all sequences + the dense "
+                     "weights every rank streams; per GPU"},
+        "e2e": {"value": total * K / (e2e_ms / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": 8 * n,
+                "d2h_bytes_per_step": 4 * n},
+        "gpu_launches": K * (L * 12 + 3),
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        rate, threads, nt, sample = cpu_batched_rate(cfg, a.context, c)
+        line["cpu_baseline"] = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
+    batch.close()
+    model.close()
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     a = parse()
     if a.impl == "reference":
         return run_reference(a)
+    if a.workload == "c5":
+        return run_batched(a)
 
     import torch
     import torch.distributed as dist

@@ -138,6 +138,39 @@ int lastro_model_set_options(lastro_model *model, int32_t use_graphs, int32_t us
 int lastro_model_fused(const lastro_model *model);
 void lastro_model_destroy(lastro_model *model);
 
+/* ---- batched decode with expert parallelism (no counterpart in the reference, which decodes one sequence) ------- */
+/* Many independent sequences decoded together on a model's weights (bf16); each sequence's results equal its own
+ * single-sequence step up to summation order (the reference's multi-position contract, cpu.rs:234-238).  The MoE
+ * experts are partitioned over the `world` ranks of an expert-parallel group, one process per GPU: rank r computes the
+ * experts [r*E/world, (r+1)*E/world) for the pairs every rank routes to them, while attention and the dense layers stay
+ * with each rank's own sequences.  Every rank creates its batch with the same max_seqs and world, passes the handle
+ * of its exchange region (lastro_batch_exchange_handle, 64 bytes) to the others, and connects with all of them in rank
+ * order (lastro_batch_connect; world 1: handles may be NULL).  The ranks then call lastro_batch_step/decode the same
+ * number of times, each with at least one of its own sequences.  Destroy a batch before its model.  A rank that does
+ * not arrive makes the others' waits give up after 10 s (LASTRO_E_CUDA, batch poisoned). */
+typedef struct lastro_batch lastro_batch;
+int lastro_batch_create(lastro_model *model, int32_t max_seqs, int32_t max_len, int32_t rank, int32_t world,
+                        lastro_batch **out);
+int lastro_batch_exchange_handle(lastro_batch *batch, void *handle, int32_t bytes);
+int lastro_batch_connect(lastro_batch *batch, const void *handles, int32_t bytes_each);
+/* per-layer router logit bias [layers, experts] added before the top-k (NULL removes it): a workload knob for skewed
+ * expert load; Granite's router has no bias */
+int lastro_batch_set_router_bias(lastro_batch *batch, const float *bias);
+/* one token for each of n distinct sequences (ids < max_seqs): next [n] greedy ids (last maximum), logits [n, V] and
+ * route_ids [n, layers, k] when non-NULL */
+int lastro_batch_step(lastro_batch *batch, int32_t n, const int32_t *seq_ids, const int32_t *tokens, int32_t *next,
+                      float *logits, int32_t *route_ids);
+/* `steps` greedy steps of the n sequences on the device, each step's ids fed back as the next step's tokens;
+ * out_ids [steps, n] when non-NULL */
+int lastro_batch_decode(lastro_batch *batch, int32_t n, const int32_t *seq_ids, const int32_t *tokens, int32_t steps,
+                        int32_t *out_ids);
+/* a context of n positions with synthetic K/V for sequence `seq` (benchmarks and profiling) */
+int lastro_batch_fill_kv_synthetic(lastro_batch *batch, int32_t seq, int32_t n, uint64_t seed, float stddev);
+int lastro_batch_reset(lastro_batch *batch, int32_t seq);
+int lastro_batch_position(const lastro_batch *batch, int32_t seq, int32_t *pos);
+int lastro_batch_set_options(lastro_batch *batch, int32_t use_graphs);
+void lastro_batch_destroy(lastro_batch *batch);
+
 #ifdef __cplusplus
 }
 #endif

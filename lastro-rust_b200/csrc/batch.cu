@@ -1,0 +1,672 @@
+// Batched decode step kernels (see batch.h for the step's order and the exchange region).
+#include <cuda_bf16.h>
+
+#include "batch.h"
+#include "common.cuh"
+#include "kernels.h"
+#include "ops.cuh"
+
+namespace lastro {
+
+namespace {
+
+// ---- tensor-core GEMM helpers ----------------------------------------------------------------------------------
+// 16-byte global -> shared copy; `valid` false fills the 16 bytes with zeros (nothing is read)
+LDEV void cp_async16(uint32_t dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+LDEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+LDEV void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+LDEV void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+// d += a (16x16, row) * b (16x8, col), bf16 operands, f32 accumulators
+LDEV void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// shared tiles are rows of 64 bf16 (128 bytes = 8 chunks of 16 bytes); chunk c of row r sits at c ^ (r & 7) so that
+// the 8 rows one ldmatrix phase reads fall in 8 different bank groups
+LDEV uint32_t swz(int row, int chunk) { return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4)); }
+
+LDEV void split_bf16(float v, uint16_t& hi, uint16_t& lo) {
+    hi = f32_to_bf16_rne(v);
+    lo = f32_to_bf16_rne(__fsub_rn(v, __uint_as_float((uint32_t)hi << 16)));
+}
+
+// ---- bounded waits on flags written by other GPUs ---------------------------------------------------------------
+LDEV uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+LDEV unsigned int ld_acquire_sys(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+LDEV void st_release_sys(unsigned int* p, unsigned int v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Waits until *flag reaches `want` (epochs only grow), at most kFlagWaitNs; on time-out records `code` and fails.
+constexpr uint64_t kFlagWaitNs = 10ull * 1000 * 1000 * 1000;
+LDEV bool wait_flag(const unsigned int* flag, unsigned int want, int* err, int code) {
+    const uint64_t t0 = global_ns();
+    while ((int)(ld_acquire_sys(flag) - want) < 0) {
+        if (global_ns() - t0 > kFlagWaitNs) {
+            atomicExch(err, code);
+            return false;
+        }
+        __nanosleep(64);
+    }
+    return true;
+}
+
+// last-CTA election across a grid whose CTAs wrote to other GPUs: system-scope fence first
+LDEV bool last_block_arrives_sys(unsigned int* counter, unsigned int total, bool* flag_smem) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int t = atomicAdd(counter, 1u);
+        const bool last = (t == total - 1);
+        if (last) atomicExch(counter, 0u);
+        *flag_smem = last;
+    }
+    __syncthreads();
+    const bool last = *flag_smem;
+    if (last) __threadfence_system();
+    return last;
+}
+
+LDEV unsigned int* flag_ptr(unsigned char* region, const XLayout& L, int kind, int who) {
+    return reinterpret_cast<unsigned int*>(region + L.flags + ((size_t)kind * 64 + who) * 128);
+}
+
+}  // namespace
+
+XLayout x_layout(int world, int tokens_per_rank, int k, int H) {
+    auto up = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    XLayout L{};
+    L.cap = tokens_per_rank * k;
+    size_t o = 0;
+    L.rx = o;
+    o = up(o + (size_t)world * L.cap * H * 4);
+    L.rx_ids = o;
+    o = up(o + (size_t)world * L.cap * 4);
+    L.rx_n = o;
+    o = up(o + (size_t)world * 4);
+    L.cb = o;
+    o = up(o + (size_t)L.cap * H * 4);
+    L.flags = o;
+    o = up(o + (size_t)2 * 64 * 128);
+    L.bytes = o;
+    return L;
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// GEMM: y[pos][row] = sum_k W[row][k] * x[pos][k] for the weight rows of one CTA (128, or 64 gate + 64 up rows) and
+// all tokens of its group, tiles of 64 tokens at a time.  4 warps; warp w owns rows {16w..16w+15} of each 64-row half
+// (m-tiles mt = 0, 1), so a SwiGLU thread holds gate and up of the same (row, token).  K streams through a 3-stage
+// cp.async pipeline in chunks of 64; per 16-wide K step a warp loads its A fragments (ldmatrix.x4) once and issues
+// 2 m-tiles x 8 token n-tiles x {hi, lo} mma.sync.
+// ------------------------------------------------------------------------------------------------------------------
+template <int EPI>
+__global__ void __launch_bounds__(128) bgemm_kernel(BGemmArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = blockIdx.y, bx = blockIdx.x;
+    int p0 = 0, ntot = a.n;
+    if (a.g_cnt) {
+        p0 = __ldcg(a.g_off + g);
+        ntot = __ldcg(a.g_cnt + g);
+    }
+    if (ntot <= 0) return;
+    const uint16_t* W = a.w + (size_t)(a.group0 + g) * a.group_stride;
+    const int kbeg = blockIdx.z * a.k_split;
+    const int nk = min(a.k_split, a.K - kbeg) / kBK;
+    if (nk <= 0) return;
+    const int ch = tid & 7;
+    // this thread's 8 weight rows in the tile (fixed for the CTA)
+    auto grow_of = [&](int sr) -> int {
+        if (EPI == BEPI_SWIGLU) return sr < 64 ? bx * 64 + sr : a.I + bx * 64 + (sr - 64);
+        return bx * kBRows + sr;
+    };
+
+    for (int t0 = 0; t0 < ntot; t0 += kBTok) {
+        const int n = min(kBTok, ntot - t0);
+        int xrow[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int tok = (tid >> 3) + 16 * i;
+            const int p = p0 + t0 + tok;
+            xrow[i] = tok < n ? (a.x_rows ? __ldcg(a.x_rows + p) : p) : 0;
+        }
+        auto load_stage = [&](int slot, int kt) {
+            unsigned char* st = smem + (size_t)slot * kBStageBytes;
+            const int k0 = kbeg + kt * kBK + ch * 8;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int sr = (tid >> 3) + 16 * i;
+                const int gr = grow_of(sr);
+                const bool v = gr < a.rows;
+                cp_async16(smem_addr(st) + swz(sr, ch), W + (size_t)(v ? gr : 0) * a.K + k0, v);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int tok = (tid >> 3) + 16 * i;
+                const bool v = tok < n;
+                const size_t xo = (size_t)xrow[i] * a.ldx + k0;
+                const uint32_t d = swz(tok, ch);
+                cp_async16(smem_addr(st + kBRows * 128) + d, a.x_hi + xo, v);
+                cp_async16(smem_addr(st + kBRows * 128 + kBTok * 128) + d, a.x_lo + xo, v);
+            }
+        };
+
+        float acc[2][8][4];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[mt][j][c] = 0.0f;
+        const int ntp = (n + 15) >> 4;  // active pairs of 8-token n-tiles
+
+        if (t0 > 0) __syncthreads();  // the previous tile's last stage reads are done
+#pragma unroll
+        for (int s = 0; s < kBStages - 1; ++s) {
+            if (s < nk) load_stage(s, s);
+            cp_async_commit();
+        }
+        for (int kt = 0; kt < nk; ++kt) {
+            cp_async_wait<kBStages - 2>();
+            __syncthreads();
+            const int pf = kt + kBStages - 1;
+            if (pf < nk) load_stage(pf % kBStages, pf);
+            cp_async_commit();
+            const uint32_t sW = smem_addr(smem + (size_t)(kt % kBStages) * kBStageBytes);
+            const uint32_t sXh = sW + kBRows * 128, sXl = sXh + kBTok * 128;
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+                const int mi = lane >> 3, r8 = lane & 7;
+                uint32_t af[2][4];
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt) {
+                    const int sr = mt * 64 + warp * 16 + (mi & 1) * 8 + r8;
+                    ldsm_x4(sW + swz(sr, kk * 2 + (mi >> 1)), af[mt]);
+                }
+#pragma unroll
+                for (int jp = 0; jp < 4; ++jp) {
+                    if (jp < ntp) {
+                        const int tok = (2 * jp + (mi >> 1)) * 8 + r8;
+                        const uint32_t off = swz(tok, kk * 2 + (mi & 1));
+                        uint32_t bh[4], bl[4];
+                        ldsm_x4(sXh + off, bh);
+                        ldsm_x4(sXl + off, bl);
+#pragma unroll
+                        for (int mt = 0; mt < 2; ++mt) {
+                            mma_bf16(acc[mt][2 * jp], af[mt], bh[0], bh[1]);
+                            mma_bf16(acc[mt][2 * jp], af[mt], bl[0], bl[1]);
+                            mma_bf16(acc[mt][2 * jp + 1], af[mt], bh[2], bh[3]);
+                            mma_bf16(acc[mt][2 * jp + 1], af[mt], bl[2], bl[3]);
+                        }
+                    }
+                }
+            }
+        }
+        cp_async_wait<0>();
+
+        // epilogue: acc[mt][j][c] is (tile row mt*64 + 16 warp + lane/4 + 8 (c >= 2), token 8 j + 2 (lane % 4) + c % 2)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (j * 8 >= n) break;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int tok = j * 8 + (lane & 3) * 2 + (c & 1);
+                if (tok >= n) continue;
+                const int rr = warp * 16 + (lane >> 2) + ((c >> 1) << 3);  // row within a 64-row half
+                const size_t p = (size_t)(p0 + t0 + tok);
+                if (EPI == BEPI_SWIGLU) {
+                    const float gv = acc[0][j][c], uv = acc[1][j][c];
+                    const float v = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
+                    uint16_t hi, lo;
+                    split_bf16(v, hi, lo);
+                    const size_t o = p * a.I + bx * 64 + rr;
+                    a.a_hi[o] = hi;
+                    a.a_lo[o] = lo;
+                } else {
+#pragma unroll
+                    for (int mt = 0; mt < 2; ++mt) {
+                        const int gr = bx * kBRows + mt * 64 + rr;
+                        if (gr < a.rows)
+                            a.y[blockIdx.z * a.z_stride + p * a.ldy + gr] = a.div == 1.0f ? acc[mt][j][c]
+                                                                                            : __fdiv_rn(acc[mt][j][c], a.div);
+                    }
+                }
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// attention norm: h = embedding row x multiplier (layer 0) or the residual stream; xn = ln * (h * r) split hi + lo
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) battn_norm_kernel(BNormArgs a) {
+    constexpr int BLOCK = 256, NV = 2;  // H <= 2048
+    __shared__ float red[BLOCK / 32];
+    const int t = blockIdx.x;
+    float* h = a.h + (size_t)t * a.H;
+    float4 v[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int i = threadIdx.x + k * BLOCK;
+        v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (4 * i >= a.H) continue;
+        if (a.embed) {
+            const int tok = __ldg(a.tokens + t);
+            const uint2 u = __ldg(reinterpret_cast<const uint2*>(a.embed + (size_t)tok * a.H) + i);
+            v[k] = make_float4(__fmul_rn(bf_lo(u.x), a.emb_mult), __fmul_rn(bf_hi(u.x), a.emb_mult),
+                               __fmul_rn(bf_lo(u.y), a.emb_mult), __fmul_rn(bf_hi(u.y), a.emb_mult));
+            reinterpret_cast<float4*>(h)[i] = v[k];
+        } else {
+            v[k] = __ldcg(reinterpret_cast<const float4*>(h) + i);
+        }
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        ss = fmaf(v[k].x, v[k].x, ss);
+        ss = fmaf(v[k].y, v[k].y, ss);
+        ss = fmaf(v[k].z, v[k].z, ss);
+        ss = fmaf(v[k].w, v[k].w, ss);
+    }
+    const float tot = block_sum(ss, red);
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.H), a.eps)));
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int i = threadIdx.x + k * BLOCK;
+        if (4 * i >= a.H) continue;
+        const float4 ln = __ldg(reinterpret_cast<const float4*>(a.ln) + i);
+        const float4 x = ln_times(ln, v[k], r);
+        ushort4 hi, lo;
+        split_bf16(x.x, hi.x, lo.x);
+        split_bf16(x.y, hi.y, lo.y);
+        split_bf16(x.z, hi.z, lo.z);
+        split_bf16(x.w, hi.w, lo.w);
+        reinterpret_cast<ushort4*>(a.x_hi + (size_t)t * a.H)[i] = hi;
+        reinterpret_cast<ushort4*>(a.x_lo + (size_t)t * a.H)[i] = lo;
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// RoPE + KV append: the q/k/v partial slices summed in slice order, then per RoPE pair (j, j + d/2) of each head
+// x1*c - x2*s, x2*c + x1*s (model.rs:153-155); q to its buffer, K (roped) and V to the token's sequence page.
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) brope_kv_kernel(BRopeArgs a) {
+    const int t = blockIdx.x;
+    const int R = a.qd + 2 * a.kvd, half = a.d >> 1;
+    const int sq = __ldg(a.seq + t);
+    const int pos = __ldcg(a.pos + sq);
+    const float* cs = a.rope_cs + (size_t)pos * a.d;
+    const int page = __ldg(a.page_table + (size_t)sq * a.pt_stride + pos / a.page_size), slot = pos % a.page_size;
+    for (int pi = threadIdx.x; pi < R / 2; pi += blockDim.x) {
+        const int head = pi / half, j = pi - head * half;
+        const int r0 = head * a.d + j, r1 = r0 + half;
+        float x1 = 0.0f, x2 = 0.0f;
+        for (int z = 0; z < a.ks; ++z) {
+            const float* pz = a.part + ((size_t)z * a.n + t) * R;
+            x1 = __fadd_rn(x1, __ldcg(pz + r0));
+            x2 = __fadd_rn(x2, __ldcg(pz + r1));
+        }
+        const float c = __ldg(cs + j), s = __ldg(cs + half + j);
+        const float ro0 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+        const float ro1 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+        if (r0 < a.qd) {
+            a.q[(size_t)t * a.qd + r0] = ro0;
+            a.q[(size_t)t * a.qd + r1] = ro1;
+            continue;
+        }
+        int rr = r0 - a.qd;
+        const bool is_k = rr < a.kvd;
+        if (!is_k) rr -= a.kvd;
+        const int kvh = rr / a.d;
+        const float v0 = is_k ? ro0 : x1, v1 = is_k ? ro1 : x2;
+        const size_t base = (((size_t)page * a.kv_heads + kvh) * a.page_size + slot) * a.d;
+        void* pool = is_k ? a.k_pool : a.v_pool;
+        if (a.kv_f32) {
+            float* p = static_cast<float*>(pool) + base;
+            p[j] = v0;
+            p[j + half] = v1;
+        } else {
+            uint16_t* p = static_cast<uint16_t*>(pool) + base;
+            p[j] = f32_to_bf16_rne(v0);
+            p[j + half] = f32_to_bf16_rne(v1);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// router: h += resid * (o-projection slices summed in order); xn = RMSNorm(h) (f32, kept for the router, split hi + lo
+// for the experts); logits_e = W_r[e] . xn (+ bias_e), one warp per expert; top-k in block.rs:81-89's order, softmax.
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) brouter_kernel(BRouterArgs a) {
+    constexpr int BLOCK = 256, NV = 2;
+    extern __shared__ __align__(16) float xs[];  // [H]
+    __shared__ float red[BLOCK / 32];
+    __shared__ float lg[kMaxExperts];
+    __shared__ int sid[kMaxTopK];
+    __shared__ float sval[kMaxTopK], sw[kMaxTopK];
+    const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float* h = a.h + (size_t)t * a.H;
+    float4 v[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int i = threadIdx.x + k * BLOCK;
+        v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (4 * i >= a.H) continue;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int z = 0; z < a.ks; ++z) {
+            const float4 p = __ldcg(reinterpret_cast<const float4*>(a.opart + ((size_t)z * a.n + t) * a.H) + i);
+            o.x = __fadd_rn(o.x, p.x);
+            o.y = __fadd_rn(o.y, p.y);
+            o.z = __fadd_rn(o.z, p.z);
+            o.w = __fadd_rn(o.w, p.w);
+        }
+        const float4 hv = __ldcg(reinterpret_cast<const float4*>(h) + i);
+        v[k] = make_float4(__fadd_rn(hv.x, __fmul_rn(a.resid, o.x)), __fadd_rn(hv.y, __fmul_rn(a.resid, o.y)),
+                           __fadd_rn(hv.z, __fmul_rn(a.resid, o.z)), __fadd_rn(hv.w, __fmul_rn(a.resid, o.w)));
+        reinterpret_cast<float4*>(h)[i] = v[k];
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        ss = fmaf(v[k].x, v[k].x, ss);
+        ss = fmaf(v[k].y, v[k].y, ss);
+        ss = fmaf(v[k].z, v[k].z, ss);
+        ss = fmaf(v[k].w, v[k].w, ss);
+    }
+    const float tot = block_sum(ss, red);
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.H), a.eps)));
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int i = threadIdx.x + k * BLOCK;
+        if (4 * i >= a.H) continue;
+        const float4 x = ln_times(__ldg(reinterpret_cast<const float4*>(a.ln) + i), v[k], r);
+        reinterpret_cast<float4*>(xs)[i] = x;
+        ushort4 hi, lo;
+        split_bf16(x.x, hi.x, lo.x);
+        split_bf16(x.y, hi.y, lo.y);
+        split_bf16(x.z, hi.z, lo.z);
+        split_bf16(x.w, hi.w, lo.w);
+        reinterpret_cast<ushort4*>(a.x_hi + (size_t)t * a.H)[i] = hi;
+        reinterpret_cast<ushort4*>(a.x_lo + (size_t)t * a.H)[i] = lo;
+    }
+    __syncthreads();
+    for (int e = warp; e < a.E; e += BLOCK / 32) {
+        const uint16_t* row = a.wr + (size_t)e * a.H;
+        float acc = 0.0f;
+        for (int c = lane * 8; c < a.H; c += 256) {
+            const uint4 w = ld_weight(row + c);
+            const float4 xa = *reinterpret_cast<const float4*>(xs + c);
+            const float4 xb = *reinterpret_cast<const float4*>(xs + c + 4);
+            acc = dot8(w, xa, xb, acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) lg[e] = a.bias ? __fadd_rn(acc, __ldg(a.bias + e)) : acc;
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    const float v0 = lane < a.E ? lg[lane] : 0.0f;
+    const float v1 = lane + 32 < a.E ? lg[lane + 32] : 0.0f;
+    route_topk_warp(v0, v1, a.E, a.k, sid, sval, sw);
+    if (lane < a.k) {
+        a.ids[(size_t)t * a.k + lane] = sid[lane];
+        a.weights[(size_t)t * a.k + lane] = sw[lane];
+        if (a.route_hist) a.route_hist[((size_t)t * a.layers + a.layer) * a.k + lane] = sid[lane];
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// dispatch: CTA per (token, slot) pair: the token's MoE input row (hi then lo) to the exchange region of the rank that
+// owns the pair's expert, at [sender = this rank][pair]; CTA 0 also writes this rank's routing (ids, token count) to
+// every rank.  The last CTA publishes the dispatch flag of this rank on every rank.
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) ep_dispatch_kernel(BExchangeArgs a) {
+    __shared__ bool is_last;
+    const int p = blockIdx.x;  // pair index t * k + j (grid covers cap pairs; pairs past n * k only vote)
+    const XLayout& L = a.lay;
+    const unsigned int epoch = __ldcg(a.epoch_base) + a.layer + 1;
+    if (p < a.n * a.k) {
+        const int t = p / a.k;
+        const int e = __ldcg(a.ids + p);
+        const int owner = min(max(e / a.experts_per_rank, 0), a.world - 1);
+        unsigned char* dst = a.peers[owner] + L.rx + ((size_t)a.rank * L.cap + p) * (size_t)a.H * 4;
+        const uint4* sh = reinterpret_cast<const uint4*>(a.x_hi + (size_t)t * a.H);
+        const uint4* sl = reinterpret_cast<const uint4*>(a.x_lo + (size_t)t * a.H);
+        const int nc = a.H / 8;  // 16-byte chunks per half row
+        for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+            reinterpret_cast<uint4*>(dst)[c] = __ldcg(sh + c);
+            reinterpret_cast<uint4*>(dst)[nc + c] = __ldcg(sl + c);
+        }
+    }
+    if (p == 0) {
+        for (int q = 0; q < a.world; ++q) {
+            int* ids = reinterpret_cast<int*>(a.peers[q] + L.rx_ids) + (size_t)a.rank * L.cap;
+            for (int i = threadIdx.x; i < a.n * a.k; i += blockDim.x) ids[i] = __ldcg(a.ids + i);
+            if (threadIdx.x == 0) reinterpret_cast<int*>(a.peers[q] + L.rx_n)[a.rank] = a.n;
+        }
+    }
+    if (!last_block_arrives_sys(a.counter, gridDim.x, &is_last)) return;
+    if (threadIdx.x < a.world) st_release_sys(flag_ptr(a.peers[threadIdx.x], L, 0, a.rank), epoch);
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// group (owner, one CTA): after every sender's dispatch flag, the received pairs whose expert is local are ordered by
+// (local expert, sender, pair): per expert offsets and counts for the grouped GEMMs, and per position its rx row.
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) ep_group_kernel(BExchangeArgs a) {
+    __shared__ short le[kBMaxSlots];
+    __shared__ int cnt[kMaxExperts], off[kMaxExperts];
+    __shared__ int ok_all;
+    const XLayout& L = a.lay;
+    unsigned char* me = a.peers[a.rank];
+    const unsigned int epoch = __ldcg(a.epoch_base) + a.layer + 1;
+    if (threadIdx.x == 0) ok_all = 1;
+    if (threadIdx.x < kMaxExperts) cnt[threadIdx.x] = 0;
+    __syncthreads();
+    if (threadIdx.x < a.world && !wait_flag(flag_ptr(me, L, 0, threadIdx.x), epoch, a.err, 10 + threadIdx.x))
+        atomicExch(&ok_all, 0);
+    __syncthreads();
+    const int slots = a.world * L.cap;
+    const int e0 = a.rank * a.experts_per_rank;
+    const int* rx_ids = reinterpret_cast<const int*>(me + L.rx_ids);
+    const int* rx_n = reinterpret_cast<const int*>(me + L.rx_n);
+    for (int i = threadIdx.x; i < slots; i += blockDim.x) {
+        const int s = i / L.cap, p = i - s * L.cap;
+        int x = -1;
+        if (ok_all && p < ld_acquire_sys(reinterpret_cast<const unsigned int*>(rx_n) + s) * a.k) {
+            const int e = __ldcg(rx_ids + i) - e0;
+            if (e >= 0 && e < a.experts_per_rank) {
+                x = e;
+                atomicAdd(&cnt[e], 1);
+            }
+        }
+        le[i] = (short)x;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int o = 0;
+        for (int e = 0; e < a.experts_per_rank; ++e) {
+            off[e] = o;
+            o += cnt[e];
+            a.g_off[e] = off[e];
+            a.g_cnt[e] = cnt[e];
+        }
+        *a.n_pos = o;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < slots; i += blockDim.x) {
+        const int e = le[i];
+        if (e < 0) continue;
+        int rank = 0;
+        for (int j = 0; j < i; ++j) rank += (le[j] == e);
+        const int pos = off[e] + rank;
+        a.x_rows[pos] = i;
+        a.src[pos] = i;
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// return (owner): CTA per position: the down-projection row back to its sender's combine rows, at the sender's pair
+// index; the last CTA publishes this rank's return flag on every rank.
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) ep_return_kernel(BExchangeArgs a) {
+    __shared__ bool is_last;
+    const XLayout& L = a.lay;
+    const unsigned int epoch = __ldcg(a.epoch_base) + a.layer + 1;
+    const int pos = blockIdx.x;
+    if (pos < __ldcg(a.n_pos)) {
+        const int i = __ldcg(a.src + pos);
+        const int s = i / L.cap, p = i - s * L.cap;
+        const float4* src = reinterpret_cast<const float4*>(a.y + (size_t)pos * a.H);
+        float4* dst = reinterpret_cast<float4*>(a.peers[s] + L.cb + (size_t)p * a.H * 4);
+        for (int c = threadIdx.x; c < a.H / 4; c += blockDim.x) dst[c] = __ldcg(src + c);
+    }
+    if (!last_block_arrives_sys(a.counter, gridDim.x, &is_last)) return;
+    if (threadIdx.x < a.world) st_release_sys(flag_ptr(a.peers[threadIdx.x], L, 1, a.rank), epoch);
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// combine (sender): CTA per token, after every owner's return flag: h += resid * sum_j w_j y_j, slots in routing
+// order (cpu.rs:231-238).
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) ep_combine_kernel(BExchangeArgs a) {
+    __shared__ int ok_all;
+    const XLayout& L = a.lay;
+    unsigned char* me = a.peers[a.rank];
+    const unsigned int epoch = __ldcg(a.epoch_base) + a.layer + 1;
+    const int t = blockIdx.x;
+    if (threadIdx.x == 0) ok_all = 1;
+    __syncthreads();
+    if (threadIdx.x < a.world && !wait_flag(flag_ptr(me, L, 1, threadIdx.x), epoch, a.err, 30 + threadIdx.x))
+        atomicExch(&ok_all, 0);
+    __syncthreads();
+    if (!ok_all) return;
+    float w[kMaxTopK];
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) w[j] = j < a.k ? __ldcg(a.weights + (size_t)t * a.k + j) : 0.0f;
+    const float* cb = reinterpret_cast<const float*>(me + L.cb) + (size_t)t * a.k * a.H;
+    float* h = a.h + (size_t)t * a.H;
+    for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j)
+            if (j < a.k) acc = __fadd_rn(acc, __fmul_rn(w[j], __ldcg(cb + (size_t)j * a.H + i)));
+        h[i] = __fadd_rn(__ldcg(h + i), __fmul_rn(a.resid, acc));
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// argmax per token (the last maximum, bin/m1b-gulosa.rs:22-24), position advanced, next token fed back
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) bargmax_kernel(BHeadArgs a) {
+    __shared__ unsigned long long best[8];
+    const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float* lg = a.logits + (size_t)t * a.V;
+    unsigned long long b = 0ull;
+    for (int v = threadIdx.x; v < a.V; v += blockDim.x) {
+        const unsigned long long key = arg_key(__ldcg(lg + v), v);
+        b = key > b ? key : b;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long x = shfl_xor_u64(b, o);
+        b = x > b ? x : b;
+    }
+    if (lane == 0) best[warp] = b;
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) b = best[w] > b ? best[w] : b;
+    b = best[0] > b ? best[0] : b;
+    const int id = (int)(uint32_t)b;
+    a.next[t] = id;
+    if (a.tokens) a.tokens[t] = id;
+    a.pos[__ldg(a.seq + t)] += 1;
+    if (t == 0) *a.epoch_base += (unsigned int)a.layers;
+}
+
+// ---- launchers ----------------------------------------------------------------------------------------------------
+template <typename Kern>
+cudaError_t set_smem(Kern k, size_t bytes) {
+    return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+cudaError_t launch_bgemm(const BGemmArgs& a, int epi, int groups, cudaStream_t s) {
+    if (a.K % kBK || a.k_split % kBK || a.k_split <= 0 || a.ldx % 8 || groups < 1) return cudaErrorInvalidValue;
+    const int ks = (a.K + a.k_split - 1) / a.k_split;
+    if (epi == BEPI_SWIGLU) {
+        if (a.I % 64 || a.rows != 2 * a.I || ks != 1) return cudaErrorInvalidValue;
+        cudaError_t e = set_smem(bgemm_kernel<BEPI_SWIGLU>, kBGemmSmem);
+        if (e != cudaSuccess) return e;
+        bgemm_kernel<BEPI_SWIGLU><<<dim3(a.I / 64, groups, 1), 128, kBGemmSmem, s>>>(a);
+    } else {
+        cudaError_t e = set_smem(bgemm_kernel<BEPI_STORE>, kBGemmSmem);
+        if (e != cudaSuccess) return e;
+        bgemm_kernel<BEPI_STORE><<<dim3((a.rows + kBRows - 1) / kBRows, groups, ks), 128, kBGemmSmem, s>>>(a);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_battn_norm(const BNormArgs& a, int n, cudaStream_t s) {
+    if (a.H % 4 || a.H > 2048 || n < 1) return cudaErrorInvalidValue;
+    battn_norm_kernel<<<n, 256, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_brope_kv(const BRopeArgs& a, cudaStream_t s) {
+    if (a.n < 1) return cudaErrorInvalidValue;
+    brope_kv_kernel<<<a.n, 128, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_brouter(const BRouterArgs& a, cudaStream_t s) {
+    if (a.H % 8 || a.H > 2048 || a.E > kMaxExperts || a.k > kMaxTopK || a.n < 1) return cudaErrorInvalidValue;
+    brouter_kernel<<<a.n, 256, sizeof(float) * a.H, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_dispatch(const BExchangeArgs& a, cudaStream_t s) {
+    if (a.world > 32 || a.H % 8) return cudaErrorInvalidValue;
+    ep_dispatch_kernel<<<a.lay.cap, 128, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_group(const BExchangeArgs& a, cudaStream_t s) {
+    if (a.world * a.lay.cap > kBMaxSlots || a.experts_per_rank > kMaxExperts) return cudaErrorInvalidValue;
+    ep_group_kernel<<<1, 1024, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_return(const BExchangeArgs& a, int max_positions, cudaStream_t s) {
+    ep_return_kernel<<<max_positions, 128, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_combine(const BExchangeArgs& a, cudaStream_t s) {
+    ep_combine_kernel<<<a.n, 256, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bargmax(const BHeadArgs& a, cudaStream_t s) {
+    bargmax_kernel<<<a.n, 256, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace lastro

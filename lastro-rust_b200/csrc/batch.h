@@ -1,0 +1,168 @@
+// Kernel arguments and launchers of the batched decode step (many independent sequences, one token each), with the
+// MoE experts partitioned over the ranks of an expert-parallel group.
+//
+// Per layer, on every rank for its own tokens:
+//   attn_norm    RMSNorm(h) (layer 0: the embedding row x multiplier) -> bf16 hi + lo split of xn
+//   gemm         [q;k;v] partial sums over K slices (tensor cores, split-K)
+//   rope_kv      slices summed in order -> RoPE -> q; K/V appended to each sequence's paged cache
+//   attention    the batch-1 split-KV kernel with a grid dimension over tokens; writes att split into hi + lo
+//   gemm         o-projection partial sums over K slices
+//   router       h += resid * sum of the slices; RMSNorm(h) -> router GEMV (+ bias) -> top-k -> softmax; xn hi + lo
+//   dispatch     each (token, slot) pair's xn row pushed to the exchange region of the rank owning its expert
+//   group        (owner) received pairs grouped by local expert, in (sender, pair) order
+//   gemm         gate_up of every local expert on its pairs, SwiGLU in the epilogue -> a hi + lo
+//   gemm         down of every local expert -> y rows
+//   return       y rows pushed back to the exchange region of the pair's sender
+//   combine      h += resid * sum_j w_j y_j, slots in routing order
+// and the step ends with the final norm, the tied lm_head GEMM and a per-token argmax.
+//
+// The GEMMs run on the tensor cores (mma.sync m16n8k16, bf16 operands, f32 accumulators): the weights are bf16 and
+// each f32 activation x is split into hi = bf16(x) and lo = bf16(x - hi), both multiplied (x - hi - lo is below
+// 2^-17 |x|), so the products carry f32-level accuracy rather than bf16 rounding of the activations.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lastro {
+
+constexpr int kBTok = 64;         // tokens of one GEMM tile (a CTA loops over tiles)
+constexpr int kBRows = 128;       // weight rows of one GEMM CTA (SwiGLU: 64 gate rows + the 64 matching up rows)
+constexpr int kBK = 64;           // K of one pipeline stage
+constexpr int kBStages = 3;
+constexpr size_t kBStageBytes = (size_t)kBRows * kBK * 2 + 2 * (size_t)kBTok * kBK * 2;  // 32 KB
+constexpr size_t kBGemmSmem = kBStages * kBStageBytes;
+constexpr int kBMaxSlots = 4096;  // pairs one rank may receive in one layer (world * tokens per rank * k)
+
+enum BEpi { BEPI_STORE = 0, BEPI_SWIGLU = 1 };
+
+struct BGemmArgs {
+    const uint16_t* w;        // bf16 [groups][rows][K]
+    long long group_stride;   // elements between groups
+    int group0;               // first group of this launch (expert parallelism: the rank's first expert)
+    int rows, K, k_split;     // k_split: K of one grid-z slice (multiple of kBK)
+    const uint16_t* x_hi;     // activation rows, bf16 hi / lo, row stride ldx elements
+    const uint16_t* x_lo;
+    int ldx;
+    const int* x_rows;        // optional: position -> activation row (null: the position itself)
+    const int* g_off;         // optional (grouped): per group first position and count; null: positions 0..n-1
+    const int* g_cnt;
+    int n;
+    // BEPI_STORE: y[z * z_stride + pos * ldy + row] = acc / div (div 1: acc as is)
+    float* y;
+    int ldy;
+    long long z_stride;
+    float div;
+    // BEPI_SWIGLU: a[pos * I + r] = silu(gate_r) * up_r, split into hi + lo (gate rows r, up rows I + r)
+    uint16_t* a_hi;
+    uint16_t* a_lo;
+    int I;
+};
+
+struct BNormArgs {
+    float* h;                  // [n, H] residual stream (written in embed mode)
+    const uint16_t* embed;     // embed mode: [V, H] bf16, rows tokens[t]
+    const int* tokens;
+    float emb_mult;
+    const float* ln;           // [H]
+    float eps;
+    uint16_t* x_hi;            // [n, H]
+    uint16_t* x_lo;
+    int H;
+};
+
+struct BRopeArgs {
+    const float* part;         // [ks][n][qd + 2 kvd] partial sums
+    int ks;
+    const int* seq;            // [n] sequence of each token
+    const int* pos;            // [sequences] position of the current token
+    const float* rope_cs;      // [max_len, d]
+    float* q;                  // [n, qd]
+    void* k_pool;              // [pages, kv_heads, page, d]
+    void* v_pool;
+    const int* page_table;     // [sequences, pt_stride]
+    int pt_stride, page_size, kv_f32;
+    int n, qd, kvd, d, kv_heads;
+};
+
+struct BRouterArgs {
+    float* h;                  // [n, H], updated: h += resid * sum_z opart[z]
+    const float* opart;        // [ks][n][H]
+    int ks;
+    float resid;
+    const float* ln;           // MoE norm [H]
+    float eps;
+    const uint16_t* wr;        // [E, H] bf16
+    const float* bias;         // [E] or null
+    uint16_t* x_hi;            // [n, H] MoE input split
+    uint16_t* x_lo;
+    int* ids;                  // [n, k]
+    float* weights;            // [n, k]
+    int* route_hist;           // optional [n][layers][k] history of the step
+    int layer, layers;
+    int n, H, E, k;
+};
+
+// Exchange region of one rank (the same layout on every rank; every rank maps every other rank's region):
+//   rx      [world][cap] pair rows, each bf16 hi [H] then lo [H]   (written by the senders)
+//   rx_ids  [world][cap] expert of each pair                       (written by the senders)
+//   rx_n    [world] tokens of each sender in this layer           (written by the senders)
+//   cb      [cap] f32 [H] result rows of this rank's pairs        (written by the owners)
+//   flags   [2][world] u32, 128 bytes apart: dispatch, return     (written with release stores by the peers)
+struct XLayout {
+    size_t rx, rx_ids, rx_n, cb, flags, bytes;
+    int cap;  // pairs per sender: tokens per rank * k
+};
+
+XLayout x_layout(int world, int tokens_per_rank, int k, int H);
+
+struct BExchangeArgs {
+    unsigned char* const* peers;  // [world] exchange region of every rank (this rank's own at [rank])
+    XLayout lay;
+    int rank, world;
+    int experts_per_rank;
+    const unsigned int* epoch_base;  // flags carry epoch_base + layer + 1
+    int layer;
+    int* err;
+    unsigned int* counter;        // last-CTA election, zero between launches
+    // dispatch
+    const uint16_t* x_hi;         // [n, H]
+    const uint16_t* x_lo;
+    const int* ids;               // [n, k]
+    int n, k, H;
+    // group (owner): outputs for the grouped GEMMs and the return
+    int* x_rows;                  // [positions] -> rx row (sender * cap + pair)
+    int* src;                     // [positions] -> rx row, for the return
+    int* g_off;                   // [experts_per_rank]
+    int* g_cnt;
+    int* n_pos;                   // [1]
+    // return (owner)
+    const float* y;               // [positions, H]
+    // combine (sender)
+    float* h;                     // [n, H]
+    const float* weights;         // [n, k]
+    float resid;
+};
+
+struct BHeadArgs {
+    const float* logits;          // [n, V]
+    int V, n;
+    const int* seq;
+    int* pos;                     // incremented per token's sequence
+    int* next;                    // [n] argmax (last maximum)
+    int* tokens;                  // optional: next token fed back as the next step's input
+    unsigned int* epoch_base;     // advanced by `layers` (CTA 0)
+    int layers;
+};
+
+cudaError_t launch_bgemm(const BGemmArgs& a, int epi, int groups, cudaStream_t s);
+cudaError_t launch_battn_norm(const BNormArgs& a, int n, cudaStream_t s);
+cudaError_t launch_brope_kv(const BRopeArgs& a, cudaStream_t s);
+cudaError_t launch_brouter(const BRouterArgs& a, cudaStream_t s);
+cudaError_t launch_ep_dispatch(const BExchangeArgs& a, cudaStream_t s);
+cudaError_t launch_ep_group(const BExchangeArgs& a, cudaStream_t s);
+cudaError_t launch_ep_return(const BExchangeArgs& a, int max_positions, cudaStream_t s);
+cudaError_t launch_ep_combine(const BExchangeArgs& a, cudaStream_t s);
+cudaError_t launch_bargmax(const BHeadArgs& a, cudaStream_t s);
+
+}  // namespace lastro

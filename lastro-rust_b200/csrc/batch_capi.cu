@@ -1,0 +1,640 @@
+// C ABI of the batched decode step: many independent sequences decoded together on the weights of one lastro_model,
+// with the MoE experts partitioned over the ranks of an expert-parallel group (one process per GPU).
+//
+// The reference decodes one sequence at a time (gpu_model.rs GpuModel::step); a batched step has the reference's
+// own multi-position contract: every sequence's results equal its single-sequence step up to summation order
+// (cpu.rs:234-238).  A lastro_batch holds the sequences' paged KV caches and the step's scratch; the weights stay in
+// the model.  Every rank of a group creates its batch with the same max_seqs and world, exchanges the handle of its
+// exchange region (lastro_batch_exchange_handle) with the others, and connects (lastro_batch_connect); the ranks then
+// call the step functions the same number of times, each for its own sequences.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <map>
+#include <vector>
+
+#include "batch.h"
+#include "capi_internal.h"
+
+using namespace lastro;
+using namespace lastro_capi;
+
+struct lastro_batch {
+    lastro_model* m = nullptr;
+    lastro_ctx* ctx = nullptr;
+    int max_seqs = 0, max_len = 0, max_pages = 0, rank = 0, world = 1, epr = 0, e0 = 0;
+    int ks_qkv = 1, ks_o = 1, R = 0;
+    bool poisoned = false, connected = false, use_graphs = true;
+    Arena arena;
+    std::vector<void*> kpool, vpool;  // per layer: [max_seqs * max_pages pages][kv_heads][page][d]
+    float* rope_cs = nullptr;
+    int *page_table = nullptr, *d_pos = nullptr;
+    std::vector<int> pos_host;
+    int *d_seq = nullptr, *d_tok = nullptr, *d_next = nullptr, *d_hist = nullptr;
+    int *h_seq = nullptr, *h_tok = nullptr, *h_err = nullptr;  // pinned
+    float *h = nullptr, *qkv_part = nullptr, *q = nullptr, *att = nullptr, *part_acc = nullptr, *part_ml = nullptr;
+    float *o_part = nullptr, *rw = nullptr, *y = nullptr, *logits = nullptr, *bias = nullptr;
+    uint16_t *xa_hi = nullptr, *xa_lo = nullptr, *att_hi = nullptr, *att_lo = nullptr, *xm_hi = nullptr, *xm_lo = nullptr;
+    uint16_t *a_hi = nullptr, *a_lo = nullptr;
+    unsigned int *attn_counters = nullptr, *counters = nullptr, *epoch = nullptr;
+    int *ids = nullptr, *route_hist = nullptr, *x_rows = nullptr, *src = nullptr, *g_off = nullptr, *g_cnt = nullptr;
+    int *n_pos = nullptr, *d_err = nullptr;
+    XLayout lay{};
+    unsigned char* xreg = nullptr;
+    unsigned char** d_peers = nullptr;
+    std::vector<void*> opened;  // peer regions mapped from IPC handles
+    std::map<int, cudaGraphExec_t> graphs;  // one per token count
+    bool has_bias = false, want_hist = false;
+};
+
+namespace {
+
+int bfail(lastro_batch* b, cudaError_t e, const char* what) { return cuda_fail(b->ctx, &b->poisoned, e, what); }
+
+#define BTRY(expr, what)                                        \
+    do {                                                        \
+        cudaError_t e_ = (expr);                                \
+        if (e_ != cudaSuccess) return bfail(b, e_, what);       \
+    } while (0)
+
+// split-K slices for a dense GEMM of `rows` x K: enough CTAs for two per SM, slices of at least 128 columns
+int pick_ks(int rows, int K, int n_sm) {
+    const int tiles = (rows + kBRows - 1) / kBRows, chunks = K / kBK;
+    int best = 1;
+    for (int d = 1; d <= chunks; ++d)
+        if (chunks % d == 0 && K / d >= 128 && tiles * d <= 2 * n_sm) best = d;
+    return best;
+}
+
+cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
+    lastro_model* m = b->m;
+    const lastro_model_desc& d = m->d;
+    const int H = d.hidden, I = d.inter, E = d.experts, k = d.k, qd = m->qd, kvd = m->kvd, R = b->R;
+    cudaError_t e = cudaSuccess;
+    BExchangeArgs xa{};
+    xa.peers = b->d_peers;
+    xa.lay = b->lay;
+    xa.rank = b->rank;
+    xa.world = b->world;
+    xa.experts_per_rank = b->epr;
+    xa.epoch_base = b->epoch;
+    xa.err = b->d_err;
+    xa.x_hi = b->xm_hi;
+    xa.x_lo = b->xm_lo;
+    xa.ids = b->ids;
+    xa.n = n;
+    xa.k = k;
+    xa.H = H;
+    xa.x_rows = b->x_rows;
+    xa.src = b->src;
+    xa.g_off = b->g_off;
+    xa.g_cnt = b->g_cnt;
+    xa.n_pos = b->n_pos;
+    xa.y = b->y;
+    xa.h = b->h;
+    xa.weights = b->rw;
+    xa.resid = d.residual_multiplier;
+    const uint16_t* rx = reinterpret_cast<const uint16_t*>(b->xreg + b->lay.rx);
+    for (int l = 0; l < d.layers && e == cudaSuccess; ++l) {
+        const LayerDev& L = m->L[l];
+        BNormArgs na{};
+        na.h = b->h;
+        na.embed = l == 0 ? m->embed : nullptr;
+        na.tokens = b->d_tok;
+        na.emb_mult = d.embedding_multiplier;
+        na.ln = L.ln_attn;
+        na.eps = d.eps;
+        na.x_hi = b->xa_hi;
+        na.x_lo = b->xa_lo;
+        na.H = H;
+        if ((e = launch_battn_norm(na, n, s))) break;
+
+        BGemmArgs ga{};
+        ga.w = reinterpret_cast<const uint16_t*>(L.wqkv);
+        ga.rows = R;
+        ga.K = H;
+        ga.k_split = H / b->ks_qkv;
+        ga.x_hi = b->xa_hi;
+        ga.x_lo = b->xa_lo;
+        ga.ldx = H;
+        ga.n = n;
+        ga.y = b->qkv_part;
+        ga.ldy = R;
+        ga.z_stride = (long long)n * R;
+        ga.div = 1.0f;
+        if ((e = launch_bgemm(ga, BEPI_STORE, 1, s))) break;
+
+        BRopeArgs ra{};
+        ra.part = b->qkv_part;
+        ra.ks = b->ks_qkv;
+        ra.seq = b->d_seq;
+        ra.pos = b->d_pos;
+        ra.rope_cs = b->rope_cs;
+        ra.q = b->q;
+        ra.k_pool = b->kpool[l];
+        ra.v_pool = b->vpool[l];
+        ra.page_table = b->page_table;
+        ra.pt_stride = b->max_pages;
+        ra.page_size = kPageSize;
+        ra.kv_f32 = d.kv_dtype == LASTRO_DTYPE_F32;
+        ra.n = n;
+        ra.qd = qd;
+        ra.kvd = kvd;
+        ra.d = d.head_dim;
+        ra.kv_heads = d.kv_heads;
+        if ((e = launch_brope_kv(ra, s))) break;
+
+        AttnArgs aa{};
+        aa.q = b->q;
+        aa.k_pool = b->kpool[l];
+        aa.v_pool = b->vpool[l];
+        aa.page_table = b->page_table;
+        aa.page_size = kPageSize;
+        aa.kv_f32 = ra.kv_f32;
+        aa.pos = b->d_pos;
+        aa.part_acc = b->part_acc;
+        aa.part_ml = b->part_ml;
+        aa.counters = b->attn_counters;
+        aa.att_out = b->att;
+        aa.err = b->d_err;
+        aa.kv_heads = d.kv_heads;
+        aa.G = m->G;
+        aa.d = d.head_dim;
+        aa.max_len = b->max_len;
+        aa.split_cap = attn_split_cap(b->max_len);
+        aa.scale = d.attention_multiplier;
+        aa.seq = b->d_seq;
+        aa.tokens = n;
+        aa.pt_stride = b->max_pages;
+        aa.att_hi = b->att_hi;
+        aa.att_lo = b->att_lo;
+        if ((e = launch_attention(aa, s, false))) break;
+
+        BGemmArgs oa{};
+        oa.w = reinterpret_cast<const uint16_t*>(L.wo);
+        oa.rows = H;
+        oa.K = qd;
+        oa.k_split = qd / b->ks_o;
+        oa.x_hi = b->att_hi;
+        oa.x_lo = b->att_lo;
+        oa.ldx = qd;
+        oa.n = n;
+        oa.y = b->o_part;
+        oa.ldy = H;
+        oa.z_stride = (long long)n * H;
+        oa.div = 1.0f;
+        if ((e = launch_bgemm(oa, BEPI_STORE, 1, s))) break;
+
+        BRouterArgs rta{};
+        rta.h = b->h;
+        rta.opart = b->o_part;
+        rta.ks = b->ks_o;
+        rta.resid = d.residual_multiplier;
+        rta.ln = L.ln_moe;
+        rta.eps = d.eps;
+        rta.wr = reinterpret_cast<const uint16_t*>(L.router);
+        rta.bias = b->has_bias ? b->bias + (size_t)l * E : nullptr;
+        rta.x_hi = b->xm_hi;
+        rta.x_lo = b->xm_lo;
+        rta.ids = b->ids;
+        rta.weights = b->rw;
+        rta.route_hist = b->want_hist ? b->route_hist : nullptr;
+        rta.layer = l;
+        rta.layers = d.layers;
+        rta.n = n;
+        rta.H = H;
+        rta.E = E;
+        rta.k = k;
+        if ((e = launch_brouter(rta, s))) break;
+
+        xa.layer = l;
+        xa.counter = b->counters;
+        if ((e = launch_ep_dispatch(xa, s))) break;
+        if ((e = launch_ep_group(xa, s))) break;
+
+        BGemmArgs gu{};
+        gu.w = reinterpret_cast<const uint16_t*>(L.gate_up);
+        gu.group_stride = (long long)2 * I * H;
+        gu.group0 = b->e0;
+        gu.rows = 2 * I;
+        gu.K = H;
+        gu.k_split = H;
+        gu.x_hi = rx;
+        gu.x_lo = rx + H;
+        gu.ldx = 2 * H;
+        gu.x_rows = b->x_rows;
+        gu.g_off = b->g_off;
+        gu.g_cnt = b->g_cnt;
+        gu.a_hi = b->a_hi;
+        gu.a_lo = b->a_lo;
+        gu.I = I;
+        gu.div = 1.0f;
+        if ((e = launch_bgemm(gu, BEPI_SWIGLU, b->epr, s))) break;
+
+        BGemmArgs dn{};
+        dn.w = reinterpret_cast<const uint16_t*>(L.down);
+        dn.group_stride = (long long)H * I;
+        dn.group0 = b->e0;
+        dn.rows = H;
+        dn.K = I;
+        dn.k_split = I;
+        dn.x_hi = b->a_hi;
+        dn.x_lo = b->a_lo;
+        dn.ldx = I;
+        dn.g_off = b->g_off;
+        dn.g_cnt = b->g_cnt;
+        dn.y = b->y;
+        dn.ldy = H;
+        dn.div = 1.0f;
+        if ((e = launch_bgemm(dn, BEPI_STORE, b->epr, s))) break;
+
+        xa.counter = b->counters + 32;
+        if ((e = launch_ep_return(xa, b->world * b->lay.cap, s))) break;
+        if ((e = launch_ep_combine(xa, s))) break;
+    }
+    if (e) return e;
+    BNormArgs fa{};
+    fa.h = b->h;
+    fa.ln = m->norm;
+    fa.eps = d.eps;
+    fa.x_hi = b->xa_hi;
+    fa.x_lo = b->xa_lo;
+    fa.H = H;
+    if ((e = launch_battn_norm(fa, n, s))) return e;
+    BGemmArgs ha{};
+    ha.w = m->embed;
+    ha.rows = d.vocab;
+    ha.K = H;
+    ha.k_split = H;
+    ha.x_hi = b->xa_hi;
+    ha.x_lo = b->xa_lo;
+    ha.ldx = H;
+    ha.n = n;
+    ha.y = b->logits;
+    ha.ldy = d.vocab;
+    ha.div = d.logits_scaling;
+    if ((e = launch_bgemm(ha, BEPI_STORE, 1, s))) return e;
+    BHeadArgs hd{};
+    hd.logits = b->logits;
+    hd.V = d.vocab;
+    hd.n = n;
+    hd.seq = b->d_seq;
+    hd.pos = b->d_pos;
+    hd.next = b->d_next;
+    hd.tokens = b->d_tok;
+    hd.epoch_base = b->epoch;
+    hd.layers = d.layers;
+    return launch_bargmax(hd, s);
+}
+
+int run_bstep(lastro_batch* b, int n) {
+    cudaStream_t s = b->ctx->stream;
+    if (!b->use_graphs) {
+        BTRY(enqueue_bstep(b, n, s), "batch step launch");
+        return LASTRO_OK;
+    }
+    auto it = b->graphs.find(n);
+    if (it == b->graphs.end()) {
+        cudaGraph_t g = nullptr;
+        BTRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
+        cudaError_t e = enqueue_bstep(b, n, s);
+        cudaError_t e2 = cudaStreamEndCapture(s, &g);
+        if (e == cudaSuccess) e = e2;
+        if (e != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            return bfail(b, e, "batch step capture");
+        }
+        cudaGraphExec_t x = nullptr;
+        e = cudaGraphInstantiate(&x, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return bfail(b, e, "batch graph instantiate");
+        it = b->graphs.emplace(n, x).first;
+    }
+    BTRY(cudaGraphLaunch(it->second, s), "batch graph launch");
+    return LASTRO_OK;
+}
+
+int bfinish(lastro_batch* b, const char* what) {
+    cudaStream_t s = b->ctx->stream;
+    BTRY(cudaMemcpyAsync(b->h_err, b->d_err, sizeof(int), cudaMemcpyDeviceToHost, s), what);
+    BTRY(cudaStreamSynchronize(s), what);
+    if (*b->h_err) {
+        b->poisoned = true;
+        return set_err(b->ctx, LASTRO_E_CUDA, "%s: a kernel wait gave up (code %d); batch poisoned", what, *b->h_err);
+    }
+    return LASTRO_OK;
+}
+
+int bready(lastro_batch* b) {
+    if (b->poisoned) return set_err(b->ctx, LASTRO_E_POISONED, "batch unusable after an earlier error");
+    if (!b->connected) return set_err(b->ctx, LASTRO_E_STATE, "batch not connected (lastro_batch_connect)");
+    return model_check_ready(b->m);
+}
+
+// seq ids in range and distinct, tokens in range, room for `steps` more positions; copies them to the device
+int bstage(lastro_batch* b, int n, const int32_t* seq, const int32_t* tok, int steps) {
+    const lastro_model_desc& d = b->m->d;
+    if (n < 1 || n > b->max_seqs || !seq || !tok) return set_err(b->ctx, LASTRO_E_ARG, "batch of %d sequences", n);
+    std::vector<char> seen(b->max_seqs, 0);
+    for (int i = 0; i < n; ++i) {
+        if (seq[i] < 0 || seq[i] >= b->max_seqs || seen[seq[i]])
+            return set_err(b->ctx, LASTRO_E_ARG, "sequence id %d out of range or repeated", seq[i]);
+        seen[seq[i]] = 1;
+        if (tok[i] < 0 || tok[i] >= d.vocab) return set_err(b->ctx, LASTRO_E_ARG, "token %d out of range", tok[i]);
+        if (b->pos_host[seq[i]] + steps > b->max_len)
+            return set_err(b->ctx, LASTRO_E_FULL, "sequence %d: KV cache full (max_len %d)", seq[i], b->max_len);
+    }
+    memcpy(b->h_seq, seq, sizeof(int) * n);
+    memcpy(b->h_tok, tok, sizeof(int) * n);
+    cudaStream_t s = b->ctx->stream;
+    BTRY(cudaMemcpyAsync(b->d_seq, b->h_seq, sizeof(int) * n, cudaMemcpyHostToDevice, s), "stage");
+    BTRY(cudaMemcpyAsync(b->d_tok, b->h_tok, sizeof(int) * n, cudaMemcpyHostToDevice, s), "stage");
+    return LASTRO_OK;
+}
+
+}  // namespace
+
+extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t max_len, int32_t rank, int32_t world,
+                                   lastro_batch** out) {
+    if (!m || !out) return LASTRO_E_ARG;
+    *out = nullptr;
+    lastro_ctx* ctx = m->ctx;
+    const lastro_model_desc& d = m->d;
+    if (max_seqs < 1 || max_len < 1 || world < 1 || world > 32 || rank < 0 || rank >= world)
+        return set_err(ctx, LASTRO_E_ARG, "batch: max_seqs %d, max_len %d, rank %d of %d", max_seqs, max_len, rank, world);
+    if (m->q8) return set_err(ctx, LASTRO_E_UNSUPPORTED, "batched decode runs bf16 weights");
+    if (d.experts % world) return set_err(ctx, LASTRO_E_UNSUPPORTED, "%d experts over %d ranks", d.experts, world);
+    if (d.hidden % kBK || m->qd % kBK || d.inter % 64 || d.hidden > 2048)
+        return set_err(ctx, LASTRO_E_UNSUPPORTED, "batched GEMMs need hidden, heads*head_dim, inter multiples of 64");
+    if (world * max_seqs * d.k > kBMaxSlots)
+        return set_err(ctx, LASTRO_E_UNSUPPORTED, "world x max_seqs x k = %d pairs exceed %d", world * max_seqs * d.k, kBMaxSlots);
+    if (attn_smem(max_len, d.kv_dtype == LASTRO_DTYPE_F32) > kMaxSmemBytes)
+        return set_err(ctx, LASTRO_E_UNSUPPORTED, "max_len %d: attention tiles exceed shared memory", max_len);
+    cudaSetDevice(ctx->device);
+    int n_sm = 148;
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, ctx->device);
+    lastro_batch* b = new lastro_batch();
+    b->m = m;
+    b->ctx = ctx;
+    b->max_seqs = max_seqs;
+    b->max_len = max_len;
+    b->max_pages = (max_len + kPageSize - 1) / kPageSize;
+    b->rank = rank;
+    b->world = world;
+    b->epr = d.experts / world;
+    b->e0 = rank * b->epr;
+    b->R = m->qd + 2 * m->kvd;
+    b->ks_qkv = pick_ks(b->R, d.hidden, n_sm);
+    b->ks_o = pick_ks(d.hidden, m->qd, n_sm);
+    b->pos_host.assign(max_seqs, 0);
+    b->lay = x_layout(world, max_seqs, d.k, d.hidden);
+    const size_t H = d.hidden, I = d.inter, S = max_seqs, E = d.experts, k = d.k, V = d.vocab;
+    const size_t pairs = (size_t)world * b->lay.cap;
+    const size_t kv_elems = S * b->max_pages * kPageSize * (size_t)m->kvd;
+    const size_t kv_bytes = kv_elems * (d.kv_dtype == LASTRO_DTYPE_F32 ? 4 : 2);
+    Arena& A = b->arena;
+    bool bad = false;
+    b->kpool.assign(d.layers, nullptr);
+    b->vpool.assign(d.layers, nullptr);
+    for (int l = 0; l < d.layers && !bad; ++l)
+        bad = A.alloc(&b->kpool[l], kv_bytes) || A.alloc(&b->vpool[l], kv_bytes);
+    bad = bad || A.alloc(&b->rope_cs, (size_t)max_len * d.head_dim) || A.alloc(&b->page_table, S * b->max_pages) ||
+          A.alloc(&b->d_pos, S) || A.alloc(&b->d_seq, S) || A.alloc(&b->d_tok, S) || A.alloc(&b->d_next, S) ||
+          A.alloc(&b->d_hist, (size_t)max_len * S) || A.alloc(&b->h, S * H) || A.alloc(&b->xa_hi, S * H) ||
+          A.alloc(&b->xa_lo, S * H) || A.alloc(&b->qkv_part, (size_t)b->ks_qkv * S * b->R) ||
+          A.alloc(&b->q, S * m->qd) || A.alloc(&b->att, S * m->qd) || A.alloc(&b->att_hi, S * m->qd) ||
+          A.alloc(&b->att_lo, S * m->qd) || A.alloc(&b->part_acc, S * d.heads * kAttnSplits * d.head_dim) ||
+          A.alloc(&b->part_ml, S * d.heads * kAttnSplits * 2) || A.alloc(&b->attn_counters, S * d.kv_heads) ||
+          A.alloc(&b->o_part, (size_t)b->ks_o * S * H) || A.alloc(&b->ids, S * k) || A.alloc(&b->rw, S * k) ||
+          A.alloc(&b->xm_hi, S * H) || A.alloc(&b->xm_lo, S * H) || A.alloc(&b->bias, (size_t)d.layers * E) ||
+          A.alloc(&b->x_rows, pairs) || A.alloc(&b->src, pairs) || A.alloc(&b->g_off, kMaxExperts) ||
+          A.alloc(&b->g_cnt, kMaxExperts) || A.alloc(&b->n_pos, 1) || A.alloc(&b->a_hi, pairs * I) ||
+          A.alloc(&b->a_lo, pairs * I) || A.alloc(&b->y, pairs * H) || A.alloc(&b->logits, S * V) ||
+          A.alloc(&b->route_hist, S * d.layers * k) || A.alloc(&b->counters, 64) || A.alloc(&b->epoch, 1) ||
+          A.alloc(&b->d_err, 1) || A.alloc(&b->xreg, b->lay.bytes) || A.alloc(&b->d_peers, (size_t)world);
+    if (!bad) bad = cudaMallocHost(&b->h_seq, sizeof(int) * S) != cudaSuccess;
+    if (!bad) bad = cudaMallocHost(&b->h_tok, sizeof(int) * S) != cudaSuccess;
+    if (!bad) bad = cudaMallocHost(&b->h_err, sizeof(int)) != cudaSuccess;
+    if (bad) {
+        cudaGetLastError();
+        if (b->h_seq) cudaFreeHost(b->h_seq);
+        if (b->h_tok) cudaFreeHost(b->h_tok);
+        if (b->h_err) cudaFreeHost(b->h_err);
+        A.release();
+        delete b;
+        return set_err(ctx, LASTRO_E_NOMEM, "batch allocation failed");
+    }
+    *b->h_err = 0;
+    cudaStream_t s = ctx->stream;
+    std::vector<int> pt(S * b->max_pages);
+    for (size_t i = 0; i < pt.size(); ++i) pt[i] = (int)i;  // sequence q owns pages [q * max_pages, (q+1) * max_pages)
+    const std::vector<float> cs = rope_table(d, max_len);
+    cudaError_t e = cudaMemcpyAsync(b->page_table, pt.data(), sizeof(int) * pt.size(), cudaMemcpyHostToDevice, s);
+    if (!e) e = cudaMemcpyAsync(b->rope_cs, cs.data(), sizeof(float) * cs.size(), cudaMemcpyHostToDevice, s);
+    if (!e) e = cudaMemsetAsync(b->d_pos, 0, sizeof(int) * S, s);
+    if (!e) e = cudaMemsetAsync(b->attn_counters, 0, sizeof(unsigned int) * S * d.kv_heads, s);
+    if (!e) e = cudaMemsetAsync(b->counters, 0, sizeof(unsigned int) * 64, s);
+    if (!e) e = cudaMemsetAsync(b->epoch, 0, sizeof(unsigned int), s);
+    if (!e) e = cudaMemsetAsync(b->d_err, 0, sizeof(int), s);
+    if (!e) e = cudaMemsetAsync(b->xreg, 0, b->lay.bytes, s);
+    if (!e) e = cudaMemsetAsync(b->route_hist, 0, sizeof(int) * S * d.layers * k, s);
+    if (!e) e = cudaStreamSynchronize(s);
+    if (e) {
+        cudaGetLastError();
+        cudaFreeHost(b->h_seq);
+        cudaFreeHost(b->h_tok);
+        cudaFreeHost(b->h_err);
+        A.release();
+        delete b;
+        return set_err(ctx, LASTRO_E_CUDA, "batch init: %s", cudaGetErrorString(e));
+    }
+    ctx_retain(ctx);
+    *out = b;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_batch_exchange_handle(lastro_batch* b, void* handle, int32_t bytes) {
+    if (!b || !handle || bytes < (int)sizeof(cudaIpcMemHandle_t)) return LASTRO_E_ARG;
+    cudaSetDevice(b->ctx->device);
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, b->xreg);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_err(b->ctx, LASTRO_E_CUDA, "exchange handle: %s", cudaGetErrorString(e));
+    }
+    memcpy(handle, &h, sizeof h);
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_batch_connect(lastro_batch* b, const void* handles, int32_t bytes_each) {
+    if (!b) return LASTRO_E_ARG;
+    if (b->connected) return set_err(b->ctx, LASTRO_E_STATE, "batch already connected");
+    if (b->world > 1 && (!handles || bytes_each < (int)sizeof(cudaIpcMemHandle_t)))
+        return set_err(b->ctx, LASTRO_E_ARG, "connect: %d handles of %d bytes", b->world, bytes_each);
+    cudaSetDevice(b->ctx->device);
+    std::vector<unsigned char*> peers(b->world, nullptr);
+    for (int q = 0; q < b->world; ++q) {
+        if (q == b->rank) {
+            peers[q] = b->xreg;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const unsigned char*>(handles) + (size_t)q * bytes_each, sizeof h);
+        void* p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            for (void* o : b->opened) cudaIpcCloseMemHandle(o);
+            b->opened.clear();
+            return set_err(b->ctx, LASTRO_E_CUDA, "connect to rank %d: %s", q, cudaGetErrorString(e));
+        }
+        b->opened.push_back(p);
+        peers[q] = static_cast<unsigned char*>(p);
+    }
+    cudaError_t e = cudaMemcpyAsync(b->d_peers, peers.data(), sizeof(unsigned char*) * b->world, cudaMemcpyHostToDevice,
+                                    b->ctx->stream);
+    if (!e) e = cudaStreamSynchronize(b->ctx->stream);
+    if (e) return bfail(b, e, "connect");
+    b->connected = true;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_batch_set_router_bias(lastro_batch* b, const float* bias) {
+    if (!b) return LASTRO_E_ARG;
+    if (b->poisoned) return set_err(b->ctx, LASTRO_E_POISONED, "batch unusable after an earlier error");
+    cudaSetDevice(b->ctx->device);
+    if (bias) {
+        BTRY(cudaMemcpyAsync(b->bias, bias, sizeof(float) * b->m->d.layers * b->m->d.experts, cudaMemcpyHostToDevice,
+                             b->ctx->stream),
+             "bias upload");
+        BTRY(cudaStreamSynchronize(b->ctx->stream), "bias upload");
+    }
+    if ((bias != nullptr) != b->has_bias) {  // the captured graphs read the flag at capture time
+        for (auto& g : b->graphs) cudaGraphExecDestroy(g.second);
+        b->graphs.clear();
+    }
+    b->has_bias = bias != nullptr;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_batch_step(lastro_batch* b, int32_t n, const int32_t* seq_ids, const int32_t* tokens,
+                                 int32_t* next, float* logits, int32_t* route_ids) {
+    if (!b) return LASTRO_E_ARG;
+    int rc = bready(b);
+    if (rc) return rc;
+    cudaSetDevice(b->ctx->device);
+    if ((rc = bstage(b, n, seq_ids, tokens, 1))) return rc;
+    const bool hist = route_ids != nullptr;
+    if (hist != b->want_hist) {
+        for (auto& g : b->graphs) cudaGraphExecDestroy(g.second);
+        b->graphs.clear();
+        b->want_hist = hist;
+    }
+    if ((rc = run_bstep(b, n))) return rc;
+    cudaStream_t s = b->ctx->stream;
+    const lastro_model_desc& d = b->m->d;
+    if (next) BTRY(cudaMemcpyAsync(next, b->d_next, sizeof(int) * n, cudaMemcpyDeviceToHost, s), "next download");
+    if (logits)
+        BTRY(cudaMemcpyAsync(logits, b->logits, sizeof(float) * n * d.vocab, cudaMemcpyDeviceToHost, s), "logits download");
+    if (route_ids)
+        BTRY(cudaMemcpyAsync(route_ids, b->route_hist, sizeof(int) * n * d.layers * d.k, cudaMemcpyDeviceToHost, s),
+             "routes download");
+    if ((rc = bfinish(b, "batch step"))) return rc;
+    for (int i = 0; i < n; ++i) b->pos_host[seq_ids[i]] += 1;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_batch_decode(lastro_batch* b, int32_t n, const int32_t* seq_ids, const int32_t* tokens,
+                                   int32_t steps, int32_t* out_ids) {
+    if (!b) return LASTRO_E_ARG;
+    int rc = bready(b);
+    if (rc) return rc;
+    if (steps < 0) return set_err(b->ctx, LASTRO_E_ARG, "steps %d", steps);
+    cudaSetDevice(b->ctx->device);
+    if ((rc = bstage(b, n, seq_ids, tokens, steps))) return rc;
+    if (b->want_hist) {
+        for (auto& g : b->graphs) cudaGraphExecDestroy(g.second);
+        b->graphs.clear();
+        b->want_hist = false;
+    }
+    cudaStream_t s = b->ctx->stream;
+    for (int i = 0; i < steps; ++i) {
+        if ((rc = run_bstep(b, n))) return rc;
+        if (out_ids && i < b->max_len)
+            BTRY(cudaMemcpyAsync(b->d_hist + (size_t)i * n, b->d_next, sizeof(int) * n, cudaMemcpyDeviceToDevice, s),
+                 "history");
+    }
+    if (out_ids && steps > 0)
+        BTRY(cudaMemcpyAsync(out_ids, b->d_hist, sizeof(int) * (size_t)steps * n, cudaMemcpyDeviceToHost, s), "ids");
+    if ((rc = bfinish(b, "batch decode"))) return rc;
+    for (int i = 0; i < n; ++i) b->pos_host[seq_ids[i]] += steps;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_batch_fill_kv_synthetic(lastro_batch* b, int32_t seq, int32_t n, uint64_t seed, float sd) {
+    if (!b) return LASTRO_E_ARG;
+    if (b->poisoned) return set_err(b->ctx, LASTRO_E_POISONED, "batch unusable after an earlier error");
+    if (seq < 0 || seq >= b->max_seqs || n < 0 || n > b->max_len)
+        return set_err(b->ctx, LASTRO_E_ARG, "fill_kv_synthetic: sequence %d, %d positions", seq, n);
+    cudaSetDevice(b->ctx->device);
+    const lastro_model_desc& d = b->m->d;
+    const size_t per_seq = (size_t)b->max_pages * kPageSize * b->m->kvd;  // elements of one sequence's pages
+    const float sc = synth_scale(sd);
+    cudaStream_t s = b->ctx->stream;
+    for (int l = 0; l < d.layers; ++l) {
+        const uint64_t sk = mix64_host(seed + 2 * (uint64_t)l + 1000003u * (uint64_t)seq);
+        const uint64_t sv = mix64_host(seed + 2 * (uint64_t)l + 1 + 1000003u * (uint64_t)seq);
+        const size_t elems = (size_t)((n + kPageSize - 1) / kPageSize) * kPageSize * b->m->kvd;
+        if (d.kv_dtype == LASTRO_DTYPE_F32) {
+            BTRY(launch_synth_f32(static_cast<float*>(b->kpool[l]) + seq * per_seq, elems, sk, sc, s), "kv fill");
+            BTRY(launch_synth_f32(static_cast<float*>(b->vpool[l]) + seq * per_seq, elems, sv, sc, s), "kv fill");
+        } else {
+            BTRY(launch_synth_bf16(static_cast<uint16_t*>(b->kpool[l]) + seq * per_seq, elems, sk, sc, 0.0f, s), "kv fill");
+            BTRY(launch_synth_bf16(static_cast<uint16_t*>(b->vpool[l]) + seq * per_seq, elems, sv, sc, 0.0f, s), "kv fill");
+        }
+    }
+    BTRY(cudaMemcpyAsync(b->d_pos + seq, &n, sizeof(int), cudaMemcpyHostToDevice, s), "position");
+    BTRY(cudaStreamSynchronize(s), "kv fill");
+    b->pos_host[seq] = n;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_batch_reset(lastro_batch* b, int32_t seq) {
+    if (!b) return LASTRO_E_ARG;
+    if (b->poisoned) return set_err(b->ctx, LASTRO_E_POISONED, "batch unusable after an earlier error");
+    if (seq < 0 || seq >= b->max_seqs) return set_err(b->ctx, LASTRO_E_ARG, "sequence %d", seq);
+    cudaSetDevice(b->ctx->device);
+    const int zero = 0;
+    BTRY(cudaMemcpyAsync(b->d_pos + seq, &zero, sizeof(int), cudaMemcpyHostToDevice, b->ctx->stream), "reset");
+    BTRY(cudaStreamSynchronize(b->ctx->stream), "reset");
+    b->pos_host[seq] = 0;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_batch_position(const lastro_batch* b, int32_t seq, int32_t* pos) {
+    if (!b || !pos || seq < 0 || seq >= b->max_seqs) return LASTRO_E_ARG;
+    *pos = b->pos_host[seq];
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_batch_set_options(lastro_batch* b, int32_t use_graphs) {
+    if (!b) return LASTRO_E_ARG;
+    b->use_graphs = use_graphs != 0;
+    return LASTRO_OK;
+}
+
+extern "C" void lastro_batch_destroy(lastro_batch* b) {
+    if (!b) return;
+    cudaSetDevice(b->ctx->device);
+    cudaStreamSynchronize(b->ctx->stream);
+    for (auto& g : b->graphs) cudaGraphExecDestroy(g.second);
+    for (void* p : b->opened) cudaIpcCloseMemHandle(p);
+    if (b->h_seq) cudaFreeHost(b->h_seq);
+    if (b->h_tok) cudaFreeHost(b->h_tok);
+    if (b->h_err) cudaFreeHost(b->h_err);
+    b->arena.release();
+    lastro_ctx* ctx = b->ctx;
+    delete b;
+    ctx_release(ctx);
+}

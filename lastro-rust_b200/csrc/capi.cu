@@ -19,79 +19,12 @@
 #include <string>
 #include <vector>
 
-#include "../../include/lastro_b200.h"
-#include "kernels.h"
+#include "capi_internal.h"
 
 using namespace lastro;
+using namespace lastro_capi;
 
 #define LASTRO_VERSION "lastro-b200 0.1.0 (sm_100a)"
-
-// Reference-counted by its layers and models, so that the context and its objects may be destroyed in any order
-// (a garbage-collected host language finalises objects in no fixed order).
-struct lastro_ctx {
-    int device = 0;
-    cudaStream_t stream = nullptr;
-    bool own_stream = false;
-    std::string err;
-    std::atomic<int> refs{1};
-    std::atomic<bool> closed{false};
-};
-
-namespace {
-
-int set_err(lastro_ctx* c, int code, const char* fmt, ...) {
-    if (c) {
-        char buf[512];
-        va_list ap;
-        va_start(ap, fmt);
-        vsnprintf(buf, sizeof buf, fmt, ap);
-        va_end(ap);
-        c->err = buf;
-    }
-    return code;
-}
-
-// synthetic tensor seed: the same formula as the CPU oracle's lo_tensor_seed
-uint64_t mix64_host(uint64_t z) {
-    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-    return z ^ (z >> 31);
-}
-
-uint64_t tensor_seed(uint64_t base, int layer, int kind) {
-    return mix64_host(base * 0x9E3779B97F4A7C15ull + ((uint64_t)(uint32_t)(layer + 1) << 8) + (uint64_t)kind + 1u);
-}
-
-float synth_scale(float sd) { return sd / 37837.2265f; }
-
-enum { K_EMBED = 0, K_NORM, K_LN_ATTN, K_LN_MOE, K_Q, K_K, K_V, K_O, K_ROUTER, K_GATE_UP, K_DOWN, K_COUNT };
-
-// Device allocations of one object, freed together.
-struct Arena {
-    std::vector<void*> ptrs;
-    size_t bytes = 0;
-    cudaError_t alloc(void** p, size_t n) {
-        *p = nullptr;
-        if (n == 0) n = 16;
-        cudaError_t e = cudaMalloc(p, n);
-        if (e == cudaSuccess) {
-            ptrs.push_back(*p);
-            bytes += n;
-        }
-        return e;
-    }
-    template <typename T>
-    cudaError_t alloc(T** p, size_t count) {
-        return alloc(reinterpret_cast<void**>(p), count * sizeof(T));
-    }
-    void release() {
-        for (void* p : ptrs) cudaFree(p);
-        ptrs.clear();
-        bytes = 0;
-    }
-};
-
-}  // namespace
 
 // =====================================================================================================================
 // context
@@ -123,19 +56,6 @@ extern "C" int lastro_ctx_create(int32_t device, void* stream, lastro_ctx** out)
     return LASTRO_OK;
 }
 
-namespace {
-
-void ctx_retain(lastro_ctx* c) { c->refs.fetch_add(1); }
-
-void ctx_release(lastro_ctx* c) {
-    if (c->refs.fetch_sub(1) != 1) return;
-    cudaSetDevice(c->device);
-    if (c->stream) cudaStreamSynchronize(c->stream);
-    if (c->own_stream) cudaStreamDestroy(c->stream);
-    delete c;
-}
-
-}  // namespace
 
 extern "C" void lastro_ctx_destroy(lastro_ctx* c) {
     if (!c || c->closed.exchange(true)) return;
@@ -183,14 +103,6 @@ int check_block_shape(lastro_ctx* c, int E, int H, int I, int k, int q8 = 0) {
     if (down_smem(H, I, k, q8) > kMaxSmemBytes || gate_up_smem(H, q8) > kMaxSmemBytes)
         return set_err(c, LASTRO_E_UNSUPPORTED, "k=%d, I=%d, H=%d: expert tiles exceed shared memory", k, I, H);
     return LASTRO_OK;
-}
-
-// gpu.rs:345-355: synchronize the stream before reporting, then poison
-int cuda_fail(lastro_ctx* c, bool* poisoned, cudaError_t e, const char* what) {
-    cudaStreamSynchronize(c->stream);
-    cudaGetLastError();
-    *poisoned = true;
-    return set_err(c, LASTRO_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
 #define LASTRO_TRY(expr, what)                                                   \
@@ -391,57 +303,7 @@ extern "C" void lastro_layer_destroy(lastro_layer* obj) {
 // =====================================================================================================================
 // whole model (GpuModel)
 // =====================================================================================================================
-namespace {
 
-struct LayerDev {
-    float *ln_attn = nullptr, *ln_moe = nullptr;
-    float* wr_t = nullptr;  // [H, E] router weight x ln_moe, transposed (fused router operand)
-    bool fold_dirty = true;
-    // linear weights: bf16 rows, or Q8_0 rows in the device layout (wrow_bytes): byte buffers either way
-    unsigned char *wqkv = nullptr, *wo = nullptr, *router = nullptr, *gate_up = nullptr, *down = nullptr;
-    void *k_pool = nullptr, *v_pool = nullptr;
-};
-
-constexpr int kPageSize = 64;
-
-}  // namespace
-
-struct lastro_model {
-    lastro_ctx* ctx = nullptr;
-    lastro_model_desc d{};
-    int max_len = 0, qd = 0, kvd = 0, G = 1, max_pages = 0, head_grid = 1;
-    int q8 = 0;  // linear weights are Q8_0
-    bool poisoned = false;
-    bool use_graphs = true, use_pdl = true;
-    Arena arena;
-    uint16_t* embed = nullptr;
-    float* norm = nullptr;
-    std::vector<LayerDev> L;
-    float* rope_cs = nullptr;
-    int* page_table = nullptr;
-    // per-step state
-    float *h = nullptr, *q = nullptr, *att = nullptr;
-    float *part_acc = nullptr, *part_ml = nullptr;  // attention splits [heads, kAttnSplits, d] / [.., 2]
-    float *rlogits = nullptr, *route_w = nullptr, *rnorm = nullptr, *a = nullptr, *logits = nullptr;
-    int *route_ids = nullptr, *d_token = nullptr, *d_pos = nullptr, *d_step = nullptr, *d_out_ids = nullptr;
-    int* d_prompt = nullptr;
-    unsigned int *router_counter = nullptr, *head_counter = nullptr, *attn_counters = nullptr;
-    unsigned long long* head_partial = nullptr;
-    float* op_partial = nullptr;  // [oproj_grid(H), E + 1]
-    int* d_err = nullptr;    // error word of the bounded waits
-    int* h_token = nullptr;  // pinned
-    int* h_err = nullptr;    // pinned copy of d_err
-    int pos_host = 0;
-    std::vector<char> loaded;  // per (layer, kind)
-    cudaGraphExec_t graph = nullptr;
-    // fused step (one persistent launch per step) when the shapes fit it
-    bool fused_ok = false, use_fused = false;
-    FusedLayout flay{};
-    FusedLayer* f_layers = nullptr;  // [layers] (device)
-    unsigned int *f_ticket = nullptr, *f_epoch = nullptr, *f_count = nullptr;
-    FusedExchange fx{};
-    unsigned long long* f_best = nullptr;
-};
 
 namespace {
 
@@ -744,6 +606,8 @@ int init_page_table(lastro_model* m) {
 
 }  // namespace
 
+int lastro_capi::model_check_ready(lastro_model* m) { return check_ready(m); }
+
 extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* desc, int32_t max_len, lastro_model** out) {
     if (!ctx || !desc || !out) return LASTRO_E_ARG;
     *out = nullptr;
@@ -870,16 +734,7 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
     }
     if (!e) e = cudaMemsetAsync(m->route_ids, 0, sizeof(int) * d.layers * d.k, s);
     if (!e) e = cudaMemsetAsync(m->route_w, 0, sizeof(float) * d.layers * d.k, s);
-    // model.rs:63-73: inv_freq = 1/theta^(2j/d) and cos/sin of pos*inv_freq, in f32 on the host
-    std::vector<float> cs((size_t)max_len * d.head_dim);
-    const int half = d.head_dim / 2;
-    for (int p = 0; p < max_len; ++p)
-        for (int j = 0; j < half; ++j) {
-            const float inv = 1.0f / powf(d.rope_theta, (float)(2 * j) / (float)d.head_dim);
-            const float f = (float)p * inv;
-            cs[(size_t)p * d.head_dim + j] = cosf(f);
-            cs[(size_t)p * d.head_dim + half + j] = sinf(f);
-        }
+    const std::vector<float> cs = rope_table(d, max_len);
     if (!e) e = cudaMemcpyAsync(m->rope_cs, cs.data(), sizeof(float) * cs.size(), cudaMemcpyHostToDevice, s);
     if (!e) e = cudaStreamSynchronize(s);
     if (e) {

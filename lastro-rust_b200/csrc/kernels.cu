@@ -148,11 +148,17 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
     __shared__ __align__(8) uint64_t bar;
     __shared__ float cw[kAttnSplits][G], cden[G];
     __shared__ bool is_last;
-    const int NS = gridDim.x, s = blockIdx.x, kvh = blockIdx.y;
+    const int NS = gridDim.x, s = blockIdx.x, kvh = blockIdx.y, z = blockIdx.z;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int HD = a.kv_heads * G * D;  // q / output floats of one token
+    const int seq_id = a.seq ? __ldg(a.seq + z) : 0;
+    const int* page_table = a.page_table + (size_t)seq_id * a.pt_stride;
+    float* part_acc = a.part_acc + (size_t)z * HD * NS;
+    float* part_ml = a.part_ml + (size_t)z * a.kv_heads * G * NS * 2;
+    float* att_out = a.att_out + (size_t)z * HD;
 
     // the position is written only by the previous step's head kernel: constant for the whole step
-    const int pos = __ldcg(a.pos);
+    const int pos = __ldcg(a.pos + seq_id);
     const int len = pos + 1;
     const int p0 = (int)(((long long)len * s) / NS), p1 = (int)(((long long)len * (s + 1)) / NS);
     const int pb = min(p1, pos);  // rows [p0, pb) are final already
@@ -167,7 +173,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
         for (int t = threadIdx.x; t <= pg1 - pg0; t += blockDim.x) {
             const int pg = pg0 + t;
             const int lo = max(p0, pg * a.page_size), hi = min(pb, (pg + 1) * a.page_size);
-            const int page = __ldcg(a.page_table + pg);
+            const int page = __ldcg(page_table + pg);
             const size_t off = (((size_t)page * a.kv_heads + kvh) * a.page_size + (lo - pg * a.page_size)) * RB;
             bulk_g2s(kt + (size_t)(lo - p0) * RB, static_cast<const unsigned char*>(a.k_pool) + off, (uint32_t)(hi - lo) * RB, &bar);
             bulk_g2s(vt + (size_t)(lo - p0) * RB, static_cast<const unsigned char*>(a.v_pool) + off, (uint32_t)(hi - lo) * RB, &bar);
@@ -178,11 +184,11 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
     pdl_launch();
 
     for (int i = threadIdx.x; i < G * D / 4; i += blockDim.x)
-        reinterpret_cast<float4*>(&sq[0][0])[i] = __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)kvh * G * D) + i);
+        reinterpret_cast<float4*>(&sq[0][0])[i] = __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)z * HD + (size_t)kvh * G * D) + i);
     if (pos >= p0 && pos < p1 && threadIdx.x < 2 * CH) {
         // the row this layer's qkv kernel just appended
         const int pg = pos / a.page_size, slot = pos - pg * a.page_size;
-        const size_t off = (((size_t)__ldcg(a.page_table + pg) * a.kv_heads + kvh) * a.page_size + slot) * RB;
+        const size_t off = (((size_t)__ldcg(page_table + pg) * a.kv_heads + kvh) * a.page_size + slot) * RB;
         const int c = threadIdx.x % CH;
         const bool is_v = threadIdx.x >= CH;
         const uint4* src = reinterpret_cast<const uint4*>(static_cast<const unsigned char*>(is_v ? a.v_pool : a.k_pool) + off);
@@ -296,18 +302,18 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
             }
         }
         const size_t hs = (size_t)(kvh * G + g) * NS + s;
-        a.part_acc[hs * D + dim] = A;
+        part_acc[hs * D + dim] = A;
         if (dim == 0) {
-            a.part_ml[hs * 2] = M;
-            a.part_ml[hs * 2 + 1] = L;
+            part_ml[hs * 2] = M;
+            part_ml[hs * 2 + 1] = L;
         }
     }
     // the last CTA of this KV head merges the NS splits of its G heads: every load (each thread's NS partial outputs,
     // and one (m, l) pair per (head, split)) in one round, the per-head max and denominator by 16-lane shuffles
     static_assert(kAttnSplits == 16, "the merge reduces one head's splits within 16 lanes");
-    if (!last_block_arrives(a.counters + kvh, (unsigned int)NS, &is_last)) return;
+    if (!last_block_arrives(a.counters + (size_t)z * a.kv_heads + kvh, (unsigned int)NS, &is_last)) return;
     constexpr int NT = 32 * kAttnWarps, KO = (G * D + NT - 1) / NT;
-    const float* pa = a.part_acc + (size_t)kvh * G * kAttnSplits * D;
+    const float* pa = part_acc + (size_t)kvh * G * kAttnSplits * D;
     float v[KO][kAttnSplits];
 #pragma unroll
     for (int k = 0; k < KO; ++k) {
@@ -318,7 +324,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
             v[k][sp] = t < G * D ? __ldcg(pa + ((size_t)g * kAttnSplits + sp) * D + dim) : 0.0f;
     }
     const int i = threadIdx.x;
-    const float2 mlv = i < G * kAttnSplits ? __ldcg(reinterpret_cast<const float2*>(a.part_ml) + (size_t)kvh * G * kAttnSplits + i)
+    const float2 mlv = i < G * kAttnSplits ? __ldcg(reinterpret_cast<const float2*>(part_ml) + (size_t)kvh * G * kAttnSplits + i)
                                            : make_float2(-INFINITY, 0.0f);
     if (i < ((G * kAttnSplits + 31) & ~31)) {  // whole warps
         float M = mlv.x;
@@ -342,7 +348,14 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
         float num = 0.0f;
 #pragma unroll
         for (int sp = 0; sp < kAttnSplits; ++sp) num = fmaf(v[k][sp], cw[sp][g], num);
-        a.att_out[((size_t)kvh * G + g) * D + dim] = num / cden[g];
+        const float o = num / cden[g];
+        const size_t oi = ((size_t)kvh * G + g) * D + dim;
+        att_out[oi] = o;
+        if (a.att_hi) {
+            const uint16_t hi = f32_to_bf16_rne(o);
+            a.att_hi[(size_t)z * HD + oi] = hi;
+            a.att_lo[(size_t)z * HD + oi] = f32_to_bf16_rne(__fsub_rn(o, __uint_as_float((uint32_t)hi << 16)));
+        }
     }
 }
 
@@ -834,7 +847,7 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     if (a.d != kHeadDim || a.split_cap != attn_split_cap(a.max_len)) return cudaErrorInvalidValue;
     const size_t smem = attn_smem(a.max_len, a.kv_f32);
     if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
-    const dim3 grid(kAttnSplits, a.kv_heads), block(32 * kAttnWarps);
+    const dim3 grid(kAttnSplits, a.kv_heads, a.seq ? a.tokens : 1), block(32 * kAttnWarps);
 #define LASTRO_ATTN_G(GV)                                                                                  \
     case GV: {                                                                                             \
         auto k = a.kv_f32 ? attention_kernel<true, GV> : attention_kernel<false, GV>;                      \

@@ -60,6 +60,13 @@ struct AttnArgs {
     int kv_heads, G, d;
     int max_len, split_cap;  // split_cap = attn_split_cap(max_len): K/V rows one CTA stages
     float scale;
+    // batched decode (grid z = the launch's tokens, null seq = batch-1): token z reads q and writes att_out at
+    // z * heads * d and its partials/counters at its own offsets, and attends the cache of sequence seq[z] (page-table
+    // row seq[z] of pt_stride entries, position pos[seq[z]])
+    const int* seq;
+    int tokens, pt_stride;
+    uint16_t* att_hi;  // optional: att_out split into bf16 hi + lo (the batched o-projection's operands)
+    uint16_t* att_lo;
 };
 
 struct OprojArgs {

@@ -74,7 +74,21 @@ EXPORTS = {
     "lastro_model_set_options": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32]),
     "lastro_model_fused": (C.c_int, [C.c_void_p]),
     "lastro_model_destroy": (None, [C.c_void_p]),
+    "lastro_batch_create": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_void_p)]),
+    "lastro_batch_exchange_handle": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32]),
+    "lastro_batch_connect": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32]),
+    "lastro_batch_set_router_bias": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "lastro_batch_step": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                    C.c_void_p]),
+    "lastro_batch_decode": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p]),
+    "lastro_batch_fill_kv_synthetic": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_uint64, C.c_float]),
+    "lastro_batch_reset": (C.c_int, [C.c_void_p, C.c_int32]),
+    "lastro_batch_position": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_int32)]),
+    "lastro_batch_set_options": (C.c_int, [C.c_void_p, C.c_int32]),
+    "lastro_batch_destroy": (None, [C.c_void_p]),
 }
+
+HANDLE_BYTES = 64  # cudaIpcMemHandle_t
 
 
 def lib():
@@ -200,6 +214,7 @@ class GpuModel:
         ctx.check(lib().lastro_model_create(ctx.h, C.byref(d), max_len, C.byref(h)))
         self.h = h
         ctx._children.add(self)
+        self._batches = weakref.WeakSet()  # destroyed before the model
         self._logits = np.empty(cfg["vocab"], np.float32)
         self._ids = np.empty(cfg["layers"] * cfg["k"], np.int32)
         self._w = np.empty(cfg["layers"] * cfg["k"], np.float32)
@@ -283,7 +298,87 @@ class GpuModel:
 
     def close(self):
         if getattr(self, "h", None):
+            for b in list(getattr(self, "_batches", ())):
+                b.close()
             lib().lastro_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
+class GpuBatch:
+    """Batched decode of many independent sequences on a GpuModel's weights, the MoE experts partitioned over the
+    `world` ranks of an expert-parallel group (one process per GPU).  world 1: call connect() with no handles.
+    world > 1: every rank passes exchange_handle() to the others (e.g. torch.distributed.all_gather_object) and calls
+    connect(handles in rank order); the ranks then step the same number of times."""
+
+    def __init__(self, model: GpuModel, max_seqs: int, max_len: int, rank: int = 0, world: int = 1):
+        self.model, self.ctx, self.cfg = model, model.ctx, model.cfg
+        self.max_seqs, self.max_len, self.rank, self.world = max_seqs, max_len, rank, world
+        h = C.c_void_p()
+        self.ctx.check(lib().lastro_batch_create(model.h, max_seqs, max_len, rank, world, C.byref(h)))
+        self.h = h
+        model._batches.add(self)
+        self.ctx._children.add(self)
+
+    def exchange_handle(self) -> bytes:
+        buf = (C.c_char * HANDLE_BYTES)()
+        self.ctx.check(lib().lastro_batch_exchange_handle(self.h, buf, HANDLE_BYTES))
+        return bytes(buf)
+
+    def connect(self, handles=None):
+        if handles is None:
+            self.ctx.check(lib().lastro_batch_connect(self.h, None, HANDLE_BYTES))
+            return
+        assert len(handles) == self.world and all(len(x) == HANDLE_BYTES for x in handles)
+        buf = (C.c_char * (HANDLE_BYTES * self.world)).from_buffer_copy(b"".join(handles))
+        self.ctx.check(lib().lastro_batch_connect(self.h, buf, HANDLE_BYTES))
+
+    def set_router_bias(self, bias):
+        if bias is None:
+            self.ctx.check(lib().lastro_batch_set_router_bias(self.h, None))
+            return
+        b = np.ascontiguousarray(bias, dtype=np.float32)
+        assert b.shape == (self.cfg["layers"], self.cfg["experts"])
+        self.ctx.check(lib().lastro_batch_set_router_bias(self.h, _p(b)))
+
+    def step(self, seq_ids, tokens, want_logits: bool = False, want_routes: bool = False):
+        """(next [n], logits [n, V] or None, route ids [n, layers, k] or None) for one token of each sequence."""
+        sq = np.ascontiguousarray(seq_ids, dtype=np.int32)
+        tk = np.ascontiguousarray(tokens, dtype=np.int32)
+        n, c = sq.size, self.cfg
+        nxt = np.empty(n, np.int32)
+        lg = np.empty((n, c["vocab"]), np.float32) if want_logits else None
+        rt = np.empty((n, c["layers"], c["k"]), np.int32) if want_routes else None
+        self.ctx.check(lib().lastro_batch_step(self.h, n, _p(sq), _p(tk), _p(nxt), _p(lg), _p(rt)))
+        return nxt, lg, rt
+
+    def decode(self, seq_ids, tokens, steps: int, want_ids: bool = True):
+        """`steps` greedy steps on the device (each step's ids fed back); ids [steps, n]."""
+        sq = np.ascontiguousarray(seq_ids, dtype=np.int32)
+        tk = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.empty((max(steps, 1), sq.size), np.int32) if want_ids else None
+        self.ctx.check(lib().lastro_batch_decode(self.h, sq.size, _p(sq), _p(tk), steps, _p(out)))
+        return out[:steps] if want_ids else None
+
+    def fill_kv_synthetic(self, seq: int, n: int, seed: int = 7, std: float = 0.5):
+        self.ctx.check(lib().lastro_batch_fill_kv_synthetic(self.h, seq, n, seed, std))
+
+    def reset(self, seq: int):
+        self.ctx.check(lib().lastro_batch_reset(self.h, seq))
+
+    def position(self, seq: int) -> int:
+        v = C.c_int32()
+        self.ctx.check(lib().lastro_batch_position(self.h, seq, C.byref(v)))
+        return v.value
+
+    def set_options(self, graphs: bool = True):
+        self.ctx.check(lib().lastro_batch_set_options(self.h, int(graphs)))
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().lastro_batch_destroy(self.h)
             self.h = None
 
     def __del__(self):

@@ -6,6 +6,9 @@ config.json).  Weights are random-init (no checkpoints here): every tensor is
 drawn from the library's synthetic generator with the seeds below, std 0.02
 (transformers' initializer_range), RMSNorm weights 1.0 (transformers' init).
 """
+import math
+
+import numpy as np
 
 # Granite muP multipliers (model.rs:1-7; values of the 1B/3B Granite 3.0 configs)
 GRANITE_MUP = dict(embedding_multiplier=12.0, residual_multiplier=0.22, attention_multiplier=0.015625,
@@ -83,3 +86,26 @@ def _mix64(z: int) -> int:
 def synthetic_tokens(n: int, seed: int, vocab: int) -> list:
     """Uniform random token ids: mix64(seed + (i + 1) * golden) % vocab (the generator of the synthetic weights)."""
     return [_mix64((seed + (i + 1) * _GOLDEN) & _MASK) % vocab for i in range(n)]
+
+
+def zipf_router_bias(cfg: dict, s: float = 0.8, beta: float = 0.8, std: float = WEIGHT_STD) -> np.ndarray:
+    """Router logit bias [layers, experts] that skews expert load towards Zipf(s) (the C5 workload).
+
+    bias_e = beta * sigma * ln(p_e), p_e = (e + 1)^-s / sum, sigma = std * sqrt(hidden) the spread of the random router's
+    logits.  With top-k routing an expert is chosen at most once per token, so the largest shares are capped; beta = 0.8
+    minimises the L1 distance of the top-8 load shares to Zipf(0.8) for 40 experts (expert 0 gets ~10% of the
+    token-expert pairs, experts 0-4 ~36%, against 16% and 43% for the uncapped distribution).
+    """
+    E = cfg["experts"]
+    p = np.arange(1, E + 1, dtype=np.float64) ** -s
+    p /= p.sum()
+    b = beta * std * math.sqrt(cfg["hidden"]) * np.log(p)
+    return np.tile(b.astype(np.float32), (cfg["layers"], 1))
+
+
+def shard(total: int, rank: int, world: int) -> range:
+    """Contiguous share of `total` items (sequences or experts) owned by `rank` of `world` (earlier ranks get the
+    remainder first)."""
+    base, extra = divmod(total, world)
+    lo = rank * base + min(rank, extra)
+    return range(lo, lo + base + (rank < extra))

@@ -609,12 +609,15 @@ void lo_routing(const float *logits, int32_t e, int32_t k, int32_t *ids, float *
     free(order);
 }
 
-/* block.rs:56-62 HostLayer::forward_cpu, either weight type */
-void lo_block_forward_w(lo_pool *p, int32_t dtype, const void *router, const void *gate_up, const void *down,
-                        int32_t experts, int32_t hidden, int32_t inter, int32_t k, const float *x, float *y,
-                        int32_t *ids, float *weights, float *logits_or_null) {
+/* block.rs:56-62 HostLayer::forward_cpu, either weight type; `bias` (or NULL) is added to the router logits before
+ * the routing (a workload knob of the batched benchmark, not part of Granite) */
+static void block_forward_impl(lo_pool *p, int32_t dtype, const void *router, const void *gate_up, const void *down,
+                               int32_t experts, int32_t hidden, int32_t inter, int32_t k, const float *x, float *y,
+                               int32_t *ids, float *weights, float *logits_or_null, const float *bias) {
     float *logits = (float *)malloc(sizeof(float) * (size_t)experts);
     lo_gemv_w(p, dtype, router, experts, hidden, x, logits);
+    if (bias)
+        for (int32_t e = 0; e < experts; ++e) logits[e] += bias[e];
     lo_routing(logits, experts, k, ids, weights);
     const void **gu = (const void **)malloc(sizeof(void *) * (size_t)k);
     const void **dn = (const void **)malloc(sizeof(void *) * (size_t)k);
@@ -629,6 +632,13 @@ void lo_block_forward_w(lo_pool *p, int32_t dtype, const void *router, const voi
     free(gu);
     free(dn);
     free(logits);
+}
+
+void lo_block_forward_w(lo_pool *p, int32_t dtype, const void *router, const void *gate_up, const void *down,
+                        int32_t experts, int32_t hidden, int32_t inter, int32_t k, const float *x, float *y,
+                        int32_t *ids, float *weights, float *logits_or_null) {
+    block_forward_impl(p, dtype, router, gate_up, down, experts, hidden, inter, k, x, y, ids, weights, logits_or_null,
+                       NULL);
 }
 
 void lo_block_forward(lo_pool *p, const uint16_t *router, const uint16_t *gate_up, const uint16_t *down,
@@ -693,6 +703,7 @@ struct lo_model {
     const uint16_t *embed;
     const float *norm;
     lo_layer_weights *layers;
+    float *router_bias; /* [layers, experts] or NULL */
     /* owned storage (synthetic models) */
     void **owned;
     int n_owned;
@@ -772,7 +783,17 @@ void lo_model_destroy(lo_model *m) {
     for (int i = 0; i < m->n_owned; ++i) free(m->owned[i]);
     free(m->owned);
     free(m->layers);
+    free(m->router_bias);
     free(m);
+}
+
+void lo_model_set_router_bias(lo_model *m, const float *bias) {
+    free(m->router_bias);
+    m->router_bias = NULL;
+    if (!bias) return;
+    size_t n = (size_t)m->cfg.layers * m->cfg.experts;
+    m->router_bias = (float *)malloc(sizeof(float) * n);
+    memcpy(m->router_bias, bias, sizeof(float) * n);
 }
 
 const lo_config *lo_model_config(const lo_model *m) { return &m->cfg; }
@@ -803,6 +824,7 @@ struct lo_session {
     int32_t layers; /* own copy: the session may be destroyed after its model */
     int32_t kv_bf16; /* store K/V rows rounded to bf16 (RNE), as a paged bf16 KV cache holds them */
     float **k_cache, **v_cache; /* per layer [max_len, kvd] */
+    float *router_logits;       /* [layers, experts] of the last step (bias included) */
 };
 
 lo_session *lo_session_create(const lo_model *m, lo_pool *p, int32_t max_len) {
@@ -812,6 +834,7 @@ lo_session *lo_session_create(const lo_model *m, lo_pool *p, int32_t max_len) {
     s->max_len = max_len;
     s->layers = m->cfg.layers;
     size_t kvd = (size_t)m->cfg.kv_heads * m->cfg.head_dim;
+    s->router_logits = (float *)calloc((size_t)m->cfg.layers * m->cfg.experts, sizeof(float));
     s->k_cache = (float **)calloc((size_t)m->cfg.layers, sizeof(float *));
     s->v_cache = (float **)calloc((size_t)m->cfg.layers, sizeof(float *));
     for (int32_t l = 0; l < m->cfg.layers; ++l) {
@@ -829,11 +852,13 @@ void lo_session_destroy(lo_session *s) {
     }
     free(s->k_cache);
     free(s->v_cache);
+    free(s->router_logits);
     free(s);
 }
 
 void lo_session_reset(lo_session *s) { s->pos = 0; }
 void lo_session_set_kv_bf16(lo_session *s, int32_t on) { s->kv_bf16 = on != 0; }
+const float *lo_session_router_logits(const lo_session *s) { return s->router_logits; }
 
 static void round_bf16(float *v, size_t n) {
     for (size_t i = 0; i < n; ++i) v[i] = bf2f(lo_f32_to_bf16(v[i]));
@@ -933,8 +958,9 @@ int lo_session_step(lo_session *s, int32_t token, float *logits, int32_t *ids, f
         lo_gemv_w(s->pool, c->weight_dtype, w->o, h, qd, att, o);
         for (int32_t i = 0; i < h; ++i) x[i] += c->residual_multiplier * o[i];
         lo_rmsnorm(x, w->ln_moe, h, c->eps, xn);
-        lo_block_forward_w(s->pool, c->weight_dtype, w->router, w->gate_up, w->down, c->experts, h, c->inter, c->k, xn,
-                           y, ri, rw, NULL);
+        block_forward_impl(s->pool, c->weight_dtype, w->router, w->gate_up, w->down, c->experts, h, c->inter, c->k, xn,
+                           y, ri, rw, s->router_logits + (size_t)l * c->experts,
+                           m->router_bias ? m->router_bias + (size_t)l * c->experts : NULL);
         for (int32_t i = 0; i < h; ++i) x[i] += c->residual_multiplier * y[i];
         if (ids) memcpy(ids + (size_t)l * c->k, ri, sizeof(int32_t) * (size_t)c->k);
         if (weights) memcpy(weights + (size_t)l * c->k, rw, sizeof(float) * (size_t)c->k);

@@ -109,6 +109,8 @@ lo_model *lo_model_create(const lo_config *cfg, const uint16_t *embed, const flo
 /* allocates and fills every tensor from the synthetic generator (owned by the model) */
 lo_model *lo_model_create_synthetic(const lo_config *cfg, uint64_t seed, float stddev,
                                     float norm_std, int threads);
+/* router logit bias [layers, experts] added before every layer's routing (NULL: none); copied */
+void lo_model_set_router_bias(lo_model *m, const float *bias);
 void lo_model_destroy(lo_model *m);
 const lo_config *lo_model_config(const lo_model *m);
 const void *lo_model_tensor(const lo_model *m, int32_t layer, int32_t kind);
@@ -118,6 +120,8 @@ lo_session *lo_session_create(const lo_model *m, lo_pool *p, int32_t max_len);
 void lo_session_destroy(lo_session *s);
 /* K/V rows rounded to bf16 (RNE) when stored: the arithmetic of a paged bf16 KV cache (off by default) */
 void lo_session_set_kv_bf16(lo_session *s, int32_t on);
+/* router logits [layers, experts] of the session's last step (bias included) */
+const float *lo_session_router_logits(const lo_session *s);
 void lo_session_reset(lo_session *s);
 int32_t lo_session_pos(const lo_session *s);
 /* CpuSession::step: logits [V]; ids/weights [L*k] may be NULL. Returns 0, or -1 when full. */

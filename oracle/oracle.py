@@ -98,11 +98,13 @@ def _declare(L):
         "lo_model_create": (_P, [C.POINTER(Config), _P, _P, C.POINTER(LayerWeights)]),
         "lo_model_create_synthetic": (_P, [C.POINTER(Config), _U64, _F, _F, C.c_int]),
         "lo_model_destroy": (None, [_P]),
+        "lo_model_set_router_bias": (None, [_P, _P]),
         "lo_model_tensor": (_P, [_P, _I, _I]),
         "lo_session_create": (_P, [_P, _P, _I]),
         "lo_session_destroy": (None, [_P]),
         "lo_session_reset": (None, [_P]),
         "lo_session_set_kv_bf16": (None, [_P, C.c_int32]),
+        "lo_session_router_logits": (_P, [_P]),
         "lo_session_pos": (_I, [_P]),
         "lo_session_step": (C.c_int, [_P, _I, _P, _P, _P]),
         "lo_session_fill_kv": (C.c_int, [_P, _I, _U64, _F]),
@@ -317,6 +319,15 @@ class Model:
             self._keep += [emb, norm, arr]
             self.h = lib().lo_model_create(C.byref(self._c), _ptr(emb), _ptr(norm), arr)
 
+    def set_router_bias(self, bias):
+        """[layers, experts] f32 added to the router logits before every layer's routing (None removes it)."""
+        if bias is None:
+            lib().lo_model_set_router_bias(self.h, None)
+            return
+        b = np.ascontiguousarray(bias, dtype=np.float32)
+        assert b.shape == (self.cfg["layers"], self.cfg["experts"])
+        lib().lo_model_set_router_bias(self.h, _ptr(b))
+
     def tensor(self, layer: int, kind: int, count: int, dtype=np.uint16) -> np.ndarray:
         p = lib().lo_model_tensor(self.h, layer, kind)
         buf = (C.c_char * (count * np.dtype(dtype).itemsize)).from_address(p)
@@ -349,6 +360,13 @@ class Session:
             raise ValueError("oracle step refused (KV full or token out of range)")
         c = self.model.cfg
         return self.logits.copy(), self.ids.reshape(c["layers"], c["k"]).copy(), self.w.reshape(c["layers"], c["k"]).copy()
+
+    def router_logits(self) -> np.ndarray:
+        """[layers, experts] router logits of the last step (bias included)."""
+        c = self.model.cfg
+        n = c["layers"] * c["experts"]
+        buf = (C.c_float * n).from_address(lib().lo_session_router_logits(self.h))
+        return np.frombuffer(buf, dtype=np.float32, count=n).reshape(c["layers"], c["experts"]).copy()
 
     def fill_kv(self, n: int, seed: int, std: float):
         if lib().lo_session_fill_kv(self.h, n, seed, std) != 0:

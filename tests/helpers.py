@@ -96,3 +96,20 @@ def exact_logit_router(logits, H):
     x = np.zeros(H, np.float32)
     x[:3] = 1.0
     return w, x
+
+
+def first_route_difference(ids, ids_ref, logits_ref, tol=1e-4):
+    """Compares per-layer routes ([layers, k] ids) against the reference's and its router logits [layers, experts].
+
+    Returns None when every layer routes the same, else (layer, slot, gap) of the first difference, where gap is the
+    reference's logit difference between the expert it chose at that slot and the one chosen instead -- a difference
+    the north star allows when the gap is below 1e-4 (the two sides then round differently across the tie), after
+    which the sequence's later layers and positions legitimately diverge.
+    """
+    for l in range(ids.shape[0]):
+        if np.array_equal(ids[l], ids_ref[l]):
+            continue
+        j = int(np.argmax(ids[l] != ids_ref[l]))
+        gap = abs(float(logits_ref[l, ids_ref[l, j]]) - float(logits_ref[l, ids[l, j]]))
+        return l, j, gap
+    return None
