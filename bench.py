@@ -251,6 +251,10 @@ def run_batched(a):
     c = CFG.C5_BATCH
     cfg = c["model"]
     K, W = a.steps, a.warmup
+    if a.profile_only:  # small run for ncu: a 3B-shaped model with --layers layers, synthetic contexts, 2 steps
+        cfg = dict(cfg, layers=a.layers or 2)
+        K, W = 2, 1
+        a.synthetic_kv = True
     total = c["batch"]
     mine = list(CFG.shard(total, rank, world))
     n = len(mine)
@@ -279,6 +283,16 @@ def run_batched(a):
             nxt, _, _ = batch.step(seqs, [p[t] for p in prompts])
         toks = [int(x) for x in nxt]
     prefill_s = time.time() - t0
+    if a.profile_only:
+        batch.decode(seqs, toks, K, want_ids=False)
+        ctx.synchronize()
+        batch.close()
+        model.close()
+        ctx.close()
+        if world > 1:
+            dist.destroy_process_group()
+        print(json.dumps({"profile_only": True, "layers": cfg["layers"], "rank": rank}))
+        return 0
     # expert load of one step: share of the token-expert pairs each rank's experts receive (all ranks' tokens)
     nxt, _, routes = batch.step(seqs, toks, want_routes=True)
     toks = [int(x) for x in nxt]
@@ -325,6 +339,7 @@ def run_batched(a):
         t = torch.tensor([e2e_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
+    prof = batch.profile(seqs, toks, 2)
     mean_ctx = ctx0 + (K + 1) / 2.0
     H, I, L, E, kk = cfg["hidden"], cfg["inter"], cfg["layers"], cfg["experts"], cfg["k"]
     qd, kvd = cfg["heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
@@ -354,9 +369,10 @@ def run_batched(a):
                      "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": None,
                      "bytes_per_step": step_bytes, "bytes_note": "touched experts + KV of all sequences + the dense "
                      "weights every rank streams; per GPU"},
+        "kernels_ms_per_step": {k: round(v, 4) for k, v in prof.items()},
         "e2e": {"value": total * K / (e2e_ms / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": 8 * n,
                 "d2h_bytes_per_step": 4 * n},
-        "gpu_launches": K * (L * 12 + 3),
+        "gpu_launches": K * (L * 9 + 3),
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not a.no_cpu_baseline:

@@ -168,6 +168,12 @@ int lastro_batch_decode(lastro_batch *batch, int32_t n, const int32_t *seq_ids, 
 int lastro_batch_fill_kv_synthetic(lastro_batch *batch, int32_t seq, int32_t n, uint64_t seed, float stddev);
 int lastro_batch_reset(lastro_batch *batch, int32_t seq);
 int lastro_batch_position(const lastro_batch *batch, int32_t seq, int32_t *pos);
+/* mean device ms per step of each kernel kind over `steps` directly launched greedy steps (tokens as for
+ * lastro_batch_decode), timed with events between launches: norm (layer 0), qkv, rope_kv, attention, oproj, router
+ * (with the dispatch), group, gate_up, down (with the return), combine (with the next norm), lm_head, argmax
+ * (n_kinds >= 12) */
+int lastro_batch_profile(lastro_batch *batch, int32_t n, const int32_t *seq_ids, const int32_t *tokens, int32_t steps,
+                         float *kernel_ms, int32_t n_kinds);
 int lastro_batch_set_options(lastro_batch *batch, int32_t use_graphs);
 void lastro_batch_destroy(lastro_batch *batch);
 

@@ -96,9 +96,10 @@ XLayout x_layout(int world, int tokens_per_rank, int k, int H) {
     auto up = [](size_t v) { return (v + 255) & ~(size_t)255; };
     XLayout L{};
     L.cap = tokens_per_rank * k;
+    L.cap_tok = tokens_per_rank;
     size_t o = 0;
     L.rx = o;
-    o = up(o + (size_t)world * L.cap * H * 4);
+    o = up(o + (size_t)world * L.cap_tok * H * 4);
     L.rx_ids = o;
     o = up(o + (size_t)world * L.cap * 4);
     L.rx_n = o;
@@ -123,16 +124,19 @@ __global__ void __launch_bounds__(128) bgemm_kernel(BGemmArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = blockIdx.y, bx = blockIdx.x;
+    pdl_wait();
+    pdl_launch();
+    __shared__ bool is_last;
     int p0 = 0, ntot = a.n;
     if (a.g_cnt) {
         p0 = __ldcg(a.g_off + g);
         ntot = __ldcg(a.g_cnt + g);
     }
-    if (ntot <= 0) return;
     const uint16_t* W = a.w + (size_t)(a.group0 + g) * a.group_stride;
     const int kbeg = blockIdx.z * a.k_split;
     const int nk = min(a.k_split, a.K - kbeg) / kBK;
-    if (nk <= 0) return;
+    if (nk <= 0) ntot = 0;
+    if (EPI != BEPI_RETURN && ntot <= 0) return;  // (a RETURN CTA still votes below)
     const int ch = tid & 7;
     // this thread's 8 weight rows in the tile (fixed for the CTA)
     auto grow_of = [&](int sr) -> int {
@@ -210,11 +214,16 @@ __global__ void __launch_bounds__(128) bgemm_kernel(BGemmArgs a) {
                         uint32_t bh[4], bl[4];
                         ldsm_x4(sXh + off, bh);
                         ldsm_x4(sXl + off, bl);
+                        // the four hi products first, then the four lo products: an accumulator's two updates are
+                        // three independent MMAs apart
 #pragma unroll
                         for (int mt = 0; mt < 2; ++mt) {
                             mma_bf16(acc[mt][2 * jp], af[mt], bh[0], bh[1]);
-                            mma_bf16(acc[mt][2 * jp], af[mt], bl[0], bl[1]);
                             mma_bf16(acc[mt][2 * jp + 1], af[mt], bh[2], bh[3]);
+                        }
+#pragma unroll
+                        for (int mt = 0; mt < 2; ++mt) {
+                            mma_bf16(acc[mt][2 * jp], af[mt], bl[0], bl[1]);
                             mma_bf16(acc[mt][2 * jp + 1], af[mt], bl[2], bl[3]);
                         }
                     }
@@ -222,6 +231,37 @@ __global__ void __launch_bounds__(128) bgemm_kernel(BGemmArgs a) {
             }
         }
         cp_async_wait<0>();
+
+        if (EPI == BEPI_RETURN) {
+            // the tile through shared memory ([token][128 rows] f32), then one 512-byte row block per token to the
+            // combine rows of the pair's sender
+            __syncthreads();
+            float* stile = reinterpret_cast<float*>(smem);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (j * 8 >= n) break;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const int tok = j * 8 + (lane & 3) * 2 + (c & 1);
+                    const int rr = warp * 16 + (lane >> 2) + ((c >> 1) << 3);
+                    if (tok < n) {
+                        stile[tok * kBRows + rr] = acc[0][j][c];
+                        stile[tok * kBRows + 64 + rr] = acc[1][j][c];
+                    }
+                }
+            }
+            __syncthreads();
+            const XLayout& L = a.x.lay;
+            for (int tok = warp; tok < n; tok += 4) {
+                const int i = __ldcg(a.x.src + p0 + t0 + tok);
+                const int sender = i / L.cap, pair = i - sender * L.cap;
+                float4* dst = reinterpret_cast<float4*>(a.x.peers[sender] + L.cb +
+                                                        ((size_t)pair * a.rows + (size_t)bx * kBRows) * 4);
+                dst[lane] = reinterpret_cast<const float4*>(stile + tok * kBRows)[lane];
+            }
+            __syncthreads();
+            continue;
+        }
 
         // epilogue: acc[mt][j][c] is (tile row mt*64 + 16 warp + lane/4 + 8 (c >= 2), token 8 j + 2 (lane % 4) + c % 2)
 #pragma unroll
@@ -253,6 +293,13 @@ __global__ void __launch_bounds__(128) bgemm_kernel(BGemmArgs a) {
             }
         }
     }
+    if (EPI == BEPI_RETURN) {
+        if (!last_block_arrives_sys(a.x.counter, gridDim.x * gridDim.y * gridDim.z, &is_last)) return;
+        if (tid < a.x.world) {
+            const unsigned int epoch = __ldcg(a.x.epoch_base) + a.x.layer + 1;
+            st_release_sys(flag_ptr(a.x.peers[tid], a.x.lay, 1, a.x.rank), epoch);
+        }
+    }
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -263,6 +310,8 @@ __global__ void __launch_bounds__(256) battn_norm_kernel(BNormArgs a) {
     __shared__ float red[BLOCK / 32];
     const int t = blockIdx.x;
     float* h = a.h + (size_t)t * a.H;
+    pdl_wait();
+    pdl_launch();
     float4 v[NV];
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
@@ -310,45 +359,251 @@ __global__ void __launch_bounds__(256) battn_norm_kernel(BNormArgs a) {
 // x1*c - x2*s, x2*c + x1*s (model.rs:153-155); q to its buffer, K (roped) and V to the token's sequence page.
 // ------------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) brope_kv_kernel(BRopeArgs a) {
+    constexpr int kMaxKs = 16;
     const int t = blockIdx.x;
     const int R = a.qd + 2 * a.kvd, half = a.d >> 1;
+    const int pi = blockIdx.y * blockDim.x + threadIdx.x;  // RoPE pair of this thread
+    pdl_wait();
+    pdl_launch();
+    if (pi >= R / 2) return;
     const int sq = __ldg(a.seq + t);
     const int pos = __ldcg(a.pos + sq);
     const float* cs = a.rope_cs + (size_t)pos * a.d;
-    const int page = __ldg(a.page_table + (size_t)sq * a.pt_stride + pos / a.page_size), slot = pos % a.page_size;
-    for (int pi = threadIdx.x; pi < R / 2; pi += blockDim.x) {
-        const int head = pi / half, j = pi - head * half;
-        const int r0 = head * a.d + j, r1 = r0 + half;
-        float x1 = 0.0f, x2 = 0.0f;
-        for (int z = 0; z < a.ks; ++z) {
+    const int head = pi / half, j = pi - head * half;
+    const int r0 = head * a.d + j, r1 = r0 + half;
+    // every slice's two values in flight at once, then summed in slice order
+    float v1[kMaxKs], v2[kMaxKs];
+#pragma unroll
+    for (int z = 0; z < kMaxKs; ++z) {
+        if (z < a.ks) {
             const float* pz = a.part + ((size_t)z * a.n + t) * R;
-            x1 = __fadd_rn(x1, __ldcg(pz + r0));
-            x2 = __fadd_rn(x2, __ldcg(pz + r1));
+            v1[z] = __ldcg(pz + r0);
+            v2[z] = __ldcg(pz + r1);
         }
-        const float c = __ldg(cs + j), s = __ldg(cs + half + j);
-        const float ro0 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
-        const float ro1 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
-        if (r0 < a.qd) {
-            a.q[(size_t)t * a.qd + r0] = ro0;
-            a.q[(size_t)t * a.qd + r1] = ro1;
-            continue;
+    }
+    float x1 = 0.0f, x2 = 0.0f;
+#pragma unroll
+    for (int z = 0; z < kMaxKs; ++z) {
+        if (z < a.ks) {
+            x1 = __fadd_rn(x1, v1[z]);
+            x2 = __fadd_rn(x2, v2[z]);
         }
-        int rr = r0 - a.qd;
-        const bool is_k = rr < a.kvd;
-        if (!is_k) rr -= a.kvd;
-        const int kvh = rr / a.d;
-        const float v0 = is_k ? ro0 : x1, v1 = is_k ? ro1 : x2;
-        const size_t base = (((size_t)page * a.kv_heads + kvh) * a.page_size + slot) * a.d;
-        void* pool = is_k ? a.k_pool : a.v_pool;
-        if (a.kv_f32) {
-            float* p = static_cast<float*>(pool) + base;
-            p[j] = v0;
-            p[j + half] = v1;
-        } else {
-            uint16_t* p = static_cast<uint16_t*>(pool) + base;
-            p[j] = f32_to_bf16_rne(v0);
-            p[j + half] = f32_to_bf16_rne(v1);
+    }
+    const float c = __ldg(cs + j), s = __ldg(cs + half + j);
+    const float ro0 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+    const float ro1 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+    if (r0 < a.qd) {
+        a.q[(size_t)t * a.qd + r0] = ro0;
+        a.q[(size_t)t * a.qd + r1] = ro1;
+        return;
+    }
+    const int page = __ldg(a.page_table + (size_t)sq * a.pt_stride + pos / a.page_size), slot = pos % a.page_size;
+    int rr = r0 - a.qd;
+    const bool is_k = rr < a.kvd;
+    if (!is_k) rr -= a.kvd;
+    const int kvh = rr / a.d;
+    const float w0 = is_k ? ro0 : x1, w1 = is_k ? ro1 : x2;
+    const size_t base = (((size_t)page * a.kv_heads + kvh) * a.page_size + slot) * a.d;
+    void* pool = is_k ? a.k_pool : a.v_pool;
+    if (a.kv_f32) {
+        float* p = static_cast<float*>(pool) + base;
+        p[j] = w0;
+        p[j + half] = w1;
+    } else {
+        uint16_t* p = static_cast<uint16_t*>(pool) + base;
+        p[j] = f32_to_bf16_rne(w0);
+        p[j + half] = f32_to_bf16_rne(w1);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// batched attention: CTA (split s, KV head, token z), 4 warps.  The split's K/V rows (at most cap) arrive in shared
+// memory by bulk copies (one thread per page run); lane l of warp w scores row 32 w + l (+ 128 ...) against the G query
+// heads, reading the row's 16-byte chunks in the order (c + l) mod 8 so that the 8 lanes of a shared-memory phase hit
+// 8 different chunks (no bank conflicts on K, nor on q); each warp keeps its online-softmax partial, P.V with lane l
+// owning dims 2l, 2l+1; the warps merge in shared memory and the CTA writes its partial.  The last CTA of (token, KV
+// head) merges the S partials in split order.
+// ------------------------------------------------------------------------------------------------------------------
+template <bool KV_F32, int G>
+__global__ void __launch_bounds__(128) battn_kernel(BAttnArgs a) {
+    constexpr int D = kHeadDim, NW = 4;
+    constexpr int ESZ = KV_F32 ? 4 : 2;
+    constexpr int RB = D * ESZ;  // bytes per K/V row of one head
+    constexpr int CH = RB / 16;  // 16-byte chunks per row
+    constexpr int EPC = 16 / ESZ;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    unsigned char* kt = smem_raw;
+    unsigned char* vt = smem_raw + (size_t)a.cap * RB;
+    __shared__ __align__(16) float sq[G][D];
+    __shared__ float wm[NW][G], wl[NW][G];
+    __shared__ __align__(16) float wacc[NW][G][D];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ bool is_last;
+    const int S = gridDim.x, s = blockIdx.x, kvh = blockIdx.y, z = blockIdx.z;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int HD = a.kv_heads * G * D;
+    pdl_wait();
+    pdl_launch();
+    const int sqid = __ldg(a.seq + z);
+    const int* page_table = a.page_table + (size_t)sqid * a.pt_stride;
+    const int len = __ldcg(a.pos + sqid) + 1;
+    const int p0 = (int)(((long long)len * s) / S), p1 = (int)(((long long)len * (s + 1)) / S);
+    const int nrow = min(p1 - p0, a.cap);
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_expect_tx(&bar, nrow > 0 ? (uint32_t)nrow * RB * 2 : 0u);
+    }
+    __syncthreads();
+    if (nrow > 0) {
+        const int pe = p0 + nrow;
+        const int pg0 = p0 / a.page_size, pg1 = (pe - 1) / a.page_size;
+        for (int t = threadIdx.x; t <= pg1 - pg0; t += blockDim.x) {
+            const int pg = pg0 + t;
+            const int lo = max(p0, pg * a.page_size), hi = min(pe, (pg + 1) * a.page_size);
+            const int page = __ldcg(page_table + pg);
+            const size_t off = (((size_t)page * a.kv_heads + kvh) * a.page_size + (lo - pg * a.page_size)) * RB;
+            bulk_g2s(kt + (size_t)(lo - p0) * RB, static_cast<const unsigned char*>(a.k_pool) + off, (uint32_t)(hi - lo) * RB, &bar);
+            bulk_g2s(vt + (size_t)(lo - p0) * RB, static_cast<const unsigned char*>(a.v_pool) + off, (uint32_t)(hi - lo) * RB, &bar);
         }
+    }
+    for (int i = threadIdx.x; i < G * D / 4; i += blockDim.x)
+        reinterpret_cast<float4*>(&sq[0][0])[i] = __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)z * HD + (size_t)kvh * G * D) + i);
+    __syncthreads();
+    const bool ok = mbar_wait(&bar, 0, a.err, 4);
+
+    float m[G], l[G], acc0[G], acc1[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+        acc0[g] = 0.0f;
+        acc1[g] = 0.0f;
+    }
+    const int nr = ok ? nrow : 0;
+    for (int base = warp * 32; base < nr; base += NW * 32) {
+        const int r = base + lane;
+        const bool valid = r < nr;
+        float sc[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) sc[g] = 0.0f;
+        if (valid) {
+            const uint4* kr = reinterpret_cast<const uint4*>(kt + (size_t)r * RB);
+#pragma unroll
+            for (int c0 = 0; c0 < CH; ++c0) {
+                const int c = (c0 + lane) & (CH - 1);
+                const uint4 kc = kr[c];
+                float kf[8];
+                if (KV_F32) {
+                    kf[0] = __uint_as_float(kc.x);
+                    kf[1] = __uint_as_float(kc.y);
+                    kf[2] = __uint_as_float(kc.z);
+                    kf[3] = __uint_as_float(kc.w);
+                } else {
+                    kf[0] = bf_lo(kc.x);
+                    kf[1] = bf_hi(kc.x);
+                    kf[2] = bf_lo(kc.y);
+                    kf[3] = bf_hi(kc.y);
+                    kf[4] = bf_lo(kc.z);
+                    kf[5] = bf_hi(kc.z);
+                    kf[6] = bf_lo(kc.w);
+                    kf[7] = bf_hi(kc.w);
+                }
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float* qg = &sq[g][c * EPC];
+#pragma unroll
+                    for (int e = 0; e < EPC; ++e) sc[g] = fmaf(qg[e], kf[e], sc[g]);
+                }
+            }
+        }
+        float pr[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float scv = valid ? __fmul_rn(sc[g], a.scale) : -INFINITY;
+            const float mn = fmaxf(m[g], warp_max(scv));
+            pr[g] = valid ? expf(scv - mn) : 0.0f;
+            const float alpha = (m[g] == -INFINITY) ? 0.0f : expf(m[g] - mn);
+            l[g] = l[g] * alpha + warp_sum(pr[g]);
+            acc0[g] *= alpha;
+            acc1[g] *= alpha;
+            m[g] = mn;
+        }
+        const int nj = min(32, nr - base);
+        for (int jj = 0; jj < nj; ++jj) {
+            float v0, v1;
+            if (KV_F32) {
+                const float2 t = reinterpret_cast<const float2*>(vt + (size_t)(base + jj) * RB)[lane];
+                v0 = t.x;
+                v1 = t.y;
+            } else {
+                const uint32_t t = reinterpret_cast<const uint32_t*>(vt + (size_t)(base + jj) * RB)[lane];
+                v0 = bf_lo(t);
+                v1 = bf_hi(t);
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float pj = __shfl_sync(0xffffffffu, pr[g], jj);
+                acc0[g] = fmaf(pj, v0, acc0[g]);
+                acc1[g] = fmaf(pj, v1, acc1[g]);
+            }
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        if (lane == 0) {
+            wm[warp][g] = m[g];
+            wl[warp][g] = l[g];
+        }
+        wacc[warp][g][2 * lane] = acc0[g];
+        wacc[warp][g][2 * lane + 1] = acc1[g];
+    }
+    __syncthreads();
+    float* part_acc = a.part_acc + (size_t)z * HD * S;
+    float* part_ml = a.part_ml + (size_t)z * a.kv_heads * G * S * 2;
+    for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
+        const int g = t / D, dim = t - g * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
+        float L = 0.0f, A = 0.0f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+                if (wm[w][g] == -INFINITY) continue;
+                const float e = expf(wm[w][g] - M);
+                L = fmaf(wl[w][g], e, L);
+                A = fmaf(wacc[w][g][dim], e, A);
+            }
+        }
+        const size_t hs = (size_t)(kvh * G + g) * S + s;
+        part_acc[hs * D + dim] = A;
+        if (dim == 0) {
+            part_ml[hs * 2] = M;
+            part_ml[hs * 2 + 1] = L;
+        }
+    }
+    if (!last_block_arrives(a.counters + (size_t)z * a.kv_heads + kvh, (unsigned int)S, &is_last)) return;
+    // merge the S splits of the G heads, in split order
+    for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
+        const int g = t / D, dim = t - g * D;
+        const size_t h0 = (size_t)(kvh * G + g) * S;
+        float M = -INFINITY;
+        for (int sp = 0; sp < S; ++sp) M = fmaxf(M, __ldcg(part_ml + (h0 + sp) * 2));
+        float den = 0.0f, num = 0.0f;
+        for (int sp = 0; sp < S; ++sp) {
+            const float ms = __ldcg(part_ml + (h0 + sp) * 2);
+            if (ms == -INFINITY) continue;
+            const float e = expf(ms - M);
+            den = fmaf(__ldcg(part_ml + (h0 + sp) * 2 + 1), e, den);
+            num = fmaf(__ldcg(part_acc + (h0 + sp) * D + dim), e, num);
+        }
+        const float o = num / den;
+        const size_t oi = (size_t)z * HD + ((size_t)kvh * G + g) * D + dim;
+        a.att_out[oi] = o;
+        uint16_t hi, lo;
+        split_bf16(o, hi, lo);
+        a.att_hi[oi] = hi;
+        a.att_lo[oi] = lo;
     }
 }
 
@@ -363,8 +618,11 @@ __global__ void __launch_bounds__(256) brouter_kernel(BRouterArgs a) {
     __shared__ float lg[kMaxExperts];
     __shared__ int sid[kMaxTopK];
     __shared__ float sval[kMaxTopK], sw[kMaxTopK];
+    __shared__ bool is_last;
     const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float* h = a.h + (size_t)t * a.H;
+    pdl_wait();
+    pdl_launch();
     float4 v[NV];
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
@@ -372,12 +630,18 @@ __global__ void __launch_bounds__(256) brouter_kernel(BRouterArgs a) {
         v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (4 * i >= a.H) continue;
         float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int z = 0; z < a.ks; ++z) {
-            const float4 p = __ldcg(reinterpret_cast<const float4*>(a.opart + ((size_t)z * a.n + t) * a.H) + i);
-            o.x = __fadd_rn(o.x, p.x);
-            o.y = __fadd_rn(o.y, p.y);
-            o.z = __fadd_rn(o.z, p.z);
-            o.w = __fadd_rn(o.w, p.w);
+        float4 pz[16];  // every slice in flight at once (ks <= 16), summed in slice order
+#pragma unroll
+        for (int z = 0; z < 16; ++z)
+            if (z < a.ks) pz[z] = __ldcg(reinterpret_cast<const float4*>(a.opart + ((size_t)z * a.n + t) * a.H) + i);
+#pragma unroll
+        for (int z = 0; z < 16; ++z) {
+            if (z < a.ks) {
+                o.x = __fadd_rn(o.x, pz[z].x);
+                o.y = __fadd_rn(o.y, pz[z].y);
+                o.z = __fadd_rn(o.z, pz[z].z);
+                o.w = __fadd_rn(o.w, pz[z].w);
+            }
         }
         const float4 hv = __ldcg(reinterpret_cast<const float4*>(h) + i);
         v[k] = make_float4(__fadd_rn(hv.x, __fmul_rn(a.resid, o.x)), __fadd_rn(hv.y, __fmul_rn(a.resid, o.y)),
@@ -398,15 +662,7 @@ __global__ void __launch_bounds__(256) brouter_kernel(BRouterArgs a) {
     for (int k = 0; k < NV; ++k) {
         const int i = threadIdx.x + k * BLOCK;
         if (4 * i >= a.H) continue;
-        const float4 x = ln_times(__ldg(reinterpret_cast<const float4*>(a.ln) + i), v[k], r);
-        reinterpret_cast<float4*>(xs)[i] = x;
-        ushort4 hi, lo;
-        split_bf16(x.x, hi.x, lo.x);
-        split_bf16(x.y, hi.y, lo.y);
-        split_bf16(x.z, hi.z, lo.z);
-        split_bf16(x.w, hi.w, lo.w);
-        reinterpret_cast<ushort4*>(a.x_hi + (size_t)t * a.H)[i] = hi;
-        reinterpret_cast<ushort4*>(a.x_lo + (size_t)t * a.H)[i] = lo;
+        reinterpret_cast<float4*>(xs)[i] = ln_times(__ldg(reinterpret_cast<const float4*>(a.ln) + i), v[k], r);
     }
     __syncthreads();
     for (int e = warp; e < a.E; e += BLOCK / 32) {
@@ -422,49 +678,48 @@ __global__ void __launch_bounds__(256) brouter_kernel(BRouterArgs a) {
         if (lane == 0) lg[e] = a.bias ? __fadd_rn(acc, __ldg(a.bias + e)) : acc;
     }
     __syncthreads();
-    if (warp != 0) return;
-    const float v0 = lane < a.E ? lg[lane] : 0.0f;
-    const float v1 = lane + 32 < a.E ? lg[lane + 32] : 0.0f;
-    route_topk_warp(v0, v1, a.E, a.k, sid, sval, sw);
-    if (lane < a.k) {
-        a.ids[(size_t)t * a.k + lane] = sid[lane];
-        a.weights[(size_t)t * a.k + lane] = sw[lane];
-        if (a.route_hist) a.route_hist[((size_t)t * a.layers + a.layer) * a.k + lane] = sid[lane];
-    }
-}
-
-// ------------------------------------------------------------------------------------------------------------------
-// dispatch: CTA per (token, slot) pair: the token's MoE input row (hi then lo) to the exchange region of the rank that
-// owns the pair's expert, at [sender = this rank][pair]; CTA 0 also writes this rank's routing (ids, token count) to
-// every rank.  The last CTA publishes the dispatch flag of this rank on every rank.
-// ------------------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) ep_dispatch_kernel(BExchangeArgs a) {
-    __shared__ bool is_last;
-    const int p = blockIdx.x;  // pair index t * k + j (grid covers cap pairs; pairs past n * k only vote)
-    const XLayout& L = a.lay;
-    const unsigned int epoch = __ldcg(a.epoch_base) + a.layer + 1;
-    if (p < a.n * a.k) {
-        const int t = p / a.k;
-        const int e = __ldcg(a.ids + p);
-        const int owner = min(max(e / a.experts_per_rank, 0), a.world - 1);
-        unsigned char* dst = a.peers[owner] + L.rx + ((size_t)a.rank * L.cap + p) * (size_t)a.H * 4;
-        const uint4* sh = reinterpret_cast<const uint4*>(a.x_hi + (size_t)t * a.H);
-        const uint4* sl = reinterpret_cast<const uint4*>(a.x_lo + (size_t)t * a.H);
-        const int nc = a.H / 8;  // 16-byte chunks per half row
-        for (int c = threadIdx.x; c < nc; c += blockDim.x) {
-            reinterpret_cast<uint4*>(dst)[c] = __ldcg(sh + c);
-            reinterpret_cast<uint4*>(dst)[nc + c] = __ldcg(sl + c);
+    if (warp == 0) {
+        const float v0 = lane < a.E ? lg[lane] : 0.0f;
+        const float v1 = lane + 32 < a.E ? lg[lane + 32] : 0.0f;
+        route_topk_warp(v0, v1, a.E, a.k, sid, sval, sw);
+        if (lane < a.k) {
+            a.ids[(size_t)t * a.k + lane] = sid[lane];
+            a.weights[(size_t)t * a.k + lane] = sw[lane];
+            if (a.route_hist) a.route_hist[((size_t)t * a.layers + a.layer) * a.k + lane] = sid[lane];
         }
     }
-    if (p == 0) {
-        for (int q = 0; q < a.world; ++q) {
-            int* ids = reinterpret_cast<int*>(a.peers[q] + L.rx_ids) + (size_t)a.rank * L.cap;
-            for (int i = threadIdx.x; i < a.n * a.k; i += blockDim.x) ids[i] = __ldcg(a.ids + i);
-            if (threadIdx.x == 0) reinterpret_cast<int*>(a.peers[q] + L.rx_n)[a.rank] = a.n;
+    __syncthreads();
+    // dispatch: the token's MoE input row (hi then lo) once to every rank that owns one of its experts, its k expert
+    // ids to every rank; the last CTA publishes this rank's dispatch flag on every rank
+    const BExchangeArgs& x = a.x;
+    const XLayout& L = x.lay;
+    for (int j = 0; j < a.k; ++j) {
+        const int o = min(sid[j] / x.experts_per_rank, x.world - 1);
+        bool seen = false;
+        for (int jj = 0; jj < j; ++jj) seen |= min(sid[jj] / x.experts_per_rank, x.world - 1) == o;
+        if (seen) continue;  // the same for every thread (sid is shared)
+        unsigned char* dst = x.peers[o] + L.rx + ((size_t)x.rank * L.cap_tok + t) * (size_t)a.H * 4;
+        for (int i = threadIdx.x; i < a.H / 4; i += BLOCK) {
+            const float4 v4 = reinterpret_cast<const float4*>(xs)[i];
+            ushort4 hi, lo;
+            split_bf16(v4.x, hi.x, lo.x);
+            split_bf16(v4.y, hi.y, lo.y);
+            split_bf16(v4.z, hi.z, lo.z);
+            split_bf16(v4.w, hi.w, lo.w);
+            reinterpret_cast<ushort4*>(dst)[i] = hi;
+            reinterpret_cast<ushort4*>(dst + (size_t)a.H * 2)[i] = lo;
         }
     }
-    if (!last_block_arrives_sys(a.counter, gridDim.x, &is_last)) return;
-    if (threadIdx.x < a.world) st_release_sys(flag_ptr(a.peers[threadIdx.x], L, 0, a.rank), epoch);
+    for (int i = threadIdx.x; i < x.world * a.k; i += BLOCK) {
+        const int q = i / a.k, j = i - q * a.k;
+        reinterpret_cast<int*>(x.peers[q] + L.rx_ids)[(size_t)x.rank * L.cap + (size_t)t * a.k + j] = sid[j];
+    }
+    if (t == 0 && threadIdx.x < x.world) reinterpret_cast<int*>(x.peers[threadIdx.x] + L.rx_n)[x.rank] = a.n;
+    if (!last_block_arrives_sys(x.counter, gridDim.x, &is_last)) return;
+    if (threadIdx.x < x.world) {
+        const unsigned int epoch = __ldcg(x.epoch_base) + x.layer + 1;
+        st_release_sys(flag_ptr(x.peers[threadIdx.x], L, 0, x.rank), epoch);
+    }
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -478,6 +733,8 @@ __global__ void __launch_bounds__(1024) ep_group_kernel(BExchangeArgs a) {
     const XLayout& L = a.lay;
     unsigned char* me = a.peers[a.rank];
     const unsigned int epoch = __ldcg(a.epoch_base) + a.layer + 1;
+    pdl_wait();
+    pdl_launch();
     if (threadIdx.x == 0) ok_all = 1;
     if (threadIdx.x < kMaxExperts) cnt[threadIdx.x] = 0;
     __syncthreads();
@@ -518,29 +775,10 @@ __global__ void __launch_bounds__(1024) ep_group_kernel(BExchangeArgs a) {
         int rank = 0;
         for (int j = 0; j < i; ++j) rank += (le[j] == e);
         const int pos = off[e] + rank;
-        a.x_rows[pos] = i;
+        const int sender = i / L.cap, pair = i - sender * L.cap;
+        a.x_rows[pos] = sender * L.cap_tok + pair / a.k;
         a.src[pos] = i;
     }
-}
-
-// ------------------------------------------------------------------------------------------------------------------
-// return (owner): CTA per position: the down-projection row back to its sender's combine rows, at the sender's pair
-// index; the last CTA publishes this rank's return flag on every rank.
-// ------------------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) ep_return_kernel(BExchangeArgs a) {
-    __shared__ bool is_last;
-    const XLayout& L = a.lay;
-    const unsigned int epoch = __ldcg(a.epoch_base) + a.layer + 1;
-    const int pos = blockIdx.x;
-    if (pos < __ldcg(a.n_pos)) {
-        const int i = __ldcg(a.src + pos);
-        const int s = i / L.cap, p = i - s * L.cap;
-        const float4* src = reinterpret_cast<const float4*>(a.y + (size_t)pos * a.H);
-        float4* dst = reinterpret_cast<float4*>(a.peers[s] + L.cb + (size_t)p * a.H * 4);
-        for (int c = threadIdx.x; c < a.H / 4; c += blockDim.x) dst[c] = __ldcg(src + c);
-    }
-    if (!last_block_arrives_sys(a.counter, gridDim.x, &is_last)) return;
-    if (threadIdx.x < a.world) st_release_sys(flag_ptr(a.peers[threadIdx.x], L, 1, a.rank), epoch);
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -548,11 +786,15 @@ __global__ void __launch_bounds__(128) ep_return_kernel(BExchangeArgs a) {
 // order (cpu.rs:231-238).
 // ------------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) ep_combine_kernel(BExchangeArgs a) {
+    constexpr int BLOCK = 256, NV = 8;  // H <= 2048
     __shared__ int ok_all;
+    __shared__ float red[BLOCK / 32];
     const XLayout& L = a.lay;
     unsigned char* me = a.peers[a.rank];
-    const unsigned int epoch = __ldcg(a.epoch_base) + a.layer + 1;
     const int t = blockIdx.x;
+    pdl_wait();
+    pdl_launch();
+    const unsigned int epoch = __ldcg(a.epoch_base) + a.layer + 1;
     if (threadIdx.x == 0) ok_all = 1;
     __syncthreads();
     if (threadIdx.x < a.world && !wait_flag(flag_ptr(me, L, 1, threadIdx.x), epoch, a.err, 30 + threadIdx.x))
@@ -564,12 +806,33 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(BExchangeArgs a) {
     for (int j = 0; j < kMaxTopK; ++j) w[j] = j < a.k ? __ldcg(a.weights + (size_t)t * a.k + j) : 0.0f;
     const float* cb = reinterpret_cast<const float*>(me + L.cb) + (size_t)t * a.k * a.H;
     float* h = a.h + (size_t)t * a.H;
-    for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
+    float hv[NV];
+    float ss = 0.0f;
+#pragma unroll
+    for (int q = 0; q < NV; ++q) {
+        const int i = threadIdx.x + q * BLOCK;
+        hv[q] = 0.0f;
+        if (i >= a.H) continue;
         float acc = 0.0f;
 #pragma unroll
         for (int j = 0; j < kMaxTopK; ++j)
             if (j < a.k) acc = __fadd_rn(acc, __fmul_rn(w[j], __ldcg(cb + (size_t)j * a.H + i)));
-        h[i] = __fadd_rn(__ldcg(h + i), __fmul_rn(a.resid, acc));
+        hv[q] = __fadd_rn(__ldcg(h + i), __fmul_rn(a.resid, acc));
+        h[i] = hv[q];
+        ss = fmaf(hv[q], hv[q], ss);
+    }
+    if (!a.ln_next) return;
+    // the next RMSNorm (model.rs:141-145): xn = ln * (h * r), split into hi + lo
+    const float tot = block_sum(ss, red);
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.H), a.eps)));
+#pragma unroll
+    for (int q = 0; q < NV; ++q) {
+        const int i = threadIdx.x + q * BLOCK;
+        if (i >= a.H) continue;
+        uint16_t hi, lo;
+        split_bf16(__fmul_rn(__ldg(a.ln_next + i), __fmul_rn(hv[q], r)), hi, lo);
+        a.xn_hi[(size_t)t * a.H + i] = hi;
+        a.xn_lo[(size_t)t * a.H + i] = lo;
     }
 }
 
@@ -580,6 +843,8 @@ __global__ void __launch_bounds__(256) bargmax_kernel(BHeadArgs a) {
     __shared__ unsigned long long best[8];
     const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float* lg = a.logits + (size_t)t * a.V;
+    pdl_wait();
+    pdl_launch();
     unsigned long long b = 0ull;
     for (int v = threadIdx.x; v < a.V; v += blockDim.x) {
         const unsigned long long key = arg_key(__ldcg(lg + v), v);
@@ -602,71 +867,106 @@ __global__ void __launch_bounds__(256) bargmax_kernel(BHeadArgs a) {
     if (t == 0) *a.epoch_base += (unsigned int)a.layers;
 }
 
-// ---- launchers ----------------------------------------------------------------------------------------------------
+// ---- launchers: every batched kernel waits for its predecessor with griddepcontrol.wait first, so all launch with
+// programmatic dependent launch (the next kernel's launch overlaps the tail of the current one) -------------------
 template <typename Kern>
 cudaError_t set_smem(Kern k, size_t bytes) {
     return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
+template <typename Kern, typename... Args>
+cudaError_t launch_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 cudaError_t launch_bgemm(const BGemmArgs& a, int epi, int groups, cudaStream_t s) {
     if (a.K % kBK || a.k_split % kBK || a.k_split <= 0 || a.ldx % 8 || groups < 1) return cudaErrorInvalidValue;
     const int ks = (a.K + a.k_split - 1) / a.k_split;
+    cudaError_t e;
     if (epi == BEPI_SWIGLU) {
         if (a.I % 64 || a.rows != 2 * a.I || ks != 1) return cudaErrorInvalidValue;
-        cudaError_t e = set_smem(bgemm_kernel<BEPI_SWIGLU>, kBGemmSmem);
+        e = set_smem(bgemm_kernel<BEPI_SWIGLU>, kBGemmSmem);
         if (e != cudaSuccess) return e;
-        bgemm_kernel<BEPI_SWIGLU><<<dim3(a.I / 64, groups, 1), 128, kBGemmSmem, s>>>(a);
+        e = launch_pdl(bgemm_kernel<BEPI_SWIGLU>, dim3(a.I / 64, groups, 1), dim3(128), kBGemmSmem, s, a);
+        if (e != cudaSuccess) return e;
+    } else if (epi == BEPI_RETURN) {
+        if (a.rows % kBRows || ks != 1 || a.x.world > 32) return cudaErrorInvalidValue;
+        e = set_smem(bgemm_kernel<BEPI_RETURN>, kBGemmSmem);
+        if (e != cudaSuccess) return e;
+        e = launch_pdl(bgemm_kernel<BEPI_RETURN>, dim3(a.rows / kBRows, groups, 1), dim3(128), kBGemmSmem, s, a);
+        if (e != cudaSuccess) return e;
     } else {
-        cudaError_t e = set_smem(bgemm_kernel<BEPI_STORE>, kBGemmSmem);
+        e = set_smem(bgemm_kernel<BEPI_STORE>, kBGemmSmem);
         if (e != cudaSuccess) return e;
-        bgemm_kernel<BEPI_STORE><<<dim3((a.rows + kBRows - 1) / kBRows, groups, ks), 128, kBGemmSmem, s>>>(a);
+        e = launch_pdl(bgemm_kernel<BEPI_STORE>, dim3((a.rows + kBRows - 1) / kBRows, groups, ks), dim3(128), kBGemmSmem,
+                       s, a);
+        if (e != cudaSuccess) return e;
     }
     return cudaGetLastError();
 }
 
+size_t battn_smem(int cap, int kv_f32) { return (size_t)2 * cap * kHeadDim * (kv_f32 ? 4 : 2); }
+
+cudaError_t launch_battention(const BAttnArgs& a, cudaStream_t s) {
+    if (a.S < 1 || a.S > kBAttnMaxSplits || a.cap < 1 || a.n < 1) return cudaErrorInvalidValue;
+    const size_t smem = battn_smem(a.cap, a.kv_f32);
+    if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
+    const dim3 grid(a.S, a.kv_heads, a.n), block(128);
+#define LASTRO_BATTN_G(GV)                                                                     \
+    case GV: {                                                                                 \
+        auto k = a.kv_f32 ? battn_kernel<true, GV> : battn_kernel<false, GV>;                  \
+        cudaError_t e = set_smem(k, smem);                                                     \
+        return e != cudaSuccess ? e : launch_pdl(k, grid, block, smem, s, a);                  \
+    }
+    switch (a.G) {
+        LASTRO_BATTN_G(1)
+        LASTRO_BATTN_G(2)
+        LASTRO_BATTN_G(3)
+        LASTRO_BATTN_G(4)
+        LASTRO_BATTN_G(6)
+        LASTRO_BATTN_G(8)
+    default: return cudaErrorInvalidValue;
+    }
+#undef LASTRO_BATTN_G
+}
+
 cudaError_t launch_battn_norm(const BNormArgs& a, int n, cudaStream_t s) {
     if (a.H % 4 || a.H > 2048 || n < 1) return cudaErrorInvalidValue;
-    battn_norm_kernel<<<n, 256, 0, s>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(battn_norm_kernel, dim3(n), dim3(256), 0, s, a);
 }
 
 cudaError_t launch_brope_kv(const BRopeArgs& a, cudaStream_t s) {
-    if (a.n < 1) return cudaErrorInvalidValue;
-    brope_kv_kernel<<<a.n, 128, 0, s>>>(a);
-    return cudaGetLastError();
+    if (a.n < 1 || a.ks > 16) return cudaErrorInvalidValue;
+    return launch_pdl(brope_kv_kernel, dim3(a.n, (a.qd + 2 * a.kvd + 255) / 256), dim3(128), 0, s, a);
 }
 
 cudaError_t launch_brouter(const BRouterArgs& a, cudaStream_t s) {
-    if (a.H % 8 || a.H > 2048 || a.E > kMaxExperts || a.k > kMaxTopK || a.n < 1) return cudaErrorInvalidValue;
-    brouter_kernel<<<a.n, 256, sizeof(float) * a.H, s>>>(a);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_ep_dispatch(const BExchangeArgs& a, cudaStream_t s) {
-    if (a.world > 32 || a.H % 8) return cudaErrorInvalidValue;
-    ep_dispatch_kernel<<<a.lay.cap, 128, 0, s>>>(a);
-    return cudaGetLastError();
+    if (a.ks > 16 || a.H % 8 || a.H > 2048 || a.E > kMaxExperts || a.k > kMaxTopK || a.n < 1) return cudaErrorInvalidValue;
+    return launch_pdl(brouter_kernel, dim3(a.n), dim3(256), sizeof(float) * a.H, s, a);
 }
 
 cudaError_t launch_ep_group(const BExchangeArgs& a, cudaStream_t s) {
     if (a.world * a.lay.cap > kBMaxSlots || a.experts_per_rank > kMaxExperts) return cudaErrorInvalidValue;
-    ep_group_kernel<<<1, 1024, 0, s>>>(a);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_ep_return(const BExchangeArgs& a, int max_positions, cudaStream_t s) {
-    ep_return_kernel<<<max_positions, 128, 0, s>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(ep_group_kernel, dim3(1), dim3(1024), 0, s, a);
 }
 
 cudaError_t launch_ep_combine(const BExchangeArgs& a, cudaStream_t s) {
-    ep_combine_kernel<<<a.n, 256, 0, s>>>(a);
-    return cudaGetLastError();
+    if (a.H > 2048) return cudaErrorInvalidValue;
+    return launch_pdl(ep_combine_kernel, dim3(a.n), dim3(256), 0, s, a);
 }
 
 cudaError_t launch_bargmax(const BHeadArgs& a, cudaStream_t s) {
-    bargmax_kernel<<<a.n, 256, 0, s>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(bargmax_kernel, dim3(a.n), dim3(256), 0, s, a);
 }
 
 }  // namespace lastro

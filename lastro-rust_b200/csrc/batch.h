@@ -7,14 +7,15 @@
 //   rope_kv      slices summed in order -> RoPE -> q; K/V appended to each sequence's paged cache
 //   attention    the batch-1 split-KV kernel with a grid dimension over tokens; writes att split into hi + lo
 //   gemm         o-projection partial sums over K slices
-//   router       h += resid * sum of the slices; RMSNorm(h) -> router GEMV (+ bias) -> top-k -> softmax; xn hi + lo
-//   dispatch     each (token, slot) pair's xn row pushed to the exchange region of the rank owning its expert
+//   router       h += resid * sum of the slices; RMSNorm(h) -> router GEMV (+ bias) -> top-k -> softmax; then the
+//                token's xn row (hi + lo) is pushed once to the exchange region of every rank owning one of its experts
 //   group        (owner) received pairs grouped by local expert, in (sender, pair) order
 //   gemm         gate_up of every local expert on its pairs, SwiGLU in the epilogue -> a hi + lo
-//   gemm         down of every local expert -> y rows
-//   return       y rows pushed back to the exchange region of the pair's sender
-//   combine      h += resid * sum_j w_j y_j, slots in routing order
-// and the step ends with the final norm, the tied lm_head GEMM and a per-token argmax.
+//   gemm         down of every local expert; the epilogue writes each result row into the combine rows of the
+//                pair's sender (peer memory)
+//   combine      h += resid * sum_j w_j y_j, slots in routing order; then the next layer's attention norm (or the
+//                final norm) -> xn hi + lo
+// and the step ends with the tied lm_head GEMM and a per-token argmax.
 //
 // The GEMMs run on the tensor cores (mma.sync m16n8k16, bf16 operands, f32 accumulators): the weights are bf16 and
 // each f32 activation x is split into hi = bf16(x) and lo = bf16(x - hi), both multiplied (x - hi - lo is below
@@ -34,7 +35,47 @@ constexpr size_t kBStageBytes = (size_t)kBRows * kBK * 2 + 2 * (size_t)kBTok * k
 constexpr size_t kBGemmSmem = kBStages * kBStageBytes;
 constexpr int kBMaxSlots = 4096;  // pairs one rank may receive in one layer (world * tokens per rank * k)
 
-enum BEpi { BEPI_STORE = 0, BEPI_SWIGLU = 1 };
+// Exchange region of one rank (the same layout on every rank; every rank maps every other rank's region):
+//   rx      [world][cap_tok] token rows, each bf16 hi [H] then lo [H] (written by the senders, once per owner)
+//   rx_ids  [world][cap] expert of each pair                       (written by the senders)
+//   rx_n    [world] tokens of each sender in this layer           (written by the senders)
+//   cb      [cap] f32 [H] result rows of this rank's pairs        (written by the owners)
+//   flags   [2][world] u32, 128 bytes apart: dispatch, return     (written with release stores by the peers)
+struct XLayout {
+    size_t rx, rx_ids, rx_n, cb, flags, bytes;
+    int cap;      // pairs per sender: tokens per rank * k
+    int cap_tok;  // tokens per sender
+};
+
+XLayout x_layout(int world, int tokens_per_rank, int k, int H);
+
+struct BExchangeArgs {
+    unsigned char* const* peers;  // [world] exchange region of every rank (this rank's own at [rank])
+    XLayout lay;
+    int rank, world;
+    int experts_per_rank;
+    const unsigned int* epoch_base;  // flags carry epoch_base + layer + 1
+    int layer;
+    int* err;
+    unsigned int* counter;        // last-CTA election, zero between launches
+    int n, k, H;
+    // group (owner): outputs for the grouped GEMMs and the return
+    int* x_rows;                  // [positions] -> rx token row (sender * cap_tok + token)
+    int* src;                     // [positions] -> pair (sender * cap + pair), for the return
+    int* g_off;                   // [experts_per_rank]
+    int* g_cnt;
+    int* n_pos;                   // [1]
+    // combine (sender), then the next norm: xn = ln_next * (h * r) split into hi + lo (ln_next null: none)
+    float* h;                     // [n, H]
+    const float* weights;         // [n, k]
+    float resid;
+    const float* ln_next;
+    float eps;
+    uint16_t* xn_hi;
+    uint16_t* xn_lo;
+};
+
+enum BEpi { BEPI_STORE = 0, BEPI_SWIGLU = 1, BEPI_RETURN = 2 };
 
 struct BGemmArgs {
     const uint16_t* w;        // bf16 [groups][rows][K]
@@ -57,6 +98,9 @@ struct BGemmArgs {
     uint16_t* a_hi;
     uint16_t* a_lo;
     int I;
+    // BEPI_RETURN: row block of position pos to the combine rows of its sender (x.src[pos]), then the grid's last
+    // CTA publishes this rank's return flag on every rank
+    BExchangeArgs x;
 };
 
 struct BNormArgs {
@@ -94,54 +138,12 @@ struct BRouterArgs {
     float eps;
     const uint16_t* wr;        // [E, H] bf16
     const float* bias;         // [E] or null
-    uint16_t* x_hi;            // [n, H] MoE input split
-    uint16_t* x_lo;
+    BExchangeArgs x;           // dispatch of the MoE input rows
     int* ids;                  // [n, k]
     float* weights;            // [n, k]
     int* route_hist;           // optional [n][layers][k] history of the step
     int layer, layers;
     int n, H, E, k;
-};
-
-// Exchange region of one rank (the same layout on every rank; every rank maps every other rank's region):
-//   rx      [world][cap] pair rows, each bf16 hi [H] then lo [H]   (written by the senders)
-//   rx_ids  [world][cap] expert of each pair                       (written by the senders)
-//   rx_n    [world] tokens of each sender in this layer           (written by the senders)
-//   cb      [cap] f32 [H] result rows of this rank's pairs        (written by the owners)
-//   flags   [2][world] u32, 128 bytes apart: dispatch, return     (written with release stores by the peers)
-struct XLayout {
-    size_t rx, rx_ids, rx_n, cb, flags, bytes;
-    int cap;  // pairs per sender: tokens per rank * k
-};
-
-XLayout x_layout(int world, int tokens_per_rank, int k, int H);
-
-struct BExchangeArgs {
-    unsigned char* const* peers;  // [world] exchange region of every rank (this rank's own at [rank])
-    XLayout lay;
-    int rank, world;
-    int experts_per_rank;
-    const unsigned int* epoch_base;  // flags carry epoch_base + layer + 1
-    int layer;
-    int* err;
-    unsigned int* counter;        // last-CTA election, zero between launches
-    // dispatch
-    const uint16_t* x_hi;         // [n, H]
-    const uint16_t* x_lo;
-    const int* ids;               // [n, k]
-    int n, k, H;
-    // group (owner): outputs for the grouped GEMMs and the return
-    int* x_rows;                  // [positions] -> rx row (sender * cap + pair)
-    int* src;                     // [positions] -> rx row, for the return
-    int* g_off;                   // [experts_per_rank]
-    int* g_cnt;
-    int* n_pos;                   // [1]
-    // return (owner)
-    const float* y;               // [positions, H]
-    // combine (sender)
-    float* h;                     // [n, H]
-    const float* weights;         // [n, k]
-    float resid;
 };
 
 struct BHeadArgs {
@@ -155,13 +157,39 @@ struct BHeadArgs {
     int layers;
 };
 
+// Batched decode attention: CTA per (split, KV head, token) over the token's sequence; splits of at most kBAttnRows
+// positions (S = ceil(max_len / kBAttnRows) splits), staged to shared memory with bulk copies; the last CTA of each
+// (token, KV head) merges the S partials.
+constexpr int kBAttnRows = 128;
+constexpr int kBAttnMaxSplits = 32;
+
+struct BAttnArgs {
+    const float* q;            // [n][heads * d] roped queries
+    const void* k_pool;        // [pages][kv_heads][page][d]
+    const void* v_pool;
+    const int* page_table;     // [sequences][pt_stride]
+    int pt_stride, page_size, kv_f32;
+    const int* seq;            // [n]
+    const int* pos;            // [sequences]: the token attends positions 0..pos
+    float* part_acc;           // [n][heads][S][d]
+    float* part_ml;            // [n][heads][S][2]
+    unsigned int* counters;    // [n][kv_heads], zero between launches
+    float* att_out;            // [n][heads * d]
+    uint16_t* att_hi;          // [n][heads * d] split of att_out
+    uint16_t* att_lo;
+    int* err;
+    int n, kv_heads, G, S, cap;  // cap: positions one split stages (>= ceil(max_len / S))
+    float scale;
+};
+
+cudaError_t launch_battention(const BAttnArgs& a, cudaStream_t s);
+size_t battn_smem(int cap, int kv_f32);
+
 cudaError_t launch_bgemm(const BGemmArgs& a, int epi, int groups, cudaStream_t s);
 cudaError_t launch_battn_norm(const BNormArgs& a, int n, cudaStream_t s);
 cudaError_t launch_brope_kv(const BRopeArgs& a, cudaStream_t s);
 cudaError_t launch_brouter(const BRouterArgs& a, cudaStream_t s);
-cudaError_t launch_ep_dispatch(const BExchangeArgs& a, cudaStream_t s);
 cudaError_t launch_ep_group(const BExchangeArgs& a, cudaStream_t s);
-cudaError_t launch_ep_return(const BExchangeArgs& a, int max_positions, cudaStream_t s);
 cudaError_t launch_ep_combine(const BExchangeArgs& a, cudaStream_t s);
 cudaError_t launch_bargmax(const BHeadArgs& a, cudaStream_t s);
 

@@ -25,6 +25,7 @@ struct lastro_batch {
     lastro_ctx* ctx = nullptr;
     int max_seqs = 0, max_len = 0, max_pages = 0, rank = 0, world = 1, epr = 0, e0 = 0;
     int ks_qkv = 1, ks_o = 1, R = 0;
+    int attn_S = 1, attn_cap = 1;  // attention splits per (token, KV head) and positions one split stages
     bool poisoned = false, connected = false, use_graphs = true;
     Arena arena;
     std::vector<void*> kpool, vpool;  // per layer: [max_seqs * max_pages pages][kv_heads][page][d]
@@ -34,8 +35,8 @@ struct lastro_batch {
     int *d_seq = nullptr, *d_tok = nullptr, *d_next = nullptr, *d_hist = nullptr;
     int *h_seq = nullptr, *h_tok = nullptr, *h_err = nullptr;  // pinned
     float *h = nullptr, *qkv_part = nullptr, *q = nullptr, *att = nullptr, *part_acc = nullptr, *part_ml = nullptr;
-    float *o_part = nullptr, *rw = nullptr, *y = nullptr, *logits = nullptr, *bias = nullptr;
-    uint16_t *xa_hi = nullptr, *xa_lo = nullptr, *att_hi = nullptr, *att_lo = nullptr, *xm_hi = nullptr, *xm_lo = nullptr;
+    float *o_part = nullptr, *rw = nullptr, *logits = nullptr, *bias = nullptr;
+    uint16_t *xa_hi = nullptr, *xa_lo = nullptr, *att_hi = nullptr, *att_lo = nullptr;
     uint16_t *a_hi = nullptr, *a_lo = nullptr;
     unsigned int *attn_counters = nullptr, *counters = nullptr, *epoch = nullptr;
     int *ids = nullptr, *route_hist = nullptr, *x_rows = nullptr, *src = nullptr, *g_off = nullptr, *g_cnt = nullptr;
@@ -46,11 +47,27 @@ struct lastro_batch {
     std::vector<void*> opened;  // peer regions mapped from IPC handles
     std::map<int, cudaGraphExec_t> graphs;  // one per token count
     bool has_bias = false, want_hist = false;
+    // profiling: an event recorded after every launch of a direct (uncaptured) step, with the launch's kind
+    std::vector<cudaEvent_t>* prof_ev = nullptr;
+    std::vector<int>* prof_kind = nullptr;
 };
 
 namespace {
 
 int bfail(lastro_batch* b, cudaError_t e, const char* what) { return cuda_fail(b->ctx, &b->poisoned, e, what); }
+
+// kernel kinds of the batched step, in launch order within a layer, then the head
+enum { BK_NORM = 0, BK_QKV, BK_ROPE, BK_ATTN, BK_OPROJ, BK_ROUTER, BK_GROUP, BK_GATE_UP, BK_DOWN, BK_COMBINE,
+       BK_LM_HEAD, BK_ARGMAX, BK_COUNT };
+
+cudaError_t mark(lastro_batch* b, cudaStream_t s, int kind, cudaError_t e) {
+    if (e != cudaSuccess || !b->prof_ev) return e;
+    cudaEvent_t ev;
+    if ((e = cudaEventCreate(&ev)) != cudaSuccess) return e;
+    b->prof_ev->push_back(ev);
+    b->prof_kind->push_back(kind);
+    return cudaEventRecord(ev, s);
+}
 
 #define BTRY(expr, what)                                        \
     do {                                                        \
@@ -63,7 +80,7 @@ int pick_ks(int rows, int K, int n_sm) {
     const int tiles = (rows + kBRows - 1) / kBRows, chunks = K / kBK;
     int best = 1;
     for (int d = 1; d <= chunks; ++d)
-        if (chunks % d == 0 && K / d >= 128 && tiles * d <= 2 * n_sm) best = d;
+        if (chunks % d == 0 && K / d >= 128 && tiles * d <= 2 * n_sm && d <= 16) best = d;
     return best;
 }
 
@@ -80,9 +97,6 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
     xa.experts_per_rank = b->epr;
     xa.epoch_base = b->epoch;
     xa.err = b->d_err;
-    xa.x_hi = b->xm_hi;
-    xa.x_lo = b->xm_lo;
-    xa.ids = b->ids;
     xa.n = n;
     xa.k = k;
     xa.H = H;
@@ -91,25 +105,28 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
     xa.g_off = b->g_off;
     xa.g_cnt = b->g_cnt;
     xa.n_pos = b->n_pos;
-    xa.y = b->y;
     xa.h = b->h;
     xa.weights = b->rw;
     xa.resid = d.residual_multiplier;
+    xa.eps = d.eps;
+    xa.xn_hi = b->xa_hi;
+    xa.xn_lo = b->xa_lo;
     const uint16_t* rx = reinterpret_cast<const uint16_t*>(b->xreg + b->lay.rx);
+    // layer 0's attention norm on the embedding rows; every later norm (and the final one) comes out of the combine
+    BNormArgs na{};
+    na.h = b->h;
+    na.embed = m->embed;
+    na.tokens = b->d_tok;
+    na.emb_mult = d.embedding_multiplier;
+    na.ln = m->L[0].ln_attn;
+    na.eps = d.eps;
+    na.x_hi = b->xa_hi;
+    na.x_lo = b->xa_lo;
+    na.H = H;
+    if ((e = mark(b, s, BK_NORM, launch_battn_norm(na, n, s)))) return e;
     for (int l = 0; l < d.layers && e == cudaSuccess; ++l) {
         const LayerDev& L = m->L[l];
-        BNormArgs na{};
-        na.h = b->h;
-        na.embed = l == 0 ? m->embed : nullptr;
-        na.tokens = b->d_tok;
-        na.emb_mult = d.embedding_multiplier;
-        na.ln = L.ln_attn;
-        na.eps = d.eps;
-        na.x_hi = b->xa_hi;
-        na.x_lo = b->xa_lo;
-        na.H = H;
-        if ((e = launch_battn_norm(na, n, s))) break;
-
+        xa.layer = l;
         BGemmArgs ga{};
         ga.w = reinterpret_cast<const uint16_t*>(L.wqkv);
         ga.rows = R;
@@ -123,7 +140,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         ga.ldy = R;
         ga.z_stride = (long long)n * R;
         ga.div = 1.0f;
-        if ((e = launch_bgemm(ga, BEPI_STORE, 1, s))) break;
+        if ((e = mark(b, s, BK_QKV, launch_bgemm(ga, BEPI_STORE, 1, s)))) break;
 
         BRopeArgs ra{};
         ra.part = b->qkv_part;
@@ -143,33 +160,32 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         ra.kvd = kvd;
         ra.d = d.head_dim;
         ra.kv_heads = d.kv_heads;
-        if ((e = launch_brope_kv(ra, s))) break;
+        if ((e = mark(b, s, BK_ROPE, launch_brope_kv(ra, s)))) break;
 
-        AttnArgs aa{};
+        BAttnArgs aa{};
         aa.q = b->q;
         aa.k_pool = b->kpool[l];
         aa.v_pool = b->vpool[l];
         aa.page_table = b->page_table;
+        aa.pt_stride = b->max_pages;
         aa.page_size = kPageSize;
         aa.kv_f32 = ra.kv_f32;
+        aa.seq = b->d_seq;
         aa.pos = b->d_pos;
         aa.part_acc = b->part_acc;
         aa.part_ml = b->part_ml;
         aa.counters = b->attn_counters;
         aa.att_out = b->att;
-        aa.err = b->d_err;
-        aa.kv_heads = d.kv_heads;
-        aa.G = m->G;
-        aa.d = d.head_dim;
-        aa.max_len = b->max_len;
-        aa.split_cap = attn_split_cap(b->max_len);
-        aa.scale = d.attention_multiplier;
-        aa.seq = b->d_seq;
-        aa.tokens = n;
-        aa.pt_stride = b->max_pages;
         aa.att_hi = b->att_hi;
         aa.att_lo = b->att_lo;
-        if ((e = launch_attention(aa, s, false))) break;
+        aa.err = b->d_err;
+        aa.n = n;
+        aa.kv_heads = d.kv_heads;
+        aa.G = m->G;
+        aa.S = b->attn_S;
+        aa.cap = b->attn_cap;
+        aa.scale = d.attention_multiplier;
+        if ((e = mark(b, s, BK_ATTN, launch_battention(aa, s)))) break;
 
         BGemmArgs oa{};
         oa.w = reinterpret_cast<const uint16_t*>(L.wo);
@@ -184,7 +200,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         oa.ldy = H;
         oa.z_stride = (long long)n * H;
         oa.div = 1.0f;
-        if ((e = launch_bgemm(oa, BEPI_STORE, 1, s))) break;
+        if ((e = mark(b, s, BK_OPROJ, launch_bgemm(oa, BEPI_STORE, 1, s)))) break;
 
         BRouterArgs rta{};
         rta.h = b->h;
@@ -195,8 +211,8 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         rta.eps = d.eps;
         rta.wr = reinterpret_cast<const uint16_t*>(L.router);
         rta.bias = b->has_bias ? b->bias + (size_t)l * E : nullptr;
-        rta.x_hi = b->xm_hi;
-        rta.x_lo = b->xm_lo;
+        rta.x = xa;
+        rta.x.counter = b->counters;
         rta.ids = b->ids;
         rta.weights = b->rw;
         rta.route_hist = b->want_hist ? b->route_hist : nullptr;
@@ -206,12 +222,9 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         rta.H = H;
         rta.E = E;
         rta.k = k;
-        if ((e = launch_brouter(rta, s))) break;
+        if ((e = mark(b, s, BK_ROUTER, launch_brouter(rta, s)))) break;
 
-        xa.layer = l;
-        xa.counter = b->counters;
-        if ((e = launch_ep_dispatch(xa, s))) break;
-        if ((e = launch_ep_group(xa, s))) break;
+        if ((e = mark(b, s, BK_GROUP, launch_ep_group(xa, s)))) break;
 
         BGemmArgs gu{};
         gu.w = reinterpret_cast<const uint16_t*>(L.gate_up);
@@ -230,7 +243,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         gu.a_lo = b->a_lo;
         gu.I = I;
         gu.div = 1.0f;
-        if ((e = launch_bgemm(gu, BEPI_SWIGLU, b->epr, s))) break;
+        if ((e = mark(b, s, BK_GATE_UP, launch_bgemm(gu, BEPI_SWIGLU, b->epr, s)))) break;
 
         BGemmArgs dn{};
         dn.w = reinterpret_cast<const uint16_t*>(L.down);
@@ -244,24 +257,16 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         dn.ldx = I;
         dn.g_off = b->g_off;
         dn.g_cnt = b->g_cnt;
-        dn.y = b->y;
-        dn.ldy = H;
         dn.div = 1.0f;
-        if ((e = launch_bgemm(dn, BEPI_STORE, b->epr, s))) break;
+        dn.x = xa;
+        dn.x.counter = b->counters + 32;
+        if ((e = mark(b, s, BK_DOWN, launch_bgemm(dn, BEPI_RETURN, b->epr, s)))) break;
 
-        xa.counter = b->counters + 32;
-        if ((e = launch_ep_return(xa, b->world * b->lay.cap, s))) break;
-        if ((e = launch_ep_combine(xa, s))) break;
+        BExchangeArgs ca = xa;
+        ca.ln_next = l + 1 < d.layers ? m->L[l + 1].ln_attn : m->norm;
+        if ((e = mark(b, s, BK_COMBINE, launch_ep_combine(ca, s)))) break;
     }
     if (e) return e;
-    BNormArgs fa{};
-    fa.h = b->h;
-    fa.ln = m->norm;
-    fa.eps = d.eps;
-    fa.x_hi = b->xa_hi;
-    fa.x_lo = b->xa_lo;
-    fa.H = H;
-    if ((e = launch_battn_norm(fa, n, s))) return e;
     BGemmArgs ha{};
     ha.w = m->embed;
     ha.rows = d.vocab;
@@ -274,7 +279,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
     ha.y = b->logits;
     ha.ldy = d.vocab;
     ha.div = d.logits_scaling;
-    if ((e = launch_bgemm(ha, BEPI_STORE, 1, s))) return e;
+    if ((e = mark(b, s, BK_LM_HEAD, launch_bgemm(ha, BEPI_STORE, 1, s)))) return e;
     BHeadArgs hd{};
     hd.logits = b->logits;
     hd.V = d.vocab;
@@ -285,7 +290,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
     hd.tokens = b->d_tok;
     hd.epoch_base = b->epoch;
     hd.layers = d.layers;
-    return launch_bargmax(hd, s);
+    return mark(b, s, BK_ARGMAX, launch_bargmax(hd, s));
 }
 
 int run_bstep(lastro_batch* b, int n) {
@@ -365,12 +370,13 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
         return set_err(ctx, LASTRO_E_ARG, "batch: max_seqs %d, max_len %d, rank %d of %d", max_seqs, max_len, rank, world);
     if (m->q8) return set_err(ctx, LASTRO_E_UNSUPPORTED, "batched decode runs bf16 weights");
     if (d.experts % world) return set_err(ctx, LASTRO_E_UNSUPPORTED, "%d experts over %d ranks", d.experts, world);
-    if (d.hidden % kBK || m->qd % kBK || d.inter % 64 || d.hidden > 2048)
-        return set_err(ctx, LASTRO_E_UNSUPPORTED, "batched GEMMs need hidden, heads*head_dim, inter multiples of 64");
+    if (d.hidden % kBRows || m->qd % kBK || d.inter % 64 || d.hidden > 2048)
+        return set_err(ctx, LASTRO_E_UNSUPPORTED, "batched GEMMs need hidden a multiple of 128, heads*head_dim and inter of 64");
     if (world * max_seqs * d.k > kBMaxSlots)
         return set_err(ctx, LASTRO_E_UNSUPPORTED, "world x max_seqs x k = %d pairs exceed %d", world * max_seqs * d.k, kBMaxSlots);
-    if (attn_smem(max_len, d.kv_dtype == LASTRO_DTYPE_F32) > kMaxSmemBytes)
-        return set_err(ctx, LASTRO_E_UNSUPPORTED, "max_len %d: attention tiles exceed shared memory", max_len);
+    const int attn_S = (max_len + kBAttnRows - 1) / kBAttnRows;
+    if (attn_S > kBAttnMaxSplits)
+        return set_err(ctx, LASTRO_E_UNSUPPORTED, "max_len %d beyond %d positions", max_len, kBAttnRows * kBAttnMaxSplits);
     cudaSetDevice(ctx->device);
     int n_sm = 148;
     cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, ctx->device);
@@ -385,6 +391,8 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
     b->epr = d.experts / world;
     b->e0 = rank * b->epr;
     b->R = m->qd + 2 * m->kvd;
+    b->attn_S = attn_S;
+    b->attn_cap = (max_len + attn_S - 1) / attn_S + 1;
     b->ks_qkv = pick_ks(b->R, d.hidden, n_sm);
     b->ks_o = pick_ks(d.hidden, m->qd, n_sm);
     b->pos_host.assign(max_seqs, 0);
@@ -404,13 +412,13 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
           A.alloc(&b->d_hist, (size_t)max_len * S) || A.alloc(&b->h, S * H) || A.alloc(&b->xa_hi, S * H) ||
           A.alloc(&b->xa_lo, S * H) || A.alloc(&b->qkv_part, (size_t)b->ks_qkv * S * b->R) ||
           A.alloc(&b->q, S * m->qd) || A.alloc(&b->att, S * m->qd) || A.alloc(&b->att_hi, S * m->qd) ||
-          A.alloc(&b->att_lo, S * m->qd) || A.alloc(&b->part_acc, S * d.heads * kAttnSplits * d.head_dim) ||
-          A.alloc(&b->part_ml, S * d.heads * kAttnSplits * 2) || A.alloc(&b->attn_counters, S * d.kv_heads) ||
+          A.alloc(&b->att_lo, S * m->qd) || A.alloc(&b->part_acc, S * d.heads * attn_S * d.head_dim) ||
+          A.alloc(&b->part_ml, S * d.heads * attn_S * 2) || A.alloc(&b->attn_counters, S * d.kv_heads) ||
           A.alloc(&b->o_part, (size_t)b->ks_o * S * H) || A.alloc(&b->ids, S * k) || A.alloc(&b->rw, S * k) ||
-          A.alloc(&b->xm_hi, S * H) || A.alloc(&b->xm_lo, S * H) || A.alloc(&b->bias, (size_t)d.layers * E) ||
+          A.alloc(&b->bias, (size_t)d.layers * E) ||
           A.alloc(&b->x_rows, pairs) || A.alloc(&b->src, pairs) || A.alloc(&b->g_off, kMaxExperts) ||
           A.alloc(&b->g_cnt, kMaxExperts) || A.alloc(&b->n_pos, 1) || A.alloc(&b->a_hi, pairs * I) ||
-          A.alloc(&b->a_lo, pairs * I) || A.alloc(&b->y, pairs * H) || A.alloc(&b->logits, S * V) ||
+          A.alloc(&b->a_lo, pairs * I) || A.alloc(&b->logits, S * V) ||
           A.alloc(&b->route_hist, S * d.layers * k) || A.alloc(&b->counters, 64) || A.alloc(&b->epoch, 1) ||
           A.alloc(&b->d_err, 1) || A.alloc(&b->xreg, b->lay.bytes) || A.alloc(&b->d_peers, (size_t)world);
     if (!bad) bad = cudaMallocHost(&b->h_seq, sizeof(int) * S) != cudaSuccess;
@@ -615,6 +623,46 @@ extern "C" int lastro_batch_reset(lastro_batch* b, int32_t seq) {
 extern "C" int lastro_batch_position(const lastro_batch* b, int32_t seq, int32_t* pos) {
     if (!b || !pos || seq < 0 || seq >= b->max_seqs) return LASTRO_E_ARG;
     *pos = b->pos_host[seq];
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_batch_profile(lastro_batch* b, int32_t n, const int32_t* seq_ids, const int32_t* tokens,
+                                    int32_t steps, float* kernel_ms, int32_t n_kinds) {
+    if (!b || !kernel_ms || n_kinds < BK_COUNT || steps < 1) return LASTRO_E_ARG;
+    int rc = bready(b);
+    if (rc) return rc;
+    cudaSetDevice(b->ctx->device);
+    if ((rc = bstage(b, n, seq_ids, tokens, steps))) return rc;
+    cudaStream_t s = b->ctx->stream;
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> kind;
+    cudaEvent_t start;
+    BTRY(cudaEventCreate(&start), "profile");
+    for (int k = 0; k < n_kinds; ++k) kernel_ms[k] = 0.0f;
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < steps && e == cudaSuccess; ++i) {
+        ev.clear();
+        kind.clear();
+        b->prof_ev = &ev;
+        b->prof_kind = &kind;
+        e = cudaEventRecord(start, s);
+        if (e == cudaSuccess) e = enqueue_bstep(b, n, s);
+        b->prof_ev = nullptr;
+        b->prof_kind = nullptr;
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        cudaEvent_t prev = start;
+        for (size_t j = 0; j < ev.size() && e == cudaSuccess; ++j) {
+            float ms = 0.0f;
+            e = cudaEventElapsedTime(&ms, prev, ev[j]);
+            kernel_ms[kind[j]] += ms / (float)steps;
+            prev = ev[j];
+        }
+        for (cudaEvent_t x : ev) cudaEventDestroy(x);
+    }
+    cudaEventDestroy(start);
+    if (e) return bfail(b, e, "batch profile");
+    if ((rc = bfinish(b, "batch profile"))) return rc;
+    for (int i = 0; i < n; ++i) b->pos_host[seq_ids[i]] += steps;
     return LASTRO_OK;
 }
 

@@ -85,6 +85,8 @@ EXPORTS = {
     "lastro_batch_reset": (C.c_int, [C.c_void_p, C.c_int32]),
     "lastro_batch_position": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_int32)]),
     "lastro_batch_set_options": (C.c_int, [C.c_void_p, C.c_int32]),
+    "lastro_batch_profile": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p,
+                                       C.c_int32]),
     "lastro_batch_destroy": (None, [C.c_void_p]),
 }
 
@@ -375,6 +377,17 @@ class GpuBatch:
 
     def set_options(self, graphs: bool = True):
         self.ctx.check(lib().lastro_batch_set_options(self.h, int(graphs)))
+
+    KERNELS = ("norm", "qkv", "rope_kv", "attention", "oproj", "router", "group", "gate_up", "down", "combine",
+               "lm_head", "argmax")
+
+    def profile(self, seq_ids, tokens, steps: int) -> dict:
+        """Mean device ms per step of each kernel kind (summed over layers), direct launches timed with events."""
+        sq = np.ascontiguousarray(seq_ids, dtype=np.int32)
+        tk = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.zeros(len(self.KERNELS), np.float32)
+        self.ctx.check(lib().lastro_batch_profile(self.h, sq.size, _p(sq), _p(tk), steps, _p(out), out.size))
+        return dict(zip(self.KERNELS, out.tolist()))
 
     def close(self):
         if getattr(self, "h", None):
