@@ -174,7 +174,9 @@ int lastro_batch_position(const lastro_batch *batch, int32_t seq, int32_t *pos);
  * (n_kinds >= 12) */
 int lastro_batch_profile(lastro_batch *batch, int32_t n, const int32_t *seq_ids, const int32_t *tokens, int32_t steps,
                          float *kernel_ms, int32_t n_kinds);
-int lastro_batch_set_options(lastro_batch *batch, int32_t use_graphs);
+/* use_graphs: replay each step as a CUDA graph (default 1); use_tcgen05: the GEMMs on the 5th-generation tensor cores
+ * with tensor-memory accumulators (default 1) or on mma.sync (0) */
+int lastro_batch_set_options(lastro_batch *batch, int32_t use_graphs, int32_t use_tcgen05);
 void lastro_batch_destroy(lastro_batch *batch);
 
 #ifdef __cplusplus

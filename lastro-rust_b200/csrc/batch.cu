@@ -70,9 +70,12 @@ LDEV bool wait_flag(const unsigned int* flag, unsigned int want, int* err, int c
     return true;
 }
 
-// last-CTA election across a grid whose CTAs wrote to other GPUs: system-scope fence first
+// Last-CTA election across a grid whose CTAs wrote to other GPUs.  Each CTA orders its writes before its arrival with
+// a GPU-scope fence; the last CTA, which has observed every arrival, then issues one system-scope fence before it
+// publishes the flag with a system-scope release store: every CTA's peer writes precede the flag in causality order,
+// without a system-scope fence in each of the grid's CTAs.
 LDEV bool last_block_arrives_sys(unsigned int* counter, unsigned int total, bool* flag_smem) {
-    __threadfence_system();
+    __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
         const unsigned int t = atomicAdd(counter, 1u);
@@ -867,6 +870,254 @@ __global__ void __launch_bounds__(256) bargmax_kernel(BHeadArgs a) {
     if (t == 0) *a.epoch_base += (unsigned int)a.layers;
 }
 
+// ------------------------------------------------------------------------------------------------------------------
+// The same GEMM on the 5th-generation tensor cores.  The shared-memory tiles are those of bgemm_kernel (rows of 128 bytes,
+// 16-byte chunk c of row r at c ^ (r & 7): the 128-byte swizzle of the K-major canonical layout, atoms of 8 rows = 1024
+// bytes), loaded by all threads with cp.async; thread 0 issues, per 16-wide K step, tcgen05.mma kind::f16 (bf16 A = 128
+// weight rows, bf16 B = the N token rows, N = n rounded up to 16) twice -- x hi, then x lo -- into one f32 accumulator of
+// 128 lanes x N columns in tensor memory, and commits each stage to an mbarrier that frees the stage for the next load.
+// The epilogue reads the accumulator with tcgen05.ld (warp w: lanes 32w..32w+31 = weight rows, one register per token).
+// ------------------------------------------------------------------------------------------------------------------
+namespace {
+
+LDEV uint64_t smem_desc_sw128(uint32_t addr) {
+    // start address >> 4 [0,14), leading byte offset 16 B >> 4 [16,30), stride byte offset 1024 B >> 4 [32,46),
+    // descriptor version 1 [46,48), base offset 0, 128-byte swizzle (2) [61,64)
+    return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) |
+           ((uint64_t)2 << 61);
+}
+
+// kind::f16 instruction descriptor: f32 accumulator (bits 4-5 = 1), bf16 A and B (bits 7-9, 10-12 = 1), both K-major,
+// N >> 3 at bits 17-22, M >> 4 at bits 24-28
+LDEV uint32_t idesc_bf16_f32(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+LDEV void tc_mma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, bool accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"((uint32_t)accumulate)
+        : "memory");
+}
+
+LDEV void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+LDEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+LDEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+LDEV void tc_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+constexpr int kTmemCols = 64;  // accumulator columns (tokens of one tile)
+
+}  // namespace
+
+template <int EPI>
+__global__ void __launch_bounds__(128) bgemm_tc_kernel(BGemmArgs a) {
+    extern __shared__ unsigned char smem_dyn[];
+    // tiles on a 1024-byte boundary (the swizzle atom); the launch reserves the slack
+    unsigned char* smem = smem_dyn + ((1024 - (smem_addr(smem_dyn) & 1023)) & 1023);
+    __shared__ __align__(8) uint64_t bar[kBStages];
+    __shared__ uint32_t tmem_base;
+    __shared__ bool is_last;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = blockIdx.y, bx = blockIdx.x;
+    pdl_wait();
+    pdl_launch();
+    int p0 = 0, ntot = a.n;
+    if (a.g_cnt) {
+        p0 = __ldcg(a.g_off + g);
+        ntot = __ldcg(a.g_cnt + g);
+    }
+    const uint16_t* W = a.w + (size_t)(a.group0 + g) * a.group_stride;
+    const int kbeg = blockIdx.z * a.k_split;
+    const int nk = min(a.k_split, a.K - kbeg) / kBK;
+    if (nk <= 0) ntot = 0;
+    if (EPI != BEPI_RETURN && ntot <= 0) return;  // (a RETURN CTA still votes below)
+    const int ch = tid & 7;
+    auto grow_of = [&](int sr) -> int {
+        if (EPI == BEPI_SWIGLU) return sr < 64 ? bx * 64 + sr : a.I + bx * 64 + (sr - 64);
+        return bx * kBRows + sr;
+    };
+    if (ntot > 0) {
+        if (warp == 0) {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
+                         "r"(kTmemCols)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
+        if (tid == 0)
+            for (int i = 0; i < kBStages; ++i) mbar_init(&bar[i], 1);
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    const uint32_t tmem = tmem_base;
+    // per stage barrier: bit s of `used` once a commit has targeted it, bit s of `par` the parity of its commit count
+    // (every thread tracks them alike); the wait for the latest commit of stage s is on phase parity par_s ^ 1
+    uint32_t used = 0, par = 0;
+    bool ok = true;
+
+    for (int t0 = 0; t0 < ntot && ok; t0 += kBTok) {
+        const int n = min(kBTok, ntot - t0);
+        const int N = (n + 15) & ~15;
+        const uint32_t idesc = idesc_bf16_f32(128, N);
+        int xrow[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int tok = (tid >> 3) + 16 * i;
+            const int p = p0 + t0 + tok;
+            xrow[i] = tok < n ? (a.x_rows ? __ldcg(a.x_rows + p) : p) : 0;
+        }
+        auto load_stage = [&](int slot, int kt) {
+            unsigned char* st = smem + (size_t)slot * kBStageBytes;
+            const int k0 = kbeg + kt * kBK + ch * 8;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int sr = (tid >> 3) + 16 * i;
+                const int gr = grow_of(sr);
+                const bool v = gr < a.rows;
+                cp_async16(smem_addr(st) + swz(sr, ch), W + (size_t)(v ? gr : 0) * a.K + k0, v);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int tok = (tid >> 3) + 16 * i;
+                const bool v = tok < n;
+                const size_t xo = (size_t)xrow[i] * a.ldx + k0;
+                const uint32_t d = swz(tok, ch);
+                cp_async16(smem_addr(st + kBRows * 128) + d, a.x_hi + xo, v);
+                cp_async16(smem_addr(st + kBRows * 128 + kBTok * 128) + d, a.x_lo + xo, v);
+            }
+        };
+        // wait until the MMAs that read `slot` last have completed (bounded)
+        auto stage_free = [&](int slot) -> bool {
+            if (!((used >> slot) & 1)) return true;
+            return mbar_wait(&bar[slot], ((par >> slot) & 1) ^ 1, a.x.err, 5);
+        };
+#pragma unroll
+        for (int s = 0; s < kBStages - 1; ++s) {
+            if (s < nk) {
+                ok = ok && stage_free(s);
+                load_stage(s, s);
+            }
+            cp_async_commit();
+        }
+        for (int kt = 0; kt < nk; ++kt) {
+            const int slot = kt % kBStages;
+            cp_async_wait<kBStages - 2>();
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // cp.async data visible to the tensor core
+            __syncthreads();
+            if (tid == 0) {
+                tc_fence_after();
+                const uint32_t sW = smem_addr(smem + (size_t)slot * kBStageBytes);
+                const uint32_t sXh = sW + kBRows * 128, sXl = sXh + kBTok * 128;
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk) {
+                    const uint64_t ad = smem_desc_sw128(sW + kk * 32);
+                    tc_mma(tmem, ad, smem_desc_sw128(sXh + kk * 32), idesc, kt > 0 || kk > 0);
+                    tc_mma(tmem, ad, smem_desc_sw128(sXl + kk * 32), idesc, true);
+                }
+                tc_commit(&bar[slot]);
+            }
+            used |= 1u << slot;
+            par ^= 1u << slot;
+            const int pf = kt + kBStages - 1;
+            if (pf < nk) {
+                const int ps = pf % kBStages;
+                ok = ok && stage_free(ps);
+                load_stage(ps, pf);
+            }
+            cp_async_commit();
+        }
+        cp_async_wait<0>();
+        // every MMA of this tile done: the last stage's barrier (commits track all earlier MMAs of the thread)
+        const int last = (nk - 1) % kBStages;
+        ok = ok && mbar_wait(&bar[last], ((par >> last) & 1) ^ 1, a.x.err, 6);
+        tc_fence_after();
+        if (!ok) break;
+
+        // epilogue: thread (warp w, lane) holds tile row 32w + lane, columns = tokens
+        const int row = warp * 32 + lane;
+        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+        if (EPI == BEPI_STORE) {
+            const int gr = bx * kBRows + row;
+            for (int c0 = 0; c0 < N; c0 += 16) {
+                float v[16];
+                tc_ld16(trow + c0, v);
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const int tok = c0 + c;
+                    if (tok < n && gr < a.rows)
+                        a.y[blockIdx.z * a.z_stride + (size_t)(p0 + t0 + tok) * a.ldy + gr] =
+                            a.div == 1.0f ? v[c] : __fdiv_rn(v[c], a.div);
+                }
+            }
+        } else {
+            // stage the tile as [token][128 rows] f32 in shared memory (the pipeline buffers are free now)
+            __syncthreads();
+            float* stile = reinterpret_cast<float*>(smem);
+            for (int c0 = 0; c0 < N; c0 += 16) {
+                float v[16];
+                tc_ld16(trow + c0, v);
+#pragma unroll
+                for (int c = 0; c < 16; ++c) stile[(c0 + c) * kBRows + row] = v[c];
+            }
+            __syncthreads();
+            if (EPI == BEPI_SWIGLU) {
+                for (int i = tid; i < n * 64; i += 128) {
+                    const int tok = i >> 6, r = i & 63;
+                    const float gv = stile[tok * kBRows + r], uv = stile[tok * kBRows + 64 + r];
+                    const float v = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
+                    uint16_t hi, lo;
+                    split_bf16(v, hi, lo);
+                    const size_t o = (size_t)(p0 + t0 + tok) * a.I + bx * 64 + r;
+                    a.a_hi[o] = hi;
+                    a.a_lo[o] = lo;
+                }
+            } else {
+                const XLayout& L = a.x.lay;
+                for (int tok = warp; tok < n; tok += 4) {
+                    const int i = __ldcg(a.x.src + p0 + t0 + tok);
+                    const int sender = i / L.cap, pair = i - sender * L.cap;
+                    float4* dst = reinterpret_cast<float4*>(a.x.peers[sender] + L.cb +
+                                                            ((size_t)pair * a.rows + (size_t)bx * kBRows) * 4);
+                    dst[lane] = reinterpret_cast<const float4*>(stile + tok * kBRows)[lane];
+                }
+            }
+            __syncthreads();
+        }
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    if (ntot > 0) {
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 0)
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+    if (EPI == BEPI_RETURN) {
+        if (!last_block_arrives_sys(a.x.counter, gridDim.x * gridDim.y * gridDim.z, &is_last)) return;
+        if (tid < a.x.world) {
+            const unsigned int epoch = __ldcg(a.x.epoch_base) + a.x.layer + 1;
+            st_release_sys(flag_ptr(a.x.peers[tid], a.x.lay, 1, a.x.rank), epoch);
+        }
+    }
+}
+
 // ---- launchers: every batched kernel waits for its predecessor with griddepcontrol.wait first, so all launch with
 // programmatic dependent launch (the next kernel's launch overlaps the tail of the current one) -------------------
 template <typename Kern>
@@ -893,6 +1144,23 @@ cudaError_t launch_bgemm(const BGemmArgs& a, int epi, int groups, cudaStream_t s
     if (a.K % kBK || a.k_split % kBK || a.k_split <= 0 || a.ldx % 8 || groups < 1) return cudaErrorInvalidValue;
     const int ks = (a.K + a.k_split - 1) / a.k_split;
     cudaError_t e;
+    if (a.tc) {
+        const size_t smem = kBGemmSmem + 1024;
+        const dim3 block(128);
+        if (epi == BEPI_SWIGLU) {
+            if (a.I % 64 || a.rows != 2 * a.I || ks != 1) return cudaErrorInvalidValue;
+            if ((e = set_smem(bgemm_tc_kernel<BEPI_SWIGLU>, smem)) != cudaSuccess) return e;
+            return launch_pdl(bgemm_tc_kernel<BEPI_SWIGLU>, dim3(a.I / 64, groups, 1), block, smem, s, a);
+        }
+        if (epi == BEPI_RETURN) {
+            if (a.rows % kBRows || ks != 1 || a.x.world > 32) return cudaErrorInvalidValue;
+            if ((e = set_smem(bgemm_tc_kernel<BEPI_RETURN>, smem)) != cudaSuccess) return e;
+            return launch_pdl(bgemm_tc_kernel<BEPI_RETURN>, dim3(a.rows / kBRows, groups, 1), block, smem, s, a);
+        }
+        if ((e = set_smem(bgemm_tc_kernel<BEPI_STORE>, smem)) != cudaSuccess) return e;
+        return launch_pdl(bgemm_tc_kernel<BEPI_STORE>, dim3((a.rows + kBRows - 1) / kBRows, groups, ks), block, smem, s,
+                          a);
+    }
     if (epi == BEPI_SWIGLU) {
         if (a.I % 64 || a.rows != 2 * a.I || ks != 1) return cudaErrorInvalidValue;
         e = set_smem(bgemm_kernel<BEPI_SWIGLU>, kBGemmSmem);

@@ -101,6 +101,7 @@ struct BGemmArgs {
     // BEPI_RETURN: row block of position pos to the combine rows of its sender (x.src[pos]), then the grid's last
     // CTA publishes this rank's return flag on every rank
     BExchangeArgs x;
+    int tc;  // 1: tcgen05 tensor cores (accumulator in tensor memory); 0: mma.sync (accumulators in registers)
 };
 
 struct BNormArgs {

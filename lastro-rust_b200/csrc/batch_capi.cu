@@ -26,7 +26,7 @@ struct lastro_batch {
     int max_seqs = 0, max_len = 0, max_pages = 0, rank = 0, world = 1, epr = 0, e0 = 0;
     int ks_qkv = 1, ks_o = 1, R = 0;
     int attn_S = 1, attn_cap = 1;  // attention splits per (token, KV head) and positions one split stages
-    bool poisoned = false, connected = false, use_graphs = true;
+    bool poisoned = false, connected = false, use_graphs = true, use_tc = true;
     Arena arena;
     std::vector<void*> kpool, vpool;  // per layer: [max_seqs * max_pages pages][kv_heads][page][d]
     float* rope_cs = nullptr;
@@ -140,6 +140,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         ga.ldy = R;
         ga.z_stride = (long long)n * R;
         ga.div = 1.0f;
+        ga.tc = b->use_tc;
         if ((e = mark(b, s, BK_QKV, launch_bgemm(ga, BEPI_STORE, 1, s)))) break;
 
         BRopeArgs ra{};
@@ -200,6 +201,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         oa.ldy = H;
         oa.z_stride = (long long)n * H;
         oa.div = 1.0f;
+        oa.tc = b->use_tc;
         if ((e = mark(b, s, BK_OPROJ, launch_bgemm(oa, BEPI_STORE, 1, s)))) break;
 
         BRouterArgs rta{};
@@ -243,6 +245,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         gu.a_lo = b->a_lo;
         gu.I = I;
         gu.div = 1.0f;
+        gu.tc = b->use_tc;
         if ((e = mark(b, s, BK_GATE_UP, launch_bgemm(gu, BEPI_SWIGLU, b->epr, s)))) break;
 
         BGemmArgs dn{};
@@ -258,6 +261,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         dn.g_off = b->g_off;
         dn.g_cnt = b->g_cnt;
         dn.div = 1.0f;
+        dn.tc = b->use_tc;
         dn.x = xa;
         dn.x.counter = b->counters + 32;
         if ((e = mark(b, s, BK_DOWN, launch_bgemm(dn, BEPI_RETURN, b->epr, s)))) break;
@@ -279,6 +283,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
     ha.y = b->logits;
     ha.ldy = d.vocab;
     ha.div = d.logits_scaling;
+    ha.tc = b->use_tc;
     if ((e = mark(b, s, BK_LM_HEAD, launch_bgemm(ha, BEPI_STORE, 1, s)))) return e;
     BHeadArgs hd{};
     hd.logits = b->logits;
@@ -666,9 +671,14 @@ extern "C" int lastro_batch_profile(lastro_batch* b, int32_t n, const int32_t* s
     return LASTRO_OK;
 }
 
-extern "C" int lastro_batch_set_options(lastro_batch* b, int32_t use_graphs) {
+extern "C" int lastro_batch_set_options(lastro_batch* b, int32_t use_graphs, int32_t use_tcgen05) {
     if (!b) return LASTRO_E_ARG;
     b->use_graphs = use_graphs != 0;
+    if ((use_tcgen05 != 0) != b->use_tc) {  // the captured graphs hold the other GEMM kernels
+        for (auto& g : b->graphs) cudaGraphExecDestroy(g.second);
+        b->graphs.clear();
+    }
+    b->use_tc = use_tcgen05 != 0;
     return LASTRO_OK;
 }
 

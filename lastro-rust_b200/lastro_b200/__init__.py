@@ -84,7 +84,7 @@ EXPORTS = {
     "lastro_batch_fill_kv_synthetic": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_uint64, C.c_float]),
     "lastro_batch_reset": (C.c_int, [C.c_void_p, C.c_int32]),
     "lastro_batch_position": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_int32)]),
-    "lastro_batch_set_options": (C.c_int, [C.c_void_p, C.c_int32]),
+    "lastro_batch_set_options": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32]),
     "lastro_batch_profile": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p,
                                        C.c_int32]),
     "lastro_batch_destroy": (None, [C.c_void_p]),
@@ -375,8 +375,8 @@ class GpuBatch:
         self.ctx.check(lib().lastro_batch_position(self.h, seq, C.byref(v)))
         return v.value
 
-    def set_options(self, graphs: bool = True):
-        self.ctx.check(lib().lastro_batch_set_options(self.h, int(graphs)))
+    def set_options(self, graphs: bool = True, tcgen05: bool = True):
+        self.ctx.check(lib().lastro_batch_set_options(self.h, int(graphs), int(tcgen05)))
 
     KERNELS = ("norm", "qkv", "rope_kv", "attention", "oproj", "router", "group", "gate_up", "down", "combine",
                "lm_head", "argmax")

@@ -21,22 +21,24 @@ pytestmark = pytest.mark.gpu
 GATE = 1e-4
 
 
-def batch_for(ctx, cfg, w, max_seqs, max_len, kv="f32"):
+def batch_for(ctx, cfg, w, max_seqs, max_len, kv="f32", tc=True):
     m = LB.GpuModel(ctx, cfg, 8, kv_dtype=kv)
     m.load_weights(w)
     b = LB.GpuBatch(m, max_seqs, max_len)
     b.connect()
+    b.set_options(tcgen05=tc)
     return m, b
 
 
+@pytest.mark.parametrize("tc", [True, False], ids=["tcgen05", "mma.sync"])
 @pytest.mark.parametrize("kv", ["f32", "bf16"])
 @pytest.mark.parametrize("biased", [False, True], ids=["plain", "zipf-bias"])
 @pytest.mark.parametrize("base", ["tiny", "tiny768"])
-def test_batch_matches_oracle_per_sequence(gpu_ctx, pool, kv, biased, base):
+def test_batch_matches_oracle_per_sequence(gpu_ctx, pool, kv, tc, biased, base):
     cfg = CFG.TINY if base == "tiny" else CFG.TINY_768
     w = reference_tiny_weights(cfg)
     nseq, max_len = 5, 96
-    m, b = batch_for(gpu_ctx, cfg, w, nseq, max_len, kv)
+    m, b = batch_for(gpu_ctx, cfg, w, nseq, max_len, kv, tc)
     om = O.Model(cfg, weights=w)
     bias = CFG.zipf_router_bias(cfg, std=0.5) if biased else None
     if biased:
