@@ -64,7 +64,8 @@ def parse():
                     "decoding the prompt through the model")
     ap.add_argument("--layers", type=int, default=0, help="with --profile-only: a 3B-shaped model with this many "
                     "layers (small ncu captures; the kernels are those of the full model)")
-    ap.add_argument("--no-tcgen05", action="store_true", help="c5: the batched GEMMs on mma.sync instead of tcgen05")
+    ap.add_argument("--gemm", type=int, default=2, choices=(0, 1, 2), help="c5 GEMMs: 2 tcgen05 warp-specialised "
+                    "(TMA weight tiles), 1 tcgen05 with all-thread cp.async stages, 0 mma.sync")
     ap.add_argument("--fused", action="store_true", help="the fused step kernel (one persistent launch per step) instead "
                     "of the per-layer kernel chain")
     a = ap.parse_args()
@@ -272,7 +273,7 @@ def run_batched(a):
     else:
         batch.connect()
     batch.set_router_bias(CFG.zipf_router_bias(cfg))
-    batch.set_options(tcgen05=not a.no_tcgen05)
+    batch.set_options(gemm=a.gemm)
     seqs = list(range(n))
     t0 = time.time()
     if a.synthetic_kv:
@@ -362,8 +363,9 @@ def run_batched(a):
                    "mean_context": mean_ctx, "kv_cache": f"paged {a.kv}",
                    "parallelism": f"ep{world}: experts {E // world}/rank, attention data-parallel over sequences"
                    if world > 1 else "single GPU",
-                   "weights": "bf16; batched GEMMs on tensor cores (" + ("mma.sync" if a.no_tcgen05 else
-                              "tcgen05, accumulators in tensor memory") + ", bf16 operands, activations split hi + lo)",
+                   "weights": "bf16; batched GEMMs on tensor cores (" + ("mma.sync", "tcgen05, cp.async stages",
+                              "tcgen05 warp-specialised, TMA weight tiles")[a.gemm] + ", accumulators f32, bf16 operands, "
+                              "activations split hi + lo)",
                    "expert_load_share_by_rank": [round(x, 4) for x in share], "experts_touched": touched,
                    "router_bias": "Zipf(0.8), beta 0.8", "prefill": "synthetic KV" if a.synthetic_kv else
                    "teacher-forced batched steps", "prefill_s": round(prefill_s, 2),

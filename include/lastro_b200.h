@@ -175,7 +175,8 @@ int lastro_batch_position(const lastro_batch *batch, int32_t seq, int32_t *pos);
 int lastro_batch_profile(lastro_batch *batch, int32_t n, const int32_t *seq_ids, const int32_t *tokens, int32_t steps,
                          float *kernel_ms, int32_t n_kinds);
 /* use_graphs: replay each step as a CUDA graph (default 1); use_tcgen05: the GEMMs on the 5th-generation tensor cores
- * with tensor-memory accumulators (default 1) or on mma.sync (0) */
+ * with tensor-memory accumulators, warp-specialised with TMA weight tiles (2, default), the same with all threads
+ * loading the stages (1), or on mma.sync with register accumulators (0) */
 int lastro_batch_set_options(lastro_batch *batch, int32_t use_graphs, int32_t use_tcgen05);
 void lastro_batch_destroy(lastro_batch *batch);
 

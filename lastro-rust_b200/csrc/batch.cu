@@ -1,5 +1,6 @@
 // Batched decode step kernels (see batch.h for the step's order and the exchange region).
 #include <cuda_bf16.h>
+#include <cudaTypedefs.h>
 
 #include "batch.h"
 #include "common.cuh"
@@ -1118,6 +1119,245 @@ __global__ void __launch_bounds__(128) bgemm_tc_kernel(BGemmArgs a) {
     }
 }
 
+// ------------------------------------------------------------------------------------------------------------------
+// Warp-specialised tcgen05 GEMM (mode 2).  Per stage: 16 KB of weight rows by TMA (two boxes of 64 rows x 64 columns,
+// 128-byte swizzle, issued by lane 0 of warp 0) and the token rows' hi and lo (cp.async by warps 2-3, 16 each per
+// thread, arriving on the stage's full barrier when they land); lane 0 of warp 1 waits for the full barrier, issues
+// the 8 MMAs of the stage and commits them to the stage's empty barrier, which the producers wait on before they
+// refill it.  No block-wide barrier inside the K loop.  The epilogue (all 4 warps) follows the final commit.
+// ------------------------------------------------------------------------------------------------------------------
+namespace {
+
+LDEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+LDEV void cp_async_arrive_noinc(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+}  // namespace
+
+template <int EPI>
+__global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ CUtensorMap wmap, BGemmArgs a) {
+    constexpr int S = kBStages;
+    extern __shared__ unsigned char smem_dyn[];
+    unsigned char* smem = smem_dyn + ((1024 - (smem_addr(smem_dyn) & 1023)) & 1023);
+    __shared__ __align__(8) uint64_t full[S], empty[S], done;
+    __shared__ uint32_t tmem_base;
+    __shared__ bool is_last;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = blockIdx.y, bx = blockIdx.x;
+    pdl_wait();
+    pdl_launch();
+    int p0 = 0, ntot = a.n;
+    if (a.g_cnt) {
+        p0 = __ldcg(a.g_off + g);
+        ntot = __ldcg(a.g_cnt + g);
+    }
+    const int kbeg = blockIdx.z * a.k_split;
+    const int nk = min(a.k_split, a.K - kbeg) / kBK;
+    if (nk <= 0) ntot = 0;
+    if (EPI != BEPI_RETURN && ntot <= 0) return;  // (a RETURN CTA still votes below)
+    // weight rows of the tile's two 64-row boxes (row coordinates in the tensor map)
+    const int wrow0 = (a.group0 + g) * a.rows + (EPI == BEPI_SWIGLU ? bx * 64 : bx * kBRows);
+    const int wrow1 = (a.group0 + g) * a.rows + (EPI == BEPI_SWIGLU ? a.I + bx * 64 : bx * kBRows + 64);
+    if (ntot > 0) {
+        if (warp == 0) {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
+                         "r"(kTmemCols)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
+        if (tid == 0) {
+            for (int i = 0; i < S; ++i) {
+                mbar_init(&full[i], 1 + 64);  // the TMA thread's expect_tx arrival + 64 cp.async arrivals
+                mbar_init(&empty[i], 1);      // one MMA commit
+            }
+            mbar_init(&done, 1);
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+        }
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    const uint32_t tmem = tmem_base;
+    bool ok = true;
+    int it = 0;  // global stage counter over the CTA's tiles (stage it % S, round it / S)
+    int tile = 0;
+    for (int t0 = 0; t0 < ntot; t0 += kBTok, ++tile) {
+        const int n = min(kBTok, ntot - t0);
+        const int N = (n + 15) & ~15;
+        // (the whole of warps 0 and 1 runs their loops, lane 0 doing the work, so that the idle lanes wait at
+        // __syncwarp instead of spinning on a barrier in the lanes' own divergent path)
+        if (warp == 0) {
+            bool go = true;
+            for (int kt = 0; kt < nk && go; ++kt) {
+                if (lane == 0) {
+                    const int s = (it + kt) % S, r = (it + kt) / S;
+                    if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, a.x.err, 7)) {
+                        go = false;
+                    } else {
+                        unsigned char* st = smem + (size_t)s * kBStageBytes;
+                        mbar_expect_tx(&full[s], kBRows * 128);
+                        const int x = kbeg + kt * kBK;
+                        tma_load_2d(st, &wmap, x, wrow0, &full[s]);
+                        tma_load_2d(st + 64 * 128, &wmap, x, wrow1, &full[s]);
+                    }
+                }
+                go = __shfl_sync(0xffffffffu, go, 0);
+            }
+        } else if (warp == 1) {
+            const uint32_t idesc = idesc_bf16_f32(128, N);
+            bool go = true;
+            for (int kt = 0; kt < nk && go; ++kt) {
+                if (lane == 0) {
+                    const int s = (it + kt) % S, r = (it + kt) / S;
+                    if (!mbar_wait(&full[s], r & 1, a.x.err, 8)) {
+                        go = false;
+                    } else {
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the cp.async rows, for the MMA
+                        tc_fence_after();
+                        const uint32_t sW = smem_addr(smem + (size_t)s * kBStageBytes);
+                        const uint32_t sXh = sW + kBRows * 128, sXl = sXh + kBTok * 128;
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 16; ++kk) {
+                            const uint64_t ad = smem_desc_sw128(sW + kk * 32);
+                            tc_mma(tmem, ad, smem_desc_sw128(sXh + kk * 32), idesc, kt > 0 || kk > 0);
+                            tc_mma(tmem, ad, smem_desc_sw128(sXl + kk * 32), idesc, true);
+                        }
+                        tc_commit(&empty[s]);
+                    }
+                }
+                go = __shfl_sync(0xffffffffu, go, 0);
+            }
+            if (!go) ok = false;
+            if (lane == 0) tc_commit(&done);  // all MMAs of the tile
+            __syncwarp();
+        } else {
+            // warps 2-3: the token rows of every stage, 16 cp.async per thread, then an arrival when they land
+            const int pt = tid - 64;  // 0..63
+            const int ch = pt & 7;
+            int xrow[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int tok = (pt >> 3) + 8 * i;
+                const int p = p0 + t0 + tok;
+                xrow[i] = tok < n ? (a.x_rows ? __ldcg(a.x_rows + p) : p) : 0;
+            }
+            for (int kt = 0; kt < nk; ++kt) {
+                const int s = (it + kt) % S, r = (it + kt) / S;
+                if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, a.x.err, 9)) break;
+                unsigned char* st = smem + (size_t)s * kBStageBytes;
+                const int k0 = kbeg + kt * kBK + ch * 8;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int tok = (pt >> 3) + 8 * i;
+                    const bool v = tok < n;
+                    const size_t xo = (size_t)xrow[i] * a.ldx + k0;
+                    const uint32_t d = swz(tok, ch);
+                    cp_async16(smem_addr(st + kBRows * 128) + d, a.x_hi + xo, v);
+                    cp_async16(smem_addr(st + kBRows * 128 + kBTok * 128) + d, a.x_lo + xo, v);
+                }
+                cp_async_arrive_noinc(&full[s]);
+            }
+        }
+        it += nk;
+        // epilogue (all warps): after the tile's final commit
+        ok = mbar_wait(&done, tile & 1, a.x.err, 10) && ok;
+        tc_fence_after();
+        if (!ok) break;
+        const int row = warp * 32 + lane;
+        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+        if (EPI == BEPI_STORE) {
+            const int gr = bx * kBRows + row;
+            for (int c0 = 0; c0 < N; c0 += 16) {
+                float v[16];
+                tc_ld16(trow + c0, v);
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const int tok = c0 + c;
+                    if (tok < n && gr < a.rows)
+                        a.y[blockIdx.z * a.z_stride + (size_t)(p0 + t0 + tok) * a.ldy + gr] =
+                            a.div == 1.0f ? v[c] : __fdiv_rn(v[c], a.div);
+                }
+            }
+        } else {
+            // the pipeline buffers are idle: the tile goes through shared memory as [token][128 rows] f32
+            float* stile = reinterpret_cast<float*>(smem);
+            for (int c0 = 0; c0 < N; c0 += 16) {
+                float v[16];
+                tc_ld16(trow + c0, v);
+#pragma unroll
+                for (int c = 0; c < 16; ++c) stile[(c0 + c) * kBRows + row] = v[c];
+            }
+            __syncthreads();
+            if (EPI == BEPI_SWIGLU) {
+                for (int i = tid; i < n * 64; i += 128) {
+                    const int tok = i >> 6, r = i & 63;
+                    const float gv = stile[tok * kBRows + r], uv = stile[tok * kBRows + 64 + r];
+                    const float v = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
+                    uint16_t hi, lo;
+                    split_bf16(v, hi, lo);
+                    const size_t o = (size_t)(p0 + t0 + tok) * a.I + bx * 64 + r;
+                    a.a_hi[o] = hi;
+                    a.a_lo[o] = lo;
+                }
+            } else {
+                const XLayout& L = a.x.lay;
+                for (int tok = warp; tok < n; tok += 4) {
+                    const int i = __ldcg(a.x.src + p0 + t0 + tok);
+                    const int sender = i / L.cap, pair = i - sender * L.cap;
+                    float4* dst = reinterpret_cast<float4*>(a.x.peers[sender] + L.cb +
+                                                            ((size_t)pair * a.rows + (size_t)bx * kBRows) * 4);
+                    dst[lane] = reinterpret_cast<const float4*>(stile + tok * kBRows)[lane];
+                }
+            }
+        }
+        // the next tile's loads and MMAs reuse shared memory and the accumulator
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    if (ntot > 0) {
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 0)
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+    if (EPI == BEPI_RETURN) {
+        if (!last_block_arrives_sys(a.x.counter, gridDim.x * gridDim.y * gridDim.z, &is_last)) return;
+        if (tid < a.x.world) {
+            const unsigned int epoch = __ldcg(a.x.epoch_base) + a.x.layer + 1;
+            st_release_sys(flag_ptr(a.x.peers[tid], a.x.lay, 1, a.x.rank), epoch);
+        }
+    }
+}
+
+cudaError_t make_weight_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return e != cudaSuccess ? e : cudaErrorNotSupported;
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 2) % 16 || rows >= (1ull << 31)) return cudaErrorInvalidValue;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {64, 64};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 // ---- launchers: every batched kernel waits for its predecessor with griddepcontrol.wait first, so all launch with
 // programmatic dependent launch (the next kernel's launch overlaps the tail of the current one) -------------------
 template <typename Kern>
@@ -1140,10 +1380,28 @@ cudaError_t launch_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStre
     return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
-cudaError_t launch_bgemm(const BGemmArgs& a, int epi, int groups, cudaStream_t s) {
+cudaError_t launch_bgemm(const BGemmArgs& a, int epi, int groups, cudaStream_t s, const CUtensorMap* wmap) {
     if (a.K % kBK || a.k_split % kBK || a.k_split <= 0 || a.ldx % 8 || groups < 1) return cudaErrorInvalidValue;
     const int ks = (a.K + a.k_split - 1) / a.k_split;
     cudaError_t e;
+    if (a.tc == 2) {
+        if (!wmap) return cudaErrorInvalidValue;
+        const size_t smem = kBGemmSmem + 1024;
+        const dim3 block(128);
+        if (epi == BEPI_SWIGLU) {
+            if (a.I % 64 || a.rows != 2 * a.I || ks != 1) return cudaErrorInvalidValue;
+            if ((e = set_smem(bgemm_ws_kernel<BEPI_SWIGLU>, smem)) != cudaSuccess) return e;
+            return launch_pdl(bgemm_ws_kernel<BEPI_SWIGLU>, dim3(a.I / 64, groups, 1), block, smem, s, *wmap, a);
+        }
+        if (epi == BEPI_RETURN) {
+            if (a.rows % kBRows || ks != 1 || a.x.world > 32) return cudaErrorInvalidValue;
+            if ((e = set_smem(bgemm_ws_kernel<BEPI_RETURN>, smem)) != cudaSuccess) return e;
+            return launch_pdl(bgemm_ws_kernel<BEPI_RETURN>, dim3(a.rows / kBRows, groups, 1), block, smem, s, *wmap, a);
+        }
+        if ((e = set_smem(bgemm_ws_kernel<BEPI_STORE>, smem)) != cudaSuccess) return e;
+        return launch_pdl(bgemm_ws_kernel<BEPI_STORE>, dim3((a.rows + kBRows - 1) / kBRows, groups, ks), block, smem, s,
+                          *wmap, a);
+    }
     if (a.tc) {
         const size_t smem = kBGemmSmem + 1024;
         const dim3 block(128);

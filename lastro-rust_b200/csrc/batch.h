@@ -22,6 +22,7 @@
 // 2^-17 |x|), so the products carry f32-level accuracy rather than bf16 rounding of the activations.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -101,7 +102,10 @@ struct BGemmArgs {
     // BEPI_RETURN: row block of position pos to the combine rows of its sender (x.src[pos]), then the grid's last
     // CTA publishes this rank's return flag on every rank
     BExchangeArgs x;
-    int tc;  // 1: tcgen05 tensor cores (accumulator in tensor memory); 0: mma.sync (accumulators in registers)
+    // 0: mma.sync (register accumulators); 1: tcgen05, all threads load the stages with cp.async; 2: tcgen05,
+    // warp-specialised: weight tiles by TMA (the launch's tensor map), activation tiles by two cp.async warps, one
+    // thread issuing the MMAs
+    int tc;
 };
 
 struct BNormArgs {
@@ -186,7 +190,11 @@ struct BAttnArgs {
 cudaError_t launch_battention(const BAttnArgs& a, cudaStream_t s);
 size_t battn_smem(int cap, int kv_f32);
 
-cudaError_t launch_bgemm(const BGemmArgs& a, int epi, int groups, cudaStream_t s);
+// `wmap` (mode 2): 2-D bf16 tensor map over the weight rows [groups * rows][K], box 64 columns x 64 rows, 128-byte
+// swizzle (make_weight_map)
+cudaError_t launch_bgemm(const BGemmArgs& a, int epi, int groups, cudaStream_t s, const CUtensorMap* wmap = nullptr);
+// host: tensor map for launch_bgemm's mode 2 over a row-major bf16 matrix [rows][cols]
+cudaError_t make_weight_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols);
 cudaError_t launch_battn_norm(const BNormArgs& a, int n, cudaStream_t s);
 cudaError_t launch_brope_kv(const BRopeArgs& a, cudaStream_t s);
 cudaError_t launch_brouter(const BRouterArgs& a, cudaStream_t s);

@@ -26,7 +26,10 @@ struct lastro_batch {
     int max_seqs = 0, max_len = 0, max_pages = 0, rank = 0, world = 1, epr = 0, e0 = 0;
     int ks_qkv = 1, ks_o = 1, R = 0;
     int attn_S = 1, attn_cap = 1;  // attention splits per (token, KV head) and positions one split stages
-    bool poisoned = false, connected = false, use_graphs = true, use_tc = true;
+    bool poisoned = false, connected = false, use_graphs = true;
+    int gemm_mode = 2;  // 0 mma.sync, 1 tcgen05 (cp.async stages), 2 tcgen05 warp-specialised (TMA weight tiles)
+    // TMA tensor maps of the weights (mode 2): per layer qkv, o, gate_up, down; then the embedding (lm_head)
+    std::vector<CUtensorMap> wmaps;
     Arena arena;
     std::vector<void*> kpool, vpool;  // per layer: [max_seqs * max_pages pages][kv_heads][page][d]
     float* rope_cs = nullptr;
@@ -74,6 +77,11 @@ cudaError_t mark(lastro_batch* b, cudaStream_t s, int kind, cudaError_t e) {
         cudaError_t e_ = (expr);                                \
         if (e_ != cudaSuccess) return bfail(b, e_, what);       \
     } while (0)
+
+const CUtensorMap* wmap(const lastro_batch* b, int layer, int which) {
+    const size_t i = (size_t)layer * 4 + which;
+    return i < b->wmaps.size() ? &b->wmaps[i] : nullptr;
+}
 
 // split-K slices for a dense GEMM of `rows` x K: enough CTAs for two per SM, slices of at least 128 columns
 int pick_ks(int rows, int K, int n_sm) {
@@ -140,8 +148,8 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         ga.ldy = R;
         ga.z_stride = (long long)n * R;
         ga.div = 1.0f;
-        ga.tc = b->use_tc;
-        if ((e = mark(b, s, BK_QKV, launch_bgemm(ga, BEPI_STORE, 1, s)))) break;
+        ga.tc = b->gemm_mode;
+        if ((e = mark(b, s, BK_QKV, launch_bgemm(ga, BEPI_STORE, 1, s, wmap(b, l, 0))))) break;
 
         BRopeArgs ra{};
         ra.part = b->qkv_part;
@@ -201,8 +209,8 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         oa.ldy = H;
         oa.z_stride = (long long)n * H;
         oa.div = 1.0f;
-        oa.tc = b->use_tc;
-        if ((e = mark(b, s, BK_OPROJ, launch_bgemm(oa, BEPI_STORE, 1, s)))) break;
+        oa.tc = b->gemm_mode;
+        if ((e = mark(b, s, BK_OPROJ, launch_bgemm(oa, BEPI_STORE, 1, s, wmap(b, l, 1))))) break;
 
         BRouterArgs rta{};
         rta.h = b->h;
@@ -245,8 +253,8 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         gu.a_lo = b->a_lo;
         gu.I = I;
         gu.div = 1.0f;
-        gu.tc = b->use_tc;
-        if ((e = mark(b, s, BK_GATE_UP, launch_bgemm(gu, BEPI_SWIGLU, b->epr, s)))) break;
+        gu.tc = b->gemm_mode;
+        if ((e = mark(b, s, BK_GATE_UP, launch_bgemm(gu, BEPI_SWIGLU, b->epr, s, wmap(b, l, 2))))) break;
 
         BGemmArgs dn{};
         dn.w = reinterpret_cast<const uint16_t*>(L.down);
@@ -261,10 +269,10 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         dn.g_off = b->g_off;
         dn.g_cnt = b->g_cnt;
         dn.div = 1.0f;
-        dn.tc = b->use_tc;
+        dn.tc = b->gemm_mode;
         dn.x = xa;
         dn.x.counter = b->counters + 32;
-        if ((e = mark(b, s, BK_DOWN, launch_bgemm(dn, BEPI_RETURN, b->epr, s)))) break;
+        if ((e = mark(b, s, BK_DOWN, launch_bgemm(dn, BEPI_RETURN, b->epr, s, wmap(b, l, 3))))) break;
 
         BExchangeArgs ca = xa;
         ca.ln_next = l + 1 < d.layers ? m->L[l + 1].ln_attn : m->norm;
@@ -283,8 +291,8 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
     ha.y = b->logits;
     ha.ldy = d.vocab;
     ha.div = d.logits_scaling;
-    ha.tc = b->use_tc;
-    if ((e = mark(b, s, BK_LM_HEAD, launch_bgemm(ha, BEPI_STORE, 1, s)))) return e;
+    ha.tc = b->gemm_mode;
+    if ((e = mark(b, s, BK_LM_HEAD, launch_bgemm(ha, BEPI_STORE, 1, s, wmap(b, b->m->d.layers, 0))))) return e;
     BHeadArgs hd{};
     hd.logits = b->logits;
     hd.V = d.vocab;
@@ -461,6 +469,22 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
         A.release();
         delete b;
         return set_err(ctx, LASTRO_E_CUDA, "batch init: %s", cudaGetErrorString(e));
+    }
+    // tensor maps of the weight matrices for the warp-specialised GEMM; without them the GEMMs run mode 1
+    b->wmaps.resize((size_t)d.layers * 4 + 1);
+    bool maps_ok = true;
+    for (int l = 0; l < d.layers && maps_ok; ++l) {
+        const LayerDev& L = m->L[l];
+        maps_ok = make_weight_map(&b->wmaps[l * 4 + 0], L.wqkv, b->R, H) == cudaSuccess &&
+                  make_weight_map(&b->wmaps[l * 4 + 1], L.wo, H, m->qd) == cudaSuccess &&
+                  make_weight_map(&b->wmaps[l * 4 + 2], L.gate_up, E * 2 * I, H) == cudaSuccess &&
+                  make_weight_map(&b->wmaps[l * 4 + 3], L.down, E * H, I) == cudaSuccess;
+    }
+    maps_ok = maps_ok && make_weight_map(&b->wmaps[(size_t)d.layers * 4], m->embed, V, H) == cudaSuccess;
+    if (!maps_ok) {
+        cudaGetLastError();
+        b->wmaps.clear();
+        b->gemm_mode = 1;
     }
     ctx_retain(ctx);
     *out = b;
@@ -673,12 +697,15 @@ extern "C" int lastro_batch_profile(lastro_batch* b, int32_t n, const int32_t* s
 
 extern "C" int lastro_batch_set_options(lastro_batch* b, int32_t use_graphs, int32_t use_tcgen05) {
     if (!b) return LASTRO_E_ARG;
+    if (use_tcgen05 < 0 || use_tcgen05 > 2) return set_err(b->ctx, LASTRO_E_ARG, "GEMM mode %d", use_tcgen05);
+    if (use_tcgen05 == 2 && b->wmaps.empty())
+        return set_err(b->ctx, LASTRO_E_UNSUPPORTED, "no weight tensor maps (TMA unavailable)");
     b->use_graphs = use_graphs != 0;
-    if ((use_tcgen05 != 0) != b->use_tc) {  // the captured graphs hold the other GEMM kernels
+    if (use_tcgen05 != b->gemm_mode) {  // the captured graphs hold the other GEMM kernels
         for (auto& g : b->graphs) cudaGraphExecDestroy(g.second);
         b->graphs.clear();
     }
-    b->use_tc = use_tcgen05 != 0;
+    b->gemm_mode = use_tcgen05;
     return LASTRO_OK;
 }
 

@@ -375,8 +375,9 @@ class GpuBatch:
         self.ctx.check(lib().lastro_batch_position(self.h, seq, C.byref(v)))
         return v.value
 
-    def set_options(self, graphs: bool = True, tcgen05: bool = True):
-        self.ctx.check(lib().lastro_batch_set_options(self.h, int(graphs), int(tcgen05)))
+    def set_options(self, graphs: bool = True, gemm: int = 2):
+        """gemm: 2 tcgen05 warp-specialised (TMA weight tiles), 1 tcgen05 with all threads loading, 0 mma.sync."""
+        self.ctx.check(lib().lastro_batch_set_options(self.h, int(graphs), int(gemm)))
 
     KERNELS = ("norm", "qkv", "rope_kv", "attention", "oproj", "router", "group", "gate_up", "down", "combine",
                "lm_head", "argmax")

@@ -21,24 +21,24 @@ pytestmark = pytest.mark.gpu
 GATE = 1e-4
 
 
-def batch_for(ctx, cfg, w, max_seqs, max_len, kv="f32", tc=True):
+def batch_for(ctx, cfg, w, max_seqs, max_len, kv="f32", gemm=2):
     m = LB.GpuModel(ctx, cfg, 8, kv_dtype=kv)
     m.load_weights(w)
     b = LB.GpuBatch(m, max_seqs, max_len)
     b.connect()
-    b.set_options(tcgen05=tc)
+    b.set_options(gemm=gemm)
     return m, b
 
 
-@pytest.mark.parametrize("tc", [True, False], ids=["tcgen05", "mma.sync"])
+@pytest.mark.parametrize("gemm", [2, 1, 0], ids=["tcgen05-ws", "tcgen05", "mma.sync"])
 @pytest.mark.parametrize("kv", ["f32", "bf16"])
 @pytest.mark.parametrize("biased", [False, True], ids=["plain", "zipf-bias"])
 @pytest.mark.parametrize("base", ["tiny", "tiny768"])
-def test_batch_matches_oracle_per_sequence(gpu_ctx, pool, kv, tc, biased, base):
+def test_batch_matches_oracle_per_sequence(gpu_ctx, pool, kv, gemm, biased, base):
     cfg = CFG.TINY if base == "tiny" else CFG.TINY_768
     w = reference_tiny_weights(cfg)
     nseq, max_len = 5, 96
-    m, b = batch_for(gpu_ctx, cfg, w, nseq, max_len, kv, tc)
+    m, b = batch_for(gpu_ctx, cfg, w, nseq, max_len, kv, gemm)
     om = O.Model(cfg, weights=w)
     bias = CFG.zipf_router_bias(cfg, std=0.5) if biased else None
     if biased:
