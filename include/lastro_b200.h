@@ -176,8 +176,9 @@ int lastro_batch_profile(lastro_batch *batch, int32_t n, const int32_t *seq_ids,
                          float *kernel_ms, int32_t n_kinds);
 /* use_graphs: replay each step as a CUDA graph (default 1); use_tcgen05: the GEMMs on the 5th-generation tensor cores
  * with tensor-memory accumulators, warp-specialised with TMA weight tiles (2, default), the same with all threads
- * loading the stages (1), or on mma.sync with register accumulators (0) */
-int lastro_batch_set_options(lastro_batch *batch, int32_t use_graphs, int32_t use_tcgen05);
+ * loading the stages (1), or on mma.sync with register accumulators (0); attn_tc: attention on tensor cores with TMA
+ * page loads (1, the default with bf16 KV) or on CUDA cores (0, the only choice with f32 KV) */
+int lastro_batch_set_options(lastro_batch *batch, int32_t use_graphs, int32_t use_tcgen05, int32_t attn_tc);
 void lastro_batch_destroy(lastro_batch *batch);
 
 #ifdef __cplusplus

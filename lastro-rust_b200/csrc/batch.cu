@@ -1358,6 +1358,197 @@ cudaError_t make_weight_map(CUtensorMap* map, const void* base, uint64_t rows, u
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// ------------------------------------------------------------------------------------------------------------------
+// Batched attention on tensor cores (bf16 KV), streaming.  CTA per (KV head, token), 4 warps, walking the token's
+// context one 64-position page at a time through a 3-stage TMA pipeline (K and V page per stage, 128-byte swizzle):
+// warp w owns rows 16w..16w+15 of every page.  Per page: S = Q K^T with the G query heads as the M = 16 rows (padded
+// with zeros) and q split into bf16 hi + lo (mma.sync m16n8k16, f32 accumulators), online softmax per head across
+// the quad of lanes that holds it, O += P V with P (split hi + lo) taken straight from the S accumulators as the A
+// operand and V through ldmatrix.trans.  Positions past the context carry finite values (the pools are zeroed at
+// creation and only ever hold model outputs) and get P = 0.  The 4 warps merge in shared memory at the end: no
+// partials, no cross-CTA merge.
+// ------------------------------------------------------------------------------------------------------------------
+namespace {
+LDEV void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+LDEV uint32_t pack_bf16(uint16_t lo, uint16_t hi) { return (uint32_t)lo | ((uint32_t)hi << 16); }
+LDEV void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+constexpr int kAttnStages = 3;
+constexpr int kPageBytes = 64 * 128;  // one KV head's 64 positions, bf16
+}  // namespace
+
+template <int G>
+__global__ void __launch_bounds__(128) battn_tc_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                       const __grid_constant__ CUtensorMap vmap, BAttnArgs a) {
+    constexpr int D = kHeadDim, NW = 4, P = kAttnStages;
+    static_assert(G <= 8, "heads of a group padded to the MMA's 16 rows");
+    extern __shared__ unsigned char smem_dyn[];
+    unsigned char* st0 = smem_dyn + ((1024 - (smem_addr(smem_dyn) & 1023)) & 1023);  // [P][K page, V page]
+    __shared__ __align__(8) uint64_t full[P], empty[P];
+    __shared__ float wm[NW][G], wl[NW][G];
+    __shared__ __align__(16) float wacc[NW][G][D];
+    const int kvh = blockIdx.x, z = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gq = lane >> 2, tq = lane & 3;
+    const int HD = a.kv_heads * G * D;
+    pdl_wait();
+    pdl_launch();
+    const int sqid = __ldg(a.seq + z);
+    const int* page_table = a.page_table + (size_t)sqid * a.pt_stride;
+    const int len = __ldcg(a.pos + sqid) + 1;
+    const int npages = (len + 63) / 64;
+    auto issue = [&](int pg) {  // thread 0: page pg into its stage
+        const int st = pg % P;
+        const int y = (__ldcg(page_table + pg) * a.kv_heads + kvh) * 64;
+        mbar_expect_tx(&full[st], 2 * kPageBytes);
+        tma_load_2d(st0 + (size_t)st * 2 * kPageBytes, &kmap, 0, y, &full[st]);
+        tma_load_2d(st0 + (size_t)st * 2 * kPageBytes + kPageBytes, &vmap, 0, y, &full[st]);
+    };
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < P; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], NW);
+        }
+        for (int pg = 0; pg < min(P, npages); ++pg) issue(pg);
+    }
+    // q fragments: a0 = (head gq, dims 16kk + 2tq, +1), a2 = (head gq, dims 16kk + 8 + 2tq, +1); heads >= G are zero
+    uint32_t qh[4][2], ql[4][2];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            float2 v = make_float2(0.f, 0.f);
+            if (gq < G) v = __ldcg(reinterpret_cast<const float2*>(a.q + (size_t)z * HD + ((size_t)kvh * G + gq) * D +
+                                                                   16 * kk + 8 * hf + 2 * tq));
+            uint16_t h0, l0, h1, l1;
+            split_bf16(v.x, h0, l0);
+            split_bf16(v.y, h1, l1);
+            qh[kk][hf] = pack_bf16(h0, h1);
+            ql[kk][hf] = pack_bf16(l0, l1);
+        }
+    __syncthreads();  // barriers initialised
+
+    float m_run = -INFINITY, l_run = 0.0f;
+    float o[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) o[j][c] = 0.0f;
+    const int mi = lane >> 3, r8 = lane & 7;
+    bool ok = true;
+    for (int pg = 0; pg < npages && ok; ++pg) {
+        const int st = pg % P;
+        ok = mbar_wait(&full[st], (pg / P) & 1, a.err, 4);
+        if (!ok) break;
+        const uint32_t sK = smem_addr(st0 + (size_t)st * 2 * kPageBytes), sV = sK + kPageBytes;
+        const int r0 = warp * 16;              // rows of this warp in the page
+        const int nrow = min(64, len - pg * 64);  // valid rows of the page
+        if (r0 < nrow) {
+            float sf[2][4];
+#pragma unroll
+            for (int q = 0; q < 2; ++q)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) sf[q][c] = 0.0f;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                uint32_t b[4];
+                ldsm_x4(sK + swz(r0 + (mi >> 1) * 8 + r8, kk * 2 + (mi & 1)), b);
+                const uint32_t ah[4] = {qh[kk][0], 0u, qh[kk][1], 0u}, al[4] = {ql[kk][0], 0u, ql[kk][1], 0u};
+                mma_bf16(sf[0], ah, b[0], b[1]);
+                mma_bf16(sf[1], ah, b[2], b[3]);
+                mma_bf16(sf[0], al, b[0], b[1]);
+                mma_bf16(sf[1], al, b[2], b[3]);
+            }
+            const int rr[4] = {r0 + 2 * tq, r0 + 2 * tq + 1, r0 + 8 + 2 * tq, r0 + 9 + 2 * tq};
+            const float raw[4] = {sf[0][0], sf[0][1], sf[1][0], sf[1][1]};
+            float sc[4], cmax = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                sc[i] = rr[i] < nrow ? __fmul_rn(raw[i], a.scale) : -INFINITY;
+                cmax = fmaxf(cmax, sc[i]);
+            }
+            cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 1));
+            cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 2));
+            const float mn = fmaxf(m_run, cmax);
+            const float alpha = m_run == -INFINITY ? 0.0f : expf(m_run - mn);
+            float pv[4], ps = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                pv[i] = rr[i] < nrow ? expf(sc[i] - mn) : 0.0f;
+                ps += pv[i];
+            }
+            ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+            l_run = l_run * alpha + ps;
+            m_run = mn;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                o[j][0] *= alpha;
+                o[j][1] *= alpha;
+            }
+            uint16_t h[4], l[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) split_bf16(pv[i], h[i], l[i]);
+            const uint32_t ph[4] = {pack_bf16(h[0], h[1]), 0u, pack_bf16(h[2], h[3]), 0u};
+            const uint32_t pl[4] = {pack_bf16(l[0], l[1]), 0u, pack_bf16(l[2], l[3]), 0u};
+#pragma unroll
+            for (int jp = 0; jp < 4; ++jp) {
+                uint32_t b[4];
+                ldsm_x4_trans(sV + swz(r0 + (mi & 1) * 8 + r8, 2 * jp + (mi >> 1)), b);
+                mma_bf16(o[2 * jp], ph, b[0], b[1]);
+                mma_bf16(o[2 * jp + 1], ph, b[2], b[3]);
+                mma_bf16(o[2 * jp], pl, b[0], b[1]);
+                mma_bf16(o[2 * jp + 1], pl, b[2], b[3]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        // thread 0 refills the stage with page pg + P once all 4 warps have released it
+        if (threadIdx.x == 0 && pg + P < npages) {
+            ok = mbar_wait(&empty[st], (pg / P) & 1, a.err, 11);
+            if (ok) issue(pg + P);
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+    if (gq < G) {
+        if (tq == 0) {
+            wm[warp][gq] = m_run;
+            wl[warp][gq] = l_run;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            wacc[warp][gq][8 * j + 2 * tq] = o[j][0];
+            wacc[warp][gq][8 * j + 2 * tq + 1] = o[j][1];
+        }
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
+        const int g = t / D, dim = t - g * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
+        float L = 0.0f, A = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            if (wm[w][g] == -INFINITY) continue;
+            const float e = expf(wm[w][g] - M);
+            L = fmaf(wl[w][g], e, L);
+            A = fmaf(wacc[w][g][dim], e, A);
+        }
+        const float ov = A / L;
+        const size_t oi = (size_t)z * HD + ((size_t)kvh * G + g) * D + dim;
+        a.att_out[oi] = ov;
+        uint16_t hi, lo;
+        split_bf16(ov, hi, lo);
+        a.att_hi[oi] = hi;
+        a.att_lo[oi] = lo;
+    }
+}
+
 // ---- launchers: every batched kernel waits for its predecessor with griddepcontrol.wait first, so all launch with
 // programmatic dependent launch (the next kernel's launch overlaps the tail of the current one) -------------------
 template <typename Kern>
@@ -1378,6 +1569,32 @@ cudaError_t launch_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStre
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+cudaError_t make_kv_map(CUtensorMap* map, const void* pool, uint64_t rows) {
+    // K or V pool of one layer as [pages * kv_heads * 64 rows][64 dims] bf16: the same 64 x 64 box as the weights
+    return make_weight_map(map, pool, rows, kHeadDim);
+}
+
+cudaError_t launch_battention_tc(const BAttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap, cudaStream_t s) {
+    if (a.kv_f32 || a.n < 1 || !kmap || !vmap) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)kAttnStages * 2 * kPageBytes + 1024;
+    const dim3 grid(a.kv_heads, a.n), block(128);
+#define LASTRO_BATTN_TC(GV)                                                                    \
+    case GV: {                                                                                 \
+        cudaError_t e = set_smem(battn_tc_kernel<GV>, smem);                                   \
+        return e != cudaSuccess ? e : launch_pdl(battn_tc_kernel<GV>, grid, block, smem, s, *kmap, *vmap, a); \
+    }
+    switch (a.G) {
+        LASTRO_BATTN_TC(1)
+        LASTRO_BATTN_TC(2)
+        LASTRO_BATTN_TC(3)
+        LASTRO_BATTN_TC(4)
+        LASTRO_BATTN_TC(6)
+        LASTRO_BATTN_TC(8)
+    default: return cudaErrorInvalidValue;
+    }
+#undef LASTRO_BATTN_TC
 }
 
 cudaError_t launch_bgemm(const BGemmArgs& a, int epi, int groups, cudaStream_t s, const CUtensorMap* wmap) {

@@ -188,6 +188,10 @@ struct BAttnArgs {
 };
 
 cudaError_t launch_battention(const BAttnArgs& a, cudaStream_t s);
+// bf16 KV on tensor cores: CTA per (KV head, token) streaming the context's pages by TMA through `kmap` / `vmap`
+// (make_kv_map over the layer's pools); positions past the context must hold finite values (zeroed pools)
+cudaError_t launch_battention_tc(const BAttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap, cudaStream_t s);
+cudaError_t make_kv_map(CUtensorMap* map, const void* pool, uint64_t rows);
 size_t battn_smem(int cap, int kv_f32);
 
 // `wmap` (mode 2): 2-D bf16 tensor map over the weight rows [groups * rows][K], box 64 columns x 64 rows, 128-byte

@@ -30,6 +30,9 @@ struct lastro_batch {
     int gemm_mode = 2;  // 0 mma.sync, 1 tcgen05 (cp.async stages), 2 tcgen05 warp-specialised (TMA weight tiles)
     // TMA tensor maps of the weights (mode 2): per layer qkv, o, gate_up, down; then the embedding (lm_head)
     std::vector<CUtensorMap> wmaps;
+    // bf16 KV: attention on tensor cores with TMA page loads (per layer: K map, V map); else the CUDA-core kernel
+    std::vector<CUtensorMap> kvmaps;
+    bool attn_tc = false;
     Arena arena;
     std::vector<void*> kpool, vpool;  // per layer: [max_seqs * max_pages pages][kv_heads][page][d]
     float* rope_cs = nullptr;
@@ -194,7 +197,11 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         aa.S = b->attn_S;
         aa.cap = b->attn_cap;
         aa.scale = d.attention_multiplier;
-        if ((e = mark(b, s, BK_ATTN, launch_battention(aa, s)))) break;
+        if (b->attn_tc)
+            e = mark(b, s, BK_ATTN, launch_battention_tc(aa, &b->kvmaps[2 * l], &b->kvmaps[2 * l + 1], s));
+        else
+            e = mark(b, s, BK_ATTN, launch_battention(aa, s));
+        if (e) break;
 
         BGemmArgs oa{};
         oa.w = reinterpret_cast<const uint16_t*>(L.wo);
@@ -459,6 +466,10 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
     if (!e) e = cudaMemsetAsync(b->epoch, 0, sizeof(unsigned int), s);
     if (!e) e = cudaMemsetAsync(b->d_err, 0, sizeof(int), s);
     if (!e) e = cudaMemsetAsync(b->xreg, 0, b->lay.bytes, s);
+    for (int l = 0; l < d.layers && !e; ++l) {  // finite values past every context (the attention reads whole pages)
+        e = cudaMemsetAsync(b->kpool[l], 0, kv_bytes, s);
+        if (!e) e = cudaMemsetAsync(b->vpool[l], 0, kv_bytes, s);
+    }
     if (!e) e = cudaMemsetAsync(b->route_hist, 0, sizeof(int) * S * d.layers * k, s);
     if (!e) e = cudaStreamSynchronize(s);
     if (e) {
@@ -485,6 +496,19 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
         cudaGetLastError();
         b->wmaps.clear();
         b->gemm_mode = 1;
+    }
+    if (d.kv_dtype == LASTRO_DTYPE_BF16 && m->G <= 8) {
+        const uint64_t kv_rows = (uint64_t)S * b->max_pages * d.kv_heads * kPageSize;
+        b->kvmaps.resize((size_t)d.layers * 2);
+        bool kv_ok = true;
+        for (int l = 0; l < d.layers && kv_ok; ++l)
+            kv_ok = make_kv_map(&b->kvmaps[2 * l], b->kpool[l], kv_rows) == cudaSuccess &&
+                    make_kv_map(&b->kvmaps[2 * l + 1], b->vpool[l], kv_rows) == cudaSuccess;
+        if (!kv_ok) {
+            cudaGetLastError();
+            b->kvmaps.clear();
+        }
+        b->attn_tc = kv_ok;
     }
     ctx_retain(ctx);
     *out = b;
@@ -695,17 +719,20 @@ extern "C" int lastro_batch_profile(lastro_batch* b, int32_t n, const int32_t* s
     return LASTRO_OK;
 }
 
-extern "C" int lastro_batch_set_options(lastro_batch* b, int32_t use_graphs, int32_t use_tcgen05) {
+extern "C" int lastro_batch_set_options(lastro_batch* b, int32_t use_graphs, int32_t use_tcgen05, int32_t attn_tc) {
     if (!b) return LASTRO_E_ARG;
+    if (attn_tc && b->kvmaps.empty())
+        return set_err(b->ctx, LASTRO_E_UNSUPPORTED, "tensor-core attention needs bf16 KV and TMA page maps");
     if (use_tcgen05 < 0 || use_tcgen05 > 2) return set_err(b->ctx, LASTRO_E_ARG, "GEMM mode %d", use_tcgen05);
     if (use_tcgen05 == 2 && b->wmaps.empty())
         return set_err(b->ctx, LASTRO_E_UNSUPPORTED, "no weight tensor maps (TMA unavailable)");
     b->use_graphs = use_graphs != 0;
-    if (use_tcgen05 != b->gemm_mode) {  // the captured graphs hold the other GEMM kernels
+    if (use_tcgen05 != b->gemm_mode || (attn_tc != 0) != b->attn_tc) {  // the captured graphs hold the other kernels
         for (auto& g : b->graphs) cudaGraphExecDestroy(g.second);
         b->graphs.clear();
     }
     b->gemm_mode = use_tcgen05;
+    b->attn_tc = attn_tc != 0;
     return LASTRO_OK;
 }
 

@@ -84,7 +84,7 @@ EXPORTS = {
     "lastro_batch_fill_kv_synthetic": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_uint64, C.c_float]),
     "lastro_batch_reset": (C.c_int, [C.c_void_p, C.c_int32]),
     "lastro_batch_position": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_int32)]),
-    "lastro_batch_set_options": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32]),
+    "lastro_batch_set_options": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32]),
     "lastro_batch_profile": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p,
                                        C.c_int32]),
     "lastro_batch_destroy": (None, [C.c_void_p]),
@@ -208,7 +208,7 @@ class GpuModel:
     """Whole model resident on one GPU (gpu_model.rs GpuModel), batch-1 decode."""
 
     def __init__(self, ctx: Context, cfg: dict, max_len: int, kv_dtype: str = "bf16"):
-        self.ctx, self.cfg, self.max_len = ctx, dict(cfg), max_len
+        self.ctx, self.cfg, self.max_len, self.kv_dtype = ctx, dict(cfg), max_len, kv_dtype
         wd = DTYPE_Q8_0 if cfg.get("weight_dtype", "bf16") == "q8_0" else DTYPE_BF16
         d = ModelDesc(**{f: cfg[f] for f, _ in ModelDesc._fields_[:15]}, weight_dtype=wd,
                       kv_dtype=DTYPE_F32 if kv_dtype == "f32" else DTYPE_BF16)
@@ -318,6 +318,7 @@ class GpuBatch:
     def __init__(self, model: GpuModel, max_seqs: int, max_len: int, rank: int = 0, world: int = 1):
         self.model, self.ctx, self.cfg = model, model.ctx, model.cfg
         self.max_seqs, self.max_len, self.rank, self.world = max_seqs, max_len, rank, world
+        self.kv_dtype = model.kv_dtype
         h = C.c_void_p()
         self.ctx.check(lib().lastro_batch_create(model.h, max_seqs, max_len, rank, world, C.byref(h)))
         self.h = h
@@ -375,9 +376,12 @@ class GpuBatch:
         self.ctx.check(lib().lastro_batch_position(self.h, seq, C.byref(v)))
         return v.value
 
-    def set_options(self, graphs: bool = True, gemm: int = 2):
-        """gemm: 2 tcgen05 warp-specialised (TMA weight tiles), 1 tcgen05 with all threads loading, 0 mma.sync."""
-        self.ctx.check(lib().lastro_batch_set_options(self.h, int(graphs), int(gemm)))
+    def set_options(self, graphs: bool = True, gemm: int = 2, attn_tc: bool | None = None):
+        """gemm: 2 tcgen05 warp-specialised (TMA weight tiles), 1 tcgen05 with all threads loading, 0 mma.sync;
+        attn_tc: attention on tensor cores (default where available: bf16 KV) or CUDA cores."""
+        if attn_tc is None:
+            attn_tc = self.kv_dtype == "bf16"
+        self.ctx.check(lib().lastro_batch_set_options(self.h, int(graphs), int(gemm), int(attn_tc)))
 
     KERNELS = ("norm", "qkv", "rope_kv", "attention", "oproj", "router", "group", "gate_up", "down", "combine",
                "lm_head", "argmax")

@@ -21,31 +21,34 @@ pytestmark = pytest.mark.gpu
 GATE = 1e-4
 
 
-def batch_for(ctx, cfg, w, max_seqs, max_len, kv="f32", gemm=2):
+def batch_for(ctx, cfg, w, max_seqs, max_len, kv="f32", gemm=2, attn_tc=None):
     m = LB.GpuModel(ctx, cfg, 8, kv_dtype=kv)
     m.load_weights(w)
     b = LB.GpuBatch(m, max_seqs, max_len)
     b.connect()
-    b.set_options(gemm=gemm)
+    b.set_options(gemm=gemm, attn_tc=attn_tc)
     return m, b
 
 
 @pytest.mark.parametrize("gemm", [2, 1, 0], ids=["tcgen05-ws", "tcgen05", "mma.sync"])
-@pytest.mark.parametrize("kv", ["f32", "bf16"])
+@pytest.mark.parametrize("kv", ["f32", "bf16", "bf16-cuda-core-attention"])
 @pytest.mark.parametrize("biased", [False, True], ids=["plain", "zipf-bias"])
 @pytest.mark.parametrize("base", ["tiny", "tiny768"])
 def test_batch_matches_oracle_per_sequence(gpu_ctx, pool, kv, gemm, biased, base):
     cfg = CFG.TINY if base == "tiny" else CFG.TINY_768
     w = reference_tiny_weights(cfg)
-    nseq, max_len = 5, 96
-    m, b = batch_for(gpu_ctx, cfg, w, nseq, max_len, kv, gemm)
+    nseq, max_len = 5, 200  # 200 positions: two 128-position attention splits, the second partial
+    attn_tc = None
+    if kv == "bf16-cuda-core-attention":
+        kv, attn_tc = "bf16", False
+    m, b = batch_for(gpu_ctx, cfg, w, nseq, max_len, kv, gemm, attn_tc)
     om = O.Model(cfg, weights=w)
     bias = CFG.zipf_router_bias(cfg, std=0.5) if biased else None
     if biased:
         b.set_router_bias(bias)
         om.set_router_bias(bias)
     sessions = [O.Session(om, pool, max_len, kv_bf16=kv == "bf16") for _ in range(nseq)]
-    lengths = [70, 9, 33, 1, 52]  # sequence q decodes lengths[q] tokens
+    lengths = [150, 9, 33, 1, 130]  # sequence q decodes lengths[q] tokens (past one 128-position split for 2 of them)
     prompts = [S.tokens(n, 100 + q, cfg["vocab"]) for q, n in enumerate(lengths)]
     rng = np.random.default_rng(5)
     for t in range(max(lengths)):
