@@ -1365,8 +1365,9 @@ cudaError_t make_weight_map(CUtensorMap* map, const void* base, uint64_t rows, u
 // with zeros) and q split into bf16 hi + lo (mma.sync m16n8k16, f32 accumulators), online softmax per head across
 // the quad of lanes that holds it, O += P V with P (split hi + lo) taken straight from the S accumulators as the A
 // operand and V through ldmatrix.trans.  Positions past the context carry finite values (the pools are zeroed at
-// creation and only ever hold model outputs) and get P = 0.  The 4 warps merge in shared memory at the end: no
-// partials, no cross-CTA merge.
+// creation and only ever hold model outputs) and get P = 0.  The 4 warps merge in shared memory at the end.  With
+// few tokens (expert parallelism leaves a rank 64/N of them) the context is split over gridDim.x CTAs of consecutive
+// pages, each writing a partial (m, l, acc); the last CTA of (token, KV head) merges them in split order.
 // ------------------------------------------------------------------------------------------------------------------
 namespace {
 LDEV void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
@@ -1392,7 +1393,8 @@ __global__ void __launch_bounds__(128) battn_tc_kernel(const __grid_constant__ C
     __shared__ __align__(8) uint64_t full[P], empty[P];
     __shared__ float wm[NW][G], wl[NW][G];
     __shared__ __align__(16) float wacc[NW][G][D];
-    const int kvh = blockIdx.x, z = blockIdx.y;
+    __shared__ bool is_last;
+    const int S = gridDim.x, sp = blockIdx.x, kvh = blockIdx.y, z = blockIdx.z;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gq = lane >> 2, tq = lane & 3;
     const int HD = a.kv_heads * G * D;
     pdl_wait();
@@ -1400,9 +1402,12 @@ __global__ void __launch_bounds__(128) battn_tc_kernel(const __grid_constant__ C
     const int sqid = __ldg(a.seq + z);
     const int* page_table = a.page_table + (size_t)sqid * a.pt_stride;
     const int len = __ldcg(a.pos + sqid) + 1;
-    const int npages = (len + 63) / 64;
-    auto issue = [&](int pg) {  // thread 0: page pg into its stage
-        const int st = pg % P;
+    const int ntot = (len + 63) / 64;
+    const int per = (ntot + S - 1) / S;
+    const int pbeg = min(ntot, sp * per), npages = min(ntot, pbeg + per) - pbeg;  // this split's pages
+    auto issue = [&](int i) {  // thread 0: the split's i-th page into stage i % P
+        const int pg = pbeg + i;
+        const int st = i % P;
         const int y = (__ldcg(page_table + pg) * a.kv_heads + kvh) * 64;
         mbar_expect_tx(&full[st], 2 * kPageBytes);
         tma_load_2d(st0 + (size_t)st * 2 * kPageBytes, &kmap, 0, y, &full[st]);
@@ -1445,8 +1450,8 @@ __global__ void __launch_bounds__(128) battn_tc_kernel(const __grid_constant__ C
         ok = mbar_wait(&full[st], (pg / P) & 1, a.err, 4);
         if (!ok) break;
         const uint32_t sK = smem_addr(st0 + (size_t)st * 2 * kPageBytes), sV = sK + kPageBytes;
-        const int r0 = warp * 16;              // rows of this warp in the page
-        const int nrow = min(64, len - pg * 64);  // valid rows of the page
+        const int r0 = warp * 16;                        // rows of this warp in the page
+        const int nrow = min(64, len - (pbeg + pg) * 64);  // valid rows of the page
         if (r0 < nrow) {
             float sf[2][4];
 #pragma unroll
@@ -1526,6 +1531,8 @@ __global__ void __launch_bounds__(128) battn_tc_kernel(const __grid_constant__ C
         }
     }
     __syncthreads();
+    float* part_acc = a.part_acc + (size_t)z * HD * S;
+    float* part_ml = a.part_ml + (size_t)z * a.kv_heads * G * S * 2;
     for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
         const int g = t / D, dim = t - g * D;
         float M = -INFINITY;
@@ -1539,7 +1546,39 @@ __global__ void __launch_bounds__(128) battn_tc_kernel(const __grid_constant__ C
             L = fmaf(wl[w][g], e, L);
             A = fmaf(wacc[w][g][dim], e, A);
         }
-        const float ov = A / L;
+        if (S == 1) {
+            const float ov = A / L;
+            const size_t oi = (size_t)z * HD + ((size_t)kvh * G + g) * D + dim;
+            a.att_out[oi] = ov;
+            uint16_t hi, lo;
+            split_bf16(ov, hi, lo);
+            a.att_hi[oi] = hi;
+            a.att_lo[oi] = lo;
+        } else {
+            const size_t hs = (size_t)(kvh * G + g) * S + sp;
+            part_acc[hs * D + dim] = A;
+            if (dim == 0) {
+                part_ml[hs * 2] = M;
+                part_ml[hs * 2 + 1] = L;
+            }
+        }
+    }
+    if (S == 1) return;
+    if (!last_block_arrives(a.counters + (size_t)z * a.kv_heads + kvh, (unsigned int)S, &is_last)) return;
+    for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
+        const int g = t / D, dim = t - g * D;
+        const size_t h0 = (size_t)(kvh * G + g) * S;
+        float M = -INFINITY;
+        for (int q = 0; q < S; ++q) M = fmaxf(M, __ldcg(part_ml + (h0 + q) * 2));
+        float den = 0.0f, num = 0.0f;
+        for (int q = 0; q < S; ++q) {
+            const float ms = __ldcg(part_ml + (h0 + q) * 2);
+            if (ms == -INFINITY) continue;
+            const float e = expf(ms - M);
+            den = fmaf(__ldcg(part_ml + (h0 + q) * 2 + 1), e, den);
+            num = fmaf(__ldcg(part_acc + (h0 + q) * D + dim), e, num);
+        }
+        const float ov = num / den;
         const size_t oi = (size_t)z * HD + ((size_t)kvh * G + g) * D + dim;
         a.att_out[oi] = ov;
         uint16_t hi, lo;
@@ -1577,9 +1616,9 @@ cudaError_t make_kv_map(CUtensorMap* map, const void* pool, uint64_t rows) {
 }
 
 cudaError_t launch_battention_tc(const BAttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap, cudaStream_t s) {
-    if (a.kv_f32 || a.n < 1 || !kmap || !vmap) return cudaErrorInvalidValue;
+    if (a.kv_f32 || a.n < 1 || !kmap || !vmap || a.S < 1 || a.S > kBAttnMaxSplits) return cudaErrorInvalidValue;
     const size_t smem = (size_t)kAttnStages * 2 * kPageBytes + 1024;
-    const dim3 grid(a.kv_heads, a.n), block(128);
+    const dim3 grid(a.S, a.kv_heads, a.n), block(128);
 #define LASTRO_BATTN_TC(GV)                                                                    \
     case GV: {                                                                                 \
         cudaError_t e = set_smem(battn_tc_kernel<GV>, smem);                                   \

@@ -26,6 +26,7 @@ struct lastro_batch {
     int max_seqs = 0, max_len = 0, max_pages = 0, rank = 0, world = 1, epr = 0, e0 = 0;
     int ks_qkv = 1, ks_o = 1, R = 0;
     int attn_S = 1, attn_cap = 1;  // attention splits per (token, KV head) and positions one split stages
+    int n_sm = 148;
     bool poisoned = false, connected = false, use_graphs = true;
     int gemm_mode = 2;  // 0 mma.sync, 1 tcgen05 (cp.async stages), 2 tcgen05 warp-specialised (TMA weight tiles)
     // TMA tensor maps of the weights (mode 2): per layer qkv, o, gate_up, down; then the embedding (lm_head)
@@ -197,8 +198,13 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         aa.S = b->attn_S;
         aa.cap = b->attn_cap;
         aa.scale = d.attention_multiplier;
-        if (b->attn_tc)
+        if (b->attn_tc) {
+            // context splits for few tokens: at most about 4 CTAs per SM in all (one split while the tokens alone
+            // fill that), at most 16 splits, at least 2 pages each
+            const int want = (4 * b->n_sm) / (n * d.kv_heads);
+            aa.S = std::max(1, std::min({want, 16, b->max_pages / 2}));
             e = mark(b, s, BK_ATTN, launch_battention_tc(aa, &b->kvmaps[2 * l], &b->kvmaps[2 * l + 1], s));
+        }
         else
             e = mark(b, s, BK_ATTN, launch_battention(aa, s));
         if (e) break;
@@ -412,6 +418,7 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
     b->e0 = rank * b->epr;
     b->R = m->qd + 2 * m->kvd;
     b->attn_S = attn_S;
+    b->n_sm = n_sm;
     b->attn_cap = (max_len + attn_S - 1) / attn_S + 1;
     b->ks_qkv = pick_ks(b->R, d.hidden, n_sm);
     b->ks_o = pick_ks(d.hidden, m->qd, n_sm);
@@ -432,8 +439,8 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
           A.alloc(&b->d_hist, (size_t)max_len * S) || A.alloc(&b->h, S * H) || A.alloc(&b->xa_hi, S * H) ||
           A.alloc(&b->xa_lo, S * H) || A.alloc(&b->qkv_part, (size_t)b->ks_qkv * S * b->R) ||
           A.alloc(&b->q, S * m->qd) || A.alloc(&b->att, S * m->qd) || A.alloc(&b->att_hi, S * m->qd) ||
-          A.alloc(&b->att_lo, S * m->qd) || A.alloc(&b->part_acc, S * d.heads * attn_S * d.head_dim) ||
-          A.alloc(&b->part_ml, S * d.heads * attn_S * 2) || A.alloc(&b->attn_counters, S * d.kv_heads) ||
+          A.alloc(&b->att_lo, S * m->qd) || A.alloc(&b->part_acc, S * d.heads * std::max(attn_S, 16) * d.head_dim) ||
+          A.alloc(&b->part_ml, S * d.heads * std::max(attn_S, 16) * 2) || A.alloc(&b->attn_counters, S * d.kv_heads) ||
           A.alloc(&b->o_part, (size_t)b->ks_o * S * H) || A.alloc(&b->ids, S * k) || A.alloc(&b->rw, S * k) ||
           A.alloc(&b->bias, (size_t)d.layers * E) ||
           A.alloc(&b->x_rows, pairs) || A.alloc(&b->src, pairs) || A.alloc(&b->g_off, kMaxExperts) ||
