@@ -1142,9 +1142,15 @@ LDEV void cp_async_arrive_noinc(uint64_t* bar) {
 
 }  // namespace
 
-template <int EPI>
+template <int EPI, int TOK>
 __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ CUtensorMap wmap, BGemmArgs a) {
-    constexpr int S = kBStages;
+    // TOK tokens per tile: 64 with 3 stages of 32 KB (2 CTAs per SM), or 32 with 2 stages of 24 KB (4 CTAs per SM).
+    // Measured on the C5 step (1 B200): 64/3 for every GEMM 5.05 ms, 32/4 for the expert groups 5.15 ms, 32/2 5.21 ms;
+    // the launches use 64.
+    static_assert(TOK == 32 || TOK == 64, "token tile");
+    constexpr int S = TOK == 64 ? 3 : 2;
+    constexpr size_t STAGE = (size_t)kBRows * 128 + 2 * (size_t)TOK * 128;
+    static_assert(S * STAGE <= kBGemmSmem, "stages fit the launch's shared memory");
     extern __shared__ unsigned char smem_dyn[];
     unsigned char* smem = smem_dyn + ((1024 - (smem_addr(smem_dyn) & 1023)) & 1023);
     __shared__ __align__(8) uint64_t full[S], empty[S], done;
@@ -1189,8 +1195,8 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
     bool ok = true;
     int it = 0;  // global stage counter over the CTA's tiles (stage it % S, round it / S)
     int tile = 0;
-    for (int t0 = 0; t0 < ntot; t0 += kBTok, ++tile) {
-        const int n = min(kBTok, ntot - t0);
+    for (int t0 = 0; t0 < ntot; t0 += TOK, ++tile) {
+        const int n = min(TOK, ntot - t0);
         const int N = (n + 15) & ~15;
         // (the whole of warps 0 and 1 runs their loops, lane 0 doing the work, so that the idle lanes wait at
         // __syncwarp instead of spinning on a barrier in the lanes' own divergent path)
@@ -1202,7 +1208,7 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
                     if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, a.x.err, 7)) {
                         go = false;
                     } else {
-                        unsigned char* st = smem + (size_t)s * kBStageBytes;
+                        unsigned char* st = smem + (size_t)s * STAGE;
                         mbar_expect_tx(&full[s], kBRows * 128);
                         const int x = kbeg + kt * kBK;
                         tma_load_2d(st, &wmap, x, wrow0, &full[s]);
@@ -1222,8 +1228,8 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
                     } else {
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the cp.async rows, for the MMA
                         tc_fence_after();
-                        const uint32_t sW = smem_addr(smem + (size_t)s * kBStageBytes);
-                        const uint32_t sXh = sW + kBRows * 128, sXl = sXh + kBTok * 128;
+                        const uint32_t sW = smem_addr(smem + (size_t)s * STAGE);
+                        const uint32_t sXh = sW + kBRows * 128, sXl = sXh + TOK * 128;
 #pragma unroll
                         for (int kk = 0; kk < kBK / 16; ++kk) {
                             const uint64_t ad = smem_desc_sw128(sW + kk * 32);
@@ -1242,9 +1248,9 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
             // warps 2-3: the token rows of every stage, 16 cp.async per thread, then an arrival when they land
             const int pt = tid - 64;  // 0..63
             const int ch = pt & 7;
-            int xrow[8];
+            int xrow[TOK / 8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int i = 0; i < TOK / 8; ++i) {
                 const int tok = (pt >> 3) + 8 * i;
                 const int p = p0 + t0 + tok;
                 xrow[i] = tok < n ? (a.x_rows ? __ldcg(a.x_rows + p) : p) : 0;
@@ -1252,16 +1258,16 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
             for (int kt = 0; kt < nk; ++kt) {
                 const int s = (it + kt) % S, r = (it + kt) / S;
                 if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, a.x.err, 9)) break;
-                unsigned char* st = smem + (size_t)s * kBStageBytes;
+                unsigned char* st = smem + (size_t)s * STAGE;
                 const int k0 = kbeg + kt * kBK + ch * 8;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
+                for (int i = 0; i < TOK / 8; ++i) {
                     const int tok = (pt >> 3) + 8 * i;
                     const bool v = tok < n;
                     const size_t xo = (size_t)xrow[i] * a.ldx + k0;
                     const uint32_t d = swz(tok, ch);
                     cp_async16(smem_addr(st + kBRows * 128) + d, a.x_hi + xo, v);
-                    cp_async16(smem_addr(st + kBRows * 128 + kBTok * 128) + d, a.x_lo + xo, v);
+                    cp_async16(smem_addr(st + kBRows * 128 + TOK * 128) + d, a.x_lo + xo, v);
                 }
                 cp_async_arrive_noinc(&full[s]);
             }
@@ -1642,21 +1648,21 @@ cudaError_t launch_bgemm(const BGemmArgs& a, int epi, int groups, cudaStream_t s
     cudaError_t e;
     if (a.tc == 2) {
         if (!wmap) return cudaErrorInvalidValue;
-        const size_t smem = kBGemmSmem + 1024;
+        const size_t smem = kBGemmSmem + 1024;                                       // token tiles of 64, 3 stages
         const dim3 block(128);
         if (epi == BEPI_SWIGLU) {
             if (a.I % 64 || a.rows != 2 * a.I || ks != 1) return cudaErrorInvalidValue;
-            if ((e = set_smem(bgemm_ws_kernel<BEPI_SWIGLU>, smem)) != cudaSuccess) return e;
-            return launch_pdl(bgemm_ws_kernel<BEPI_SWIGLU>, dim3(a.I / 64, groups, 1), block, smem, s, *wmap, a);
+            if ((e = set_smem(bgemm_ws_kernel<BEPI_SWIGLU, 64>, smem)) != cudaSuccess) return e;
+            return launch_pdl(bgemm_ws_kernel<BEPI_SWIGLU, 64>, dim3(a.I / 64, groups, 1), block, smem, s, *wmap, a);
         }
         if (epi == BEPI_RETURN) {
             if (a.rows % kBRows || ks != 1 || a.x.world > 32) return cudaErrorInvalidValue;
-            if ((e = set_smem(bgemm_ws_kernel<BEPI_RETURN>, smem)) != cudaSuccess) return e;
-            return launch_pdl(bgemm_ws_kernel<BEPI_RETURN>, dim3(a.rows / kBRows, groups, 1), block, smem, s, *wmap, a);
+            if ((e = set_smem(bgemm_ws_kernel<BEPI_RETURN, 64>, smem)) != cudaSuccess) return e;
+            return launch_pdl(bgemm_ws_kernel<BEPI_RETURN, 64>, dim3(a.rows / kBRows, groups, 1), block, smem, s, *wmap, a);
         }
-        if ((e = set_smem(bgemm_ws_kernel<BEPI_STORE>, smem)) != cudaSuccess) return e;
-        return launch_pdl(bgemm_ws_kernel<BEPI_STORE>, dim3((a.rows + kBRows - 1) / kBRows, groups, ks), block, smem, s,
-                          *wmap, a);
+        if ((e = set_smem(bgemm_ws_kernel<BEPI_STORE, 64>, smem)) != cudaSuccess) return e;
+        return launch_pdl(bgemm_ws_kernel<BEPI_STORE, 64>, dim3((a.rows + kBRows - 1) / kBRows, groups, ks), block, smem,
+                          s, *wmap, a);
     }
     if (a.tc) {
         const size_t smem = kBGemmSmem + 1024;
