@@ -136,6 +136,9 @@ int lastro_model_profile(lastro_model *model, int32_t steps, float *kernel_ms, i
 int lastro_model_set_options(lastro_model *model, int32_t use_graphs, int32_t use_pdl, int32_t use_fused);
 /* 1 when decode steps run as the fused step kernel (shapes fit and the option is on), else 0 */
 int lastro_model_fused(const lastro_model *model);
+/* attention kernel of the step chain with bf16 KV: tensor cores with TMA page loads (1) or the CUDA-core split kernel
+ * (0, the default: faster at batch 1 on B200; the only one with f32 KV) */
+int lastro_model_set_attention(lastro_model *model, int32_t tensor_cores);
 void lastro_model_destroy(lastro_model *model);
 
 /* ---- batched decode with expert parallelism (no counterpart in the reference, which decodes one sequence) ------- */

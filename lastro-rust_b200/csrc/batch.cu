@@ -1403,14 +1403,17 @@ __global__ void __launch_bounds__(128) battn_tc_kernel(const __grid_constant__ C
     const int S = gridDim.x, sp = blockIdx.x, kvh = blockIdx.y, z = blockIdx.z;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gq = lane >> 2, tq = lane & 3;
     const int HD = a.kv_heads * G * D;
-    pdl_wait();
-    pdl_launch();
-    const int sqid = __ldg(a.seq + z);
+    // The sequence, its page table and position were written two or more kernels back (the host's copy, the previous
+    // step's argmax): read before griddepcontrol.wait.  Pages wholly below the current position hold K/V of earlier
+    // steps: their TMA loads start before the wait too, overlapping the previous kernel's tail; the page of the
+    // current position (written by the previous kernel) is loaded after it.
+    const int sqid = a.seq ? __ldg(a.seq + z) : 0;
     const int* page_table = a.page_table + (size_t)sqid * a.pt_stride;
     const int len = __ldcg(a.pos + sqid) + 1;
     const int ntot = (len + 63) / 64;
     const int per = (ntot + S - 1) / S;
     const int pbeg = min(ntot, sp * per), npages = min(ntot, pbeg + per) - pbeg;  // this split's pages
+    const int fresh = (len - 1) / 64;  // page of the current position
     auto issue = [&](int i) {  // thread 0: the split's i-th page into stage i % P
         const int pg = pbeg + i;
         const int st = i % P;
@@ -1419,13 +1422,20 @@ __global__ void __launch_bounds__(128) battn_tc_kernel(const __grid_constant__ C
         tma_load_2d(st0 + (size_t)st * 2 * kPageBytes, &kmap, 0, y, &full[st]);
         tma_load_2d(st0 + (size_t)st * 2 * kPageBytes + kPageBytes, &vmap, 0, y, &full[st]);
     };
+    const int pre = min(P, npages);
     if (threadIdx.x == 0) {
         for (int i = 0; i < P; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], NW);
         }
-        for (int pg = 0; pg < min(P, npages); ++pg) issue(pg);
+        for (int i = 0; i < pre; ++i)
+            if (pbeg + i < fresh) issue(i);
     }
+    pdl_wait();
+    pdl_launch();
+    if (threadIdx.x == 0)
+        for (int i = 0; i < pre; ++i)
+            if (pbeg + i >= fresh) issue(i);
     // q fragments: a0 = (head gq, dims 16kk + 2tq, +1), a2 = (head gq, dims 16kk + 8 + 2tq, +1); heads >= G are zero
     uint32_t qh[4][2], ql[4][2];
 #pragma unroll
@@ -1556,10 +1566,12 @@ __global__ void __launch_bounds__(128) battn_tc_kernel(const __grid_constant__ C
             const float ov = A / L;
             const size_t oi = (size_t)z * HD + ((size_t)kvh * G + g) * D + dim;
             a.att_out[oi] = ov;
-            uint16_t hi, lo;
-            split_bf16(ov, hi, lo);
-            a.att_hi[oi] = hi;
-            a.att_lo[oi] = lo;
+            if (a.att_hi) {
+                uint16_t hi, lo;
+                split_bf16(ov, hi, lo);
+                a.att_hi[oi] = hi;
+                a.att_lo[oi] = lo;
+            }
         } else {
             const size_t hs = (size_t)(kvh * G + g) * S + sp;
             part_acc[hs * D + dim] = A;
@@ -1587,10 +1599,12 @@ __global__ void __launch_bounds__(128) battn_tc_kernel(const __grid_constant__ C
         const float ov = num / den;
         const size_t oi = (size_t)z * HD + ((size_t)kvh * G + g) * D + dim;
         a.att_out[oi] = ov;
-        uint16_t hi, lo;
-        split_bf16(ov, hi, lo);
-        a.att_hi[oi] = hi;
-        a.att_lo[oi] = lo;
+        if (a.att_hi) {
+            uint16_t hi, lo;
+            split_bf16(ov, hi, lo);
+            a.att_hi[oi] = hi;
+            a.att_lo[oi] = lo;
+        }
     }
 }
 

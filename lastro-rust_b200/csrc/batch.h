@@ -174,13 +174,13 @@ struct BAttnArgs {
     const void* v_pool;
     const int* page_table;     // [sequences][pt_stride]
     int pt_stride, page_size, kv_f32;
-    const int* seq;            // [n]
+    const int* seq;            // [n] (null: one token, sequence 0)
     const int* pos;            // [sequences]: the token attends positions 0..pos
     float* part_acc;           // [n][heads][S][d]
     float* part_ml;            // [n][heads][S][2]
     unsigned int* counters;    // [n][kv_heads], zero between launches
     float* att_out;            // [n][heads * d]
-    uint16_t* att_hi;          // [n][heads * d] split of att_out
+    uint16_t* att_hi;          // [n][heads * d] split of att_out (null: not written)
     uint16_t* att_lo;
     int* err;
     int n, kv_heads, G, S, cap;  // cap: positions one split stages (>= ceil(max_len / S))

@@ -461,7 +461,30 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         aa.max_len = m->max_len;
         aa.split_cap = attn_split_cap(m->max_len);
         aa.scale = d.attention_multiplier;
-        if ((e = launch_attention(aa, s, pdl)) != cudaSuccess) return e;
+        if (m->attn_tc) {
+            BAttnArgs ba{};
+            ba.q = m->q;
+            ba.k_pool = L.k_pool;
+            ba.v_pool = L.v_pool;
+            ba.page_table = m->page_table;
+            ba.pt_stride = m->max_pages;
+            ba.page_size = kPageSize;
+            ba.kv_f32 = 0;
+            ba.pos = m->d_pos;
+            ba.part_acc = m->part_acc;
+            ba.part_ml = m->part_ml;
+            ba.counters = m->attn_counters;
+            ba.att_out = m->att;
+            ba.err = m->d_err;
+            ba.n = 1;
+            ba.kv_heads = d.kv_heads;
+            ba.G = m->G;
+            ba.S = kAttnSplits;
+            ba.scale = d.attention_multiplier;
+            if ((e = launch_battention_tc(ba, &m->kvmaps[2 * l], &m->kvmaps[2 * l + 1], s)) != cudaSuccess) return e;
+        } else {
+            if ((e = launch_attention(aa, s, pdl)) != cudaSuccess) return e;
+        }
         if ((e = mark(pe, s, KK_ATTN)) != cudaSuccess) return e;
 
         OprojArgs oa{};
@@ -749,6 +772,21 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
         cudaFreeHost(m->h_token);
         delete m;
         return LASTRO_E_CUDA;
+    }
+    if (d.kv_dtype == LASTRO_DTYPE_BF16 && m->G <= 8) {  // TMA page maps for the tensor-core attention
+        const uint64_t rows = (uint64_t)m->max_pages * d.kv_heads * kPageSize;
+        m->kvmaps.resize((size_t)d.layers * 2);
+        bool ok = true;
+        for (int l = 0; l < d.layers && ok; ++l)
+            ok = make_kv_map(&m->kvmaps[2 * l], m->L[l].k_pool, rows) == cudaSuccess &&
+                 make_kv_map(&m->kvmaps[2 * l + 1], m->L[l].v_pool, rows) == cudaSuccess;
+        if (!ok) {
+            cudaGetLastError();
+            m->kvmaps.clear();
+        }
+        // off by default: at batch 1 (16 splits, one token) the CUDA-core kernel, whose split merge is one round of
+        // loads and shuffles, measures faster on B200 (C3: 16.4 vs 13 us per launch)
+        m->attn_tc = false;
     }
     ctx_retain(ctx);
     *out = m;
@@ -1060,6 +1098,20 @@ extern "C" int lastro_model_set_options(lastro_model* m, int32_t use_graphs, int
 }
 
 extern "C" int lastro_model_fused(const lastro_model* m) { return m && m->fused_ok && m->use_fused ? 1 : 0; }
+
+extern "C" int lastro_model_set_attention(lastro_model* m, int32_t tensor_cores) {
+    if (!m) return LASTRO_E_ARG;
+    if (tensor_cores && m->kvmaps.empty())
+        return set_err(m->ctx, LASTRO_E_UNSUPPORTED, "tensor-core attention needs bf16 KV and TMA page maps");
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    if (m->graph) {
+        cudaGraphExecDestroy(m->graph);
+        m->graph = nullptr;
+    }
+    m->attn_tc = tensor_cores != 0;
+    return LASTRO_OK;
+}
 
 extern "C" void lastro_model_destroy(lastro_model* m) {
     if (!m) return;

@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "../../include/lastro_b200.h"
+#include "batch.h"
 #include "kernels.h"
 
 // Reference-counted by its layers and models, so that the context and its objects may be destroyed in any order
@@ -164,6 +165,10 @@ struct lastro_model {
     unsigned int *f_ticket = nullptr, *f_epoch = nullptr, *f_count = nullptr;
     lastro::FusedExchange fx{};
     unsigned long long* f_best = nullptr;
+    // bf16 KV: optional attention on tensor cores (the batched step's streaming kernel, 16 context splits) with TMA page
+    // loads through these maps (per layer: K, V); the CUDA-core split kernel by default
+    std::vector<CUtensorMap> kvmaps;
+    bool attn_tc = false;
 };
 
 namespace lastro_capi {

@@ -73,6 +73,7 @@ EXPORTS = {
     "lastro_model_profile": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32]),
     "lastro_model_set_options": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32]),
     "lastro_model_fused": (C.c_int, [C.c_void_p]),
+    "lastro_model_set_attention": (C.c_int, [C.c_void_p, C.c_int32]),
     "lastro_model_destroy": (None, [C.c_void_p]),
     "lastro_batch_create": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_void_p)]),
     "lastro_batch_exchange_handle": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32]),
@@ -292,6 +293,10 @@ class GpuModel:
 
     def set_options(self, graphs: bool = True, pdl: bool = True, fused: bool = False):
         self.ctx.check(lib().lastro_model_set_options(self.h, int(graphs), int(pdl), int(fused)))
+
+    def set_attention(self, tensor_cores: bool = True):
+        """bf16 KV: attention on tensor cores or the CUDA-core split kernel (the default: faster at batch 1)."""
+        self.ctx.check(lib().lastro_model_set_attention(self.h, int(tensor_cores)))
 
     @property
     def fused(self) -> bool:

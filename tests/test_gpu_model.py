@@ -21,10 +21,12 @@ GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 TIE_GAP = 1e-3  # bin/m1b-gulosa.rs:20
 
 
-def gpu_model(ctx, cfg, weights, max_len, kv="f32", fused=False):
+def gpu_model(ctx, cfg, weights, max_len, kv="f32", fused=False, attn_tc=None):
     m = LB.GpuModel(ctx, cfg, max_len, kv_dtype=kv)
     m.load_weights(weights)
     m.set_options(fused=fused)
+    if attn_tc is not None:
+        m.set_attention(attn_tc)
     assert m.fused == fused
     return m
 
@@ -266,4 +268,24 @@ def test_profile_direct_launches_report_every_kernel(gpu_ctx):
     assert all(v == 0.0 for k, v in prof.items() if k != "fused_step")
     lg, _, _, _ = m.step(5)
     assert np.isfinite(lg).all()
+    m.close()
+
+
+@pytest.mark.parametrize("attn_tc", [True, False], ids=["tensor-core-attention", "cuda-core-attention"])
+def test_bf16_kv_attention_kernels_match_oracle(gpu_ctx, pool, attn_tc):
+    """The chain with bf16 KV on either attention kernel (tensor cores with TMA page loads, the default; or the CUDA-core
+    split kernel) against the oracle storing bf16-rounded K/V (Session(kv_bf16=True)): 150 positions, three KV pages,
+    so the 16 context splits of the tensor-core kernel hold 0, 1 or 2 pages."""
+    cfg = CFG.TINY_768
+    w = reference_tiny_weights(cfg)
+    m = gpu_model(gpu_ctx, cfg, w, 256, "bf16", False, attn_tc)
+    om = O.Model(cfg, weights=w)
+    s = O.Session(om, pool, 256, kv_bf16=True)
+    for t, tok in enumerate(toks_like_reference(150, cfg["vocab"])):
+        lg, nxt, ids, _ = m.step(tok)
+        lo, io, _ = s.step(tok)
+        assert rel_l2(lg, lo) < 1e-4, f"position {t}: {rel_l2(lg, lo):.2e}"
+        assert np.array_equal(ids, io), f"position {t}: routing"
+    s.close()
+    om.close()
     m.close()
