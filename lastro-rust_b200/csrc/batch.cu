@@ -843,17 +843,29 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(BExchangeArgs a) {
 // ------------------------------------------------------------------------------------------------------------------
 // argmax per token (the last maximum, bin/m1b-gulosa.rs:22-24), position advanced, next token fed back
 // ------------------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) bargmax_kernel(BHeadArgs a) {
-    __shared__ unsigned long long best[8];
+__global__ void __launch_bounds__(1024) bargmax_kernel(BHeadArgs a) {
+    __shared__ unsigned long long best[32];
     const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float* lg = a.logits + (size_t)t * a.V;
     pdl_wait();
     pdl_launch();
-    unsigned long long b = 0ull;
-    for (int v = threadIdx.x; v < a.V; v += blockDim.x) {
-        const unsigned long long key = arg_key(__ldcg(lg + v), v);
-        b = key > b ? key : b;
+    // four independent running maxima per thread (keys order by value, then by index: the last maximum wins)
+    unsigned long long b0 = 0ull, b1 = 0ull, b2 = 0ull, b3 = 0ull;
+    const int stride = 4 * blockDim.x;
+    for (int v = threadIdx.x; v < a.V; v += stride) {
+        const int v1 = v + blockDim.x, v2 = v + 2 * blockDim.x, v3 = v + 3 * blockDim.x;
+        const unsigned long long k0 = arg_key(__ldcg(lg + v), v);
+        const unsigned long long k1 = v1 < a.V ? arg_key(__ldcg(lg + v1), v1) : 0ull;
+        const unsigned long long k2 = v2 < a.V ? arg_key(__ldcg(lg + v2), v2) : 0ull;
+        const unsigned long long k3 = v3 < a.V ? arg_key(__ldcg(lg + v3), v3) : 0ull;
+        b0 = k0 > b0 ? k0 : b0;
+        b1 = k1 > b1 ? k1 : b1;
+        b2 = k2 > b2 ? k2 : b2;
+        b3 = k3 > b3 ? k3 : b3;
     }
+    unsigned long long b = b0 > b1 ? b0 : b1;
+    b = b2 > b ? b2 : b;
+    b = b3 > b ? b3 : b;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const unsigned long long x = shfl_xor_u64(b, o);
@@ -862,8 +874,7 @@ __global__ void __launch_bounds__(256) bargmax_kernel(BHeadArgs a) {
     if (lane == 0) best[warp] = b;
     __syncthreads();
     if (threadIdx.x != 0) return;
-    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) b = best[w] > b ? best[w] : b;
-    b = best[0] > b ? best[0] : b;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) b = best[w] > b ? best[w] : b;
     const int id = (int)(uint32_t)b;
     a.next[t] = id;
     if (a.tokens) a.tokens[t] = id;
@@ -1768,7 +1779,7 @@ cudaError_t launch_ep_combine(const BExchangeArgs& a, cudaStream_t s) {
 }
 
 cudaError_t launch_bargmax(const BHeadArgs& a, cudaStream_t s) {
-    return launch_pdl(bargmax_kernel, dim3(a.n), dim3(256), 0, s, a);
+    return launch_pdl(bargmax_kernel, dim3(a.n), dim3(1024), 0, s, a);
 }
 
 }  // namespace lastro
