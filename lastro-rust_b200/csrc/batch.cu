@@ -670,13 +670,20 @@ __global__ void __launch_bounds__(256) brouter_kernel(BRouterArgs a) {
     }
     __syncthreads();
     for (int e = warp; e < a.E; e += BLOCK / 32) {
+        // the row's chunks (H <= 2048: at most 8 per lane) all loaded before the first product
         const uint16_t* row = a.wr + (size_t)e * a.H;
+        uint4 w[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int c = lane * 8 + q * 256;
+            w[q] = c < a.H ? ld_weight(row + c) : make_uint4(0u, 0u, 0u, 0u);
+        }
         float acc = 0.0f;
-        for (int c = lane * 8; c < a.H; c += 256) {
-            const uint4 w = ld_weight(row + c);
-            const float4 xa = *reinterpret_cast<const float4*>(xs + c);
-            const float4 xb = *reinterpret_cast<const float4*>(xs + c + 4);
-            acc = dot8(w, xa, xb, acc);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int c = lane * 8 + q * 256;
+            if (c < a.H)
+                acc = dot8(w[q], *reinterpret_cast<const float4*>(xs + c), *reinterpret_cast<const float4*>(xs + c + 4), acc);
         }
         acc = warp_sum(acc);
         if (lane == 0) lg[e] = a.bias ? __fadd_rn(acc, __ldg(a.bias + e)) : acc;
@@ -773,15 +780,39 @@ __global__ void __launch_bounds__(1024) ep_group_kernel(BExchangeArgs a) {
         *a.n_pos = o;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < slots; i += blockDim.x) {
-        const int e = le[i];
-        if (e < 0) continue;
-        int rank = 0;
-        for (int j = 0; j < i; ++j) rank += (le[j] == e);
-        const int pos = off[e] + rank;
-        const int sender = i / L.cap, pair = i - sender * L.cap;
-        a.x_rows[pos] = sender * L.cap_tok + pair / a.k;
-        a.src[pos] = i;
+    // position of slot i = off[e] + (slots of expert e before i): per chunk of 1024 slots, the rank within the warp
+    // from __match_any_sync, the warps' counts per expert prefixed in warp order, plus the earlier chunks' counts
+    __shared__ int wcnt[32][kMaxExperts];
+    __shared__ int run[kMaxExperts];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x < kMaxExperts) run[threadIdx.x] = 0;
+    for (int c0 = 0; c0 < slots; c0 += blockDim.x) {
+        const int i = c0 + threadIdx.x;
+        const int e = i < slots ? le[i] : -1;
+        wcnt[warp][lane] = 0;
+        wcnt[warp][lane + 32] = 0;
+        __syncwarp();
+        const unsigned int same = __match_any_sync(0xffffffffu, e);
+        const int rk = __popc(same & ((1u << lane) - 1u));
+        if (e >= 0 && rk == 0) wcnt[warp][e] = __popc(same);
+        __syncthreads();
+        if (threadIdx.x < a.experts_per_rank) {
+            int acc = run[threadIdx.x];
+            for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+                const int c = wcnt[w][threadIdx.x];
+                wcnt[w][threadIdx.x] = acc;
+                acc += c;
+            }
+            run[threadIdx.x] = acc;
+        }
+        __syncthreads();
+        if (e >= 0) {
+            const int pos = off[e] + wcnt[warp][e] + rk;
+            const int sender = i / L.cap, pair = i - sender * L.cap;
+            a.x_rows[pos] = sender * L.cap_tok + pair / a.k;
+            a.src[pos] = i;
+        }
+        __syncthreads();
     }
 }
 
@@ -810,18 +841,25 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(BExchangeArgs a) {
     for (int j = 0; j < kMaxTopK; ++j) w[j] = j < a.k ? __ldcg(a.weights + (size_t)t * a.k + j) : 0.0f;
     const float* cb = reinterpret_cast<const float*>(me + L.cb) + (size_t)t * a.k * a.H;
     float* h = a.h + (size_t)t * a.H;
-    float hv[NV];
+    // every load of the thread first (the stores to h below would otherwise keep the compiler from hoisting them)
+    float hv[NV], yv[NV][kMaxTopK];
+#pragma unroll
+    for (int q = 0; q < NV; ++q) {
+        const int i = threadIdx.x + q * BLOCK;
+        hv[q] = i < a.H ? __ldcg(h + i) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j) yv[q][j] = (i < a.H && j < a.k) ? __ldcg(cb + (size_t)j * a.H + i) : 0.0f;
+    }
     float ss = 0.0f;
 #pragma unroll
     for (int q = 0; q < NV; ++q) {
         const int i = threadIdx.x + q * BLOCK;
-        hv[q] = 0.0f;
         if (i >= a.H) continue;
         float acc = 0.0f;
 #pragma unroll
         for (int j = 0; j < kMaxTopK; ++j)
-            if (j < a.k) acc = __fadd_rn(acc, __fmul_rn(w[j], __ldcg(cb + (size_t)j * a.H + i)));
-        hv[q] = __fadd_rn(__ldcg(h + i), __fmul_rn(a.resid, acc));
+            if (j < a.k) acc = __fadd_rn(acc, __fmul_rn(w[j], yv[q][j]));
+        hv[q] = __fadd_rn(hv[q], __fmul_rn(a.resid, acc));
         h[i] = hv[q];
         ss = fmaf(hv[q], hv[q], ss);
     }
