@@ -87,12 +87,13 @@ const CUtensorMap* wmap(const lastro_batch* b, int layer, int which) {
     return i < b->wmaps.size() ? &b->wmaps[i] : nullptr;
 }
 
-// split-K slices for a dense GEMM of `rows` x K: enough CTAs for two per SM, slices of at least 128 columns
+// split-K slices for a dense GEMM of `rows` x K: at most two CTAs per SM, slices of at least 256 columns (4 stages; on
+// C5 slices of 128 measured the same kernel times with twice the partial-sum traffic)
 int pick_ks(int rows, int K, int n_sm) {
     const int tiles = (rows + kBRows - 1) / kBRows, chunks = K / kBK;
     int best = 1;
     for (int d = 1; d <= chunks; ++d)
-        if (chunks % d == 0 && K / d >= 128 && tiles * d <= 2 * n_sm && d <= 16) best = d;
+        if (chunks % d == 0 && K / d >= 256 && tiles * d <= 2 * n_sm && d <= 16) best = d;
     return best;
 }
 
