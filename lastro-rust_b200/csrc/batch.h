@@ -2,10 +2,11 @@
 // MoE experts partitioned over the ranks of an expert-parallel group.
 //
 // Per layer, on every rank for its own tokens:
-//   attn_norm    RMSNorm(h) (layer 0: the embedding row x multiplier) -> bf16 hi + lo split of xn
-//   gemm         [q;k;v] partial sums over K slices (tensor cores, split-K)
+//   gemm         [q;k;v] partial sums over K slices (split-K)
 //   rope_kv      slices summed in order -> RoPE -> q; K/V appended to each sequence's paged cache
-//   attention    the batch-1 split-KV kernel with a grid dimension over tokens; writes att split into hi + lo
+//   attention    bf16 KV: streaming tensor-core kernel, CTA per (KV head, token) over TMA-loaded pages (context
+//                splits with an in-order merge when a rank holds few tokens); f32 KV: CUDA-core split kernel;
+//                writes att split into hi + lo
 //   gemm         o-projection partial sums over K slices
 //   router       h += resid * sum of the slices; RMSNorm(h) -> router GEMV (+ bias) -> top-k -> softmax; then the
 //                token's xn row (hi + lo) is pushed once to the exchange region of every rank owning one of its experts
@@ -15,11 +16,13 @@
 //                pair's sender (peer memory)
 //   combine      h += resid * sum_j w_j y_j, slots in routing order; then the next layer's attention norm (or the
 //                final norm) -> xn hi + lo
-// and the step ends with the tied lm_head GEMM and a per-token argmax.
+// (layer 0's attention norm runs on the embedding rows first) and the step ends with the tied lm_head GEMM and a
+// per-token argmax.
 //
-// The GEMMs run on the tensor cores (mma.sync m16n8k16, bf16 operands, f32 accumulators): the weights are bf16 and
-// each f32 activation x is split into hi = bf16(x) and lo = bf16(x - hi), both multiplied (x - hi - lo is below
-// 2^-17 |x|), so the products carry f32-level accuracy rather than bf16 rounding of the activations.
+// The GEMMs run on the tensor cores with bf16 operands and f32 accumulators: tcgen05 with the accumulator in tensor
+// memory (default: warp-specialised, TMA weight tiles) or mma.sync.  The weights are bf16 and each f32 activation x is
+// split into hi = bf16(x) and lo = bf16(x - hi), both multiplied (x - hi - lo is below 2^-17 |x|), so the products
+// carry f32-level accuracy rather than bf16 rounding of the activations.
 #pragma once
 
 #include <cuda.h>
