@@ -377,7 +377,7 @@ def run_batched(a):
         "kernels_ms_per_step": {k: round(v, 4) for k, v in prof.items()},
         "e2e": {"value": total * K / (e2e_ms / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": 8 * n,
                 "d2h_bytes_per_step": 4 * n},
-        "gpu_launches": K * (L * 9 + 3),
+        "gpu_launches": K * (L * 8 + 3),  # norm; 8 kernels per layer; lm_head, argmax
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not a.no_cpu_baseline:

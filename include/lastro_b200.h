@@ -173,8 +173,8 @@ int lastro_batch_reset(lastro_batch *batch, int32_t seq);
 int lastro_batch_position(const lastro_batch *batch, int32_t seq, int32_t *pos);
 /* mean device ms per step of each kernel kind over `steps` directly launched greedy steps (tokens as for
  * lastro_batch_decode), timed with events between launches: norm (layer 0), qkv, rope_kv, attention, oproj, router
- * (with the dispatch), group, gate_up, down (with the return), combine (with the next norm), lm_head, argmax
- * (n_kinds >= 12) */
+ * (with the dispatch and the grouping of the received pairs), group (0: part of the router), gate_up, down (with the
+ * return), combine (with the next norm), lm_head, argmax (n_kinds >= 12) */
 int lastro_batch_profile(lastro_batch *batch, int32_t n, const int32_t *seq_ids, const int32_t *tokens, int32_t steps,
                          float *kernel_ms, int32_t n_kinds);
 /* use_graphs: replay each step as a CUDA graph (default 1); use_tcgen05: the GEMMs on the 5th-generation tensor cores

@@ -612,6 +612,92 @@ __global__ void __launch_bounds__(128) battn_kernel(BAttnArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------------------------------
+// group (owner, run by the router grid's last CTA): after every sender's dispatch flag, the received pairs whose
+// expert is local are ordered by (local expert, sender, pair): per expert offsets and counts for the grouped GEMMs,
+// and per position its rx token row and pair.
+// ------------------------------------------------------------------------------------------------------------------
+LDEV void group_pairs(const BExchangeArgs& a) {
+    __shared__ short le[kBMaxSlots];
+    __shared__ int cnt[kMaxExperts], off[kMaxExperts];
+    __shared__ int ok_all;
+    __shared__ int pairs[kBMaxRanks];  // pairs each sender dispatched in this layer
+    const XLayout& L = a.lay;
+    unsigned char* me = a.peers[a.rank];
+    const unsigned int epoch = __ldcg(a.epoch_base) + a.layer + 1;
+    if (threadIdx.x == 0) ok_all = 1;
+    if (threadIdx.x < kMaxExperts) cnt[threadIdx.x] = 0;
+    __syncthreads();
+    if (threadIdx.x < a.world) {
+        if (wait_flag(flag_ptr(me, L, 0, threadIdx.x), epoch, a.err, 10 + threadIdx.x))
+            pairs[threadIdx.x] = (int)ld_acquire_sys(reinterpret_cast<const unsigned int*>(me + L.rx_n) + threadIdx.x) * a.k;
+        else
+            atomicExch(&ok_all, 0);
+    }
+    __syncthreads();
+    const int slots = a.world * L.cap;
+    const int e0 = a.rank * a.experts_per_rank;
+    const int* rx_ids = reinterpret_cast<const int*>(me + L.rx_ids);
+    for (int i = threadIdx.x; i < slots; i += blockDim.x) {
+        const int s = i / L.cap, p = i - s * L.cap;
+        int x = -1;
+        if (ok_all && p < pairs[s]) {
+            const int e = __ldcg(rx_ids + i) - e0;
+            if (e >= 0 && e < a.experts_per_rank) {
+                x = e;
+                atomicAdd(&cnt[e], 1);
+            }
+        }
+        le[i] = (short)x;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int o = 0;
+        for (int e = 0; e < a.experts_per_rank; ++e) {
+            off[e] = o;
+            o += cnt[e];
+            a.g_off[e] = off[e];
+            a.g_cnt[e] = cnt[e];
+        }
+        *a.n_pos = o;
+    }
+    __syncthreads();
+    // position of slot i = off[e] + (slots of expert e before i): per chunk of 1024 slots, the rank within the warp
+    // from __match_any_sync, the warps' counts per expert prefixed in warp order, plus the earlier chunks' counts
+    __shared__ int wcnt[32][kMaxExperts];
+    __shared__ int run[kMaxExperts];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x < kMaxExperts) run[threadIdx.x] = 0;
+    for (int c0 = 0; c0 < slots; c0 += blockDim.x) {
+        const int i = c0 + threadIdx.x;
+        const int e = i < slots ? le[i] : -1;
+        wcnt[warp][lane] = 0;
+        wcnt[warp][lane + 32] = 0;
+        __syncwarp();
+        const unsigned int same = __match_any_sync(0xffffffffu, e);
+        const int rk = __popc(same & ((1u << lane) - 1u));
+        if (e >= 0 && rk == 0) wcnt[warp][e] = __popc(same);
+        __syncthreads();
+        if (threadIdx.x < a.experts_per_rank) {
+            int acc = run[threadIdx.x];
+            for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+                const int c = wcnt[w][threadIdx.x];
+                wcnt[w][threadIdx.x] = acc;
+                acc += c;
+            }
+            run[threadIdx.x] = acc;
+        }
+        __syncthreads();
+        if (e >= 0) {
+            const int pos = off[e] + wcnt[warp][e] + rk;
+            const int sender = i / L.cap, pair = i - sender * L.cap;
+            a.x_rows[pos] = sender * L.cap_tok + pair / a.k;
+            a.src[pos] = i;
+        }
+        __syncthreads();
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
 // router: h += resid * (o-projection slices summed in order); xn = RMSNorm(h) (f32, kept for the router, split hi + lo
 // for the experts); logits_e = W_r[e] . xn (+ bias_e), one warp per expert; top-k in block.rs:81-89's order, softmax.
 // ------------------------------------------------------------------------------------------------------------------
@@ -731,89 +817,9 @@ __global__ void __launch_bounds__(256) brouter_kernel(BRouterArgs a) {
         const unsigned int epoch = __ldcg(x.epoch_base) + x.layer + 1;
         st_release_sys(flag_ptr(x.peers[threadIdx.x], L, 0, x.rank), epoch);
     }
-}
-
-// ------------------------------------------------------------------------------------------------------------------
-// group (owner, one CTA): after every sender's dispatch flag, the received pairs whose expert is local are ordered by
-// (local expert, sender, pair): per expert offsets and counts for the grouped GEMMs, and per position its rx row.
-// ------------------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) ep_group_kernel(BExchangeArgs a) {
-    __shared__ short le[kBMaxSlots];
-    __shared__ int cnt[kMaxExperts], off[kMaxExperts];
-    __shared__ int ok_all;
-    const XLayout& L = a.lay;
-    unsigned char* me = a.peers[a.rank];
-    const unsigned int epoch = __ldcg(a.epoch_base) + a.layer + 1;
-    pdl_wait();
-    pdl_launch();
-    if (threadIdx.x == 0) ok_all = 1;
-    if (threadIdx.x < kMaxExperts) cnt[threadIdx.x] = 0;
+    // the same CTA then waits for every rank's dispatch and groups the pairs this rank's experts received
     __syncthreads();
-    if (threadIdx.x < a.world && !wait_flag(flag_ptr(me, L, 0, threadIdx.x), epoch, a.err, 10 + threadIdx.x))
-        atomicExch(&ok_all, 0);
-    __syncthreads();
-    const int slots = a.world * L.cap;
-    const int e0 = a.rank * a.experts_per_rank;
-    const int* rx_ids = reinterpret_cast<const int*>(me + L.rx_ids);
-    const int* rx_n = reinterpret_cast<const int*>(me + L.rx_n);
-    for (int i = threadIdx.x; i < slots; i += blockDim.x) {
-        const int s = i / L.cap, p = i - s * L.cap;
-        int x = -1;
-        if (ok_all && p < ld_acquire_sys(reinterpret_cast<const unsigned int*>(rx_n) + s) * a.k) {
-            const int e = __ldcg(rx_ids + i) - e0;
-            if (e >= 0 && e < a.experts_per_rank) {
-                x = e;
-                atomicAdd(&cnt[e], 1);
-            }
-        }
-        le[i] = (short)x;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int o = 0;
-        for (int e = 0; e < a.experts_per_rank; ++e) {
-            off[e] = o;
-            o += cnt[e];
-            a.g_off[e] = off[e];
-            a.g_cnt[e] = cnt[e];
-        }
-        *a.n_pos = o;
-    }
-    __syncthreads();
-    // position of slot i = off[e] + (slots of expert e before i): per chunk of 1024 slots, the rank within the warp
-    // from __match_any_sync, the warps' counts per expert prefixed in warp order, plus the earlier chunks' counts
-    __shared__ int wcnt[32][kMaxExperts];
-    __shared__ int run[kMaxExperts];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (threadIdx.x < kMaxExperts) run[threadIdx.x] = 0;
-    for (int c0 = 0; c0 < slots; c0 += blockDim.x) {
-        const int i = c0 + threadIdx.x;
-        const int e = i < slots ? le[i] : -1;
-        wcnt[warp][lane] = 0;
-        wcnt[warp][lane + 32] = 0;
-        __syncwarp();
-        const unsigned int same = __match_any_sync(0xffffffffu, e);
-        const int rk = __popc(same & ((1u << lane) - 1u));
-        if (e >= 0 && rk == 0) wcnt[warp][e] = __popc(same);
-        __syncthreads();
-        if (threadIdx.x < a.experts_per_rank) {
-            int acc = run[threadIdx.x];
-            for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
-                const int c = wcnt[w][threadIdx.x];
-                wcnt[w][threadIdx.x] = acc;
-                acc += c;
-            }
-            run[threadIdx.x] = acc;
-        }
-        __syncthreads();
-        if (e >= 0) {
-            const int pos = off[e] + wcnt[warp][e] + rk;
-            const int sender = i / L.cap, pair = i - sender * L.cap;
-            a.x_rows[pos] = sender * L.cap_tok + pair / a.k;
-            a.src[pos] = i;
-        }
-        __syncthreads();
-    }
+    group_pairs(x);
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -1802,13 +1808,9 @@ cudaError_t launch_brope_kv(const BRopeArgs& a, cudaStream_t s) {
 }
 
 cudaError_t launch_brouter(const BRouterArgs& a, cudaStream_t s) {
+    if (a.x.world * a.x.lay.cap > kBMaxSlots || a.x.experts_per_rank > kMaxExperts) return cudaErrorInvalidValue;
     if (a.ks > 16 || a.H % 8 || a.H > 2048 || a.E > kMaxExperts || a.k > kMaxTopK || a.n < 1) return cudaErrorInvalidValue;
     return launch_pdl(brouter_kernel, dim3(a.n), dim3(256), sizeof(float) * a.H, s, a);
-}
-
-cudaError_t launch_ep_group(const BExchangeArgs& a, cudaStream_t s) {
-    if (a.world * a.lay.cap > kBMaxSlots || a.experts_per_rank > kMaxExperts) return cudaErrorInvalidValue;
-    return launch_pdl(ep_group_kernel, dim3(1), dim3(1024), 0, s, a);
 }
 
 cudaError_t launch_ep_combine(const BExchangeArgs& a, cudaStream_t s) {

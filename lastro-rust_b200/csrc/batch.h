@@ -9,8 +9,9 @@
 //                writes att split into hi + lo
 //   gemm         o-projection partial sums over K slices
 //   router       h += resid * sum of the slices; RMSNorm(h) -> router GEMV (+ bias) -> top-k -> softmax; then the
-//                token's xn row (hi + lo) is pushed once to the exchange region of every rank owning one of its experts
-//   group        (owner) received pairs grouped by local expert, in (sender, pair) order
+//                token's xn row (hi + lo) is pushed once to the exchange region of every rank owning one of its experts;
+//                the grid's last CTA then waits for every rank's dispatch and groups the received pairs by local
+//                expert, in (sender, pair) order
 //   gemm         gate_up of every local expert on its pairs, SwiGLU in the epilogue -> a hi + lo
 //   gemm         down of every local expert; the epilogue writes each result row into the combine rows of the
 //                pair's sender (peer memory)
@@ -38,6 +39,7 @@ constexpr int kBStages = 3;
 constexpr size_t kBStageBytes = (size_t)kBRows * kBK * 2 + 2 * (size_t)kBTok * kBK * 2;  // 32 KB
 constexpr size_t kBGemmSmem = kBStages * kBStageBytes;
 constexpr int kBMaxSlots = 4096;  // pairs one rank may receive in one layer (world * tokens per rank * k)
+constexpr int kBMaxRanks = 32;    // ranks of one expert-parallel group
 
 // Exchange region of one rank (the same layout on every rank; every rank maps every other rank's region):
 //   rx      [world][cap_tok] token rows, each bf16 hi [H] then lo [H] (written by the senders, once per owner)
@@ -205,7 +207,6 @@ cudaError_t make_weight_map(CUtensorMap* map, const void* base, uint64_t rows, u
 cudaError_t launch_battn_norm(const BNormArgs& a, int n, cudaStream_t s);
 cudaError_t launch_brope_kv(const BRopeArgs& a, cudaStream_t s);
 cudaError_t launch_brouter(const BRouterArgs& a, cudaStream_t s);
-cudaError_t launch_ep_group(const BExchangeArgs& a, cudaStream_t s);
 cudaError_t launch_ep_combine(const BExchangeArgs& a, cudaStream_t s);
 cudaError_t launch_bargmax(const BHeadArgs& a, cudaStream_t s);
 

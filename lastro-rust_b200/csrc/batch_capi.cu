@@ -248,8 +248,6 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         rta.k = k;
         if ((e = mark(b, s, BK_ROUTER, launch_brouter(rta, s)))) break;
 
-        if ((e = mark(b, s, BK_GROUP, launch_ep_group(xa, s)))) break;
-
         BGemmArgs gu{};
         gu.w = reinterpret_cast<const uint16_t*>(L.gate_up);
         gu.group_stride = (long long)2 * I * H;
@@ -393,7 +391,7 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
     *out = nullptr;
     lastro_ctx* ctx = m->ctx;
     const lastro_model_desc& d = m->d;
-    if (max_seqs < 1 || max_len < 1 || world < 1 || world > 32 || rank < 0 || rank >= world)
+    if (max_seqs < 1 || max_len < 1 || world < 1 || world > kBMaxRanks || rank < 0 || rank >= world)
         return set_err(ctx, LASTRO_E_ARG, "batch: max_seqs %d, max_len %d, rank %d of %d", max_seqs, max_len, rank, world);
     if (m->q8) return set_err(ctx, LASTRO_E_UNSUPPORTED, "batched decode runs bf16 weights");
     if (d.experts % world) return set_err(ctx, LASTRO_E_UNSUPPORTED, "%d experts over %d ranks", d.experts, world);
