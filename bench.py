@@ -64,6 +64,9 @@ def parse():
                     "decoding the prompt through the model")
     ap.add_argument("--layers", type=int, default=0, help="with --profile-only: a 3B-shaped model with this many "
                     "layers (small ncu captures; the kernels are those of the full model)")
+    ap.add_argument("--placement", choices=("balanced", "interleaved", "contiguous"), default="balanced",
+                    help="c5 on N > 1 GPUs: experts over ranks, balanced over the pair counts of the first step "
+                    "(greedy, E/N per rank), e mod N, or contiguous blocks")
     ap.add_argument("--gemm", type=int, default=2, choices=(0, 1, 2), help="c5 GEMMs: 2 tcgen05 warp-specialised "
                     "(TMA weight tiles), 1 tcgen05 with all-thread cp.async stages, 0 mma.sync")
     ap.add_argument("--fused", action="store_true", help="the fused step kernel (one persistent launch per step) instead "
@@ -237,11 +240,12 @@ def cpu_batched_rate(cfg, context, c, steps=2, seqs=4):
 
 def run_batched(a):
     """C5: 64 sequences (64/N per rank) with 1024-token contexts decode together; every layer's MoE pairs go to the
-    rank that owns their expert (experts 40/N per rank, contiguous) through the peer-memory exchange."""
+    rank that owns their expert (experts 40/N per rank, placed by --placement) through the peer-memory exchange."""
     import torch
     import torch.distributed as dist
 
     import lastro_b200 as LB
+    from lastro_b200 import ep as EP
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -304,6 +308,14 @@ def run_batched(a):
         tc = torch.tensor(counts, device="cuda")
         dist.all_reduce(tc)
         counts = tc.cpu().numpy()
+    if a.placement == "balanced":
+        owner = EP.balanced_placement(counts, world)
+    elif a.placement == "interleaved":
+        owner = EP.interleaved_placement(cfg["experts"], world)
+    else:
+        owner = EP.contiguous_placement(cfg["experts"], world)
+    if world > 1:
+        batch.set_expert_placement(owner)  # the same on every rank (counts were all-reduced)
     batch.decode(seqs, toks, W, want_ids=False)
     toks = [int(x) for x in batch.decode(seqs, toks, 1)[-1]]
     if world > 1:
@@ -354,15 +366,15 @@ def run_batched(a):
     step_s = ms / 1000.0 / K
     hbm, peak_kind = peaks()
     achieved = step_bytes / world / step_s / 1e9  # per GPU
-    share = [float(counts[list(CFG.shard(E, r, world))].sum() / counts.sum()) for r in range(world)]
+    share = [float(counts[EP.owned(owner, r)].sum() / counts.sum()) for r in range(world)]
     line = {
         "metric": BATCH_METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
         "config": {"workload": c["name"], "batch": total, "seqs_per_rank": n, "context_start": ctx0,
                    "mean_context": mean_ctx, "kv_cache": f"paged {a.kv}",
-                   "parallelism": f"ep{world}: experts {E // world}/rank, attention data-parallel over sequences"
-                   if world > 1 else "single GPU",
+                   "parallelism": f"ep{world}: experts {E // world}/rank ({a.placement} placement), attention "
+                   "data-parallel over sequences" if world > 1 else "single GPU",
                    "weights": "bf16; batched GEMMs on tensor cores (" + ("mma.sync", "tcgen05, cp.async stages",
                               "tcgen05 warp-specialised, TMA weight tiles")[a.gemm] + ", accumulators f32, bf16 operands, "
                               "activations split hi + lo)",

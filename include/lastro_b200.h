@@ -144,9 +144,9 @@ void lastro_model_destroy(lastro_model *model);
 /* ---- batched decode with expert parallelism (no counterpart in the reference, which decodes one sequence) ------- */
 /* Many independent sequences decoded together on a model's weights (bf16); each sequence's results equal its own
  * single-sequence step up to summation order (the reference's multi-position contract, cpu.rs:234-238).  The MoE
- * experts are partitioned over the `world` ranks of an expert-parallel group, one process per GPU: rank r computes the
- * experts [r*E/world, (r+1)*E/world) for the pairs every rank routes to them, while attention and the dense layers stay
- * with each rank's own sequences.  Every rank creates its batch with the same max_seqs and world, passes the handle
+ * experts are partitioned over the `world` ranks of an expert-parallel group, one process per GPU: rank r computes
+ * E/world experts (by default [r*E/world, (r+1)*E/world); lastro_batch_set_expert_placement) for the pairs every rank
+ * routes to them, while attention and the dense layers stay with each rank's own sequences.  Every rank creates its batch with the same max_seqs and world, passes the handle
  * of its exchange region (lastro_batch_exchange_handle, 64 bytes) to the others, and connects with all of them in rank
  * order (lastro_batch_connect; world 1: handles may be NULL).  The ranks then call lastro_batch_step/decode the same
  * number of times, each with at least one of its own sequences.  Destroy a batch before its model.  A rank that does
@@ -159,6 +159,10 @@ int lastro_batch_connect(lastro_batch *batch, const void *handles, int32_t bytes
 /* per-layer router logit bias [layers, experts] added before the top-k (NULL removes it): a workload knob for skewed
  * expert load; Granite's router has no bias */
 int lastro_batch_set_router_bias(lastro_batch *batch, const float *bias);
+/* owner[e] (n_experts = E entries): the rank that computes expert e, every rank owning E/world experts.  All ranks of
+ * the group set the same placement between the same two steps; results do not depend on it (each expert still sees
+ * its pairs in global token order).  Refused (batch usable) for a wrong count or an uneven placement. */
+int lastro_batch_set_expert_placement(lastro_batch *batch, const int32_t *owner, int32_t n_experts);
 /* one token for each of n distinct sequences (ids < max_seqs): next [n] greedy ids (last maximum), logits [n, V] and
  * route_ids [n, layers, k] when non-NULL */
 int lastro_batch_step(lastro_batch *batch, int32_t n, const int32_t *seq_ids, const int32_t *tokens, int32_t *next,

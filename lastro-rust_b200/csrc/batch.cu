@@ -94,6 +94,9 @@ LDEV unsigned int* flag_ptr(unsigned char* region, const XLayout& L, int kind, i
     return reinterpret_cast<unsigned int*>(region + L.flags + ((size_t)kind * 64 + who) * 128);
 }
 
+// weight group (expert) of a launch's group g
+LDEV int weight_group(const BGemmArgs& a, int g) { return a.group_expert ? __ldg(a.group_expert + g) : a.group0 + g; }
+
 }  // namespace
 
 XLayout x_layout(int world, int tokens_per_rank, int k, int H) {
@@ -136,7 +139,7 @@ __global__ void __launch_bounds__(128) bgemm_kernel(BGemmArgs a) {
         p0 = __ldcg(a.g_off + g);
         ntot = __ldcg(a.g_cnt + g);
     }
-    const uint16_t* W = a.w + (size_t)(a.group0 + g) * a.group_stride;
+    const uint16_t* W = a.w + (size_t)weight_group(a, g) * a.group_stride;
     const int kbeg = blockIdx.z * a.k_split;
     const int nk = min(a.k_split, a.K - kbeg) / kBK;
     if (nk <= 0) ntot = 0;
@@ -635,16 +638,16 @@ LDEV void group_pairs(const BExchangeArgs& a) {
     }
     __syncthreads();
     const int slots = a.world * L.cap;
-    const int e0 = a.rank * a.experts_per_rank;
+    const int n_experts = a.world * a.experts_per_rank;
     const int* rx_ids = reinterpret_cast<const int*>(me + L.rx_ids);
     for (int i = threadIdx.x; i < slots; i += blockDim.x) {
         const int s = i / L.cap, p = i - s * L.cap;
         int x = -1;
         if (ok_all && p < pairs[s]) {
-            const int e = __ldcg(rx_ids + i) - e0;
-            if (e >= 0 && e < a.experts_per_rank) {
-                x = e;
-                atomicAdd(&cnt[e], 1);
+            const int id = __ldcg(rx_ids + i);
+            if (id >= 0 && id < n_experts && __ldg(a.owner + id) == a.rank) {
+                x = __ldg(a.local + id);
+                atomicAdd(&cnt[x], 1);
             }
         }
         le[i] = (short)x;
@@ -791,9 +794,9 @@ __global__ void __launch_bounds__(256) brouter_kernel(BRouterArgs a) {
     const BExchangeArgs& x = a.x;
     const XLayout& L = x.lay;
     for (int j = 0; j < a.k; ++j) {
-        const int o = min(sid[j] / x.experts_per_rank, x.world - 1);
+        const int o = __ldg(x.owner + sid[j]);
         bool seen = false;
-        for (int jj = 0; jj < j; ++jj) seen |= min(sid[jj] / x.experts_per_rank, x.world - 1) == o;
+        for (int jj = 0; jj < j; ++jj) seen |= __ldg(x.owner + sid[jj]) == o;
         if (seen) continue;  // the same for every thread (sid is shared)
         unsigned char* dst = x.peers[o] + L.rx + ((size_t)x.rank * L.cap_tok + t) * (size_t)a.H * 4;
         for (int i = threadIdx.x; i < a.H / 4; i += BLOCK) {
@@ -998,7 +1001,7 @@ __global__ void __launch_bounds__(128) bgemm_tc_kernel(BGemmArgs a) {
         p0 = __ldcg(a.g_off + g);
         ntot = __ldcg(a.g_cnt + g);
     }
-    const uint16_t* W = a.w + (size_t)(a.group0 + g) * a.group_stride;
+    const uint16_t* W = a.w + (size_t)weight_group(a, g) * a.group_stride;
     const int kbeg = blockIdx.z * a.k_split;
     const int nk = min(a.k_split, a.K - kbeg) / kBK;
     if (nk <= 0) ntot = 0;
@@ -1174,6 +1177,29 @@ __global__ void __launch_bounds__(128) bgemm_tc_kernel(BGemmArgs a) {
     }
 }
 
+// bgemm_ws setup (all threads): the accumulator's tensor-memory columns, the stage barriers (full: the TMA thread's
+// expect_tx arrival + 64 cp.async arrivals; empty: one MMA commit), the tile's done barrier
+LDEV void bgemm_ws_setup(uint32_t* tmem_base, uint64_t* full, uint64_t* empty, uint64_t* done, int stages,
+                         const CUtensorMap* wmap, int tid, int warp) {
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_base)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        for (int i = 0; i < stages; ++i) {
+            mbar_init(&full[i], 1 + 64);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(done, 1);
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(wmap)) : "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+}
+
 // ------------------------------------------------------------------------------------------------------------------
 // Warp-specialised tcgen05 GEMM (mode 2).  Per stage: 16 KB of weight rows by TMA (two boxes of 64 rows x 64 columns,
 // 128-byte swizzle, issued by lane 0 of warp 0) and the token rows' hi and lo (cp.async by warps 2-3, 16 each per
@@ -1213,6 +1239,26 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
     __shared__ bool is_last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = blockIdx.y, bx = blockIdx.x;
+    const int kbeg = blockIdx.z * a.k_split;
+    const int nk = min(a.k_split, a.K - kbeg) / kBK;
+    // weight rows of the tile's two 64-row boxes (row coordinates in the tensor map)
+    const int wg = weight_group(a, g);
+    const int wrow0 = wg * a.rows + (EPI == BEPI_SWIGLU ? bx * 64 : bx * kBRows);
+    const int wrow1 = wg * a.rows + (EPI == BEPI_SWIGLU ? a.I + bx * 64 : bx * kBRows + 64);
+    // a dense launch (no groups) knows its tokens and weights before the previous kernel ends: its setup and the
+    // weight tiles of the first S stages are issued before griddepcontrol.wait
+    const int pre = (!a.g_cnt && a.n > 0 && nk > 0) ? min(S, nk) : 0;
+    if (pre > 0) {
+        bgemm_ws_setup(&tmem_base, full, empty, &done, S, &wmap, tid, warp);
+        if (tid == 0) {
+            for (int kt = 0; kt < pre; ++kt) {
+                unsigned char* st = smem + (size_t)kt * STAGE;
+                mbar_expect_tx(&full[kt], kBRows * 128);
+                tma_load_2d(st, &wmap, kbeg + kt * kBK, wrow0, &full[kt]);
+                tma_load_2d(st + 64 * 128, &wmap, kbeg + kt * kBK, wrow1, &full[kt]);
+            }
+        }
+    }
     pdl_wait();
     pdl_launch();
     int p0 = 0, ntot = a.n;
@@ -1220,32 +1266,9 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
         p0 = __ldcg(a.g_off + g);
         ntot = __ldcg(a.g_cnt + g);
     }
-    const int kbeg = blockIdx.z * a.k_split;
-    const int nk = min(a.k_split, a.K - kbeg) / kBK;
     if (nk <= 0) ntot = 0;
     if (EPI != BEPI_RETURN && ntot <= 0) return;  // (a RETURN CTA still votes below)
-    // weight rows of the tile's two 64-row boxes (row coordinates in the tensor map)
-    const int wrow0 = (a.group0 + g) * a.rows + (EPI == BEPI_SWIGLU ? bx * 64 : bx * kBRows);
-    const int wrow1 = (a.group0 + g) * a.rows + (EPI == BEPI_SWIGLU ? a.I + bx * 64 : bx * kBRows + 64);
-    if (ntot > 0) {
-        if (warp == 0) {
-            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
-                         "r"(kTmemCols)
-                         : "memory");
-            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-        }
-        if (tid == 0) {
-            for (int i = 0; i < S; ++i) {
-                mbar_init(&full[i], 1 + 64);  // the TMA thread's expect_tx arrival + 64 cp.async arrivals
-                mbar_init(&empty[i], 1);      // one MMA commit
-            }
-            mbar_init(&done, 1);
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
-        }
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-    }
+    if (ntot > 0 && pre == 0) bgemm_ws_setup(&tmem_base, full, empty, &done, S, &wmap, tid, warp);
     const uint32_t tmem = tmem_base;
     bool ok = true;
     int it = 0;  // global stage counter over the CTA's tiles (stage it % S, round it / S)
@@ -1258,7 +1281,7 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
         if (warp == 0) {
             bool go = true;
             for (int kt = 0; kt < nk && go; ++kt) {
-                if (lane == 0) {
+                if (lane == 0 && it + kt >= pre) {
                     const int s = (it + kt) % S, r = (it + kt) / S;
                     if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, a.x.err, 7)) {
                         go = false;

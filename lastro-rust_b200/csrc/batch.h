@@ -60,6 +60,8 @@ struct BExchangeArgs {
     XLayout lay;
     int rank, world;
     int experts_per_rank;
+    const int* owner;             // [world * experts_per_rank] rank that computes each expert
+    const int* local;             // [same] the expert's index among its owner's experts (ascending expert ids)
     const unsigned int* epoch_base;  // flags carry epoch_base + layer + 1
     int layer;
     int* err;
@@ -86,7 +88,8 @@ enum BEpi { BEPI_STORE = 0, BEPI_SWIGLU = 1, BEPI_RETURN = 2 };
 struct BGemmArgs {
     const uint16_t* w;        // bf16 [groups][rows][K]
     long long group_stride;   // elements between groups
-    int group0;               // first group of this launch (expert parallelism: the rank's first expert)
+    int group0;               // first group of this launch (no group_expert)
+    const int* group_expert;  // optional [groups]: weight group of launch group g (null: group0 + g)
     int rows, K, k_split;     // k_split: K of one grid-z slice (multiple of kBK)
     const uint16_t* x_hi;     // activation rows, bf16 hi / lo, row stride ldx elements
     const uint16_t* x_lo;

@@ -23,7 +23,7 @@ using namespace lastro_capi;
 struct lastro_batch {
     lastro_model* m = nullptr;
     lastro_ctx* ctx = nullptr;
-    int max_seqs = 0, max_len = 0, max_pages = 0, rank = 0, world = 1, epr = 0, e0 = 0;
+    int max_seqs = 0, max_len = 0, max_pages = 0, rank = 0, world = 1, epr = 0;
     int ks_qkv = 1, ks_o = 1, R = 0;
     int attn_S = 1, attn_cap = 1;  // attention splits per (token, KV head) and positions one split stages
     int n_sm = 148;
@@ -51,6 +51,8 @@ struct lastro_batch {
     XLayout lay{};
     unsigned char* xreg = nullptr;
     unsigned char** d_peers = nullptr;
+    // expert placement: owner rank and index among the owner's experts of every expert, this rank's experts
+    int *d_owner = nullptr, *d_local = nullptr, *d_gexp = nullptr;
     std::vector<void*> opened;  // peer regions mapped from IPC handles
     std::map<int, cudaGraphExec_t> graphs;  // one per token count
     bool has_bias = false, want_hist = false;
@@ -87,6 +89,28 @@ const CUtensorMap* wmap(const lastro_batch* b, int layer, int which) {
     return i < b->wmaps.size() ? &b->wmaps[i] : nullptr;
 }
 
+struct Placement {
+    std::vector<int> owner, local, mine;
+};
+
+// local index of every expert among its owner's experts (ascending ids) and this rank's experts in that order, then
+// the tables to the device (asynchronously on the batch's stream: `pl` must live until the stream passes the copies)
+cudaError_t upload_placement(lastro_batch* b, Placement& pl) {
+    const int E = (int)pl.owner.size();
+    std::vector<int> seen(b->world, 0);
+    pl.local.assign(E, 0);
+    pl.mine.clear();
+    for (int x = 0; x < E; ++x) {
+        pl.local[x] = seen[pl.owner[x]]++;
+        if (pl.owner[x] == b->rank) pl.mine.push_back(x);
+    }
+    cudaStream_t s = b->ctx->stream;
+    cudaError_t e = cudaMemcpyAsync(b->d_owner, pl.owner.data(), sizeof(int) * E, cudaMemcpyHostToDevice, s);
+    if (!e) e = cudaMemcpyAsync(b->d_local, pl.local.data(), sizeof(int) * E, cudaMemcpyHostToDevice, s);
+    if (!e) e = cudaMemcpyAsync(b->d_gexp, pl.mine.data(), sizeof(int) * pl.mine.size(), cudaMemcpyHostToDevice, s);
+    return e;
+}
+
 // split-K slices for a dense GEMM of `rows` x K: at most two CTAs per SM, slices of at least 256 columns (4 stages; on
 // C5 slices of 128 measured the same kernel times with twice the partial-sum traffic)
 int pick_ks(int rows, int K, int n_sm) {
@@ -108,6 +132,8 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
     xa.rank = b->rank;
     xa.world = b->world;
     xa.experts_per_rank = b->epr;
+    xa.owner = b->d_owner;
+    xa.local = b->d_local;
     xa.epoch_base = b->epoch;
     xa.err = b->d_err;
     xa.n = n;
@@ -251,7 +277,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         BGemmArgs gu{};
         gu.w = reinterpret_cast<const uint16_t*>(L.gate_up);
         gu.group_stride = (long long)2 * I * H;
-        gu.group0 = b->e0;
+        gu.group_expert = b->d_gexp;
         gu.rows = 2 * I;
         gu.K = H;
         gu.k_split = H;
@@ -271,7 +297,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         BGemmArgs dn{};
         dn.w = reinterpret_cast<const uint16_t*>(L.down);
         dn.group_stride = (long long)H * I;
-        dn.group0 = b->e0;
+        dn.group_expert = b->d_gexp;
         dn.rows = H;
         dn.K = I;
         dn.k_split = I;
@@ -414,7 +440,6 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
     b->rank = rank;
     b->world = world;
     b->epr = d.experts / world;
-    b->e0 = rank * b->epr;
     b->R = m->qd + 2 * m->kvd;
     b->attn_S = attn_S;
     b->n_sm = n_sm;
@@ -446,7 +471,8 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
           A.alloc(&b->g_cnt, kMaxExperts) || A.alloc(&b->n_pos, 1) || A.alloc(&b->a_hi, pairs * I) ||
           A.alloc(&b->a_lo, pairs * I) || A.alloc(&b->logits, S * V) ||
           A.alloc(&b->route_hist, S * d.layers * k) || A.alloc(&b->counters, 64) || A.alloc(&b->epoch, 1) ||
-          A.alloc(&b->d_err, 1) || A.alloc(&b->xreg, b->lay.bytes) || A.alloc(&b->d_peers, (size_t)world);
+          A.alloc(&b->d_err, 1) || A.alloc(&b->xreg, b->lay.bytes) || A.alloc(&b->d_peers, (size_t)world) ||
+          A.alloc(&b->d_owner, E) || A.alloc(&b->d_local, E) || A.alloc(&b->d_gexp, (size_t)b->epr);
     if (!bad) bad = cudaMallocHost(&b->h_seq, sizeof(int) * S) != cudaSuccess;
     if (!bad) bad = cudaMallocHost(&b->h_tok, sizeof(int) * S) != cudaSuccess;
     if (!bad) bad = cudaMallocHost(&b->h_err, sizeof(int)) != cudaSuccess;
@@ -477,6 +503,9 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
         if (!e) e = cudaMemsetAsync(b->vpool[l], 0, kv_bytes, s);
     }
     if (!e) e = cudaMemsetAsync(b->route_hist, 0, sizeof(int) * S * d.layers * k, s);
+    Placement pl;  // contiguous: experts [r * E / world, (r + 1) * E / world) on rank r
+    for (int x = 0; x < (int)E; ++x) pl.owner.push_back(x / b->epr);
+    if (!e) e = upload_placement(b, pl);
     if (!e) e = cudaStreamSynchronize(s);
     if (e) {
         cudaGetLastError();
@@ -582,6 +611,30 @@ extern "C" int lastro_batch_set_router_bias(lastro_batch* b, const float* bias) 
         b->graphs.clear();
     }
     b->has_bias = bias != nullptr;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_batch_set_expert_placement(lastro_batch* b, const int32_t* owner, int32_t n_experts) {
+    if (!b) return LASTRO_E_ARG;
+    if (b->poisoned) return set_err(b->ctx, LASTRO_E_POISONED, "batch unusable after an earlier error");
+    const int E = b->m->d.experts;
+    if (!owner || n_experts != E)
+        return set_err(b->ctx, LASTRO_E_ARG, "placement of %d experts, the model has %d", n_experts, E);
+    std::vector<int> per(b->world, 0);
+    for (int x = 0; x < E; ++x) {
+        if (owner[x] < 0 || owner[x] >= b->world)
+            return set_err(b->ctx, LASTRO_E_ARG, "expert %d placed on rank %d of %d", x, owner[x], b->world);
+        ++per[owner[x]];
+    }
+    for (int r = 0; r < b->world; ++r)
+        if (per[r] != b->epr)
+            return set_err(b->ctx, LASTRO_E_ARG, "rank %d gets %d experts, every rank must get %d", r, per[r], b->epr);
+    cudaSetDevice(b->ctx->device);
+    Placement pl;
+    pl.owner.assign(owner, owner + E);
+    BTRY(cudaStreamSynchronize(b->ctx->stream), "placement");  // no step in flight reads the tables
+    BTRY(upload_placement(b, pl), "placement upload");
+    BTRY(cudaStreamSynchronize(b->ctx->stream), "placement upload");
     return LASTRO_OK;
 }
 

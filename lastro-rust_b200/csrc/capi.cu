@@ -538,6 +538,13 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         da.I = d.inter;
         da.k = d.k;
         da.E = d.experts;
+        if (l + 1 < d.layers) {  // L2 hint: the next layer's q/k/v and output-projection rows (C3: +1 %)
+            const LayerDev& N = m->L[l + 1];
+            da.pf[0] = N.wqkv;
+            da.pf_bytes[0] = (unsigned long long)(m->qd + 2 * m->kvd) * wrow_bytes(d.hidden, m->q8);
+            da.pf[1] = N.wo;
+            da.pf_bytes[1] = (unsigned long long)d.hidden * wrow_bytes(m->qd, m->q8);
+        }
         if ((e = launch_down(da, s, pdl)) != cudaSuccess) return e;
         if ((e = mark(pe, s, KK_DOWN)) != cudaSuccess) return e;
     }

@@ -126,6 +126,21 @@ LDEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
                  : "memory");
 }
 
+// hint: bring [src, src + bytes) into L2 (16-byte aligned address, size a multiple of 16); no completion to wait for
+LDEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// this CTA's share (of `ctas`, in 16-byte multiples) of an L2 prefetch of [base, base + bytes)
+LDEV void prefetch_share_l2(const void* base, unsigned long long bytes, int cta, int ctas) {
+    if (!base || bytes == 0) return;
+    const unsigned long long share = ((bytes + ctas - 1) / ctas + 15) & ~15ull;
+    const unsigned long long off = (unsigned long long)cta * share;
+    if (off >= bytes) return;
+    const unsigned long long n = min(share, bytes - off);
+    bulk_prefetch_l2(static_cast<const unsigned char*>(base) + off, (uint32_t)n);
+}
+
 LDEV bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
     uint32_t ok;
     asm volatile(

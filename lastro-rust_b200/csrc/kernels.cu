@@ -594,6 +594,9 @@ __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
             bulk_g2s(wd + (size_t)j * R * rbi, static_cast<const unsigned char*>(a.w) + ((size_t)e * a.H + r0) * rbi, bytes,
                      &bar);
         }
+        // the next layer's dense weights into L2 while this layer's MoE runs (qkv_rope then reads them from L2)
+        prefetch_share_l2(a.pf[0], a.pf_bytes[0], blockIdx.x, gridDim.x);
+        prefetch_share_l2(a.pf[1], a.pf_bytes[1], blockIdx.x, gridDim.x);
     }
     __syncthreads();  // the barrier is initialized before any thread waits on it
     float gw[kMaxTopK];

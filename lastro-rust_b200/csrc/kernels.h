@@ -134,6 +134,9 @@ struct DownArgs {
     int accumulate;
     int* err;
     int H, I, k, E;
+    // optional: byte ranges prefetched into L2 for the kernels that follow (the next layer's dense weights)
+    const void* pf[2];
+    unsigned long long pf_bytes[2];
 };
 
 struct HeadArgs {

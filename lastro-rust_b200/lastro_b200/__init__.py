@@ -79,6 +79,7 @@ EXPORTS = {
     "lastro_batch_exchange_handle": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32]),
     "lastro_batch_connect": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32]),
     "lastro_batch_set_router_bias": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "lastro_batch_set_expert_placement": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32]),
     "lastro_batch_step": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_void_p]),
     "lastro_batch_decode": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p]),
@@ -350,6 +351,11 @@ class GpuBatch:
         b = np.ascontiguousarray(bias, dtype=np.float32)
         assert b.shape == (self.cfg["layers"], self.cfg["experts"])
         self.ctx.check(lib().lastro_batch_set_router_bias(self.h, _p(b)))
+
+    def set_expert_placement(self, owner):
+        """owner[e]: the rank that computes expert e (E/world experts per rank; the same on every rank)."""
+        o = np.ascontiguousarray(owner, dtype=np.int32)
+        self.ctx.check(lib().lastro_batch_set_expert_placement(self.h, _p(o), o.size))
 
     def step(self, seq_ids, tokens, want_logits: bool = False, want_routes: bool = False):
         """(next [n], logits [n, V] or None, route ids [n, layers, k] or None) for one token of each sequence."""

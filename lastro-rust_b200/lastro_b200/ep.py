@@ -21,6 +21,45 @@ def experts(n_experts: int, rank: int, world: int) -> range:
     return shard(n_experts, rank, world)
 
 
+def contiguous_placement(n_experts: int, world: int) -> list:
+    """owner[e] with experts in contiguous blocks of n_experts / world (the batch's default placement)."""
+    if n_experts % world:
+        raise ValueError(f"{n_experts} experts do not split over {world} ranks")
+    return [e // (n_experts // world) for e in range(n_experts)]
+
+
+def interleaved_placement(n_experts: int, world: int) -> list:
+    """owner[e] = e mod world: neighbouring expert ids on different ranks."""
+    if n_experts % world:
+        raise ValueError(f"{n_experts} experts do not split over {world} ranks")
+    return [e % world for e in range(n_experts)]
+
+
+def balanced_placement(loads, world: int) -> list:
+    """owner[e] that evens out the ranks' summed `loads` (e.g. the pairs routed to each expert over earlier steps)
+    with n_experts / world experts per rank: experts in decreasing load (lower id first on ties), each to the rank
+    with the least load so far among those with room left (lower rank first on ties)."""
+    loads = [float(x) for x in loads]
+    n = len(loads)
+    if n % world:
+        raise ValueError(f"{n} experts do not split over {world} ranks")
+    per = n // world
+    owner = [0] * n
+    total = [0.0] * world
+    count = [0] * world
+    for e in sorted(range(n), key=lambda i: (-loads[i], i)):
+        r = min((q for q in range(world) if count[q] < per), key=lambda q: (total[q], q))
+        owner[e] = r
+        total[r] += loads[e]
+        count[r] += 1
+    return owner
+
+
+def owned(owner, rank: int) -> list:
+    """Experts of `rank` under the placement owner[e], ascending (the order of its grouped GEMMs)."""
+    return [e for e, r in enumerate(owner) if r == rank]
+
+
 def connect_group(batch, group=None):
     """All-gathers the exchange-region handle of every rank's batch, in rank order, and connects this rank's batch to
     all of them.  Every rank of the group must call it (it is a collective)."""

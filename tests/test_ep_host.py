@@ -24,6 +24,29 @@ def test_partitions_cover_everything_once():
         ep.experts(40, 0, 3)
 
 
+def test_expert_placements():
+    for world in (1, 2, 4, 8):
+        assert ep.contiguous_placement(40, world) == [e // (40 // world) for e in range(40)]
+        assert [ep.owned(ep.contiguous_placement(40, world), r) for r in range(world)] == \
+            [list(ep.experts(40, r, world)) for r in range(world)]
+        assert ep.interleaved_placement(40, world) == [e % world for e in range(40)]
+    with pytest.raises(ValueError):
+        ep.interleaved_placement(40, 3)
+    # balanced: E/world experts per rank, the heaviest loads spread, deterministic on ties
+    zipf = [(e + 1) ** -0.8 for e in range(40)]
+    for world in (2, 4, 8):
+        owner = ep.balanced_placement(zipf, world)
+        per = [ep.owned(owner, r) for r in range(world)]
+        assert sorted(sum(per, [])) == list(range(40)) and all(len(p) == 40 // world for p in per)
+        sums = [sum(zipf[e] for e in p) for p in per]
+        cont = [sum(zipf[e] for e in ep.owned(ep.contiguous_placement(40, world), r)) for r in range(world)]
+        assert max(sums) - min(sums) < 0.25 * (max(cont) - min(cont)) and max(sums) < max(cont)
+        assert owner[:world] == list(range(world))  # the world heaviest experts on distinct ranks, in rank order
+    assert ep.balanced_placement([1.0] * 8, 2) == [0, 1, 0, 1, 0, 1, 0, 1]
+    with pytest.raises(ValueError):
+        ep.balanced_placement([1.0] * 7, 2)
+
+
 class FakeBatch:
     """Stands in for GpuBatch: a handle that names the rank, and a record of what connect() received."""
 

@@ -141,6 +141,12 @@ def test_batch_refusals_leave_it_usable(gpu_ctx):
         b.step([0], [1])  # not connected
     assert e.value.code == LB.E_STATE
     b.connect()
+    E = cfg["experts"]
+    for owner in ([0] * (E - 1), [1] + [0] * (E - 1), [-1] * E):  # wrong count, ranks outside the group
+        with pytest.raises(LB.LastroError) as e:
+            b.set_expert_placement(owner)
+        assert e.value.code == LB.E_ARG
+    b.set_expert_placement([0] * E)
     for seqs, toks in (([0, 0], [1, 2]), ([3], [1]), ([0], [cfg["vocab"]]), ([], [])):
         with pytest.raises(LB.LastroError) as e:
             b.step(seqs, toks)

@@ -16,7 +16,20 @@ pytestmark = pytest.mark.gpu
 NSEQ, STEPS, MAX_LEN = 8, 5, 32
 
 
-def _run(rank, world, port, out_dir):
+def _placement(kind, n_experts, world):
+    from lastro_b200 import ep
+
+    if kind == "contiguous":
+        return ep.contiguous_placement(n_experts, world)
+    if kind == "interleaved":
+        return ep.interleaved_placement(n_experts, world)
+    # balanced over a Zipf-like load, then experts shuffled between ranks' slots: an arbitrary placement
+    owner = ep.balanced_placement([(e + 1) ** -0.8 for e in range(n_experts)], world)
+    rng = np.random.default_rng(5)
+    return [int(x) for x in rng.permutation(owner)]
+
+
+def _run(rank, world, port, out_dir, kind="contiguous"):
     import torch
     import torch.distributed as dist
 
@@ -37,6 +50,8 @@ def _run(rank, world, port, out_dir):
     mine = list(ep.sequences(NSEQ, rank, world))
     b = LB.GpuBatch(m, len(mine), MAX_LEN, rank, world)
     ep.connect_group(b)
+    if kind != "contiguous":
+        b.set_expert_placement(_placement(kind, cfg["experts"], world))
     b.set_router_bias(CFG.zipf_router_bias(cfg))
     prompts = {g: S.tokens(STEPS, 700 + g, cfg["vocab"]) for g in mine}
     res = {"next": [], "logits": [], "routes": []}
@@ -66,8 +81,10 @@ def _gather(out_dir, world):
     return cat
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_expert_parallel_equals_single_gpu_bitwise(world, tmp_path):
+@pytest.mark.parametrize("world,kind", [(2, "contiguous"), (2, "interleaved"), (2, "shuffled"), (4, "contiguous"),
+                                        (4, "shuffled"), (8, "contiguous"), (8, "shuffled")])
+def test_expert_parallel_equals_single_gpu_bitwise(world, kind, tmp_path):
+    """Every placement of the experts over the ranks gives the single-GPU results bitwise."""
     import torch
     import torch.multiprocessing as mp
 
@@ -78,7 +95,7 @@ def test_expert_parallel_equals_single_gpu_bitwise(world, tmp_path):
         sk.bind(("127.0.0.1", 0))
         port = sk.getsockname()[1]
     for w in (1, world):
-        procs = [mpc.Process(target=_run, args=(r, w, port, str(tmp_path))) for r in range(w)]
+        procs = [mpc.Process(target=_run, args=(r, w, port, str(tmp_path), kind)) for r in range(w)]
         for p in procs:
             p.start()
         for p in procs:
