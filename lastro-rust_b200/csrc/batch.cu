@@ -57,11 +57,27 @@ LDEV unsigned int ld_acquire_sys(const unsigned int* p) {
 LDEV void st_release_sys(unsigned int* p, unsigned int v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+LDEV unsigned int ld_acquire_gpu(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+LDEV void st_release_gpu(unsigned int* p, unsigned int v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// the exchange's flags: system scope when the group spans GPUs, GPU scope for a group of one
+LDEV unsigned int ld_acquire_x(const unsigned int* p, bool sys) { return sys ? ld_acquire_sys(p) : ld_acquire_gpu(p); }
+LDEV void st_release_x(unsigned int* p, unsigned int v, bool sys) {
+    if (sys)
+        st_release_sys(p, v);
+    else
+        st_release_gpu(p, v);
+}
 // Waits until *flag reaches `want` (epochs only grow), at most kFlagWaitNs; on time-out records `code` and fails.
 constexpr uint64_t kFlagWaitNs = 10ull * 1000 * 1000 * 1000;
-LDEV bool wait_flag(const unsigned int* flag, unsigned int want, int* err, int code) {
+LDEV bool wait_flag(const unsigned int* flag, unsigned int want, int* err, int code, bool sys) {
     const uint64_t t0 = global_ns();
-    while ((int)(ld_acquire_sys(flag) - want) < 0) {
+    while ((int)(ld_acquire_x(flag, sys) - want) < 0) {
         if (global_ns() - t0 > kFlagWaitNs) {
             atomicExch(err, code);
             return false;
@@ -74,8 +90,8 @@ LDEV bool wait_flag(const unsigned int* flag, unsigned int want, int* err, int c
 // Last-CTA election across a grid whose CTAs wrote to other GPUs.  Each CTA orders its writes before its arrival with
 // a GPU-scope fence; the last CTA, which has observed every arrival, then issues one system-scope fence before it
 // publishes the flag with a system-scope release store: every CTA's peer writes precede the flag in causality order,
-// without a system-scope fence in each of the grid's CTAs.
-LDEV bool last_block_arrives_sys(unsigned int* counter, unsigned int total, bool* flag_smem) {
+// without a system-scope fence in each of the grid's CTAs.  A group of one GPU (sys false) stays at GPU scope.
+LDEV bool last_block_arrives_sys(unsigned int* counter, unsigned int total, bool* flag_smem, bool sys) {
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -86,7 +102,7 @@ LDEV bool last_block_arrives_sys(unsigned int* counter, unsigned int total, bool
     }
     __syncthreads();
     const bool last = *flag_smem;
-    if (last) __threadfence_system();
+    if (last && sys) __threadfence_system();
     return last;
 }
 
@@ -301,10 +317,10 @@ __global__ void __launch_bounds__(128) bgemm_kernel(BGemmArgs a) {
         }
     }
     if (EPI == BEPI_RETURN) {
-        if (!last_block_arrives_sys(a.x.counter, gridDim.x * gridDim.y * gridDim.z, &is_last)) return;
+        if (!last_block_arrives_sys(a.x.counter, gridDim.x * gridDim.y * gridDim.z, &is_last, a.x.world > 1)) return;
         if (tid < a.x.world) {
             const unsigned int epoch = __ldcg(a.x.epoch_base) + a.x.layer + 1;
-            st_release_sys(flag_ptr(a.x.peers[tid], a.x.lay, 1, a.x.rank), epoch);
+            st_release_x(flag_ptr(a.x.peers[tid], a.x.lay, 1, a.x.rank), epoch, a.x.world > 1);
         }
     }
 }
@@ -631,8 +647,9 @@ LDEV void group_pairs(const BExchangeArgs& a) {
     if (threadIdx.x < kMaxExperts) cnt[threadIdx.x] = 0;
     __syncthreads();
     if (threadIdx.x < a.world) {
-        if (wait_flag(flag_ptr(me, L, 0, threadIdx.x), epoch, a.err, 10 + threadIdx.x))
-            pairs[threadIdx.x] = (int)ld_acquire_sys(reinterpret_cast<const unsigned int*>(me + L.rx_n) + threadIdx.x) * a.k;
+        if (wait_flag(flag_ptr(me, L, 0, threadIdx.x), epoch, a.err, 10 + threadIdx.x, a.world > 1))
+            pairs[threadIdx.x] =
+                (int)ld_acquire_x(reinterpret_cast<const unsigned int*>(me + L.rx_n) + threadIdx.x, a.world > 1) * a.k;
         else
             atomicExch(&ok_all, 0);
     }
@@ -815,10 +832,10 @@ __global__ void __launch_bounds__(256) brouter_kernel(BRouterArgs a) {
         reinterpret_cast<int*>(x.peers[q] + L.rx_ids)[(size_t)x.rank * L.cap + (size_t)t * a.k + j] = sid[j];
     }
     if (t == 0 && threadIdx.x < x.world) reinterpret_cast<int*>(x.peers[threadIdx.x] + L.rx_n)[x.rank] = a.n;
-    if (!last_block_arrives_sys(x.counter, gridDim.x, &is_last)) return;
+    if (!last_block_arrives_sys(x.counter, gridDim.x, &is_last, x.world > 1)) return;
     if (threadIdx.x < x.world) {
         const unsigned int epoch = __ldcg(x.epoch_base) + x.layer + 1;
-        st_release_sys(flag_ptr(x.peers[threadIdx.x], L, 0, x.rank), epoch);
+        st_release_x(flag_ptr(x.peers[threadIdx.x], L, 0, x.rank), epoch, x.world > 1);
     }
     // the same CTA then waits for every rank's dispatch and groups the pairs this rank's experts received
     __syncthreads();
@@ -841,7 +858,8 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(BExchangeArgs a) {
     const unsigned int epoch = __ldcg(a.epoch_base) + a.layer + 1;
     if (threadIdx.x == 0) ok_all = 1;
     __syncthreads();
-    if (threadIdx.x < a.world && !wait_flag(flag_ptr(me, L, 1, threadIdx.x), epoch, a.err, 30 + threadIdx.x))
+    if (threadIdx.x < a.world &&
+        !wait_flag(flag_ptr(me, L, 1, threadIdx.x), epoch, a.err, 30 + threadIdx.x, a.world > 1))
         atomicExch(&ok_all, 0);
     __syncthreads();
     if (!ok_all) return;
@@ -1169,10 +1187,10 @@ __global__ void __launch_bounds__(128) bgemm_tc_kernel(BGemmArgs a) {
             asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
     }
     if (EPI == BEPI_RETURN) {
-        if (!last_block_arrives_sys(a.x.counter, gridDim.x * gridDim.y * gridDim.z, &is_last)) return;
+        if (!last_block_arrives_sys(a.x.counter, gridDim.x * gridDim.y * gridDim.z, &is_last, a.x.world > 1)) return;
         if (tid < a.x.world) {
             const unsigned int epoch = __ldcg(a.x.epoch_base) + a.x.layer + 1;
-            st_release_sys(flag_ptr(a.x.peers[tid], a.x.lay, 1, a.x.rank), epoch);
+            st_release_x(flag_ptr(a.x.peers[tid], a.x.lay, 1, a.x.rank), epoch, a.x.world > 1);
         }
     }
 }
@@ -1414,10 +1432,10 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
             asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
     }
     if (EPI == BEPI_RETURN) {
-        if (!last_block_arrives_sys(a.x.counter, gridDim.x * gridDim.y * gridDim.z, &is_last)) return;
+        if (!last_block_arrives_sys(a.x.counter, gridDim.x * gridDim.y * gridDim.z, &is_last, a.x.world > 1)) return;
         if (tid < a.x.world) {
             const unsigned int epoch = __ldcg(a.x.epoch_base) + a.x.layer + 1;
-            st_release_sys(flag_ptr(a.x.peers[tid], a.x.lay, 1, a.x.rank), epoch);
+            st_release_x(flag_ptr(a.x.peers[tid], a.x.lay, 1, a.x.rank), epoch, a.x.world > 1);
         }
     }
 }
