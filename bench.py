@@ -514,8 +514,8 @@ def main():
     achieved = kb[dominant] / (per_launch_ms / 1000.0) / 1e9
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tp):
-        traffic = json.load(open(tp)).get(dominant)
+    if os.path.exists(tp):  # per workload: c3 bf16, c4 Q8_0 (half the weight bytes)
+        traffic = json.load(open(tp)).get(a.workload, {}).get(dominant)
     # the router GEMV runs inside the oproj kernel; the MoE block's streamed bytes are the experts'
     moe_bytes = kb["gate_up"] + kb["down"]
     moe_ms = (prof["gate_up"] + prof["down"]) / L
