@@ -7,13 +7,17 @@ by decoding 2048 uniform random ids (seed 2) through the model itself, then gree
 decoded token.  --workload c4: the same architecture with every linear weight Q8_0 (int8 ~U[-127,127] and one fp16
 scale ~U(1e-4, 4e-3) per 32 values; embedding bf16), seeds 4, context 512.
 
+Under torchrun (WORLD_SIZE set) the default workload is c5 at every world size: 64 sequences in total (strong
+scaling), experts partitioned over the ranks; a plain `python bench.py` runs c3.
+
   value  device-resident throughput: K graph-replayed decode steps, the token fed back on the device, timed with
          CUDA events on the library's stream (max over ranks; every rank decodes its own replica: batch-1 decode
          does not shard, so N GPUs run N independent replicas = weak scaling)
   e2e    the same decode through the public C-ABI step call a user makes (lastro_model_step): the token goes
          host->device and the next token device->host every step, inside the timed region
-  roofline  the dominant kernel (by device time) of the step: algorithmic bytes per launch / its mean duration,
-         measured live with events around direct launches (lastro_model_profile).  --fused runs the step as one
+  roofline  the dominant kernel of the step (by its share of the step's critical path in the replayed graph):
+         algorithmic bytes per launch / its in-graph duration (first CTA start to last CTA exit, every CTA stamping
+         %globaltimer in a graph captured like the product's, lastro_model_trace).  --fused runs the step as one
          persistent kernel instead of the per-layer chain; its roofline is then the whole step's bytes / its duration
   cpu_baseline  the CPU oracle (a C restatement of the reference's CPU path, rust/moe-rt/src/{cpu,model}.rs)
          decoding the same model at the same context on this host's cores
@@ -52,9 +56,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", choices=("lastro", "reference"), default="lastro")
-    ap.add_argument("--workload", choices=tuple(WORKLOADS), default="c3",
-                    help="c3: bf16 weights, ctx 2048 (the headline); c4: Q8_0 weights, ctx 512; c5: 64 sequences x "
-                         "ctx 1024, Zipf expert load, experts partitioned over the torchrun ranks")
+    ap.add_argument("--workload", choices=tuple(WORKLOADS), default=None,
+                    help="c3: bf16 weights, ctx 2048 (the headline; the default of a plain `python bench.py`); c4: "
+                         "Q8_0 weights, ctx 512; c5: 64 sequences x ctx 1024, Zipf expert load, experts partitioned "
+                         "over the torchrun ranks (the default under torchrun, at every world size including 1)")
     ap.add_argument("--context", type=int, default=None, help="context length (default: the workload's)")
     ap.add_argument("--kv", choices=("bf16", "f32"), default="bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -72,9 +77,24 @@ def parse():
     ap.add_argument("--fused", action="store_true", help="the fused step kernel (one persistent launch per step) instead "
                     "of the per-layer kernel chain")
     a = ap.parse_args()
+    if a.workload is None:
+        # under torchrun the driver measures scaling: the expert-parallel batched decode (strong scaling, 64 sequences
+        # in total at every N); a single process measures the batch-1 headline
+        a.workload = "c5" if under_torchrun() else "c3"
     if a.context is None:
         a.context = WORKLOADS[a.workload]["context"]
     return a
+
+
+def under_torchrun():
+    return "WORLD_SIZE" in os.environ or "TORCHELASTIC_RUN_ID" in os.environ
+
+
+def workload_config(a):
+    """The `config` object, identical in both arms for the same workload (the run's own measurements go elsewhere)."""
+    c = WORKLOADS[a.workload]
+    return {"workload": c["name"], "batch": c.get("batch", 1), "context": a.context, "kv_cache": f"paged {a.kv}",
+            "weights": c["model"].get("weight_dtype", "bf16")}
 
 
 def peaks():
@@ -193,9 +213,9 @@ def run_reference(a):
     line = {
         "impl": "reference", "metric": metric_name(c, a.context) if a.workload != "c5" else BATCH_METRIC, "value": rate,
         "unit": "tok/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1000.0 / rate,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if a.workload == "c5" else "weak", "vs_baseline": None,
         "dtype": cfg.get("weight_dtype", "bf16"), "data": "synthetic",
-        "config": {"workload": c["name"], "context": a.context, "batch": c.get("batch", 1)},
+        "config": workload_config(a),
         "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference (Rust + cuTile, rust/moe-rt) cannot be built here; its CPU path is timed through the "
@@ -371,17 +391,17 @@ def run_batched(a):
         "metric": BATCH_METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": c["name"], "batch": total, "seqs_per_rank": n, "context_start": ctx0,
-                   "mean_context": mean_ctx, "kv_cache": f"paged {a.kv}",
-                   "parallelism": f"ep{world}: experts {E // world}/rank ({a.placement} placement), attention "
-                   "data-parallel over sequences" if world > 1 else "single GPU",
-                   "weights": "bf16; batched GEMMs on tensor cores (" + ("mma.sync", "tcgen05, cp.async stages",
-                              "tcgen05 warp-specialised, TMA weight tiles")[a.gemm] + ", accumulators f32, bf16 operands, "
-                              "activations split hi + lo)",
-                   "expert_load_share_by_rank": [round(x, 4) for x in share], "experts_touched": touched,
-                   "router_bias": "Zipf(0.8), beta 0.8", "prefill": "synthetic KV" if a.synthetic_kv else
-                   "teacher-forced batched steps", "prefill_s": round(prefill_s, 2),
-                   "l2": f"inputs larger than L2: every step streams ~{step_bytes / 1e9:.1f} GB (L2 126 MB)"},
+        "config": workload_config(a),
+        "run": {"seqs_per_rank": n, "context_start": ctx0, "mean_context": mean_ctx,
+                "parallelism": f"ep{world}: experts {E // world}/rank ({a.placement} placement), attention "
+                "data-parallel over sequences" if world > 1 else "single GPU",
+                "weights": "bf16; batched GEMMs on tensor cores (" + ("mma.sync", "tcgen05, cp.async stages",
+                           "tcgen05 warp-specialised, TMA weight tiles")[a.gemm] + ", accumulators f32, bf16 operands, "
+                           "activations split hi + lo)",
+                "expert_load_share_by_rank": [round(x, 4) for x in share], "experts_touched": touched,
+                "router_bias": "Zipf(0.8), beta 0.8", "prefill": "synthetic KV" if a.synthetic_kv else
+                "teacher-forced batched steps", "prefill_s": round(prefill_s, 2),
+                "l2": f"inputs larger than L2: every step streams ~{step_bytes / 1e9:.1f} GB (L2 126 MB)"},
         "roofline": {"bound": "hbm", "kernel": "batched step (all kernels)", "achieved": achieved, "peak": hbm,
                      "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": None,
                      "bytes_per_step": step_bytes, "bytes_note": "touched experts + KV of all sequences + the dense "
@@ -501,50 +521,67 @@ def main():
         e2e_ms = float(t.item())
     e2e = {"value": world * K / (e2e_ms / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4}
 
-    # ---- per-kernel device time (direct launches, events between kernels) --------------------------------------
-    prof = model.profile(4)
+    # ---- per-kernel device time -------------------------------------------------------------------------------
+    # in the replayed graph (the step's own regime): every CTA stamps the global timer; exposed = each kind's share of
+    # the step's critical path, span = first CTA start to last CTA exit of each launch
     L = cfg["layers"]
+    launches = {k: (1 if k in ("head", "fused_step") else L) for k in KERNELS}
+    fused = model.fused
+    tr = None if fused else model.trace(4)
+    # direct launches with an event between kernels (no PDL overlap): the serialised per-kernel figure
+    prof = model.profile(4)
     prof_ctx = model.pos - 2
     kb = kernel_bytes(cfg, prof_ctx)
-    launches = {k: (1 if k in ("head", "fused_step") else L) for k in KERNELS}
-    dominant = max(KERNELS, key=lambda k: prof[k])
-    fused = model.fused
-    per_launch_ms = prof[dominant] / launches[dominant]
     hbm, peak_kind = peaks()
-    achieved = kb[dominant] / (per_launch_ms / 1000.0) / 1e9
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if fused:
+        dominant = "fused_step"
+        per_launch_ms = prof[dominant]
+        regime = "direct launch, CUDA events"
+    else:
+        dominant = max(("qkv_rope", "attention", "oproj", "gate_up", "down", "head"), key=lambda k: tr["exposed"][k])
+        per_launch_ms = tr["span"][dominant] / launches[dominant]
+        regime = "in graph: first CTA start to last CTA exit, %globaltimer, mean over launches and 4 steps"
+    achieved = kb[dominant] / (per_launch_ms / 1000.0) / 1e9
     if os.path.exists(tp):  # per workload: c3 bf16, c4 Q8_0 (half the weight bytes)
         traffic = json.load(open(tp)).get(a.workload, {}).get(dominant)
     # the router GEMV runs inside the oproj kernel; the MoE block's streamed bytes are the experts'
     moe_bytes = kb["gate_up"] + kb["down"]
-    moe_ms = (prof["gate_up"] + prof["down"]) / L
+    moe_ms = ((tr["exposed"]["gate_up"] + tr["exposed"]["down"]) if tr else (prof["gate_up"] + prof["down"])) / L
     B = CFG.bytes_per_token(cfg, mean_ctx)
     step_s = ms / 1000.0 / K
     line = {
         "metric": metric_name(c, a.context), "value": value, "unit": "tok/s",
         "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "q8_0" if q8 else "bf16", "data": "synthetic",
-        "config": {"workload": c["name"], "batch": 1, "context_start": ctx0, "mean_context": mean_ctx,
-                   "kv_cache": f"paged {a.kv}",
-                   "weights": ("Q8_0 linears (int8 + fp16 scale per 32, dequantised in registers), bf16 embedding"
-                               if q8 else "bf16") + ", activations/accumulators f32",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "step_kernel": "fused: one persistent cooperative launch per step" if fused else
-                   "chain: 5 kernels per layer + head, PDL, CUDA graph",
-                   "l2": f"inputs larger than L2: every step streams ~{B['full'] / 1e9:.1f} GB of weights and KV "
-                         "(L2 126 MB)",
-                   "prefill_s": round(prefill_s, 2)},
+        "config": workload_config(a),
+        "run": {"context_start": ctx0, "mean_context": mean_ctx,
+                "weights": ("Q8_0 linears (int8 + fp16 scale per 32, dequantised in registers), bf16 embedding"
+                            if q8 else "bf16") + ", activations/accumulators f32",
+                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "step_kernel": "fused: one persistent cooperative launch per step" if fused else
+                "chain: 5 kernels per layer + head, PDL, CUDA graph",
+                "l2": f"inputs larger than L2: every step streams ~{B['full'] / 1e9:.1f} GB of weights and KV "
+                      "(L2 126 MB)",
+                "prefill": "synthetic KV" if a.synthetic_kv else "the prompt decoded through the model",
+                "prefill_s": round(prefill_s, 2)},
         "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": traffic,
-                     "bytes_per_launch": kb[dominant], "ms_per_launch": per_launch_ms},
+                     "bytes_per_launch": kb[dominant], "ms_per_launch": per_launch_ms, "timing": regime},
         "step_roofline": {"literal_bytes": B["literal"], "full_bytes": B["full"],
                           "literal_frac": B["literal"] / step_s / 1e9 / hbm,
                           "full_frac": B["full"] / step_s / 1e9 / hbm,
                           "literal_frac_vs_8tbs": B["literal"] / step_s / 1e9 / 8000.0},
         "moe_block": None if fused else {"gbs": moe_bytes / (moe_ms / 1000.0) / 1e9,
-                                         "frac": moe_bytes / (moe_ms / 1000.0) / 1e9 / hbm, "us_per_layer": moe_ms * 1000.0},
+                                         "frac": moe_bytes / (moe_ms / 1000.0) / 1e9 / hbm, "us_per_layer": moe_ms * 1000.0,
+                                         "timing": "gate_up + down exposed time in the graph"},
         "kernels_ms_per_step": {k: round(v, 4) for k, v in prof.items()},
+        "in_graph_ms_per_step": None if fused else {
+            "exposed": {k: round(v, 4) for k, v in tr["exposed"].items() if k not in ("router", "fused_step")},
+            "span": {k: round(v, 4) for k, v in tr["span"].items() if k not in ("router", "fused_step")},
+            "handoff": {k: round(v, 4) for k, v in tr["wait"].items() if k not in ("router", "fused_step")},
+            "step": round(tr["step_ms"], 4)},
         "e2e": e2e,
         "gpu_launches": K * (1 if fused else 5 * L + 1),
         "clocks": clk,

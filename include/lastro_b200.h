@@ -91,11 +91,18 @@ void lastro_layer_destroy(lastro_layer *layer);
  * address up (cudaGetSymbolAddress), so make that first call before any stream capture.  Every call shares the
  * array: calls that overlap on the GPU (other streams, other threads) race; serialise them.  The call clears the
  * array's ticket and error word itself; nothing else in it needs to start at zero.  Returns LASTRO_E_ARG or
- * LASTRO_E_UNSUPPORTED for shapes beyond the limits, before any launch; it does not report the kernels' bounded
- * copy-wait status (the error word stays in the scratch). */
+ * LASTRO_E_UNSUPPORTED for shapes beyond the limits, before any launch.  The kernels' bounded copy waits report
+ * through the scratch's error word: read it with lastro_moe_block_noalloc_status.  The cached scratch address is keyed
+ * by device and CUDA context, so a device reset only costs the next call a fresh look-up (again outside a capture). */
 int lastro_moe_block_forward_noalloc(const float *x, const uint16_t *router, const uint16_t *gate_up,
                                      const uint16_t *down, int32_t experts, int32_t hidden, int32_t inter, int32_t k,
                                      float *y, int32_t *ids, float *weights, void *stream);
+/* Status of the allocation-free block calls on the current device, no counterpart in the reference: enqueues on
+ * `stream` a 4-byte copy of the scratch's error word into *status (host or device memory the caller owns; pinned
+ * host memory keeps the copy asynchronous), allocating nothing.  After the stream reaches it: 0 when every bounded
+ * copy wait of the last call completed, else the code of the wait that gave up (y, ids and weights of that call are
+ * then not valid).  Make the first call of either entry point before any stream capture. */
+int lastro_moe_block_noalloc_status(int32_t *status, void *stream);
 
 /* ---- whole model: GpuModel (gpu_model.rs:154-455) --------------------------------------------------------------- */
 /* GpuModel::upload (gpu_model.rs:191-242): allocates weights, the paged KV cache for max_len positions and the
@@ -107,9 +114,14 @@ int lastro_model_load_tensor(lastro_model *model, const char *name, int32_t dtyp
                              int32_t ndim, const void *host);
 /* random-init every tensor on the device from the synthetic generator (weights ~ std, norms 1 + norm_std) */
 int lastro_model_fill_synthetic(lastro_model *model, uint64_t seed, float stddev, float norm_stddev);
-/* benchmark/test helper, no reference counterpart: fill every K/V page with synthetic values and set the position
- * to n, a context of n positions without running n steps */
+/* benchmark/test helper, no reference counterpart: a context of n positions without running n steps.  Every layer's
+ * K/V rows of positions [0, n) get synthetic values, element for element the CPU oracle's lo_session_fill_kv (logical
+ * element pos * kv_heads * head_dim + head * head_dim + j of layer l's K stream seeded mix64(seed + 2l), of its V
+ * stream mix64(seed + 2l + 1); rounded to bf16 in a bf16 cache); the position becomes n */
 int lastro_model_fill_kv_synthetic(lastro_model *model, int32_t n, uint64_t seed, float stddev);
+/* test helper, no reference counterpart: K and V rows of positions [pos0, pos0 + n) (< the current position) of one
+ * layer as f32 [n, kv_heads * head_dim] (bf16 caches widened exactly); either output may be NULL */
+int lastro_model_read_kv(lastro_model *model, int32_t layer, int32_t pos0, int32_t n, float *k_out, float *v_out);
 /* GpuModel::step (gpu_model.rs:251-267): one token; logits [V] (already / logits_scaling), the greedy next token
  * (argmax, last maximum on ties), routes ids/weights [layers*k]; every output may be NULL */
 int lastro_model_step(lastro_model *model, int32_t token, float *logits, int32_t *next_token, int32_t *route_ids,
@@ -118,6 +130,14 @@ int lastro_model_step(lastro_model *model, int32_t token, float *logits, int32_t
  * tokens, each step's argmax fed back without a host round trip; out_ids [n_new] may be NULL */
 int lastro_model_generate(lastro_model *model, const int32_t *prompt, int32_t n_prompt, int32_t n_new,
                           int32_t *out_ids);
+/* the greedy loop of geracao_regra.rs:181-245 in normal use: feeds prompt[0..n_prompt), then generates up to n_new
+ * tokens, each fed back on the device, stopping after the first `eos` (Granite's <|end_of_text|> is id 0,
+ * geracao_regra.rs:31; eos < 0 never stops, which is lastro_model_generate).  out_ids [n_new] receives the generated
+ * ids, the end-of-text token included; *n_out their count.  The model ends where the reference's loop leaves it: the
+ * prompt and every generated token but the last have been fed (the steps run in chunks of 16 with one host read each,
+ * and the position is rolled back over any step run past the end of text). */
+int lastro_model_generate_until(lastro_model *model, const int32_t *prompt, int32_t n_prompt, int32_t n_new,
+                                int32_t eos, int32_t *out_ids, int32_t *n_out);
 /* device-resident greedy decode of n tokens continuing from the last token (no host copies; for timing) */
 int lastro_model_decode(lastro_model *model, int32_t n);
 /* GpuModel::reset (gpu_model.rs:244-247): position 0, page table reset */
@@ -129,6 +149,15 @@ int lastro_model_position(const lastro_model *model, int32_t *pos);
  * position like lastro_model_decode.  No reference counterpart: measurement only (the reference's step_probe,
  * gpu_model.rs:275-300, times whole steps). */
 int lastro_model_profile(lastro_model *model, int32_t steps, float *kernel_ms, int32_t n_kinds);
+/* in-graph timeline of `steps` decode steps: the step graph captured again with every CTA stamping the global timer
+ * (start, release from griddepcontrol.wait, exit) and replayed like lastro_model_decode.  Per kernel kind (the kinds of
+ * lastro_model_profile), summed over layers and averaged over steps: exposed_ms = the kind's share of the step's
+ * critical path (each launch's last exit minus the previous launch's, so the kinds sum to the step), span_ms = last
+ * exit minus first CTA start (includes the time resident under the predecessor), wait_ms = first release from
+ * griddepcontrol.wait minus the previous launch's last exit (the hand-off latency); step_ms = first start to last exit.  Launches without stamps (tensor-core attention) count 0.  Advances the
+ * position like lastro_model_decode.  No reference counterpart: measurement only. */
+int lastro_model_trace(lastro_model *model, int32_t steps, float *exposed_ms, float *span_ms, float *wait_ms,
+                       int32_t n_kinds, float *step_ms);
 /* tuning: use CUDA graphs (default 1), programmatic dependent launch between the per-layer kernels (default 1),
  * and the fused step -- the whole step as one persistent cooperative launch, one CTA per SM -- where the model's
  * shapes fit it (default 0: on B200 it measures slower than the per-layer kernels; lastro_model_fused reports
@@ -150,7 +179,7 @@ void lastro_model_destroy(lastro_model *model);
  * of its exchange region (lastro_batch_exchange_handle, 64 bytes) to the others, and connects with all of them in rank
  * order (lastro_batch_connect; world 1: handles may be NULL).  The ranks then call lastro_batch_step/decode the same
  * number of times, each with at least one of its own sequences.  Destroy a batch before its model.  A rank that does
- * not arrive makes the others' waits give up after 10 s (LASTRO_E_CUDA, batch poisoned). */
+ * not arrive makes the others' waits give up after 10 s (LASTRO_E_CUDA, batch poisoned; lastro_batch_set_wait_limit). */
 typedef struct lastro_batch lastro_batch;
 int lastro_batch_create(lastro_model *model, int32_t max_seqs, int32_t max_len, int32_t rank, int32_t world,
                         lastro_batch **out);
@@ -186,6 +215,10 @@ int lastro_batch_profile(lastro_batch *batch, int32_t n, const int32_t *seq_ids,
  * loading the stages (1), or on mma.sync with register accumulators (0); attn_tc: attention on tensor cores with TMA
  * page loads (1, the default with bf16 KV) or on CUDA cores (0, the only choice with f32 KV) */
 int lastro_batch_set_options(lastro_batch *batch, int32_t use_graphs, int32_t use_tcgen05, int32_t attn_tc);
+/* bound of every wait on another rank's exchange flag (default 10 s; 1 ms to 600 s): a rank that does not arrive
+ * within it makes the step return LASTRO_E_CUDA and poisons the batch; later waits of the same step give up at once
+ * (gpu_model.rs:249-267's poison policy; no reference counterpart for the limit itself) */
+int lastro_batch_set_wait_limit(lastro_batch *batch, uint64_t wait_ns);
 void lastro_batch_destroy(lastro_batch *batch);
 
 #ifdef __cplusplus

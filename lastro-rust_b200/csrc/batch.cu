@@ -43,12 +43,7 @@ LDEV void split_bf16(float v, uint16_t& hi, uint16_t& lo) {
     lo = f32_to_bf16_rne(__fsub_rn(v, __uint_as_float((uint32_t)hi << 16)));
 }
 
-// ---- bounded waits on flags written by other GPUs ---------------------------------------------------------------
-LDEV uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
+// ---- bounded waits on flags written by other GPUs (global_ns: common.cuh) -----------------------------------------
 LDEV unsigned int ld_acquire_sys(const unsigned int* p) {
     unsigned int v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -73,13 +68,15 @@ LDEV void st_release_x(unsigned int* p, unsigned int v, bool sys) {
     else
         st_release_gpu(p, v);
 }
-// Waits until *flag reaches `want` (epochs only grow), at most kFlagWaitNs; on time-out records `code` and fails.
-constexpr uint64_t kFlagWaitNs = 10ull * 1000 * 1000 * 1000;
-LDEV bool wait_flag(const unsigned int* flag, unsigned int want, int* err, int code, bool sys) {
+// Waits until *flag reaches `want` (epochs only grow), at most `limit_ns`; on time-out records `code` in the error word
+// and fails.  A wait that finds the error word already set (an earlier wait of this step gave up) fails at once, so a
+// dead peer costs one limit per step, not one per layer.
+LDEV bool wait_flag(const unsigned int* flag, unsigned int want, int* err, int code, bool sys, uint64_t limit_ns) {
     const uint64_t t0 = global_ns();
-    while ((int)(ld_acquire_x(flag, sys) - want) < 0) {
-        if (global_ns() - t0 > kFlagWaitNs) {
-            atomicExch(err, code);
+    for (uint32_t i = 0; (int)(ld_acquire_x(flag, sys) - want) < 0; ++i) {
+        if ((i & 63) == 0 && *reinterpret_cast<volatile int*>(err)) return false;
+        if (global_ns() - t0 > limit_ns) {
+            atomicCAS(err, 0, code);
             return false;
         }
         __nanosleep(64);
@@ -647,7 +644,7 @@ LDEV void group_pairs(const BExchangeArgs& a) {
     if (threadIdx.x < kMaxExperts) cnt[threadIdx.x] = 0;
     __syncthreads();
     if (threadIdx.x < a.world) {
-        if (wait_flag(flag_ptr(me, L, 0, threadIdx.x), epoch, a.err, 10 + threadIdx.x, a.world > 1))
+        if (wait_flag(flag_ptr(me, L, 0, threadIdx.x), epoch, a.err, 10 + threadIdx.x, a.world > 1, a.wait_ns))
             pairs[threadIdx.x] =
                 (int)ld_acquire_x(reinterpret_cast<const unsigned int*>(me + L.rx_n) + threadIdx.x, a.world > 1) * a.k;
         else
@@ -859,7 +856,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(BExchangeArgs a) {
     if (threadIdx.x == 0) ok_all = 1;
     __syncthreads();
     if (threadIdx.x < a.world &&
-        !wait_flag(flag_ptr(me, L, 1, threadIdx.x), epoch, a.err, 30 + threadIdx.x, a.world > 1))
+        !wait_flag(flag_ptr(me, L, 1, threadIdx.x), epoch, a.err, 30 + threadIdx.x, a.world > 1, a.wait_ns))
         atomicExch(&ok_all, 0);
     __syncthreads();
     if (!ok_all) return;

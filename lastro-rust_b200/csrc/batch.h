@@ -65,6 +65,7 @@ struct BExchangeArgs {
     const unsigned int* epoch_base;  // flags carry epoch_base + layer + 1
     int layer;
     int* err;
+    unsigned long long wait_ns;   // bound of every flag wait (lastro_batch_set_wait_limit)
     unsigned int* counter;        // last-CTA election, zero between launches
     int n, k, H;
     // group (owner): outputs for the grouped GEMMs and the return

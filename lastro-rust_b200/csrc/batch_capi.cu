@@ -28,6 +28,7 @@ struct lastro_batch {
     int attn_S = 1, attn_cap = 1;  // attention splits per (token, KV head) and positions one split stages
     int n_sm = 148;
     bool poisoned = false, connected = false, use_graphs = true;
+    unsigned long long wait_ns = 10ull * 1000 * 1000 * 1000;  // bound of the exchange's flag waits
     int gemm_mode = 2;  // 0 mma.sync, 1 tcgen05 (cp.async stages), 2 tcgen05 warp-specialised (TMA weight tiles)
     // TMA tensor maps of the weights (mode 2): per layer qkv, o, gate_up, down; then the embedding (lm_head)
     std::vector<CUtensorMap> wmaps;
@@ -136,6 +137,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
     xa.local = b->d_local;
     xa.epoch_base = b->epoch;
     xa.err = b->d_err;
+    xa.wait_ns = b->wait_ns;
     xa.n = n;
     xa.k = k;
     xa.H = H;
@@ -792,6 +794,20 @@ extern "C" int lastro_batch_set_options(lastro_batch* b, int32_t use_graphs, int
     }
     b->gemm_mode = use_tcgen05;
     b->attn_tc = attn_tc != 0;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_batch_set_wait_limit(lastro_batch* b, uint64_t wait_ns) {
+    if (!b) return LASTRO_E_ARG;
+    if (wait_ns < 1000000ull || wait_ns > 600ull * 1000 * 1000 * 1000)
+        return set_err(b->ctx, LASTRO_E_ARG, "wait limit %llu ns outside [1 ms, 600 s]", (unsigned long long)wait_ns);
+    cudaSetDevice(b->ctx->device);
+    cudaStreamSynchronize(b->ctx->stream);
+    if (wait_ns != b->wait_ns) {  // the captured graphs hold the old limit in their kernel arguments
+        for (auto& g : b->graphs) cudaGraphExecDestroy(g.second);
+        b->graphs.clear();
+    }
+    b->wait_ns = wait_ns;
     return LASTRO_OK;
 }
 

@@ -404,10 +404,15 @@ cudaError_t mark(StepEvents* pe, cudaStream_t s, int kind = -1) {
 }
 
 // Enqueue the kernels of one decode step; the token is read from d_token, the position from d_pos.
-cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullptr) {
+// trace: with a timeline buffer ([launches][kTraceMaxCtas][3] words), launch i of the step stamps slot i
+cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullptr, unsigned long long* trace = nullptr) {
     const lastro_model_desc& d = m->d;
     const bool pdl = m->use_pdl && !pe;
     cudaError_t e;
+    int launch = 0;
+    auto slot = [&]() -> unsigned long long* {
+        return trace ? trace + (size_t)(launch++) * kTraceMaxCtas * 3 : nullptr;
+    };
     if ((e = mark(pe, s)) != cudaSuccess) return e;
     if (m->fused_ok && m->use_fused) {
         if ((e = launch_fused_step(fused_args(m), d.kv_dtype == LASTRO_DTYPE_F32, s)) != cudaSuccess) return e;
@@ -439,6 +444,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         qa.d = d.head_dim;
         qa.kv_heads = d.kv_heads;
         qa.eps = d.eps;
+        qa.trace = slot();
         if ((e = launch_qkv_rope(qa, s, pdl && l > 0)) != cudaSuccess) return e;
         if ((e = mark(pe, s, KK_QKV)) != cudaSuccess) return e;
 
@@ -461,6 +467,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         aa.max_len = m->max_len;
         aa.split_cap = attn_split_cap(m->max_len);
         aa.scale = d.attention_multiplier;
+        aa.trace = slot();
         if (m->attn_tc) {
             BAttnArgs ba{};
             ba.q = m->q;
@@ -499,6 +506,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         oa.wr_t = L.wr_t;
         oa.shares = m->op_partial;
         oa.E = d.experts;
+        oa.trace = slot();
         if ((e = launch_oproj(oa, s, pdl)) != cudaSuccess) return e;
         if ((e = mark(pe, s, KK_OPROJ)) != cudaSuccess) return e;
 
@@ -522,6 +530,9 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         ga.I = d.inter;
         ga.k = d.k;
         ga.E = d.experts;
+        ga.down_w = L.down;
+        ga.down_row_bytes = wrow_bytes(d.inter, m->q8);
+        ga.trace = slot();
         if ((e = launch_gate_up(ga, s, pdl)) != cudaSuccess) return e;
         if ((e = mark(pe, s, KK_GATE_UP)) != cudaSuccess) return e;
 
@@ -545,6 +556,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
             da.pf[1] = N.wo;
             da.pf_bytes[1] = (unsigned long long)d.hidden * wrow_bytes(m->qd, m->q8);
         }
+        da.trace = slot();
         if ((e = launch_down(da, s, pdl)) != cudaSuccess) return e;
         if ((e = mark(pe, s, KK_DOWN)) != cudaSuccess) return e;
     }
@@ -564,6 +576,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
     ha.pos = m->d_pos;
     ha.V = d.vocab;
     ha.H = d.hidden;
+    ha.trace = slot();
     if ((e = launch_head(ha, s, pdl, nullptr)) != cudaSuccess) return e;
     return mark(pe, s, KK_HEAD);
 }
@@ -936,22 +949,66 @@ extern "C" int lastro_model_fill_kv_synthetic(lastro_model* m, int32_t n, uint64
     cudaSetDevice(ctx->device);
     cudaStream_t s = ctx->stream;
     const lastro_model_desc& d = m->d;
-    const size_t elems = (size_t)m->max_pages * d.kv_heads * kPageSize * d.head_dim;
     const float sc = synth_scale(sd);
+    const int f32 = d.kv_dtype == LASTRO_DTYPE_F32;
+    // layer l's K and V streams are seeded mix64(seed + 2l) and mix64(seed + 2l + 1), as the CPU oracle's fill
     for (int l = 0; l < d.layers; ++l) {
-        const uint64_t sk = tensor_seed(seed, l, 100), sv = tensor_seed(seed, l, 101);
-        if (d.kv_dtype == LASTRO_DTYPE_F32) {
-            MTRY(launch_synth_f32(static_cast<float*>(m->L[l].k_pool), elems, sk, sc, s), "kv fill");
-            MTRY(launch_synth_f32(static_cast<float*>(m->L[l].v_pool), elems, sv, sc, s), "kv fill");
-        } else {
-            MTRY(launch_synth_bf16(static_cast<uint16_t*>(m->L[l].k_pool), elems, sk, sc, 0.0f, s), "kv fill");
-            MTRY(launch_synth_bf16(static_cast<uint16_t*>(m->L[l].v_pool), elems, sv, sc, 0.0f, s), "kv fill");
-        }
+        const uint64_t sk = mix64_host(seed + 2 * (uint64_t)l), sv = mix64_host(seed + 2 * (uint64_t)l + 1);
+        MTRY(launch_synth_kv_pages(m->L[l].k_pool, f32, m->page_table, n, d.kv_heads, d.head_dim, kPageSize, sk, sc, s),
+             "kv fill");
+        MTRY(launch_synth_kv_pages(m->L[l].v_pool, f32, m->page_table, n, d.kv_heads, d.head_dim, kPageSize, sv, sc, s),
+             "kv fill");
     }
     MTRY(cudaMemcpyAsync(m->d_pos, &n, sizeof(int), cudaMemcpyHostToDevice, s), "kv fill");
     MTRY(cudaMemsetAsync(m->d_step, 0, sizeof(int), s), "kv fill");
     MTRY(cudaStreamSynchronize(s), "kv fill");
     m->pos_host = n;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_model_read_kv(lastro_model* m, int32_t layer, int32_t pos0, int32_t n, float* k_out, float* v_out) {
+    if (!m) return LASTRO_E_ARG;
+    lastro_ctx* ctx = m->ctx;
+    if (m->poisoned) return set_err(ctx, LASTRO_E_POISONED, "model unusable after an earlier error");
+    const lastro_model_desc& d = m->d;
+    if (layer < 0 || layer >= d.layers || pos0 < 0 || n < 0 || (int64_t)pos0 + n > m->pos_host)
+        return set_err(ctx, LASTRO_E_ARG, "read_kv: layer %d, positions [%d, %d) of %d", layer, pos0, pos0 + n,
+                       m->pos_host);
+    if (n == 0) return LASTRO_OK;
+    cudaSetDevice(ctx->device);
+    cudaStream_t s = ctx->stream;
+    const int ps = kPageSize, dh = d.head_dim, kvh = d.kv_heads;
+    const size_t eb = kv_elem_bytes(m), page_elems = (size_t)kvh * ps * dh;
+    const int pg0 = pos0 / ps, pg1 = (pos0 + n - 1) / ps;
+    std::vector<int> pt(pg1 + 1);
+    MTRY(cudaMemcpyAsync(pt.data(), m->page_table, sizeof(int) * pt.size(), cudaMemcpyDeviceToHost, s), "read_kv");
+    MTRY(cudaStreamSynchronize(s), "read_kv");
+    std::vector<unsigned char> buf(page_elems * eb);
+    for (int which = 0; which < 2; ++which) {
+        float* out = which ? v_out : k_out;
+        if (!out) continue;
+        const unsigned char* pool = static_cast<const unsigned char*>(which ? m->L[layer].v_pool : m->L[layer].k_pool);
+        for (int pg = pg0; pg <= pg1; ++pg) {
+            MTRY(cudaMemcpyAsync(buf.data(), pool + (size_t)pt[pg] * page_elems * eb, buf.size(), cudaMemcpyDeviceToHost, s),
+                 "read_kv");
+            MTRY(cudaStreamSynchronize(s), "read_kv");
+            for (int p = std::max(pos0, pg * ps); p < std::min(pos0 + n, (pg + 1) * ps); ++p)
+                for (int h = 0; h < kvh; ++h)
+                    for (int j = 0; j < dh; ++j) {
+                        const size_t src = ((size_t)h * ps + (p - pg * ps)) * dh + j;
+                        float v;
+                        if (eb == 4) {
+                            memcpy(&v, buf.data() + src * 4, 4);
+                        } else {
+                            uint16_t b;
+                            memcpy(&b, buf.data() + src * 2, 2);
+                            const uint32_t u = (uint32_t)b << 16;
+                            memcpy(&v, &u, 4);
+                        }
+                        out[(size_t)(p - pos0) * kvh * dh + (size_t)h * dh + j] = v;
+                    }
+        }
+    }
     return LASTRO_OK;
 }
 
@@ -1014,6 +1071,69 @@ extern "C" int lastro_model_generate(lastro_model* m, const int32_t* prompt, int
     if (rc) return rc;
     m->pos_host += steps;
     return LASTRO_OK;
+}
+
+extern "C" int lastro_model_generate_until(lastro_model* m, const int32_t* prompt, int32_t n_prompt, int32_t n_new,
+                                           int32_t eos, int32_t* out_ids, int32_t* n_out) {
+    if (!m) return LASTRO_E_ARG;
+    lastro_ctx* ctx = m->ctx;
+    int rc = check_ready(m);
+    if (rc) return rc;
+    if (n_prompt < 1 || n_new < 1 || !prompt || !out_ids || !n_out)
+        return set_err(ctx, LASTRO_E_ARG, "generate_until needs a prompt, n_new >= 1 and both outputs");
+    if (eos >= m->d.vocab) return set_err(ctx, LASTRO_E_ARG, "eos %d out of range", eos);
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= m->d.vocab) return set_err(ctx, LASTRO_E_ARG, "prompt token %d out of range", prompt[i]);
+    if (m->pos_host + n_prompt + n_new - 1 > m->max_len)
+        return set_err(ctx, LASTRO_E_FULL, "generate would overflow the KV cache");
+    cudaSetDevice(ctx->device);
+    cudaStream_t s = ctx->stream;
+    const int start = m->pos_host;
+    MTRY(cudaMemcpyAsync(m->d_prompt, prompt, sizeof(int) * n_prompt, cudaMemcpyHostToDevice, s), "prompt upload");
+    MTRY(cudaMemsetAsync(m->d_step, 0, sizeof(int), s), "step reset");
+    for (int i = 0; i < n_prompt; ++i) {
+        MTRY(cudaMemcpyAsync(m->d_token, m->d_prompt + i, sizeof(int), cudaMemcpyDeviceToDevice, s), "token");
+        rc = run_step(m);
+        if (rc) return rc;
+    }
+    // generated token i sits at d_out_ids[n_prompt - 1 + i]; steps run in chunks, each chunk's ids read back once, so
+    // the host sees an end of text at most kChunk - 1 steps late; the position is then rolled back to the reference's
+    // (geracao_regra.rs:230-245: the end-of-text token is emitted, never fed)
+    constexpr int kChunk = 16;
+    int produced = 1, done = 0;  // the prompt's last step produced token 0
+    while (true) {
+        MTRY(cudaMemcpyAsync(out_ids + done, m->d_out_ids + (n_prompt - 1) + done, sizeof(int) * (produced - done),
+                             cudaMemcpyDeviceToHost, s),
+             "ids download");
+        rc = finish(m, "generate");
+        if (rc) return rc;
+        int stop = -1;
+        if (eos >= 0)
+            for (int i = done; i < produced; ++i)
+                if (out_ids[i] == eos) {
+                    stop = i;
+                    break;
+                }
+        if (stop >= 0 || produced == n_new) {
+            const int n = stop >= 0 ? stop + 1 : produced;
+            const int pos = start + n_prompt + n - 1;  // prompt and the generated tokens before the last one were fed
+            *n_out = n;
+            if (pos != start + n_prompt + produced - 1) {
+                MTRY(cudaMemcpyAsync(m->d_pos, &pos, sizeof(int), cudaMemcpyHostToDevice, s), "position rollback");
+                MTRY(cudaMemcpyAsync(m->d_token, out_ids + n - 1, sizeof(int), cudaMemcpyHostToDevice, s), "token");
+                MTRY(cudaStreamSynchronize(s), "position rollback");
+            }
+            m->pos_host = pos;
+            return LASTRO_OK;
+        }
+        done = produced;
+        const int run = std::min(kChunk, n_new - produced);
+        for (int i = 0; i < run; ++i) {
+            rc = run_step(m);
+            if (rc) return rc;
+        }
+        produced += run;
+    }
 }
 
 extern "C" int lastro_model_decode(lastro_model* m, int32_t n) {
@@ -1090,6 +1210,85 @@ extern "C" int lastro_model_profile(lastro_model* m, int32_t steps, float* kerne
     return result;
 }
 
+extern "C" int lastro_model_trace(lastro_model* m, int32_t steps, float* exposed_ms, float* span_ms, float* wait_ms,
+                                  int32_t n_kinds, float* step_ms) {
+    if (!m) return LASTRO_E_ARG;
+    lastro_ctx* ctx = m->ctx;
+    int rc = check_ready(m);
+    if (rc) return rc;
+    if (steps < 1 || !exposed_ms || !span_ms || !wait_ms || !step_ms || n_kinds < KK_COUNT)
+        return set_err(ctx, LASTRO_E_ARG, "trace arguments");
+    if (m->fused_ok && m->use_fused) return set_err(ctx, LASTRO_E_UNSUPPORTED, "trace: the fused step has no per-kernel launches");
+    if (m->pos_host + steps > m->max_len) return set_err(ctx, LASTRO_E_FULL, "trace would overflow the KV cache");
+    cudaSetDevice(ctx->device);
+    cudaStream_t s = ctx->stream;
+    const int launches = 5 * m->d.layers + 1;
+    const size_t words = (size_t)launches * kTraceMaxCtas * 3;
+    if (!m->d_trace) MTRY(m->arena.alloc(&m->d_trace, words), "trace buffer");
+    if (!m->trace_graph) {
+        // the product step's kernels, launch for launch, with the stamps on; captured like the product graph
+        cudaGraph_t g = nullptr;
+        MTRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
+        cudaError_t e = cudaMemsetAsync(m->d_trace, 0, words * sizeof(unsigned long long), s);
+        if (e == cudaSuccess) e = enqueue_step(m, s, nullptr, m->d_trace);
+        cudaError_t e2 = cudaStreamEndCapture(s, &g);
+        if (e == cudaSuccess) e = e2;
+        if (e == cudaSuccess) e = cudaGraphInstantiate(&m->trace_graph, g, 0);
+        if (g) cudaGraphDestroy(g);
+        if (e != cudaSuccess) {
+            m->trace_graph = nullptr;
+            return model_fail(m, e, "trace capture");
+        }
+    }
+    std::vector<int> kind(launches);
+    for (int l = 0; l < m->d.layers; ++l) {
+        const int k5[5] = {KK_QKV, KK_ATTN, KK_OPROJ, KK_GATE_UP, KK_DOWN};
+        for (int i = 0; i < 5; ++i) kind[5 * l + i] = k5[i];
+    }
+    kind[launches - 1] = KK_HEAD;
+    std::vector<unsigned long long> h(words);
+    std::vector<double> ex(KK_COUNT, 0.0), sp(KK_COUNT, 0.0), wt(KK_COUNT, 0.0);
+    double step_acc = 0.0;
+    MTRY(cudaMemsetAsync(m->d_step, 0, sizeof(int), s), "step reset");
+    for (int st = 0; st < steps; ++st) {
+        MTRY(cudaGraphLaunch(m->trace_graph, s), "trace launch");
+        MTRY(cudaMemcpyAsync(h.data(), m->d_trace, words * sizeof(unsigned long long), cudaMemcpyDeviceToHost, s),
+             "trace copy");
+        MTRY(cudaStreamSynchronize(s), "trace");
+        unsigned long long first = ~0ull, prev_end = 0, last = 0;
+        for (int i = 0; i < launches; ++i) {
+            unsigned long long t0 = ~0ull, rel = ~0ull, t1 = 0;
+            for (int c = 0; c < kTraceMaxCtas; ++c) {
+                const unsigned long long* w = &h[((size_t)i * kTraceMaxCtas + c) * 3];
+                if (!w[0]) continue;
+                t0 = std::min(t0, w[0]);
+                if (w[1]) rel = std::min(rel, w[1]);
+                t1 = std::max(t1, w[2]);
+            }
+            if (t0 == ~0ull) continue;  // a launch without stamps (tensor-core attention)
+            if (rel == ~0ull) rel = t0;
+            first = std::min(first, t0);
+            last = std::max(last, t1);
+            const unsigned long long from = prev_end ? prev_end : t0;  // a gap before the launch counts as its own
+            ex[kind[i]] += t1 > from ? (double)(t1 - from) : 0.0;
+            sp[kind[i]] += (double)(t1 - t0);
+            wt[kind[i]] += prev_end && rel > prev_end ? (double)(rel - prev_end) : 0.0;  // hand-off latency
+            prev_end = std::max(prev_end, t1);
+        }
+        if (last > first && first != ~0ull) step_acc += (double)(last - first);
+    }
+    rc = finish(m, "trace");
+    if (rc) return rc;
+    m->pos_host += steps;
+    for (int k = 0; k < KK_COUNT; ++k) {
+        exposed_ms[k] = (float)(ex[k] / steps * 1e-6);
+        span_ms[k] = (float)(sp[k] / steps * 1e-6);
+        wait_ms[k] = (float)(wt[k] / steps * 1e-6);
+    }
+    *step_ms = (float)(step_acc / steps * 1e-6);
+    return LASTRO_OK;
+}
+
 extern "C" int lastro_model_set_options(lastro_model* m, int32_t use_graphs, int32_t use_pdl, int32_t use_fused) {
     if (!m) return LASTRO_E_ARG;
     cudaSetDevice(m->ctx->device);
@@ -1097,6 +1296,10 @@ extern "C" int lastro_model_set_options(lastro_model* m, int32_t use_graphs, int
     if (m->graph) {
         cudaGraphExecDestroy(m->graph);
         m->graph = nullptr;
+    }
+    if (m->trace_graph) {
+        cudaGraphExecDestroy(m->trace_graph);
+        m->trace_graph = nullptr;
     }
     m->use_graphs = use_graphs != 0;
     m->use_pdl = use_pdl != 0;
@@ -1116,6 +1319,10 @@ extern "C" int lastro_model_set_attention(lastro_model* m, int32_t tensor_cores)
         cudaGraphExecDestroy(m->graph);
         m->graph = nullptr;
     }
+    if (m->trace_graph) {
+        cudaGraphExecDestroy(m->trace_graph);
+        m->trace_graph = nullptr;
+    }
     m->attn_tc = tensor_cores != 0;
     return LASTRO_OK;
 }
@@ -1125,6 +1332,7 @@ extern "C" void lastro_model_destroy(lastro_model* m) {
     cudaSetDevice(m->ctx->device);
     cudaStreamSynchronize(m->ctx->stream);  // gpu_model.rs:448-455
     if (m->graph) cudaGraphExecDestroy(m->graph);
+    if (m->trace_graph) cudaGraphExecDestroy(m->trace_graph);
     m->arena.release();
     if (m->h_token) cudaFreeHost(m->h_token);
     lastro_ctx* ctx = m->ctx;

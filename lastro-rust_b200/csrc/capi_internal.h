@@ -158,6 +158,9 @@ struct lastro_model {
     int pos_host = 0;
     std::vector<char> loaded;  // per (layer, kind)
     cudaGraphExec_t graph = nullptr;
+    // in-graph timeline (lastro_model_trace): stamp buffer and the step graph captured with the stamps on
+    unsigned long long* d_trace = nullptr;
+    cudaGraphExec_t trace_graph = nullptr;
     // fused step (one persistent launch per step) when the shapes fit it
     bool fused_ok = false, use_fused = false;
     lastro::FusedLayout flay{};

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "kernels.h"  // kTraceMaxCtas
+
 #define LDEV __device__ __forceinline__
 
 namespace lastro {
@@ -17,6 +19,32 @@ constexpr int kWarp = 32;
 // scheduled early so that its weight loads overlap this kernel.
 LDEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 LDEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---- in-graph timeline (lastro_model_trace) -----------------------------------------------------------------------
+// With a non-null trace base, every CTA of a launch stamps the global timer (ns) into its own three words: [0] when
+// thread 0 starts, [1] when thread 0 passes griddepcontrol.wait, [2] the latest exit of any warp (atomicMax by lane 0
+// of each warp; the destructor runs on every return path).  The host reduces over CTAs: min start, min release, max
+// end.  A null base (the product path) costs one predicated branch per stamp.
+LDEV unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+struct CtaTrace {
+    unsigned long long* p;
+    LDEV explicit CtaTrace(unsigned long long* base) : p(nullptr) {
+        const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+        if (base && cta < (unsigned)kTraceMaxCtas) p = base + 3 * (size_t)cta;
+        if (p && threadIdx.x == 0) p[0] = global_ns();
+    }
+    LDEV void released() const {
+        if (p && threadIdx.x == 0) p[1] = global_ns();
+    }
+    LDEV ~CtaTrace() {
+        if (p && (threadIdx.x & 31) == 0) atomicMax(p + 2, global_ns());
+    }
+};
 
 // ---- loads ------------------------------------------------------------------------------------------------------
 // 16-byte weight load, read once per step: non-coherent path, no L1 allocation.

@@ -41,6 +41,7 @@ cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStrea
 // ------------------------------------------------------------------------------------------------------------------
 template <int NCH, bool KV_F32, bool Q8>
 __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
+    const CtaTrace trace_(a.trace);
     constexpr int BLOCK = 128;
     constexpr int NV = Vec<NCH, BLOCK>::NV;
     extern __shared__ __align__(16) float smem[];
@@ -61,11 +62,22 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
     w1.load(wb + (size_t)r1 * rbh, a.H, lane, active);
     float4 ln[NV];
     vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
+    // The position changes only in the previous step's head kernel, which completed before this step's first kernel
+    // started (that launch is not programmatic): so the position, its RoPE row and the K/V page of this token are
+    // final before the wait, and their loads leave the critical path.
+    const int pos = __ldcg(a.pos);
+    float rc = 1.0f, rs = 0.0f;
+    int page = 0;
+    if (active && lane == 0) {
+        rc = __ldg(a.rope_cs + (size_t)pos * a.d + j);
+        rs = __ldg(a.rope_cs + (size_t)pos * a.d + half + j);
+        if (r0 >= a.qd) page = __ldcg(a.page_table + pos / a.page_size);
+    }
 
     pdl_wait();
     pdl_launch();
+    trace_.released();
 
-    const int pos = __ldcg(a.pos);
     float4 v[NV];
     if (a.embed_mode) {
         // model.rs:134-138: embedding row x embedding_multiplier is the residual stream of layer 0
@@ -92,11 +104,9 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
     const float x1 = warp_sum(w0.dot(xs, a.H, lane));
     const float x2 = warp_sum(w1.dot(xs, a.H, lane));
     if (lane != 0) return;
-    const float* cs = a.rope_cs + (size_t)pos * a.d;
-    const float c = __ldg(cs + j), s = __ldg(cs + half + j);
     // model.rs:153-155: x1*c - x2*s, x2*c + x1*s (no contraction)
-    const float ro0 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
-    const float ro1 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+    const float ro0 = __fsub_rn(__fmul_rn(x1, rc), __fmul_rn(x2, rs));
+    const float ro1 = __fadd_rn(__fmul_rn(x2, rc), __fmul_rn(x1, rs));
     if (r0 < a.qd) {
         a.q_out[r0] = ro0;
         a.q_out[r1] = ro1;
@@ -107,7 +117,7 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
     if (!is_k) rr -= a.kvd;
     const int kvh = rr / a.d;
     const float v0 = is_k ? ro0 : x1, v1 = is_k ? ro1 : x2;
-    const int page = __ldcg(a.page_table + pos / a.page_size), slot = pos % a.page_size;
+    const int slot = pos % a.page_size;
     const size_t base = (((size_t)page * a.kv_heads + kvh) * a.page_size + slot) * a.d;
     void* pool = is_k ? a.k_pool : a.v_pool;
     if (KV_F32) {
@@ -134,6 +144,7 @@ constexpr int kAttnWarps = 8;
 
 template <bool KV_F32, int G>
 __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) {
+    const CtaTrace trace_(a.trace);
     constexpr int D = kHeadDim;
     constexpr int NW = kAttnWarps;
     constexpr int ESZ = KV_F32 ? 4 : 2;
@@ -182,6 +193,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
 
     pdl_wait();
     pdl_launch();
+    trace_.released();
 
     for (int i = threadIdx.x; i < G * D / 4; i += blockDim.x)
         reinterpret_cast<float4*>(&sq[0][0])[i] = __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)z * HD + (size_t)kvh * G * D) + i);
@@ -413,6 +425,7 @@ constexpr int kOpRows = 2 * kOpWarps;
 
 template <int NCH, bool Q8>
 __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
+    const CtaTrace trace_(a.trace);
     constexpr int BLOCK = 32 * kOpWarps;
     extern __shared__ __align__(16) float smem[];
     float* xs = smem;          // [qd]
@@ -432,6 +445,7 @@ __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
     }
     pdl_wait();
     pdl_launch();
+    trace_.released();
     const float ha = (lane == 0 && ra < a.H) ? __ldcg(a.h + ra) : 0.0f;
     const float hb = (lane == 0 && rb < a.H) ? __ldcg(a.h + rb) : 0.0f;
     copy_to_smem<BLOCK>(a.att, a.qd, xs);
@@ -491,6 +505,7 @@ constexpr int kGuPairs = 16;
 
 template <int NCH, bool Q8>
 __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
+    const CtaTrace trace_(a.trace);
     constexpr int BLOCK = 256, R = kGuPairs, HALF = R / 2;
     constexpr int NV = Vec<NCH, BLOCK>::NV;
     static_assert(HALF == BLOCK / 32, "one row pair per warp per stage");
@@ -516,6 +531,7 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
 
     pdl_wait();
     pdl_launch();
+    trace_.released();
 
     float4 v[NV];
     float r = 0.0f;
@@ -561,6 +577,97 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------------------------------
+// gate_up, streaming form (the model step): one wave of CTAs, about one per SM.  The k experts' (gate row j, up row j)
+// pairs, slot-major (pair p = slot * I + j), are split into equal contiguous ranges, one per CTA.  Right after the
+// routing is known every CTA requests ALL of its rows at once (a few hundred KB per SM at most, so the whole 25 MB of
+// the 3B model's experts is in flight together), in kGsGroups groups that complete on their own barriers so warps
+// start on the first group while the rest stream; then it hints into L2 its share of the chosen experts' down
+// weights, which the down kernel reads next.  Warp w computes pairs w, w + 8, ...: a = silu(g) * u (cpu.rs:65).
+// ------------------------------------------------------------------------------------------------------------------
+constexpr int kGsGroups = 8;
+constexpr int kGsThreads = 256;
+constexpr int kGsMaxH = 2048;  // x staged in static shared memory
+
+template <int NCH, bool Q8>
+__global__ void __launch_bounds__(kGsThreads, 1) gate_up_stream_kernel(GateUpArgs a) {
+    const CtaTrace trace_(a.trace);
+    constexpr int BLOCK = kGsThreads, NW = BLOCK / 32;
+    constexpr int NV = Vec<NCH, BLOCK>::NV;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    const size_t rbh = wrow_bytes(a.H, Q8);
+    unsigned char* wrows = smem_raw;  // [np][2][rbh]: gate row then up row of each pair
+    __shared__ __align__(8) uint64_t bar[kGsGroups];
+    __shared__ float red[BLOCK];
+    __shared__ int sid[kMaxTopK];
+    __shared__ float sval[kMaxTopK], sw[kMaxTopK], s_r;
+    __shared__ __align__(16) float xs[kGsMaxH];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int total = a.k * a.I;
+    const int p0 = (int)((long long)total * blockIdx.x / gridDim.x);
+    const int np = (int)((long long)total * (blockIdx.x + 1) / gridDim.x) - p0;
+    const int gsz = (np + kGsGroups - 1) / kGsGroups;  // pairs per barrier group
+    if (threadIdx.x == 0)
+        for (int g = 0; g < kGsGroups; ++g) mbar_init(&bar[g], 1);
+    float4 ln[NV];
+    vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
+
+    pdl_wait();
+    pdl_launch();
+    trace_.released();
+
+    float4 v[NV];
+    vec_load_cg<BLOCK, NV>(a.x, a.H, v);  // in flight while the routing is reduced
+    // every CTA reduces the same shares in the same order: bitwise the same routing (CTA 0 publishes it); the
+    // reduction's __syncthreads also makes the barrier initialisation visible
+    const float r = route_from_shares<BLOCK>(a.rs, a.E, a.k, a.H, red, sid, sval, sw, &s_r, blockIdx.x == 0);
+    if (threadIdx.x == 0) {
+        const unsigned char* w = static_cast<const unsigned char*>(a.w);
+        for (int g = 0; g * gsz < np; ++g) {
+            const int q0 = g * gsz, q1 = min(np, q0 + gsz);
+            mbar_expect_tx(&bar[g], (uint32_t)((q1 - q0) * 2 * rbh));
+            for (int q = q0; q < q1; ++q) {
+                const int p = p0 + q, slot = p / a.I, j = p - slot * a.I;
+                // expert id clamped so that a stale id can never address outside the weights
+                const int e = min(max(sid[slot], 0), a.E - 1);
+                const unsigned char* base = w + (size_t)e * 2 * a.I * rbh;
+                bulk_g2s(wrows + (size_t)(2 * q) * rbh, base + (size_t)j * rbh, (uint32_t)rbh, &bar[g]);
+                bulk_g2s(wrows + (size_t)(2 * q + 1) * rbh, base + (size_t)(a.I + j) * rbh, (uint32_t)rbh, &bar[g]);
+            }
+        }
+        // this CTA's share of the chosen experts' down slabs (k slabs of H rows), hinted into L2
+        if (a.down_w) {
+            const unsigned long long slab = (unsigned long long)a.H * a.down_row_bytes, all = slab * a.k;
+            const unsigned long long share = ((all + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
+            unsigned long long o0 = share * blockIdx.x;
+            const unsigned long long o1 = min(all, o0 + share);
+            while (o0 < o1) {
+                const int slot = (int)(o0 / slab);
+                const unsigned long long in = o0 - (unsigned long long)slot * slab;
+                const unsigned long long n = min(o1 - o0, slab - in);
+                const int e = min(max(sid[slot], 0), a.E - 1);
+                bulk_prefetch_l2(static_cast<const unsigned char*>(a.down_w) + (size_t)e * slab + in, (uint32_t)n);
+                o0 += n;
+            }
+        }
+    }
+    // xn = ln * (h * r) (model.rs:141-145)
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int i = threadIdx.x + k * BLOCK;
+        if (4 * i < a.H) reinterpret_cast<float4*>(xs)[i] = ln_times(ln[k], v[k], r);
+    }
+    __syncthreads();
+    float4 xa[NCH], xb[NCH];
+    x_to_regs<NCH>(xs, a.H, lane, xa, xb);
+    for (int q = warp; q < np; q += NW) {
+        if (!mbar_wait(&bar[q / gsz], 0, a.err, 1)) return;
+        const float g = warp_sum(smem_row_dot_w<NCH, Q8>(wrows + (size_t)(2 * q) * rbh, xa, xb, a.H, lane));
+        const float u = warp_sum(smem_row_dot_w<NCH, Q8>(wrows + (size_t)(2 * q + 1) * rbh, xa, xb, a.H, lane));
+        if (lane == 0) a.a[p0 + q] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
 // down: CTA per block of kDnRows output rows; warp j takes expert slot j for all rows of the block, so a_j is read
 // once into registers.  Expert ids and weights come from the router, two kernels back, so before
 // griddepcontrol.wait thread 0 already streams the k contiguous [kDnRows, I] slabs W_d[e_j][r0 .. r0+R] into
@@ -571,6 +678,7 @@ constexpr int kDnRows = 8;
 
 template <int NCI, bool Q8>
 __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
+    const CtaTrace trace_(a.trace);
     constexpr int BLOCK = 256, R = kDnRows;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const size_t rbi = wrow_bytes(a.I, Q8);                              // bytes per weight row
@@ -604,6 +712,7 @@ __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
     for (int j = 0; j < kMaxTopK; ++j) gw[j] = j < a.k ? (fused ? sw[j] : __ldcg(a.weights + j)) : 0.0f;
     pdl_wait();
     pdl_launch();
+    trace_.released();
     const float hr = (threadIdx.x < R && a.accumulate) ? __ldcg(a.out + r0 + threadIdx.x) : 0.0f;
     float4 xa[NCI], xb[NCI];
     if (warp < a.k) x_to_regs_global<NCI>(a.a + (size_t)warp * a.I, a.I, lane, xa, xb);
@@ -657,6 +766,7 @@ LDEV void head_load(uint4 (&w)[2][NCH], int row, const HeadArgs& a, int lane) {
 
 template <int NCH>
 __global__ void __launch_bounds__(256) head_kernel(HeadArgs a) {
+    const CtaTrace trace_(a.trace);
     constexpr int BLOCK = 32 * kHeadWarps;
     constexpr int NV = Vec<NCH, BLOCK>::NV;
     extern __shared__ __align__(16) float smem[];
@@ -673,6 +783,7 @@ __global__ void __launch_bounds__(256) head_kernel(HeadArgs a) {
     vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
     pdl_wait();
     pdl_launch();
+    trace_.released();
     {
         float4 v[NV];
         vec_load_cg<BLOCK, NV>(a.h, a.H, v);
@@ -747,6 +858,25 @@ __global__ void synth_bf16_kernel(uint16_t* out, size_t n, uint64_t seed, float 
 __global__ void synth_f32_kernel(float* out, size_t n, uint64_t seed, float scale) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         out[i] = synth_value(seed, i, scale);
+}
+
+// Synthetic K/V context in the paged layout [page][kv_head][slot][d]: logical element i = pos * kvd + head * d + j of
+// positions [0, n) gets the generator's value i (the CPU oracle's lo_session_fill_kv, element for element), rounded to
+// bf16 when the pool is bf16.
+template <bool F32>
+__global__ void synth_kv_pages_kernel(void* pool, const int* page_table, int n, int kv_heads, int d, int page_size,
+                                      uint64_t seed, float scale) {
+    const size_t kvd = (size_t)kv_heads * d, total = (size_t)n * kvd;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int p = (int)(i / kvd);
+        const int r = (int)(i - (size_t)p * kvd), h = r / d, j = r - h * d;
+        const size_t dst = (((size_t)__ldg(page_table + p / page_size) * kv_heads + h) * page_size + p % page_size) * d + j;
+        const float v = synth_value(seed, i, scale);
+        if (F32)
+            static_cast<float*>(pool)[dst] = v;
+        else
+            static_cast<uint16_t*>(pool)[dst] = f32_to_bf16_rne(v);
+    }
 }
 
 __global__ void synth_norm_kernel(float* out, size_t n, uint64_t seed, float scale) {
@@ -919,7 +1049,51 @@ size_t down_smem(int H, int I, int k, int q8) {
 int gate_up_rows_per_cta() { return kGuPairs; }
 int down_rows_per_cta() { return kDnRows; }
 
+// SMs of the current device (the streaming kernels launch about one CTA per SM)
+int sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!cached[dev]) {
+        int n = 0;
+        cached[dev] = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0 ? n : 148;
+    }
+    return cached[dev];
+}
+
+cudaError_t launch_gate_up_stream(const GateUpArgs& a, cudaStream_t s, bool pdl) {
+    if (a.H > kGsMaxH || a.H % 8) return cudaErrorInvalidValue;
+    const size_t pair_bytes = 2 * wrow_bytes(a.H, a.q8);
+    const size_t budget = kMaxSmemBytes - 12 * 1024;  // the kernel's static shared memory stays below 12 KB
+    const int total = a.k * a.I;
+    const int cap = (int)(budget / pair_bytes);  // pairs one CTA can stage
+    if (cap < 1) return cudaErrorInvalidValue;
+    int grid = sm_count();
+    if ((total + grid - 1) / grid > cap) grid = (total + cap - 1) / cap;
+    if (grid > total) grid = total;
+    const size_t smem = (size_t)((total + grid - 1) / grid) * pair_bytes;
+#define LASTRO_GS(N)                                                                                   \
+    {                                                                                                  \
+        auto k = a.q8 ? gate_up_stream_kernel<N, true> : gate_up_stream_kernel<N, false>;             \
+        cudaError_t e = allow_smem(k, smem);                                                           \
+        return e != cudaSuccess ? e : launch_ex(k, dim3(grid), dim3(kGsThreads), smem, s, pdl, a);     \
+    }
+    switch (chunks_for(a.H)) {
+    case 1: LASTRO_GS(1)
+    case 2: LASTRO_GS(2)
+    case 3: LASTRO_GS(3)
+    case 4: LASTRO_GS(4)
+    case 5: LASTRO_GS(5)
+    case 6: LASTRO_GS(6)
+    case 7: LASTRO_GS(7)
+    case 8: LASTRO_GS(8)
+    default: return cudaErrorInvalidValue;
+    }
+#undef LASTRO_GS
+}
+
 cudaError_t launch_gate_up(const GateUpArgs& a, cudaStream_t s, bool pdl) {
+    if (a.rs.shares) return launch_gate_up_stream(a, s, pdl);
     if (a.I % kGuPairs) return cudaErrorInvalidValue;
     const dim3 grid(a.k * (a.I / kGuPairs)), block(256);
     const size_t smem = gate_up_smem(a.H, a.q8);
@@ -1002,6 +1176,19 @@ cudaError_t launch_synth_f32(float* out, size_t n, uint64_t seed, float scale, c
     size_t blocks = (n + 255) / 256;
     if (blocks > 148 * 64) blocks = 148 * 64;
     synth_f32_kernel<<<(unsigned)blocks, 256, 0, s>>>(out, n, seed, scale);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_synth_kv_pages(void* pool, int kv_f32, const int* page_table, int n, int kv_heads, int d,
+                                  int page_size, uint64_t seed, float scale, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    const size_t total = (size_t)n * kv_heads * d;
+    size_t blocks = (total + 255) / 256;
+    if (blocks > 148 * 64) blocks = 148 * 64;
+    if (kv_f32)
+        synth_kv_pages_kernel<true><<<(unsigned)blocks, 256, 0, s>>>(pool, page_table, n, kv_heads, d, page_size, seed, scale);
+    else
+        synth_kv_pages_kernel<false><<<(unsigned)blocks, 256, 0, s>>>(pool, page_table, n, kv_heads, d, page_size, seed, scale);
     return cudaGetLastError();
 }
 

@@ -17,6 +17,9 @@
 
 namespace lastro {
 
+// in-graph timeline: CTAs per launch that stamp their three words (CtaTrace in common.cuh)
+constexpr int kTraceMaxCtas = 1024;
+
 // Linear weights are bf16 ([rows, cols] row-major) or Q8_0.  A Q8_0 row on the device is its cols int8 values, then its
 // cols/32 fp16 block scales, padded to a multiple of 16 bytes (so rows stay 16-byte aligned for bulk copies); weight =
 // scale * value.  `q8` in the argument structs below selects the Q8_0 kernels.
@@ -43,6 +46,7 @@ struct QkvArgs {
     int page_size, kv_f32;
     int H, qd, kvd, d, kv_heads;
     float eps;
+    unsigned long long* trace;  // in-graph timeline stamps of this launch (CtaTrace), or null
 };
 
 struct AttnArgs {
@@ -67,6 +71,7 @@ struct AttnArgs {
     int tokens, pt_stride;
     uint16_t* att_hi;  // optional: att_out split into bf16 hi + lo (the batched o-projection's operands)
     uint16_t* att_lo;
+    unsigned long long* trace;  // in-graph timeline stamps of this launch (CtaTrace), or null
 };
 
 struct OprojArgs {
@@ -81,6 +86,7 @@ struct OprojArgs {
     const float* wr_t;      // [H, E]: router weight x MoE norm weight, transposed (launch_router_fold)
     float* shares;          // [oproj_grid(H), E + 1]
     int E;
+    unsigned long long* trace;  // in-graph timeline stamps of this launch (CtaTrace), or null
 };
 
 // Routing of the fused path: the output projection's per-CTA shares, reduced by every CTA of the expert kernels in
@@ -120,6 +126,10 @@ struct GateUpArgs {
     float* a;             // [k, I]
     int* err;             // error word: a bounded wait that gave up writes its code here
     int H, I, k, E;
+    // optional (streaming kernel of the model step): the down weights [E, H, I], whose chosen slabs are hinted into L2
+    const void* down_w;
+    size_t down_row_bytes;
+    unsigned long long* trace;  // in-graph timeline stamps of this launch (CtaTrace), or null
 };
 
 struct DownArgs {
@@ -137,6 +147,7 @@ struct DownArgs {
     // optional: byte ranges prefetched into L2 for the kernels that follow (the next layer's dense weights)
     const void* pf[2];
     unsigned long long pf_bytes[2];
+    unsigned long long* trace;  // in-graph timeline stamps of this launch (CtaTrace), or null
 };
 
 struct HeadArgs {
@@ -154,6 +165,7 @@ struct HeadArgs {
     int* step;                      // index into out_ids
     int* pos;                       // incremented once per step
     int V, H;
+    unsigned long long* trace;  // in-graph timeline stamps of this launch (CtaTrace), or null
 };
 
 // Launchers: `pdl` marks the launch as programmatic-dependent on the previous kernel of the stream.
@@ -177,6 +189,9 @@ cudaError_t launch_synth_f32(float* out, size_t n, uint64_t seed, float scale, c
 cudaError_t launch_synth_q8_0(unsigned char* out, size_t rows, int cols, uint64_t seed, cudaStream_t s);
 // norms: bf16(1 + value) widened to f32
 cudaError_t launch_synth_norm_f32(float* out, size_t n, uint64_t seed, float scale, cudaStream_t s);
+// positions [0, n) of a paged K or V pool, element for element the CPU oracle's synthetic context
+cudaError_t launch_synth_kv_pages(void* pool, int kv_f32, const int* page_table, int n, int kv_heads, int d,
+                                  int page_size, uint64_t seed, float scale, cudaStream_t s);
 
 // ---- fused decode step: the whole step (every layer and the head) in one persistent cooperative launch -----------
 // One CTA per SM.  Every value one CTA hands to another inside the step travels as a 64-bit word {f32 value, u32 tag}

@@ -5,6 +5,7 @@
 // capture, or a latency-critical path where cudaMalloc's implicit synchronisation is not acceptable.  They pass
 // every input and output buffer themselves; the only other memory this entry point touches is the scratch below, a
 // file-scope __device__ array that every GPU loading the library holds until the process exits.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -32,10 +33,34 @@ struct NoAllocScratch {
 static __device__ __align__(256) NoAllocScratch g_noalloc_scratch;
 
 // The host name g_noalloc_scratch is only a stand-in for the symbol, not a device address: the address is looked
-// up once per device, with that device current, and cached here.
+// up with the device current and cached per device, together with the CUDA context it was looked up in.  A device
+// reset (or a primary context torn down and re-created) loads the module again at another address; the context
+// changes with it, so the next call looks the address up again instead of using a stale one.
 constexpr int kMaxDevices = 64;
-NoAllocScratch* g_scratch_addr[kMaxDevices] = {};
+struct ScratchAddr {
+    NoAllocScratch* p = nullptr;
+    CUcontext ctx = nullptr;
+};
+ScratchAddr g_scratch_addr[kMaxDevices];
 std::mutex g_scratch_mu;
+
+// cuCtxGetCurrent through the runtime's driver entry point (the library links only the runtime)
+CUcontext current_context() {
+    using GetCurrent = CUresult (*)(CUcontext*);
+    static GetCurrent fn = nullptr;
+    if (!fn) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !f) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        fn = reinterpret_cast<GetCurrent>(f);
+    }
+    CUcontext c = nullptr;
+    return fn(&c) == CUDA_SUCCESS ? c : nullptr;
+}
 
 int scratch_for_current_device(NoAllocScratch** out) {
     int dev = -1;
@@ -43,16 +68,19 @@ int scratch_for_current_device(NoAllocScratch** out) {
         cudaGetLastError();
         return LASTRO_E_CUDA;
     }
+    const CUcontext ctx = current_context();
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
+    ScratchAddr& a = g_scratch_addr[dev];
+    if (!a.p || !ctx || a.ctx != ctx) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
             cudaGetLastError();
             return LASTRO_E_CUDA;
         }
-        g_scratch_addr[dev] = static_cast<NoAllocScratch*>(p);
+        a.p = static_cast<NoAllocScratch*>(p);
+        a.ctx = current_context();  // the runtime may only now have made the primary context current
     }
-    *out = g_scratch_addr[dev];
+    *out = a.p;
     return LASTRO_OK;
 }
 
@@ -117,5 +145,17 @@ extern "C" int lastro_moe_block_forward_noalloc(const float* x, const uint16_t* 
     da.k = k;
     da.E = experts;
     if (launch_down(da, s, true) != cudaSuccess) return launch_failed();
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_moe_block_noalloc_status(int32_t* status, void* stream) {
+    if (!status) return LASTRO_E_ARG;
+    NoAllocScratch* sc = nullptr;
+    int rc = scratch_for_current_device(&sc);
+    if (rc) return rc;
+    // enqueued after the caller's blocks on the same stream: the word the last of them left (0 = every wait completed)
+    if (cudaMemcpyAsync(status, &sc->err, sizeof(int), cudaMemcpyDefault, static_cast<cudaStream_t>(stream)) !=
+        cudaSuccess)
+        return launch_failed();
     return LASTRO_OK;
 }

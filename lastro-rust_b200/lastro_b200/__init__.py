@@ -60,17 +60,23 @@ EXPORTS = {
     "lastro_layer_add_into": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p]),
     "lastro_layer_destroy": (None, [C.c_void_p]),
     "lastro_moe_block_forward_noalloc": (C.c_int, [C.c_void_p] * 4 + [C.c_int32] * 4 + [C.c_void_p] * 4),
+    "lastro_moe_block_noalloc_status": (C.c_int, [C.c_void_p, C.c_void_p]),
     "lastro_model_create": (C.c_int, [C.c_void_p, C.POINTER(ModelDesc), C.c_int32, C.POINTER(C.c_void_p)]),
     "lastro_model_load_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int32, C.POINTER(C.c_int64), C.c_int32,
                                            C.c_void_p]),
     "lastro_model_fill_synthetic": (C.c_int, [C.c_void_p, C.c_uint64, C.c_float, C.c_float]),
     "lastro_model_fill_kv_synthetic": (C.c_int, [C.c_void_p, C.c_int32, C.c_uint64, C.c_float]),
+    "lastro_model_read_kv": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
     "lastro_model_step": (C.c_int, [C.c_void_p, C.c_int32] + [C.c_void_p] * 4),
     "lastro_model_generate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
+    "lastro_model_generate_until": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
+                                              C.POINTER(C.c_int32)]),
     "lastro_model_decode": (C.c_int, [C.c_void_p, C.c_int32]),
     "lastro_model_reset": (C.c_int, [C.c_void_p]),
     "lastro_model_position": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
     "lastro_model_profile": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32]),
+    "lastro_model_trace": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32,
+                                     C.c_void_p]),
     "lastro_model_set_options": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32]),
     "lastro_model_fused": (C.c_int, [C.c_void_p]),
     "lastro_model_set_attention": (C.c_int, [C.c_void_p, C.c_int32]),
@@ -89,6 +95,7 @@ EXPORTS = {
     "lastro_batch_set_options": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32]),
     "lastro_batch_profile": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p,
                                        C.c_int32]),
+    "lastro_batch_set_wait_limit": (C.c_int, [C.c_void_p, C.c_uint64]),
     "lastro_batch_destroy": (None, [C.c_void_p]),
 }
 
@@ -199,6 +206,12 @@ def moe_block_forward_noalloc(x: int, router: int, gate_up: int, down: int, expe
                                                   stream)
 
 
+def moe_block_noalloc_status(status: int, stream: int | None = None) -> int:
+    """Enqueue a copy of the allocation-free block's error word into caller memory at `status`
+    (lastro_moe_block_noalloc_status); returns the status code of the call itself."""
+    return lib().lastro_moe_block_noalloc_status(status, stream)
+
+
 TENSOR_NAMES = ("input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_proj.weight",
                 "self_attn.k_proj.weight", "self_attn.v_proj.weight", "self_attn.o_proj.weight",
                 "block_sparse_moe.router.layer.weight", "block_sparse_moe.input_linear.weight",
@@ -253,8 +266,17 @@ class GpuModel:
         self.ctx.check(lib().lastro_model_fill_synthetic(self.h, seed, std, norm_std))
 
     def fill_kv_synthetic(self, n: int, seed: int = 7, std: float = 0.5):
-        """A context of n positions with synthetic K/V (no model steps): for benchmarks and profiling."""
+        """A context of n positions with synthetic K/V (no model steps), element for element the CPU oracle's
+        Session.fill_kv(n, seed, std): for benchmarks, profiling and parity at long contexts."""
         self.ctx.check(lib().lastro_model_fill_kv_synthetic(self.h, n, seed, std))
+
+    def read_kv(self, layer: int, pos0: int, n: int):
+        """K and V rows of positions [pos0, pos0 + n) of one layer as f32 [n, kv_heads * head_dim]."""
+        kvd = self.cfg["kv_heads"] * self.cfg["head_dim"]
+        k = np.empty((n, kvd), np.float32)
+        v = np.empty((n, kvd), np.float32)
+        self.ctx.check(lib().lastro_model_read_kv(self.h, layer, pos0, n, _p(k), _p(v)))
+        return k, v
 
     def step(self, token: int, want_logits: bool = True, want_routes: bool = True):
         """(logits, next_token, route_ids [L,k], route_w [L,k]) (GpuModel::step)."""
@@ -271,6 +293,14 @@ class GpuModel:
         out = np.empty(max(n_new, 1), np.int32)
         self.ctx.check(lib().lastro_model_generate(self.h, _p(p), p.size, n_new, _p(out)))
         return out[:n_new]
+
+    def generate_until(self, prompt, n_new: int, eos: int = 0) -> np.ndarray:
+        """Greedy generation that stops after the first `eos` (included), geracao_regra.rs's normal use."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.empty(n_new, np.int32)
+        n = C.c_int32()
+        self.ctx.check(lib().lastro_model_generate_until(self.h, _p(p), p.size, n_new, eos, _p(out), C.byref(n)))
+        return out[:n.value]
 
     def decode(self, n: int):
         self.ctx.check(lib().lastro_model_decode(self.h, n))
@@ -291,6 +321,17 @@ class GpuModel:
         out = np.zeros(len(self.KERNELS), np.float32)
         self.ctx.check(lib().lastro_model_profile(self.h, steps, _p(out), out.size))
         return dict(zip(self.KERNELS, out.tolist()))
+
+    def trace(self, steps: int) -> dict:
+        """In-graph timeline of `steps` graph-replayed steps: {"exposed": {kind: ms}, "span": {..}, "wait": {..},
+        "step_ms": ms}; exposed times are each kind's share of the step's critical path (they sum to the step); wait
+        is the hand-off latency from the previous launch's last exit to the first release from griddepcontrol.wait."""
+        ex, sp, wt = (np.zeros(len(self.KERNELS), np.float32) for _ in range(3))
+        st = np.zeros(1, np.float32)
+        self.ctx.check(lib().lastro_model_trace(self.h, steps, _p(ex), _p(sp), _p(wt), ex.size, _p(st)))
+        kinds = self.KERNELS
+        return {"exposed": dict(zip(kinds, ex.tolist())), "span": dict(zip(kinds, sp.tolist())),
+                "wait": dict(zip(kinds, wt.tolist())), "step_ms": float(st[0])}
 
     def set_options(self, graphs: bool = True, pdl: bool = True, fused: bool = False):
         self.ctx.check(lib().lastro_model_set_options(self.h, int(graphs), int(pdl), int(fused)))
@@ -393,6 +434,10 @@ class GpuBatch:
         if attn_tc is None:
             attn_tc = self.kv_dtype == "bf16"
         self.ctx.check(lib().lastro_batch_set_options(self.h, int(graphs), int(gemm), int(attn_tc)))
+
+    def set_wait_limit(self, seconds: float):
+        """Bound of every wait on another rank's exchange flag (default 10 s)."""
+        self.ctx.check(lib().lastro_batch_set_wait_limit(self.h, int(seconds * 1e9)))
 
     KERNELS = ("norm", "qkv", "rope_kv", "attention", "oproj", "router", "group", "gate_up", "down", "combine",
                "lm_head", "argmax")

@@ -390,6 +390,15 @@ class Session:
             out.append(np.frombuffer(buf, dtype=np.float32, count=n).reshape(self.pos, kvd).copy())
         return out
 
+    def write_kv(self, layer: int, pos: int, k: np.ndarray, v: np.ndarray):
+        """Overwrite the cached K and V rows of position pos (< self.pos) of one layer (state-synchronised tests)."""
+        c = self.model.cfg
+        kvd = c["kv_heads"] * c["head_dim"]
+        assert 0 <= pos < self.pos and k.size == kvd and v.size == kvd
+        for f, row in ((lib().lo_session_k, k), (lib().lo_session_v, v)):
+            src = np.ascontiguousarray(row, dtype=np.float32)
+            C.memmove(f(self.h, layer) + pos * kvd * 4, src.ctypes.data, kvd * 4)
+
     def close(self):
         if getattr(self, "h", None):
             lib().lo_session_destroy(self.h)

@@ -150,3 +150,54 @@ def test_c4_3b_q8_matches_oracle_at_full_size(gpu_ctx, pool):
     s.close()
     om.close()
     m.close()
+
+
+def test_c4_3b_q8_64_greedy_steps_state_synchronised(gpu_ctx):
+    """bench.py's C4 model (every linear Q8_0, norm weights 1.0, a synthetic 512-position context filled identically on
+    both sides) for 64 greedy steps.  These weights are chaotic (module notes): two free-running trajectories part
+    after a few positions whatever the kernels do, so each step is compared from the same state -- after every step
+    the K/V rows the GPU wrote replace the oracle's.  The cache is f32 here: within ONE step this model turns a bf16
+    rounding flip of a stored K/V element (2^-9) into logits ~1e-1 apart (measured: 0.15 at the second step with bf16
+    KV), so bf16 storage of the Q8_0 path is compared on the tiny models above.  Per step: logits within 5e-2 (the
+    north star's Q8_0 bar), the greedy id the oracle's except at top1-top2 gaps < 1e-2, layer 0's routing identical
+    except at router gaps < 1e-4, and >= 95 % of all (layer, slot) ids equal."""
+    c = CFG.C4_3B_Q8
+    cfg = c["model"]
+    n_ctx, steps = c["context"], 64
+    threads = os.cpu_count() or 8
+    m = LB.GpuModel(gpu_ctx, cfg, n_ctx + steps + 8, kv_dtype="f32")
+    m.fill_synthetic(c["weight_seed"], CFG.WEIGHT_STD, 0.0)
+    m.fill_kv_synthetic(n_ctx, c["prompt_seed"], 0.5)
+    om = O.Model(cfg, synthetic_seed=c["weight_seed"], std=CFG.WEIGHT_STD, norm_std=0.0, threads=threads)
+    pool = O.Pool(threads)
+    s = O.Session(om, pool, n_ctx + steps + 8)
+    s.fill_kv(n_ctx, c["prompt_seed"], 0.5)
+    k0, v0 = m.read_kv(0, 0, n_ctx)
+    assert np.array_equal(k0, s.kv(0)[0]) and np.array_equal(v0, s.kv(0)[1])
+    tok = int(CFG.synthetic_tokens(1, c["prompt_seed"], cfg["vocab"])[0])
+    worst, same = 0.0, []
+    for t in range(steps):
+        lg, nxt, ids, _ = m.step(tok)
+        lo, io, _ = s.step(tok)
+        rl = s.router_logits()
+        err = rel_l2(lg, lo)
+        assert err < 5e-2, f"step {t}: logits rel-L2 {err:.2e}"
+        worst = max(worst, err)
+        if not np.array_equal(ids[0], io[0]):
+            j = int(np.argmax(ids[0] != io[0]))
+            gap = abs(float(rl[0, io[0, j]]) - float(rl[0, ids[0, j]]))
+            assert gap < 1e-4, f"step {t}: layer 0 slot {j} routes differ at router gap {gap:.2e}"
+        same.append(float((ids == io).mean()))
+        top2 = np.sort(lo)[-2:]
+        assert nxt == O.argmax_last(lo) or top2[1] - top2[0] < 1e-2, f"step {t}: greedy {nxt}"
+        pos = m.pos - 1
+        for layer in range(cfg["layers"]):
+            k, v = m.read_kv(layer, pos, 1)
+            s.write_kv(layer, pos, k, v)
+        tok = O.argmax_last(lo)
+    print(f"C4 64 steps: worst logits rel-L2 {worst:.2e}, routes equal {np.mean(same):.4f} (min {min(same):.4f})")
+    assert np.mean(same) >= 0.95
+    s.close()
+    pool.close()
+    om.close()
+    m.close()

@@ -45,6 +45,11 @@ def test_noalloc_matches_layer_forward(gpu_ctx, E, H, I, k):
         assert ids.cpu().numpy().tolist() == want_ids.tolist(), f"call {t}"
         np.testing.assert_allclose(w.cpu().numpy(), want_w, rtol=2e-6, atol=1e-7)
         assert rel_l2(y.cpu().numpy(), want_y) < REL, f"call {t}"
+        # every bounded copy wait of the call completed: the error word the status call copies out is 0
+        status = torch.full((1,), -1, dtype=torch.int32, device="cuda:0")
+        assert LB.moe_block_noalloc_status(status.data_ptr(), stream.cuda_stream) == LB.OK
+        stream.synchronize()
+        assert int(status.item()) == 0, f"call {t}"
     layer.close()
 
 
@@ -58,3 +63,4 @@ def test_noalloc_refuses_shapes_beyond_its_scratch():
     assert LB.moe_block_forward_noalloc(p, p, p, p, 8, 256, 2056, 8, p, p, p, None) == LB.E_UNSUPPORTED
     assert LB.moe_block_forward_noalloc(p, p, p, p, 16, 256, 2048, 9, p, p, p, None) == LB.E_UNSUPPORTED
     assert LB.moe_block_forward_noalloc(0, p, p, p, 8, 256, 128, 2, p, p, p, None) == LB.E_ARG
+    assert LB.moe_block_noalloc_status(0, None) == LB.E_ARG
