@@ -31,6 +31,7 @@ extern "C" {
 #define LASTRO_E_NOMEM 5       /* device allocation failed */
 #define LASTRO_E_UNSUPPORTED 6 /* shape/dtype outside what the kernels implement */
 #define LASTRO_E_STATE 7       /* e.g. a weight tensor not loaded yet */
+#define LASTRO_E_IO 8          /* a file could not be opened or read (WeightError::Io, weights.rs:26-29) */
 
 #define LASTRO_DTYPE_BF16 1
 #define LASTRO_DTYPE_F32 2
@@ -169,6 +170,38 @@ int lastro_model_fused(const lastro_model *model);
  * (0, the default: faster at batch 1 on B200; the only one with f32 KV) */
 int lastro_model_set_attention(lastro_model *model, int32_t tensor_cores);
 void lastro_model_destroy(lastro_model *model);
+
+/* ---- checkpoints on disk: safetensors + config.json (weights.rs:52-122, model.rs:34-61, model.rs:99-132) ------- */
+/* Host-only (no GPU needed) except lastro_model_load_checkpoint.  Errors of the checkpoint and config calls are
+ * written to err (err_len bytes, may be NULL) like the reference's WeightError / Config::from_json strings:
+ * LASTRO_E_ARG for a malformed file or a refusal, LASTRO_E_IO for a file that cannot be opened or read,
+ * LASTRO_E_UNSUPPORTED for a config the kernels do not implement. */
+typedef struct lastro_checkpoint lastro_checkpoint;
+/* Checkpoint::open (weights.rs:52-106): indexes every *.safetensors file of dir (sorted by name): header length
+ * (8 bytes little-endian, at most 100 MiB), JSON header name -> {dtype, shape, data_offsets}; refuses missing fields,
+ * non-numeric or != 2 data_offsets, offsets that overflow or end past the file.  Only the index stays in memory. */
+int lastro_checkpoint_open(const char *dir, lastro_checkpoint **out, char *err, int32_t err_len);
+void lastro_checkpoint_close(lastro_checkpoint *ck);
+/* number of tensors indexed */
+int lastro_checkpoint_count(const lastro_checkpoint *ck);
+/* one index entry: dtype string (dtype_len bytes), shape (up to max_ndim dims; -1 for a dim beyond INT64_MAX) and
+ * its rank; LASTRO_E_ARG when the tensor is absent */
+int lastro_checkpoint_tensor(const lastro_checkpoint *ck, const char *name, char *dtype, int32_t dtype_len,
+                             int64_t *shape, int32_t max_ndim, int32_t *ndim);
+/* Checkpoint::bf16 (weights.rs:108-122): a whole BF16 tensor into dst (capacity elements); refuses an absent tensor,
+ * another dtype, or a byte count that does not match the shape (overflow included) */
+int lastro_checkpoint_read_bf16(const lastro_checkpoint *ck, const char *name, uint16_t *dst, int64_t capacity,
+                                char *err, int32_t err_len);
+/* Config::from_json (model.rs:34-61) on the text of a config.json: refuses model_type != "granitemoe", a non-null
+ * rope_scaling, attention_bias true and tie_word_embeddings false (LASTRO_E_UNSUPPORTED), or a missing field
+ * (LASTRO_E_ARG); head_dim defaults to hidden / heads.  weight_dtype and kv_dtype come back BF16. */
+int lastro_config_from_json(const char *json, lastro_model_desc *out, char *err, int32_t err_len);
+/* the same on the checkpoint directory's config.json */
+int lastro_checkpoint_config(const lastro_checkpoint *ck, lastro_model_desc *out, char *err, int32_t err_len);
+/* HostModel::load + GpuModel::upload (model.rs:99-132, block.rs:31-53): every tensor of the model, each refused
+ * before it is read when absent or of another shape, dtype or byte size; BF16 tensors, or for a Q8_0 model its linear
+ * weights as U8 tensors whose last axis holds each row's 34-byte blocks.  Errors through lastro_last_error. */
+int lastro_model_load_checkpoint(lastro_model *model, const lastro_checkpoint *ck);
 
 /* ---- batched decode with expert parallelism (no counterpart in the reference, which decodes one sequence) ------- */
 /* Many independent sequences decoded together on a model's weights (bf16); each sequence's results equal its own

@@ -841,7 +841,7 @@ __global__ void __launch_bounds__(256) brouter_kernel(BRouterArgs a) {
 
 // ------------------------------------------------------------------------------------------------------------------
 // combine (sender): CTA per token, after every owner's return flag: h += resid * sum_j w_j y_j, slots in routing
-// order (cpu.rs:231-238).
+// order (cpu.rs:141-148).
 // ------------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) ep_combine_kernel(BExchangeArgs a) {
     constexpr int BLOCK = 256, NV = 8;  // H <= 2048

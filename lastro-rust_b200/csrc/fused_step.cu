@@ -31,8 +31,8 @@
 // word, drains the CTA's own copies in flight and returns; the other CTAs see the error word and return too.
 //
 // Reference behaviour restated (brenoperucchi/lastro-rust, rust/moe-rt/src): RMSNorm model.rs:141-145, RoPE
-// rotate_half model.rs:147-158, attention model.rs:203-222, routing block.rs:79-89, SwiGLU cpu.rs:154-158, experts
-// cpu.rs:205-240, step model.rs:181-243, argmax (last maximum) bin/m1b-gulosa.rs:22-24.
+// rotate_half model.rs:147-158, attention model.rs:203-222, routing block.rs:79-89, SwiGLU cpu.rs:64-68, experts
+// cpu.rs:115-150, step model.rs:181-243, argmax (last maximum) bin/m1b-gulosa.rs:22-24.
 #include <algorithm>
 
 #include "common.cuh"
@@ -891,7 +891,7 @@ __global__ void __launch_bounds__(kFT, 1) fused_step_kernel(const FusedArgs a) {
             #pragma unroll 1
             for (int t = threadIdx.x; t < npg; t += kFT) {
                 const float g = guout[2 * t], u = guout[2 * t + 1];
-                st_word(a.x.act + g0 + t, __fmul_rn(div_rn(g, __fadd_rn(1.0f, exp_f(-g))), u), tu);  // cpu.rs:154-158
+                st_word(a.x.act + g0 + t, __fmul_rn(div_rn(g, __fadd_rn(1.0f, exp_f(-g))), u), tu);  // cpu.rs:64-68
             }
             // arrive (synchronises the CTA: every read of the gate_up rows is done before the region is refilled)
             arrive_count(CNT(TG_UP));
@@ -976,7 +976,7 @@ __global__ void __launch_bounds__(kFT, 1) fused_step_kernel(const FusedArgs a) {
                 float acc = 0.0f;
                 #pragma unroll 1
                 for (int jj = 0; jj < a.k; ++jj) acc = __fadd_rn(acc, __fmul_rn(sw[jj], dpart[jj * a.lay.rows + t]));
-                const float hn = __fadd_rn(SM_OWN[t], __fmul_rn(a.resid, acc));  // cpu.rs:231-238, model.rs:230
+                const float hn = __fadd_rn(SM_OWN[t], __fmul_rn(a.resid, acc));  // cpu.rs:141-148, model.rs:230
                 SM_OWN[t] = hn;
                 st_word(a.x.h + r0 + t, hn, td);
             }

@@ -11,7 +11,7 @@
 //
 // Reference behaviour restated (brenoperucchi/lastro-rust, rust/moe-rt/src):
 //   RMSNorm  model.rs:141-145   RoPE rotate_half model.rs:147-158   attention model.rs:203-222
-//   routing  block.rs:79-89     SwiGLU cpu.rs:154-158               experts cpu.rs:205-240
+//   routing  block.rs:79-89     SwiGLU cpu.rs:64-68               experts cpu.rs:115-150
 //   step     model.rs:181-243   argmax (last maximum) bin/m1b-gulosa.rs:22-24
 #include "common.cuh"
 #include "kernels.h"
@@ -499,7 +499,7 @@ __global__ void router_fold_kernel(const void* wr, const float* ln, float* wr_t,
 // rows into shared memory with bulk async copies, in two stages (the first half of the rows completes on its own
 // barrier, so warps start on it while the second half is in flight); meanwhile the CTA builds xn = ln * (h * r).
 // Warp w then computes rows j0+w and j0+w+8: g = W[e][j] . xn, u = W[e][I+j] . xn, a = silu(g) * u
-// (cpu.rs:154-158, gpu.rs:45-74).  All k experts in one grid; every byte is requested at the start.
+// (cpu.rs:64-68, gpu.rs:45-74).  All k experts in one grid; every byte is requested at the start.
 // ------------------------------------------------------------------------------------------------------------------
 constexpr int kGuPairs = 16;
 
@@ -582,7 +582,7 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
 // routing is known every CTA requests ALL of its rows at once (a few hundred KB per SM at most, so the whole 25 MB of
 // the 3B model's experts is in flight together), in kGsGroups groups that complete on their own barriers so warps
 // start on the first group while the rest stream; then it hints into L2 its share of the chosen experts' down
-// weights, which the down kernel reads next.  Warp w computes pairs w, w + 8, ...: a = silu(g) * u (cpu.rs:65).
+// weights, which the down kernel reads next.  Warp w computes pairs w, w + 8, ...: a = silu(g) * u (cpu.rs:64-68).
 // ------------------------------------------------------------------------------------------------------------------
 constexpr int kGsGroups = 8;
 constexpr int kGsThreads = 256;
@@ -671,7 +671,7 @@ __global__ void __launch_bounds__(kGsThreads, 1) gate_up_stream_kernel(GateUpArg
 // down: CTA per block of kDnRows output rows; warp j takes expert slot j for all rows of the block, so a_j is read
 // once into registers.  Expert ids and weights come from the router, two kernels back, so before
 // griddepcontrol.wait thread 0 already streams the k contiguous [kDnRows, I] slabs W_d[e_j][r0 .. r0+R] into
-// shared memory.  Per row the k expert dots are then summed in routing order, y = sum_j w_j * d_j (cpu.rs:231-238),
+// shared memory.  Per row the k expert dots are then summed in routing order, y = sum_j w_j * d_j (cpu.rs:141-148),
 // and h[r] += resid * y (model.rs:230-232) or out[r] = y (block forward).
 // ------------------------------------------------------------------------------------------------------------------
 constexpr int kDnRows = 8;

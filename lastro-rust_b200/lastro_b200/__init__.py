@@ -19,7 +19,7 @@ PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB_PATH = os.path.join(PKG_DIR, "liblastro_b200.so")
 HEADER = os.path.join(PKG_DIR, "..", "include", "lastro_b200.h")
 
-OK, E_ARG, E_CUDA, E_POISONED, E_FULL, E_NOMEM, E_UNSUPPORTED, E_STATE = range(8)
+OK, E_ARG, E_CUDA, E_POISONED, E_FULL, E_NOMEM, E_UNSUPPORTED, E_STATE, E_IO = range(9)
 DTYPE_BF16, DTYPE_F32, DTYPE_Q8_0 = 1, 2, 3
 
 _lib = None
@@ -81,6 +81,15 @@ EXPORTS = {
     "lastro_model_fused": (C.c_int, [C.c_void_p]),
     "lastro_model_set_attention": (C.c_int, [C.c_void_p, C.c_int32]),
     "lastro_model_destroy": (None, [C.c_void_p]),
+    "lastro_checkpoint_open": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p), C.c_char_p, C.c_int32]),
+    "lastro_checkpoint_close": (None, [C.c_void_p]),
+    "lastro_checkpoint_count": (C.c_int, [C.c_void_p]),
+    "lastro_checkpoint_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_char_p, C.c_int32, C.c_void_p, C.c_int32,
+                                           C.POINTER(C.c_int32)]),
+    "lastro_checkpoint_read_bf16": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p, C.c_int64, C.c_char_p, C.c_int32]),
+    "lastro_config_from_json": (C.c_int, [C.c_char_p, C.c_void_p, C.c_char_p, C.c_int32]),
+    "lastro_checkpoint_config": (C.c_int, [C.c_void_p, C.c_void_p, C.c_char_p, C.c_int32]),
+    "lastro_model_load_checkpoint": (C.c_int, [C.c_void_p, C.c_void_p]),
     "lastro_batch_create": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_void_p)]),
     "lastro_batch_exchange_handle": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32]),
     "lastro_batch_connect": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32]),
@@ -212,6 +221,76 @@ def moe_block_noalloc_status(status: int, stream: int | None = None) -> int:
     return lib().lastro_moe_block_noalloc_status(status, stream)
 
 
+DESC_KEYS = ("hidden", "inter", "layers", "heads", "kv_heads", "head_dim", "vocab", "experts", "k", "rope_theta",
+             "eps", "embedding_multiplier", "residual_multiplier", "attention_multiplier", "logits_scaling")
+
+
+def _desc_dict(d: "ModelDesc") -> dict:
+    return {k: getattr(d, k) for k in DESC_KEYS}
+
+
+def config_from_json(text: str) -> dict:
+    """Config::from_json (model.rs:34-61) through the C ABI: the model config dict, or LastroError with the reason."""
+    d = ModelDesc()
+    err = C.create_string_buffer(512)
+    rc = lib().lastro_config_from_json(text.encode(), C.byref(d), err, len(err))
+    if rc != OK:
+        raise LastroError(rc, err.value.decode())
+    return _desc_dict(d)
+
+
+class Checkpoint:
+    """A safetensors checkpoint directory (weights.rs Checkpoint): index on open, tensors read on request.  Host-only."""
+
+    def __init__(self, path: str):
+        h = C.c_void_p()
+        err = C.create_string_buffer(512)
+        rc = lib().lastro_checkpoint_open(os.fsencode(path), C.byref(h), err, len(err))
+        if rc != OK:
+            raise LastroError(rc, err.value.decode())
+        self.h, self.path = h, path
+
+    def __len__(self):
+        return lib().lastro_checkpoint_count(self.h)
+
+    def info(self, name: str):
+        """(dtype, shape) of one tensor, or None when absent."""
+        dt = C.create_string_buffer(32)
+        shape = (C.c_int64 * 8)()
+        nd = C.c_int32()
+        if lib().lastro_checkpoint_tensor(self.h, name.encode(), dt, len(dt), shape, 8, C.byref(nd)) != OK:
+            return None
+        return dt.value.decode(), tuple(shape[i] for i in range(min(nd.value, 8)))
+
+    def bf16(self, name: str) -> np.ndarray:
+        """Checkpoint::bf16: the tensor's bf16 bits (uint16) with its shape."""
+        inf = self.info(name)
+        shape = inf[1] if inf else ()
+        n = int(np.prod(shape)) if inf and all(d >= 0 for d in shape) and np.prod([float(d) for d in shape]) < 2**40 else 0
+        out = np.empty(max(n, 1), np.uint16)
+        err = C.create_string_buffer(512)
+        rc = lib().lastro_checkpoint_read_bf16(self.h, name.encode(), _p(out), n, err, len(err))
+        if rc != OK:
+            raise LastroError(rc, err.value.decode())
+        return out[:n].reshape(shape)
+
+    def config(self) -> dict:
+        d = ModelDesc()
+        err = C.create_string_buffer(512)
+        rc = lib().lastro_checkpoint_config(self.h, C.byref(d), err, len(err))
+        if rc != OK:
+            raise LastroError(rc, err.value.decode())
+        return _desc_dict(d)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().lastro_checkpoint_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
 TENSOR_NAMES = ("input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_proj.weight",
                 "self_attn.k_proj.weight", "self_attn.v_proj.weight", "self_attn.o_proj.weight",
                 "block_sparse_moe.router.layer.weight", "block_sparse_moe.input_linear.weight",
@@ -261,6 +340,10 @@ class GpuModel:
         for l, lw in enumerate(w["layers"]):
             for key, name in zip(LAYER_KEYS, TENSOR_NAMES):
                 self.load_tensor(f"model.layers.{l}.{name}", lw[key])
+
+    def load_checkpoint(self, ck: "Checkpoint"):
+        """HostModel::load + GpuModel::upload from a safetensors checkpoint (every tensor checked before it is read)."""
+        self.ctx.check(lib().lastro_model_load_checkpoint(self.h, ck.h))
 
     def fill_synthetic(self, seed: int, std: float = 0.02, norm_std: float = 0.0):
         self.ctx.check(lib().lastro_model_fill_synthetic(self.h, seed, std, norm_std))

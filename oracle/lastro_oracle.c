@@ -7,7 +7,7 @@
  * cpu_baseline leg load it through oracle/oracle.py.
  *
  * Build: see oracle/Makefile (gcc -O2 -ffp-contract=off; the AVX2 dot is compiled
- * with a target attribute and chosen at run time, like cpu.rs:145-152).
+ * with a target attribute and chosen at run time, like cpu.rs:54-62).
  */
 #define _GNU_SOURCE
 #include "lastro_oracle.h"
@@ -25,7 +25,7 @@
 /* bf16 <-> f32                                                                */
 /* ------------------------------------------------------------------------- */
 
-/* cpu.rs:103-105: bf16 -> f32 is a 16-bit shift */
+/* cpu.rs:12-15: bf16 -> f32 is a 16-bit shift */
 static inline float bf2f(uint16_t b) {
     uint32_t u = (uint32_t)b << 16;
     float f;
@@ -343,10 +343,10 @@ void lo_synth_q8_0(uint8_t *out, size_t rows, size_t cols, uint64_t seed, int th
 }
 
 /* ------------------------------------------------------------------------- */
-/* dot product -- cpu.rs:107-152                                               */
+/* dot product -- cpu.rs:12-62                                               */
 /* ------------------------------------------------------------------------- */
 
-/* cpu.rs:107-116 dot_scalar: 4 accumulators over chunks of 4, then the tail */
+/* cpu.rs:17-26 dot_scalar: 4 accumulators over chunks of 4, then the tail */
 static float dot_scalar(const uint16_t *w, const float *x, size_t n) {
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     size_t c = n & ~(size_t)3;
@@ -357,7 +357,7 @@ static float dot_scalar(const uint16_t *w, const float *x, size_t n) {
     return acc[0] + acc[1] + acc[2] + acc[3] + tail;
 }
 
-/* cpu.rs:118-142 dot_avx2, lane by lane: 4 vectors of 8 FMA accumulators over
+/* cpu.rs:28-53 dot_avx2, lane by lane: 4 vectors of 8 FMA accumulators over
  * blocks of 32, the same horizontal reduction, then dot_scalar on the rest. */
 float lo_dot_portable(const uint16_t *w, const float *x, size_t n) {
     float acc[4][8];
@@ -401,7 +401,7 @@ static int have_avx2(void) {
 }
 #endif
 
-/* cpu.rs:145-152 */
+/* cpu.rs:54-62 */
 float lo_dot(const uint16_t *w, const float *x, size_t n) {
 #if defined(__x86_64__)
     if (have_avx2()) return dot_avx2(w, x, n);
@@ -466,9 +466,9 @@ static inline float dot_w(int32_t dtype, const void *row, const float *x, size_t
 }
 
 /* ------------------------------------------------------------------------- */
-/* GEMV, SwiGLU, experts -- cpu.rs:154-240                                     */
+/* GEMV, SwiGLU, experts -- cpu.rs:64-150                                     */
 /* ------------------------------------------------------------------------- */
-#define ROWS_PER_TASK 16 /* cpu.rs:100 */
+#define ROWS_PER_TASK 16 /* cpu.rs:9-10 */
 
 typedef struct {
     const void *w;
@@ -486,7 +486,7 @@ static void gemv_task(void *c, size_t t) {
     for (size_t r = r0; r < r1; ++r) g->y[r] = dot_w(g->dtype, (const uint8_t *)g->w + r * rb, g->x, (size_t)g->cols);
 }
 
-/* cpu.rs:197-203 Cpu::gemv (rows in tasks of 16 over the pool, cpu.rs:185-195), either weight type */
+/* cpu.rs:107-113 Cpu::gemv (rows in tasks of 16 over the pool, cpu.rs:95-106), either weight type */
 void lo_gemv_w(lo_pool *p, int32_t dtype, const void *w, int32_t rows, int32_t cols, const float *x, float *y) {
     gemv_ctx g = {w, dtype, rows, cols, x, y};
     pool_run(p, ((size_t)rows + ROWS_PER_TASK - 1) / ROWS_PER_TASK, gemv_task, &g);
@@ -496,7 +496,7 @@ void lo_gemv(lo_pool *p, const uint16_t *w, int32_t rows, int32_t cols, const fl
     lo_gemv_w(p, LO_W_BF16, w, rows, cols, x, y);
 }
 
-/* cpu.rs:154-158: a[j] = h[j] / (1 + exp(-h[j])) * h[I + j] */
+/* cpu.rs:64-68: a[j] = h[j] / (1 + exp(-h[j])) * h[I + j] */
 void lo_swiglu(const float *h, int32_t inter, float *a) {
     for (int32_t j = 0; j < inter; ++j) a[j] = h[j] / (1.0f + expf(-h[j])) * h[inter + j];
 }
@@ -538,7 +538,7 @@ static void experts_down_task(void *c, size_t t) {
     }
 }
 
-/* cpu.rs:205-240 Cpu::experts: dispatch 1 = the 2I gate_up rows of every chosen
+/* cpu.rs:115-150 Cpu::experts: dispatch 1 = the 2I gate_up rows of every chosen
  * expert, SwiGLU per expert, dispatch 2 = each row of y summed over the experts
  * in routing order. */
 void lo_experts_w(lo_pool *p, int32_t dtype, const float *x, int32_t k, const void *const *gate_up,

@@ -61,7 +61,7 @@ void lo_pool_destroy(lo_pool *p);
 int lo_pool_threads(const lo_pool *p);
 
 /* ---- kernels of the CPU path --------------------------------------------- */
-float lo_dot(const uint16_t *w, const float *x, size_t n);          /* cpu.rs:145-152 */
+float lo_dot(const uint16_t *w, const float *x, size_t n);          /* cpu.rs:54-62 */
 float lo_dot_portable(const uint16_t *w, const float *x, size_t n); /* same order, no SIMD */
 void lo_gemv(lo_pool *p, const uint16_t *w, int32_t rows, int32_t cols, const float *x, float *y);
 void lo_gemv_w(lo_pool *p, int32_t dtype, const void *w, int32_t rows, int32_t cols, const float *x, float *y);

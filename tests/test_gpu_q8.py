@@ -45,7 +45,7 @@ def q8_model(ctx, cfg, max_len, kv, seed=12):
 @pytest.mark.parametrize("E,H,I,k", [(4, 256, 128, 2), (32, 1024, 512, 8), (40, 1536, 512, 8)])
 def test_q8_block_matches_oracle(gpu_ctx, pool, E, H, I, k):
     """The Q8_0 MoE block (router, gate_up with SwiGLU, down with the weighted combine) against the oracle's
-    dequantised block (cpu.rs:224-238 on weight = scale x value) for 6 tokens: routing identical, y within 1e-5."""
+    dequantised block (cpu.rs:115-150 on weight = scale x value) for 6 tokens: routing identical, y within 1e-5."""
     router, gu, dn = S.q8_0(E, H, 11), S.q8_0(E * 2 * I, H, 12), S.q8_0(E * H, I, 13)
     layer = LB.GpuLayer(gpu_ctx, router, gu.reshape(E, 2 * I, -1), dn.reshape(E, H, -1), k)
     for t in range(6):
