@@ -825,6 +825,7 @@ struct lo_session {
     int32_t kv_bf16; /* store K/V rows rounded to bf16 (RNE), as a paged bf16 KV cache holds them */
     float **k_cache, **v_cache; /* per layer [max_len, kvd] */
     float *router_logits;       /* [layers, experts] of the last step (bias included) */
+    struct lo_step *st;         /* buffers of the step in progress (lo_session_step_begin .. _end) */
 };
 
 lo_session *lo_session_create(const lo_model *m, lo_pool *p, int32_t max_len) {
@@ -844,8 +845,11 @@ lo_session *lo_session_create(const lo_model *m, lo_pool *p, int32_t max_len) {
     return s;
 }
 
+static void step_free(lo_session *s);
+
 void lo_session_destroy(lo_session *s) {
     if (!s) return;
+    step_free(s);
     for (int32_t l = 0; l < s->layers; ++l) {
         free(s->k_cache[l]);
         free(s->v_cache[l]);
@@ -919,64 +923,116 @@ static void attn_task(void *cx, size_t hq) {
     free(scores);
 }
 
-/* model.rs:181-243 CpuSession::step */
-int lo_session_step(lo_session *s, int32_t token, float *logits, int32_t *ids, float *weights) {
+/* model.rs:181-243 CpuSession::step, in phases: the decoder layer's attention half (lo_session_layer_attention), its
+ * MoE half (the block, or lo_session_layer_moe with a result computed elsewhere), then the head.  A step that runs
+ * the phases in order is the same arithmetic as lo_session_step, which is written with them. */
+struct lo_step {
+    float *cs, *x, *xn, *q, *att, *o, *y, *rw;
+    int32_t *ri;
+};
+
+static void step_free(lo_session *s) {
+    struct lo_step *t = s->st;
+    if (!t) return;
+    free(t->cs);
+    free(t->x);
+    free(t->xn);
+    free(t->q);
+    free(t->att);
+    free(t->o);
+    free(t->y);
+    free(t->rw);
+    free(t->ri);
+    free(t);
+    s->st = NULL;
+}
+
+int lo_session_step_begin(lo_session *s, int32_t token) {
     const lo_model *m = s->m;
     const lo_config *c = &m->cfg;
     if (s->pos >= s->max_len || token < 0 || token >= c->vocab) return -1;
-    int32_t h = c->hidden, d = c->head_dim;
-    int32_t qd = c->heads * d, kvd = c->kv_heads * d;
-    float *cs = (float *)malloc(sizeof(float) * (size_t)d);
-    lo_rope_cos_sin(c->rope_theta, d, s->pos, cs);
-    float *x = (float *)malloc(sizeof(float) * (size_t)h);
-    float *xn = (float *)malloc(sizeof(float) * (size_t)h);
-    float *q = (float *)malloc(sizeof(float) * (size_t)qd);
-    float *att = (float *)malloc(sizeof(float) * (size_t)qd);
-    float *o = (float *)malloc(sizeof(float) * (size_t)h);
-    float *y = (float *)malloc(sizeof(float) * (size_t)h);
-    float *rw = (float *)malloc(sizeof(float) * (size_t)c->k);
-    int32_t *ri = (int32_t *)malloc(sizeof(int32_t) * (size_t)c->k);
+    step_free(s);
+    struct lo_step *t = (struct lo_step *)calloc(1, sizeof(struct lo_step));
+    int32_t h = c->hidden, d = c->head_dim, qd = c->heads * d;
+    t->cs = (float *)malloc(sizeof(float) * (size_t)d);
+    lo_rope_cos_sin(c->rope_theta, d, s->pos, t->cs);
+    t->x = (float *)malloc(sizeof(float) * (size_t)h);
+    t->xn = (float *)malloc(sizeof(float) * (size_t)h);
+    t->q = (float *)malloc(sizeof(float) * (size_t)qd);
+    t->att = (float *)malloc(sizeof(float) * (size_t)qd);
+    t->o = (float *)malloc(sizeof(float) * (size_t)h);
+    t->y = (float *)malloc(sizeof(float) * (size_t)h);
+    t->rw = (float *)malloc(sizeof(float) * (size_t)c->k);
+    t->ri = (int32_t *)malloc(sizeof(int32_t) * (size_t)c->k);
+    s->st = t;
     /* model.rs:134-138 embedding x embedding_multiplier */
-    for (int32_t i = 0; i < h; ++i) x[i] = bf2f(m->embed[(size_t)token * h + i]) * c->embedding_multiplier;
-    for (int32_t l = 0; l < c->layers; ++l) {
-        const lo_layer_weights *w = &m->layers[l];
-        lo_rmsnorm(x, w->ln_attn, h, c->eps, xn);
-        float *kr = s->k_cache[l] + (size_t)s->pos * kvd;
-        float *vr = s->v_cache[l] + (size_t)s->pos * kvd;
-        lo_gemv_w(s->pool, c->weight_dtype, w->q, qd, h, xn, q);
-        lo_gemv_w(s->pool, c->weight_dtype, w->k, kvd, h, xn, kr);
-        lo_gemv_w(s->pool, c->weight_dtype, w->v, kvd, h, xn, vr);
-        lo_rope(q, qd, d, cs);
-        lo_rope(kr, kvd, d, cs);
-        if (s->kv_bf16) {
-            round_bf16(kr, (size_t)kvd);
-            round_bf16(vr, (size_t)kvd);
-        }
-        memset(att, 0, sizeof(float) * (size_t)qd);
-        attn_ctx ac = {c, q, s->k_cache[l], s->v_cache[l], s->pos + 1, att};
-        pool_run(s->pool, (size_t)c->heads, attn_task, &ac);
-        lo_gemv_w(s->pool, c->weight_dtype, w->o, h, qd, att, o);
-        for (int32_t i = 0; i < h; ++i) x[i] += c->residual_multiplier * o[i];
-        lo_rmsnorm(x, w->ln_moe, h, c->eps, xn);
-        block_forward_impl(s->pool, c->weight_dtype, w->router, w->gate_up, w->down, c->experts, h, c->inter, c->k, xn,
-                           y, ri, rw, s->router_logits + (size_t)l * c->experts,
-                           m->router_bias ? m->router_bias + (size_t)l * c->experts : NULL);
-        for (int32_t i = 0; i < h; ++i) x[i] += c->residual_multiplier * y[i];
-        if (ids) memcpy(ids + (size_t)l * c->k, ri, sizeof(int32_t) * (size_t)c->k);
-        if (weights) memcpy(weights + (size_t)l * c->k, rw, sizeof(float) * (size_t)c->k);
+    for (int32_t i = 0; i < h; ++i) t->x[i] = bf2f(m->embed[(size_t)token * h + i]) * c->embedding_multiplier;
+    return 0;
+}
+
+/* layer l up to the MoE input: xn_out = RMSNorm(x + resid * attention, ln_moe) [H] */
+void lo_session_layer_attention(lo_session *s, int32_t l, float *xn_out) {
+    const lo_model *m = s->m;
+    const lo_config *c = &m->cfg;
+    struct lo_step *t = s->st;
+    int32_t h = c->hidden, d = c->head_dim, qd = c->heads * d, kvd = c->kv_heads * d;
+    const lo_layer_weights *w = &m->layers[l];
+    lo_rmsnorm(t->x, w->ln_attn, h, c->eps, t->xn);
+    float *kr = s->k_cache[l] + (size_t)s->pos * kvd;
+    float *vr = s->v_cache[l] + (size_t)s->pos * kvd;
+    lo_gemv_w(s->pool, c->weight_dtype, w->q, qd, h, t->xn, t->q);
+    lo_gemv_w(s->pool, c->weight_dtype, w->k, kvd, h, t->xn, kr);
+    lo_gemv_w(s->pool, c->weight_dtype, w->v, kvd, h, t->xn, vr);
+    lo_rope(t->q, qd, d, t->cs);
+    lo_rope(kr, kvd, d, t->cs);
+    if (s->kv_bf16) {
+        round_bf16(kr, (size_t)kvd);
+        round_bf16(vr, (size_t)kvd);
     }
-    lo_rmsnorm(x, m->norm, h, c->eps, xn);
-    lo_gemv(s->pool, m->embed, c->vocab, h, xn, logits);
+    memset(t->att, 0, sizeof(float) * (size_t)qd);
+    attn_ctx ac = {c, t->q, s->k_cache[l], s->v_cache[l], s->pos + 1, t->att};
+    pool_run(s->pool, (size_t)c->heads, attn_task, &ac);
+    lo_gemv_w(s->pool, c->weight_dtype, w->o, h, qd, t->att, t->o);
+    for (int32_t i = 0; i < h; ++i) t->x[i] += c->residual_multiplier * t->o[i];
+    lo_rmsnorm(t->x, w->ln_moe, h, c->eps, t->xn);
+    if (xn_out) memcpy(xn_out, t->xn, sizeof(float) * (size_t)h);
+}
+
+/* layer l's MoE half from a block output y computed elsewhere: x += resid * y */
+void lo_session_layer_moe(lo_session *s, int32_t l, const float *y) {
+    const lo_config *c = &s->m->cfg;
+    (void)l;
+    for (int32_t i = 0; i < c->hidden; ++i) s->st->x[i] += c->residual_multiplier * y[i];
+}
+
+/* final norm, tied lm_head, / logits_scaling (gpu_model.rs:436-439); the position advances */
+void lo_session_step_end(lo_session *s, float *logits) {
+    const lo_model *m = s->m;
+    const lo_config *c = &m->cfg;
+    struct lo_step *t = s->st;
+    lo_rmsnorm(t->x, m->norm, c->hidden, c->eps, t->xn);
+    lo_gemv(s->pool, m->embed, c->vocab, c->hidden, t->xn, logits);
     for (int32_t v = 0; v < c->vocab; ++v) logits[v] /= c->logits_scaling;
     s->pos += 1;
-    free(cs);
-    free(x);
-    free(xn);
-    free(q);
-    free(att);
-    free(o);
-    free(y);
-    free(rw);
-    free(ri);
+    step_free(s);
+}
+
+int lo_session_step(lo_session *s, int32_t token, float *logits, int32_t *ids, float *weights) {
+    const lo_model *m = s->m;
+    const lo_config *c = &m->cfg;
+    if (lo_session_step_begin(s, token)) return -1;
+    struct lo_step *t = s->st;
+    int32_t h = c->hidden;
+    for (int32_t l = 0; l < c->layers; ++l) {
+        const lo_layer_weights *w = &m->layers[l];
+        lo_session_layer_attention(s, l, NULL);
+        block_forward_impl(s->pool, c->weight_dtype, w->router, w->gate_up, w->down, c->experts, h, c->inter, c->k,
+                           t->xn, t->y, t->ri, t->rw, s->router_logits + (size_t)l * c->experts,
+                           m->router_bias ? m->router_bias + (size_t)l * c->experts : NULL);
+        lo_session_layer_moe(s, l, t->y);
+        if (ids) memcpy(ids + (size_t)l * c->k, t->ri, sizeof(int32_t) * (size_t)c->k);
+        if (weights) memcpy(weights + (size_t)l * c->k, t->rw, sizeof(float) * (size_t)c->k);
+    }
+    lo_session_step_end(s, logits);
     return 0;
 }

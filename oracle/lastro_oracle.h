@@ -126,6 +126,14 @@ void lo_session_reset(lo_session *s);
 int32_t lo_session_pos(const lo_session *s);
 /* CpuSession::step: logits [V]; ids/weights [L*k] may be NULL. Returns 0, or -1 when full. */
 int lo_session_step(lo_session *s, int32_t token, float *logits, int32_t *ids, float *weights);
+/* CpuSession::step in phases (the batched expert-parallel restatement runs the MoE block itself): begin (embedding;
+ * -1 when full or the token is out of range), then for every layer in order the attention half (xn_out [H] = the
+ * MoE block's input) and the MoE half (x += residual_multiplier * y), then end (logits [V]; the position advances).
+ * lo_session_step is these phases with the block in between. */
+int lo_session_step_begin(lo_session *s, int32_t token);
+void lo_session_layer_attention(lo_session *s, int32_t layer, float *xn_out);
+void lo_session_layer_moe(lo_session *s, int32_t layer, const float *y);
+void lo_session_step_end(lo_session *s, float *logits);
 /* append synthetic K/V rows (tests/bench only: a context of `n` positions without running the model) */
 int lo_session_fill_kv(lo_session *s, int32_t n, uint64_t seed, float stddev);
 /* the K/V cache of layer l as [pos, kvd] f32 */

@@ -108,6 +108,10 @@ def _declare(L):
         "lo_session_pos": (_I, [_P]),
         "lo_session_step": (C.c_int, [_P, _I, _P, _P, _P]),
         "lo_session_fill_kv": (C.c_int, [_P, _I, _U64, _F]),
+        "lo_session_step_begin": (C.c_int, [_P, _I]),
+        "lo_session_layer_attention": (None, [_P, _I, _P]),
+        "lo_session_layer_moe": (None, [_P, _I, _P]),
+        "lo_session_step_end": (None, [_P, _P]),
         "lo_session_k": (_P, [_P, _I]),
         "lo_session_v": (_P, [_P, _I]),
     }
@@ -360,6 +364,25 @@ class Session:
             raise ValueError("oracle step refused (KV full or token out of range)")
         c = self.model.cfg
         return self.logits.copy(), self.ids.reshape(c["layers"], c["k"]).copy(), self.w.reshape(c["layers"], c["k"]).copy()
+
+    # CpuSession::step in phases, for a caller that runs every layer's MoE block itself (oracle/ep.py): begin, then
+    # per layer in order layer_attention (returns the block's input xn) and layer_moe (x += resid * y), then end.
+    def step_begin(self, token: int):
+        if lib().lo_session_step_begin(self.h, int(token)) != 0:
+            raise ValueError("oracle step refused (KV full or token out of range)")
+
+    def layer_attention(self, layer: int) -> np.ndarray:
+        xn = np.empty(self.model.cfg["hidden"], dtype=np.float32)
+        lib().lo_session_layer_attention(self.h, layer, _ptr(xn))
+        return xn
+
+    def layer_moe(self, layer: int, y: np.ndarray):
+        y = np.ascontiguousarray(y, dtype=np.float32)
+        lib().lo_session_layer_moe(self.h, layer, _ptr(y))
+
+    def step_end(self) -> np.ndarray:
+        lib().lo_session_step_end(self.h, _ptr(self.logits))
+        return self.logits.copy()
 
     def router_logits(self) -> np.ndarray:
         """[layers, experts] router logits of the last step (bias included)."""
