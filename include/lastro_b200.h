@@ -141,12 +141,20 @@ int lastro_model_generate_until(lastro_model *model, const int32_t *prompt, int3
                                 int32_t eos, int32_t *out_ids, int32_t *n_out);
 /* device-resident greedy decode of n tokens continuing from the last token (no host copies; for timing) */
 int lastro_model_decode(lastro_model *model, int32_t n);
+/* the multi-position step (cuda_backend.rs:264-274, cpu.rs:234-297 experts_step): n consecutive positions of the
+ * model's sequence (1 <= n <= 32) in one step, causal inside the step (position i attends to every earlier position
+ * and itself), on the batched path's tensor-core GEMMs (bf16 weights).  Per-position results equal the token-by-token
+ * step up to summation order.  logits [n, V] (/ logits_scaling) and next [n] (greedy ids, last maximum) may be NULL;
+ * the position advances by n and the last position's greedy id becomes the token a device-side decode continues
+ * from.  Allocates its step scratch on first use. */
+int lastro_model_step_positions(lastro_model *model, int32_t n, const int32_t *tokens, float *logits, int32_t *next);
 /* GpuModel::reset (gpu_model.rs:244-247): position 0, page table reset */
 int lastro_model_reset(lastro_model *model);
 int lastro_model_position(const lastro_model *model, int32_t *pos);
 /* per-kernel device time of `steps` decode steps (direct launches with an event between kernels, no graph, no
- * PDL), averaged per step and summed over layers: kernel_ms[0..7] = qkv_rope, attention, oproj, router, gate_up,
- * down, head, fused_step (the whole step when the fused kernel runs it; then the others are 0).  Advances the
+ * PDL), averaged per step and summed over layers: kernel_ms[0..8] = qkv_rope, attention, oproj, router, gate_up,
+ * down, head, fused_step (the whole step when the fused kernel runs it; then the others are 0), moe (the one-launch
+ * MoE block; then gate_up and down are 0).  Advances the
  * position like lastro_model_decode.  No reference counterpart: measurement only (the reference's step_probe,
  * gpu_model.rs:275-300, times whole steps). */
 int lastro_model_profile(lastro_model *model, int32_t steps, float *kernel_ms, int32_t n_kinds);
@@ -164,6 +172,12 @@ int lastro_model_trace(lastro_model *model, int32_t steps, float *exposed_ms, fl
  * shapes fit it (default 0: on B200 it measures slower than the per-layer kernels; lastro_model_fused reports
  * whether the fused step runs) */
 int lastro_model_set_options(lastro_model *model, int32_t use_graphs, int32_t use_pdl, int32_t use_fused);
+/* the MoE block of every layer as one persistent launch (1, the default where the shapes fit: routing, gate_up and
+ * down streamed through one ring of shared memory, a grid barrier between them) or as the gate_up and down kernels
+ * (0); LASTRO_E_UNSUPPORTED for 1 when the shapes do not fit it */
+int lastro_model_set_moe(lastro_model *model, int32_t one_launch);
+/* 1 when the MoE blocks run as one launch per layer */
+int lastro_model_moe(const lastro_model *model);
 /* 1 when decode steps run as the fused step kernel (shapes fit and the option is on), else 0 */
 int lastro_model_fused(const lastro_model *model);
 /* attention kernel of the step chain with bf16 KV: tensor cores with TMA page loads (1) or the CUDA-core split kernel

@@ -387,7 +387,7 @@ __global__ void __launch_bounds__(128) brope_kv_kernel(BRopeArgs a) {
     pdl_launch();
     if (pi >= R / 2) return;
     const int sq = __ldg(a.seq + t);
-    const int pos = __ldcg(a.pos + sq);
+    const int pos = __ldcg(a.pos + sq) + (a.off ? __ldg(a.off + t) : 0);
     const float* cs = a.rope_cs + (size_t)pos * a.d;
     const int head = pi / half, j = pi - head * half;
     const int r0 = head * a.d + j, r1 = r0 + half;
@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(128) battn_kernel(BAttnArgs a) {
     pdl_launch();
     const int sqid = __ldg(a.seq + z);
     const int* page_table = a.page_table + (size_t)sqid * a.pt_stride;
-    const int len = __ldcg(a.pos + sqid) + 1;
+    const int len = __ldcg(a.pos + sqid) + (a.off ? __ldg(a.off + z) : 0) + 1;  // causal within a multi-position step
     const int p0 = (int)(((long long)len * s) / S), p1 = (int)(((long long)len * (s + 1)) / S);
     const int nrow = min(p1 - p0, a.cap);
     if (threadIdx.x == 0) {
@@ -940,7 +940,7 @@ __global__ void __launch_bounds__(1024) bargmax_kernel(BHeadArgs a) {
     const int id = (int)(uint32_t)b;
     a.next[t] = id;
     if (a.tokens) a.tokens[t] = id;
-    a.pos[__ldg(a.seq + t)] += 1;
+    atomicAdd(a.pos + __ldg(a.seq + t), 1);  // a multi-position step has several tokens of one sequence
     if (t == 0) *a.epoch_base += (unsigned int)a.layers;
 }
 
@@ -1502,11 +1502,12 @@ __global__ void __launch_bounds__(128) battn_tc_kernel(const __grid_constant__ C
     // current position (written by the previous kernel) is loaded after it.
     const int sqid = a.seq ? __ldg(a.seq + z) : 0;
     const int* page_table = a.page_table + (size_t)sqid * a.pt_stride;
-    const int len = __ldcg(a.pos + sqid) + 1;
+    const int base = __ldcg(a.pos + sqid);  // this step's first new position (of the sequence)
+    const int len = base + (a.off ? __ldg(a.off + z) : 0) + 1;  // causal within a multi-position step
     const int ntot = (len + 63) / 64;
     const int per = (ntot + S - 1) / S;
     const int pbeg = min(ntot, sp * per), npages = min(ntot, pbeg + per) - pbeg;  // this split's pages
-    const int fresh = (len - 1) / 64;  // page of the current position
+    const int fresh = base / 64;  // first page holding a row the previous kernel wrote
     auto issue = [&](int i) {  // thread 0: the split's i-th page into stage i % P
         const int pg = pbeg + i;
         const int st = i % P;

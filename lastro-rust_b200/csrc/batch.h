@@ -134,6 +134,7 @@ struct BRopeArgs {
     int ks;
     const int* seq;            // [n] sequence of each token
     const int* pos;            // [sequences] position of the current token
+    const int* off;            // optional [n]: token z writes position pos[seq[z]] + off[z] (a multi-position step)
     const float* rope_cs;      // [max_len, d]
     float* q;                  // [n, qd]
     void* k_pool;              // [pages, kv_heads, page, d]
@@ -165,6 +166,7 @@ struct BHeadArgs {
     int V, n;
     const int* seq;
     int* pos;                     // incremented per token's sequence
+    const int* off;               // optional [n] (a multi-position step: several tokens of one sequence)
     int* next;                    // [n] argmax (last maximum)
     int* tokens;                  // optional: next token fed back as the next step's input
     unsigned int* epoch_base;     // advanced by `layers` (CTA 0)
@@ -184,7 +186,8 @@ struct BAttnArgs {
     const int* page_table;     // [sequences][pt_stride]
     int pt_stride, page_size, kv_f32;
     const int* seq;            // [n] (null: one token, sequence 0)
-    const int* pos;            // [sequences]: the token attends positions 0..pos
+    const int* pos;            // [sequences]: the token attends positions 0..pos (+ off[z])
+    const int* off;            // optional [n]: token z sits off[z] positions past its sequence's position
     float* part_acc;           // [n][heads][S][d]
     float* part_ml;            // [n][heads][S][2]
     unsigned int* counters;    // [n][kv_heads], zero between launches

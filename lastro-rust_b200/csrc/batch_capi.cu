@@ -57,6 +57,10 @@ struct lastro_batch {
     std::vector<void*> opened;  // peer regions mapped from IPC handles
     std::map<int, cudaGraphExec_t> graphs;  // one per token count
     bool has_bias = false, want_hist = false;
+    // multi-position steps of a model's own sequence (lastro_model_step_positions): the KV pools, page table, position
+    // and RoPE table are the model's; token z of a step sits off[z] = z positions past the sequence's position
+    bool alias = false;
+    int* d_off = nullptr;
     // profiling: an event recorded after every launch of a direct (uncaptured) step, with the launch's kind
     std::vector<cudaEvent_t>* prof_ev = nullptr;
     std::vector<int>* prof_kind = nullptr;
@@ -189,6 +193,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         ra.ks = b->ks_qkv;
         ra.seq = b->d_seq;
         ra.pos = b->d_pos;
+        ra.off = b->d_off;
         ra.rope_cs = b->rope_cs;
         ra.q = b->q;
         ra.k_pool = b->kpool[l];
@@ -214,6 +219,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         aa.kv_f32 = ra.kv_f32;
         aa.seq = b->d_seq;
         aa.pos = b->d_pos;
+        aa.off = b->d_off;
         aa.part_acc = b->part_acc;
         aa.part_ml = b->part_ml;
         aa.counters = b->attn_counters;
@@ -339,6 +345,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
     hd.n = n;
     hd.seq = b->d_seq;
     hd.pos = b->d_pos;
+    hd.off = b->d_off;
     hd.next = b->d_next;
     hd.tokens = b->d_tok;
     hd.epoch_base = b->epoch;
@@ -413,8 +420,11 @@ int bstage(lastro_batch* b, int n, const int32_t* seq, const int32_t* tok, int s
 
 }  // namespace
 
-extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t max_len, int32_t rank, int32_t world,
-                                   lastro_batch** out) {
+namespace {
+
+// alias: a batch of up to max_seqs tokens of the model's own sequence (world 1), on the model's KV cache
+int batch_create(lastro_model* m, int32_t max_seqs, int32_t max_len, int32_t rank, int32_t world, bool alias,
+                 lastro_batch** out) {
     if (!m || !out) return LASTRO_E_ARG;
     *out = nullptr;
     lastro_ctx* ctx = m->ctx;
@@ -450,6 +460,8 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
     b->ks_o = pick_ks(d.hidden, m->qd, n_sm);
     b->pos_host.assign(max_seqs, 0);
     b->lay = x_layout(world, max_seqs, d.k, d.hidden);
+    b->alias = alias;
+    if (alias) b->max_pages = m->max_pages;
     const size_t H = d.hidden, I = d.inter, S = max_seqs, E = d.experts, k = d.k, V = d.vocab;
     const size_t pairs = (size_t)world * b->lay.cap;
     const size_t kv_elems = S * b->max_pages * kPageSize * (size_t)m->kvd;
@@ -458,10 +470,24 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
     bool bad = false;
     b->kpool.assign(d.layers, nullptr);
     b->vpool.assign(d.layers, nullptr);
-    for (int l = 0; l < d.layers && !bad; ++l)
-        bad = A.alloc(&b->kpool[l], kv_bytes) || A.alloc(&b->vpool[l], kv_bytes);
-    bad = bad || A.alloc(&b->rope_cs, (size_t)max_len * d.head_dim) || A.alloc(&b->page_table, S * b->max_pages) ||
-          A.alloc(&b->d_pos, S) || A.alloc(&b->d_seq, S) || A.alloc(&b->d_tok, S) || A.alloc(&b->d_next, S) ||
+    for (int l = 0; l < d.layers && !bad; ++l) {
+        if (alias) {
+            b->kpool[l] = m->L[l].k_pool;
+            b->vpool[l] = m->L[l].v_pool;
+        } else {
+            bad = A.alloc(&b->kpool[l], kv_bytes) || A.alloc(&b->vpool[l], kv_bytes);
+        }
+    }
+    if (alias) {
+        b->rope_cs = m->rope_cs;
+        b->page_table = m->page_table;
+        b->d_pos = m->d_pos;
+        bad = bad || A.alloc(&b->d_off, S);
+    } else {
+        bad = bad || A.alloc(&b->rope_cs, (size_t)max_len * d.head_dim) || A.alloc(&b->page_table, S * b->max_pages) ||
+              A.alloc(&b->d_pos, S);
+    }
+    bad = bad || A.alloc(&b->d_seq, S) || A.alloc(&b->d_tok, S) || A.alloc(&b->d_next, S) ||
           A.alloc(&b->d_hist, (size_t)max_len * S) || A.alloc(&b->h, S * H) || A.alloc(&b->xa_hi, S * H) ||
           A.alloc(&b->xa_lo, S * H) || A.alloc(&b->qkv_part, (size_t)b->ks_qkv * S * b->R) ||
           A.alloc(&b->q, S * m->qd) || A.alloc(&b->att, S * m->qd) || A.alloc(&b->att_hi, S * m->qd) ||
@@ -492,15 +518,23 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
     std::vector<int> pt(S * b->max_pages);
     for (size_t i = 0; i < pt.size(); ++i) pt[i] = (int)i;  // sequence q owns pages [q * max_pages, (q+1) * max_pages)
     const std::vector<float> cs = rope_table(d, max_len);
-    cudaError_t e = cudaMemcpyAsync(b->page_table, pt.data(), sizeof(int) * pt.size(), cudaMemcpyHostToDevice, s);
-    if (!e) e = cudaMemcpyAsync(b->rope_cs, cs.data(), sizeof(float) * cs.size(), cudaMemcpyHostToDevice, s);
-    if (!e) e = cudaMemsetAsync(b->d_pos, 0, sizeof(int) * S, s);
+    std::vector<int> offs(S);
+    for (size_t i = 0; i < offs.size(); ++i) offs[i] = (int)i;
+    cudaError_t e = cudaSuccess;
+    if (alias) {
+        e = cudaMemcpyAsync(b->d_off, offs.data(), sizeof(int) * S, cudaMemcpyHostToDevice, s);
+        if (!e) e = cudaMemsetAsync(b->d_seq, 0, sizeof(int) * S, s);  // every token is the model's sequence
+    } else {
+        e = cudaMemcpyAsync(b->page_table, pt.data(), sizeof(int) * pt.size(), cudaMemcpyHostToDevice, s);
+        if (!e) e = cudaMemcpyAsync(b->rope_cs, cs.data(), sizeof(float) * cs.size(), cudaMemcpyHostToDevice, s);
+        if (!e) e = cudaMemsetAsync(b->d_pos, 0, sizeof(int) * S, s);
+    }
     if (!e) e = cudaMemsetAsync(b->attn_counters, 0, sizeof(unsigned int) * S * d.kv_heads, s);
     if (!e) e = cudaMemsetAsync(b->counters, 0, sizeof(unsigned int) * 64, s);
     if (!e) e = cudaMemsetAsync(b->epoch, 0, sizeof(unsigned int), s);
     if (!e) e = cudaMemsetAsync(b->d_err, 0, sizeof(int), s);
     if (!e) e = cudaMemsetAsync(b->xreg, 0, b->lay.bytes, s);
-    for (int l = 0; l < d.layers && !e; ++l) {  // finite values past every context (the attention reads whole pages)
+    for (int l = 0; l < d.layers && !e && !alias; ++l) {  // finite values past every context (whole pages are read)
         e = cudaMemsetAsync(b->kpool[l], 0, kv_bytes, s);
         if (!e) e = cudaMemsetAsync(b->vpool[l], 0, kv_bytes, s);
     }
@@ -535,7 +569,7 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
         b->gemm_mode = 1;
     }
     if (d.kv_dtype == LASTRO_DTYPE_BF16 && m->G <= 8) {
-        const uint64_t kv_rows = (uint64_t)S * b->max_pages * d.kv_heads * kPageSize;
+        const uint64_t kv_rows = (uint64_t)(alias ? 1 : S) * b->max_pages * d.kv_heads * kPageSize;
         b->kvmaps.resize((size_t)d.layers * 2);
         bool kv_ok = true;
         for (int l = 0; l < d.layers && kv_ok; ++l)
@@ -549,6 +583,70 @@ extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t ma
     }
     ctx_retain(ctx);
     *out = b;
+    return LASTRO_OK;
+}
+
+}  // namespace
+
+extern "C" int lastro_batch_create(lastro_model* m, int32_t max_seqs, int32_t max_len, int32_t rank, int32_t world,
+                                   lastro_batch** out) {
+    return batch_create(m, max_seqs, max_len, rank, world, false, out);
+}
+
+extern "C" int lastro_model_step_positions(lastro_model* m, int32_t n, const int32_t* tokens, float* logits,
+                                           int32_t* next) {
+    if (!m) return LASTRO_E_ARG;
+    lastro_ctx* ctx = m->ctx;
+    int rc = model_check_ready(m);
+    if (rc) return rc;
+    const lastro_model_desc& d = m->d;
+    if (n < 1 || n > kMaxStepPositions || !tokens)
+        return set_err(ctx, LASTRO_E_ARG, "step of %d positions (1..%d)", n, kMaxStepPositions);
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= d.vocab) return set_err(ctx, LASTRO_E_ARG, "token %d out of range", tokens[i]);
+    if (m->pos_host + n > m->max_len) return set_err(ctx, LASTRO_E_FULL, "KV cache full (max_len %d)", m->max_len);
+    if (m->fused_ok && m->use_fused) return set_err(ctx, LASTRO_E_UNSUPPORTED, "multi-position steps run the kernel chain");
+    cudaSetDevice(ctx->device);
+    if (!m->pbatch) {
+        lastro_batch* b = nullptr;
+        rc = batch_create(m, kMaxStepPositions, m->max_len, 0, 1, true, &b);
+        if (rc) return rc;
+        rc = lastro_batch_connect(b, nullptr, (int32_t)sizeof(cudaIpcMemHandle_t));
+        if (rc) {
+            lastro_batch_destroy(b);
+            return rc;
+        }
+        m->pbatch = b;
+    }
+    lastro_batch* b = m->pbatch;
+    if (b->poisoned) {
+        m->poisoned = true;
+        return set_err(ctx, LASTRO_E_POISONED, "model unusable after an earlier error");
+    }
+    cudaStream_t s = ctx->stream;
+    memcpy(b->h_tok, tokens, sizeof(int) * n);
+    if (b->want_hist) {
+        for (auto& g : b->graphs) cudaGraphExecDestroy(g.second);
+        b->graphs.clear();
+        b->want_hist = false;
+    }
+    rc = [&]() -> int {
+        BTRY(cudaMemcpyAsync(b->d_tok, b->h_tok, sizeof(int) * n, cudaMemcpyHostToDevice, s), "stage");
+        int r = run_bstep(b, n);
+        if (r) return r;
+        // the next single-position step (or device-side decode) continues from the last position's greedy id
+        BTRY(cudaMemcpyAsync(m->d_token, b->d_next + (n - 1), sizeof(int), cudaMemcpyDeviceToDevice, s), "token");
+        if (next) BTRY(cudaMemcpyAsync(next, b->d_next, sizeof(int) * n, cudaMemcpyDeviceToHost, s), "next download");
+        if (logits)
+            BTRY(cudaMemcpyAsync(logits, b->logits, sizeof(float) * n * d.vocab, cudaMemcpyDeviceToHost, s),
+                 "logits download");
+        return bfinish(b, "multi-position step");
+    }();
+    if (rc) {
+        m->poisoned = true;
+        return rc;
+    }
+    m->pos_host += n;
     return LASTRO_OK;
 }
 

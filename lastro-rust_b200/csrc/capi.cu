@@ -345,7 +345,9 @@ int missing_tensor(lastro_model* m) {
 }
 
 // Kernel kinds of one step, in launch order within a layer (the head closes the step).
-enum { KK_QKV = 0, KK_ATTN, KK_OPROJ, KK_ROUTER, KK_GATE_UP, KK_DOWN, KK_HEAD, KK_FUSED, KK_COUNT };
+enum { KK_QKV = 0, KK_ATTN, KK_OPROJ, KK_ROUTER, KK_GATE_UP, KK_DOWN, KK_HEAD, KK_FUSED, KK_MOE, KK_COUNT };
+
+bool moe_on(const lastro_model* m) { return m->moe_ok && m->use_moe; }
 
 FusedArgs fused_args(const lastro_model* m) {
     const lastro_model_desc& d = m->d;
@@ -465,7 +467,8 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         aa.G = m->G;
         aa.d = d.head_dim;
         aa.max_len = m->max_len;
-        aa.split_cap = attn_split_cap(m->max_len);
+        aa.splits = attn_splits(m->max_len, d.kv_dtype == LASTRO_DTYPE_F32);
+        aa.split_cap = attn_split_cap(m->max_len, aa.splits);
         aa.scale = d.attention_multiplier;
         aa.trace = slot();
         if (m->attn_tc) {
@@ -506,9 +509,53 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         oa.wr_t = L.wr_t;
         oa.shares = m->op_partial;
         oa.E = d.experts;
+        if (!m->attn_tc) {  // the CUDA-core attention leaves per-split partials; the tensor-core one merges itself
+            oa.part_acc = m->part_acc;
+            oa.part_ml = m->part_ml;
+            oa.splits = aa.splits;
+            oa.heads = d.heads;
+        }
         oa.trace = slot();
         if ((e = launch_oproj(oa, s, pdl)) != cudaSuccess) return e;
         if ((e = mark(pe, s, KK_OPROJ)) != cudaSuccess) return e;
+
+        if (moe_on(m)) {
+            MoeArgs ma{};
+            ma.h = m->h;
+            ma.ln = L.ln_moe;
+            ma.rs.shares = m->op_partial;
+            ma.rs.nb = oproj_grid(d.hidden);
+            ma.rs.eps = d.eps;
+            ma.rs.ids_out = m->route_ids + (size_t)l * d.k;
+            ma.rs.weights_out = m->route_w + (size_t)l * d.k;
+            ma.rs.logits_out = m->rlogits;
+            ma.w_gu = L.gate_up;
+            ma.w_dn = L.down;
+            ma.q8 = m->q8;
+            ma.a = m->a;
+            ma.barrier = m->moe_barrier;
+            ma.err = m->d_err;
+            ma.resid = d.residual_multiplier;
+            ma.H = d.hidden;
+            ma.I = d.inter;
+            ma.k = d.k;
+            ma.E = d.experts;
+            ma.stages = m->moe.stages;
+            ma.stage_bytes = m->moe.stage_bytes;
+            ma.gu_chunk = m->moe.gu_chunk;
+            ma.slots_per_chunk = m->moe.slots_per_chunk;
+            if (l + 1 < d.layers) {  // L2 hint: the next layer's q/k/v and output-projection rows
+                const LayerDev& N = m->L[l + 1];
+                ma.pf[0] = N.wqkv;
+                ma.pf_bytes[0] = (unsigned long long)(m->qd + 2 * m->kvd) * wrow_bytes(d.hidden, m->q8);
+                ma.pf[1] = N.wo;
+                ma.pf_bytes[1] = (unsigned long long)d.hidden * wrow_bytes(m->qd, m->q8);
+            }
+            ma.trace = slot();
+            if ((e = launch_moe(ma, m->moe, s, pdl)) != cudaSuccess) return e;
+            if ((e = mark(pe, s, KK_MOE)) != cudaSuccess) return e;
+            continue;
+        }
 
         RouteShares rs{};
         rs.shares = m->op_partial;
@@ -676,7 +723,8 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
         return set_err(ctx, LASTRO_E_UNSUPPORTED, "kv dtype %d", d.kv_dtype);
     if (!(d.eps >= 0.0f) || !(d.logits_scaling != 0.0f) || !(d.rope_theta > 0.0f))
         return set_err(ctx, LASTRO_E_ARG, "bad eps / logits_scaling / rope_theta");
-    if (attn_smem(max_len, d.kv_dtype == LASTRO_DTYPE_F32) > kMaxSmemBytes)
+    if (attn_smem(max_len, d.kv_dtype == LASTRO_DTYPE_F32, attn_splits(max_len, d.kv_dtype == LASTRO_DTYPE_F32)) >
+        kMaxSmemBytes)
         return set_err(ctx, LASTRO_E_UNSUPPORTED, "max_len %d: the attention CTAs cannot stage their K/V share", max_len);
 
     cudaSetDevice(ctx->device);
@@ -714,7 +762,8 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
           A.alloc(&m->d_out_ids, (size_t)max_len + 1) || A.alloc(&m->d_prompt, (size_t)max_len + 1) ||
           A.alloc(&m->router_counter, 1) || A.alloc(&m->head_counter, 1) || A.alloc(&m->attn_counters, d.kv_heads) ||
           A.alloc(&m->head_partial, m->head_grid) || A.alloc(&m->d_err, 1) ||
-          A.alloc(&m->op_partial, (size_t)oproj_grid(d.hidden) * (E + 1));
+          A.alloc(&m->op_partial, (size_t)oproj_grid(d.hidden) * (E + 1)) || A.alloc(&m->moe_barrier, 1);
+    m->moe_ok = !bad && moe_plan(d.hidden, d.inter, d.k, m->q8, &m->moe);
     // the fused step: one CTA per SM, when the per-CTA shares of every phase fit in shared memory
     int n_sm = 0, coop = 0;
     if (cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, ctx->device) != cudaSuccess ||
@@ -756,6 +805,7 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
                     (void*)m->d_token, (void*)m->d_err})
         if (!e) e = cudaMemsetAsync(p, 0, sizeof(int), s);
     if (!e) e = cudaMemsetAsync(m->attn_counters, 0, sizeof(unsigned) * d.kv_heads, s);
+    if (!e) e = cudaMemsetAsync(m->moe_barrier, 0, sizeof(unsigned long long), s);
     std::vector<FusedLayer> fl;
     if (m->fused_ok) {
         // tag 0 is never written: zeroed exchange words never match a wait
@@ -1222,9 +1272,11 @@ extern "C" int lastro_model_trace(lastro_model* m, int32_t steps, float* exposed
     if (m->pos_host + steps > m->max_len) return set_err(ctx, LASTRO_E_FULL, "trace would overflow the KV cache");
     cudaSetDevice(ctx->device);
     cudaStream_t s = ctx->stream;
-    const int launches = 5 * m->d.layers + 1;
+    const int per_layer = moe_on(m) ? 4 : 5;
+    const int launches = per_layer * m->d.layers + 1;
     const size_t words = (size_t)launches * kTraceMaxCtas * 3;
-    if (!m->d_trace) MTRY(m->arena.alloc(&m->d_trace, words), "trace buffer");
+    const size_t words_max = (size_t)(5 * m->d.layers + 1) * kTraceMaxCtas * 3;  // either chain fits the buffer
+    if (!m->d_trace) MTRY(m->arena.alloc(&m->d_trace, words_max), "trace buffer");
     if (!m->trace_graph) {
         // the product step's kernels, launch for launch, with the stamps on; captured like the product graph
         cudaGraph_t g = nullptr;
@@ -1243,7 +1295,7 @@ extern "C" int lastro_model_trace(lastro_model* m, int32_t steps, float* exposed
     std::vector<int> kind(launches);
     for (int l = 0; l < m->d.layers; ++l) {
         const int k5[5] = {KK_QKV, KK_ATTN, KK_OPROJ, KK_GATE_UP, KK_DOWN};
-        for (int i = 0; i < 5; ++i) kind[5 * l + i] = k5[i];
+        for (int i = 0; i < per_layer; ++i) kind[per_layer * l + i] = (per_layer == 4 && i == 3) ? KK_MOE : k5[i];
     }
     kind[launches - 1] = KK_HEAD;
     std::vector<unsigned long long> h(words);
@@ -1307,6 +1359,23 @@ extern "C" int lastro_model_set_options(lastro_model* m, int32_t use_graphs, int
     return LASTRO_OK;
 }
 
+extern "C" int lastro_model_set_moe(lastro_model* m, int32_t one_launch) {
+    if (!m) return LASTRO_E_ARG;
+    if (one_launch && !m->moe_ok)
+        return set_err(m->ctx, LASTRO_E_UNSUPPORTED, "the one-launch MoE block does not fit these shapes");
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    for (cudaGraphExec_t* g : {&m->graph, &m->trace_graph})
+        if (*g) {
+            cudaGraphExecDestroy(*g);
+            *g = nullptr;
+        }
+    m->use_moe = one_launch != 0;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_model_moe(const lastro_model* m) { return m && moe_on(m) ? 1 : 0; }
+
 extern "C" int lastro_model_fused(const lastro_model* m) { return m && m->fused_ok && m->use_fused ? 1 : 0; }
 
 extern "C" int lastro_model_set_attention(lastro_model* m, int32_t tensor_cores) {
@@ -1331,6 +1400,7 @@ extern "C" void lastro_model_destroy(lastro_model* m) {
     if (!m) return;
     cudaSetDevice(m->ctx->device);
     cudaStreamSynchronize(m->ctx->stream);  // gpu_model.rs:448-455
+    if (m->pbatch) lastro_batch_destroy(m->pbatch);  // aliases the model's KV cache: destroyed first
     if (m->graph) cudaGraphExecDestroy(m->graph);
     if (m->trace_graph) cudaGraphExecDestroy(m->trace_graph);
     m->arena.release();

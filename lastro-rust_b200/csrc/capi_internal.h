@@ -172,9 +172,18 @@ struct lastro_model {
     // loads through these maps (per layer: K, V); the CUDA-core split kernel by default
     std::vector<CUtensorMap> kvmaps;
     bool attn_tc = false;
+    // the MoE block as one persistent launch per layer (moe_kernel) where the shapes fit it (default on), else the
+    // gate_up and down kernels; its grid barrier's counter
+    lastro::MoePlan moe{};
+    bool moe_ok = false, use_moe = true;
+    unsigned long long* moe_barrier = nullptr;
+    // multi-position steps (lastro_model_step_positions): a batch of the model's own sequence on its KV cache
+    lastro_batch* pbatch = nullptr;
 };
 
 namespace lastro_capi {
+// positions of one multi-position step (cuda_backend.rs:264-266: 1..=32)
+constexpr int kMaxStepPositions = 32;
 // every tensor loaded, router folds current, not poisoned (defined in capi.cu)
 int model_check_ready(lastro_model* m);
 }  // namespace lastro_capi

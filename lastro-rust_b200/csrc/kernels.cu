@@ -13,6 +13,8 @@
 //   RMSNorm  model.rs:141-145   RoPE rotate_half model.rs:147-158   attention model.rs:203-222
 //   routing  block.rs:79-89     SwiGLU cpu.rs:64-68               experts cpu.rs:115-150
 //   step     model.rs:181-243   argmax (last maximum) bin/m1b-gulosa.rs:22-24
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "ops.cuh"
@@ -138,7 +140,9 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
 // copies (one thread per page run); after it the CTA reads q and the new row.  Each lane scores one position against
 // the G query heads of the group (GQA: K/V read once for all G heads), warps keep online-softmax partials and merge
 // them in shared memory, and the CTA writes its partial (m, l, acc) per query head; the output-projection kernel
-// merges the splits as it loads the attention output (flash-decoding).  Positions past `len` are never read.
+// merges the splits as it loads the attention output (flash-decoding), so no CTA here waits for another.  A lane
+// reads its row's 16-byte chunks starting at chunk (lane mod chunks): the 8 lanes of one shared-memory phase then hit
+// 8 different bank groups instead of one.  Positions past `len` are never read.
 // ------------------------------------------------------------------------------------------------------------------
 constexpr int kAttnWarps = 8;
 
@@ -157,8 +161,6 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
     __shared__ float wm[NW][G], wl[NW][G];
     __shared__ __align__(16) float wacc[NW][G][D];
     __shared__ __align__(8) uint64_t bar;
-    __shared__ float cw[kAttnSplits][G], cden[G];
-    __shared__ bool is_last;
     const int NS = gridDim.x, s = blockIdx.x, kvh = blockIdx.y, z = blockIdx.z;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int HD = a.kv_heads * G * D;  // q / output floats of one token
@@ -166,7 +168,6 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
     const int* page_table = a.page_table + (size_t)seq_id * a.pt_stride;
     float* part_acc = a.part_acc + (size_t)z * HD * NS;
     float* part_ml = a.part_ml + (size_t)z * a.kv_heads * G * NS * 2;
-    float* att_out = a.att_out + (size_t)z * HD;
 
     // the position is written only by the previous step's head kernel: constant for the whole step
     const int pos = __ldcg(a.pos + seq_id);
@@ -227,7 +228,8 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
         if (valid) {
             const uint4* kr = reinterpret_cast<const uint4*>(kt + (size_t)r * RB);
 #pragma unroll
-            for (int c = 0; c < CH; ++c) {
+            for (int cr = 0; cr < CH; ++cr) {
+                const int c = (cr + lane) & (CH - 1);
                 const uint4 kc = kr[c];
                 // the row's elements are unpacked once and used for all G heads
                 float kf[8];
@@ -249,7 +251,16 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
                 constexpr int EPC = KV_F32 ? 4 : 8;
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    const float* qg = &sq[g][c * EPC];
+                    float qg[EPC];
+                    const float4* q4 = reinterpret_cast<const float4*>(&sq[g][c * EPC]);
+#pragma unroll
+                    for (int e4 = 0; e4 < EPC / 4; ++e4) {
+                        const float4 t = q4[e4];
+                        qg[4 * e4] = t.x;
+                        qg[4 * e4 + 1] = t.y;
+                        qg[4 * e4 + 2] = t.z;
+                        qg[4 * e4 + 3] = t.w;
+                    }
 #pragma unroll
                     for (int e = 0; e < EPC; ++e) sc[g] = fmaf(qg[e], kf[e], sc[g]);
                 }
@@ -320,55 +331,6 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
             part_ml[hs * 2 + 1] = L;
         }
     }
-    // the last CTA of this KV head merges the NS splits of its G heads: every load (each thread's NS partial outputs,
-    // and one (m, l) pair per (head, split)) in one round, the per-head max and denominator by 16-lane shuffles
-    static_assert(kAttnSplits == 16, "the merge reduces one head's splits within 16 lanes");
-    if (!last_block_arrives(a.counters + (size_t)z * a.kv_heads + kvh, (unsigned int)NS, &is_last)) return;
-    constexpr int NT = 32 * kAttnWarps, KO = (G * D + NT - 1) / NT;
-    const float* pa = part_acc + (size_t)kvh * G * kAttnSplits * D;
-    float v[KO][kAttnSplits];
-#pragma unroll
-    for (int k = 0; k < KO; ++k) {
-        const int t = threadIdx.x + k * NT;
-        const int g = t / D, dim = t - (t / D) * D;
-#pragma unroll
-        for (int sp = 0; sp < kAttnSplits; ++sp)
-            v[k][sp] = t < G * D ? __ldcg(pa + ((size_t)g * kAttnSplits + sp) * D + dim) : 0.0f;
-    }
-    const int i = threadIdx.x;
-    const float2 mlv = i < G * kAttnSplits ? __ldcg(reinterpret_cast<const float2*>(part_ml) + (size_t)kvh * G * kAttnSplits + i)
-                                           : make_float2(-INFINITY, 0.0f);
-    if (i < ((G * kAttnSplits + 31) & ~31)) {  // whole warps
-        float M = mlv.x;
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o, 16));
-        const float e = mlv.x == -INFINITY ? 0.0f : expf(mlv.x - M);
-        float dn = mlv.y * e;
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) dn += __shfl_xor_sync(0xffffffffu, dn, o, 16);
-        if (i < G * kAttnSplits) {
-            cw[i % kAttnSplits][i / kAttnSplits] = e;
-            if (i % kAttnSplits == 0) cden[i / kAttnSplits] = dn;
-        }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int k = 0; k < KO; ++k) {
-        const int t = threadIdx.x + k * NT;
-        if (t >= G * D) break;
-        const int g = t / D, dim = t - (t / D) * D;
-        float num = 0.0f;
-#pragma unroll
-        for (int sp = 0; sp < kAttnSplits; ++sp) num = fmaf(v[k][sp], cw[sp][g], num);
-        const float o = num / cden[g];
-        const size_t oi = ((size_t)kvh * G + g) * D + dim;
-        att_out[oi] = o;
-        if (a.att_hi) {
-            const uint16_t hi = f32_to_bf16_rne(o);
-            a.att_hi[(size_t)z * HD + oi] = hi;
-            a.att_lo[(size_t)z * HD + oi] = f32_to_bf16_rne(__fsub_rn(o, __uint_as_float((uint32_t)hi << 16)));
-        }
-    }
 }
 
 template <int NCH, bool Q8>
@@ -423,6 +385,41 @@ __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
 constexpr int kOpWarps = 16;
 constexpr int kOpRows = 2 * kOpWarps;
 
+// The attention output from the attention kernel's per-split partials (flash-decoding): for head h,
+// att[h] = sum_s acc[h][s] * e_s / sum_s l[h][s] * e_s with e_s = exp(m[h][s] - max_s m[h][s]), splits in order.  Every
+// partial is loaded at once into shared memory (one round of L2 latency), then weighted.  xs receives [heads * D].
+template <int BLOCK>
+LDEV void merge_attention(const OprojArgs& a, float* xs, float* pacc, float* pml, float* pw) {
+    constexpr int D = kHeadDim;
+    const int S = a.splits, HS = a.heads * S;
+    const int n4 = HS * D / 4;
+    const float4* src = reinterpret_cast<const float4*>(a.part_acc);
+    for (int i = threadIdx.x; i < n4; i += BLOCK) reinterpret_cast<float4*>(pacc)[i] = __ldcg(src + i);
+    for (int i = threadIdx.x; i < HS; i += BLOCK)
+        reinterpret_cast<float2*>(pml)[i] = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + i);
+    __syncthreads();
+    for (int h = threadIdx.x; h < a.heads; h += BLOCK) {
+        float M = -INFINITY;
+        for (int sp = 0; sp < S; ++sp) M = fmaxf(M, pml[2 * (h * S + sp)]);
+        float L = 0.0f;
+        for (int sp = 0; sp < S; ++sp) {
+            const float m = pml[2 * (h * S + sp)];
+            const float e = m == -INFINITY ? 0.0f : expf(m - M);
+            pw[h * S + sp] = e;
+            L = fmaf(pml[2 * (h * S + sp) + 1], e, L);
+        }
+        pw[HS + h] = L;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < a.heads * D; i += BLOCK) {
+        const int h = i / D, dim = i - h * D;
+        float num = 0.0f;
+        for (int sp = 0; sp < S; ++sp) num = fmaf(pacc[(h * S + sp) * D + dim], pw[h * S + sp], num);
+        xs[i] = num / pw[HS + h];
+    }
+    __syncthreads();
+}
+
 template <int NCH, bool Q8>
 __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
     const CtaTrace trace_(a.trace);
@@ -448,7 +445,15 @@ __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
     trace_.released();
     const float ha = (lane == 0 && ra < a.H) ? __ldcg(a.h + ra) : 0.0f;
     const float hb = (lane == 0 && rb < a.H) ? __ldcg(a.h + rb) : 0.0f;
-    copy_to_smem<BLOCK>(a.att, a.qd, xs);
+    if (a.part_acc) {
+        // after xs and the router operand: the partials [heads*S*D], their (m, l) [heads*S*2], weights and sums
+        float* pacc = wrs + (a.route ? (size_t)kOpRows * a.E : 0);
+        float* pml = pacc + (size_t)a.heads * a.splits * kHeadDim;
+        float* pw = pml + (size_t)a.heads * a.splits * 2;
+        merge_attention<BLOCK>(a, xs, pacc, pml, pw);
+    } else {
+        copy_to_smem<BLOCK>(a.att, a.qd, xs);
+    }
     float4 xa[NCH], xb[NCH];
     x_to_regs<NCH>(xs, a.qd, lane, xa, xb);
     const float oa = warp_sum(wa.dot_regs(xa, xb, a.qd, lane));
@@ -665,6 +670,194 @@ __global__ void __launch_bounds__(kGsThreads, 1) gate_up_stream_kernel(GateUpArg
         const float u = warp_sum(smem_row_dot_w<NCH, Q8>(wrows + (size_t)(2 * q + 1) * rbh, xa, xb, a.H, lane));
         if (lane == 0) a.a[p0 + q] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
     }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// moe: the whole MoE block of the model step (routing, gate_up + SwiGLU, down + weighted combine + residual) as one
+// persistent launch of one CTA per SM: 8 consumer warps and a producer warp.  The routing is reduced from the output
+// projection's shares (bitwise the same in every CTA).  Then the producer's lane 0 streams, through a ring of shared
+// memory stages (TMA bulk copies completing on `full` barriers, recycled through `empty` barriers), first this CTA's
+// range of (gate row, up row) pairs of the k chosen experts, then -- as soon as stages free up -- the CTA's rows of
+// the k experts' down matrices: the down weights stream while the gate_up pairs are still being computed, so HBM
+// stays busy across the whole block.  Consumers compute a = silu(g) * u (cpu.rs:64-68) into global memory, meet at a
+// grid barrier (every CTA is resident: one per SM), then each warp takes one routing slot j, holds a_j in registers
+// and computes d_j = W_d[e_j] . a_j for the CTA's rows; the rows' y = sum_j w_j d_j is summed in routing order
+// (cpu.rs:141-148) and h += resid * y (model.rs:230-232).  Every wait is bounded and reports through the error word.
+// ------------------------------------------------------------------------------------------------------------------
+constexpr int kMoeWarps = 8;
+constexpr int kMoeThreads = 32 * (kMoeWarps + 1);
+constexpr int kMoeMaxStages = 8;
+constexpr int kMoeMaxRows = 32;  // down rows of one CTA (H / grid)
+constexpr uint64_t kMoeBarrierNs = 2000000000ull;  // bound of the grid barrier: 2 s
+
+LDEV void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+LDEV void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"r"(32 * kMoeWarps) : "memory"); }
+
+LDEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+template <int NCH, int NCI, bool Q8>
+__global__ void __launch_bounds__(kMoeThreads, 1) moe_kernel(MoeArgs a) {
+    const CtaTrace trace_(a.trace);
+    constexpr int BLOCK = kMoeThreads, NW = kMoeWarps;
+    constexpr int NV = Vec<NCH, BLOCK>::NV;
+    extern __shared__ __align__(128) unsigned char ring[];  // [stages][stage_bytes]
+    __shared__ __align__(8) uint64_t full[kMoeMaxStages], empty[kMoeMaxStages];
+    __shared__ float red[BLOCK];
+    __shared__ int sid[kMaxTopK];
+    __shared__ float sval[kMaxTopK], sw[kMaxTopK], s_r;
+    __shared__ __align__(16) float xs[kGsMaxH];
+    __shared__ float part[kMaxTopK][kMoeMaxRows];
+    __shared__ int s_ok;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int G = gridDim.x, c = blockIdx.x;
+    const size_t rbh = wrow_bytes(a.H, Q8), rbi = wrow_bytes(a.I, Q8);
+    const int total = a.k * a.I;
+    const int p0 = (int)((long long)total * c / G), np = (int)((long long)total * (c + 1) / G) - p0;
+    const int r0 = (int)((long long)a.H * c / G), nr = (int)((long long)a.H * (c + 1) / G) - r0;
+    const int S = a.stages, CP = a.gu_chunk, SPC = a.slots_per_chunk;
+    const int n1 = (np + CP - 1) / CP, n2 = (a.k + SPC - 1) / SPC;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], NW);
+        }
+        s_ok = 1;
+    }
+    float4 ln[NV];
+    vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
+
+    pdl_wait();
+    pdl_launch();
+    trace_.released();
+
+    float4 v[NV];
+    vec_load_cg<BLOCK, NV>(a.h, a.H, v);  // in flight while the routing is reduced
+    const float r = route_from_shares<BLOCK>(a.rs, a.E, a.k, a.H, red, sid, sval, sw, &s_r, c == 0);
+
+    // producer: one chunk of the ring; chunks [0, n1) are gate_up pairs, [n1, n1 + n2) down rows
+    const unsigned char* wgu = static_cast<const unsigned char*>(a.w_gu);
+    const unsigned char* wdn = static_cast<const unsigned char*>(a.w_dn);
+    auto issue = [&](int i) {
+        const int st = i % S;
+        unsigned char* dst = ring + (size_t)st * a.stage_bytes;
+        if (i < n1) {
+            // pairs [q0, q1) of this CTA's range: gate rows at dst, up rows after them, in runs within one slot
+            const int q0 = i * CP, q1 = min(np, q0 + CP), cnt = q1 - q0;
+            mbar_expect_tx(&full[st], (uint32_t)(2 * cnt * rbh));
+            for (int qa = q0; qa < q1;) {
+                const int p = p0 + qa, slot = p / a.I, j = p - slot * a.I;
+                const int qb = min(q1, qa + (a.I - j));  // the run stays inside one slot
+                const int e = min(max(sid[slot], 0), a.E - 1);
+                const unsigned char* base = wgu + (size_t)e * 2 * a.I * rbh;
+                const uint32_t bytes = (uint32_t)((qb - qa) * rbh);
+                bulk_g2s(dst + (size_t)(qa - q0) * rbh, base + (size_t)j * rbh, bytes, &full[st]);
+                bulk_g2s(dst + (size_t)(cnt + qa - q0) * rbh, base + (size_t)(a.I + j) * rbh, bytes, &full[st]);
+                qa = qb;
+            }
+        } else {
+            // slots [j0, j1): rows [r0, r0 + nr) of each chosen expert's down matrix
+            const int j0 = (i - n1) * SPC, j1 = min(a.k, j0 + SPC);
+            mbar_expect_tx(&full[st], (uint32_t)((j1 - j0) * nr * rbi));
+            for (int j = j0; j < j1 && nr > 0; ++j) {
+                const int e = min(max(sid[j], 0), a.E - 1);
+                bulk_g2s(dst + (size_t)(j - j0) * nr * rbi, wdn + ((size_t)e * a.H + r0) * rbi, (uint32_t)(nr * rbi),
+                         &full[st]);
+            }
+        }
+    };
+    // the first S chunks go out at once (fresh stages, nothing to wait for)
+    const int n_all = n1 + n2, first = min(S, n_all);
+    if (warp == NW && lane == 0)
+        for (int i = 0; i < first; ++i) issue(i);
+    // xn = ln * (h * r) (model.rs:141-145), every thread its share
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int i = threadIdx.x + k * BLOCK;
+        if (4 * i < a.H) reinterpret_cast<float4*>(xs)[i] = ln_times(ln[k], v[k], r);
+    }
+    __syncthreads();
+    if (warp == NW) {
+        // the rest of the chunks, each into a stage the consumers have released
+        if (lane != 0) return;
+        for (int i = first; i < n_all; ++i) {
+            if (!mbar_wait(&empty[i % S], (uint32_t)((i / S - 1) & 1), a.err, 21)) return;
+            issue(i);
+        }
+        // the next layer's dense weights into L2 while this block computes (qkv_rope then reads them from L2)
+        prefetch_share_l2(a.pf[0], a.pf_bytes[0], c, G);
+        prefetch_share_l2(a.pf[1], a.pf_bytes[1], c, G);
+        return;
+    }
+
+    // ---- consumers ---------------------------------------------------------------------------------------------
+    bool ok = true;
+    {
+        float4 xa[NCH], xb[NCH];
+        x_to_regs<NCH>(xs, a.H, lane, xa, xb);
+        for (int i = 0; i < n1 && ok; ++i) {
+            const int st = i % S;
+            ok = mbar_wait(&full[st], (uint32_t)((i / S) & 1), a.err, 22);
+            if (!ok) break;
+            const unsigned char* src = ring + (size_t)st * a.stage_bytes;
+            const int q0 = i * CP, cnt = min(np, q0 + CP) - q0;
+            for (int q = warp; q < cnt; q += NW) {
+                const float g = warp_sum(smem_row_dot_w<NCH, Q8>(src + (size_t)q * rbh, xa, xb, a.H, lane));
+                const float u = warp_sum(smem_row_dot_w<NCH, Q8>(src + (size_t)(cnt + q) * rbh, xa, xb, a.H, lane));
+                if (lane == 0) a.a[p0 + q0 + q] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+    }
+    if (!ok) atomicExch(&s_ok, 0);
+    // grid barrier: every CTA's activations written before any CTA reads them
+    __threadfence();
+    consumers_sync();
+    if (threadIdx.x == 0 && s_ok) {
+        const unsigned long long old = atomicAdd(a.barrier, 1ull);
+        const unsigned long long target = (old / (unsigned long long)G + 1ull) * (unsigned long long)G;
+        const uint64_t t0 = global_ns();
+        while (ld_acquire_u64(a.barrier) < target) {
+            if (*reinterpret_cast<volatile int*>(a.err) || global_ns() - t0 > kMoeBarrierNs) {
+                atomicCAS(a.err, 0, 23);
+                s_ok = 0;
+                break;
+            }
+            __nanosleep(32);
+        }
+    }
+    consumers_sync();
+    if (!s_ok) return;
+    // down: warp w takes slot j = w: a_j in registers, its rows from the ring
+    for (int j = warp; j < a.k; j += NW) {
+        const int i = n1 + j / SPC, st = i % S;
+        if (!mbar_wait(&full[st], (uint32_t)((i / S) & 1), a.err, 24)) {
+            atomicExch(&s_ok, 0);
+            break;
+        }
+        float4 xa[NCI], xb[NCI];
+        x_to_regs_global<NCI>(a.a + (size_t)j * a.I, a.I, lane, xa, xb);
+        const unsigned char* src = ring + (size_t)st * a.stage_bytes + (size_t)(j - (j / SPC) * SPC) * nr * rbi;
+        for (int rr = 0; rr < nr; ++rr) {
+            const float d = warp_sum(smem_row_dot_w<NCI, Q8>(src + (size_t)rr * rbi, xa, xb, a.I, lane));
+            if (lane == 0) part[j][rr] = d;
+        }
+    }
+    consumers_sync();
+    if (!s_ok || threadIdx.x >= nr) return;
+    float acc = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j)
+        if (j < a.k) acc = __fadd_rn(acc, __fmul_rn(sw[j], part[j][threadIdx.x]));
+    float* hp = a.h + r0 + threadIdx.x;
+    *hp = __fadd_rn(__ldcg(hp), __fmul_rn(a.resid, acc));
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -972,15 +1165,24 @@ cudaError_t launch_qkv_rope(const QkvArgs& a, cudaStream_t s, bool pdl) {
     LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(qkv_rope_kernel<N, false, false>, grid, block, smem, s, pdl, a));
 }
 
-int attn_split_cap(int max_len) { return (max_len + kAttnSplits - 1) / kAttnSplits + 1; }
+int attn_split_cap(int max_len, int splits) { return (max_len + splits - 1) / splits + 1; }
 
-size_t attn_smem(int max_len, int kv_f32) { return (size_t)2 * attn_split_cap(max_len) * kHeadDim * (kv_f32 ? 4 : 2); }
+size_t attn_smem(int max_len, int kv_f32, int splits) {
+    return (size_t)2 * attn_split_cap(max_len, splits) * kHeadDim * (kv_f32 ? 4 : 2);
+}
+
+// context splits of the batch-1 attention: 8 while a split's rows fit about one pass of the CTA's 8 warps (256
+// positions each at max_len 2048) and its staging fits shared memory, else 16
+int attn_splits(int max_len, int kv_f32) {
+    return (max_len <= 8 * 32 * kAttnWarps + 512 && attn_smem(max_len, kv_f32, 8) <= kMaxSmemBytes) ? 8 : kAttnSplits;
+}
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
-    if (a.d != kHeadDim || a.split_cap != attn_split_cap(a.max_len)) return cudaErrorInvalidValue;
-    const size_t smem = attn_smem(a.max_len, a.kv_f32);
+    if (a.d != kHeadDim || a.splits < 1 || a.splits > kAttnSplits || a.split_cap != attn_split_cap(a.max_len, a.splits))
+        return cudaErrorInvalidValue;
+    const size_t smem = attn_smem(a.max_len, a.kv_f32, a.splits);
     if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
-    const dim3 grid(kAttnSplits, a.kv_heads, a.seq ? a.tokens : 1), block(32 * kAttnWarps);
+    const dim3 grid(a.splits, a.kv_heads, a.seq ? a.tokens : 1), block(32 * kAttnWarps);
 #define LASTRO_ATTN_G(GV)                                                                                  \
     case GV: {                                                                                             \
         auto k = a.kv_f32 ? attention_kernel<true, GV> : attention_kernel<false, GV>;                      \
@@ -1004,7 +1206,10 @@ int oproj_grid(int H) { return (H + kOpRows - 1) / kOpRows; }
 cudaError_t launch_oproj(const OprojArgs& a, cudaStream_t s, bool pdl) {
     const dim3 grid(oproj_grid(a.H)), block(32 * kOpWarps);
     if (a.route && a.E > kMaxExperts) return cudaErrorInvalidValue;
-    const size_t smem = sizeof(float) * (a.qd + (a.route ? (size_t)kOpRows * a.E : 0));
+    if (a.part_acc && (a.heads * kHeadDim != a.qd || a.splits < 1)) return cudaErrorInvalidValue;
+    const size_t merge = a.part_acc ? (size_t)a.heads * a.splits * (kHeadDim + 3) + a.heads : 0;
+    const size_t smem = sizeof(float) * (a.qd + (a.route ? (size_t)kOpRows * a.E : 0) + merge);
+    if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
 #define LASTRO_OP(N)                                                                  \
     {                                                                                 \
         auto k = a.q8 ? oproj_kernel<N, true> : oproj_kernel<N, false>;               \
@@ -1093,7 +1298,7 @@ cudaError_t launch_gate_up_stream(const GateUpArgs& a, cudaStream_t s, bool pdl)
 }
 
 cudaError_t launch_gate_up(const GateUpArgs& a, cudaStream_t s, bool pdl) {
-    if (a.rs.shares) return launch_gate_up_stream(a, s, pdl);
+    if (a.rs.shares && a.stream) return launch_gate_up_stream(a, s, pdl);
     if (a.I % kGuPairs) return cudaErrorInvalidValue;
     const dim3 grid(a.k * (a.I / kGuPairs)), block(256);
     const size_t smem = gate_up_smem(a.H, a.q8);
@@ -1116,6 +1321,57 @@ cudaError_t launch_gate_up(const GateUpArgs& a, cudaStream_t s, bool pdl) {
     default: return cudaErrorInvalidValue;
     }
 #undef LASTRO_GU
+}
+
+bool moe_plan(int H, int I, int k, int q8, MoePlan* out) {
+    if (H > kGsMaxH || H % 8 || I % 8 || k < 1 || k > kMaxTopK || chunks_for(H) > 8 || chunks_for(I) > 2) return false;
+    const int total = k * I;
+    int grid = sm_count();
+    grid = std::min(grid, std::min(total, H));
+    const size_t rbh = wrow_bytes(H, q8), rbi = wrow_bytes(I, q8);
+    const int nr_max = (H + grid - 1) / grid;
+    if (nr_max > kMoeMaxRows) return false;
+    int cp = 8;  // pairs per gate_up chunk: one per consumer warp
+    while (cp > 1 && (size_t)cp * 2 * rbh > 64 * 1024) --cp;
+    size_t stage = std::max((size_t)cp * 2 * rbh, (size_t)nr_max * rbi);
+    stage = (stage + 127) & ~(size_t)127;
+    const size_t budget = kMaxSmemBytes - 16 * 1024;  // the kernel's static shared memory stays below 16 KB
+    const int stages = (int)std::min<size_t>(kMoeMaxStages, budget / stage);
+    const int spc = (int)std::min<size_t>((size_t)k, stage / ((size_t)nr_max * rbi));
+    const int n2 = (k + spc - 1) / spc;
+    if (stages < 2 || spc < 1 || n2 > stages) return false;  // every down chunk must reuse a gate_up chunk's stage
+    out->grid = grid;
+    out->stages = stages;
+    out->stage_bytes = (int)stage;
+    out->gu_chunk = cp;
+    out->slots_per_chunk = spc;
+    out->smem = (size_t)stages * stage;
+    return true;
+}
+
+cudaError_t launch_moe(const MoeArgs& a, const MoePlan& p, cudaStream_t s, bool pdl) {
+    if (a.stages != p.stages || a.stage_bytes != p.stage_bytes || !a.barrier) return cudaErrorInvalidValue;
+#define LASTRO_MOE(N, NI)                                                                                    \
+    {                                                                                                        \
+        auto k = a.q8 ? moe_kernel<N, NI, true> : moe_kernel<N, NI, false>;                                  \
+        cudaError_t e = allow_smem(k, p.smem);                                                               \
+        return e != cudaSuccess ? e : launch_ex(k, dim3(p.grid), dim3(kMoeThreads), p.smem, s, pdl, a);      \
+    }
+#define LASTRO_MOE_I(N)                                                                                      \
+    if (chunks_for(a.I) == 1) LASTRO_MOE(N, 1) else LASTRO_MOE(N, 2)
+    switch (chunks_for(a.H)) {
+    case 1: LASTRO_MOE_I(1)
+    case 2: LASTRO_MOE_I(2)
+    case 3: LASTRO_MOE_I(3)
+    case 4: LASTRO_MOE_I(4)
+    case 5: LASTRO_MOE_I(5)
+    case 6: LASTRO_MOE_I(6)
+    case 7: LASTRO_MOE_I(7)
+    case 8: LASTRO_MOE_I(8)
+    default: return cudaErrorInvalidValue;
+    }
+#undef LASTRO_MOE_I
+#undef LASTRO_MOE
 }
 
 cudaError_t launch_down(const DownArgs& a, cudaStream_t s, bool pdl) {

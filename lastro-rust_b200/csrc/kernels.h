@@ -62,7 +62,8 @@ struct AttnArgs {
     float* att_out;          // [heads * d], merged by the last CTA of each KV head
     int* err;
     int kv_heads, G, d;
-    int max_len, split_cap;  // split_cap = attn_split_cap(max_len): K/V rows one CTA stages
+    int max_len, split_cap;  // split_cap = attn_split_cap(max_len, splits): K/V rows one CTA stages
+    int splits;              // context splits (grid x): attn_splits(max_len, kv_f32)
     float scale;
     // batched decode (grid z = the launch's tokens, null seq = batch-1): token z reads q and writes att_out at
     // z * heads * d and its partials/counters at its own offsets, and attends the cache of sequence seq[z] (page-table
@@ -86,6 +87,11 @@ struct OprojArgs {
     const float* wr_t;      // [H, E]: router weight x MoE norm weight, transposed (launch_router_fold)
     float* shares;          // [oproj_grid(H), E + 1]
     int E;
+    // optional: the attention's per-split partials (part_acc [heads, splits, d], part_ml [heads, splits, 2]), merged
+    // into the attention output on load; null: att holds the merged output
+    const float* part_acc;
+    const float* part_ml;
+    int splits, heads;
     unsigned long long* trace;  // in-graph timeline stamps of this launch (CtaTrace), or null
 };
 
@@ -129,6 +135,7 @@ struct GateUpArgs {
     // optional (streaming kernel of the model step): the down weights [E, H, I], whose chosen slabs are hinted into L2
     const void* down_w;
     size_t down_row_bytes;
+    int stream;  // the streaming kernel (one wave, all rows in flight): measured slower on C3, kept selectable
     unsigned long long* trace;  // in-graph timeline stamps of this launch (CtaTrace), or null
 };
 
@@ -149,6 +156,34 @@ struct DownArgs {
     unsigned long long pf_bytes[2];
     unsigned long long* trace;  // in-graph timeline stamps of this launch (CtaTrace), or null
 };
+
+// The MoE block of the model step in one persistent launch (moe_kernel): routing from the output projection's shares,
+// gate_up + SwiGLU, down + combine + residual, streamed through a ring of shared-memory stages.
+struct MoeArgs {
+    float* h;              // residual [H]: read for the MoE norm, updated in place (h += resid * y)
+    const float* ln;       // MoE norm weight [H]
+    RouteShares rs;
+    const void* w_gu;      // [E, 2I, H] (bf16 or Q8_0 rows)
+    const void* w_dn;      // [E, H, I]
+    int q8;
+    float* a;              // [k, I] SwiGLU activations (global: every CTA reads every slot's after the grid barrier)
+    unsigned long long* barrier;  // grid barrier counter: zero at creation, grows by the grid size per launch
+    int* err;
+    float resid;
+    int H, I, k, E;
+    int stages, stage_bytes, gu_chunk, slots_per_chunk;  // ring geometry (moe_plan)
+    const void* pf[2];                                   // optional: byte ranges hinted into L2 (the next layer's)
+    unsigned long long pf_bytes[2];
+    unsigned long long* trace;
+};
+
+struct MoePlan {
+    int grid, stages, stage_bytes, gu_chunk, slots_per_chunk;
+    size_t smem;
+};
+// ring geometry of moe_kernel for these shapes on the current device; false when the shapes do not fit it
+bool moe_plan(int H, int I, int k, int q8, MoePlan* out);
+cudaError_t launch_moe(const MoeArgs& a, const MoePlan& p, cudaStream_t s, bool pdl);
 
 struct HeadArgs {
     const float* h;                 // [H]
@@ -283,8 +318,9 @@ constexpr size_t kMaxSmemBytes = 220 * 1024;  // dynamic shared memory one CTA m
 
 // attention: splits (CTAs) per KV head and the shared memory they stage K/V rows in
 constexpr int kAttnSplits = 16;
-int attn_split_cap(int max_len);
-size_t attn_smem(int max_len, int kv_f32);
+int attn_split_cap(int max_len, int splits);
+size_t attn_smem(int max_len, int kv_f32, int splits);
+int attn_splits(int max_len, int kv_f32);
 
 // shared memory the grouped expert kernels need (host-side checks)
 size_t gate_up_smem(int H, int q8 = 0);

@@ -68,6 +68,7 @@ EXPORTS = {
     "lastro_model_fill_kv_synthetic": (C.c_int, [C.c_void_p, C.c_int32, C.c_uint64, C.c_float]),
     "lastro_model_read_kv": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
     "lastro_model_step": (C.c_int, [C.c_void_p, C.c_int32] + [C.c_void_p] * 4),
+    "lastro_model_step_positions": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
     "lastro_model_generate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
     "lastro_model_generate_until": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
                                               C.POINTER(C.c_int32)]),
@@ -79,6 +80,8 @@ EXPORTS = {
                                      C.c_void_p]),
     "lastro_model_set_options": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32]),
     "lastro_model_fused": (C.c_int, [C.c_void_p]),
+    "lastro_model_set_moe": (C.c_int, [C.c_void_p, C.c_int32]),
+    "lastro_model_moe": (C.c_int, [C.c_void_p]),
     "lastro_model_set_attention": (C.c_int, [C.c_void_p, C.c_int32]),
     "lastro_model_destroy": (None, [C.c_void_p]),
     "lastro_checkpoint_open": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p), C.c_char_p, C.c_int32]),
@@ -371,6 +374,23 @@ class GpuModel:
                 self._ids.reshape(c["layers"], c["k"]).copy() if want_routes else None,
                 self._w.reshape(c["layers"], c["k"]).copy() if want_routes else None)
 
+    def step_positions(self, tokens, want_logits: bool = True):
+        """Multi-position step: (logits [n, V] or None, next ids [n]) for n = len(tokens) <= 32 consecutive positions."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        n = t.size
+        lg = np.empty((n, self.cfg["vocab"]), np.float32) if want_logits else None
+        nxt = np.empty(n, np.int32)
+        self.ctx.check(lib().lastro_model_step_positions(self.h, n, _p(t), _p(lg), _p(nxt)))
+        return lg, nxt
+
+    def prefill(self, prompt, chunk: int = 32):
+        """Feed a prompt through multi-position steps of up to `chunk` positions; returns the last greedy id."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        nxt = None
+        for i in range(0, p.size, chunk):
+            _, nxt = self.step_positions(p[i:i + chunk], want_logits=False)
+        return int(nxt[-1])
+
     def generate(self, prompt, n_new: int) -> np.ndarray:
         p = np.ascontiguousarray(prompt, dtype=np.int32)
         out = np.empty(max(n_new, 1), np.int32)
@@ -397,7 +417,7 @@ class GpuModel:
         self.ctx.check(lib().lastro_model_position(self.h, C.byref(v)))
         return v.value
 
-    KERNELS = ("qkv_rope", "attention", "oproj", "router", "gate_up", "down", "head", "fused_step")
+    KERNELS = ("qkv_rope", "attention", "oproj", "router", "gate_up", "down", "head", "fused_step", "moe")
 
     def profile(self, steps: int) -> dict:
         """Per-kernel device ms per step (summed over layers), measured with events between direct launches."""
@@ -418,6 +438,14 @@ class GpuModel:
 
     def set_options(self, graphs: bool = True, pdl: bool = True, fused: bool = False):
         self.ctx.check(lib().lastro_model_set_options(self.h, int(graphs), int(pdl), int(fused)))
+
+    def set_moe(self, one_launch: bool = True):
+        """The MoE block as one persistent launch per layer (default where it fits) or the gate_up + down kernels."""
+        self.ctx.check(lib().lastro_model_set_moe(self.h, int(one_launch)))
+
+    @property
+    def moe(self) -> bool:
+        return bool(lib().lastro_model_moe(self.h))
 
     def set_attention(self, tensor_cores: bool = True):
         """bf16 KV: attention on tensor cores or the CUDA-core split kernel (the default: faster at batch 1)."""

@@ -220,8 +220,8 @@ def test_model_loaded_from_a_checkpoint_decodes_like_the_loaded_weights(gpu_ctx,
         assert na == nb and np.array_equal(la, lb) and np.array_equal(ia, ib)
     ck.close()
     for sub, kw, msg in (("drop", dict(drop="model.layers.1.self_attn.o_proj.weight"), "absent"),
-                         ("shape", dict(reshape=("model.layers.0.self_attn.q_proj.weight",
-                                                 [cfg["hidden"], cfg["heads"] * cfg["head_dim"]])), "shape")):
+                         ("shape", dict(reshape=("model.layers.0.self_attn.k_proj.weight",
+                                                 [cfg["hidden"], cfg["kv_heads"] * cfg["head_dim"]])), "shape")):
         dd = tmp_path / sub
         dd.mkdir()
         write_model_checkpoint(str(dd), cfg, w, **kw)

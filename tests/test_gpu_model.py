@@ -376,3 +376,33 @@ def test_generate_until_stops_after_the_end_of_text(gpu_ctx):
     assert e.value.code == LB.E_ARG
     ref.close()
     m.close()
+
+
+@pytest.mark.parametrize("which", ["tiny", "tiny768", "tiny_q8", "c3"])
+def test_one_launch_moe_equals_the_gate_up_and_down_kernels_bitwise(gpu_ctx, which):
+    """The MoE block as one persistent launch (routing, gate_up and down streamed through one ring, a grid barrier
+    between them) computes every dot in the same order as the gate_up + down kernels: logits and routes bitwise
+    equal over 20 positions, bf16 and Q8_0 weights, up to the 3B shape."""
+    if which == "c3":
+        c = CFG.C3_3B
+        cfg = c["model"]
+        models = []
+        for _ in range(2):
+            m = LB.GpuModel(gpu_ctx, cfg, 64, kv_dtype="bf16")
+            m.fill_synthetic(c["weight_seed"], CFG.WEIGHT_STD, 0.0)
+            models.append(m)
+    else:
+        cfg = {"tiny": CFG.TINY, "tiny768": CFG.TINY_768, "tiny_q8": dict(CFG.TINY, weight_dtype="q8_0")}[which]
+        w = S.model_weights_q8(cfg, 12) if which == "tiny_q8" else reference_tiny_weights(cfg)
+        models = [gpu_model(gpu_ctx, cfg, w, 64, "bf16") for _ in range(2)]
+    a, b = models
+    assert a.moe  # the default where the shapes fit
+    b.set_moe(False)
+    assert not b.moe
+    for t in range(20):
+        tok = (t * 7 + 3) % cfg["vocab"]
+        la, na, ia, wa = a.step(tok)
+        lb, nb, ib, wb = b.step(tok)
+        assert np.array_equal(la, lb) and na == nb and np.array_equal(ia, ib) and np.array_equal(wa, wb), f"position {t}"
+    a.close()
+    b.close()
