@@ -167,15 +167,26 @@ int lastro_model_profile(lastro_model *model, int32_t steps, float *kernel_ms, i
  * position like lastro_model_decode.  No reference counterpart: measurement only. */
 int lastro_model_trace(lastro_model *model, int32_t steps, float *exposed_ms, float *span_ms, float *wait_ms,
                        int32_t n_kinds, float *step_ms);
+/* the stamps of launch `launch` (in step order) of the last step lastro_model_trace timed: for each of up to 1024
+ * CTAs, 8 words of global-timer ns (start, release from griddepcontrol.wait, exit, then 5 of the kernel's own
+ * milestones; 0 where not stamped); words >= 8192.  Diagnostics only. */
+int lastro_model_trace_raw(const lastro_model *model, int32_t launch, unsigned long long *out, int32_t words);
 /* tuning: use CUDA graphs (default 1), programmatic dependent launch between the per-layer kernels (default 1),
  * and the fused step -- the whole step as one persistent cooperative launch, one CTA per SM -- where the model's
  * shapes fit it (default 0: on B200 it measures slower than the per-layer kernels; lastro_model_fused reports
  * whether the fused step runs) */
 int lastro_model_set_options(lastro_model *model, int32_t use_graphs, int32_t use_pdl, int32_t use_fused);
-/* the MoE block of every layer as one persistent launch (1, the default where the shapes fit: routing, gate_up and
- * down streamed through one ring of shared memory, a grid barrier between them) or as the gate_up and down kernels
- * (0); LASTRO_E_UNSUPPORTED for 1 when the shapes do not fit it */
+/* the MoE block of every layer as one persistent launch (1: routing, gate_up and down streamed through one ring of
+ * shared memory, a grid barrier between them) or as the gate_up and down kernels (0, the default: faster on C3);
+ * LASTRO_E_UNSUPPORTED for 1 when the shapes do not fit it */
 int lastro_model_set_moe(lastro_model *model, int32_t one_launch);
+/* tuning of the batch-1 attention kernel (CUDA-core, the default): attn_splits context splits per KV head (8 or 16;
+ * 0 picks 8 when a split's rows fit one pass of the CTA, else 16) and how the splits are merged (0: by the last CTA
+ * of each KV head, through global memory, the default; 1: by the output projection as it loads the attention output;
+ * 2: the splits of a KV head are one thread-block cluster that merges them in distributed shared memory, splits 8);
+ * oproj_smem: the output projection's weight rows staged in shared memory by 256-thread CTAs (1) or held in the
+ * registers of 512-thread CTAs (0, the default); results are bitwise the same either way */
+int lastro_model_set_tuning(lastro_model *model, int32_t attn_splits, int32_t attn_merge, int32_t oproj_smem);
 /* 1 when the MoE blocks run as one launch per layer */
 int lastro_model_moe(const lastro_model *model);
 /* 1 when decode steps run as the fused step kernel (shapes fit and the option is on), else 0 */

@@ -413,7 +413,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
     cudaError_t e;
     int launch = 0;
     auto slot = [&]() -> unsigned long long* {
-        return trace ? trace + (size_t)(launch++) * kTraceMaxCtas * 3 : nullptr;
+        return trace ? trace + (size_t)(launch++) * kTraceMaxCtas * kTraceWords : nullptr;
     };
     if ((e = mark(pe, s)) != cudaSuccess) return e;
     if (m->fused_ok && m->use_fused) {
@@ -467,8 +467,10 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         aa.G = m->G;
         aa.d = d.head_dim;
         aa.max_len = m->max_len;
-        aa.splits = attn_splits(m->max_len, d.kv_dtype == LASTRO_DTYPE_F32);
+        aa.splits = m->attn_splits;
         aa.split_cap = attn_split_cap(m->max_len, aa.splits);
+        aa.merge = m->attn_merge == 0 ? 1 : 0;
+        aa.cluster = m->attn_merge == 2 ? 1 : 0;
         aa.scale = d.attention_multiplier;
         aa.trace = slot();
         if (m->attn_tc) {
@@ -509,7 +511,9 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         oa.wr_t = L.wr_t;
         oa.shares = m->op_partial;
         oa.E = d.experts;
-        if (!m->attn_tc) {  // the CUDA-core attention leaves per-split partials; the tensor-core one merges itself
+        oa.smem_weights = m->oproj_smem && !(!m->attn_tc && m->attn_merge == 1) ? 1 : 0;
+        oa.err = m->d_err;
+        if (!m->attn_tc && m->attn_merge == 1) {  // the attention left its per-split partials
             oa.part_acc = m->part_acc;
             oa.part_ml = m->part_ml;
             oa.splits = aa.splits;
@@ -723,8 +727,7 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
         return set_err(ctx, LASTRO_E_UNSUPPORTED, "kv dtype %d", d.kv_dtype);
     if (!(d.eps >= 0.0f) || !(d.logits_scaling != 0.0f) || !(d.rope_theta > 0.0f))
         return set_err(ctx, LASTRO_E_ARG, "bad eps / logits_scaling / rope_theta");
-    if (attn_smem(max_len, d.kv_dtype == LASTRO_DTYPE_F32, attn_splits(max_len, d.kv_dtype == LASTRO_DTYPE_F32)) >
-        kMaxSmemBytes)
+    if (attn_smem(max_len, d.kv_dtype == LASTRO_DTYPE_F32, kAttnSplits) > kMaxSmemBytes)
         return set_err(ctx, LASTRO_E_UNSUPPORTED, "max_len %d: the attention CTAs cannot stage their K/V share", max_len);
 
     cudaSetDevice(ctx->device);
@@ -1274,8 +1277,8 @@ extern "C" int lastro_model_trace(lastro_model* m, int32_t steps, float* exposed
     cudaStream_t s = ctx->stream;
     const int per_layer = moe_on(m) ? 4 : 5;
     const int launches = per_layer * m->d.layers + 1;
-    const size_t words = (size_t)launches * kTraceMaxCtas * 3;
-    const size_t words_max = (size_t)(5 * m->d.layers + 1) * kTraceMaxCtas * 3;  // either chain fits the buffer
+    const size_t words = (size_t)launches * kTraceMaxCtas * kTraceWords;
+    const size_t words_max = (size_t)(5 * m->d.layers + 1) * kTraceMaxCtas * kTraceWords;  // either chain fits
     if (!m->d_trace) MTRY(m->arena.alloc(&m->d_trace, words_max), "trace buffer");
     if (!m->trace_graph) {
         // the product step's kernels, launch for launch, with the stamps on; captured like the product graph
@@ -1311,7 +1314,7 @@ extern "C" int lastro_model_trace(lastro_model* m, int32_t steps, float* exposed
         for (int i = 0; i < launches; ++i) {
             unsigned long long t0 = ~0ull, rel = ~0ull, t1 = 0;
             for (int c = 0; c < kTraceMaxCtas; ++c) {
-                const unsigned long long* w = &h[((size_t)i * kTraceMaxCtas + c) * 3];
+                const unsigned long long* w = &h[((size_t)i * kTraceMaxCtas + c) * kTraceWords];
                 if (!w[0]) continue;
                 t0 = std::min(t0, w[0]);
                 if (w[1]) rel = std::min(rel, w[1]);
@@ -1331,6 +1334,7 @@ extern "C" int lastro_model_trace(lastro_model* m, int32_t steps, float* exposed
     }
     rc = finish(m, "trace");
     if (rc) return rc;
+    m->trace_host.assign(h.begin(), h.begin() + words);  // the last traced step, for lastro_model_trace_raw
     m->pos_host += steps;
     for (int k = 0; k < KK_COUNT; ++k) {
         exposed_ms[k] = (float)(ex[k] / steps * 1e-6);
@@ -1338,6 +1342,14 @@ extern "C" int lastro_model_trace(lastro_model* m, int32_t steps, float* exposed
         wait_ms[k] = (float)(wt[k] / steps * 1e-6);
     }
     *step_ms = (float)(step_acc / steps * 1e-6);
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_model_trace_raw(const lastro_model* m, int32_t launch, unsigned long long* out, int32_t words) {
+    if (!m || !out || launch < 0) return LASTRO_E_ARG;
+    const size_t per = (size_t)kTraceMaxCtas * kTraceWords;
+    if ((size_t)(launch + 1) * per > m->trace_host.size() || (size_t)words < per) return LASTRO_E_ARG;
+    memcpy(out, m->trace_host.data() + (size_t)launch * per, per * sizeof(unsigned long long));
     return LASTRO_OK;
 }
 
@@ -1375,6 +1387,28 @@ extern "C" int lastro_model_set_moe(lastro_model* m, int32_t one_launch) {
 }
 
 extern "C" int lastro_model_moe(const lastro_model* m) { return m && moe_on(m) ? 1 : 0; }
+
+extern "C" int lastro_model_set_tuning(lastro_model* m, int32_t attn_splits, int32_t attn_merge, int32_t oproj_smem) {
+    if (!m) return LASTRO_E_ARG;
+    const int f32 = m->d.kv_dtype == LASTRO_DTYPE_F32;
+    const int splits = attn_splits == 0 ? attn_splits_default(m->max_len, f32) : attn_splits;
+    if (splits != 8 && splits != kAttnSplits) return set_err(m->ctx, LASTRO_E_ARG, "attention splits %d (8 or 16)", splits);
+    if (attn_merge < 0 || attn_merge > 2 || (attn_merge == 2 && splits > 8))
+        return set_err(m->ctx, LASTRO_E_ARG, "attention merge %d with %d splits", attn_merge, splits);
+    if (attn_smem(m->max_len, f32, splits) > kMaxSmemBytes)
+        return set_err(m->ctx, LASTRO_E_UNSUPPORTED, "%d attention splits do not fit max_len %d", splits, m->max_len);
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    for (cudaGraphExec_t* g : {&m->graph, &m->trace_graph})
+        if (*g) {
+            cudaGraphExecDestroy(*g);
+            *g = nullptr;
+        }
+    m->attn_splits = splits;
+    m->attn_merge = attn_merge;
+    m->oproj_smem = oproj_smem != 0;
+    return LASTRO_OK;
+}
 
 extern "C" int lastro_model_fused(const lastro_model* m) { return m && m->fused_ok && m->use_fused ? 1 : 0; }
 

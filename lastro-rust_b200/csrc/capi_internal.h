@@ -161,6 +161,7 @@ struct lastro_model {
     // in-graph timeline (lastro_model_trace): stamp buffer and the step graph captured with the stamps on
     unsigned long long* d_trace = nullptr;
     cudaGraphExec_t trace_graph = nullptr;
+    std::vector<unsigned long long> trace_host;  // the last traced step's stamps
     // fused step (one persistent launch per step) when the shapes fit it
     bool fused_ok = false, use_fused = false;
     lastro::FusedLayout flay{};
@@ -175,7 +176,12 @@ struct lastro_model {
     // the MoE block as one persistent launch per layer (moe_kernel) where the shapes fit it (default on), else the
     // gate_up and down kernels; its grid barrier's counter
     lastro::MoePlan moe{};
-    bool moe_ok = false, use_moe = true;
+    // batch-1 attention: context splits (8 or 16) and where the splits are merged (the attention kernel's last CTA, or
+    // the output projection as it loads them); lastro_model_set_tuning
+    int attn_splits = 16;
+    int attn_merge = 0;  // 0: the attention's last CTA per KV head, 1: the output projection, 2: a cluster per KV head
+    bool oproj_smem = false;  // the output projection's weights staged in shared memory (oproj_smem_kernel)
+    bool moe_ok = false, use_moe = false;
     unsigned long long* moe_barrier = nullptr;
     // multi-position steps (lastro_model_step_positions): a batch of the model's own sequence on its KV cache
     lastro_batch* pbatch = nullptr;

@@ -21,9 +21,9 @@ LDEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 LDEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---- in-graph timeline (lastro_model_trace) -----------------------------------------------------------------------
-// With a non-null trace base, every CTA of a launch stamps the global timer (ns) into its own three words: [0] when
-// thread 0 starts, [1] when thread 0 passes griddepcontrol.wait, [2] the latest exit of any warp (atomicMax by lane 0
-// of each warp; the destructor runs on every return path).  The host reduces over CTAs: min start, min release, max
+// With a non-null trace base, every CTA of a launch stamps the global timer (ns) into its own kTraceWords words: [0]
+// when thread 0 starts, [1] when thread 0 passes griddepcontrol.wait, [2] the latest exit of any warp (atomicMax by
+// lane 0 of each warp; the destructor runs on every return path), [3..] the kernel's own milestones (mark).  The host reduces over CTAs: min start, min release, max
 // end.  A null base (the product path) costs one predicated branch per stamp.
 LDEV unsigned long long global_ns() {
     unsigned long long t;
@@ -35,11 +35,15 @@ struct CtaTrace {
     unsigned long long* p;
     LDEV explicit CtaTrace(unsigned long long* base) : p(nullptr) {
         const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-        if (base && cta < (unsigned)kTraceMaxCtas) p = base + 3 * (size_t)cta;
+        if (base && cta < (unsigned)kTraceMaxCtas) p = base + kTraceWords * (size_t)cta;
         if (p && threadIdx.x == 0) p[0] = global_ns();
     }
     LDEV void released() const {
         if (p && threadIdx.x == 0) p[1] = global_ns();
+    }
+    // a kernel's own milestone i (< kTraceMarks) as thread `tid` reaches it (diagnostics of the phases inside a launch)
+    LDEV void mark(int i, unsigned tid = 0) const {
+        if (p && threadIdx.x == tid) p[3 + i] = global_ns();
     }
     LDEV ~CtaTrace() {
         if (p && (threadIdx.x & 31) == 0) atomicMax(p + 2, global_ns());

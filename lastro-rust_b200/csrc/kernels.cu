@@ -13,6 +13,8 @@
 //   RMSNorm  model.rs:141-145   RoPE rotate_half model.rs:147-158   attention model.rs:203-222
 //   routing  block.rs:79-89     SwiGLU cpu.rs:64-68               experts cpu.rs:115-150
 //   step     model.rs:181-243   argmax (last maximum) bin/m1b-gulosa.rs:22-24
+#include <cooperative_groups.h>
+
 #include <algorithm>
 
 #include "common.cuh"
@@ -35,6 +37,27 @@ cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStrea
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// the same with thread-block clusters of `cluster_x` CTAs along x
+template <typename Kern, typename... Args>
+cudaError_t launch_cluster_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, int cluster_x,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cluster_x;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
@@ -101,6 +124,7 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
         vec_load_cg<BLOCK, NV>(a.h, a.H, v);
     }
     norm_regs<BLOCK, NV>(v, ln, a.H, a.eps, xs, red);
+    trace_.mark(0);
     if (!active) return;
 
     const float x1 = warp_sum(w0.dot(xs, a.H, lane));
@@ -140,13 +164,12 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
 // copies (one thread per page run); after it the CTA reads q and the new row.  Each lane scores one position against
 // the G query heads of the group (GQA: K/V read once for all G heads), warps keep online-softmax partials and merge
 // them in shared memory, and the CTA writes its partial (m, l, acc) per query head; the output-projection kernel
-// merges the splits as it loads the attention output (flash-decoding), so no CTA here waits for another.  A lane
-// reads its row's 16-byte chunks starting at chunk (lane mod chunks): the 8 lanes of one shared-memory phase then hit
-// 8 different bank groups instead of one.  Positions past `len` are never read.
+// merges the splits as it loads the attention output (flash-decoding), or the last CTA of each KV head merges them
+// (lastro_model_set_tuning).  Positions past `len` are never read.
 // ------------------------------------------------------------------------------------------------------------------
 constexpr int kAttnWarps = 8;
 
-template <bool KV_F32, int G>
+template <bool KV_F32, int G, bool CL>
 __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) {
     const CtaTrace trace_(a.trace);
     constexpr int D = kHeadDim;
@@ -161,6 +184,10 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
     __shared__ float wm[NW][G], wl[NW][G];
     __shared__ __align__(16) float wacc[NW][G][D];
     __shared__ __align__(8) uint64_t bar;
+    __shared__ float cw[kAttnSplits][G], cden[G];
+    __shared__ bool is_last;
+    __shared__ float cM[G], cL[G];            // CL: this CTA's partial, read by the other CTAs of its cluster
+    __shared__ __align__(16) float cA[G][D];
     const int NS = gridDim.x, s = blockIdx.x, kvh = blockIdx.y, z = blockIdx.z;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int HD = a.kv_heads * G * D;  // q / output floats of one token
@@ -168,6 +195,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
     const int* page_table = a.page_table + (size_t)seq_id * a.pt_stride;
     float* part_acc = a.part_acc + (size_t)z * HD * NS;
     float* part_ml = a.part_ml + (size_t)z * a.kv_heads * G * NS * 2;
+    float* att_out = a.att_out + (size_t)z * HD;
 
     // the position is written only by the previous step's head kernel: constant for the whole step
     const int pos = __ldcg(a.pos + seq_id);
@@ -209,6 +237,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
     }
     __syncthreads();
     const bool ok = mbar_wait(&bar, 0, a.err, 3);
+    trace_.mark(0);
 
     float m[G], l[G], acc0[G], acc1[G];
 #pragma unroll
@@ -228,8 +257,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
         if (valid) {
             const uint4* kr = reinterpret_cast<const uint4*>(kt + (size_t)r * RB);
 #pragma unroll
-            for (int cr = 0; cr < CH; ++cr) {
-                const int c = (cr + lane) & (CH - 1);
+            for (int c = 0; c < CH; ++c) {
                 const uint4 kc = kr[c];
                 // the row's elements are unpacked once and used for all G heads
                 float kf[8];
@@ -251,16 +279,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
                 constexpr int EPC = KV_F32 ? 4 : 8;
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    float qg[EPC];
-                    const float4* q4 = reinterpret_cast<const float4*>(&sq[g][c * EPC]);
-#pragma unroll
-                    for (int e4 = 0; e4 < EPC / 4; ++e4) {
-                        const float4 t = q4[e4];
-                        qg[4 * e4] = t.x;
-                        qg[4 * e4 + 1] = t.y;
-                        qg[4 * e4 + 2] = t.z;
-                        qg[4 * e4 + 3] = t.w;
-                    }
+                    const float* qg = &sq[g][c * EPC];
 #pragma unroll
                     for (int e = 0; e < EPC; ++e) sc[g] = fmaf(qg[e], kf[e], sc[g]);
                 }
@@ -324,13 +343,100 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
                 A = fmaf(wacc[w][g][dim], e, A);
             }
         }
-        const size_t hs = (size_t)(kvh * G + g) * NS + s;
-        part_acc[hs * D + dim] = A;
-        if (dim == 0) {
-            part_ml[hs * 2] = M;
-            part_ml[hs * 2 + 1] = L;
+        if (CL) {
+            cA[g][dim] = A;
+            if (dim == 0) {
+                cM[g] = M;
+                cL[g] = L;
+            }
+        } else {
+            const size_t hs = (size_t)(kvh * G + g) * NS + s;
+            part_acc[hs * D + dim] = A;
+            if (dim == 0) {
+                part_ml[hs * 2] = M;
+                part_ml[hs * 2 + 1] = L;
+            }
         }
     }
+    trace_.mark(1);
+    if (CL) {
+        // the NS splits of this KV head are one thread-block cluster: after a cluster barrier each CTA merges its
+        // share of the G*D outputs from every CTA's partial in distributed shared memory (splits in order); a second
+        // barrier keeps every CTA's shared memory alive until the others have read it
+        namespace cg = cooperative_groups;
+        cg::cluster_group cl = cg::this_cluster();
+        cl.sync();
+        const int per = (G * D + NS - 1) / NS;
+        for (int t = threadIdx.x; t < per; t += blockDim.x) {
+            const int o = s * per + t;
+            if (o >= G * D) break;
+            const int g = o / D, dim = o - (o / D) * D;
+            float mq[kAttnSplits];
+            float M = -INFINITY;
+#pragma unroll
+            for (int q = 0; q < kAttnSplits; ++q) {
+                mq[q] = q < NS ? *cl.map_shared_rank(&cM[g], q) : -INFINITY;
+                M = fmaxf(M, mq[q]);
+            }
+            float dn = 0.0f, num = 0.0f;
+#pragma unroll
+            for (int q = 0; q < kAttnSplits; ++q) {
+                if (q >= NS || mq[q] == -INFINITY) continue;
+                const float e = expf(mq[q] - M);
+                dn = fmaf(*cl.map_shared_rank(&cL[g], q), e, dn);
+                num = fmaf(*cl.map_shared_rank(&cA[g][dim], q), e, num);
+            }
+            att_out[((size_t)kvh * G + g) * D + dim] = num / dn;
+        }
+        cl.sync();
+        trace_.mark(2);
+        return;
+    }
+    if (!a.merge) return;  // the output projection merges the partials as it loads them
+    // else the last CTA of this KV head merges the NS (<= 16) splits of its G heads: every load (each thread's NS
+    // partial outputs, and one (m, l) pair per (head, split)) in one round, the per-head max and denominator by
+    // 16-lane shuffles over the splits (padded with empty ones)
+    if (!last_block_arrives(a.counters + (size_t)z * a.kv_heads + kvh, (unsigned int)NS, &is_last)) return;
+    constexpr int NT = 32 * kAttnWarps, KO = (G * D + NT - 1) / NT;
+    const float* pa = part_acc + (size_t)kvh * G * NS * D;
+    float v[KO][kAttnSplits];
+#pragma unroll
+    for (int k = 0; k < KO; ++k) {
+        const int t = threadIdx.x + k * NT;
+        const int g = t / D, dim = t - (t / D) * D;
+#pragma unroll
+        for (int sp = 0; sp < kAttnSplits; ++sp)
+            v[k][sp] = (t < G * D && sp < NS) ? __ldcg(pa + ((size_t)g * NS + sp) * D + dim) : 0.0f;
+    }
+    const int i = threadIdx.x, ig = i / kAttnSplits, isp = i - ig * kAttnSplits;
+    const float2 mlv = (ig < G && isp < NS)
+                           ? __ldcg(reinterpret_cast<const float2*>(part_ml) + (size_t)(kvh * G + ig) * NS + isp)
+                           : make_float2(-INFINITY, 0.0f);
+    if (i < ((G * kAttnSplits + 31) & ~31)) {  // whole warps
+        float M = mlv.x;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o, 16));
+        const float e = mlv.x == -INFINITY ? 0.0f : expf(mlv.x - M);
+        float dn = mlv.y * e;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) dn += __shfl_xor_sync(0xffffffffu, dn, o, 16);
+        if (i < G * kAttnSplits) {
+            cw[isp][ig] = e;
+            if (isp == 0) cden[ig] = dn;
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < KO; ++k) {
+        const int t = threadIdx.x + k * NT;
+        if (t >= G * D) break;
+        const int g = t / D, dim = t - (t / D) * D;
+        float num = 0.0f;
+#pragma unroll
+        for (int sp = 0; sp < kAttnSplits; ++sp) num = fmaf(v[k][sp], cw[sp][g], num);
+        att_out[((size_t)kvh * G + g) * D + dim] = num / cden[g];
+    }
+    trace_.mark(2);
 }
 
 template <int NCH, bool Q8>
@@ -454,6 +560,7 @@ __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
     } else {
         copy_to_smem<BLOCK>(a.att, a.qd, xs);
     }
+    trace_.mark(0);
     float4 xa[NCH], xb[NCH];
     x_to_regs<NCH>(xs, a.qd, lane, xa, xb);
     const float oa = warp_sum(wa.dot_regs(xa, xb, a.qd, lane));
@@ -465,6 +572,74 @@ __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
         hs[2 * warp] = ra < a.H ? na : 0.0f;
         hs[2 * warp + 1] = rb < a.H ? nb : 0.0f;
     }
+    trace_.mark(1);
+    if (!a.route) return;
+    __syncthreads();
+    const int E1 = a.E + 1;
+    if (threadIdx.x < a.E) {
+        float p = 0.0f;
+#pragma unroll 8
+        for (int i = 0; i < kOpRows; ++i) p = fmaf(wrs[i * a.E + threadIdx.x], hs[i], p);
+        a.shares[(size_t)blockIdx.x * E1 + threadIdx.x] = p;
+    } else if (threadIdx.x == a.E) {
+        float ss = 0.0f;
+#pragma unroll 8
+        for (int i = 0; i < kOpRows; ++i) ss = fmaf(hs[i], hs[i], ss);
+        a.shares[(size_t)blockIdx.x * E1 + a.E] = ss;
+    }
+}
+
+// The same output projection with its 32 weight rows staged in shared memory by one bulk copy issued before
+// griddepcontrol.wait, and 256 threads (8 warps x 4 rows): about a third of the registers of the register-resident
+// form, so its CTAs fit on the SMs beside the attention kernel's and their weights land while the attention still
+// runs.  Every row's dot runs in the same order as oproj_kernel's: bitwise the same results.
+template <int NCH, bool Q8>
+__global__ void __launch_bounds__(256) oproj_smem_kernel(OprojArgs a) {
+    const CtaTrace trace_(a.trace);
+    constexpr int BLOCK = 256, NW = BLOCK / 32, RPW = kOpRows / NW;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    const size_t rbq = wrow_bytes(a.qd, Q8);
+    unsigned char* wrows = smem_raw;                                   // [kOpRows][rbq]
+    float* xs = reinterpret_cast<float*>(wrows + (size_t)kOpRows * rbq);  // [qd]
+    float* wrs = xs + a.qd;                                             // [kOpRows, E]
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ float orow[kOpRows], hs[kOpRows];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int r0 = blockIdx.x * kOpRows, nrows = min(kOpRows, a.H - r0);
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_expect_tx(&bar, (uint32_t)(nrows * rbq));
+        bulk_g2s(wrows, static_cast<const unsigned char*>(a.w) + (size_t)r0 * rbq, (uint32_t)(nrows * rbq), &bar);
+    }
+    if (a.route) {
+        const int n = kOpRows * a.E;
+        for (int t = threadIdx.x; t < n; t += BLOCK) wrs[t] = (r0 + t / a.E < a.H) ? __ldg(a.wr_t + (size_t)r0 * a.E + t) : 0.0f;
+    }
+    pdl_wait();
+    pdl_launch();
+    trace_.released();
+    const float hv = threadIdx.x < nrows ? __ldcg(a.h + r0 + threadIdx.x) : 0.0f;
+    copy_to_smem<BLOCK>(a.att, a.qd, xs);  // ends with __syncthreads: the barrier's initialisation is visible too
+    trace_.mark(0);
+    float4 xa[NCH], xb[NCH];
+    x_to_regs<NCH>(xs, a.qd, lane, xa, xb);
+    const bool ok = mbar_wait(&bar, 0, a.err, 5);  // on a give-up the CTA still meets its barriers, then leaves
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+        const int row = warp * RPW + i;
+        if (ok && row < nrows) {
+            const float o = warp_sum(smem_row_dot_w<NCH, Q8>(wrows + (size_t)row * rbq, xa, xb, a.qd, lane));
+            if (lane == 0) orow[row] = o;
+        }
+    }
+    __syncthreads();
+    if (!ok) return;
+    if (threadIdx.x < kOpRows) {
+        const float nh = threadIdx.x < nrows ? __fadd_rn(hv, __fmul_rn(a.resid, orow[threadIdx.x])) : 0.0f;
+        if (threadIdx.x < nrows) a.h[r0 + threadIdx.x] = nh;
+        hs[threadIdx.x] = nh;
+    }
+    trace_.mark(1);
     if (!a.route) return;
     __syncthreads();
     const int E1 = a.E + 1;
@@ -542,10 +717,11 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
     float r = 0.0f;
     if (fused) {
         vec_load_cg<BLOCK, NV>(a.x, a.H, v);  // in flight while the routing is reduced
-        r = route_from_shares<BLOCK>(a.rs, a.E, a.k, a.H, red, sid, sval, sw, &s_r, blockIdx.x == 0);
+        r = route_from_shares<BLOCK>(a.rs, a.E, a.k, a.H, red, sid, sval, sw, &s_r, blockIdx.x == 0, &trace_);
     } else {
         __syncthreads();  // barrier init visible to every waiting thread
     }
+    trace_.mark(0);
     if (threadIdx.x == 0) {
         // expert id, clamped so that a stale id can never address outside the weights
         const int e = min(max(fused ? sid[slot] : __ldcg(a.ids + slot), 0), a.E - 1);
@@ -574,6 +750,7 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
 #pragma unroll
     for (int st = 0; st < 2; ++st) {
         if (!mbar_wait(&bar[st], 0, a.err, 1)) return;
+        trace_.mark(1 + st);
         const int pr = st * HALF + warp;
         const float g = warp_sum(smem_row_dot_w<NCH, Q8>(wg + (size_t)pr * rbh, xa, xb, a.H, lane));
         const float u = warp_sum(smem_row_dot_w<NCH, Q8>(wu + (size_t)pr * rbh, xa, xb, a.H, lane));
@@ -740,6 +917,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_kernel(MoeArgs a) {
     float4 v[NV];
     vec_load_cg<BLOCK, NV>(a.h, a.H, v);  // in flight while the routing is reduced
     const float r = route_from_shares<BLOCK>(a.rs, a.E, a.k, a.H, red, sid, sval, sw, &s_r, c == 0);
+    trace_.mark(0);
 
     // producer: one chunk of the ring; chunks [0, n1) are gate_up pairs, [n1, n1 + n2) down rows
     const unsigned char* wgu = static_cast<const unsigned char*>(a.w_gu);
@@ -816,6 +994,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_kernel(MoeArgs a) {
             if (lane == 0) mbar_arrive(&empty[st]);
         }
     }
+    trace_.mark(1);
     if (!ok) atomicExch(&s_ok, 0);
     // grid barrier: every CTA's activations written before any CTA reads them
     __threadfence();
@@ -834,6 +1013,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_kernel(MoeArgs a) {
         }
     }
     consumers_sync();
+    trace_.mark(2);
     if (!s_ok) return;
     // down: warp w takes slot j = w: a_j in registers, its rows from the ring
     for (int j = warp; j < a.k; j += NW) {
@@ -851,6 +1031,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_kernel(MoeArgs a) {
         }
     }
     consumers_sync();
+    trace_.mark(3);
     if (!s_ok || threadIdx.x >= nr) return;
     float acc = 0.0f;
 #pragma unroll
@@ -910,6 +1091,7 @@ __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
     float4 xa[NCI], xb[NCI];
     if (warp < a.k) x_to_regs_global<NCI>(a.a + (size_t)warp * a.I, a.I, lane, xa, xb);
     const bool ok = mbar_wait(&bar, 0, a.err, 2);
+    trace_.mark(0);
     if (ok && warp < a.k) {
 #pragma unroll
         for (int r = 0; r < R; ++r) {
@@ -1173,19 +1355,25 @@ size_t attn_smem(int max_len, int kv_f32, int splits) {
 
 // context splits of the batch-1 attention: 8 while a split's rows fit about one pass of the CTA's 8 warps (256
 // positions each at max_len 2048) and its staging fits shared memory, else 16
-int attn_splits(int max_len, int kv_f32) {
+int attn_splits_default(int max_len, int kv_f32) {
     return (max_len <= 8 * 32 * kAttnWarps + 512 && attn_smem(max_len, kv_f32, 8) <= kMaxSmemBytes) ? 8 : kAttnSplits;
 }
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     if (a.d != kHeadDim || a.splits < 1 || a.splits > kAttnSplits || a.split_cap != attn_split_cap(a.max_len, a.splits))
         return cudaErrorInvalidValue;
+    if (a.cluster && (a.splits > 8 || a.seq)) return cudaErrorInvalidValue;  // portable cluster size; batch-1 only
     const size_t smem = attn_smem(a.max_len, a.kv_f32, a.splits);
     if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
     const dim3 grid(a.splits, a.kv_heads, a.seq ? a.tokens : 1), block(32 * kAttnWarps);
 #define LASTRO_ATTN_G(GV)                                                                                  \
     case GV: {                                                                                             \
-        auto k = a.kv_f32 ? attention_kernel<true, GV> : attention_kernel<false, GV>;                      \
+        if (a.cluster) {                                                                                   \
+            auto k = a.kv_f32 ? attention_kernel<true, GV, true> : attention_kernel<false, GV, true>;      \
+            cudaError_t e = allow_smem(k, smem);                                                           \
+            return e != cudaSuccess ? e : launch_cluster_ex(k, grid, block, smem, s, pdl, a.splits, a);    \
+        }                                                                                                  \
+        auto k = a.kv_f32 ? attention_kernel<true, GV, false> : attention_kernel<false, GV, false>;        \
         cudaError_t e = allow_smem(k, smem);                                                               \
         return e != cudaSuccess ? e : launch_ex(k, grid, block, smem, s, pdl, a);                          \
     }
@@ -1203,7 +1391,34 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
 
 int oproj_grid(int H) { return (H + kOpRows - 1) / kOpRows; }
 
+cudaError_t launch_oproj_smem(const OprojArgs& a, cudaStream_t s, bool pdl) {
+    const dim3 grid(oproj_grid(a.H)), block(256);
+    if (a.route && a.E > kMaxExperts) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)kOpRows * wrow_bytes(a.qd, a.q8) +
+                        sizeof(float) * (a.qd + (a.route ? (size_t)kOpRows * a.E : 0));
+    if (smem > kMaxSmemBytes || a.part_acc) return cudaErrorInvalidValue;
+#define LASTRO_OPS(N)                                                                 \
+    {                                                                                 \
+        auto k = a.q8 ? oproj_smem_kernel<N, true> : oproj_smem_kernel<N, false>;     \
+        cudaError_t e = allow_smem(k, smem);                                          \
+        return e != cudaSuccess ? e : launch_ex(k, grid, block, smem, s, pdl, a);     \
+    }
+    switch (chunks_for(a.qd)) {
+    case 1: LASTRO_OPS(1)
+    case 2: LASTRO_OPS(2)
+    case 3: LASTRO_OPS(3)
+    case 4: LASTRO_OPS(4)
+    case 5: LASTRO_OPS(5)
+    case 6: LASTRO_OPS(6)
+    case 7: LASTRO_OPS(7)
+    case 8: LASTRO_OPS(8)
+    default: return cudaErrorInvalidValue;
+    }
+#undef LASTRO_OPS
+}
+
 cudaError_t launch_oproj(const OprojArgs& a, cudaStream_t s, bool pdl) {
+    if (a.smem_weights) return launch_oproj_smem(a, s, pdl);
     const dim3 grid(oproj_grid(a.H)), block(32 * kOpWarps);
     if (a.route && a.E > kMaxExperts) return cudaErrorInvalidValue;
     if (a.part_acc && (a.heads * kHeadDim != a.qd || a.splits < 1)) return cudaErrorInvalidValue;

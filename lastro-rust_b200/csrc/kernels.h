@@ -19,6 +19,8 @@ namespace lastro {
 
 // in-graph timeline: CTAs per launch that stamp their three words (CtaTrace in common.cuh)
 constexpr int kTraceMaxCtas = 1024;
+constexpr int kTraceMarks = 5;
+constexpr int kTraceWords = 3 + kTraceMarks;  // per CTA: start, release, end, milestones
 
 // Linear weights are bf16 ([rows, cols] row-major) or Q8_0.  A Q8_0 row on the device is its cols int8 values, then its
 // cols/32 fp16 block scales, padded to a multiple of 16 bytes (so rows stay 16-byte aligned for bulk copies); weight =
@@ -63,7 +65,11 @@ struct AttnArgs {
     int* err;
     int kv_heads, G, d;
     int max_len, split_cap;  // split_cap = attn_split_cap(max_len, splits): K/V rows one CTA stages
-    int splits;              // context splits (grid x): attn_splits(max_len, kv_f32)
+    int splits;              // context splits (grid x): 8 or 16
+    int merge;               // 1: the last CTA of each KV head merges the splits into att_out; 0: the partials are
+                             // left for the output projection (OprojArgs part_acc)
+    int cluster;             // 1: the splits of a KV head form a thread-block cluster that merges them in distributed
+                             // shared memory (splits <= 8; batch-1 only)
     float scale;
     // batched decode (grid z = the launch's tokens, null seq = batch-1): token z reads q and writes att_out at
     // z * heads * d and its partials/counters at its own offsets, and attends the cache of sequence seq[z] (page-table
@@ -92,6 +98,8 @@ struct OprojArgs {
     const float* part_acc;
     const float* part_ml;
     int splits, heads;
+    int smem_weights;  // 1: the weight rows staged in shared memory, 256 threads (oproj_smem_kernel)
+    int* err;          // error word of that kernel's bounded copy wait
     unsigned long long* trace;  // in-graph timeline stamps of this launch (CtaTrace), or null
 };
 
@@ -320,7 +328,7 @@ constexpr size_t kMaxSmemBytes = 220 * 1024;  // dynamic shared memory one CTA m
 constexpr int kAttnSplits = 16;
 int attn_split_cap(int max_len, int splits);
 size_t attn_smem(int max_len, int kv_f32, int splits);
-int attn_splits(int max_len, int kv_f32);
+int attn_splits_default(int max_len, int kv_f32);
 
 // shared memory the grouped expert kernels need (host-side checks)
 size_t gate_up_smem(int H, int q8 = 0);

@@ -353,10 +353,12 @@ LDEV void route_topk_warp(float v0, float v1, int E, int k, int* sid, float* sva
 // calls this computes bitwise the same routing.  Uses __syncthreads; results in sid/sw (shared), returns r.
 template <int BLOCK>
 LDEV float route_from_shares(const RouteShares& rs, int E, int k, int H, float* red, int* sid, float* sval, float* sw,
-                             float* s_r, bool publish) {
+                             float* s_r, bool publish, const CtaTrace* tr = nullptr) {
     constexpr int kBatch = 8;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int E1 = E + 1, groups = BLOCK / E1;
+    // groups of share loads: fixed by a 256-thread block whatever BLOCK is, so every kernel that reduces the shares
+    // (256 or 288 threads) sums them in the same order and gets bitwise the same routing
+    const int E1 = E + 1, groups = (BLOCK < 256 ? BLOCK : 256) / E1;
     float acc = 0.0f;
     if (threadIdx.x < groups * E1) {
         const int e = threadIdx.x % E1, gi = threadIdx.x / E1;
@@ -374,6 +376,7 @@ LDEV float route_from_shares(const RouteShares& rs, int E, int k, int H, float* 
     }
     red[threadIdx.x] = acc;
     __syncthreads();
+    if (tr) tr->mark(3);
     if (warp == 0) {
         float v[2];
 #pragma unroll
@@ -388,6 +391,7 @@ LDEV float route_from_shares(const RouteShares& rs, int E, int k, int H, float* 
         const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), rs.eps)));
         const float l0 = lane < E ? __fmul_rn(v[0], r) : 0.0f;
         const float l1 = lane + 32 < E ? __fmul_rn(v[1], r) : 0.0f;
+        if (tr) tr->mark(4);
         route_topk_warp(l0, l1, E, k, sid, sval, sw);
         if (lane == 0) *s_r = r;
         if (publish) {

@@ -82,6 +82,8 @@ EXPORTS = {
     "lastro_model_fused": (C.c_int, [C.c_void_p]),
     "lastro_model_set_moe": (C.c_int, [C.c_void_p, C.c_int32]),
     "lastro_model_moe": (C.c_int, [C.c_void_p]),
+    "lastro_model_set_tuning": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32]),
+    "lastro_model_trace_raw": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32]),
     "lastro_model_set_attention": (C.c_int, [C.c_void_p, C.c_int32]),
     "lastro_model_destroy": (None, [C.c_void_p]),
     "lastro_checkpoint_open": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p), C.c_char_p, C.c_int32]),
@@ -442,6 +444,18 @@ class GpuModel:
     def set_moe(self, one_launch: bool = True):
         """The MoE block as one persistent launch per layer (default where it fits) or the gate_up + down kernels."""
         self.ctx.check(lib().lastro_model_set_moe(self.h, int(one_launch)))
+
+    def trace_raw(self, launch: int) -> np.ndarray:
+        """Stamps of one launch of the last traced step: [1024 CTAs, 8] global-timer ns (0 where not stamped)."""
+        out = np.zeros((1024, 8), np.uint64)
+        self.ctx.check(lib().lastro_model_trace_raw(self.h, launch, _p(out), out.size))
+        return out
+
+    def set_tuning(self, attn_splits: int = 16, attn_merge: int = 0, oproj_smem: bool = False):
+        """Batch-1 attention: context splits (8, 16, or 0 for the size-based choice) and how they are merged (0 the
+        attention's last CTA, 1 the output projection, 2 a thread-block cluster per KV head); the output projection's
+        weights in shared memory (256-thread CTAs) or registers."""
+        self.ctx.check(lib().lastro_model_set_tuning(self.h, attn_splits, int(attn_merge), int(oproj_smem)))
 
     @property
     def moe(self) -> bool:

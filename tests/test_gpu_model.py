@@ -283,8 +283,9 @@ def test_profile_direct_launches_report_every_kernel(gpu_ctx):
     m.fill_kv_synthetic(300)
     prof = m.profile(3)
     assert m.pos == 303
-    for k in ("qkv_rope", "attention", "oproj", "gate_up", "down", "head"):
+    for k in ("qkv_rope", "attention", "oproj", "head") + (("moe",) if m.moe else ("gate_up", "down")):
         assert prof[k] > 0.0, k
+    assert (prof["gate_up"] == 0.0) == m.moe
     assert prof["router"] == 0.0  # folded into oproj
     assert prof["fused_step"] == 0.0
     m.set_options(fused=True)
@@ -330,7 +331,7 @@ def test_trace_in_graph_timeline_covers_the_step(gpu_ctx):
     tr = a.trace(3)
     b.decode(3)
     assert a.pos == b.pos == 303
-    for k in ("qkv_rope", "attention", "oproj", "gate_up", "down", "head"):
+    for k in ("qkv_rope", "attention", "oproj", "head") + (("moe",) if a.moe else ("gate_up", "down")):
         assert tr["exposed"][k] > 0.0 and tr["span"][k] > 0.0, k
     assert tr["exposed"]["router"] == 0.0 and tr["exposed"]["fused_step"] == 0.0
     total = sum(tr["exposed"].values())
@@ -396,9 +397,9 @@ def test_one_launch_moe_equals_the_gate_up_and_down_kernels_bitwise(gpu_ctx, whi
         w = S.model_weights_q8(cfg, 12) if which == "tiny_q8" else reference_tiny_weights(cfg)
         models = [gpu_model(gpu_ctx, cfg, w, 64, "bf16") for _ in range(2)]
     a, b = models
-    assert a.moe  # the default where the shapes fit
-    b.set_moe(False)
-    assert not b.moe
+    assert not a.moe  # the two kernels are the default
+    a.set_moe(True)
+    assert a.moe and not b.moe
     for t in range(20):
         tok = (t * 7 + 3) % cfg["vocab"]
         la, na, ia, wa = a.step(tok)
@@ -406,3 +407,45 @@ def test_one_launch_moe_equals_the_gate_up_and_down_kernels_bitwise(gpu_ctx, whi
         assert np.array_equal(la, lb) and na == nb and np.array_equal(ia, ib) and np.array_equal(wa, wb), f"position {t}"
     a.close()
     b.close()
+
+
+@pytest.mark.parametrize("splits,merge,smem", [(16, 0, 0), (8, 0, 0), (16, 1, 0), (8, 1, 0), (8, 2, 0), (8, 2, 1)],
+                         ids=["16-last-cta", "8-last-cta", "16-oproj", "8-oproj", "8-cluster", "8-cluster-oproj-smem"])
+def test_attention_split_and_merge_variants_match_oracle(gpu_ctx, pool, splits, merge, smem):
+    """Every tuning of the CUDA-core attention (8 or 16 context splits; the splits merged by the last CTA of a KV head,
+    by the output projection, or by a thread-block cluster in distributed shared memory) and of the output projection
+    (weights in registers or staged in shared memory) against the oracle over 150 positions (three K/V pages), f32 KV,
+    at the f32 model gate."""
+    cfg = CFG.TINY_768
+    w = reference_tiny_weights(cfg)
+    m = gpu_model(gpu_ctx, cfg, w, 256, "f32")
+    m.set_tuning(splits, merge, bool(smem))
+    om = O.Model(cfg, weights=w)
+    s = O.Session(om, pool, 256)
+    worst = 0.0
+    for t, tok in enumerate(toks_like_reference(150, cfg["vocab"])):
+        lg, _, ids, _ = m.step(tok)
+        lo, io, _ = s.step(tok)
+        worst = max(worst, rel_l2(lg, lo))
+        assert rel_l2(lg, lo) < 1e-5, f"position {t}: {rel_l2(lg, lo):.2e}"
+        assert np.array_equal(ids, io), f"position {t}: routing"
+    s.close()
+    om.close()
+    m.close()
+
+
+def test_output_projection_weights_in_shared_memory_is_bitwise_the_register_form(gpu_ctx):
+    """oproj_smem_kernel (weights staged by one bulk copy, 256 threads) against oproj_kernel (weights in registers,
+    512 threads): the same dot order, so logits and routes are bitwise equal; bf16 and Q8_0 weights."""
+    for cfg, w in ((CFG.TINY_768, reference_tiny_weights(CFG.TINY_768)),
+                   (dict(CFG.TINY, weight_dtype="q8_0"), S.model_weights_q8(dict(CFG.TINY, weight_dtype="q8_0"), 12))):
+        a = gpu_model(gpu_ctx, cfg, w, 64, "bf16")
+        b = gpu_model(gpu_ctx, cfg, w, 64, "bf16")
+        b.set_tuning(16, 0, True)
+        for t in range(12):
+            tok = (t * 5 + 2) % cfg["vocab"]
+            la, na, ia, _ = a.step(tok)
+            lb, nb, ib, _ = b.step(tok)
+            assert np.array_equal(la, lb) and na == nb and np.array_equal(ia, ib), f"position {t}"
+        a.close()
+        b.close()
