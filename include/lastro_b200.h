@@ -168,8 +168,10 @@ int lastro_model_profile(lastro_model *model, int32_t steps, float *kernel_ms, i
 int lastro_model_trace(lastro_model *model, int32_t steps, float *exposed_ms, float *span_ms, float *wait_ms,
                        int32_t n_kinds, float *step_ms);
 /* the stamps of launch `launch` (in step order) of the last step lastro_model_trace timed: for each of up to 1024
- * CTAs, 8 words of global-timer ns (start, release from griddepcontrol.wait, exit, then 5 of the kernel's own
- * milestones; 0 where not stamped); words >= 8192.  Diagnostics only. */
+ * CTAs, LASTRO_TRACE_WORDS words: global-timer ns of start, release from griddepcontrol.wait and exit, then 7 of the
+ * kernel's own milestones (0 where not stamped), then the SM the CTA ran on; words >= 1024 * LASTRO_TRACE_WORDS.
+ * Diagnostics only. */
+#define LASTRO_TRACE_WORDS 11
 int lastro_model_trace_raw(const lastro_model *model, int32_t launch, unsigned long long *out, int32_t words);
 /* tuning: use CUDA graphs (default 1), programmatic dependent launch between the per-layer kernels (default 1),
  * and the fused step -- the whole step as one persistent cooperative launch, one CTA per SM -- where the model's
@@ -183,10 +185,22 @@ int lastro_model_set_moe(lastro_model *model, int32_t one_launch);
 /* tuning of the batch-1 attention kernel (CUDA-core, the default): attn_splits context splits per KV head (8 or 16;
  * 0 picks 8 when a split's rows fit one pass of the CTA, else 16) and how the splits are merged (0: by the last CTA
  * of each KV head, through global memory, the default; 1: by the output projection as it loads the attention output;
- * 2: the splits of a KV head are one thread-block cluster that merges them in distributed shared memory, splits 8);
- * oproj_smem: the output projection's weight rows staged in shared memory by 256-thread CTAs (1) or held in the
- * registers of 512-thread CTAs (0, the default); results are bitwise the same either way */
-int lastro_model_set_tuning(lastro_model *model, int32_t attn_splits, int32_t attn_merge, int32_t oproj_smem);
+ * 2: the splits of a KV head are one thread-block cluster that merges them in distributed shared memory);
+ * flags: LASTRO_TUNE_OPROJ_SMEM stages the output projection's weight rows in shared memory in 256-thread CTAs
+ * (else they sit in the registers of 512-thread CTAs); LASTRO_TUNE_PREFETCH_DOWN has the gate_up kernel hint the
+ * chosen experts' down rows into L2; LASTRO_TUNE_ATTN_BULK stages bf16 K/V rows with one bulk copy per page run
+ * (else 8-row TMA boxes with the 128-byte swizzle, whose reads are free of shared-memory bank conflicts);
+ * LASTRO_TUNE_SPEC_L2 fetches the experts predicted from the layer's input early (bf16 weights: the qkv kernel
+ * computes the router logits of the layer's input, the top-k of which the output projection's CTAs hint into L2 while
+ * the attention runs); LASTRO_TUNE_SPEC_STAGE instead has each gate_up CTA stream the rows of the expert predicted for
+ * its slot into shared memory before the routing is known (experts the prediction missed are staged after it).  Both
+ * are off by default: on C3 they measure even with the plain chain.  Results are bitwise the same for every flag. */
+#define LASTRO_TUNE_OPROJ_SMEM 1
+#define LASTRO_TUNE_PREFETCH_DOWN 2
+#define LASTRO_TUNE_ATTN_BULK 4
+#define LASTRO_TUNE_SPEC_L2 8
+#define LASTRO_TUNE_SPEC_STAGE 16
+int lastro_model_set_tuning(lastro_model *model, int32_t attn_splits, int32_t attn_merge, int32_t flags);
 /* 1 when the MoE blocks run as one launch per layer */
 int lastro_model_moe(const lastro_model *model);
 /* 1 when decode steps run as the fused step kernel (shapes fit and the option is on), else 0 */

@@ -1224,14 +1224,6 @@ LDEV void bgemm_ws_setup(uint32_t* tmem_base, uint64_t* full, uint64_t* empty, u
 // ------------------------------------------------------------------------------------------------------------------
 namespace {
 
-LDEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_addr(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-        : "memory");
-}
-
 LDEV void cp_async_arrive_noinc(uint64_t* bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
@@ -1438,6 +1430,10 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
 }
 
 cudaError_t make_weight_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+    return make_tile_map(map, base, rows, cols, 64);
+}
+
+cudaError_t make_tile_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     if (!encode) {
         void* fn = nullptr;
@@ -1446,10 +1442,11 @@ cudaError_t make_weight_map(CUtensorMap* map, const void* base, uint64_t rows, u
         if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return e != cudaSuccess ? e : cudaErrorNotSupported;
         encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
-    if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 2) % 16 || rows >= (1ull << 31)) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 2) % 16 || rows >= (1ull << 31) || box_rows < 1 || box_rows > 256)
+        return cudaErrorInvalidValue;
     const cuuint64_t dims[2] = {cols, rows};
     const cuuint64_t strides[1] = {cols * 2};
-    const cuuint32_t box[2] = {64, 64};
+    const cuuint32_t box[2] = {64, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1722,6 +1719,10 @@ cudaError_t launch_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStre
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+cudaError_t make_kv_box_map(CUtensorMap* map, const void* pool, uint64_t rows) {
+    return make_tile_map(map, pool, rows, kHeadDim, 8);
 }
 
 cudaError_t make_kv_map(CUtensorMap* map, const void* pool, uint64_t rows) {

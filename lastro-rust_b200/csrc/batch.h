@@ -211,6 +211,11 @@ size_t battn_smem(int cap, int kv_f32);
 cudaError_t launch_bgemm(const BGemmArgs& a, int epi, int groups, cudaStream_t s, const CUtensorMap* wmap = nullptr);
 // host: tensor map for launch_bgemm's mode 2 over a row-major bf16 matrix [rows][cols]
 cudaError_t make_weight_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols);
+// the same with boxes of box_rows rows (<= 256) x 64 columns
+cudaError_t make_tile_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
+// bf16 KV pool as rows of one head's position (64 columns) in boxes of 8 rows, 128-byte swizzle: the batch-1
+// attention's staging (AttnArgs::tma)
+cudaError_t make_kv_box_map(CUtensorMap* map, const void* pool, uint64_t rows);
 cudaError_t launch_battn_norm(const BNormArgs& a, int n, cudaStream_t s);
 cudaError_t launch_brope_kv(const BRopeArgs& a, cudaStream_t s);
 cudaError_t launch_brouter(const BRouterArgs& a, cudaStream_t s);

@@ -447,6 +447,13 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         qa.kv_heads = d.kv_heads;
         qa.eps = d.eps;
         qa.trace = slot();
+        const bool spec = m->spec_mode != 0 && !m->q8 && !moe_on(m);
+        if (spec) {
+            qa.spec_router = reinterpret_cast<const uint16_t*>(L.router);
+            qa.spec_ln = L.ln_moe;
+            qa.spec_out = m->spec_logits;
+            qa.spec_E = d.experts;
+        }
         if ((e = launch_qkv_rope(qa, s, pdl && l > 0)) != cudaSuccess) return e;
         if ((e = mark(pe, s, KK_QKV)) != cudaSuccess) return e;
 
@@ -495,7 +502,10 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
             ba.scale = d.attention_multiplier;
             if ((e = launch_battention_tc(ba, &m->kvmaps[2 * l], &m->kvmaps[2 * l + 1], s)) != cudaSuccess) return e;
         } else {
-            if ((e = launch_attention(aa, s, pdl)) != cudaSuccess) return e;
+            aa.tma = m->attn_tma ? 1 : 0;
+            if ((e = launch_attention(aa, s, pdl, aa.tma ? &m->kvboxmaps[2 * l] : nullptr,
+                                      aa.tma ? &m->kvboxmaps[2 * l + 1] : nullptr)) != cudaSuccess)
+                return e;
         }
         if ((e = mark(pe, s, KK_ATTN)) != cudaSuccess) return e;
 
@@ -518,6 +528,15 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
             oa.part_ml = m->part_ml;
             oa.splits = aa.splits;
             oa.heads = d.heads;
+        }
+        if (spec && m->spec_mode == 2) {
+            oa.spec = m->spec_logits;
+            oa.spec_E = d.experts;
+            oa.spec_k = d.k;
+            oa.spec_gu = L.gate_up;
+            oa.spec_dn = L.down;
+            oa.spec_gu_bytes = (unsigned long long)2 * d.inter * wrow_bytes(d.hidden, m->q8);
+            oa.spec_dn_bytes = (unsigned long long)d.hidden * wrow_bytes(d.inter, m->q8);
         }
         oa.trace = slot();
         if ((e = launch_oproj(oa, s, pdl)) != cudaSuccess) return e;
@@ -581,8 +600,9 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         ga.I = d.inter;
         ga.k = d.k;
         ga.E = d.experts;
-        ga.down_w = L.down;
+        ga.down_w = m->gu_prefetch_down ? L.down : nullptr;
         ga.down_row_bytes = wrow_bytes(d.inter, m->q8);
+        ga.spec = spec && m->spec_mode == 1 ? m->spec_logits : nullptr;
         ga.trace = slot();
         if ((e = launch_gate_up(ga, s, pdl)) != cudaSuccess) return e;
         if ((e = mark(pe, s, KK_GATE_UP)) != cudaSuccess) return e;
@@ -756,7 +776,7 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
               A.alloc(&L.wr_t, E * H);
     }
     bad = bad || A.alloc(&m->rope_cs, (size_t)max_len * d.head_dim) || A.alloc(&m->page_table, m->max_pages) ||
-          A.alloc(&m->h, H) || A.alloc(&m->q, m->qd) || A.alloc(&m->att, m->qd) || A.alloc(&m->rlogits, E) ||
+          A.alloc(&m->h, H) || A.alloc(&m->q, m->qd) || A.alloc(&m->att, m->qd) || A.alloc(&m->rlogits, E) || A.alloc(&m->spec_logits, E) ||
           A.alloc(&m->part_acc, (size_t)d.heads * kAttnSplits * d.head_dim) ||
           A.alloc(&m->part_ml, (size_t)d.heads * kAttnSplits * 2) ||
           A.alloc(&m->route_w, (size_t)d.layers * d.k) || A.alloc(&m->route_ids, (size_t)d.layers * d.k) ||
@@ -857,10 +877,21 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
             cudaGetLastError();
             m->kvmaps.clear();
         }
+        m->kvboxmaps.resize((size_t)d.layers * 2);
+        ok = kPageSize % 8 == 0 && d.head_dim == 64;
+        for (int l = 0; l < d.layers && ok; ++l)
+            ok = make_kv_box_map(&m->kvboxmaps[2 * l], m->L[l].k_pool, rows) == cudaSuccess &&
+                 make_kv_box_map(&m->kvboxmaps[2 * l + 1], m->L[l].v_pool, rows) == cudaSuccess;
+        if (!ok) {
+            cudaGetLastError();
+            m->kvboxmaps.clear();
+        }
+        m->attn_tma = !m->kvboxmaps.empty();
         // off by default: at batch 1 (16 splits, one token) the CUDA-core kernel, whose split merge is one round of
         // loads and shuffles, measures faster on B200 (C3: 16.4 vs 13 us per launch)
         m->attn_tc = false;
     }
+    m->spec_mode = 0;  // both forms measure even with the plain chain on C3 (gate_up gains what oproj/down lose)
     ctx_retain(ctx);
     *out = m;
     return LASTRO_OK;
@@ -1388,12 +1419,12 @@ extern "C" int lastro_model_set_moe(lastro_model* m, int32_t one_launch) {
 
 extern "C" int lastro_model_moe(const lastro_model* m) { return m && moe_on(m) ? 1 : 0; }
 
-extern "C" int lastro_model_set_tuning(lastro_model* m, int32_t attn_splits, int32_t attn_merge, int32_t oproj_smem) {
+extern "C" int lastro_model_set_tuning(lastro_model* m, int32_t attn_splits, int32_t attn_merge, int32_t flags) {
     if (!m) return LASTRO_E_ARG;
     const int f32 = m->d.kv_dtype == LASTRO_DTYPE_F32;
     const int splits = attn_splits == 0 ? attn_splits_default(m->max_len, f32) : attn_splits;
     if (splits != 8 && splits != kAttnSplits) return set_err(m->ctx, LASTRO_E_ARG, "attention splits %d (8 or 16)", splits);
-    if (attn_merge < 0 || attn_merge > 2 || (attn_merge == 2 && splits > 8))
+    if (attn_merge < 0 || attn_merge > 2)
         return set_err(m->ctx, LASTRO_E_ARG, "attention merge %d with %d splits", attn_merge, splits);
     if (attn_smem(m->max_len, f32, splits) > kMaxSmemBytes)
         return set_err(m->ctx, LASTRO_E_UNSUPPORTED, "%d attention splits do not fit max_len %d", splits, m->max_len);
@@ -1406,7 +1437,10 @@ extern "C" int lastro_model_set_tuning(lastro_model* m, int32_t attn_splits, int
         }
     m->attn_splits = splits;
     m->attn_merge = attn_merge;
-    m->oproj_smem = oproj_smem != 0;
+    m->oproj_smem = (flags & LASTRO_TUNE_OPROJ_SMEM) != 0;
+    m->gu_prefetch_down = (flags & LASTRO_TUNE_PREFETCH_DOWN) != 0;
+    m->attn_tma = !m->kvboxmaps.empty() && (flags & LASTRO_TUNE_ATTN_BULK) == 0;
+    m->spec_mode = (flags & LASTRO_TUNE_SPEC_STAGE) ? 1 : (flags & LASTRO_TUNE_SPEC_L2) ? 2 : 0;
     return LASTRO_OK;
 }
 

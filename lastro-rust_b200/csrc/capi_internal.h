@@ -147,6 +147,12 @@ struct lastro_model {
     float *h = nullptr, *q = nullptr, *att = nullptr;
     float *part_acc = nullptr, *part_ml = nullptr;  // attention splits [heads, kAttnSplits, d] / [.., 2]
     float *rlogits = nullptr, *route_w = nullptr, *rnorm = nullptr, *a = nullptr, *logits = nullptr;
+    // the router logits of each layer's input (qkv kernel), from which the experts the layer will most likely route
+    // to are fetched before the routing is known (bf16 weights): 2 hinted into L2 by the output projection's CTAs
+    // while the attention runs (LASTRO_TUNE_SPEC_L2), 1 staged into shared memory by the gate_up CTAs
+    // (LASTRO_TUNE_SPEC_STAGE), 0 off (the default)
+    float* spec_logits = nullptr;
+    int spec_mode = 0;
     int *route_ids = nullptr, *d_token = nullptr, *d_pos = nullptr, *d_step = nullptr, *d_out_ids = nullptr;
     int* d_prompt = nullptr;
     unsigned int *router_counter = nullptr, *head_counter = nullptr, *attn_counters = nullptr;
@@ -173,14 +179,19 @@ struct lastro_model {
     // loads through these maps (per layer: K, V); the CUDA-core split kernel by default
     std::vector<CUtensorMap> kvmaps;
     bool attn_tc = false;
-    // the MoE block as one persistent launch per layer (moe_kernel) where the shapes fit it (default on), else the
-    // gate_up and down kernels; its grid barrier's counter
+    // bf16 KV: the CUDA-core attention kernel's staging maps (per layer: K, V; 8-row boxes, 128-byte swizzle) and
+    // whether it uses them (default) or plain bulk copies (LASTRO_TUNE_ATTN_BULK)
+    std::vector<CUtensorMap> kvboxmaps;
+    bool attn_tma = false;
+    // the MoE block as one persistent launch per layer (moe_kernel) where the shapes fit it and the option is on (off
+    // by default), else the gate_up and down kernels; its grid barrier's counter
     lastro::MoePlan moe{};
     // batch-1 attention: context splits (8 or 16) and where the splits are merged (the attention kernel's last CTA, or
     // the output projection as it loads them); lastro_model_set_tuning
     int attn_splits = 16;
     int attn_merge = 0;  // 0: the attention's last CTA per KV head, 1: the output projection, 2: a cluster per KV head
     bool oproj_smem = false;  // the output projection's weights staged in shared memory (oproj_smem_kernel)
+    bool gu_prefetch_down = false;  // gate_up hints the chosen experts' down slabs into L2
     bool moe_ok = false, use_moe = false;
     unsigned long long* moe_barrier = nullptr;
     // multi-position steps (lastro_model_step_positions): a batch of the model's own sequence on its KV cache

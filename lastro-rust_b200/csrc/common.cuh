@@ -23,7 +23,8 @@ LDEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "m
 // ---- in-graph timeline (lastro_model_trace) -----------------------------------------------------------------------
 // With a non-null trace base, every CTA of a launch stamps the global timer (ns) into its own kTraceWords words: [0]
 // when thread 0 starts, [1] when thread 0 passes griddepcontrol.wait, [2] the latest exit of any warp (atomicMax by
-// lane 0 of each warp; the destructor runs on every return path), [3..] the kernel's own milestones (mark).  The host reduces over CTAs: min start, min release, max
+// lane 0 of each warp; the destructor runs on every return path), [3..] the kernel's own milestones (mark), the last
+// word the SM id.  The host reduces over CTAs: min start, min release, max
 // end.  A null base (the product path) costs one predicated branch per stamp.
 LDEV unsigned long long global_ns() {
     unsigned long long t;
@@ -36,12 +37,18 @@ struct CtaTrace {
     LDEV explicit CtaTrace(unsigned long long* base) : p(nullptr) {
         const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
         if (base && cta < (unsigned)kTraceMaxCtas) p = base + kTraceWords * (size_t)cta;
-        if (p && threadIdx.x == 0) p[0] = global_ns();
+        if (p && threadIdx.x == 0) {
+            p[0] = global_ns();
+            unsigned sm;
+            asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+            p[3 + kTraceMarks - 1] = sm;  // the last milestone word holds the SM the CTA runs on
+        }
     }
     LDEV void released() const {
         if (p && threadIdx.x == 0) p[1] = global_ns();
     }
-    // a kernel's own milestone i (< kTraceMarks) as thread `tid` reaches it (diagnostics of the phases inside a launch)
+    // a kernel's own milestone i (< kTraceMarks - 1) as thread `tid` reaches it (diagnostics of the phases inside a
+    // launch)
     LDEV void mark(int i, unsigned tid = 0) const {
         if (p && threadIdx.x == tid) p[3 + i] = global_ns();
     }
@@ -148,6 +155,15 @@ LDEV void mbar_init(uint64_t* bar, uint32_t count) {
 
 LDEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+// one box of a 2-D tensor map (x innermost, a multiple of 16 bytes) into shared memory, completing on `bar`
+LDEV void tma_load_2d(void* dst, const void* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
 }
 
 // `bytes` and both addresses must be multiples of 16

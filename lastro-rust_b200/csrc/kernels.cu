@@ -87,6 +87,23 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
     w1.load(wb + (size_t)r1 * rbh, a.H, lane, active);
     float4 ln[NV];
     vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
+    // predicted routing: this CTA's router row times the MoE norm weight, in the layout of v
+    const bool spec = a.spec_out && (int)blockIdx.x < a.spec_E;
+    float4 sw4[NV];
+    if (spec) {
+        const uint2* rr = reinterpret_cast<const uint2*>(a.spec_router + (size_t)blockIdx.x * a.H);  // 4 bf16 per uint2
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            const int i = threadIdx.x + k * BLOCK;
+            if (4 * i < a.H) {
+                const uint2 u = __ldg(rr + i);
+                const float4 l4 = __ldg(reinterpret_cast<const float4*>(a.spec_ln) + i);
+                sw4[k] = make_float4(bf_lo(u.x) * l4.x, bf_hi(u.x) * l4.y, bf_lo(u.y) * l4.z, bf_hi(u.y) * l4.w);
+            } else {
+                sw4[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+    }
     // The position changes only in the previous step's head kernel, which completed before this step's first kernel
     // started (that launch is not programmatic): so the position, its RoPE row and the K/V page of this token are
     // final before the wait, and their loads leave the critical path.
@@ -124,6 +141,18 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
         vec_load_cg<BLOCK, NV>(a.h, a.H, v);
     }
     norm_regs<BLOCK, NV>(v, ln, a.H, a.eps, xs, red);
+    if (spec) {
+        float p = 0.0f;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            p = fmaf(sw4[k].x, v[k].x, p);
+            p = fmaf(sw4[k].y, v[k].y, p);
+            p = fmaf(sw4[k].z, v[k].z, p);
+            p = fmaf(sw4[k].w, v[k].w, p);
+        }
+        p = block_sum(p, red);
+        if (threadIdx.x == 0) a.spec_out[blockIdx.x] = p;
+    }
     trace_.mark(0);
     if (!active) return;
 
@@ -170,16 +199,23 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
 constexpr int kAttnWarps = 8;
 
 template <bool KV_F32, int G, bool CL>
-__global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                                    const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
     const CtaTrace trace_(a.trace);
     constexpr int D = kHeadDim;
     constexpr int NW = kAttnWarps;
     constexpr int ESZ = KV_F32 ? 4 : 2;
     constexpr int RB = D * ESZ;  // bytes per K/V row of one head
     constexpr int CH = RB / 16;  // 16-byte chunks per row
+    static_assert(KV_F32 || RB == 128, "swizzled boxes hold 128-byte rows");
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    unsigned char* kt = smem_raw;                             // [cap, RB]
-    unsigned char* vt = smem_raw + (size_t)a.split_cap * RB;  // [cap, RB]
+    // tma: K/V staged as 8-row boxes (TMA, 128-byte swizzle) from position p0 rounded down to a multiple of 8, each
+    // box 1024-byte aligned; else one bulk copy per page run from position p0, unswizzled
+    const bool tma = !KV_F32 && a.tma;
+    const int cap = tma ? attn_tma_rows(a.split_cap) : a.split_cap;
+    unsigned char* kt = tma ? reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023)
+                            : smem_raw;  // [cap, RB]
+    unsigned char* vt = kt + (size_t)cap * RB;  // [cap, RB]
     __shared__ __align__(16) float sq[G][D];
     __shared__ float wm[NW][G], wl[NW][G];
     __shared__ __align__(16) float wacc[NW][G][D];
@@ -202,12 +238,26 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
     const int len = pos + 1;
     const int p0 = (int)(((long long)len * s) / NS), p1 = (int)(((long long)len * (s + 1)) / NS);
     const int pb = min(p1, pos);  // rows [p0, pb) are final already
+    const int r_base = tma ? (p0 & ~7) : p0;  // position of staged row 0
+    const int roff = p0 - r_base, swz = tma ? 7 : 0;
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
-        mbar_expect_tx(&bar, pb > p0 ? (uint32_t)(pb - p0) * RB * 2 : 0u);
+        uint32_t tx = 0u;
+        if (pb > p0) tx = tma ? (uint32_t)(((pb - 1) >> 3) - (p0 >> 3) + 1) * 2u * 8u * RB : (uint32_t)(pb - p0) * RB * 2;
+        mbar_expect_tx(&bar, tx);
     }
     __syncthreads();
-    if (pb > p0) {
+    if (pb > p0 && tma) {
+        // one thread per 8-row box (a box never crosses a page: page_size is a multiple of 8); rows of the box outside
+        // [p0, pb) are in the same page and are never read
+        const int g0 = p0 >> 3, ng = ((pb - 1) >> 3) - g0 + 1;
+        for (int t = threadIdx.x; t < ng; t += blockDim.x) {
+            const int row = (g0 + t) << 3, pg = row / a.page_size, slot = row - pg * a.page_size;
+            const int y = (__ldcg(page_table + pg) * a.kv_heads + kvh) * a.page_size + slot;
+            tma_load_2d(kt + (size_t)(row - r_base) * RB, &kmap, 0, y, &bar);
+            tma_load_2d(vt + (size_t)(row - r_base) * RB, &vmap, 0, y, &bar);
+        }
+    } else if (pb > p0) {
         // one thread per page run: page-table reads and copies all in flight together
         const int pg0 = p0 / a.page_size, pg1 = (pb - 1) / a.page_size;
         for (int t = threadIdx.x; t <= pg1 - pg0; t += blockDim.x) {
@@ -226,17 +276,19 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
 
     for (int i = threadIdx.x; i < G * D / 4; i += blockDim.x)
         reinterpret_cast<float4*>(&sq[0][0])[i] = __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)z * HD + (size_t)kvh * G * D) + i);
+    // with boxes, the box that holds the new row's slot carries its stale copy: the row is written after they land
+    bool ok = tma ? mbar_wait(&bar, 0, a.err, 3) : true;
     if (pos >= p0 && pos < p1 && threadIdx.x < 2 * CH) {
         // the row this layer's qkv kernel just appended
         const int pg = pos / a.page_size, slot = pos - pg * a.page_size;
         const size_t off = (((size_t)__ldcg(page_table + pg) * a.kv_heads + kvh) * a.page_size + slot) * RB;
-        const int c = threadIdx.x % CH;
+        const int c = threadIdx.x % CH, i = pos - r_base;
         const bool is_v = threadIdx.x >= CH;
         const uint4* src = reinterpret_cast<const uint4*>(static_cast<const unsigned char*>(is_v ? a.v_pool : a.k_pool) + off);
-        reinterpret_cast<uint4*>((is_v ? vt : kt) + (size_t)(pos - p0) * RB)[c] = __ldcg(src + c);
+        reinterpret_cast<uint4*>((is_v ? vt : kt) + (size_t)i * RB)[c ^ (i & swz)] = __ldcg(src + c);
     }
     __syncthreads();
-    const bool ok = mbar_wait(&bar, 0, a.err, 3);
+    if (!tma) ok = mbar_wait(&bar, 0, a.err, 3);
     trace_.mark(0);
 
     float m[G], l[G], acc0[G], acc1[G];
@@ -248,17 +300,23 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
         acc1[g] = 0.0f;
     }
     const int nrow = ok ? p1 - p0 : 0;
-    for (int base = warp * 32; base < nrow; base += NW * 32) {
+    // rows per warp and pass: 16 (half the lanes) when that already covers the split in one pass of the 8 warps, so
+    // that every warp takes a share of a short split, else 32
+    const int rw = nrow <= NW * 16 ? 16 : 32;
+    for (int base = warp * rw; base < nrow; base += NW * rw) {
         const int r = base + lane;
-        const bool valid = r < nrow;
+        const bool valid = lane < rw && r < nrow;
         float sc[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) sc[g] = 0.0f;
         if (valid) {
-            const uint4* kr = reinterpret_cast<const uint4*>(kt + (size_t)r * RB);
+            // staged row of position p0 + r, and its 16-byte chunks' swizzle (lanes read rows of one 8-row box:
+            // chunk c of eight consecutive rows lands in eight different bank groups)
+            const int i = r + roff, sw = i & swz;
+            const uint4* kr = reinterpret_cast<const uint4*>(kt + (size_t)i * RB);
 #pragma unroll
             for (int c = 0; c < CH; ++c) {
-                const uint4 kc = kr[c];
+                const uint4 kc = kr[c ^ sw];
                 // the row's elements are unpacked once and used for all G heads
                 float kf[8];
                 if (KV_F32) {
@@ -285,38 +343,65 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
                 }
             }
         }
-        float pr[G];
+        // online softmax: the G heads' butterflies interleaved (per head the same steps as warp_max / warp_sum)
+        float scv[G], mx[G], pr[G], sm[G], alpha[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            const float scv = valid ? __fmul_rn(sc[g], a.scale) : -INFINITY;
-            const float mn = fmaxf(m[g], warp_max(scv));
-            pr[g] = valid ? expf(scv - mn) : 0.0f;
-            const float alpha = (m[g] == -INFINITY) ? 0.0f : expf(m[g] - mn);
-            l[g] = l[g] * alpha + warp_sum(pr[g]);
-            acc0[g] *= alpha;
-            acc1[g] *= alpha;
+            scv[g] = valid ? __fmul_rn(sc[g], a.scale) : -INFINITY;
+            mx[g] = scv[g];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int g = 0; g < G; ++g) mx[g] = fmaxf(mx[g], __shfl_xor_sync(0xffffffffu, mx[g], o));
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float mn = fmaxf(m[g], mx[g]);
+            pr[g] = valid ? expf(scv[g] - mn) : 0.0f;
+            alpha[g] = (m[g] == -INFINITY) ? 0.0f : expf(m[g] - mn);
+            sm[g] = pr[g];
             m[g] = mn;
         }
-        const int nj = min(32, nrow - base);
-        for (int jj = 0; jj < nj; ++jj) {
-            float v0, v1;
-            if (KV_F32) {
-                const float2 t = reinterpret_cast<const float2*>(vt + (size_t)(base + jj) * RB)[lane];
-                v0 = t.x;
-                v1 = t.y;
-            } else {
-                const uint32_t t = reinterpret_cast<const uint32_t*>(vt + (size_t)(base + jj) * RB)[lane];
-                v0 = bf_lo(t);
-                v1 = bf_hi(t);
-            }
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float pj = __shfl_sync(0xffffffffu, pr[g], jj);
-                acc0[g] = fmaf(pj, v0, acc0[g]);
-                acc1[g] = fmaf(pj, v1, acc1[g]);
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int g = 0; g < G; ++g) sm[g] += __shfl_xor_sync(0xffffffffu, sm[g], o);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            l[g] = l[g] * alpha[g] + sm[g];
+            acc0[g] *= alpha[g];
+            acc1[g] *= alpha[g];
+        }
+        // P V in blocks of 8 rows, unrolled so that a block's loads and shuffles are in flight together; rows past
+        // nj re-read the last row and get p = 0 (their lanes hold no score)
+        const int nj = min(rw, nrow - base);
+        for (int j0 = 0; j0 < nj; j0 += 8) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int jj = j0 + u;
+                const int i = base + min(jj, nj - 1) + roff;
+                float v0, v1;
+                if (KV_F32) {
+                    const float2 t = reinterpret_cast<const float2*>(vt + (size_t)i * RB)[lane];
+                    v0 = t.x;
+                    v1 = t.y;
+                } else {
+                    // lane's word (elements 2 lane, 2 lane + 1) sits in chunk lane / 4, swizzled like the K rows
+                    const uint32_t t = reinterpret_cast<const uint32_t*>(vt + (size_t)i * RB)[(((lane >> 2) ^ (i & swz)) << 2) |
+                                                                                             (lane & 3)];
+                    v0 = bf_lo(t);
+                    v1 = bf_hi(t);
+                }
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float pj = __shfl_sync(0xffffffffu, pr[g], jj & 31);
+                    acc0[g] = fmaf(pj, v0, acc0[g]);
+                    acc1[g] = fmaf(pj, v1, acc1[g]);
+                }
             }
         }
     }
+    trace_.mark(3);
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         if (lane == 0) {
@@ -327,6 +412,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(AttnArgs a) 
         wacc[warp][g][2 * lane + 1] = acc1[g];
     }
     __syncthreads();
+    trace_.mark(4);
     // this CTA's partial: warps merged; layout [head][split][...] so the consumer reads each head's splits together
     for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
         const int g = t / D, dim = t - (t / D) * D;
@@ -526,6 +612,38 @@ LDEV void merge_attention(const OprojArgs& a, float* xs, float* pacc, float* pml
     __syncthreads();
 }
 
+// The predicted top-k (OprojArgs spec) ranked like the routing, then this CTA's share of the k experts' gate_up and
+// down weights (k x (gu + dn) bytes in expert order) hinted into L2 by thread 0.  Every thread of the block calls it.
+LDEV void spec_prefetch_l2(const OprojArgs& a) {
+    __shared__ unsigned long long key[kMaxExperts];
+    __shared__ int pid[kMaxTopK];
+    if ((int)threadIdx.x < a.spec_E) key[threadIdx.x] = route_key(__ldcg(a.spec + threadIdx.x), threadIdx.x);
+    __syncthreads();
+    if ((int)threadIdx.x < a.spec_E) {
+        const unsigned long long me = key[threadIdx.x];
+        int rank = 0;
+        for (int j = 0; j < a.spec_E; ++j) rank += (int)(key[j] > me);
+        if (rank < a.spec_k) pid[rank] = threadIdx.x;
+    }
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    const unsigned long long per = a.spec_gu_bytes + a.spec_dn_bytes, all = per * a.spec_k;
+    const unsigned long long share = ((all + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
+    unsigned long long o = share * blockIdx.x;
+    const unsigned long long o1 = min(all, o + share);
+    while (o < o1) {
+        const int sl = (int)(o / per);
+        const unsigned long long in = o - (unsigned long long)sl * per;
+        const int e = min(max(pid[sl], 0), a.spec_E - 1);
+        const bool gu = in < a.spec_gu_bytes;
+        const unsigned long long part = gu ? a.spec_gu_bytes : a.spec_dn_bytes, at = gu ? in : in - a.spec_gu_bytes;
+        const unsigned long long n = min(o1 - o, part - at);
+        const unsigned char* base = static_cast<const unsigned char*>(gu ? a.spec_gu : a.spec_dn) + (size_t)e * part;
+        bulk_prefetch_l2(base + at, (uint32_t)n);
+        o += n;
+    }
+}
+
 template <int NCH, bool Q8>
 __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
     const CtaTrace trace_(a.trace);
@@ -546,6 +664,7 @@ __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
         const int n = kOpRows * a.E;
         for (int t = threadIdx.x; t < n; t += BLOCK) wrs[t] = (r0 + t / a.E < a.H) ? __ldg(a.wr_t + (size_t)r0 * a.E + t) : 0.0f;
     }
+    if (a.spec) spec_prefetch_l2(a);
     pdl_wait();
     pdl_launch();
     trace_.released();
@@ -615,6 +734,7 @@ __global__ void __launch_bounds__(256) oproj_smem_kernel(OprojArgs a) {
         const int n = kOpRows * a.E;
         for (int t = threadIdx.x; t < n; t += BLOCK) wrs[t] = (r0 + t / a.E < a.H) ? __ldg(a.wr_t + (size_t)r0 * a.E + t) : 0.0f;
     }
+    if (a.spec) spec_prefetch_l2(a);
     pdl_wait();
     pdl_launch();
     trace_.released();
@@ -683,6 +803,37 @@ __global__ void router_fold_kernel(const void* wr, const float* ln, float* wr_t,
 // ------------------------------------------------------------------------------------------------------------------
 constexpr int kGuPairs = 16;
 
+// the rows j0 .. j0 + 2 half of expert e (gate rows into wg, up rows into wu) in two stages completing on bar[0] and
+// bar[1]; thread 0
+LDEV void gu_stage(const GateUpArgs& a, int e, int j0, size_t rbh, int half, unsigned char* wg, unsigned char* wu,
+                   uint64_t* bar) {
+    e = min(max(e, 0), a.E - 1);  // clamped so that a stale id can never address outside the weights
+    const unsigned char* base = static_cast<const unsigned char*>(a.w) + (size_t)e * 2 * a.I * rbh;
+    const uint32_t bytes = (uint32_t)(half * rbh);
+#pragma unroll
+    for (int st = 0; st < 2; ++st) {
+        mbar_expect_tx(&bar[st], 2 * bytes);
+        bulk_g2s(wg + (size_t)st * half * rbh, base + (size_t)(j0 + st * half) * rbh, bytes, &bar[st]);
+        bulk_g2s(wu + (size_t)st * half * rbh, base + (size_t)(a.I + j0 + st * half) * rbh, bytes, &bar[st]);
+    }
+}
+
+// this CTA's share of the k experts' down slabs (k slabs of H rows) hinted into L2; thread 0
+LDEV void gu_prefetch_down(const GateUpArgs& a, const int* ids) {
+    const unsigned long long slab = (unsigned long long)a.H * a.down_row_bytes, all = slab * a.k;
+    const unsigned long long share = ((all + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
+    unsigned long long o0 = share * blockIdx.x;
+    const unsigned long long o1 = min(all, o0 + share);
+    while (o0 < o1) {
+        const int sl = (int)(o0 / slab);
+        const unsigned long long in = o0 - (unsigned long long)sl * slab;
+        const unsigned long long n = min(o1 - o0, slab - in);
+        const int ex = min(max(ids[sl], 0), a.E - 1);
+        bulk_prefetch_l2(static_cast<const unsigned char*>(a.down_w) + (size_t)ex * slab + in, (uint32_t)n);
+        o0 += n;
+    }
+}
+
 template <int NCH, bool Q8>
 __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
     const CtaTrace trace_(a.trace);
@@ -702,9 +853,33 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
     const int per_slot = a.I / R;
     const int slot = blockIdx.x / per_slot, j0 = (blockIdx.x - slot * per_slot) * R;
     const bool fused = a.rs.shares != nullptr;
+    const bool spec = fused && a.spec;
+    __shared__ int spid[kMaxTopK];                      // spec: the predicted experts by rank
+    __shared__ unsigned long long spkey[kMaxExperts];
     if (threadIdx.x == 0) {
         mbar_init(&bar[0], 1);
         mbar_init(&bar[1], 1);
+    }
+    if (spec) {
+        // the predicted top-k (the logits of the layer's input, final before this kernel started), ranked like the
+        // routing; then this CTA's rows of its slot's predicted expert start streaming
+        float lg = 0.0f;
+        if (threadIdx.x < a.E) {
+            lg = __ldcg(a.spec + threadIdx.x);
+            spkey[threadIdx.x] = route_key(lg, threadIdx.x);
+        }
+        __syncthreads();
+        if (threadIdx.x < a.E) {
+            const unsigned long long me = spkey[threadIdx.x];
+            int rank = 0;
+            for (int j = 0; j < a.E; ++j) rank += (int)(spkey[j] > me);
+            if (rank < a.k) spid[rank] = threadIdx.x;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            gu_stage(a, spid[slot], j0, rbh, HALF, wg, wu, bar);
+            if (a.down_w) gu_prefetch_down(a, spid);
+        }
     }
     float4 ln[NV];
     if (fused) vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
@@ -722,17 +897,43 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
         __syncthreads();  // barrier init visible to every waiting thread
     }
     trace_.mark(0);
-    if (threadIdx.x == 0) {
-        // expert id, clamped so that a stale id can never address outside the weights
-        const int e = min(max(fused ? sid[slot] : __ldcg(a.ids + slot), 0), a.E - 1);
-        const unsigned char* base = static_cast<const unsigned char*>(a.w) + (size_t)e * 2 * a.I * rbh;
-        const uint32_t bytes = (uint32_t)(HALF * rbh);
-#pragma unroll
-        for (int st = 0; st < 2; ++st) {
-            mbar_expect_tx(&bar[st], 2 * bytes);
-            bulk_g2s(wg + (size_t)st * HALF * rbh, base + (size_t)(j0 + st * HALF) * rbh, bytes, &bar[st]);
-            bulk_g2s(wu + (size_t)st * HALF * rbh, base + (size_t)(a.I + j0 + st * HALF) * rbh, bytes, &bar[st]);
+    int out_slot = slot;  // the routing slot whose rows j0.. this CTA computes
+    uint32_t parity = 0;
+    if (spec) {
+        // predicted expert of this CTA's slot taken by the routing: computed where the routing put it.  Otherwise the
+        // m-th such miss in slot order takes the m-th routed expert nobody predicted (as many of one as of the other)
+        const int ep = spid[slot];
+        int hit = -1, m = 0;
+        for (int q = 0; q < a.k; ++q) hit = sid[q] == ep ? q : hit;
+        if (hit >= 0) {
+            out_slot = hit;
+        } else {
+            for (int q = 0; q < slot; ++q) {
+                bool routed = false;
+                for (int t = 0; t < a.k; ++t) routed |= sid[t] == spid[q];
+                m += routed ? 0 : 1;
+            }
+            for (int q = 0; q < a.k; ++q) {
+                bool predicted = false;
+                for (int t = 0; t < a.k; ++t) predicted |= spid[t] == sid[q];
+                if (!predicted && m-- == 0) {
+                    out_slot = q;
+                    break;
+                }
+            }
+            // the predicted rows must have landed before the routed ones overwrite them
+            bool ok = mbar_wait(&bar[0], 0, a.err, 1);
+            ok = mbar_wait(&bar[1], 0, a.err, 1) && ok;
+            if (!__syncthreads_and(ok)) return;
+            if (threadIdx.x == 0) gu_stage(a, sid[out_slot], j0, rbh, HALF, wg, wu, bar);
+            parity = 1;
+            trace_.mark(6);  // timeline: this CTA re-staged after a misprediction
         }
+    } else if (threadIdx.x == 0) {
+        gu_stage(a, fused ? sid[slot] : __ldcg(a.ids + slot), j0, rbh, HALF, wg, wu, bar);
+        // optional: the chosen experts' down rows hinted into L2, so the down kernel's CTAs, which find room on the
+        // SMs only as these leave, read their rows from L2
+        if (fused && a.down_w) gu_prefetch_down(a, sid);
     }
     if (fused) {
         // xn = ln * (h * r) (model.rs:141-145)
@@ -749,12 +950,12 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
     x_to_regs<NCH>(xs, a.H, lane, xa, xb);
 #pragma unroll
     for (int st = 0; st < 2; ++st) {
-        if (!mbar_wait(&bar[st], 0, a.err, 1)) return;
+        if (!mbar_wait(&bar[st], parity, a.err, 1)) return;
         trace_.mark(1 + st);
         const int pr = st * HALF + warp;
         const float g = warp_sum(smem_row_dot_w<NCH, Q8>(wg + (size_t)pr * rbh, xa, xb, a.H, lane));
         const float u = warp_sum(smem_row_dot_w<NCH, Q8>(wu + (size_t)pr * rbh, xa, xb, a.H, lane));
-        if (lane == 0) a.a[(size_t)slot * a.I + j0 + pr] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+        if (lane == 0) a.a[(size_t)out_slot * a.I + j0 + pr] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
     }
 }
 
@@ -1350,7 +1551,9 @@ cudaError_t launch_qkv_rope(const QkvArgs& a, cudaStream_t s, bool pdl) {
 int attn_split_cap(int max_len, int splits) { return (max_len + splits - 1) / splits + 1; }
 
 size_t attn_smem(int max_len, int kv_f32, int splits) {
-    return (size_t)2 * attn_split_cap(max_len, splits) * kHeadDim * (kv_f32 ? 4 : 2);
+    const int cap = attn_split_cap(max_len, splits);
+    if (kv_f32) return (size_t)2 * cap * kHeadDim * 4;
+    return (size_t)2 * attn_tma_rows(cap) * kHeadDim * 2 + 1024;  // + the boxes' 1024-byte alignment
 }
 
 // context splits of the batch-1 attention: 8 while a split's rows fit about one pass of the CTA's 8 warps (256
@@ -1359,10 +1562,14 @@ int attn_splits_default(int max_len, int kv_f32) {
     return (max_len <= 8 * 32 * kAttnWarps + 512 && attn_smem(max_len, kv_f32, 8) <= kMaxSmemBytes) ? 8 : kAttnSplits;
 }
 
-cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl, const CUtensorMap* kmap, const CUtensorMap* vmap) {
     if (a.d != kHeadDim || a.splits < 1 || a.splits > kAttnSplits || a.split_cap != attn_split_cap(a.max_len, a.splits))
         return cudaErrorInvalidValue;
-    if (a.cluster && (a.splits > 8 || a.seq)) return cudaErrorInvalidValue;  // portable cluster size; batch-1 only
+    if (a.tma && (a.kv_f32 || !kmap || !vmap || a.page_size % 8)) return cudaErrorInvalidValue;
+    static const CUtensorMap none{};  // unused by launches that stage with plain bulk copies
+    const CUtensorMap& km = a.tma ? *kmap : none;
+    const CUtensorMap& vm = a.tma ? *vmap : none;
+    if (a.cluster && a.seq) return cudaErrorInvalidValue;  // batch-1 only (16 splits: a non-portable cluster size)
     const size_t smem = attn_smem(a.max_len, a.kv_f32, a.splits);
     if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
     const dim3 grid(a.splits, a.kv_heads, a.seq ? a.tokens : 1), block(32 * kAttnWarps);
@@ -1371,11 +1578,13 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
         if (a.cluster) {                                                                                   \
             auto k = a.kv_f32 ? attention_kernel<true, GV, true> : attention_kernel<false, GV, true>;      \
             cudaError_t e = allow_smem(k, smem);                                                           \
-            return e != cudaSuccess ? e : launch_cluster_ex(k, grid, block, smem, s, pdl, a.splits, a);    \
+            if (e == cudaSuccess && a.splits > 8)                                                          \
+                e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);            \
+            return e != cudaSuccess ? e : launch_cluster_ex(k, grid, block, smem, s, pdl, a.splits, km, vm, a); \
         }                                                                                                  \
         auto k = a.kv_f32 ? attention_kernel<true, GV, false> : attention_kernel<false, GV, false>;        \
         cudaError_t e = allow_smem(k, smem);                                                               \
-        return e != cudaSuccess ? e : launch_ex(k, grid, block, smem, s, pdl, a);                          \
+        return e != cudaSuccess ? e : launch_ex(k, grid, block, smem, s, pdl, km, vm, a);                  \
     }
     switch (a.G) {
         LASTRO_ATTN_G(1)

@@ -12,6 +12,7 @@
 // All activations are f32, weights bf16, accumulators f32.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -19,7 +20,7 @@ namespace lastro {
 
 // in-graph timeline: CTAs per launch that stamp their three words (CtaTrace in common.cuh)
 constexpr int kTraceMaxCtas = 1024;
-constexpr int kTraceMarks = 5;
+constexpr int kTraceMarks = 8;
 constexpr int kTraceWords = 3 + kTraceMarks;  // per CTA: start, release, end, milestones
 
 // Linear weights are bf16 ([rows, cols] row-major) or Q8_0.  A Q8_0 row on the device is its cols int8 values, then its
@@ -49,6 +50,13 @@ struct QkvArgs {
     int H, qd, kvd, d, kv_heads;
     float eps;
     unsigned long long* trace;  // in-graph timeline stamps of this launch (CtaTrace), or null
+    // optional: the routing predicted from this layer's input, for the gate_up kernel's early staging: CTA c < spec_E
+    // writes spec_out[c] = sum_i router[c][i] * ln_moe[i] * h[i] (the router logit of h itself; the MoE block's input
+    // is h after this layer's attention, normalised by a positive factor that leaves the order of the logits as is)
+    const uint16_t* spec_router;  // [E, H] bf16 router rows, or null
+    const float* spec_ln;         // [H] MoE norm weight
+    float* spec_out;              // [E]
+    int spec_E;
 };
 
 struct AttnArgs {
@@ -70,6 +78,8 @@ struct AttnArgs {
                              // left for the output projection (OprojArgs part_acc)
     int cluster;             // 1: the splits of a KV head form a thread-block cluster that merges them in distributed
                              // shared memory (splits <= 8; batch-1 only)
+    int tma;                 // 1: bf16 K/V staged by 8-row TMA boxes with the 128-byte swizzle (launch_attention's maps:
+                             // make_kv_box_map over the layer's pools; page_size a multiple of 8), else bulk copies
     float scale;
     // batched decode (grid z = the launch's tokens, null seq = batch-1): token z reads q and writes att_out at
     // z * heads * d and its partials/counters at its own offsets, and attends the cache of sequence seq[z] (page-table
@@ -101,6 +111,14 @@ struct OprojArgs {
     int smem_weights;  // 1: the weight rows staged in shared memory, 256 threads (oproj_smem_kernel)
     int* err;          // error word of that kernel's bounded copy wait
     unsigned long long* trace;  // in-graph timeline stamps of this launch (CtaTrace), or null
+    // optional: the predicted router logits (QkvArgs spec_out, final when this kernel starts): before
+    // griddepcontrol.wait the CTAs take their top spec_k and hint the predicted experts' gate_up and down weights
+    // into L2, each CTA its share, while the attention still runs
+    const float* spec;
+    int spec_E, spec_k;
+    const void* spec_gu;  // [E, 2I, H] rows: spec_gu_bytes per expert
+    const void* spec_dn;  // [E, H, I] rows: spec_dn_bytes per expert
+    unsigned long long spec_gu_bytes, spec_dn_bytes;
 };
 
 // Routing of the fused path: the output projection's per-CTA shares, reduced by every CTA of the expert kernels in
@@ -145,6 +163,11 @@ struct GateUpArgs {
     size_t down_row_bytes;
     int stream;  // the streaming kernel (one wave, all rows in flight): measured slower on C3, kept selectable
     unsigned long long* trace;  // in-graph timeline stamps of this launch (CtaTrace), or null
+    // optional (with rs.shares): the predicted router logits (QkvArgs spec_out), final when this kernel starts.  Before
+    // griddepcontrol.wait every CTA takes their top-k and stages the rows of its slot's predicted expert; after the
+    // routing a CTA whose expert was predicted computes it where the routing put it, the others re-stage the experts
+    // nobody predicted (the results do not depend on the prediction)
+    const float* spec;
 };
 
 struct DownArgs {
@@ -213,7 +236,11 @@ struct HeadArgs {
 
 // Launchers: `pdl` marks the launch as programmatic-dependent on the previous kernel of the stream.
 cudaError_t launch_qkv_rope(const QkvArgs& a, cudaStream_t s, bool pdl);
-cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl, const CUtensorMap* kmap = nullptr,
+                             const CUtensorMap* vmap = nullptr);
+// bf16 K/V staged in 8-row boxes: a split's rows [p0, p1) with p1 - p0 < cap, widened to whole boxes, span at most
+// cap + 13 rows; a multiple of 8 keeps the V rows 1024-byte aligned after the K rows
+__host__ __device__ inline int attn_tma_rows(int cap) { return (cap + 20) / 8 * 8; }
 cudaError_t launch_oproj(const OprojArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t s, bool pdl);
 int oproj_grid(int H);

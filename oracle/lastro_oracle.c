@@ -998,6 +998,11 @@ void lo_session_layer_attention(lo_session *s, int32_t l, float *xn_out) {
     if (xn_out) memcpy(xn_out, t->xn, sizeof(float) * (size_t)h);
 }
 
+/* the residual stream of the step in progress [H] (before the next lo_session_layer_attention: that layer's input) */
+void lo_session_residual(const lo_session *s, float *out) {
+    memcpy(out, s->st->x, sizeof(float) * (size_t)s->m->cfg.hidden);
+}
+
 /* layer l's MoE half from a block output y computed elsewhere: x += resid * y */
 void lo_session_layer_moe(lo_session *s, int32_t l, const float *y) {
     const lo_config *c = &s->m->cfg;

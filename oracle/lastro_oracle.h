@@ -132,6 +132,8 @@ int lo_session_step(lo_session *s, int32_t token, float *logits, int32_t *ids, f
  * lo_session_step is these phases with the block in between. */
 int lo_session_step_begin(lo_session *s, int32_t token);
 void lo_session_layer_attention(lo_session *s, int32_t layer, float *xn_out);
+/* the residual stream of the step in progress [H] (between phases) */
+void lo_session_residual(const lo_session *s, float *out);
 void lo_session_layer_moe(lo_session *s, int32_t layer, const float *y);
 void lo_session_step_end(lo_session *s, float *logits);
 /* append synthetic K/V rows (tests/bench only: a context of `n` positions without running the model) */

@@ -111,6 +111,7 @@ def _declare(L):
         "lo_session_step_begin": (C.c_int, [_P, _I]),
         "lo_session_layer_attention": (None, [_P, _I, _P]),
         "lo_session_layer_moe": (None, [_P, _I, _P]),
+        "lo_session_residual": (None, [_P, _P]),
         "lo_session_step_end": (None, [_P, _P]),
         "lo_session_k": (_P, [_P, _I]),
         "lo_session_v": (_P, [_P, _I]),
@@ -375,6 +376,12 @@ class Session:
         xn = np.empty(self.model.cfg["hidden"], dtype=np.float32)
         lib().lo_session_layer_attention(self.h, layer, _ptr(xn))
         return xn
+
+    def residual(self) -> np.ndarray:
+        """The residual stream of the step in progress (between phases: the next layer's input)."""
+        x = np.empty(self.model.cfg["hidden"], dtype=np.float32)
+        lib().lo_session_residual(self.h, _ptr(x))
+        return x
 
     def layer_moe(self, layer: int, y: np.ndarray):
         y = np.ascontiguousarray(y, dtype=np.float32)

@@ -409,8 +409,10 @@ def test_one_launch_moe_equals_the_gate_up_and_down_kernels_bitwise(gpu_ctx, whi
     b.close()
 
 
-@pytest.mark.parametrize("splits,merge,smem", [(16, 0, 0), (8, 0, 0), (16, 1, 0), (8, 1, 0), (8, 2, 0), (8, 2, 1)],
-                         ids=["16-last-cta", "8-last-cta", "16-oproj", "8-oproj", "8-cluster", "8-cluster-oproj-smem"])
+@pytest.mark.parametrize("splits,merge,smem", [(16, 0, 0), (8, 0, 0), (16, 1, 0), (8, 1, 0), (8, 2, 0), (8, 2, 1),
+                                               (16, 2, 0)],
+                         ids=["16-last-cta", "8-last-cta", "16-oproj", "8-oproj", "8-cluster", "8-cluster-oproj-smem",
+                              "16-cluster"])
 def test_attention_split_and_merge_variants_match_oracle(gpu_ctx, pool, splits, merge, smem):
     """Every tuning of the CUDA-core attention (8 or 16 context splits; the splits merged by the last CTA of a KV head,
     by the output projection, or by a thread-block cluster in distributed shared memory) and of the output projection
@@ -419,7 +421,7 @@ def test_attention_split_and_merge_variants_match_oracle(gpu_ctx, pool, splits, 
     cfg = CFG.TINY_768
     w = reference_tiny_weights(cfg)
     m = gpu_model(gpu_ctx, cfg, w, 256, "f32")
-    m.set_tuning(splits, merge, bool(smem))
+    m.set_tuning(splits, merge, bool(smem), prefetch_down=True)
     om = O.Model(cfg, weights=w)
     s = O.Session(om, pool, 256)
     worst = 0.0
@@ -432,6 +434,68 @@ def test_attention_split_and_merge_variants_match_oracle(gpu_ctx, pool, splits, 
     s.close()
     om.close()
     m.close()
+
+
+@pytest.mark.parametrize("splits,merge", [(16, 0), (8, 0), (16, 1), (8, 2)],
+                         ids=["16-last-cta", "8-last-cta", "16-oproj", "8-cluster"])
+def test_bf16_kv_staged_by_swizzled_boxes_is_bitwise_the_bulk_copy_staging(gpu_ctx, splits, merge):
+    """bf16 K/V staged as 8-row TMA boxes with the 128-byte swizzle (the default) against one bulk copy per page run:
+    the same rows in the same order, so logits and routes are bitwise equal, over 150 positions (three 64-position
+    pages; split boundaries at every offset within a box, the new row inside a staged box or starting one)."""
+    cfg = CFG.TINY_768
+    w = reference_tiny_weights(cfg)
+    a = gpu_model(gpu_ctx, cfg, w, 256, "bf16")
+    b = gpu_model(gpu_ctx, cfg, w, 256, "bf16")
+    a.set_tuning(splits, merge)
+    b.set_tuning(splits, merge, attn_bulk=True)
+    for t, tok in enumerate(toks_like_reference(150, cfg["vocab"])):
+        la, na, ia, _ = a.step(tok)
+        lb, nb, ib, _ = b.step(tok)
+        assert np.array_equal(la, lb) and na == nb and np.array_equal(ia, ib), f"position {t}"
+    a.close()
+    b.close()
+
+
+def gate_up_misses(m, layers):
+    """CTAs of the traced step's gate_up launches that re-staged their rows after a misprediction (milestone 6)."""
+    m.trace(1)  # one traced decode step: launches qkv, attention, oproj, gate_up, down per layer, then head
+    return sum(int((m.trace_raw(5 * l + 3)[:, 3 + 6] > 0).sum()) for l in range(layers))
+
+
+@pytest.mark.parametrize("mode", ["l2", "stage"])
+@pytest.mark.parametrize("which", ["tiny", "tiny768", "c3-2layer"])
+def test_speculative_expert_fetch_is_bitwise_the_plain_chain(gpu_ctx, which, mode):
+    """The experts predicted from the layer's input fetched before the routing is known -- hinted into L2 by the
+    output projection or staged into the gate_up CTAs' shared memory -- against no speculation (the default): the routing and the rows computed do not depend on the prediction, so logits and routes are bitwise
+    equal (staging: CTAs whose prediction missed re-stage, counted from the timeline)."""
+    if which == "tiny":
+        cfg, w, n = CFG.TINY, reference_tiny_weights(CFG.TINY), 60
+    elif which == "tiny768":
+        cfg, w, n = CFG.TINY_768, reference_tiny_weights(CFG.TINY_768), 120
+    else:
+        cfg, w, n = dict(CFG.C3_3B["model"], layers=2), None, 40
+    models = []
+    for spec in (True, False):
+        m = LB.GpuModel(gpu_ctx, cfg, 256, kv_dtype="bf16")
+        if w is None:
+            m.fill_synthetic(CFG.C3_3B["weight_seed"], CFG.WEIGHT_STD, 0.0)
+        else:
+            m.load_weights(w)
+        m.set_tuning(16, 0, speculation=mode if spec else False)
+        models.append(m)
+    a, b = models
+    toks = toks_like_reference(n, cfg["vocab"])
+    for t, tok in enumerate(toks):
+        la, na, ia, _ = a.step(tok)
+        lb, nb, ib, _ = b.step(tok)
+        assert np.array_equal(la, lb) and na == nb and np.array_equal(ia, ib), f"position {t}"
+    misses = gate_up_misses(a, cfg["layers"])
+    assert gate_up_misses(b, cfg["layers"]) == 0
+    if mode == "l2":
+        assert misses == 0
+    print(f"{which} {mode}: gate_up CTAs re-staged after a misprediction in one traced step: {misses}")
+    a.close()
+    b.close()
 
 
 def test_output_projection_weights_in_shared_memory_is_bitwise_the_register_form(gpu_ctx):
