@@ -293,6 +293,47 @@ int lastro_batch_set_options(lastro_batch *batch, int32_t use_graphs, int32_t us
 int lastro_batch_set_wait_limit(lastro_batch *batch, uint64_t wait_ns);
 void lastro_batch_destroy(lastro_batch *batch);
 
+/* ---- text I/O: byte-level BPE tokenizer and the Granite 3.1 chat template (rust/moe-rt/src/tokenizador.rs) ----
+ * Host-only.  Replaces Tokenizador (tokenizador.rs:192-467), renderiza_chat (:512-541) and formata_data (:544-561).
+ * Errors: LASTRO_E_ARG for bad arguments, text that is not UTF-8, an id outside the vocabulary, or an output buffer
+ * too small (the needed size is still written to the count argument); LASTRO_E_IO for a file that cannot be read;
+ * LASTRO_E_UNSUPPORTED for a tokenizer.json outside the Granite configuration (ErroTokenizador::Formato: normalizer,
+ * pre-tokenizer other than ByteLevel{add_prefix_space false, use_regex true}, decoder, dropout, unk token, byte
+ * fallback, subword affixes, ignore_merges, added tokens with lstrip/rstrip/single_word/normalized, sparse ids, merges
+ * outside the vocabulary); err (errlen bytes, NUL-terminated) receives a message. */
+typedef struct lastro_tokenizer lastro_tokenizer;
+/* Tokenizador::carrega (tokenizador.rs:215-218) */
+int lastro_tokenizer_load(const char *path, lastro_tokenizer **out, char *err, int32_t errlen);
+/* Tokenizador::de_bytes (tokenizador.rs:221-345): from the tokenizer.json text */
+int lastro_tokenizer_from_json(const char *json, size_t len, lastro_tokenizer **out, char *err, int32_t errlen);
+void lastro_tokenizer_destroy(lastro_tokenizer *tok);
+/* largest id + 1 (tamanho_vocabulario, tokenizador.rs:347-349) */
+int32_t lastro_tokenizer_vocab_size(const lastro_tokenizer *tok);
+/* codifica (tokenizador.rs:420-448): UTF-8 text of len bytes -> ids, as `tokenizers` encodes it without special
+ * tokens added (no BOS); *n_ids = the count (also when cap is too small) */
+int lastro_tokenizer_encode(const lastro_tokenizer *tok, const char *text, size_t len, int32_t *ids, int32_t cap,
+                            int32_t *n_ids);
+/* decodifica_bytes (tokenizador.rs:451-460): the exact bytes; added tokens as their literal text */
+int lastro_tokenizer_decode_bytes(const lastro_tokenizer *tok, const int32_t *ids, int32_t n, char *out, size_t cap,
+                                  size_t *n_out);
+/* decodifica (tokenizador.rs:463-466): the bytes as UTF-8 text, each maximal invalid subsequence of the whole sequence
+ * replaced by U+FFFD (no clean-up of spaces before punctuation) */
+int lastro_tokenizer_decode(const lastro_tokenizer *tok, const int32_t *ids, int32_t n, char *out, size_t cap,
+                            size_t *n_out);
+/* pre_tokeniza (tokenizador.rs:125-177): the GPT-2 regex pieces of UTF-8 text, as the byte offset where each ends */
+int lastro_tokenizer_pretokenize(const char *text, size_t len, int32_t *ends, int32_t cap, int32_t *n_pieces);
+#define LASTRO_ROLE_SYSTEM 0
+#define LASTRO_ROLE_USER 1
+#define LASTRO_ROLE_ASSISTANT 2
+/* renderiza_chat (tokenizador.rs:512-541): the Granite 3.1 chat template for n >= 1 messages (roles LASTRO_ROLE_*,
+ * contents of lens bytes); a first system message is the system turn, else the default one with `date`
+ * (strftime("%B %d, %Y"), see lastro_format_date); add_generation_prompt opens an assistant turn after the last
+ * message that follows the system turn.  *n_out = the rendered length (also when cap is too small). */
+int lastro_chat_render(const int32_t *roles, const char *const *contents, const size_t *lens, int32_t n,
+                       int32_t add_generation_prompt, const char *date, char *out, size_t cap, size_t *n_out);
+/* formata_data (tokenizador.rs:544-561): "November 07, 2026"; LASTRO_E_ARG for an invalid date (years 1..9999) */
+int lastro_format_date(int32_t year, int32_t month, int32_t day, char *out, int32_t cap);
+
 #ifdef __cplusplus
 }
 #endif

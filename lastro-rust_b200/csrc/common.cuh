@@ -26,9 +26,11 @@ LDEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "m
 // lane 0 of each warp; the destructor runs on every return path), [3..] the kernel's own milestones (mark), the last
 // word the SM id.  The host reduces over CTAs: min start, min release, max
 // end.  A null base (the product path) costs one predicated branch per stamp.
+// the memory clobber keeps loads and stores from moving across a stamp (without it a stamp can land before work that
+// the source places ahead of it)
 LDEV unsigned long long global_ns() {
     unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)::"memory");
     return t;
 }
 

@@ -418,7 +418,6 @@ LDEV float route_from_shares(const RouteShares& rs, int E, int k, int H, float* 
     }
     if (threadIdx.x == 0) *s_r = r;
     __syncthreads();
-    if (tr) tr->mark(5);
     // (d) softmax over the k: exp(v - v0), summed in order, divided
     if (warp == 0) {
         const float ex = lane < k ? expf(__fsub_rn(sval[lane], sval[0])) : 0.0f;

@@ -96,6 +96,20 @@ EXPORTS = {
     "lastro_config_from_json": (C.c_int, [C.c_char_p, C.c_void_p, C.c_char_p, C.c_int32]),
     "lastro_checkpoint_config": (C.c_int, [C.c_void_p, C.c_void_p, C.c_char_p, C.c_int32]),
     "lastro_model_load_checkpoint": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "lastro_tokenizer_load": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p), C.c_char_p, C.c_int32]),
+    "lastro_tokenizer_from_json": (C.c_int, [C.c_char_p, C.c_size_t, C.POINTER(C.c_void_p), C.c_char_p, C.c_int32]),
+    "lastro_tokenizer_destroy": (None, [C.c_void_p]),
+    "lastro_tokenizer_vocab_size": (C.c_int32, [C.c_void_p]),
+    "lastro_tokenizer_encode": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.c_void_p, C.c_int32,
+                                          C.POINTER(C.c_int32)]),
+    "lastro_tokenizer_decode_bytes": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_char_p, C.c_size_t,
+                                                C.POINTER(C.c_size_t)]),
+    "lastro_tokenizer_decode": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_char_p, C.c_size_t,
+                                          C.POINTER(C.c_size_t)]),
+    "lastro_tokenizer_pretokenize": (C.c_int, [C.c_char_p, C.c_size_t, C.c_void_p, C.c_int32, C.POINTER(C.c_int32)]),
+    "lastro_chat_render": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_char_p, C.c_char_p,
+                                     C.c_size_t, C.POINTER(C.c_size_t)]),
+    "lastro_format_date": (C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_char_p, C.c_int32]),
     "lastro_batch_create": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_void_p)]),
     "lastro_batch_exchange_handle": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32]),
     "lastro_batch_connect": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32]),
@@ -295,6 +309,129 @@ class Checkpoint:
 
     def __del__(self):
         self.close()
+
+
+class Tokenizer:
+    """Byte-level BPE tokenizer of a Granite 3.1 tokenizer.json (tokenizador.rs Tokenizador).  Host-only."""
+
+    def __init__(self, path: str | None = None, *, json_text: str | bytes | None = None):
+        h = C.c_void_p()
+        err = C.create_string_buffer(512)
+        if path is not None:
+            rc = lib().lastro_tokenizer_load(os.fsencode(path), C.byref(h), err, len(err))
+        else:
+            raw = json_text.encode() if isinstance(json_text, str) else bytes(json_text)
+            rc = lib().lastro_tokenizer_from_json(raw, len(raw), C.byref(h), err, len(err))
+        if rc != OK:
+            raise LastroError(rc, err.value.decode())
+        self.h = h
+
+    @property
+    def vocab_size(self) -> int:
+        return lib().lastro_tokenizer_vocab_size(self.h)
+
+    def encode(self, text: str) -> list[int]:
+        """codifica: text -> ids (no BOS), as `tokenizers` encodes it."""
+        raw = text.encode("utf-8")
+        n = C.c_int32()
+        lib().lastro_tokenizer_encode(self.h, raw, len(raw), None, 0, C.byref(n))
+        out = np.empty(max(n.value, 1), np.int32)
+        rc = lib().lastro_tokenizer_encode(self.h, raw, len(raw), _p(out), out.size, C.byref(n))
+        if rc != OK:
+            raise LastroError(rc, "encode")
+        return out[:n.value].tolist()
+
+    def _decode(self, fn, ids) -> bytes:
+        a = np.ascontiguousarray(np.asarray(ids, np.int32).reshape(-1))
+        n = C.c_size_t()
+        rc = fn(self.h, _p(a), a.size, None, 0, C.byref(n))
+        if rc != OK and n.value == 0 and a.size:
+            raise LastroError(rc, "decode: an id outside the vocabulary")
+        buf = C.create_string_buffer(max(n.value, 1))
+        rc = fn(self.h, _p(a), a.size, buf, len(buf), C.byref(n))
+        if rc != OK:
+            raise LastroError(rc, "decode: an id outside the vocabulary")
+        return buf.raw[:n.value]
+
+    def decode_bytes(self, ids) -> bytes:
+        """decodifica_bytes: the exact bytes (added tokens as their literal text)."""
+        return self._decode(lib().lastro_tokenizer_decode_bytes, ids)
+
+    def decode(self, ids) -> str:
+        """decodifica: UTF-8 text, invalid sequences replaced by U+FFFD, no space clean-up."""
+        return self._decode(lib().lastro_tokenizer_decode, ids).decode("utf-8")
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().lastro_tokenizer_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
+def pretokenize(text: str) -> list[str]:
+    """pre_tokeniza: the GPT-2 regex pieces of text."""
+    raw = text.encode("utf-8")
+    n = C.c_int32()
+    lib().lastro_tokenizer_pretokenize(raw, len(raw), None, 0, C.byref(n))
+    ends = np.empty(max(n.value, 1), np.int32)
+    rc = lib().lastro_tokenizer_pretokenize(raw, len(raw), _p(ends), ends.size, C.byref(n))
+    if rc != OK:
+        raise LastroError(rc, "pretokenize")
+    out, start = [], 0
+    for e in ends[:n.value].tolist():
+        out.append(raw[start:e].decode("utf-8"))
+        start = e
+    return out
+
+
+ROLES = {"system": 0, "user": 1, "assistant": 2}
+
+
+def render_chat(messages: list[dict], add_generation_prompt: bool, date: str) -> str:
+    """renderiza_chat: the Granite 3.1 chat template for [{"role": system|user|assistant, "content": str}, ...]."""
+    n = len(messages)
+    if n == 0:
+        raise LastroError(E_ARG, "an empty message list")
+    roles = np.array([ROLES[m["role"]] for m in messages], np.int32)
+    raws = [m["content"].encode("utf-8") for m in messages]
+    bufs = [C.create_string_buffer(r, max(len(r), 1)) for r in raws]
+    ptrs = (C.c_char_p * n)(*[C.cast(b, C.c_char_p) for b in bufs])
+    lens = (C.c_size_t * n)(*[len(r) for r in raws])
+    out_n = C.c_size_t()
+    lib().lastro_chat_render(_p(roles), ptrs, lens, n, int(add_generation_prompt), date.encode(), None, 0,
+                             C.byref(out_n))
+    out = C.create_string_buffer(max(out_n.value, 1))
+    rc = lib().lastro_chat_render(_p(roles), ptrs, lens, n, int(add_generation_prompt), date.encode(), out, len(out),
+                                  C.byref(out_n))
+    if rc != OK:
+        raise LastroError(rc, "render_chat")
+    return out.raw[:out_n.value].decode("utf-8")
+
+
+def chat(model, tokenizer, messages: list[dict], max_new_tokens: int, *, date: str | None = None, eos: int = 0):
+    """The reference's text loop (tokenizador.rs renderiza_chat + codifica, geracao_regra.rs greedy generation that
+    stops at the first EOS, decodifica): renders the Granite chat template with the generation prompt, encodes it,
+    generates on the device from the model's current position, and decodes the new ids without the EOS.
+    Returns (text, ids)."""
+    if date is None:
+        import datetime
+        d = datetime.date.today()
+        date = format_date(d.year, d.month, d.day)
+    prompt = tokenizer.encode(render_chat(messages, True, date))
+    ids = model.generate_until(prompt, max_new_tokens, eos)
+    body = ids[:-1] if ids.size and ids[-1] == eos else ids
+    return tokenizer.decode(body), ids
+
+
+def format_date(year: int, month: int, day: int) -> str:
+    """formata_data: strftime("%B %d, %Y") in English."""
+    out = C.create_string_buffer(48)
+    rc = lib().lastro_format_date(year, month, day, out, len(out))
+    if rc != OK:
+        raise LastroError(rc, f"invalid date {year}-{month}-{day}")
+    return out.value.decode()
 
 
 TENSOR_NAMES = ("input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_proj.weight",

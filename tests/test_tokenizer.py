@@ -1,0 +1,193 @@
+"""The byte-level BPE tokenizer and the Granite chat template behind the C ABI (csrc/tokenizer.cu), host-only.
+
+Restates the reference's own tokenizer tests (rust/moe-rt/src/tokenizador.rs:563-840): ids, byte round trips and the
+lossy text decode equal to what Hugging Face `tokenizers` gives (the library the reference matched 100 % on its
+qual-runs/A2-LOTE-20261103/5a-referencia cases), the chat template equal to transformers' rendering of the Granite
+3.1 template, and refusals of tokenizer.json files outside the supported configuration.  The Granite vocabulary is
+not available offline: ids are pinned on a synthetic tokenizer.json of the same configuration
+(tests/golden/gen_tokenizer_golden.py), over the reference's own edge-case texts, synthetic ones and, where
+`tokenizers` is importable, a sweep of every Unicode scalar value.
+"""
+import json
+import os
+import random
+
+import pytest
+
+import lastro_b200 as LB
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+TOK_JSON = os.path.join(GOLDEN, "bpe_tokenizer.json")
+
+
+@pytest.fixture(scope="module")
+def cases():
+    with open(os.path.join(GOLDEN, "tokenizer_cases.json")) as f:
+        return json.load(f)
+
+
+@pytest.fixture(scope="module")
+def tok():
+    t = LB.Tokenizer(TOK_JSON)
+    yield t
+    t.close()
+
+
+@pytest.fixture(scope="module")
+def hf():
+    tokenizers = pytest.importorskip("tokenizers")
+    return tokenizers.Tokenizer.from_file(TOK_JSON)
+
+
+def test_golden_ids_and_byte_round_trip(tok, cases):
+    """tokenizador.rs:640-700: ids equal, and the bytes decode back to the text (minus the bytes whose symbol the
+    vocabulary lacks, which encoding drops as `tokenizers` does)."""
+    missing = {0xC0, 0xC1, 0xF1} | set(range(0xF5, 0x100))
+    for c in cases["encode"]:
+        ids = tok.encode(c["text"])
+        assert ids == c["ids"], repr(c["text"][:60])
+        raw = c["text"].encode()
+        assert tok.decode_bytes(ids) == bytes(b for b in raw if b not in missing) or any(b in missing for b in raw)
+        if not any(b in missing for b in raw):
+            assert tok.decode_bytes(ids) == raw and tok.decode(ids) == c["text"]
+
+
+def test_added_tokens_longest_leftmost_and_literal_decode(tok):
+    eot = tok.encode("<|end_of_text|>")
+    assert eot == [0]
+    ab, abc = tok.encode("<|ab|>"), tok.encode("<|ab|>c")
+    assert len(ab) == 1 and len(abc) == 1 and ab != abc
+    assert tok.encode("<|ab|>cc")[0] == abc[0]
+    assert tok.decode(tok.encode("x<|start_of_role|>user<|end_of_role|>y")) == "x<|start_of_role|>user<|end_of_role|>y"
+
+
+def test_lossy_decode_of_split_characters(tok, cases):
+    """tokenizador.rs:463-466: ids that split a character decode with U+FFFD over the whole byte sequence."""
+    for c in cases["cut"]:
+        assert tok.decode(c["ids"]) == c["text"], c["ids"]
+
+
+def test_chat_template_matches_the_reference_renderings(cases):
+    """tokenizador.rs:720-780: renderiza_chat equals transformers' apply_chat_template with the Granite 3.1 template on
+    the reference's 38 chat cases (default system turn with the date, a leading system message, a system message in
+    the middle, generation prompt on and off, empty contents, contents with special-token literals)."""
+    for c in cases["chat"]:
+        got = LB.render_chat(c["messages"], c["add_generation_prompt"], c["date"])
+        assert got == c["rendered"], c["name"]
+    with pytest.raises(LB.LastroError) as e:
+        LB.render_chat([], True, "November 07, 2026")
+    assert e.value.code == LB.E_ARG
+
+
+def test_format_date():
+    """tokenizador.rs:790-810 (formata_data)."""
+    assert LB.format_date(2026, 11, 7) == "November 07, 2026"
+    assert LB.format_date(2024, 2, 29) == "February 29, 2024"
+    assert LB.format_date(1, 1, 1) == "January 01, 0001"
+    for bad in ((2023, 2, 29), (1900, 2, 29), (2026, 13, 1), (2026, 0, 1), (2026, 4, 31), (0, 1, 1), (10000, 1, 1)):
+        with pytest.raises(LB.LastroError):
+            LB.format_date(*bad)
+    assert LB.format_date(2000, 2, 29) == "February 29, 2000"
+
+
+def test_decode_refuses_unknown_ids(tok):
+    for bad in ([tok.vocab_size], [-1], [1, 2, 10 ** 6]):
+        with pytest.raises(LB.LastroError) as e:
+            tok.decode(bad)
+        assert e.value.code == LB.E_ARG
+    assert tok.decode([]) == ""
+
+
+def _variant(tmp_path, edit):
+    with open(TOK_JSON) as f:
+        spec = json.load(f)
+    edit(spec)
+    p = tmp_path / "t.json"
+    p.write_text(json.dumps(spec))
+    return str(p)
+
+
+@pytest.mark.parametrize("what", ["normalizer", "prefix_space", "no_regex", "decoder", "dropout", "unk", "byte_fallback",
+                                  "ignore_merges", "suffix", "lstrip", "normalized_added", "bad_merge", "sparse"])
+def test_refuses_configurations_it_does_not_cover(tmp_path, what):
+    """tokenizador.rs:221-278: a tokenizer.json outside the Granite configuration is refused, naming the field."""
+    edits = {
+        "normalizer": lambda s: s.__setitem__("normalizer", {"type": "NFC"}),
+        "prefix_space": lambda s: s["pre_tokenizer"].__setitem__("add_prefix_space", True),
+        "no_regex": lambda s: s["pre_tokenizer"].__setitem__("use_regex", False),
+        "decoder": lambda s: s.__setitem__("decoder", {"type": "BPEDecoder", "suffix": ""}),
+        "dropout": lambda s: s["model"].__setitem__("dropout", 0.1),
+        "unk": lambda s: s["model"].__setitem__("unk_token", "<|end_of_text|>"),
+        "byte_fallback": lambda s: s["model"].__setitem__("byte_fallback", True),
+        "ignore_merges": lambda s: s["model"].__setitem__("ignore_merges", True),
+        "suffix": lambda s: s["model"].__setitem__("end_of_word_suffix", "</w>"),
+        "lstrip": lambda s: s["added_tokens"][0].__setitem__("lstrip", True),
+        "normalized_added": lambda s: s["added_tokens"][1].__setitem__("normalized", True),
+        "bad_merge": lambda s: s["model"]["merges"].append(["Ġthe", "zzzz_not_a_token"]),
+        "sparse": lambda s: s["model"]["vocab"].__setitem__("Ġfar_away", 10 ** 7),
+    }
+    with pytest.raises(LB.LastroError) as e:
+        LB.Tokenizer(_variant(tmp_path, edits[what]))
+    assert e.value.code == LB.E_UNSUPPORTED
+    assert "outside the supported configuration" in str(e.value)
+
+
+def test_io_and_parse_errors(tmp_path):
+    with pytest.raises(LB.LastroError) as e:
+        LB.Tokenizer(str(tmp_path / "absent.json"))
+    assert e.value.code == LB.E_IO
+    with pytest.raises(LB.LastroError) as e:
+        LB.Tokenizer(json_text="{not json")
+    assert e.value.code == LB.E_ARG
+
+
+def test_live_ids_equal_tokenizers_on_random_text(tok, hf):
+    rng = random.Random(11)
+    alphabet = [chr(c) for c in range(0x20, 0x7F)] + list("\t\n\r  é日😀ⅫⓐА'") + ["<|end_of_text|>", "<|ab|>", "'s"]
+    for _ in range(2000):
+        t = "".join(rng.choice(alphabet) for _ in range(rng.randint(0, 60)))
+        assert tok.encode(t) == hf.encode(t, add_special_tokens=False).ids, repr(t)
+
+
+def test_live_sweep_of_every_scalar_value(tok, hf):
+    """Every Unicode scalar value in the reference's sweep pattern ("a" c "1" c " " per code point, 512 per text):
+    the pre-tokenizer classes (\\p{L}, \\p{N}, \\s tables), the dropped bytes and the merges against `tokenizers`."""
+    cps = [c for c in range(0x110000) if not 0xD800 <= c <= 0xDFFF]
+    texts = ["".join(f"a{chr(c)}1{chr(c)} " for c in cps[i:i + 512]) for i in range(0, len(cps), 512)]
+    got = [tok.encode(t) for t in texts]
+    want = [e.ids for e in hf.encode_batch(texts, add_special_tokens=False)]
+    bad = [i for i in range(len(texts)) if got[i] != want[i]]
+    assert not bad, f"{len(bad)} of {len(texts)} sweep texts differ, first at U+{cps[bad[0] * 512]:04X}"
+
+
+def test_live_pretokenizer_pieces_equal_tokenizers(hf):
+    from tokenizers import pre_tokenizers
+    pt = pre_tokenizers.ByteLevel(add_prefix_space=False, use_regex=True)
+    rng = random.Random(3)
+    alphabet = list(" \t\n\r 　\u0085abcXYZ019'sdtmlrve!?.,;é日Ⅻⓐ٣")
+    for _ in range(3000):
+        t = "".join(rng.choice(alphabet) for _ in range(rng.randint(1, 30)))
+        want = [p for p, _ in pt.pre_tokenize_str(t)]
+        got = ["".join(LB_BYTE_SYMBOLS[b] for b in piece.encode()) for piece in LB.pretokenize(t)]
+        assert got == want, repr(t)
+
+
+def _byte_symbols():
+    out, n = {}, 0
+    for b in range(256):
+        if 33 <= b <= 126 or 161 <= b <= 172 or 174 <= b <= 255:
+            out[b] = chr(b)
+        else:
+            out[b] = chr(256 + n)
+            n += 1
+    return out
+
+
+LB_BYTE_SYMBOLS = _byte_symbols()
+
+
+def test_encode_refuses_invalid_utf8(tok):
+    import ctypes as C
+    n = C.c_int32()
+    for raw in (b"\xff", b"a\xc0\x80", b"\xed\xa0\x80", b"\xf4\x90\x80\x80", b"\xe2\x82"):
+        assert LB.lib().lastro_tokenizer_encode(tok.h, raw, len(raw), None, 0, C.byref(n)) == LB.E_ARG
