@@ -169,9 +169,9 @@ int lastro_model_trace(lastro_model *model, int32_t steps, float *exposed_ms, fl
                        int32_t n_kinds, float *step_ms);
 /* the stamps of launch `launch` (in step order) of the last step lastro_model_trace timed: for each of up to 1024
  * CTAs, LASTRO_TRACE_WORDS words: global-timer ns of start, release from griddepcontrol.wait and exit, then 7 of the
- * kernel's own milestones (0 where not stamped), then the SM the CTA ran on; words >= 1024 * LASTRO_TRACE_WORDS.
- * Diagnostics only. */
-#define LASTRO_TRACE_WORDS 11
+ * kernel's own milestones (0 where not stamped), then the SM the CTA ran on, then thread 0's SM clock (clock64) at
+ * its start and exit and its global-timer exit; words >= 1024 * LASTRO_TRACE_WORDS.  Diagnostics only. */
+#define LASTRO_TRACE_WORDS 14
 int lastro_model_trace_raw(const lastro_model *model, int32_t launch, unsigned long long *out, int32_t words);
 /* tuning: use CUDA graphs (default 1), programmatic dependent launch between the per-layer kernels (default 1),
  * and the fused step -- the whole step as one persistent cooperative launch, one CTA per SM -- where the model's
@@ -194,12 +194,15 @@ int lastro_model_set_moe(lastro_model *model, int32_t one_launch);
  * computes the router logits of the layer's input, the top-k of which the output projection's CTAs hint into L2 while
  * the attention runs); LASTRO_TUNE_SPEC_STAGE instead has each gate_up CTA stream the rows of the expert predicted for
  * its slot into shared memory before the routing is known (experts the prediction missed are staged after it).  Both
- * are off by default: on C3 they measure even with the plain chain.  Results are bitwise the same for every flag. */
+ * are off by default: on C3 they measure even with the plain chain.  LASTRO_TUNE_ATTN_MMA scores and sums bf16 K/V
+ * on tensor cores (mma.sync with q and the probabilities split into bf16 hi + lo, a relative residue below 2^-16)
+ * instead of f32 CUDA-core dots.  Results are bitwise the same for every flag but LASTRO_TUNE_ATTN_MMA. */
 #define LASTRO_TUNE_OPROJ_SMEM 1
 #define LASTRO_TUNE_PREFETCH_DOWN 2
 #define LASTRO_TUNE_ATTN_BULK 4
 #define LASTRO_TUNE_SPEC_L2 8
 #define LASTRO_TUNE_SPEC_STAGE 16
+#define LASTRO_TUNE_ATTN_MMA 32
 int lastro_model_set_tuning(lastro_model *model, int32_t attn_splits, int32_t attn_merge, int32_t flags);
 /* 1 when the MoE blocks run as one launch per layer */
 int lastro_model_moe(const lastro_model *model);

@@ -21,27 +21,6 @@ template <int N>
 LDEV void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
-LDEV void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(addr));
-}
-// d += a (16x16, row) * b (16x8, col), bf16 operands, f32 accumulators
-LDEV void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// shared tiles are rows of 64 bf16 (128 bytes = 8 chunks of 16 bytes); chunk c of row r sits at c ^ (r & 7) so that
-// the 8 rows one ldmatrix phase reads fall in 8 different bank groups
-LDEV uint32_t swz(int row, int chunk) { return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4)); }
-
-LDEV void split_bf16(float v, uint16_t& hi, uint16_t& lo) {
-    hi = f32_to_bf16_rne(v);
-    lo = f32_to_bf16_rne(__fsub_rn(v, __uint_as_float((uint32_t)hi << 16)));
-}
 
 // ---- bounded waits on flags written by other GPUs (global_ns: common.cuh) -----------------------------------------
 LDEV unsigned int ld_acquire_sys(const unsigned int* p) {
@@ -1466,12 +1445,6 @@ cudaError_t make_tile_map(CUtensorMap* map, const void* base, uint64_t rows, uin
 // pages, each writing a partial (m, l, acc); the last CTA of (token, KV head) merges them in split order.
 // ------------------------------------------------------------------------------------------------------------------
 namespace {
-LDEV void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(addr));
-}
-LDEV uint32_t pack_bf16(uint16_t lo, uint16_t hi) { return (uint32_t)lo | ((uint32_t)hi << 16); }
 LDEV void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }

@@ -503,6 +503,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
             if ((e = launch_battention_tc(ba, &m->kvmaps[2 * l], &m->kvmaps[2 * l + 1], s)) != cudaSuccess) return e;
         } else {
             aa.tma = m->attn_tma ? 1 : 0;
+            aa.mma = m->attn_mma && !aa.kv_f32 && m->G <= 8 ? 1 : 0;
             if ((e = launch_attention(aa, s, pdl, aa.tma ? &m->kvboxmaps[2 * l] : nullptr,
                                       aa.tma ? &m->kvboxmaps[2 * l + 1] : nullptr)) != cudaSuccess)
                 return e;
@@ -1441,6 +1442,7 @@ extern "C" int lastro_model_set_tuning(lastro_model* m, int32_t attn_splits, int
     m->gu_prefetch_down = (flags & LASTRO_TUNE_PREFETCH_DOWN) != 0;
     m->attn_tma = !m->kvboxmaps.empty() && (flags & LASTRO_TUNE_ATTN_BULK) == 0;
     m->spec_mode = (flags & LASTRO_TUNE_SPEC_STAGE) ? 1 : (flags & LASTRO_TUNE_SPEC_L2) ? 2 : 0;
+    m->attn_mma = (flags & LASTRO_TUNE_ATTN_MMA) != 0;
     return LASTRO_OK;
 }
 

@@ -183,6 +183,7 @@ struct lastro_model {
     // whether it uses them (default) or plain bulk copies (LASTRO_TUNE_ATTN_BULK)
     std::vector<CUtensorMap> kvboxmaps;
     bool attn_tma = false;
+    bool attn_mma = false;  // bf16 K/V scored and summed on tensor cores (LASTRO_TUNE_ATTN_MMA)
     // the MoE block as one persistent launch per layer (moe_kernel) where the shapes fit it and the option is on (off
     // by default), else the gate_up and down kernels; its grid barrier's counter
     lastro::MoePlan moe{};

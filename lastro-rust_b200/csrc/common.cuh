@@ -23,9 +23,10 @@ LDEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "m
 // ---- in-graph timeline (lastro_model_trace) -----------------------------------------------------------------------
 // With a non-null trace base, every CTA of a launch stamps the global timer (ns) into its own kTraceWords words: [0]
 // when thread 0 starts, [1] when thread 0 passes griddepcontrol.wait, [2] the latest exit of any warp (atomicMax by
-// lane 0 of each warp; the destructor runs on every return path), [3..] the kernel's own milestones (mark), the last
-// word the SM id.  The host reduces over CTAs: min start, min release, max
-// end.  A null base (the product path) costs one predicated branch per stamp.
+// lane 0 of each warp; the destructor runs on every return path), [3..] the kernel's own milestones (mark), then
+// the SM id, then thread 0's SM clock (clock64) at its start and exit and its global-timer exit (the clock rate the
+// CTA ran at).  The host reduces over CTAs: min start, min release, max end.  A null base (the product path) costs
+// one predicated branch per stamp.
 // the memory clobber keeps loads and stores from moving across a stamp (without it a stamp can land before work that
 // the source places ahead of it)
 LDEV unsigned long long global_ns() {
@@ -44,7 +45,13 @@ struct CtaTrace {
             unsigned sm;
             asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
             p[3 + kTraceMarks - 1] = sm;  // the last milestone word holds the SM the CTA runs on
+            p[3 + kTraceMarks] = clock64_();
         }
+    }
+    LDEV static unsigned long long clock64_() {
+        unsigned long long c;
+        asm volatile("mov.u64 %0, %%clock64;" : "=l"(c)::"memory");
+        return c;
     }
     LDEV void released() const {
         if (p && threadIdx.x == 0) p[1] = global_ns();
@@ -56,6 +63,10 @@ struct CtaTrace {
     }
     LDEV ~CtaTrace() {
         if (p && (threadIdx.x & 31) == 0) atomicMax(p + 2, global_ns());
+        if (p && threadIdx.x == 0) {
+            p[3 + kTraceMarks + 1] = clock64_();
+            p[3 + kTraceMarks + 2] = global_ns();
+        }
     }
 };
 
@@ -143,6 +154,35 @@ LDEV bool last_block_arrives(unsigned int* counter, unsigned int total, bool* fl
     bool last = *flag_smem;
     if (last) __threadfence();
     return last;
+}
+
+// ---- warp-level tensor-core tiles (mma.sync m16n8k16, bf16 operands, f32 accumulators) ------------------------
+LDEV void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+LDEV void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+// d += a (16x16, row) * b (16x8, col), bf16 operands, f32 accumulators
+LDEV void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// shared tiles are rows of 64 bf16 (128 bytes = 8 chunks of 16 bytes); chunk c of row r sits at c ^ (r & 7) so that
+// the 8 rows one ldmatrix phase reads fall in 8 different bank groups (the 128-byte TMA swizzle of 1024-byte
+// aligned boxes)
+LDEV uint32_t swz(int row, int chunk) { return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4)); }
+LDEV uint32_t pack_bf16(uint16_t lo, uint16_t hi) { return (uint32_t)lo | ((uint32_t)hi << 16); }
+// v = hi + lo with both bf16: an f32 operand of a bf16 product kept to a relative 2^-17
+LDEV void split_bf16(float v, uint16_t& hi, uint16_t& lo) {
+    hi = f32_to_bf16_rne(v);
+    lo = f32_to_bf16_rne(__fsub_rn(v, __uint_as_float((uint32_t)hi << 16)));
 }
 
 // ---- bulk (TMA) copies global -> shared, completed on an mbarrier ----------------------------------------------

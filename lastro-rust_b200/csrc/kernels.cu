@@ -198,6 +198,116 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
 // ------------------------------------------------------------------------------------------------------------------
 constexpr int kAttnWarps = 8;
 
+// One warp's share of a split on tensor cores (bf16 K/V): the warp takes the split's rows in groups of 16 (positions
+// p0 + g0 .. g0 + 15 at staged row g0 + roff; K/V rows of 128 bytes, 128-byte swizzled when `swizzled`).  Per group
+// S = Q K^T with the G query heads as the MMA's 16 rows (padded with zeros) and q split into bf16 hi + lo, the online
+// softmax per head across the quad of lanes that holds it, and O += P V with P split into hi + lo from the S
+// fragments and V through ldmatrix.trans.  Rows past the split re-read its last row (finite) and get P = 0.  Writes
+// the warp's (m, l, acc) for the G heads.
+template <int G>
+LDEV void attention_rows_mma(const AttnArgs& a, const unsigned char* kt, const unsigned char* vt,
+                             const float (*sq)[kHeadDim], int roff, bool swizzled, int nrow, float* wm, float* wl,
+                             float (*wacc)[kHeadDim]) {
+    constexpr int NW = kAttnWarps;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gq = lane >> 2, tq = lane & 3;
+    const int mi = lane >> 3, r8 = lane & 7;
+    uint32_t qh[4][2], ql[4][2];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            float2 v = make_float2(0.f, 0.f);
+            if (gq < G) v = *reinterpret_cast<const float2*>(&sq[gq][16 * kk + 8 * hf + 2 * tq]);
+            uint16_t h0, l0, h1, l1;
+            split_bf16(v.x, h0, l0);
+            split_bf16(v.y, h1, l1);
+            qh[kk][hf] = pack_bf16(h0, h1);
+            ql[kk][hf] = pack_bf16(l0, l1);
+        }
+    const uint32_t sK = smem_addr(kt), sV = smem_addr(vt);
+    const int last = roff + nrow - 1;  // staged row of the split's last position
+    auto row_addr = [&](uint32_t base, int row, int chunk) {
+        row = min(row, last);
+        return base + (swizzled ? swz(row, chunk) : (uint32_t)(row * 128 + (chunk << 4)));
+    };
+    float mr = -INFINITY, lr = 0.0f;
+    float o[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) o[j][c] = 0.0f;
+    for (int g0 = warp * 16; g0 < nrow; g0 += NW * 16) {
+        const int ib = g0 + roff;
+        float sf[2][4];
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) sf[q][c] = 0.0f;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            uint32_t b[4];
+            ldsm_x4(row_addr(sK, ib + (mi >> 1) * 8 + r8, kk * 2 + (mi & 1)), b);
+            const uint32_t ah[4] = {qh[kk][0], 0u, qh[kk][1], 0u}, al[4] = {ql[kk][0], 0u, ql[kk][1], 0u};
+            mma_bf16(sf[0], ah, b[0], b[1]);
+            mma_bf16(sf[1], ah, b[2], b[3]);
+            mma_bf16(sf[0], al, b[0], b[1]);
+            mma_bf16(sf[1], al, b[2], b[3]);
+        }
+        const int rr[4] = {g0 + 2 * tq, g0 + 2 * tq + 1, g0 + 8 + 2 * tq, g0 + 9 + 2 * tq};
+        const float raw[4] = {sf[0][0], sf[0][1], sf[1][0], sf[1][1]};
+        float sc[4], cmax = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            sc[i] = rr[i] < nrow ? __fmul_rn(raw[i], a.scale) : -INFINITY;
+            cmax = fmaxf(cmax, sc[i]);
+        }
+        cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 1));
+        cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 2));
+        const float mn = fmaxf(mr, cmax);
+        const float alpha = mr == -INFINITY ? 0.0f : expf(mr - mn);
+        float pv[4], ps = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            pv[i] = rr[i] < nrow ? expf(sc[i] - mn) : 0.0f;
+            ps += pv[i];
+        }
+        ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+        lr = lr * alpha + ps;
+        mr = mn;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            o[j][0] *= alpha;
+            o[j][1] *= alpha;
+        }
+        uint16_t h[4], l[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) split_bf16(pv[i], h[i], l[i]);
+        const uint32_t ph[4] = {pack_bf16(h[0], h[1]), 0u, pack_bf16(h[2], h[3]), 0u};
+        const uint32_t pl[4] = {pack_bf16(l[0], l[1]), 0u, pack_bf16(l[2], l[3]), 0u};
+#pragma unroll
+        for (int jp = 0; jp < 4; ++jp) {
+            uint32_t b[4];
+            ldsm_x4_trans(row_addr(sV, ib + (mi & 1) * 8 + r8, 2 * jp + (mi >> 1)), b);
+            mma_bf16(o[2 * jp], ph, b[0], b[1]);
+            mma_bf16(o[2 * jp + 1], ph, b[2], b[3]);
+            mma_bf16(o[2 * jp], pl, b[0], b[1]);
+            mma_bf16(o[2 * jp + 1], pl, b[2], b[3]);
+        }
+    }
+    if (gq < G) {
+        if (tq == 0) {
+            wm[gq] = mr;
+            wl[gq] = lr;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            wacc[gq][8 * j + 2 * tq] = o[j][0];
+            wacc[gq][8 * j + 2 * tq + 1] = o[j][1];
+        }
+    }
+}
+
 template <bool KV_F32, int G, bool CL>
 __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(const __grid_constant__ CUtensorMap kmap,
                                                                     const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
@@ -300,6 +410,9 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(const __grid
         acc1[g] = 0.0f;
     }
     const int nrow = ok ? p1 - p0 : 0;
+    if (!KV_F32 && G <= 8 && a.mma) {
+        attention_rows_mma<G>(a, kt, vt, sq, roff, tma, nrow, wm[warp], wl[warp], wacc[warp]);
+    } else {
     // rows per warp and pass: 16 (half the lanes) when that already covers the split in one pass of the 8 warps, so
     // that every warp takes a share of a short split, else 32
     const int rw = nrow <= NW * 16 ? 16 : 32;
@@ -401,7 +514,6 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(const __grid
             }
         }
     }
-    trace_.mark(3);
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         if (lane == 0) {
@@ -411,6 +523,8 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(const __grid
         wacc[warp][g][2 * lane] = acc0[g];
         wacc[warp][g][2 * lane + 1] = acc1[g];
     }
+    }
+    trace_.mark(3);
     __syncthreads();
     trace_.mark(4);
     // this CTA's partial: warps merged; layout [head][split][...] so the consumer reads each head's splits together

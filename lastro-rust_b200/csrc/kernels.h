@@ -21,7 +21,7 @@ namespace lastro {
 // in-graph timeline: CTAs per launch that stamp their three words (CtaTrace in common.cuh)
 constexpr int kTraceMaxCtas = 1024;
 constexpr int kTraceMarks = 8;
-constexpr int kTraceWords = 3 + kTraceMarks;  // per CTA: start, release, end, milestones
+constexpr int kTraceWords = 3 + kTraceMarks + 3;  // per CTA: start, release, end, milestones + SM id, clocks
 
 // Linear weights are bf16 ([rows, cols] row-major) or Q8_0.  A Q8_0 row on the device is its cols int8 values, then its
 // cols/32 fp16 block scales, padded to a multiple of 16 bytes (so rows stay 16-byte aligned for bulk copies); weight =
@@ -78,6 +78,8 @@ struct AttnArgs {
                              // left for the output projection (OprojArgs part_acc)
     int cluster;             // 1: the splits of a KV head form a thread-block cluster that merges them in distributed
                              // shared memory (splits <= 8; batch-1 only)
+    int mma;                 // 1: bf16 K/V scored and summed on tensor cores (mma.sync, q and p split into bf16 hi + lo),
+                             // else on CUDA cores in f32
     int tma;                 // 1: bf16 K/V staged by 8-row TMA boxes with the 128-byte swizzle (launch_attention's maps:
                              // make_kv_box_map over the layer's pools; page_size a multiple of 8), else bulk copies
     float scale;

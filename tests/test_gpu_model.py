@@ -299,14 +299,20 @@ def test_profile_direct_launches_report_every_kernel(gpu_ctx):
     m.close()
 
 
-@pytest.mark.parametrize("attn_tc", [True, False], ids=["tensor-core-attention", "cuda-core-attention"])
-def test_bf16_kv_attention_kernels_match_oracle(gpu_ctx, pool, attn_tc):
-    """The chain with bf16 KV on either attention kernel (tensor cores with TMA page loads, the default; or the CUDA-core
-    split kernel) against the oracle storing bf16-rounded K/V (Session(kv_bf16=True)): 150 positions, three KV pages,
-    so the 16 context splits of the tensor-core kernel hold 0, 1 or 2 pages."""
+@pytest.mark.parametrize("attn_tc,mma,splits", [(True, False, 16), (False, False, 16), (False, True, 16),
+                                                 (False, True, 8)],
+                         ids=["batched-tensor-core-kernel", "split-kernel-cuda-cores", "split-kernel-mma-16",
+                              "split-kernel-mma-8"])
+def test_bf16_kv_attention_kernels_match_oracle(gpu_ctx, pool, attn_tc, mma, splits):
+    """The chain with bf16 KV on each attention form (the batched step's tensor-core kernel with TMA page loads; the
+    split kernel on CUDA cores, the default, or on tensor cores) against the oracle storing bf16-rounded K/V
+    (Session(kv_bf16=True)): 150 positions, three KV pages, so the context splits hold 0, 1 or 2 pages and every
+    offset of a split's rows within the 16-row groups of the tensor-core form."""
     cfg = CFG.TINY_768
     w = reference_tiny_weights(cfg)
     m = gpu_model(gpu_ctx, cfg, w, 256, "bf16", False, attn_tc)
+    if not attn_tc:
+        m.set_tuning(splits, 0, attn_mma=mma)
     om = O.Model(cfg, weights=w)
     s = O.Session(om, pool, 256, kv_bf16=True)
     for t, tok in enumerate(toks_like_reference(150, cfg["vocab"])):
@@ -436,9 +442,10 @@ def test_attention_split_and_merge_variants_match_oracle(gpu_ctx, pool, splits, 
     m.close()
 
 
+@pytest.mark.parametrize("mma", [False, True], ids=["cuda-cores", "tensor-cores"])
 @pytest.mark.parametrize("splits,merge", [(16, 0), (8, 0), (16, 1), (8, 2)],
                          ids=["16-last-cta", "8-last-cta", "16-oproj", "8-cluster"])
-def test_bf16_kv_staged_by_swizzled_boxes_is_bitwise_the_bulk_copy_staging(gpu_ctx, splits, merge):
+def test_bf16_kv_staged_by_swizzled_boxes_is_bitwise_the_bulk_copy_staging(gpu_ctx, splits, merge, mma):
     """bf16 K/V staged as 8-row TMA boxes with the 128-byte swizzle (the default) against one bulk copy per page run:
     the same rows in the same order, so logits and routes are bitwise equal, over 150 positions (three 64-position
     pages; split boundaries at every offset within a box, the new row inside a staged box or starting one)."""
@@ -446,8 +453,8 @@ def test_bf16_kv_staged_by_swizzled_boxes_is_bitwise_the_bulk_copy_staging(gpu_c
     w = reference_tiny_weights(cfg)
     a = gpu_model(gpu_ctx, cfg, w, 256, "bf16")
     b = gpu_model(gpu_ctx, cfg, w, 256, "bf16")
-    a.set_tuning(splits, merge)
-    b.set_tuning(splits, merge, attn_bulk=True)
+    a.set_tuning(splits, merge, attn_mma=mma)
+    b.set_tuning(splits, merge, attn_bulk=True, attn_mma=mma)
     for t, tok in enumerate(toks_like_reference(150, cfg["vocab"])):
         la, na, ia, _ = a.step(tok)
         lb, nb, ib, _ = b.step(tok)

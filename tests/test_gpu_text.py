@@ -27,7 +27,8 @@ def test_chat_round_trip_matches_the_oracle(gpu_ctx, pool):
     messages = [{"role": "user", "content": "Quem é você? Answer in one line, please: it's a test."}]
     text, ids = LB.chat(m, tok, messages, 24, date="November 07, 2026")
     prompt = tok.encode(LB.render_chat(messages, True, "November 07, 2026"))
-    assert prompt[-3:] == tok.encode("<|start_of_role|>assistant<|end_of_role|>")
+    sfx = tok.encode("<|start_of_role|>assistant<|end_of_role|>")
+    assert prompt[-len(sfx):] == sfx
     # the oracle: the prompt, then greedy ids (last maximum) until the EOS or 24 new ids
     for t in prompt[:-1]:
         s.step(int(t))
