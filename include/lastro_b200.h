@@ -168,10 +168,9 @@ int lastro_model_profile(lastro_model *model, int32_t steps, float *kernel_ms, i
 int lastro_model_trace(lastro_model *model, int32_t steps, float *exposed_ms, float *span_ms, float *wait_ms,
                        int32_t n_kinds, float *step_ms);
 /* the stamps of launch `launch` (in step order) of the last step lastro_model_trace timed: for each of up to 1024
- * CTAs, LASTRO_TRACE_WORDS words: global-timer ns of start, release from griddepcontrol.wait and exit, then 7 of the
- * kernel's own milestones (0 where not stamped), then the SM the CTA ran on, then thread 0's SM clock (clock64) at
- * its start and exit and its global-timer exit; words >= 1024 * LASTRO_TRACE_WORDS.  Diagnostics only. */
-#define LASTRO_TRACE_WORDS 14
+ * CTAs, LASTRO_TRACE_WORDS words: global-timer ns of start, release from griddepcontrol.wait and exit, then 8 of the
+ * kernel's own milestones (0 where not stamped); words >= 1024 * LASTRO_TRACE_WORDS.  Diagnostics only. */
+#define LASTRO_TRACE_WORDS 11
 int lastro_model_trace_raw(const lastro_model *model, int32_t launch, unsigned long long *out, int32_t words);
 /* tuning: use CUDA graphs (default 1), programmatic dependent launch between the per-layer kernels (default 1),
  * and the fused step -- the whole step as one persistent cooperative launch, one CTA per SM -- where the model's
@@ -188,18 +187,20 @@ int lastro_model_set_moe(lastro_model *model, int32_t one_launch);
  * 2: the splits of a KV head are one thread-block cluster that merges them in distributed shared memory);
  * flags: LASTRO_TUNE_OPROJ_SMEM stages the output projection's weight rows in shared memory in 256-thread CTAs
  * (else they sit in the registers of 512-thread CTAs); LASTRO_TUNE_PREFETCH_DOWN has the gate_up kernel hint the
- * chosen experts' down rows into L2; LASTRO_TUNE_ATTN_BULK stages bf16 K/V rows with one bulk copy per page run
- * (else 8-row TMA boxes with the 128-byte swizzle, whose reads are free of shared-memory bank conflicts);
+ * chosen experts' down rows into L2; LASTRO_TUNE_ATTN_TMA stages bf16 K/V rows as 8-row TMA boxes with the 128-byte
+ * swizzle, whose reads are free of shared-memory bank conflicts (else one bulk copy per page run, the default);
  * LASTRO_TUNE_SPEC_L2 fetches the experts predicted from the layer's input early (bf16 weights: the qkv kernel
  * computes the router logits of the layer's input, the top-k of which the output projection's CTAs hint into L2 while
  * the attention runs); LASTRO_TUNE_SPEC_STAGE instead has each gate_up CTA stream the rows of the expert predicted for
  * its slot into shared memory before the routing is known (experts the prediction missed are staged after it).  Both
  * are off by default: on C3 they measure even with the plain chain.  LASTRO_TUNE_ATTN_MMA scores and sums bf16 K/V
  * on tensor cores (mma.sync with q and the probabilities split into bf16 hi + lo, a relative residue below 2^-16)
- * instead of f32 CUDA-core dots.  Results are bitwise the same for every flag but LASTRO_TUNE_ATTN_MMA. */
+ * instead of f32 CUDA-core dots.  The cluster merge (attn_merge 2) runs without the TMA and tensor-core forms.
+ * Results are bitwise the same for every flag but LASTRO_TUNE_ATTN_MMA; LASTRO_E_UNSUPPORTED for the TMA or
+ * tensor-core form with f32 KV. */
 #define LASTRO_TUNE_OPROJ_SMEM 1
 #define LASTRO_TUNE_PREFETCH_DOWN 2
-#define LASTRO_TUNE_ATTN_BULK 4
+#define LASTRO_TUNE_ATTN_TMA 4
 #define LASTRO_TUNE_SPEC_L2 8
 #define LASTRO_TUNE_SPEC_STAGE 16
 #define LASTRO_TUNE_ATTN_MMA 32

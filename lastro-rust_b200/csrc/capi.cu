@@ -502,8 +502,8 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
             ba.scale = d.attention_multiplier;
             if ((e = launch_battention_tc(ba, &m->kvmaps[2 * l], &m->kvmaps[2 * l + 1], s)) != cudaSuccess) return e;
         } else {
-            aa.tma = m->attn_tma ? 1 : 0;
-            aa.mma = m->attn_mma && !aa.kv_f32 && m->G <= 8 ? 1 : 0;
+            aa.tma = m->attn_tma && !aa.cluster ? 1 : 0;
+            aa.mma = m->attn_mma && !aa.kv_f32 && !aa.cluster && m->G <= 8 ? 1 : 0;
             if ((e = launch_attention(aa, s, pdl, aa.tma ? &m->kvboxmaps[2 * l] : nullptr,
                                       aa.tma ? &m->kvboxmaps[2 * l + 1] : nullptr)) != cudaSuccess)
                 return e;
@@ -887,7 +887,7 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
             cudaGetLastError();
             m->kvboxmaps.clear();
         }
-        m->attn_tma = !m->kvboxmaps.empty();
+        m->attn_tma = false;  // the boxes measure slower than one bulk copy per page run on C3 (LASTRO_TUNE_ATTN_TMA)
         // off by default: at batch 1 (16 splits, one token) the CUDA-core kernel, whose split merge is one round of
         // loads and shuffles, measures faster on B200 (C3: 16.4 vs 13 us per launch)
         m->attn_tc = false;
@@ -1440,7 +1440,11 @@ extern "C" int lastro_model_set_tuning(lastro_model* m, int32_t attn_splits, int
     m->attn_merge = attn_merge;
     m->oproj_smem = (flags & LASTRO_TUNE_OPROJ_SMEM) != 0;
     m->gu_prefetch_down = (flags & LASTRO_TUNE_PREFETCH_DOWN) != 0;
-    m->attn_tma = !m->kvboxmaps.empty() && (flags & LASTRO_TUNE_ATTN_BULK) == 0;
+    if ((flags & LASTRO_TUNE_ATTN_TMA) && m->kvboxmaps.empty())
+        return set_err(m->ctx, LASTRO_E_UNSUPPORTED, "TMA staging of the attention needs bf16 KV");
+    if ((flags & LASTRO_TUNE_ATTN_MMA) && m->d.kv_dtype == LASTRO_DTYPE_F32)
+        return set_err(m->ctx, LASTRO_E_UNSUPPORTED, "tensor-core attention needs bf16 KV");
+    m->attn_tma = (flags & LASTRO_TUNE_ATTN_TMA) != 0;
     m->spec_mode = (flags & LASTRO_TUNE_SPEC_STAGE) ? 1 : (flags & LASTRO_TUNE_SPEC_L2) ? 2 : 0;
     m->attn_mma = (flags & LASTRO_TUNE_ATTN_MMA) != 0;
     return LASTRO_OK;

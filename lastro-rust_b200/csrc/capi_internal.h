@@ -179,8 +179,8 @@ struct lastro_model {
     // loads through these maps (per layer: K, V); the CUDA-core split kernel by default
     std::vector<CUtensorMap> kvmaps;
     bool attn_tc = false;
-    // bf16 KV: the CUDA-core attention kernel's staging maps (per layer: K, V; 8-row boxes, 128-byte swizzle) and
-    // whether it uses them (default) or plain bulk copies (LASTRO_TUNE_ATTN_BULK)
+    // bf16 KV: the split attention kernel's staging maps (per layer: K, V; 8-row boxes, 128-byte swizzle) and
+    // whether it uses them (LASTRO_TUNE_ATTN_TMA) or one bulk copy per page run (the default)
     std::vector<CUtensorMap> kvboxmaps;
     bool attn_tma = false;
     bool attn_mma = false;  // bf16 K/V scored and summed on tensor cores (LASTRO_TUNE_ATTN_MMA)

@@ -23,15 +23,14 @@ LDEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "m
 // ---- in-graph timeline (lastro_model_trace) -----------------------------------------------------------------------
 // With a non-null trace base, every CTA of a launch stamps the global timer (ns) into its own kTraceWords words: [0]
 // when thread 0 starts, [1] when thread 0 passes griddepcontrol.wait, [2] the latest exit of any warp (atomicMax by
-// lane 0 of each warp; the destructor runs on every return path), [3..] the kernel's own milestones (mark), then
-// the SM id, then thread 0's SM clock (clock64) at its start and exit and its global-timer exit (the clock rate the
-// CTA ran at).  The host reduces over CTAs: min start, min release, max end.  A null base (the product path) costs
-// one predicated branch per stamp.
-// the memory clobber keeps loads and stores from moving across a stamp (without it a stamp can land before work that
-// the source places ahead of it)
+// lane 0 of each warp; the destructor runs on every return path), [3..] the kernel's own milestones (mark).  The host
+// reduces over CTAs: min start, min release, max end.  A null base (the product path) costs one predicated branch per
+// stamp.  The stamps are kept this lean on purpose: a memory clobber on the timer read (which pins a stamp between
+// the loads and stores around it) and stamps of the SM id and clock cost the product path 0.9 % on C3 through the
+// code they leave in every kernel; a stamp may therefore land a little before or after the work around it.
 LDEV unsigned long long global_ns() {
     unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)::"memory");
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
 
@@ -40,33 +39,17 @@ struct CtaTrace {
     LDEV explicit CtaTrace(unsigned long long* base) : p(nullptr) {
         const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
         if (base && cta < (unsigned)kTraceMaxCtas) p = base + kTraceWords * (size_t)cta;
-        if (p && threadIdx.x == 0) {
-            p[0] = global_ns();
-            unsigned sm;
-            asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
-            p[3 + kTraceMarks - 1] = sm;  // the last milestone word holds the SM the CTA runs on
-            p[3 + kTraceMarks] = clock64_();
-        }
-    }
-    LDEV static unsigned long long clock64_() {
-        unsigned long long c;
-        asm volatile("mov.u64 %0, %%clock64;" : "=l"(c)::"memory");
-        return c;
+        if (p && threadIdx.x == 0) p[0] = global_ns();
     }
     LDEV void released() const {
         if (p && threadIdx.x == 0) p[1] = global_ns();
     }
-    // a kernel's own milestone i (< kTraceMarks - 1) as thread `tid` reaches it (diagnostics of the phases inside a
-    // launch)
+    // a kernel's own milestone i (< kTraceMarks) as thread `tid` reaches it (diagnostics of the phases inside a launch)
     LDEV void mark(int i, unsigned tid = 0) const {
         if (p && threadIdx.x == tid) p[3 + i] = global_ns();
     }
     LDEV ~CtaTrace() {
         if (p && (threadIdx.x & 31) == 0) atomicMax(p + 2, global_ns());
-        if (p && threadIdx.x == 0) {
-            p[3 + kTraceMarks + 1] = clock64_();
-            p[3 + kTraceMarks + 2] = global_ns();
-        }
     }
 };
 

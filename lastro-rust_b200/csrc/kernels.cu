@@ -64,7 +64,7 @@ cudaError_t launch_cluster_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, c
 // ------------------------------------------------------------------------------------------------------------------
 // qkv_rope: one warp per row pair (j, j + d/2) of a head, so RoPE's rotate_half partner is in the same warp.
 // ------------------------------------------------------------------------------------------------------------------
-template <int NCH, bool KV_F32, bool Q8>
+template <int NCH, bool KV_F32, bool Q8, bool SPEC = false>
 __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
     const CtaTrace trace_(a.trace);
     constexpr int BLOCK = 128;
@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
     float4 ln[NV];
     vec_load_ldg<BLOCK, NV>(a.ln, a.H, ln);
     // predicted routing: this CTA's router row times the MoE norm weight, in the layout of v
-    const bool spec = a.spec_out && (int)blockIdx.x < a.spec_E;
+    const bool spec = SPEC && (int)blockIdx.x < a.spec_E;  // a separate instantiation: its registers cost the chain
     float4 sw4[NV];
     if (spec) {
         const uint2* rr = reinterpret_cast<const uint2*>(a.spec_router + (size_t)blockIdx.x * a.H);  // 4 bf16 per uint2
@@ -308,7 +308,9 @@ LDEV void attention_rows_mma(const AttnArgs& a, const unsigned char* kt, const u
     }
 }
 
-template <bool KV_F32, int G, bool CL>
+// MODE (bf16 K/V only; 0 with f32 K/V): bit 0 stages K/V as 8-row TMA boxes with the 128-byte swizzle (AttnArgs tma),
+// bit 1 scores and sums on tensor cores (AttnArgs mma); mode 0 is the default chain's form
+template <bool KV_F32, int G, bool CL, int MODE = 0>
 __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(const __grid_constant__ CUtensorMap kmap,
                                                                     const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
     const CtaTrace trace_(a.trace);
@@ -321,7 +323,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(const __grid
     extern __shared__ __align__(128) unsigned char smem_raw[];
     // tma: K/V staged as 8-row boxes (TMA, 128-byte swizzle) from position p0 rounded down to a multiple of 8, each
     // box 1024-byte aligned; else one bulk copy per page run from position p0, unswizzled
-    const bool tma = !KV_F32 && a.tma;
+    constexpr bool tma = !KV_F32 && (MODE & 1);
     const int cap = tma ? attn_tma_rows(a.split_cap) : a.split_cap;
     unsigned char* kt = tma ? reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023)
                             : smem_raw;  // [cap, RB]
@@ -349,7 +351,8 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(const __grid
     const int p0 = (int)(((long long)len * s) / NS), p1 = (int)(((long long)len * (s + 1)) / NS);
     const int pb = min(p1, pos);  // rows [p0, pb) are final already
     const int r_base = tma ? (p0 & ~7) : p0;  // position of staged row 0
-    const int roff = p0 - r_base, swz = tma ? 7 : 0;
+    const int roff = p0 - r_base;
+    constexpr int swz = tma ? 7 : 0;
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         uint32_t tx = 0u;
@@ -410,15 +413,12 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(const __grid
         acc1[g] = 0.0f;
     }
     const int nrow = ok ? p1 - p0 : 0;
-    if (!KV_F32 && G <= 8 && a.mma) {
+    if constexpr (!KV_F32 && (MODE & 2)) {
         attention_rows_mma<G>(a, kt, vt, sq, roff, tma, nrow, wm[warp], wl[warp], wacc[warp]);
     } else {
-    // rows per warp and pass: 16 (half the lanes) when that already covers the split in one pass of the 8 warps, so
-    // that every warp takes a share of a short split, else 32
-    const int rw = nrow <= NW * 16 ? 16 : 32;
-    for (int base = warp * rw; base < nrow; base += NW * rw) {
+    for (int base = warp * 32; base < nrow; base += NW * 32) {
         const int r = base + lane;
-        const bool valid = lane < rw && r < nrow;
+        const bool valid = r < nrow;
         float sc[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) sc[g] = 0.0f;
@@ -456,61 +456,38 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(const __grid
                 }
             }
         }
-        // online softmax: the G heads' butterflies interleaved (per head the same steps as warp_max / warp_sum)
-        float scv[G], mx[G], pr[G], sm[G], alpha[G];
+        float pr[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            scv[g] = valid ? __fmul_rn(sc[g], a.scale) : -INFINITY;
-            mx[g] = scv[g];
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-            for (int g = 0; g < G; ++g) mx[g] = fmaxf(mx[g], __shfl_xor_sync(0xffffffffu, mx[g], o));
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const float mn = fmaxf(m[g], mx[g]);
-            pr[g] = valid ? expf(scv[g] - mn) : 0.0f;
-            alpha[g] = (m[g] == -INFINITY) ? 0.0f : expf(m[g] - mn);
-            sm[g] = pr[g];
+            const float scv = valid ? __fmul_rn(sc[g], a.scale) : -INFINITY;
+            const float mn = fmaxf(m[g], warp_max(scv));
+            pr[g] = valid ? expf(scv - mn) : 0.0f;
+            const float alpha = (m[g] == -INFINITY) ? 0.0f : expf(m[g] - mn);
+            l[g] = l[g] * alpha + warp_sum(pr[g]);
+            acc0[g] *= alpha;
+            acc1[g] *= alpha;
             m[g] = mn;
         }
+        const int nj = min(32, nrow - base);
+        for (int jj = 0; jj < nj; ++jj) {
+            const int i = base + jj + roff;
+            float v0, v1;
+            if (KV_F32) {
+                const float2 t = reinterpret_cast<const float2*>(vt + (size_t)i * RB)[lane];
+                v0 = t.x;
+                v1 = t.y;
+            } else {
+                // lane's word (elements 2 lane, 2 lane + 1) sits in chunk lane / 4, swizzled like the K rows
+                const uint32_t t =
+                    reinterpret_cast<const uint32_t*>(vt + (size_t)i * RB)[(((lane >> 2) ^ (i & swz)) << 2) | (lane & 3)];
+                v0 = bf_lo(t);
+                v1 = bf_hi(t);
+            }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-            for (int g = 0; g < G; ++g) sm[g] += __shfl_xor_sync(0xffffffffu, sm[g], o);
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            l[g] = l[g] * alpha[g] + sm[g];
-            acc0[g] *= alpha[g];
-            acc1[g] *= alpha[g];
-        }
-        // P V in blocks of 8 rows, unrolled so that a block's loads and shuffles are in flight together; rows past
-        // nj re-read the last row and get p = 0 (their lanes hold no score)
-        const int nj = min(rw, nrow - base);
-        for (int j0 = 0; j0 < nj; j0 += 8) {
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int jj = j0 + u;
-                const int i = base + min(jj, nj - 1) + roff;
-                float v0, v1;
-                if (KV_F32) {
-                    const float2 t = reinterpret_cast<const float2*>(vt + (size_t)i * RB)[lane];
-                    v0 = t.x;
-                    v1 = t.y;
-                } else {
-                    // lane's word (elements 2 lane, 2 lane + 1) sits in chunk lane / 4, swizzled like the K rows
-                    const uint32_t t = reinterpret_cast<const uint32_t*>(vt + (size_t)i * RB)[(((lane >> 2) ^ (i & swz)) << 2) |
-                                                                                             (lane & 3)];
-                    v0 = bf_lo(t);
-                    v1 = bf_hi(t);
-                }
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const float pj = __shfl_sync(0xffffffffu, pr[g], jj & 31);
-                    acc0[g] = fmaf(pj, v0, acc0[g]);
-                    acc1[g] = fmaf(pj, v1, acc1[g]);
-                }
+            for (int g = 0; g < G; ++g) {
+                const float pj = __shfl_sync(0xffffffffu, pr[g], jj);
+                acc0[g] = fmaf(pj, v0, acc0[g]);
+                acc1[g] = fmaf(pj, v1, acc1[g]);
             }
         }
     }
@@ -688,6 +665,9 @@ __global__ void __launch_bounds__(128) router_kernel(RouterArgs a) {
 // ln, [H, E], prepared once per layer) and of sum h^2; the last CTA sums the shares in a fixed order, applies r_norm,
 // and takes the top-k with block.rs:81-89's order and softmax.  The experts kernel reads r_norm.
 // ------------------------------------------------------------------------------------------------------------------
+// 48 CTAs for the 3B shape: more, smaller CTAs (192 x 8 rows measured 0.25 us faster here) make every gate_up and
+// down CTA reduce 4x the router shares, and those few kilobytes, read by ~450 CTAs at once, cost gate_up's routing
+// 1.1 us (C3: 1.066 vs 1.060 ms per step)
 constexpr int kOpWarps = 16;
 constexpr int kOpRows = 2 * kOpWarps;
 
@@ -758,7 +738,7 @@ LDEV void spec_prefetch_l2(const OprojArgs& a) {
     }
 }
 
-template <int NCH, bool Q8>
+template <int NCH, bool Q8, bool SPEC = false>
 __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
     const CtaTrace trace_(a.trace);
     constexpr int BLOCK = 32 * kOpWarps;
@@ -778,7 +758,7 @@ __global__ void __launch_bounds__(512) oproj_kernel(OprojArgs a) {
         const int n = kOpRows * a.E;
         for (int t = threadIdx.x; t < n; t += BLOCK) wrs[t] = (r0 + t / a.E < a.H) ? __ldg(a.wr_t + (size_t)r0 * a.E + t) : 0.0f;
     }
-    if (a.spec) spec_prefetch_l2(a);
+    if (SPEC) spec_prefetch_l2(a);  // a separate instantiation: the default one carries none of it
     pdl_wait();
     pdl_launch();
     trace_.released();
@@ -948,7 +928,7 @@ LDEV void gu_prefetch_down(const GateUpArgs& a, const int* ids) {
     }
 }
 
-template <int NCH, bool Q8>
+template <int NCH, bool Q8, bool SPEC = false>
 __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
     const CtaTrace trace_(a.trace);
     constexpr int BLOCK = 256, R = kGuPairs, HALF = R / 2;
@@ -967,9 +947,9 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
     const int per_slot = a.I / R;
     const int slot = blockIdx.x / per_slot, j0 = (blockIdx.x - slot * per_slot) * R;
     const bool fused = a.rs.shares != nullptr;
-    const bool spec = fused && a.spec;
-    __shared__ int spid[kMaxTopK];                      // spec: the predicted experts by rank
-    __shared__ unsigned long long spkey[kMaxExperts];
+    const bool spec = SPEC && fused;  // a separate instantiation: the default one carries none of it
+    __shared__ int spid[SPEC ? kMaxTopK : 1];                      // spec: the predicted experts by rank
+    __shared__ unsigned long long spkey[SPEC ? kMaxExperts : 1];
     if (threadIdx.x == 0) {
         mbar_init(&bar[0], 1);
         mbar_init(&bar[1], 1);
@@ -1656,6 +1636,12 @@ cudaError_t launch_qkv_rope(const QkvArgs& a, cudaStream_t s, bool pdl) {
         }
         LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(qkv_rope_kernel<N, false, true>, grid, block, smem, s, pdl, a));
     }
+    if (a.spec_out) {
+        if (a.kv_f32) {
+            LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(qkv_rope_kernel<N, true, false, true>, grid, block, smem, s, pdl, a));
+        }
+        LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(qkv_rope_kernel<N, false, false, true>, grid, block, smem, s, pdl, a));
+    }
     if (a.kv_f32) {
         LASTRO_NCH_SWITCH(chunks_for(a.H), launch_ex(qkv_rope_kernel<N, true, false>, grid, block, smem, s, pdl, a));
     }
@@ -1664,10 +1650,15 @@ cudaError_t launch_qkv_rope(const QkvArgs& a, cudaStream_t s, bool pdl) {
 
 int attn_split_cap(int max_len, int splits) { return (max_len + splits - 1) / splits + 1; }
 
-size_t attn_smem(int max_len, int kv_f32, int splits) {
+// shared memory of the staged K/V rows: contiguous rows from p0, or (tma) whole 8-row boxes, 1024-byte aligned
+static size_t attn_smem_staging(int max_len, int kv_f32, int splits, bool tma) {
     const int cap = attn_split_cap(max_len, splits);
-    if (kv_f32) return (size_t)2 * cap * kHeadDim * 4;
-    return (size_t)2 * attn_tma_rows(cap) * kHeadDim * 2 + 1024;  // + the boxes' 1024-byte alignment
+    if (kv_f32 || !tma) return (size_t)2 * cap * kHeadDim * (kv_f32 ? 4 : 2);
+    return (size_t)2 * attn_tma_rows(cap) * kHeadDim * 2 + 1024;
+}
+
+size_t attn_smem(int max_len, int kv_f32, int splits) {
+    return std::max(attn_smem_staging(max_len, kv_f32, splits, false), attn_smem_staging(max_len, kv_f32, splits, true));
 }
 
 // context splits of the batch-1 attention: 8 while a split's rows fit about one pass of the CTA's 8 warps (256
@@ -1684,9 +1675,12 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl, const 
     const CUtensorMap& km = a.tma ? *kmap : none;
     const CUtensorMap& vm = a.tma ? *vmap : none;
     if (a.cluster && a.seq) return cudaErrorInvalidValue;  // batch-1 only (16 splits: a non-portable cluster size)
-    const size_t smem = attn_smem(a.max_len, a.kv_f32, a.splits);
+    if (a.mma && a.kv_f32) return cudaErrorInvalidValue;
+    if (a.cluster && (a.tma || a.mma)) return cudaErrorInvalidValue;  // the cluster merge runs the default form only
+    const size_t smem = attn_smem_staging(a.max_len, a.kv_f32, a.splits, a.tma != 0);
     if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
     const dim3 grid(a.splits, a.kv_heads, a.seq ? a.tokens : 1), block(32 * kAttnWarps);
+    const int mode = (a.tma ? 1 : 0) | (a.mma ? 2 : 0);
 #define LASTRO_ATTN_G(GV)                                                                                  \
     case GV: {                                                                                             \
         if (a.cluster) {                                                                                   \
@@ -1696,7 +1690,11 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl, const 
                 e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);            \
             return e != cudaSuccess ? e : launch_cluster_ex(k, grid, block, smem, s, pdl, a.splits, km, vm, a); \
         }                                                                                                  \
-        auto k = a.kv_f32 ? attention_kernel<true, GV, false> : attention_kernel<false, GV, false>;        \
+        auto k = a.kv_f32 ? attention_kernel<true, GV, false>                                              \
+                 : mode == 1 ? attention_kernel<false, GV, false, 1>                                       \
+                 : mode == 2 ? attention_kernel<false, GV, false, 2>                                       \
+                 : mode == 3 ? attention_kernel<false, GV, false, 3>                                       \
+                             : attention_kernel<false, GV, false, 0>;                                      \
         cudaError_t e = allow_smem(k, smem);                                                               \
         return e != cudaSuccess ? e : launch_ex(k, grid, block, smem, s, pdl, km, vm, a);                  \
     }
@@ -1750,7 +1748,7 @@ cudaError_t launch_oproj(const OprojArgs& a, cudaStream_t s, bool pdl) {
     if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
 #define LASTRO_OP(N)                                                                  \
     {                                                                                 \
-        auto k = a.q8 ? oproj_kernel<N, true> : oproj_kernel<N, false>;               \
+        auto k = a.q8 ? oproj_kernel<N, true> : a.spec ? oproj_kernel<N, false, true> : oproj_kernel<N, false>; \
         cudaError_t e = allow_smem(k, smem);                                          \
         return e != cudaSuccess ? e : launch_ex(k, grid, block, smem, s, pdl, a);     \
     }
@@ -1843,7 +1841,7 @@ cudaError_t launch_gate_up(const GateUpArgs& a, cudaStream_t s, bool pdl) {
     if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
 #define LASTRO_GU(N)                                                                  \
     {                                                                                 \
-        auto k = a.q8 ? gate_up_kernel<N, true> : gate_up_kernel<N, false>;           \
+        auto k = a.q8 ? gate_up_kernel<N, true> : a.spec ? gate_up_kernel<N, false, true> : gate_up_kernel<N, false>; \
         cudaError_t e = allow_smem(k, smem);                                          \
         return e != cudaSuccess ? e : launch_ex(k, grid, block, smem, s, pdl, a);     \
     }

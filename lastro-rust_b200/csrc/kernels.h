@@ -21,7 +21,7 @@ namespace lastro {
 // in-graph timeline: CTAs per launch that stamp their three words (CtaTrace in common.cuh)
 constexpr int kTraceMaxCtas = 1024;
 constexpr int kTraceMarks = 8;
-constexpr int kTraceWords = 3 + kTraceMarks + 3;  // per CTA: start, release, end, milestones + SM id, clocks
+constexpr int kTraceWords = 3 + kTraceMarks;  // per CTA: start, release, end, milestones
 
 // Linear weights are bf16 ([rows, cols] row-major) or Q8_0.  A Q8_0 row on the device is its cols int8 values, then its
 // cols/32 fp16 block scales, padded to a multiple of 16 bytes (so rows stay 16-byte aligned for bulk copies); weight =

@@ -352,6 +352,8 @@ LDEV void route_topk_warp(float v0, float v1, int E, int k, int* sid, float* sva
 // order, then r = 1/sqrt(sum h^2 / H + eps) (model.rs:141-145), logits = r * share-sums, the top-k by rank counting in
 // block.rs:81-89's order and the softmax over the k.  Every CTA that calls this computes bitwise the same routing.
 // Uses __syncthreads (every thread of the block calls it; blockDim >= E + 1); results in sid/sw (shared), returns r.
+// (Spreading the steps after the share loads over the whole block, one step per barrier, measured slower on C3 than
+// this single warp: gate_up gained 0.3 us, the down kernel lost 0.6 us, 1.034 vs 1.027 ms per step.)
 template <int BLOCK>
 LDEV float route_from_shares(const RouteShares& rs, int E, int k, int H, float* red, int* sid, float* sval, float* sw,
                              float* s_r, bool publish, const CtaTrace* tr = nullptr) {
@@ -378,66 +380,34 @@ LDEV float route_from_shares(const RouteShares& rs, int E, int k, int H, float* 
     red[threadIdx.x] = acc;
     __syncthreads();
     if (tr) tr->mark(3);
-    // the rest spread over the block, one step per barrier (a single warp doing it all took ~1.8 us on B200)
-    __shared__ float slg[kMaxExperts + 1];
-    __shared__ unsigned long long skey[kMaxExperts];
-    // (a) every logit's (and the sum of squares') group partials, summed in group order
-    if (threadIdx.x < E1) {
-        float t = 0.0f;
-        for (int gi = 0; gi < groups; ++gi) t = __fadd_rn(t, red[gi * E1 + threadIdx.x]);
-        slg[threadIdx.x] = t;
-    }
-    __syncthreads();
-    // (b) r = 1/sqrt(sum h^2 / H + eps) (model.rs:141-145), the logits, and their keys in block.rs:81-89's order
-    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(slg[E], (float)H), rs.eps)));
-    float lg = 0.0f;
-    if (threadIdx.x < E) {
-        lg = __fmul_rn(slg[threadIdx.x], r);
-        skey[threadIdx.x] = route_key(lg, threadIdx.x);
-    }
-    __syncthreads();
-    if (tr) tr->mark(4);
-    // (c) each expert's rank among all E (keys are distinct: the index is part of the key); the k first land at theirs
-    if (threadIdx.x < E) {
-        const unsigned long long me = skey[threadIdx.x];
-        int rank = 0;
-        // in blocks of 8 independent loads (the last block's entries past E are read and not counted)
-        for (int j0 = 0; j0 < E; j0 += 8) {
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int j = j0 + u;
-                const unsigned long long kj = skey[j < kMaxExperts ? j : kMaxExperts - 1];
-                rank += (int)(j < E && kj > me);
-            }
-        }
-        if (rank < k) {
-            sid[rank] = threadIdx.x;
-            sval[rank] = lg;
-        }
-        if (publish) rs.logits_out[threadIdx.x] = lg;
-    }
-    if (threadIdx.x == 0) *s_r = r;
-    __syncthreads();
-    // (d) softmax over the k: exp(v - v0), summed in order, divided
     if (warp == 0) {
-        const float ex = lane < k ? expf(__fsub_rn(sval[lane], sval[0])) : 0.0f;
-        float exj[kMaxTopK];
+        float v[2];
 #pragma unroll
-        for (int j = 0; j < kMaxTopK; ++j) exj[j] = __shfl_sync(0xffffffffu, ex, j);
-        float sum = 0.0f;
-#pragma unroll
-        for (int j = 0; j < kMaxTopK; ++j)
-            if (j < k) sum = __fadd_rn(sum, exj[j]);
-        if (lane < k) {
-            sw[lane] = __fdiv_rn(ex, sum);
-            if (publish) {
+        for (int q = 0; q < 2; ++q) {
+            const int e = lane + 32 * q;
+            float t = 0.0f;
+            if (e < E1)
+                for (int gi = 0; gi < groups; ++gi) t = __fadd_rn(t, red[gi * E1 + e]);
+            v[q] = t;
+        }
+        const float ss = __shfl_sync(0xffffffffu, v[E >> 5], E & 31);  // entry E is the sum of squares
+        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), rs.eps)));
+        const float l0 = lane < E ? __fmul_rn(v[0], r) : 0.0f;
+        const float l1 = lane + 32 < E ? __fmul_rn(v[1], r) : 0.0f;
+        if (tr) tr->mark(4);
+        route_topk_warp(l0, l1, E, k, sid, sval, sw);
+        if (lane == 0) *s_r = r;
+        if (publish) {
+            if (lane < E) rs.logits_out[lane] = l0;
+            if (lane + 32 < E) rs.logits_out[lane + 32] = l1;
+            if (lane < k) {
                 rs.ids_out[lane] = sid[lane];
                 rs.weights_out[lane] = sw[lane];
             }
         }
     }
     __syncthreads();
-    return r;
+    return *s_r;
 }
 
 

@@ -20,7 +20,7 @@ LIB_PATH = os.path.join(PKG_DIR, "liblastro_b200.so")
 HEADER = os.path.join(PKG_DIR, "..", "include", "lastro_b200.h")
 
 OK, E_ARG, E_CUDA, E_POISONED, E_FULL, E_NOMEM, E_UNSUPPORTED, E_STATE, E_IO = range(9)
-TRACE_WORDS = 14  # LASTRO_TRACE_WORDS: start, release, exit, 7 milestones, SM id, clocks per CTA
+TRACE_WORDS = 11  # LASTRO_TRACE_WORDS: start, release, exit, 8 milestones per CTA
 DTYPE_BF16, DTYPE_F32, DTYPE_Q8_0 = 1, 2, 3
 
 _lib = None
@@ -584,25 +584,24 @@ class GpuModel:
         self.ctx.check(lib().lastro_model_set_moe(self.h, int(one_launch)))
 
     def trace_raw(self, launch: int) -> np.ndarray:
-        """Stamps of one launch of the last traced step: [1024 CTAs, 14]: global-timer ns (start, release, exit, then
-        the kernel's 7 milestones; 0 where not stamped), the SM id of the CTA, and thread 0's clock64 at start and exit
-        with its global-timer exit."""
+        """Stamps of one launch of the last traced step: [1024 CTAs, 11] global-timer ns (start, release, exit, then
+        the kernel's 8 milestones; 0 where not stamped)."""
         out = np.zeros((1024, TRACE_WORDS), np.uint64)
         self.ctx.check(lib().lastro_model_trace_raw(self.h, launch, _p(out), out.size))
         return out
 
     def set_tuning(self, attn_splits: int = 16, attn_merge: int = 0, oproj_smem: bool = False,
-                   prefetch_down: bool = False, attn_bulk: bool = False, speculation: str | bool = False,
+                   prefetch_down: bool = False, attn_tma: bool = False, speculation: str | bool = False,
                    attn_mma: bool = False):
         """Batch-1 attention: context splits (8, 16, or 0 for the size-based choice) and how they are merged (0 the
         attention's last CTA, 1 the output projection, 2 a thread-block cluster per KV head); the output projection's
         weights in shared memory (256-thread CTAs) or registers; gate_up hinting the down rows into L2; bf16 K/V
-        staged by bulk copies per page run (attn_bulk) or by swizzled 8-row TMA boxes; the experts predicted from
+        staged by swizzled 8-row TMA boxes (attn_tma) or by bulk copies per page run; the experts predicted from
         the layer's input fetched before the routing is known (speculation: "l2" hinted into L2 by the output
         projection, "stage" streamed into the gate_up CTAs' shared memory, False off: the default); bf16 K/V
         attention on tensor cores (attn_mma)."""
         assert speculation in ("l2", "stage", False)
-        flags = (1 if oproj_smem else 0) | (2 if prefetch_down else 0) | (4 if attn_bulk else 0) | \
+        flags = (1 if oproj_smem else 0) | (2 if prefetch_down else 0) | (4 if attn_tma else 0) | \
             {"l2": 8, "stage": 16, False: 0}[speculation] | (32 if attn_mma else 0)
         self.ctx.check(lib().lastro_model_set_tuning(self.h, attn_splits, int(attn_merge), flags))
 

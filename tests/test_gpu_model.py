@@ -446,15 +446,16 @@ def test_attention_split_and_merge_variants_match_oracle(gpu_ctx, pool, splits, 
 @pytest.mark.parametrize("splits,merge", [(16, 0), (8, 0), (16, 1), (8, 2)],
                          ids=["16-last-cta", "8-last-cta", "16-oproj", "8-cluster"])
 def test_bf16_kv_staged_by_swizzled_boxes_is_bitwise_the_bulk_copy_staging(gpu_ctx, splits, merge, mma):
-    """bf16 K/V staged as 8-row TMA boxes with the 128-byte swizzle (the default) against one bulk copy per page run:
+    """bf16 K/V staged as 8-row TMA boxes with the 128-byte swizzle against one bulk copy per page run (the default):
     the same rows in the same order, so logits and routes are bitwise equal, over 150 positions (three 64-position
-    pages; split boundaries at every offset within a box, the new row inside a staged box or starting one)."""
+    pages; split boundaries at every offset within a box, the new row inside a staged box or starting one); the
+    cluster merge runs the bulk-copy form only (both sides)."""
     cfg = CFG.TINY_768
     w = reference_tiny_weights(cfg)
     a = gpu_model(gpu_ctx, cfg, w, 256, "bf16")
     b = gpu_model(gpu_ctx, cfg, w, 256, "bf16")
-    a.set_tuning(splits, merge, attn_mma=mma)
-    b.set_tuning(splits, merge, attn_bulk=True, attn_mma=mma)
+    a.set_tuning(splits, merge, attn_tma=merge != 2, attn_mma=mma and merge != 2)
+    b.set_tuning(splits, merge, attn_mma=mma and merge != 2)
     for t, tok in enumerate(toks_like_reference(150, cfg["vocab"])):
         la, na, ia, _ = a.step(tok)
         lb, nb, ib, _ = b.step(tok)
