@@ -195,7 +195,9 @@ int lastro_model_set_moe(lastro_model *model, int32_t one_launch);
  * its slot into shared memory before the routing is known (experts the prediction missed are staged after it).  Both
  * are off by default: on C3 they measure even with the plain chain.  LASTRO_TUNE_ATTN_MMA scores and sums bf16 K/V
  * on tensor cores (mma.sync with q and the probabilities split into bf16 hi + lo, a relative residue below 2^-16)
- * instead of f32 CUDA-core dots.  The cluster merge (attn_merge 2) runs without the TMA and tensor-core forms.
+ * instead of f32 CUDA-core dots.  LASTRO_TUNE_DOWN_ROUTES has every down CTA reduce the router shares itself instead
+ * of taking the routing gate_up's first CTA publishes (a flag per layer stamped with a step counter, a bounded wait
+ * that falls back to the reduction).  The cluster merge (attn_merge 2) runs without the TMA and tensor-core forms.
  * Results are bitwise the same for every flag but LASTRO_TUNE_ATTN_MMA; LASTRO_E_UNSUPPORTED for the TMA or
  * tensor-core form with f32 KV. */
 #define LASTRO_TUNE_OPROJ_SMEM 1
@@ -204,6 +206,7 @@ int lastro_model_set_moe(lastro_model *model, int32_t one_launch);
 #define LASTRO_TUNE_SPEC_L2 8
 #define LASTRO_TUNE_SPEC_STAGE 16
 #define LASTRO_TUNE_ATTN_MMA 32
+#define LASTRO_TUNE_DOWN_ROUTES 64
 int lastro_model_set_tuning(lastro_model *model, int32_t attn_splits, int32_t attn_merge, int32_t flags);
 /* 1 when the MoE blocks run as one launch per layer */
 int lastro_model_moe(const lastro_model *model);

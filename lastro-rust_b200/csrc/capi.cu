@@ -447,6 +447,7 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         qa.kv_heads = d.kv_heads;
         qa.eps = d.eps;
         qa.trace = slot();
+        qa.step_ctr = m->step_ctr;
         const bool spec = m->spec_mode != 0 && !m->q8 && !moe_on(m);
         if (spec) {
             qa.spec_router = reinterpret_cast<const uint16_t*>(L.router);
@@ -604,6 +605,10 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         ga.down_w = m->gu_prefetch_down ? L.down : nullptr;
         ga.down_row_bytes = wrow_bytes(d.inter, m->q8);
         ga.spec = spec && m->spec_mode == 1 ? m->spec_logits : nullptr;
+        if (m->route_handoff) {
+            ga.route_flag = m->route_flags + l;
+            ga.step_ctr = m->step_ctr;
+        }
         ga.trace = slot();
         if ((e = launch_gate_up(ga, s, pdl)) != cudaSuccess) return e;
         if ((e = mark(pe, s, KK_GATE_UP)) != cudaSuccess) return e;
@@ -627,6 +632,10 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
             da.pf_bytes[0] = (unsigned long long)(m->qd + 2 * m->kvd) * wrow_bytes(d.hidden, m->q8);
             da.pf[1] = N.wo;
             da.pf_bytes[1] = (unsigned long long)d.hidden * wrow_bytes(m->qd, m->q8);
+        }
+        if (m->route_handoff) {
+            da.route_flag = m->route_flags + l;
+            da.step_ctr = m->step_ctr;
         }
         da.trace = slot();
         if ((e = launch_down(da, s, pdl)) != cudaSuccess) return e;
@@ -786,7 +795,8 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
           A.alloc(&m->d_out_ids, (size_t)max_len + 1) || A.alloc(&m->d_prompt, (size_t)max_len + 1) ||
           A.alloc(&m->router_counter, 1) || A.alloc(&m->head_counter, 1) || A.alloc(&m->attn_counters, d.kv_heads) ||
           A.alloc(&m->head_partial, m->head_grid) || A.alloc(&m->d_err, 1) ||
-          A.alloc(&m->op_partial, (size_t)oproj_grid(d.hidden) * (E + 1)) || A.alloc(&m->moe_barrier, 1);
+          A.alloc(&m->op_partial, (size_t)oproj_grid(d.hidden) * (E + 1)) || A.alloc(&m->moe_barrier, 1) ||
+          A.alloc(&m->step_ctr, 1) || A.alloc(&m->route_flags, (size_t)d.layers);
     m->moe_ok = !bad && moe_plan(d.hidden, d.inter, d.k, m->q8, &m->moe);
     // the fused step: one CTA per SM, when the per-CTA shares of every phase fit in shared memory
     int n_sm = 0, coop = 0;
@@ -830,6 +840,8 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
         if (!e) e = cudaMemsetAsync(p, 0, sizeof(int), s);
     if (!e) e = cudaMemsetAsync(m->attn_counters, 0, sizeof(unsigned) * d.kv_heads, s);
     if (!e) e = cudaMemsetAsync(m->moe_barrier, 0, sizeof(unsigned long long), s);
+    if (!e) e = cudaMemsetAsync(m->step_ctr, 0, sizeof(unsigned int), s);
+    if (!e) e = cudaMemsetAsync(m->route_flags, 0, sizeof(unsigned int) * (size_t)d.layers, s);
     std::vector<FusedLayer> fl;
     if (m->fused_ok) {
         // tag 0 is never written: zeroed exchange words never match a wait
@@ -1447,6 +1459,7 @@ extern "C" int lastro_model_set_tuning(lastro_model* m, int32_t attn_splits, int
     m->attn_tma = (flags & LASTRO_TUNE_ATTN_TMA) != 0;
     m->spec_mode = (flags & LASTRO_TUNE_SPEC_STAGE) ? 1 : (flags & LASTRO_TUNE_SPEC_L2) ? 2 : 0;
     m->attn_mma = (flags & LASTRO_TUNE_ATTN_MMA) != 0;
+    m->route_handoff = (flags & LASTRO_TUNE_DOWN_ROUTES) == 0;
     return LASTRO_OK;
 }
 

@@ -153,6 +153,11 @@ struct lastro_model {
     // (LASTRO_TUNE_SPEC_STAGE), 0 off (the default)
     float* spec_logits = nullptr;
     int spec_mode = 0;
+    // the routing hand-off from gate_up to down: a step counter (advanced by the step's first kernel) and a flag per
+    // layer; on unless LASTRO_TUNE_DOWN_ROUTES
+    unsigned int* step_ctr = nullptr;
+    unsigned int* route_flags = nullptr;
+    bool route_handoff = true;
     int *route_ids = nullptr, *d_token = nullptr, *d_pos = nullptr, *d_step = nullptr, *d_out_ids = nullptr;
     int* d_prompt = nullptr;
     unsigned int *router_counter = nullptr, *head_counter = nullptr, *attn_counters = nullptr;

@@ -168,6 +168,16 @@ LDEV void split_bf16(float v, uint16_t& hi, uint16_t& lo) {
     lo = f32_to_bf16_rne(__fsub_rn(v, __uint_as_float((uint32_t)hi << 16)));
 }
 
+// ---- flags written by another CTA of this GPU --------------------------------------------------------------------
+LDEV unsigned int ld_acquire_gpu(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+LDEV void st_release_gpu(unsigned int* p, unsigned int v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // ---- bulk (TMA) copies global -> shared, completed on an mbarrier ----------------------------------------------
 LDEV uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 

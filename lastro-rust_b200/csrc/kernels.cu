@@ -122,6 +122,7 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
 
     float4 v[NV];
     if (a.embed_mode) {
+        if (a.step_ctr && blockIdx.x == 0 && threadIdx.x == 0) *a.step_ctr += 1;  // read only by later kernels
         // model.rs:134-138: embedding row x embedding_multiplier is the residual stream of layer 0
         const int tok = __ldcg(a.token);
         const uint2* er = reinterpret_cast<const uint2*>(a.embed + (size_t)tok * a.H);  // 4 bf16 per uint2
@@ -987,6 +988,9 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
     if (fused) {
         vec_load_cg<BLOCK, NV>(a.x, a.H, v);  // in flight while the routing is reduced
         r = route_from_shares<BLOCK>(a.rs, a.E, a.k, a.H, red, sid, sval, sw, &s_r, blockIdx.x == 0, &trace_);
+        // the routing warp's published stores are ordered before the flag by the block barrier above and this
+        // thread's release (cumulative)
+        if (a.route_flag && blockIdx.x == 0 && threadIdx.x == 0) st_release_gpu(a.route_flag, __ldcg(a.step_ctr));
     } else {
         __syncthreads();  // barrier init visible to every waiting thread
     }
@@ -1344,6 +1348,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_kernel(MoeArgs a) {
 // and h[r] += resid * y (model.rs:230-232) or out[r] = y (block forward).
 // ------------------------------------------------------------------------------------------------------------------
 constexpr int kDnRows = 8;
+constexpr int kRouteWaitPolls = 1024;  // ~100 us at most; then the CTA reduces the shares itself
 
 template <int NCI, bool Q8>
 __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
@@ -1360,8 +1365,28 @@ __global__ void __launch_bounds__(256) down_kernel(DownArgs a) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r0 = blockIdx.x * R;
     const bool fused = a.rs.shares != nullptr;
-    // the routing was produced two kernels back (router kernel, or the output projection's shares): final already
-    if (fused) route_from_shares<BLOCK>(a.rs, a.E, a.k, a.H, red, sid, sval, sw, &s_r, false);
+    // the routing: gate_up's CTA 0 publishes it while this kernel's CTAs start (take it once its flag carries this
+    // step's counter), or reduce the output projection's shares here, like gate_up (two kernels back: final already)
+    __shared__ bool s_have;
+    bool have = false;
+    if (fused && a.route_flag) {
+        if (threadIdx.x == 0) {
+            const unsigned int want = __ldcg(a.step_ctr);
+            bool got = false;
+            for (int i = 0; i < kRouteWaitPolls && !got; ++i) {
+                got = ld_acquire_gpu(a.route_flag) == want;
+                if (!got) __nanosleep(64);
+            }
+            s_have = got;
+        }
+        __syncthreads();
+        have = s_have;
+        if (have && threadIdx.x < a.k) {
+            sid[threadIdx.x] = __ldcg(a.rs.ids_out + threadIdx.x);
+            sw[threadIdx.x] = __ldcg(a.rs.weights_out + threadIdx.x);
+        }
+    }
+    if (fused && !have) route_from_shares<BLOCK>(a.rs, a.E, a.k, a.H, red, sid, sval, sw, &s_r, false);
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         const uint32_t bytes = (uint32_t)(R * rbi);

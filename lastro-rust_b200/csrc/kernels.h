@@ -57,6 +57,9 @@ struct QkvArgs {
     const float* spec_ln;         // [H] MoE norm weight
     float* spec_out;              // [E]
     int spec_E;
+    // optional: the step counter the routing hand-off of gate_up to down is stamped with (GateUpArgs route_flag);
+    // the embedding launch (embed_mode, the first kernel of every step) advances it
+    unsigned int* step_ctr;
 };
 
 struct AttnArgs {
@@ -170,6 +173,10 @@ struct GateUpArgs {
     // routing a CTA whose expert was predicted computes it where the routing put it, the others re-stage the experts
     // nobody predicted (the results do not depend on the prediction)
     const float* spec;
+    // optional (with rs.shares): once CTA 0 has published the routing (rs.ids_out, rs.weights_out) it stamps this
+    // layer's flag with the step counter, so the down kernel takes the routing instead of reducing the shares again
+    unsigned int* route_flag;
+    const unsigned int* step_ctr;
 };
 
 struct DownArgs {
@@ -188,6 +195,10 @@ struct DownArgs {
     const void* pf[2];
     unsigned long long pf_bytes[2];
     unsigned long long* trace;  // in-graph timeline stamps of this launch (CtaTrace), or null
+    // optional (with rs.shares): the routing gate_up's CTA 0 published (rs.ids_out, rs.weights_out), taken once
+    // route_flag holds the step counter; a bounded wait, after which the CTA reduces the shares itself
+    const unsigned int* route_flag;
+    const unsigned int* step_ctr;
 };
 
 // The MoE block of the model step in one persistent launch (moe_kernel): routing from the output projection's shares,

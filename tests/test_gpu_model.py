@@ -506,6 +506,36 @@ def test_speculative_expert_fetch_is_bitwise_the_plain_chain(gpu_ctx, which, mod
     b.close()
 
 
+@pytest.mark.parametrize("which", ["tiny768", "c3-2layer"])
+def test_down_taking_the_published_routing_is_bitwise_its_own_reduction(gpu_ctx, which):
+    """The down kernel taking the routing gate_up's first CTA publishes (the default; a per-layer flag stamped with the
+    step counter) against every down CTA reducing the router shares itself: the same routing, bitwise the same logits
+    and routes, also across a reset (the counter keeps rising, so no flag of an earlier step is taken)."""
+    if which == "tiny768":
+        cfg, w = CFG.TINY_768, reference_tiny_weights(CFG.TINY_768)
+    else:
+        cfg, w = dict(CFG.C3_3B["model"], layers=2), None
+    models = []
+    for own in (False, True):
+        m = LB.GpuModel(gpu_ctx, cfg, 128, kv_dtype="bf16")
+        if w is None:
+            m.fill_synthetic(CFG.C3_3B["weight_seed"], CFG.WEIGHT_STD, 0.0)
+        else:
+            m.load_weights(w)
+        m.set_tuning(16, 0, down_routes=own)
+        models.append(m)
+    a, b = models
+    for rnd in range(2):
+        for t, tok in enumerate(toks_like_reference(40, cfg["vocab"])):
+            la, na, ia, _ = a.step(tok)
+            lb, nb, ib, _ = b.step(tok)
+            assert np.array_equal(la, lb) and na == nb and np.array_equal(ia, ib), f"round {rnd} position {t}"
+        a.reset()
+        b.reset()
+    a.close()
+    b.close()
+
+
 def test_output_projection_weights_in_shared_memory_is_bitwise_the_register_form(gpu_ctx):
     """oproj_smem_kernel (weights staged by one bulk copy, 256 threads) against oproj_kernel (weights in registers,
     512 threads): the same dot order, so logits and routes are bitwise equal; bf16 and Q8_0 weights."""
