@@ -987,6 +987,8 @@ __global__ void __launch_bounds__(256) gate_up_kernel(GateUpArgs a) {
     float r = 0.0f;
     if (fused) {
         vec_load_cg<BLOCK, NV>(a.x, a.H, v);  // in flight while the routing is reduced
+        // every CTA reduces the shares (CTA 0 alone reducing them and the others waiting for its published routing
+        // measured 1.4 us slower per layer: the flag's round trip outweighs the contention it saves)
         r = route_from_shares<BLOCK>(a.rs, a.E, a.k, a.H, red, sid, sval, sw, &s_r, blockIdx.x == 0, &trace_);
         // the routing warp's published stores are ordered before the flag by the block barrier above and this
         // thread's release (cumulative)
