@@ -192,8 +192,9 @@ int lastro_model_set_moe(lastro_model *model, int32_t one_launch);
  * LASTRO_TUNE_SPEC_L2 fetches the experts predicted from the layer's input early (bf16 weights: the qkv kernel
  * computes the router logits of the layer's input, the top-k of which the output projection's CTAs hint into L2 while
  * the attention runs); LASTRO_TUNE_SPEC_STAGE instead has each gate_up CTA stream the rows of the expert predicted for
- * its slot into shared memory before the routing is known (experts the prediction missed are staged after it).  Both
- * are off by default: on C3 they measure even with the plain chain.  LASTRO_TUNE_ATTN_MMA scores and sums bf16 K/V
+ * its slot into shared memory before the routing is known (experts the prediction missed are staged after it);
+ * LASTRO_TUNE_SPEC_ATTN hints the predicted experts' gate_up and down weights into L2 from the attention kernel's
+ * CTAs, a share each, as soon as the qkv kernel has taken their top-k.  All three are off by default.  LASTRO_TUNE_ATTN_MMA scores and sums bf16 K/V
  * on tensor cores (mma.sync with q and the probabilities split into bf16 hi + lo, a relative residue below 2^-16)
  * instead of f32 CUDA-core dots.  LASTRO_TUNE_DOWN_ROUTES has every down CTA reduce the router shares itself instead
  * of taking the routing gate_up's first CTA publishes (a flag per layer stamped with a step counter, a bounded wait
@@ -207,6 +208,7 @@ int lastro_model_set_moe(lastro_model *model, int32_t one_launch);
 #define LASTRO_TUNE_SPEC_STAGE 16
 #define LASTRO_TUNE_ATTN_MMA 32
 #define LASTRO_TUNE_DOWN_ROUTES 64
+#define LASTRO_TUNE_SPEC_ATTN 128
 int lastro_model_set_tuning(lastro_model *model, int32_t attn_splits, int32_t attn_merge, int32_t flags);
 /* 1 when the MoE blocks run as one launch per layer */
 int lastro_model_moe(const lastro_model *model);

@@ -454,6 +454,11 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
             qa.spec_ln = L.ln_moe;
             qa.spec_out = m->spec_logits;
             qa.spec_E = d.experts;
+            if (m->spec_mode == 3) {
+                qa.spec_ids = m->spec_ids;
+                qa.spec_ticket = m->spec_ticket;
+                qa.spec_k = d.k;
+            }
         }
         if ((e = launch_qkv_rope(qa, s, pdl && l > 0)) != cudaSuccess) return e;
         if ((e = mark(pe, s, KK_QKV)) != cudaSuccess) return e;
@@ -505,6 +510,15 @@ cudaError_t enqueue_step(lastro_model* m, cudaStream_t s, StepEvents* pe = nullp
         } else {
             aa.tma = m->attn_tma && !aa.cluster ? 1 : 0;
             aa.mma = m->attn_mma && !aa.kv_f32 && !aa.cluster && m->G <= 8 ? 1 : 0;
+            if (spec && m->spec_mode == 3 && !aa.tma && !aa.mma && !aa.kv_f32 && !aa.cluster) {
+                aa.spec_ids = m->spec_ids;
+                aa.spec_k = d.k;
+                aa.spec_E = d.experts;
+                aa.spec_gu = L.gate_up;
+                aa.spec_dn = L.down;
+                aa.spec_gu_bytes = (unsigned long long)2 * d.inter * wrow_bytes(d.hidden, m->q8);
+                aa.spec_dn_bytes = (unsigned long long)d.hidden * wrow_bytes(d.inter, m->q8);
+            }
             if ((e = launch_attention(aa, s, pdl, aa.tma ? &m->kvboxmaps[2 * l] : nullptr,
                                       aa.tma ? &m->kvboxmaps[2 * l + 1] : nullptr)) != cudaSuccess)
                 return e;
@@ -796,7 +810,8 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
           A.alloc(&m->router_counter, 1) || A.alloc(&m->head_counter, 1) || A.alloc(&m->attn_counters, d.kv_heads) ||
           A.alloc(&m->head_partial, m->head_grid) || A.alloc(&m->d_err, 1) ||
           A.alloc(&m->op_partial, (size_t)oproj_grid(d.hidden) * (E + 1)) || A.alloc(&m->moe_barrier, 1) ||
-          A.alloc(&m->step_ctr, 1) || A.alloc(&m->route_flags, (size_t)d.layers);
+          A.alloc(&m->step_ctr, 1) || A.alloc(&m->route_flags, (size_t)d.layers) ||
+          A.alloc(&m->spec_ids, kMaxTopK) || A.alloc(&m->spec_ticket, 1);
     m->moe_ok = !bad && moe_plan(d.hidden, d.inter, d.k, m->q8, &m->moe);
     // the fused step: one CTA per SM, when the per-CTA shares of every phase fit in shared memory
     int n_sm = 0, coop = 0;
@@ -841,6 +856,8 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
     if (!e) e = cudaMemsetAsync(m->attn_counters, 0, sizeof(unsigned) * d.kv_heads, s);
     if (!e) e = cudaMemsetAsync(m->moe_barrier, 0, sizeof(unsigned long long), s);
     if (!e) e = cudaMemsetAsync(m->step_ctr, 0, sizeof(unsigned int), s);
+    if (!e) e = cudaMemsetAsync(m->spec_ticket, 0, sizeof(unsigned int), s);
+    if (!e) e = cudaMemsetAsync(m->spec_ids, 0, sizeof(int) * kMaxTopK, s);
     if (!e) e = cudaMemsetAsync(m->route_flags, 0, sizeof(unsigned int) * (size_t)d.layers, s);
     std::vector<FusedLayer> fl;
     if (m->fused_ok) {
@@ -1457,7 +1474,8 @@ extern "C" int lastro_model_set_tuning(lastro_model* m, int32_t attn_splits, int
     if ((flags & LASTRO_TUNE_ATTN_MMA) && m->d.kv_dtype == LASTRO_DTYPE_F32)
         return set_err(m->ctx, LASTRO_E_UNSUPPORTED, "tensor-core attention needs bf16 KV");
     m->attn_tma = (flags & LASTRO_TUNE_ATTN_TMA) != 0;
-    m->spec_mode = (flags & LASTRO_TUNE_SPEC_STAGE) ? 1 : (flags & LASTRO_TUNE_SPEC_L2) ? 2 : 0;
+    m->spec_mode = (flags & LASTRO_TUNE_SPEC_STAGE) ? 1 : (flags & LASTRO_TUNE_SPEC_L2) ? 2
+                   : (flags & LASTRO_TUNE_SPEC_ATTN) ? 3 : 0;
     m->attn_mma = (flags & LASTRO_TUNE_ATTN_MMA) != 0;
     m->route_handoff = (flags & LASTRO_TUNE_DOWN_ROUTES) == 0;
     return LASTRO_OK;

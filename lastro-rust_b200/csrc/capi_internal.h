@@ -152,7 +152,9 @@ struct lastro_model {
     // while the attention runs (LASTRO_TUNE_SPEC_L2), 1 staged into shared memory by the gate_up CTAs
     // (LASTRO_TUNE_SPEC_STAGE), 0 off (the default)
     float* spec_logits = nullptr;
-    int spec_mode = 0;
+    int spec_mode = 0;  // 3: the predicted top-k hinted into L2 by the attention kernel's CTAs (LASTRO_TUNE_SPEC_ATTN)
+    int* spec_ids = nullptr;
+    unsigned int* spec_ticket = nullptr;
     // the routing hand-off from gate_up to down: a step counter (advanced by the step's first kernel) and a flag per
     // layer; on unless LASTRO_TUNE_DOWN_ROUTES
     unsigned int* step_ctr = nullptr;

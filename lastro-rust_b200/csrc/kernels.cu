@@ -153,6 +153,18 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
         }
         p = block_sum(p, red);
         if (threadIdx.x == 0) a.spec_out[blockIdx.x] = p;
+        if (a.spec_ids) {
+            // the last of the spec_E CTAs takes the predicted top-k (block.rs:81-89's order)
+            __shared__ bool s_last;
+            __shared__ int s_id[kMaxTopK];
+            __shared__ float s_val[kMaxTopK], s_w[kMaxTopK];
+            if (last_block_arrives(a.spec_ticket, (unsigned int)a.spec_E, &s_last) && warp == 0) {
+                const float v0 = lane < a.spec_E ? __ldcg(a.spec_out + lane) : 0.0f;
+                const float v1 = lane + 32 < a.spec_E ? __ldcg(a.spec_out + lane + 32) : 0.0f;
+                route_topk_warp(v0, v1, a.spec_E, a.spec_k, s_id, s_val, s_w);
+                if (lane < a.spec_k) a.spec_ids[lane] = s_id[lane];
+            }
+        }
     }
     trace_.mark(0);
     if (!active) return;
@@ -198,6 +210,26 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvArgs a) {
 // (lastro_model_set_tuning).  Positions past `len` are never read.
 // ------------------------------------------------------------------------------------------------------------------
 constexpr int kAttnWarps = 8;
+
+// this CTA's share (cta of ctas) of the k predicted experts' gate_up and down weights, k x (gu + dn) bytes in expert
+// order, hinted into L2; one thread
+LDEV void spec_prefetch_share(const int* ids, int k, int E, const void* gu_w, unsigned long long gu_bytes,
+                              const void* dn_w, unsigned long long dn_bytes, int cta, int ctas) {
+    const unsigned long long per = gu_bytes + dn_bytes, all = per * k;
+    const unsigned long long share = ((all + ctas - 1) / ctas + 15) & ~15ull;
+    unsigned long long o = share * cta;
+    const unsigned long long o1 = min(all, o + share);
+    while (o < o1) {
+        const int sl = (int)(o / per);
+        const unsigned long long in = o - (unsigned long long)sl * per;
+        const int e = min(max(ids[sl], 0), E - 1);
+        const bool gu = in < gu_bytes;
+        const unsigned long long part = gu ? gu_bytes : dn_bytes, at = gu ? in : in - gu_bytes;
+        const unsigned long long n = min(o1 - o, part - at);
+        bulk_prefetch_l2(static_cast<const unsigned char*>(gu ? gu_w : dn_w) + (size_t)e * part + at, (uint32_t)n);
+        o += n;
+    }
+}
 
 // One warp's share of a split on tensor cores (bf16 K/V): the warp takes the split's rows in groups of 16 (positions
 // p0 + g0 .. g0 + 15 at staged row g0 + roff; K/V rows of 128 bytes, 128-byte swizzled when `swizzled`).  Per group
@@ -388,6 +420,16 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(const __grid
     pdl_launch();
     trace_.released();
 
+    if constexpr ((MODE & 4) != 0) {
+        // this CTA's share of the predicted experts' weights into L2 (the routing of this layer is ~10 us away)
+        if (threadIdx.x == 32) {
+            int ids[kMaxTopK];
+#pragma unroll
+            for (int j = 0; j < kMaxTopK; ++j) ids[j] = j < a.spec_k ? __ldcg(a.spec_ids + j) : 0;
+            spec_prefetch_share(ids, a.spec_k, a.spec_E, a.spec_gu, a.spec_gu_bytes, a.spec_dn, a.spec_dn_bytes,
+                                blockIdx.x + gridDim.x * blockIdx.y, gridDim.x * gridDim.y);
+        }
+    }
     for (int i = threadIdx.x; i < G * D / 4; i += blockDim.x)
         reinterpret_cast<float4*>(&sq[0][0])[i] = __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)z * HD + (size_t)kvh * G * D) + i);
     // with boxes, the box that holds the new row's slot carries its stale copy: the row is written after they land
@@ -722,21 +764,8 @@ LDEV void spec_prefetch_l2(const OprojArgs& a) {
     }
     __syncthreads();
     if (threadIdx.x != 0) return;
-    const unsigned long long per = a.spec_gu_bytes + a.spec_dn_bytes, all = per * a.spec_k;
-    const unsigned long long share = ((all + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
-    unsigned long long o = share * blockIdx.x;
-    const unsigned long long o1 = min(all, o + share);
-    while (o < o1) {
-        const int sl = (int)(o / per);
-        const unsigned long long in = o - (unsigned long long)sl * per;
-        const int e = min(max(pid[sl], 0), a.spec_E - 1);
-        const bool gu = in < a.spec_gu_bytes;
-        const unsigned long long part = gu ? a.spec_gu_bytes : a.spec_dn_bytes, at = gu ? in : in - a.spec_gu_bytes;
-        const unsigned long long n = min(o1 - o, part - at);
-        const unsigned char* base = static_cast<const unsigned char*>(gu ? a.spec_gu : a.spec_dn) + (size_t)e * part;
-        bulk_prefetch_l2(base + at, (uint32_t)n);
-        o += n;
-    }
+    spec_prefetch_share(pid, a.spec_k, a.spec_E, a.spec_gu, a.spec_gu_bytes, a.spec_dn, a.spec_dn_bytes, blockIdx.x,
+                        gridDim.x);
 }
 
 template <int NCH, bool Q8, bool SPEC = false>
@@ -1707,7 +1736,8 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl, const 
     const size_t smem = attn_smem_staging(a.max_len, a.kv_f32, a.splits, a.tma != 0);
     if (smem > kMaxSmemBytes) return cudaErrorInvalidValue;
     const dim3 grid(a.splits, a.kv_heads, a.seq ? a.tokens : 1), block(32 * kAttnWarps);
-    const int mode = (a.tma ? 1 : 0) | (a.mma ? 2 : 0);
+    if (a.spec_ids && (a.tma || a.mma || a.kv_f32 || a.seq)) return cudaErrorInvalidValue;  // bf16, batch 1, bulk form
+    const int mode = a.spec_ids ? 4 : (a.tma ? 1 : 0) | (a.mma ? 2 : 0);
 #define LASTRO_ATTN_G(GV)                                                                                  \
     case GV: {                                                                                             \
         if (a.cluster) {                                                                                   \
@@ -1721,6 +1751,7 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl, const 
                  : mode == 1 ? attention_kernel<false, GV, false, 1>                                       \
                  : mode == 2 ? attention_kernel<false, GV, false, 2>                                       \
                  : mode == 3 ? attention_kernel<false, GV, false, 3>                                       \
+                 : mode == 4 ? attention_kernel<false, GV, false, 4>                                       \
                              : attention_kernel<false, GV, false, 0>;                                      \
         cudaError_t e = allow_smem(k, smem);                                                               \
         return e != cudaSuccess ? e : launch_ex(k, grid, block, smem, s, pdl, km, vm, a);                  \

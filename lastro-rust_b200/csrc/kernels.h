@@ -60,6 +60,11 @@ struct QkvArgs {
     // optional: the step counter the routing hand-off of gate_up to down is stamped with (GateUpArgs route_flag);
     // the embedding launch (embed_mode, the first kernel of every step) advances it
     unsigned int* step_ctr;
+    // optional (with spec_out): the last of the spec_E CTAs (ticket) also takes the top spec_k of the predicted
+    // logits into spec_ids, for the attention kernel's L2 hints (AttnArgs spec_ids)
+    int* spec_ids;
+    unsigned int* spec_ticket;  // zero between launches
+    int spec_k;
 };
 
 struct AttnArgs {
@@ -83,6 +88,13 @@ struct AttnArgs {
                              // shared memory (splits <= 8; batch-1 only)
     int mma;                 // 1: bf16 K/V scored and summed on tensor cores (mma.sync, q and p split into bf16 hi + lo),
                              // else on CUDA cores in f32
+    // optional: the experts predicted for this layer (QkvArgs spec_ids, final when this kernel is released): every CTA
+    // hints its share of their gate_up and down weights into L2 while the attention and the output projection run
+    const int* spec_ids;
+    int spec_k, spec_E;
+    const void* spec_gu;  // [E, 2I, H] rows: spec_gu_bytes per expert
+    const void* spec_dn;  // [E, H, I] rows: spec_dn_bytes per expert
+    unsigned long long spec_gu_bytes, spec_dn_bytes;
     int tma;                 // 1: bf16 K/V staged by 8-row TMA boxes with the 128-byte swizzle (launch_attention's maps:
                              // make_kv_box_map over the layer's pools; page_size a multiple of 8), else bulk copies
     float scale;

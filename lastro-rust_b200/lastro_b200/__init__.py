@@ -598,12 +598,13 @@ class GpuModel:
         weights in shared memory (256-thread CTAs) or registers; gate_up hinting the down rows into L2; bf16 K/V
         staged by swizzled 8-row TMA boxes (attn_tma) or by bulk copies per page run; the experts predicted from
         the layer's input fetched before the routing is known (speculation: "l2" hinted into L2 by the output
-        projection, "stage" streamed into the gate_up CTAs' shared memory, False off: the default); bf16 K/V
+        projection, "stage" streamed into the gate_up CTAs' shared memory, "attn" hinted into L2 by the attention
+        kernel's CTAs, False off: the default); bf16 K/V
         attention on tensor cores (attn_mma); every down CTA reducing the router shares itself (down_routes) instead
         of taking the routing gate_up publishes."""
-        assert speculation in ("l2", "stage", False)
+        assert speculation in ("l2", "stage", "attn", False)
         flags = (1 if oproj_smem else 0) | (2 if prefetch_down else 0) | (4 if attn_tma else 0) | \
-            {"l2": 8, "stage": 16, False: 0}[speculation] | (32 if attn_mma else 0) | (64 if down_routes else 0)
+            {"l2": 8, "stage": 16, "attn": 128, False: 0}[speculation] | (32 if attn_mma else 0) | (64 if down_routes else 0)
         self.ctx.check(lib().lastro_model_set_tuning(self.h, attn_splits, int(attn_merge), flags))
 
     @property

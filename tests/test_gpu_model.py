@@ -470,7 +470,7 @@ def gate_up_misses(m, layers):
     return sum(int((m.trace_raw(5 * l + 3)[:, 3 + 6] > 0).sum()) for l in range(layers))
 
 
-@pytest.mark.parametrize("mode", ["l2", "stage"])
+@pytest.mark.parametrize("mode", ["l2", "stage", "attn"])
 @pytest.mark.parametrize("which", ["tiny", "tiny768", "c3-2layer"])
 def test_speculative_expert_fetch_is_bitwise_the_plain_chain(gpu_ctx, which, mode):
     """The experts predicted from the layer's input fetched before the routing is known -- hinted into L2 by the
@@ -499,7 +499,7 @@ def test_speculative_expert_fetch_is_bitwise_the_plain_chain(gpu_ctx, which, mod
         assert np.array_equal(la, lb) and na == nb and np.array_equal(ia, ib), f"position {t}"
     misses = gate_up_misses(a, cfg["layers"])
     assert gate_up_misses(b, cfg["layers"]) == 0
-    if mode == "l2":
+    if mode != "stage":
         assert misses == 0
     print(f"{which} {mode}: gate_up CTAs re-staged after a misprediction in one traced step: {misses}")
     a.close()
