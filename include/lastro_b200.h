@@ -291,6 +291,21 @@ int lastro_batch_position(const lastro_batch *batch, int32_t seq, int32_t *pos);
  * return), combine (with the next norm), lm_head, argmax (n_kinds >= 12) */
 int lastro_batch_profile(lastro_batch *batch, int32_t n, const int32_t *seq_ids, const int32_t *tokens, int32_t steps,
                          float *kernel_ms, int32_t n_kinds);
+/* in-graph timeline of `steps` graph-replayed steps (tokens as for lastro_batch_decode; the positions advance):
+ * every CTA of the step's launches stamps the global timer (start, release from griddepcontrol.wait, exit); per kernel
+ * kind (lastro_batch_profile's order) the ms per step of its share of the step's critical path (exposed; they sum to
+ * the step), first CTA start to last CTA exit summed over the launches (span), and the hand-off from the previous
+ * launch's last exit to its first release (wait); step_ms first start to last exit.  All ranks of a group call it
+ * together.  Diagnostics only; no reference counterpart. */
+int lastro_batch_trace(lastro_batch *batch, int32_t n, const int32_t *seq_ids, const int32_t *tokens, int32_t steps,
+                       float *exposed_ms, float *span_ms, float *wait_ms, int32_t n_kinds, float *step_ms);
+/* the stamps of launch `launch` (0 the layer-0 norm, then 8 per layer: qkv, rope_kv, attention, oproj, router, gate_up,
+ * down, combine; then lm_head, argmax) of the last step lastro_batch_trace timed, laid out as for
+ * lastro_model_trace_raw.  Milestones: the router 5 (RMSNorm done), 0 (router logits), 3 (top-k), 4 (MoE rows sent),
+ * 1 (expert ids sent) and, in its last CTA, 2 (dispatch flag published; the exit then ends the wait for the senders
+ * and the grouping); the combine 0 (every owner's return flag seen); the tcgen05 GEMMs 0 (set up), 1, 4 and 5 (the
+ * first, second and middle stage landed), 2 (last MMAs issued), 3 (accumulator complete) */
+int lastro_batch_trace_raw(const lastro_batch *batch, int32_t launch, unsigned long long *out, int32_t words);
 /* use_graphs: replay each step as a CUDA graph (default 1); use_tcgen05: the GEMMs on the 5th-generation tensor cores
  * with tensor-memory accumulators, warp-specialised with TMA weight tiles (2, default), the same with all threads
  * loading the stages (1), or on mma.sync with register accumulators (0); attn_tc: attention on tensor cores with TMA

@@ -305,12 +305,14 @@ __global__ void __launch_bounds__(128) bgemm_kernel(BGemmArgs a) {
 // attention norm: h = embedding row x multiplier (layer 0) or the residual stream; xn = ln * (h * r) split hi + lo
 // ------------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) battn_norm_kernel(BNormArgs a) {
+    const CtaTrace trace_(a.trace);
     constexpr int BLOCK = 256, NV = 2;  // H <= 2048
     __shared__ float red[BLOCK / 32];
     const int t = blockIdx.x;
     float* h = a.h + (size_t)t * a.H;
     pdl_wait();
     pdl_launch();
+    trace_.released();
     float4 v[NV];
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
@@ -358,12 +360,14 @@ __global__ void __launch_bounds__(256) battn_norm_kernel(BNormArgs a) {
 // x1*c - x2*s, x2*c + x1*s (model.rs:153-155); q to its buffer, K (roped) and V to the token's sequence page.
 // ------------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) brope_kv_kernel(BRopeArgs a) {
+    const CtaTrace trace_(a.trace);
     constexpr int kMaxKs = 16;
     const int t = blockIdx.x;
     const int R = a.qd + 2 * a.kvd, half = a.d >> 1;
     const int pi = blockIdx.y * blockDim.x + threadIdx.x;  // RoPE pair of this thread
     pdl_wait();
     pdl_launch();
+    trace_.released();
     if (pi >= R / 2) return;
     const int sq = __ldg(a.seq + t);
     const int pos = __ldcg(a.pos + sq) + (a.off ? __ldg(a.off + t) : 0);
@@ -698,17 +702,20 @@ LDEV void group_pairs(const BExchangeArgs& a) {
 // for the experts); logits_e = W_r[e] . xn (+ bias_e), one warp per expert; top-k in block.rs:81-89's order, softmax.
 // ------------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) brouter_kernel(BRouterArgs a) {
+    const CtaTrace trace_(a.trace);
     constexpr int BLOCK = 256, NV = 2;
     extern __shared__ __align__(16) float xs[];  // [H]
     __shared__ float red[BLOCK / 32];
     __shared__ float lg[kMaxExperts];
     __shared__ int sid[kMaxTopK];
-    __shared__ float sval[kMaxTopK], sw[kMaxTopK];
+    __shared__ float sval[kMaxTopK], sw[kMaxTopK], ex[kMaxTopK];
+    __shared__ unsigned long long keys[kMaxExperts];
     __shared__ bool is_last;
     const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float* h = a.h + (size_t)t * a.H;
     pdl_wait();
     pdl_launch();
+    trace_.released();
     float4 v[NV];
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
@@ -751,6 +758,7 @@ __global__ void __launch_bounds__(256) brouter_kernel(BRouterArgs a) {
         reinterpret_cast<float4*>(xs)[i] = ln_times(__ldg(reinterpret_cast<const float4*>(a.ln) + i), v[k], r);
     }
     __syncthreads();
+    trace_.mark_after(5, xs[threadIdx.x]);
     for (int e = warp; e < a.E; e += BLOCK / 32) {
         // the row's chunks (H <= 2048: at most 8 per lane) all loaded before the first product
         const uint16_t* row = a.wr + (size_t)e * a.H;
@@ -771,17 +779,16 @@ __global__ void __launch_bounds__(256) brouter_kernel(BRouterArgs a) {
         if (lane == 0) lg[e] = a.bias ? __fadd_rn(acc, __ldg(a.bias + e)) : acc;
     }
     __syncthreads();
-    if (warp == 0) {
-        const float v0 = lane < a.E ? lg[lane] : 0.0f;
-        const float v1 = lane + 32 < a.E ? lg[lane + 32] : 0.0f;
-        route_topk_warp(v0, v1, a.E, a.k, sid, sval, sw);
-        if (lane < a.k) {
-            a.ids[(size_t)t * a.k + lane] = sid[lane];
-            a.weights[(size_t)t * a.k + lane] = sw[lane];
-            if (a.route_hist) a.route_hist[((size_t)t * a.layers + a.layer) * a.k + lane] = sid[lane];
-        }
+    trace_.mark_after(0, lg[threadIdx.x & 31]);
+    // the top-k over the whole block (one warp exchanging the keys by shuffles while the other seven waited at the
+    // barrier measured 17.6 us per layer with the trace stamps on; this form 1.0 us, and bitwise the same routing)
+    route_topk_block(lg, a.E, a.k, keys, ex, sid, sval, sw);
+    if (threadIdx.x < a.k) {
+        a.ids[(size_t)t * a.k + threadIdx.x] = sid[threadIdx.x];
+        a.weights[(size_t)t * a.k + threadIdx.x] = sw[threadIdx.x];
+        if (a.route_hist) a.route_hist[((size_t)t * a.layers + a.layer) * a.k + threadIdx.x] = sid[threadIdx.x];
     }
-    __syncthreads();
+    trace_.mark_after(3, sw[0]);
     // dispatch: the token's MoE input row (hi then lo) once to every rank that owns one of its experts, its k expert
     // ids to every rank; the last CTA publishes this rank's dispatch flag on every rank
     const BExchangeArgs& x = a.x;
@@ -803,16 +810,19 @@ __global__ void __launch_bounds__(256) brouter_kernel(BRouterArgs a) {
             reinterpret_cast<ushort4*>(dst + (size_t)a.H * 2)[i] = lo;
         }
     }
+    trace_.mark(4);
     for (int i = threadIdx.x; i < x.world * a.k; i += BLOCK) {
         const int q = i / a.k, j = i - q * a.k;
         reinterpret_cast<int*>(x.peers[q] + L.rx_ids)[(size_t)x.rank * L.cap + (size_t)t * a.k + j] = sid[j];
     }
     if (t == 0 && threadIdx.x < x.world) reinterpret_cast<int*>(x.peers[threadIdx.x] + L.rx_n)[x.rank] = a.n;
+    trace_.mark(1);
     if (!last_block_arrives_sys(x.counter, gridDim.x, &is_last, x.world > 1)) return;
     if (threadIdx.x < x.world) {
         const unsigned int epoch = __ldcg(x.epoch_base) + x.layer + 1;
         st_release_x(flag_ptr(x.peers[threadIdx.x], L, 0, x.rank), epoch, x.world > 1);
     }
+    trace_.mark(2);
     // the same CTA then waits for every rank's dispatch and groups the pairs this rank's experts received
     __syncthreads();
     group_pairs(x);
@@ -823,6 +833,7 @@ __global__ void __launch_bounds__(256) brouter_kernel(BRouterArgs a) {
 // order (cpu.rs:141-148).
 // ------------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) ep_combine_kernel(BExchangeArgs a) {
+    const CtaTrace trace_(a.trace);
     constexpr int BLOCK = 256, NV = 8;  // H <= 2048
     __shared__ int ok_all;
     __shared__ float red[BLOCK / 32];
@@ -831,6 +842,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(BExchangeArgs a) {
     const int t = blockIdx.x;
     pdl_wait();
     pdl_launch();
+    trace_.released();
     const unsigned int epoch = __ldcg(a.epoch_base) + a.layer + 1;
     if (threadIdx.x == 0) ok_all = 1;
     __syncthreads();
@@ -838,6 +850,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(BExchangeArgs a) {
         !wait_flag(flag_ptr(me, L, 1, threadIdx.x), epoch, a.err, 30 + threadIdx.x, a.world > 1, a.wait_ns))
         atomicExch(&ok_all, 0);
     __syncthreads();
+    trace_.mark(0);
     if (!ok_all) return;
     float w[kMaxTopK];
 #pragma unroll
@@ -885,11 +898,13 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(BExchangeArgs a) {
 // argmax per token (the last maximum, bin/m1b-gulosa.rs:22-24), position advanced, next token fed back
 // ------------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) bargmax_kernel(BHeadArgs a) {
+    const CtaTrace trace_(a.trace);
     __shared__ unsigned long long best[32];
     const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float* lg = a.logits + (size_t)t * a.V;
     pdl_wait();
     pdl_launch();
+    trace_.released();
     // four independent running maxima per thread (keys order by value, then by index: the last maximum wins)
     unsigned long long b0 = 0ull, b1 = 0ull, b2 = 0ull, b3 = 0ull;
     const int stride = 4 * blockDim.x;
@@ -1214,6 +1229,7 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
     // TOK tokens per tile: 64 with 3 stages of 32 KB (2 CTAs per SM), or 32 with 2 stages of 24 KB (4 CTAs per SM).
     // Measured on the C5 step (1 B200): 64/3 for every GEMM 5.05 ms, 32/4 for the expert groups 5.15 ms, 32/2 5.21 ms;
     // the launches use 64.
+    const CtaTrace trace_(a.trace);
     static_assert(TOK == 32 || TOK == 64, "token tile");
     constexpr int S = TOK == 64 ? 3 : 2;
     constexpr size_t STAGE = (size_t)kBRows * 128 + 2 * (size_t)TOK * 128;
@@ -1247,6 +1263,7 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
     }
     pdl_wait();
     pdl_launch();
+    trace_.released();
     int p0 = 0, ntot = a.n;
     if (a.g_cnt) {
         p0 = __ldcg(a.g_off + g);
@@ -1255,6 +1272,7 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
     if (nk <= 0) ntot = 0;
     if (EPI != BEPI_RETURN && ntot <= 0) return;  // (a RETURN CTA still votes below)
     if (ntot > 0 && pre == 0) bgemm_ws_setup(&tmem_base, full, empty, &done, S, &wmap, tid, warp);
+    trace_.mark(0);
     const uint32_t tmem = tmem_base;
     bool ok = true;
     int it = 0;  // global stage counter over the CTA's tiles (stage it % S, round it / S)
@@ -1290,6 +1308,9 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
                     if (!mbar_wait(&full[s], r & 1, a.x.err, 8)) {
                         go = false;
                     } else {
+                        if (tile == 0 && kt == 0) trace_.mark(1, 32);
+                        if (tile == 0 && kt == 1) trace_.mark(4, 32);
+                        if (tile == 0 && kt == nk / 2) trace_.mark(5, 32);
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the cp.async rows, for the MMA
                         tc_fence_after();
                         const uint32_t sW = smem_addr(smem + (size_t)s * STAGE);
@@ -1306,6 +1327,7 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
                 go = __shfl_sync(0xffffffffu, go, 0);
             }
             if (!go) ok = false;
+            if (tile == 0) trace_.mark(2, 32);
             if (lane == 0) tc_commit(&done);  // all MMAs of the tile
             __syncwarp();
         } else {
@@ -1340,6 +1362,7 @@ __global__ void __launch_bounds__(128) bgemm_ws_kernel(const __grid_constant__ C
         // epilogue (all warps): after the tile's final commit
         ok = mbar_wait(&done, tile & 1, a.x.err, 10) && ok;
         tc_fence_after();
+        if (tile == 0) trace_.mark(3);
         if (!ok) break;
         const int row = warp * 32 + lane;
         const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
@@ -1455,6 +1478,7 @@ constexpr int kPageBytes = 64 * 128;  // one KV head's 64 positions, bf16
 template <int G>
 __global__ void __launch_bounds__(128) battn_tc_kernel(const __grid_constant__ CUtensorMap kmap,
                                                        const __grid_constant__ CUtensorMap vmap, BAttnArgs a) {
+    const CtaTrace trace_(a.trace);
     constexpr int D = kHeadDim, NW = 4, P = kAttnStages;
     static_assert(G <= 8, "heads of a group padded to the MMA's 16 rows");
     extern __shared__ unsigned char smem_dyn[];
@@ -1497,6 +1521,7 @@ __global__ void __launch_bounds__(128) battn_tc_kernel(const __grid_constant__ C
     }
     pdl_wait();
     pdl_launch();
+    trace_.released();
     if (threadIdx.x == 0)
         for (int i = 0; i < pre; ++i)
             if (pbeg + i >= fresh) issue(i);

@@ -82,6 +82,7 @@ struct BExchangeArgs {
     float eps;
     uint16_t* xn_hi;
     uint16_t* xn_lo;
+    unsigned long long* trace;    // optional: CtaTrace stamps of the combine launch (lastro_batch_trace)
 };
 
 enum BEpi { BEPI_STORE = 0, BEPI_SWIGLU = 1, BEPI_RETURN = 2 };
@@ -115,6 +116,7 @@ struct BGemmArgs {
     // warp-specialised: weight tiles by TMA (the launch's tensor map), activation tiles by two cp.async warps, one
     // thread issuing the MMAs
     int tc;
+    unsigned long long* trace;    // optional: CtaTrace stamps of this launch (lastro_batch_trace)
 };
 
 struct BNormArgs {
@@ -127,6 +129,7 @@ struct BNormArgs {
     uint16_t* x_hi;            // [n, H]
     uint16_t* x_lo;
     int H;
+    unsigned long long* trace;    // optional: CtaTrace stamps of this launch (lastro_batch_trace)
 };
 
 struct BRopeArgs {
@@ -142,6 +145,7 @@ struct BRopeArgs {
     const int* page_table;     // [sequences, pt_stride]
     int pt_stride, page_size, kv_f32;
     int n, qd, kvd, d, kv_heads;
+    unsigned long long* trace;    // optional: CtaTrace stamps of this launch (lastro_batch_trace)
 };
 
 struct BRouterArgs {
@@ -159,6 +163,7 @@ struct BRouterArgs {
     int* route_hist;           // optional [n][layers][k] history of the step
     int layer, layers;
     int n, H, E, k;
+    unsigned long long* trace;    // optional: CtaTrace stamps of this launch (lastro_batch_trace)
 };
 
 struct BHeadArgs {
@@ -171,6 +176,7 @@ struct BHeadArgs {
     int* tokens;                  // optional: next token fed back as the next step's input
     unsigned int* epoch_base;     // advanced by `layers` (CTA 0)
     int layers;
+    unsigned long long* trace;    // optional: CtaTrace stamps of this launch (lastro_batch_trace)
 };
 
 // Batched decode attention: CTA per (split, KV head, token) over the token's sequence; splits of at most kBAttnRows
@@ -197,6 +203,7 @@ struct BAttnArgs {
     int* err;
     int n, kv_heads, G, S, cap;  // cap: positions one split stages (>= ceil(max_len / S))
     float scale;
+    unsigned long long* trace;    // optional: CtaTrace stamps of this launch (lastro_batch_trace)
 };
 
 cudaError_t launch_battention(const BAttnArgs& a, cudaStream_t s);

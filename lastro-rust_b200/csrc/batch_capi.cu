@@ -64,6 +64,9 @@ struct lastro_batch {
     // profiling: an event recorded after every launch of a direct (uncaptured) step, with the launch's kind
     std::vector<cudaEvent_t>* prof_ev = nullptr;
     std::vector<int>* prof_kind = nullptr;
+    // in-graph timeline (lastro_batch_trace): every CTA's stamps of the last traced step
+    unsigned long long* d_trace = nullptr;
+    std::vector<unsigned long long> trace_host;
 };
 
 namespace {
@@ -126,11 +129,19 @@ int pick_ks(int rows, int K, int n_sm) {
     return best;
 }
 
-cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
+// launches of one step: the layer-0 norm, 8 per layer, the lm_head and the argmax
+int bstep_launches(const lastro_batch* b) { return 8 * b->m->d.layers + 3; }
+
+// `trace` (optional): kTraceMaxCtas * kTraceWords stamps per launch, in launch order
+cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s, unsigned long long* trace = nullptr) {
     lastro_model* m = b->m;
     const lastro_model_desc& d = m->d;
     const int H = d.hidden, I = d.inter, E = d.experts, k = d.k, qd = m->qd, kvd = m->kvd, R = b->R;
     cudaError_t e = cudaSuccess;
+    size_t launch = 0;
+    auto tr = [&]() -> unsigned long long* {
+        return trace ? trace + (launch++) * (size_t)kTraceMaxCtas * kTraceWords : nullptr;
+    };
     BExchangeArgs xa{};
     xa.peers = b->d_peers;
     xa.lay = b->lay;
@@ -168,6 +179,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
     na.x_hi = b->xa_hi;
     na.x_lo = b->xa_lo;
     na.H = H;
+    na.trace = tr();
     if ((e = mark(b, s, BK_NORM, launch_battn_norm(na, n, s)))) return e;
     for (int l = 0; l < d.layers && e == cudaSuccess; ++l) {
         const LayerDev& L = m->L[l];
@@ -186,6 +198,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         ga.z_stride = (long long)n * R;
         ga.div = 1.0f;
         ga.tc = b->gemm_mode;
+        ga.trace = tr();
         if ((e = mark(b, s, BK_QKV, launch_bgemm(ga, BEPI_STORE, 1, s, wmap(b, l, 0))))) break;
 
         BRopeArgs ra{};
@@ -207,6 +220,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         ra.kvd = kvd;
         ra.d = d.head_dim;
         ra.kv_heads = d.kv_heads;
+        ra.trace = tr();
         if ((e = mark(b, s, BK_ROPE, launch_brope_kv(ra, s)))) break;
 
         BAttnArgs aa{};
@@ -233,6 +247,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         aa.S = b->attn_S;
         aa.cap = b->attn_cap;
         aa.scale = d.attention_multiplier;
+        aa.trace = tr();
         if (b->attn_tc) {
             // context splits for few tokens: at most about 4 CTAs per SM in all (one split while the tokens alone
             // fill that), at most 16 splits, at least 2 pages each
@@ -258,6 +273,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         oa.z_stride = (long long)n * H;
         oa.div = 1.0f;
         oa.tc = b->gemm_mode;
+        oa.trace = tr();
         if ((e = mark(b, s, BK_OPROJ, launch_bgemm(oa, BEPI_STORE, 1, s, wmap(b, l, 1))))) break;
 
         BRouterArgs rta{};
@@ -280,6 +296,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         rta.H = H;
         rta.E = E;
         rta.k = k;
+        rta.trace = tr();
         if ((e = mark(b, s, BK_ROUTER, launch_brouter(rta, s)))) break;
 
         BGemmArgs gu{};
@@ -300,6 +317,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         gu.I = I;
         gu.div = 1.0f;
         gu.tc = b->gemm_mode;
+        gu.trace = tr();
         if ((e = mark(b, s, BK_GATE_UP, launch_bgemm(gu, BEPI_SWIGLU, b->epr, s, wmap(b, l, 2))))) break;
 
         BGemmArgs dn{};
@@ -318,10 +336,12 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
         dn.tc = b->gemm_mode;
         dn.x = xa;
         dn.x.counter = b->counters + 32;
+        dn.trace = tr();
         if ((e = mark(b, s, BK_DOWN, launch_bgemm(dn, BEPI_RETURN, b->epr, s, wmap(b, l, 3))))) break;
 
         BExchangeArgs ca = xa;
         ca.ln_next = l + 1 < d.layers ? m->L[l + 1].ln_attn : m->norm;
+        ca.trace = tr();
         if ((e = mark(b, s, BK_COMBINE, launch_ep_combine(ca, s)))) break;
     }
     if (e) return e;
@@ -338,6 +358,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
     ha.ldy = d.vocab;
     ha.div = d.logits_scaling;
     ha.tc = b->gemm_mode;
+    ha.trace = tr();
     if ((e = mark(b, s, BK_LM_HEAD, launch_bgemm(ha, BEPI_STORE, 1, s, wmap(b, b->m->d.layers, 0))))) return e;
     BHeadArgs hd{};
     hd.logits = b->logits;
@@ -350,6 +371,7 @@ cudaError_t enqueue_bstep(lastro_batch* b, int n, cudaStream_t s) {
     hd.tokens = b->d_tok;
     hd.epoch_base = b->epoch;
     hd.layers = d.layers;
+    hd.trace = tr();
     return mark(b, s, BK_ARGMAX, launch_bargmax(hd, s));
 }
 
@@ -875,6 +897,90 @@ extern "C" int lastro_batch_profile(lastro_batch* b, int32_t n, const int32_t* s
     if (e) return bfail(b, e, "batch profile");
     if ((rc = bfinish(b, "batch profile"))) return rc;
     for (int i = 0; i < n; ++i) b->pos_host[seq_ids[i]] += steps;
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_batch_trace(lastro_batch* b, int32_t n, const int32_t* seq_ids, const int32_t* tokens,
+                                  int32_t steps, float* exposed_ms, float* span_ms, float* wait_ms, int32_t n_kinds,
+                                  float* step_ms) {
+    if (!b || steps < 1 || !exposed_ms || !span_ms || !wait_ms || !step_ms || n_kinds < BK_COUNT) return LASTRO_E_ARG;
+    int rc = bready(b);
+    if (rc) return rc;
+    cudaSetDevice(b->ctx->device);
+    if ((rc = bstage(b, n, seq_ids, tokens, steps))) return rc;
+    cudaStream_t s = b->ctx->stream;
+    const int L = b->m->d.layers, launches = bstep_launches(b);
+    const size_t words = (size_t)launches * kTraceMaxCtas * kTraceWords;
+    if (!b->d_trace) BTRY(b->arena.alloc(&b->d_trace, words), "trace buffer");
+    // the product step's launches with the stamps on, captured like the product graph (a fresh capture per call)
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t x = nullptr;
+    BTRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
+    cudaError_t e = cudaMemsetAsync(b->d_trace, 0, words * sizeof(unsigned long long), s);
+    if (e == cudaSuccess) e = enqueue_bstep(b, n, s, b->d_trace);
+    cudaError_t e2 = cudaStreamEndCapture(s, &g);
+    if (e == cudaSuccess) e = e2;
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&x, g, 0);
+    if (g) cudaGraphDestroy(g);
+    if (e != cudaSuccess) return bfail(b, e, "batch trace capture");
+    std::vector<int> kind(launches);
+    kind[0] = BK_NORM;
+    const int k8[8] = {BK_QKV, BK_ROPE, BK_ATTN, BK_OPROJ, BK_ROUTER, BK_GATE_UP, BK_DOWN, BK_COMBINE};
+    for (int l = 0; l < L; ++l)
+        for (int i = 0; i < 8; ++i) kind[1 + 8 * l + i] = k8[i];
+    kind[launches - 2] = BK_LM_HEAD;
+    kind[launches - 1] = BK_ARGMAX;
+    std::vector<unsigned long long> h(words);
+    std::vector<double> ex(BK_COUNT, 0.0), sp(BK_COUNT, 0.0), wt(BK_COUNT, 0.0);
+    double step_acc = 0.0;
+    for (int st = 0; st < steps && e == cudaSuccess; ++st) {
+        e = cudaGraphLaunch(x, s);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(h.data(), b->d_trace, words * sizeof(unsigned long long), cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) break;
+        unsigned long long first = ~0ull, prev_end = 0, last = 0;
+        for (int i = 0; i < launches; ++i) {
+            unsigned long long t0 = ~0ull, rel = ~0ull, t1 = 0;
+            for (int c = 0; c < kTraceMaxCtas; ++c) {
+                const unsigned long long* w = &h[((size_t)i * kTraceMaxCtas + c) * kTraceWords];
+                if (!w[0]) continue;
+                t0 = std::min(t0, w[0]);
+                if (w[1]) rel = std::min(rel, w[1]);
+                t1 = std::max(t1, w[2]);
+            }
+            if (t0 == ~0ull) continue;  // a launch without stamps (the non-default GEMM and attention forms)
+            if (rel == ~0ull) rel = t0;
+            first = std::min(first, t0);
+            last = std::max(last, t1);
+            const unsigned long long from = prev_end ? prev_end : t0;
+            ex[kind[i]] += t1 > from ? (double)(t1 - from) : 0.0;
+            sp[kind[i]] += (double)(t1 - t0);
+            wt[kind[i]] += prev_end && rel > prev_end ? (double)(rel - prev_end) : 0.0;
+            prev_end = std::max(prev_end, t1);
+        }
+        if (last > first && first != ~0ull) step_acc += (double)(last - first);
+    }
+    cudaGraphExecDestroy(x);
+    if (e != cudaSuccess) return bfail(b, e, "batch trace");
+    if ((rc = bfinish(b, "batch trace"))) return rc;
+    b->trace_host.swap(h);
+    for (int i = 0; i < n; ++i) b->pos_host[seq_ids[i]] += steps;
+    for (int k = 0; k < n_kinds; ++k) exposed_ms[k] = span_ms[k] = wait_ms[k] = 0.0f;
+    for (int k = 0; k < BK_COUNT; ++k) {
+        exposed_ms[k] = (float)(ex[k] / steps * 1e-6);
+        span_ms[k] = (float)(sp[k] / steps * 1e-6);
+        wait_ms[k] = (float)(wt[k] / steps * 1e-6);
+    }
+    *step_ms = (float)(step_acc / steps * 1e-6);
+    return LASTRO_OK;
+}
+
+extern "C" int lastro_batch_trace_raw(const lastro_batch* b, int32_t launch, unsigned long long* out, int32_t words) {
+    if (!b || !out || launch < 0) return LASTRO_E_ARG;
+    const size_t per = (size_t)kTraceMaxCtas * kTraceWords;
+    if ((size_t)(launch + 1) * per > b->trace_host.size() || (size_t)words < per) return LASTRO_E_ARG;
+    memcpy(out, b->trace_host.data() + (size_t)launch * per, per * sizeof(unsigned long long));
     return LASTRO_OK;
 }
 

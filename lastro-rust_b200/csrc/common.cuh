@@ -48,6 +48,11 @@ struct CtaTrace {
     LDEV void mark(int i, unsigned tid = 0) const {
         if (p && threadIdx.x == tid) p[3 + i] = global_ns();
     }
+    // the same, stamped only once `v` (a value the phase produced) is available: the branch on it orders the timer
+    // read after the load or arithmetic that yields v
+    LDEV void mark_after(int i, float v, unsigned tid = 0) const {
+        if (p && threadIdx.x == tid && __float_as_uint(v) != 0xffffffffu) p[3 + i] = global_ns();
+    }
     LDEV ~CtaTrace() {
         if (p && (threadIdx.x & 31) == 0) atomicMax(p + 2, global_ns());
     }

@@ -347,6 +347,35 @@ LDEV void route_topk_warp(float v0, float v1, int E, int k, int* sid, float* sva
     __syncwarp();
 }
 
+// route_topk_warp's top-k computed by the whole block (every thread calls it; blockDim >= E; lg in shared memory):
+// each expert's rank by counting the larger keys, then the softmax over the k by threads j < k.  Bitwise the same ids,
+// values and weights as route_topk_warp: the same keys and comparisons, the same exponentials, the sum in the same
+// order.  __syncthreads inside.
+LDEV void route_topk_block(const float* lg, int E, int k, unsigned long long* keys, float* ex, int* sid, float* sval,
+                           float* sw) {
+    const int t = threadIdx.x;
+    if (t < E) keys[t] = route_key(lg[t], t);
+    __syncthreads();
+    if (t < E) {
+        const unsigned long long me = keys[t];
+        int r = 0;
+        for (int j = 0; j < E; ++j) r += (int)(keys[j] > me);
+        if (r < k) {
+            sid[r] = t;
+            sval[r] = lg[t];
+        }
+    }
+    __syncthreads();
+    if (t < k) ex[t] = expf(__fsub_rn(sval[t], sval[0]));
+    __syncthreads();
+    if (t < k) {
+        float sum = 0.0f;
+        for (int j = 0; j < k; ++j) sum = __fadd_rn(sum, ex[j]);
+        sw[t] = __fdiv_rn(ex[t], sum);
+    }
+    __syncthreads();
+}
+
 // Routing from the output projection's shares (RouteShares): the shares of CTA c go to thread (c % groups) * E1 + e,
 // each thread loads its shares in batches of independent loads and sums them in order, the groups are summed in
 // order, then r = 1/sqrt(sum h^2 / H + eps) (model.rs:141-145), logits = r * share-sums, the top-k by rank counting in

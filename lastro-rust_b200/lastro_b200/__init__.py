@@ -125,6 +125,9 @@ EXPORTS = {
     "lastro_batch_profile": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p,
                                        C.c_int32]),
     "lastro_batch_set_wait_limit": (C.c_int, [C.c_void_p, C.c_uint64]),
+    "lastro_batch_trace": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p,
+                                     C.c_void_p, C.c_int32, C.c_void_p]),
+    "lastro_batch_trace_raw": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32]),
     "lastro_batch_destroy": (None, [C.c_void_p]),
 }
 
@@ -724,6 +727,26 @@ class GpuBatch:
         out = np.zeros(len(self.KERNELS), np.float32)
         self.ctx.check(lib().lastro_batch_profile(self.h, sq.size, _p(sq), _p(tk), steps, _p(out), out.size))
         return dict(zip(self.KERNELS, out.tolist()))
+
+    def trace(self, seq_ids, tokens, steps: int) -> dict:
+        """In-graph timeline of `steps` graph-replayed steps: {"exposed": {kind: ms}, "span": {..}, "wait": {..},
+        "step_ms": ms} per step (exposed: each kind's share of the step's critical path; the positions advance)."""
+        sq = np.ascontiguousarray(seq_ids, dtype=np.int32)
+        tk = np.ascontiguousarray(tokens, dtype=np.int32)
+        ex, sp, wt = (np.zeros(len(self.KERNELS), np.float32) for _ in range(3))
+        st = np.zeros(1, np.float32)
+        self.ctx.check(lib().lastro_batch_trace(self.h, sq.size, _p(sq), _p(tk), steps, _p(ex), _p(sp), _p(wt), ex.size,
+                                                _p(st)))
+        kinds = self.KERNELS
+        return {"exposed": dict(zip(kinds, ex.tolist())), "span": dict(zip(kinds, sp.tolist())),
+                "wait": dict(zip(kinds, wt.tolist())), "step_ms": float(st[0])}
+
+    def trace_raw(self, launch: int) -> np.ndarray:
+        """[1024, TRACE_WORDS] stamps of one launch of the last traced step (0 the layer-0 norm, then 8 per layer:
+        qkv, rope_kv, attention, oproj, router, gate_up, down, combine; then lm_head, argmax)."""
+        out = np.zeros((1024, TRACE_WORDS), np.uint64)
+        self.ctx.check(lib().lastro_batch_trace_raw(self.h, launch, _p(out), out.size))
+        return out
 
     def close(self):
         if getattr(self, "h", None):

@@ -93,6 +93,37 @@ def test_batch_decode_equals_steps_and_graphs_equal_direct(gpu_ctx):
     assert np.array_equal(runs[0], runs[1]) and np.array_equal(runs[1], runs[2])
 
 
+def test_batch_trace_covers_the_step_and_changes_nothing(gpu_ctx):
+    """lastro_batch_trace: the batched step graph replayed with every CTA stamping the global timer.  Every kernel kind
+    of the step shows up, the kinds' exposed times add up to the step, the router's milestones are in order, and the
+    traced steps decode like the product graph (bf16 KV: tensor-core attention; tcgen05 GEMMs)."""
+    cfg = CFG.TINY_768
+    w = reference_tiny_weights(cfg)
+    seqs, first = [2, 0, 1], [5, 11, 17]
+    m1, a = batch_for(gpu_ctx, cfg, w, 3, 64, kv="bf16")
+    m2, b = batch_for(gpu_ctx, cfg, w, 3, 64, kv="bf16")
+    tr = a.trace(seqs, first, 3)
+    ids_b = b.decode(seqs, first, 3)
+    for k in ("norm", "qkv", "rope_kv", "attention", "oproj", "router", "gate_up", "down", "combine", "lm_head",
+              "argmax"):
+        assert tr["exposed"][k] > 0.0 and tr["span"][k] > 0.0, k
+    total = sum(tr["exposed"].values())
+    assert abs(total - tr["step_ms"]) <= 0.02 * tr["step_ms"] + 1e-3, (total, tr["step_ms"])
+    L = cfg["layers"]
+    raw = a.trace_raw(1 + 8 * (L - 1) + 4).astype(np.int64)  # the last layer's router
+    raw = raw[raw[:, 0] > 0]
+    assert len(raw) == len(seqs)
+    for r in raw:  # start <= release <= RMSNorm <= logits <= top-k <= rows sent <= ids sent <= exit
+        seq = [r[0], r[1], r[8], r[3], r[6], r[7], r[4], r[2]]
+        assert all(x > 0 for x in seq) and seq == sorted(seq), seq
+    tok = ids_b[-1].tolist()
+    na, la, _ = a.step(seqs, tok, want_logits=True)
+    nb, lb, _ = b.step(seqs, tok, want_logits=True)
+    assert np.array_equal(na, nb) and np.array_equal(la, lb)  # the stamps change no result
+    m1.close()
+    m2.close()
+
+
 def test_batch_3b_shape_with_zipf_bias_matches_oracle(gpu_ctx, pool):
     """The C5 model (Granite-3B shape) with its Zipf router bias: 8 sequences, 6 positions each, against the oracle.
     Routing is identical except where the oracle's router scores of the two experts differ by less than 1e-4 (the
