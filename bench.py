@@ -290,7 +290,7 @@ def run_batched(a):
     ctx = LB.Context(local, stream.cuda_stream)
     model = LB.GpuModel(ctx, cfg, 8, kv_dtype=a.kv)
     model.fill_synthetic(c["weight_seed"], CFG.WEIGHT_STD, 0.0)
-    max_len = a.context + W + 2 * K + 8
+    max_len = a.context + W + 2 * K + 16
     batch = LB.GpuBatch(model, n, max_len, rank, world)
     if world > 1:
         handles = [None] * world
@@ -377,6 +377,17 @@ def run_batched(a):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     prof = batch.profile(seqs, toks, 2)
+    # in the replayed graph (the step's own regime): each kind's share of the step's critical path, every rank
+    tr = batch.trace(seqs, toks, 3)
+    exposed = {k: round(v, 4) for k, v in tr["exposed"].items() if v > 0}
+    if world > 1:  # the slowest rank's figures
+        t = torch.tensor([tr["step_ms"]], device="cuda")
+        gathered = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(gathered, t)
+        slow = int(torch.stack(gathered).argmax().item())
+        ex = torch.tensor([tr["exposed"][k] for k in batch.KERNELS], device="cuda")
+        dist.broadcast(ex, src=slow)
+        exposed = {k: round(float(v), 4) for k, v in zip(batch.KERNELS, ex.tolist()) if v > 0}
     mean_ctx = ctx0 + (K + 1) / 2.0
     H, I, L, E, kk = cfg["hidden"], cfg["inter"], cfg["layers"], cfg["experts"], cfg["k"]
     qd, kvd = cfg["heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
@@ -409,6 +420,7 @@ def run_batched(a):
                      "bytes_per_step": step_bytes, "bytes_note": "touched experts + KV of all sequences + the dense "
                      "weights every rank streams; per GPU"},
         "kernels_ms_per_step": {k: round(v, 4) for k, v in prof.items()},
+        "in_graph_exposed_ms_per_step": exposed,
         "e2e": {"value": total * K / (e2e_ms / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": 8 * n,
                 "d2h_bytes_per_step": 4 * n},
         "gpu_launches": K * (L * 8 + 3),  # norm; 8 kernels per layer; lm_head, argmax
