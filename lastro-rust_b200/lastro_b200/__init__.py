@@ -7,6 +7,7 @@ no GPU is present, constructing a context raises.
 from __future__ import annotations
 
 import ctypes as C
+import sys
 import os
 import subprocess
 import weakref
@@ -183,7 +184,8 @@ class Context:
             self.h = None
 
     def __del__(self):
-        self.close()
+        if not sys.is_finalizing():  # at interpreter exit the process's CUDA context goes with it
+            self.close()
 
 
 class GpuLayer:
@@ -228,7 +230,8 @@ class GpuLayer:
             self.h = None
 
     def __del__(self):
-        self.close()
+        if not sys.is_finalizing():  # at interpreter exit the process's CUDA context goes with it
+            self.close()
 
 
 def moe_block_forward_noalloc(x: int, router: int, gate_up: int, down: int, experts: int, hidden: int, inter: int,
@@ -311,7 +314,8 @@ class Checkpoint:
             self.h = None
 
     def __del__(self):
-        self.close()
+        if not sys.is_finalizing():  # at interpreter exit the process's CUDA context goes with it
+            self.close()
 
 
 class Tokenizer:
@@ -370,7 +374,8 @@ class Tokenizer:
             self.h = None
 
     def __del__(self):
-        self.close()
+        if not sys.is_finalizing():  # at interpreter exit the process's CUDA context goes with it
+            self.close()
 
 
 def pretokenize(text: str) -> list[str]:
@@ -631,7 +636,8 @@ class GpuModel:
             self.h = None
 
     def __del__(self):
-        self.close()
+        if not sys.is_finalizing():  # at interpreter exit the process's CUDA context goes with it
+            self.close()
 
 
 class GpuBatch:
@@ -754,4 +760,5 @@ class GpuBatch:
             self.h = None
 
     def __del__(self):
-        self.close()
+        if not sys.is_finalizing():  # at interpreter exit the process's CUDA context goes with it
+            self.close()
