@@ -14,7 +14,8 @@
    - "cut": id prefixes that split a character, with the bytes decoded lossily by Python (U+FFFD per maximal
      invalid subsequence).
 
-Run in a container that has /root/reference and `tokenizers`: python tests/golden/gen_tokenizer_golden.py
+Run with `tokenizers` installed and the reference checkout's root in LASTRO_REFERENCE (the cases file sits at
+qual-runs/A2-LOTE-20261103/5a-referencia/casos.json under it): python tests/golden/gen_tokenizer_golden.py
 """
 import json
 import os
@@ -23,7 +24,8 @@ import random
 from tokenizers import Tokenizer, decoders, models, pre_tokenizers, trainers
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-CASES = "/root/reference/qual-runs/A2-LOTE-20261103/5a-referencia/casos.json"
+CASES = os.path.join(os.environ.get("LASTRO_REFERENCE", "reference"), "qual-runs", "A2-LOTE-20261103", "5a-referencia",
+                     "casos.json")
 
 SPECIAL = ["<|end_of_text|>", "<fim_prefix>", "<fim_middle>", "<fim_suffix>", "<fim_pad>", "<filename>",
            "<|start_of_role|>", "<|end_of_role|>", "<|tool_call|>", "<|ab|>", "<|ab|>c"]
