@@ -805,10 +805,10 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
           A.alloc(&m->part_ml, (size_t)d.heads * kAttnSplits * 2) ||
           A.alloc(&m->route_w, (size_t)d.layers * d.k) || A.alloc(&m->route_ids, (size_t)d.layers * d.k) ||
           A.alloc(&m->rnorm, 1) || A.alloc(&m->a, (size_t)d.k * I) || A.alloc(&m->logits, V) ||
-          A.alloc(&m->d_token, 1) || A.alloc(&m->d_pos, 1) || A.alloc(&m->d_step, 1) ||
+          A.alloc(&m->d_token, 2) || A.alloc(&m->d_pos, 1) || A.alloc(&m->d_step, 1) ||
           A.alloc(&m->d_out_ids, (size_t)max_len + 1) || A.alloc(&m->d_prompt, (size_t)max_len + 1) ||
           A.alloc(&m->router_counter, 1) || A.alloc(&m->head_counter, 1) || A.alloc(&m->attn_counters, d.kv_heads) ||
-          A.alloc(&m->head_partial, m->head_grid) || A.alloc(&m->d_err, 1) ||
+          A.alloc(&m->head_partial, m->head_grid) ||
           A.alloc(&m->op_partial, (size_t)oproj_grid(d.hidden) * (E + 1)) || A.alloc(&m->moe_barrier, 1) ||
           A.alloc(&m->step_ctr, 1) || A.alloc(&m->route_flags, (size_t)d.layers) ||
           A.alloc(&m->spec_ids, kMaxTopK) || A.alloc(&m->spec_ticket, 1);
@@ -849,7 +849,9 @@ extern "C" int lastro_model_create(lastro_ctx* ctx, const lastro_model_desc* des
         e = cudaMemsetAsync(m->L[l].k_pool, 0, kvpool, s);
         if (!e) e = cudaMemsetAsync(m->L[l].v_pool, 0, kvpool, s);
     }
+    // the token and the error word sit side by side on both sides: a step reads both back in one copy
     m->h_err = m->h_token + 1;
+    m->d_err = m->d_token + 1;
     for (void* p : {(void*)m->router_counter, (void*)m->head_counter, (void*)m->d_pos, (void*)m->d_step,
                     (void*)m->d_token, (void*)m->d_err})
         if (!e) e = cudaMemsetAsync(p, 0, sizeof(int), s);
@@ -1143,13 +1145,18 @@ extern "C" int lastro_model_step(lastro_model* m, int32_t token, float* logits, 
     if (rc) return rc;
     const lastro_model_desc& d = m->d;
     if (logits) MTRY(cudaMemcpyAsync(logits, m->logits, sizeof(float) * d.vocab, cudaMemcpyDeviceToHost, s), "logits");
-    if (next_token) MTRY(cudaMemcpyAsync(next_token, m->d_token, sizeof(int), cudaMemcpyDeviceToHost, s), "token");
     if (route_ids)
         MTRY(cudaMemcpyAsync(route_ids, m->route_ids, sizeof(int) * d.layers * d.k, cudaMemcpyDeviceToHost, s), "routes");
     if (route_weights)
         MTRY(cudaMemcpyAsync(route_weights, m->route_w, sizeof(float) * d.layers * d.k, cudaMemcpyDeviceToHost, s), "routes");
-    rc = finish(m, "step");
-    if (rc) return rc;
+    // the next token and the error word in one copy into pinned memory (the token upload above read it first)
+    MTRY(cudaMemcpyAsync(m->h_token, m->d_token, 2 * sizeof(int), cudaMemcpyDeviceToHost, s), "step");
+    MTRY(cudaStreamSynchronize(s), "step");
+    if (*m->h_err) {
+        m->poisoned = true;
+        return set_err(ctx, LASTRO_E_CUDA, "step: a kernel wait gave up (code %d); model poisoned", *m->h_err);
+    }
+    if (next_token) *next_token = m->h_token[0];
     m->pos_host += 1;
     return LASTRO_OK;
 }
