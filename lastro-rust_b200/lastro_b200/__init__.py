@@ -183,8 +183,9 @@ class Context:
             lib().lastro_ctx_destroy(self.h)
             self.h = None
 
-    def __del__(self):
-        if not sys.is_finalizing():  # at interpreter exit the process's CUDA context goes with it
+    def __del__(self, _finalizing=sys.is_finalizing):
+        # at interpreter exit (module globals already cleared) the process's CUDA context goes with the process
+        if getattr(self, "h", None) and not _finalizing():
             self.close()
 
 
@@ -229,8 +230,9 @@ class GpuLayer:
             lib().lastro_layer_destroy(self.h)
             self.h = None
 
-    def __del__(self):
-        if not sys.is_finalizing():  # at interpreter exit the process's CUDA context goes with it
+    def __del__(self, _finalizing=sys.is_finalizing):
+        # at interpreter exit (module globals already cleared) the process's CUDA context goes with the process
+        if getattr(self, "h", None) and not _finalizing():
             self.close()
 
 
@@ -313,8 +315,9 @@ class Checkpoint:
             lib().lastro_checkpoint_close(self.h)
             self.h = None
 
-    def __del__(self):
-        if not sys.is_finalizing():  # at interpreter exit the process's CUDA context goes with it
+    def __del__(self, _finalizing=sys.is_finalizing):
+        # at interpreter exit (module globals already cleared) the process's CUDA context goes with the process
+        if getattr(self, "h", None) and not _finalizing():
             self.close()
 
 
@@ -373,8 +376,9 @@ class Tokenizer:
             lib().lastro_tokenizer_destroy(self.h)
             self.h = None
 
-    def __del__(self):
-        if not sys.is_finalizing():  # at interpreter exit the process's CUDA context goes with it
+    def __del__(self, _finalizing=sys.is_finalizing):
+        # at interpreter exit (module globals already cleared) the process's CUDA context goes with the process
+        if getattr(self, "h", None) and not _finalizing():
             self.close()
 
 
@@ -635,8 +639,9 @@ class GpuModel:
             lib().lastro_model_destroy(self.h)
             self.h = None
 
-    def __del__(self):
-        if not sys.is_finalizing():  # at interpreter exit the process's CUDA context goes with it
+    def __del__(self, _finalizing=sys.is_finalizing):
+        # at interpreter exit (module globals already cleared) the process's CUDA context goes with the process
+        if getattr(self, "h", None) and not _finalizing():
             self.close()
 
 
@@ -759,6 +764,7 @@ class GpuBatch:
             lib().lastro_batch_destroy(self.h)
             self.h = None
 
-    def __del__(self):
-        if not sys.is_finalizing():  # at interpreter exit the process's CUDA context goes with it
+    def __del__(self, _finalizing=sys.is_finalizing):
+        # at interpreter exit (module globals already cleared) the process's CUDA context goes with the process
+        if getattr(self, "h", None) and not _finalizing():
             self.close()
