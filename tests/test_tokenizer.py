@@ -191,3 +191,16 @@ def test_encode_refuses_invalid_utf8(tok):
     n = C.c_int32()
     for raw in (b"\xff", b"a\xc0\x80", b"\xed\xa0\x80", b"\xf4\x90\x80\x80", b"\xe2\x82"):
         assert LB.lib().lastro_tokenizer_encode(tok.h, raw, len(raw), None, 0, C.byref(n)) == LB.E_ARG
+
+
+def test_objects_left_open_at_interpreter_exit_are_quiet():
+    """A handle never closed is left to process teardown at interpreter exit: no destructor error on stderr."""
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("import sys; sys.path.insert(0, 'lastro-rust_b200'); import lastro_b200 as LB; "
+            f"t = LB.Tokenizer({TOK_JSON!r}); u = LB.Tokenizer({TOK_JSON!r}); u.close(); print(len(t.encode('hi')))")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, cwd=root, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip().isdigit(), r.stderr
+    assert "Exception ignored" not in r.stderr, r.stderr
